@@ -1,0 +1,275 @@
+"""ctypes binding of the in-tree C ABI library ``libungx.so`` (declared in include/ungx.h).
+
+There is no fallback: if the shared library is missing, importing this module raises
+``ImportError`` naming the build command.  Every call checks the returned status and
+raises :class:`UngxError` with the library's message.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import POINTER, c_char_p, c_double, c_int, c_uint8, c_uint32, c_uint64, c_void_p
+
+import numpy as np
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libungx.so")
+
+UNGX_OK = 0
+UNGX_ERR_INVALID_ARG = -1
+UNGX_ERR_OOM = -2
+UNGX_ERR_CUDA = -3
+UNGX_ERR_TIMEOUT = -4
+UNGX_ERR_ABORTED = -5
+UNGX_ERR_NO_DEVICE = -6
+UNGX_ERR_STATE = -7
+
+ROUTE_AUTO = 0
+ROUTE_TENSOR = 1
+ROUTE_EXACT = 2
+
+EMPTY_ID = 0xFFFFFFFF
+
+
+class UngxError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"ungx status {status}: {message}")
+        self.status = status
+
+
+class CrossEdgeTiming(ctypes.Structure):
+    """Layout of ``ungx_cross_edge_timing``."""
+
+    _fields_ = [
+        ("generate_ms", c_double),
+        ("gpu_h2d_ms", c_double),
+        ("gpu_kernel_ms", c_double),
+        ("gpu_d2h_ms", c_double),
+        ("plan_ms", c_double),
+        ("prepare_ms", c_double),
+        ("tc_kernel_ms", c_double),
+        ("fallback_ms", c_double),
+        ("pairs", c_uint64),
+        ("rows_certified", c_uint64),
+        ("rows_fallback", c_uint64),
+        ("route_used", c_uint32),
+        ("gpu_launches", c_uint32),
+    ]
+
+    def as_dict(self) -> dict:
+        return {name: getattr(self, name) for name, _ in self._fields_}
+
+
+class CrossEdgeProblem(ctypes.Structure):
+    """Layout of ``ungx_cross_edge_problem``."""
+
+    _fields_ = [
+        ("num_points", c_uint32),
+        ("dim", c_uint32),
+        ("topk", c_uint32),
+        ("num_groups", c_uint32),
+        ("group_ranges", POINTER(c_uint32)),
+        ("lng_out_offsets", POINTER(c_uint64)),
+        ("lng_out_ids", POINTER(c_uint32)),
+        ("skip_source_group", POINTER(c_uint8)),
+        ("route", c_uint32),
+        ("shard_rank", c_uint32),
+        ("shard_count", c_uint32),
+    ]
+
+
+# (name, restype, argtypes) of every exported function, in include/ungx.h order.
+_SIGNATURES = [
+    ("ungx_context_create", c_int, [c_int, POINTER(c_void_p)]),
+    ("ungx_context_destroy", c_int, [c_void_p]),
+    ("ungx_last_error", c_char_p, [c_void_p]),
+    ("ungx_status_string", c_char_p, [c_int]),
+    ("ungx_set_timeout_ms", c_int, [c_void_p, c_uint32]),
+    ("ungx_set_device_wait_limit_ns", c_int, [c_void_p, c_uint64]),
+    ("ungx_prepare_base_vectors", c_int, [c_void_p, c_void_p, c_uint32, c_uint32, c_int]),
+    ("ungx_release_base_vectors", c_int, [c_void_p]),
+    ("ungx_cross_edges_generate", c_int,
+     [c_void_p, POINTER(CrossEdgeProblem), c_void_p, c_void_p, POINTER(CrossEdgeTiming)]),
+    ("ungx_cross_edges_generate_device", c_int,
+     [c_void_p, POINTER(CrossEdgeProblem), c_void_p, c_void_p, c_void_p, POINTER(CrossEdgeTiming)]),
+    ("ungx_cross_edges_build", c_int,
+     [c_void_p, c_void_p, POINTER(CrossEdgeProblem), c_void_p, c_void_p, POINTER(CrossEdgeTiming)]),
+    ("ungx_shard_rows", c_int, [POINTER(CrossEdgeProblem), c_void_p, POINTER(c_uint64)]),
+    ("ungx_label_graph_build", c_int, [c_uint32, c_void_p, c_void_p, c_int, POINTER(c_void_p)]),
+    ("ungx_label_graph_destroy", c_int, [c_void_p]),
+    ("ungx_label_graph_num_groups", c_uint32, [c_void_p]),
+    ("ungx_label_graph_num_edges", c_uint64, [c_void_p]),
+    ("ungx_label_graph_copy_groups", c_int, [c_void_p, c_void_p, c_void_p]),
+    ("ungx_label_graph_copy_out_neighbors", c_int, [c_void_p, c_void_p, c_void_p]),
+    ("ungx_label_graph_copy_in_neighbors", c_int, [c_void_p, c_void_p, c_void_p]),
+    ("ungx_label_graph_num_set_labels", c_uint64, [c_void_p]),
+    ("ungx_label_graph_copy_label_sets", c_int, [c_void_p, c_void_p, c_void_p]),
+    ("ungx_flat_to_csr", c_int, [c_void_p, c_uint32, c_uint32, c_void_p, c_void_p]),
+]
+
+EXPORTED = [name for name, _, _ in _SIGNATURES]
+
+
+def _load() -> ctypes.CDLL:
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            f"{LIB_PATH} is missing: build it with `make -C filtervectorcode_refactor_b200/csrc` "
+            "or `python -c 'import __graft_entry__ as g; g.build()'` (there is no CPU fallback)")
+    lib = ctypes.CDLL(LIB_PATH)
+    for name, res, args in _SIGNATURES:
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+lib = _load()
+
+
+def _ptr(a: np.ndarray | None) -> int | None:
+    return None if a is None else a.ctypes.data
+
+
+def check(status: int, ctx: int | None = None) -> None:
+    if status != UNGX_OK:
+        msg = lib.ungx_last_error(ctx)
+        raise UngxError(status, msg.decode() if msg else lib.ungx_status_string(status).decode())
+
+
+class LabelGraph:
+    """Grouping + reorder + LNG computed by the library (owning wrapper)."""
+
+    def __init__(self, label_offsets: np.ndarray, labels: np.ndarray, num_threads: int = 0):
+        label_offsets = np.ascontiguousarray(label_offsets, dtype=np.uint64)
+        labels = np.ascontiguousarray(labels, dtype=np.uint32)
+        n = label_offsets.shape[0] - 1
+        h = c_void_p()
+        check(lib.ungx_label_graph_build(n, _ptr(label_offsets), _ptr(labels) if labels.size else None,
+                                         num_threads, ctypes.byref(h)))
+        self._h = h
+        self.num_points = n
+        self.num_groups = int(lib.ungx_label_graph_num_groups(h))
+        G = self.num_groups
+        self.new_to_old = np.empty(n, dtype=np.uint32)
+        self.group_ranges = np.empty(2 * (G + 1), dtype=np.uint32)
+        check(lib.ungx_label_graph_copy_groups(h, _ptr(self.new_to_old), _ptr(self.group_ranges)))
+        ne = int(lib.ungx_label_graph_num_edges(h))
+        self.out_offsets = np.empty(G + 2, dtype=np.uint64)
+        self.out_ids = np.empty(max(ne, 1), dtype=np.uint32)[:ne]
+        check(lib.ungx_label_graph_copy_out_neighbors(h, _ptr(self.out_offsets), _ptr(self.out_ids)))
+        self.in_offsets = np.empty(G + 2, dtype=np.uint64)
+        self.in_ids = np.empty(max(ne, 1), dtype=np.uint32)[:ne]
+        check(lib.ungx_label_graph_copy_in_neighbors(h, _ptr(self.in_offsets), _ptr(self.in_ids)))
+        nl = int(lib.ungx_label_graph_num_set_labels(h))
+        self.set_offsets = np.empty(G + 2, dtype=np.uint64)
+        self.set_labels = np.empty(max(nl, 1), dtype=np.uint32)[:nl]
+        check(lib.ungx_label_graph_copy_label_sets(h, _ptr(self.set_offsets), _ptr(self.set_labels)))
+
+    def close(self) -> None:
+        if self._h:
+            lib.ungx_label_graph_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Problem:
+    """Keeps the arrays a ``CrossEdgeProblem`` points at alive."""
+
+    def __init__(self, num_points: int, dim: int, topk: int, group_ranges: np.ndarray,
+                 out_offsets: np.ndarray, out_ids: np.ndarray, skip_source_group: np.ndarray | None = None,
+                 route: int = ROUTE_AUTO, shard_rank: int = 0, shard_count: int = 1):
+        self.group_ranges = np.ascontiguousarray(group_ranges, dtype=np.uint32)
+        self.out_offsets = np.ascontiguousarray(out_offsets, dtype=np.uint64)
+        self.out_ids = np.ascontiguousarray(out_ids, dtype=np.uint32)
+        if self.out_ids.size == 0:
+            self.out_ids = np.zeros(1, dtype=np.uint32)
+        self.skip = None if skip_source_group is None else np.ascontiguousarray(skip_source_group, dtype=np.uint8)
+        G = self.group_ranges.shape[0] // 2 - 1
+        self.c = CrossEdgeProblem(
+            num_points, dim, topk, G,
+            self.group_ranges.ctypes.data_as(POINTER(c_uint32)),
+            self.out_offsets.ctypes.data_as(POINTER(c_uint64)),
+            self.out_ids.ctypes.data_as(POINTER(c_uint32)),
+            None if self.skip is None else self.skip.ctypes.data_as(POINTER(c_uint8)),
+            route, shard_rank, shard_count)
+
+    def shard_rows(self) -> np.ndarray:
+        cnt = c_uint64()
+        check(lib.ungx_shard_rows(ctypes.byref(self.c), None, ctypes.byref(cnt)))
+        rows = np.empty(max(cnt.value, 1), dtype=np.uint32)
+        check(lib.ungx_shard_rows(ctypes.byref(self.c), _ptr(rows), ctypes.byref(cnt)))
+        return rows[:cnt.value]
+
+
+class Context:
+    """One device context (``ungx_context``)."""
+
+    def __init__(self, device: int = 0):
+        h = c_void_p()
+        check(lib.ungx_context_create(device, ctypes.byref(h)))
+        self.h = h
+        self.device = device
+
+    def close(self) -> None:
+        if self.h:
+            lib.ungx_context_destroy(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_timeout_ms(self, ms: int) -> None:
+        check(lib.ungx_set_timeout_ms(self.h, ms), self.h)
+
+    def set_device_wait_limit_ns(self, ns: int) -> None:
+        check(lib.ungx_set_device_wait_limit_ns(self.h, ns), self.h)
+
+    def prepare_base_vectors(self, vectors, num_points: int, dim: int, on_device: bool) -> None:
+        """``vectors`` is a host numpy array, or (on_device=True) an integer device pointer."""
+        ptr = vectors if on_device else _ptr(vectors)
+        check(lib.ungx_prepare_base_vectors(self.h, ptr, num_points, dim, int(on_device)), self.h)
+
+    def release_base_vectors(self) -> None:
+        check(lib.ungx_release_base_vectors(self.h), self.h)
+
+    def generate(self, problem: Problem, out_ids: np.ndarray, out_dists: np.ndarray | None) -> CrossEdgeTiming:
+        t = CrossEdgeTiming()
+        check(lib.ungx_cross_edges_generate(self.h, ctypes.byref(problem.c), _ptr(out_ids), _ptr(out_dists),
+                                            ctypes.byref(t)), self.h)
+        return t
+
+    def generate_device(self, problem: Problem, d_ids: int, d_dists: int | None, stream: int | None = None
+                        ) -> CrossEdgeTiming:
+        t = CrossEdgeTiming()
+        check(lib.ungx_cross_edges_generate_device(self.h, ctypes.byref(problem.c), d_ids, d_dists, stream,
+                                                   ctypes.byref(t)), self.h)
+        return t
+
+    def build(self, vectors: np.ndarray, problem: Problem, out_ids: np.ndarray, out_dists: np.ndarray | None
+              ) -> CrossEdgeTiming:
+        t = CrossEdgeTiming()
+        check(lib.ungx_cross_edges_build(self.h, _ptr(vectors), ctypes.byref(problem.c), _ptr(out_ids),
+                                         _ptr(out_dists), ctypes.byref(t)), self.h)
+        return t
+
+
+def flat_to_csr(flat_ids: np.ndarray, num_points: int, topk: int) -> tuple[np.ndarray, np.ndarray]:
+    flat_ids = np.ascontiguousarray(flat_ids, dtype=np.uint32)
+    off = np.empty(num_points + 1, dtype=np.uint64)
+    check(lib.ungx_flat_to_csr(_ptr(flat_ids), num_points, topk, _ptr(off), None))
+    cols = np.empty(max(int(off[-1]), 1), dtype=np.uint32)
+    check(lib.ungx_flat_to_csr(_ptr(flat_ids), num_points, topk, _ptr(off), _ptr(cols)))
+    return off, cols[:int(off[-1])]

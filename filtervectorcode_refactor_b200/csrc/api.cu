@@ -1,0 +1,666 @@
+// C ABI entry points: context, resident base vectors, and the cross-edge generate
+// step (UniNavGraph::build_cross_edges_generate_gpu_optimized's device work,
+// UNG/codes/src/uni_nav_graph_cross_edges.cpp:334-440).
+//
+// Error behaviour follows the reference's seam: it throws inside and returns false
+// to build_cross_group_edges, which falls back to the CPU or rethrows in strict mode
+// (cross_edges.cpp:394-428, 775-789).  Here every failure is a negative status plus
+// ungx_last_error(); the library itself has no CPU fallback.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <thread>
+
+#include "kernels.h"
+#include "ungx_internal.h"
+
+using ungx::Plan;
+
+namespace
+{
+struct DevBuf
+{
+   void *p = nullptr;
+   size_t bytes = 0;
+   cudaError_t ensure(size_t need)
+   {
+      if (need <= bytes && p)
+         return cudaSuccess;
+      if (p)
+         cudaFree(p);
+      p = nullptr;
+      bytes = 0;
+      const size_t alloc = std::max<size_t>(need, 256);
+      cudaError_t e = cudaMalloc(&p, alloc);
+      if (e == cudaSuccess)
+         bytes = alloc;
+      return e;
+   }
+   void release()
+   {
+      if (p)
+         cudaFree(p);
+      p = nullptr;
+      bytes = 0;
+   }
+   template <class T>
+   T *as() const
+   {
+      return static_cast<T *>(p);
+   }
+};
+
+double ms_since(std::chrono::steady_clock::time_point t0)
+{
+   return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+}
+} // namespace
+
+struct ungx_context
+{
+   int device = 0;
+   int num_sms = 148;
+   cudaStream_t stream = nullptr;
+   std::string err;
+   uint32_t timeout_ms = 120000;
+   uint64_t device_wait_ns = 4000000000ull;
+   PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+   // resident base vectors (a4)
+   bool have_vectors = false;
+   const float *X = nullptr; // device, n x d
+   DevBuf X_owned, Xp, xnorm, mean, sums;
+   uint32_t n = 0, d = 0, dp = 0;
+   // per-call scratch
+   DevBuf items, segs, empties, ranges, gmax, counters, fb_rows, fb_items, rows, row_items, out_ids, out_dists;
+   DevBuf stage[2];
+   uint32_t *h_counters = nullptr; // pinned
+   cudaEvent_t ev[8] = {};
+};
+
+namespace
+{
+int fail(ungx_context *ctx, int code, const std::string &msg)
+{
+   if (ctx)
+      ctx->err = msg;
+   ungx::set_global_error(msg);
+   return code;
+}
+
+int cuda_fail(ungx_context *ctx, cudaError_t e, const char *what)
+{
+   const int code = (e == cudaErrorMemoryAllocation) ? UNGX_ERR_OOM : UNGX_ERR_CUDA;
+   return fail(ctx, code, std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")");
+}
+
+#define UNGX_CUDA(ctx, expr, what)                                                                               \
+   do                                                                                                          \
+   {                                                                                                           \
+      cudaError_t _e = (expr);                                                                                 \
+      if (_e != cudaSuccess)                                                                                   \
+         return cuda_fail((ctx), _e, (what));                                                                  \
+   } while (0)
+
+// Host wait on an event with a deadline (the device work itself carries bounded
+// spin waits, so a timeout here means the GPU is far slower than expected).
+int wait_event(ungx_context *ctx, cudaEvent_t ev, const char *what)
+{
+   const auto t0 = std::chrono::steady_clock::now();
+   for (uint32_t spin = 0;; ++spin)
+   {
+      const cudaError_t e = cudaEventQuery(ev);
+      if (e == cudaSuccess)
+         return UNGX_OK;
+      if (e != cudaErrorNotReady)
+         return cuda_fail(ctx, e, what);
+      if (ms_since(t0) > ctx->timeout_ms)
+         return fail(ctx, UNGX_ERR_TIMEOUT, std::string(what) + ": device work exceeded the timeout");
+      if (spin > 64)
+         std::this_thread::sleep_for(std::chrono::microseconds(50));
+   }
+}
+
+int make_map(ungx_context *ctx, CUtensorMap *map, void *base, uint32_t rows, uint32_t cols, uint32_t box_rows)
+{
+   cuuint64_t dims[2] = {cols, rows};
+   cuuint64_t strides[1] = {cuuint64_t(cols) * sizeof(float)};
+   cuuint32_t box[2] = {32, box_rows};
+   cuuint32_t estr[2] = {1, 1};
+   const CUresult r = ctx->encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, estr,
+                                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+   if (r != CUDA_SUCCESS)
+      return fail(ctx, UNGX_ERR_CUDA, "cuTensorMapEncodeTiled failed with CUresult " + std::to_string((int)r));
+   return UNGX_OK;
+}
+
+// Copy host vectors to the device.  Pinned (or registered) memory goes in one
+// copy; pageable memory goes through two pinned staging buffers, alternating so the
+// host memcpy of one chunk overlaps the DMA of the other.
+int upload_vectors(ungx_context *ctx, float *dst, const float *src, size_t bytes)
+{
+   cudaPointerAttributes attr{};
+   const cudaError_t ae = cudaPointerGetAttributes(&attr, src);
+   if (ae == cudaSuccess && (attr.type == cudaMemoryTypeHost || attr.type == cudaMemoryTypeManaged))
+   {
+      UNGX_CUDA(ctx, cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, ctx->stream), "vector upload");
+      return UNGX_OK;
+   }
+   cudaGetLastError(); // clear a non-sticky attribute error for unregistered memory
+   const size_t chunk = size_t(64) << 20;
+   float *pin[2] = {nullptr, nullptr};
+   cudaEvent_t done[2] = {nullptr, nullptr};
+   int st = UNGX_OK;
+   for (int i = 0; i < 2 && st == UNGX_OK; ++i)
+   {
+      if (cudaHostAlloc(&pin[i], chunk, cudaHostAllocDefault) != cudaSuccess ||
+          cudaEventCreateWithFlags(&done[i], cudaEventDisableTiming) != cudaSuccess)
+         st = fail(ctx, UNGX_ERR_OOM, "pinned staging allocation failed");
+   }
+   for (size_t off = 0, i = 0; st == UNGX_OK && off < bytes; off += chunk, ++i)
+   {
+      const int b = int(i & 1);
+      if (i >= 2)
+         st = wait_event(ctx, done[b], "vector upload");
+      if (st != UNGX_OK)
+         break;
+      const size_t len = std::min(chunk, bytes - off);
+      std::memcpy(pin[b], reinterpret_cast<const char *>(src) + off, len);
+      cudaError_t e = cudaMemcpyAsync(reinterpret_cast<char *>(dst) + off, pin[b], len, cudaMemcpyHostToDevice,
+                                      ctx->stream);
+      if (e == cudaSuccess)
+         e = cudaEventRecord(done[b], ctx->stream);
+      if (e != cudaSuccess)
+         st = cuda_fail(ctx, e, "vector upload");
+   }
+   for (int i = 0; i < 2; ++i)
+      if (done[i])
+      {
+         if (st == UNGX_OK)
+            st = wait_event(ctx, done[i], "vector upload");
+         cudaEventDestroy(done[i]);
+      }
+   for (int i = 0; i < 2; ++i)
+      if (pin[i])
+         cudaFreeHost(pin[i]);
+   return st;
+}
+
+template <class T>
+int upload(ungx_context *ctx, DevBuf &buf, const std::vector<T> &v, const char *what)
+{
+   UNGX_CUDA(ctx, buf.ensure(v.size() * sizeof(T)), what);
+   if (!v.empty())
+      UNGX_CUDA(ctx, cudaMemcpyAsync(buf.p, v.data(), v.size() * sizeof(T), cudaMemcpyHostToDevice, ctx->stream),
+                what);
+   return UNGX_OK;
+}
+
+// The device half of generate: plan upload, kernels, counters.  Outputs are device
+// pointers.  Fills `timing` with device times.
+int run_generate(ungx_context *ctx, const ungx_cross_edge_problem &p, const Plan &plan, uint32_t *d_ids,
+                 float *d_dists, cudaStream_t s, ungx_cross_edge_timing &t)
+{
+   const uint32_t k = p.topk;
+   uint32_t route = p.route;
+   const int kp = ungx::tc_candidates_for_k(k);
+   if (route == UNGX_ROUTE_AUTO)
+      route = kp ? UNGX_ROUTE_TENSOR : UNGX_ROUTE_EXACT;
+   if (route == UNGX_ROUTE_TENSOR && !kp)
+      return fail(ctx, UNGX_ERR_INVALID_ARG,
+                  "tensor route supports k <= " + std::to_string(ungx::kTcMaxK) + "; use the exact route");
+   if (route == UNGX_ROUTE_EXACT && k > ungx::kExactMaxK)
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "k above " + std::to_string(ungx::kExactMaxK) + " is not supported");
+   if (route != UNGX_ROUTE_TENSOR && route != UNGX_ROUTE_EXACT)
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "unknown route");
+   t.route_used = route;
+   t.gpu_launches = 0;
+
+   cudaEvent_t *ev = ctx->ev;
+   UNGX_CUDA(ctx, cudaEventRecord(ev[0], s), "event");
+   // plan upload
+   std::vector<uint32_t> ranges(2 * size_t(p.num_groups + 1));
+   if (p.num_groups)
+      std::memcpy(ranges.data(), p.group_ranges, ranges.size() * sizeof(uint32_t));
+   int st;
+   if ((st = upload(ctx, ctx->items, plan.items, "plan upload")) ||
+       (st = upload(ctx, ctx->segs, plan.segs, "plan upload")) ||
+       (st = upload(ctx, ctx->empties, plan.empty_rows, "plan upload")) ||
+       (st = upload(ctx, ctx->ranges, ranges, "plan upload")))
+      return st;
+   uint64_t item_rows = 0;
+   for (const auto &it : plan.items)
+      item_rows += it.row_count;
+   UNGX_CUDA(ctx, ctx->counters.ensure(64), "counters");
+   UNGX_CUDA(ctx, cudaMemsetAsync(ctx->counters.p, 0, 64, s), "counters");
+   UNGX_CUDA(ctx, cudaEventRecord(ev[1], s), "event");
+
+   UNGX_CUDA(ctx, ungx::launch_fill_empty(ctx->empties.as<ungx::RowRange>(), (uint32_t)plan.empty_rows.size(), k,
+                                          d_ids, d_dists, s),
+             "fill kernel");
+   t.gpu_launches += plan.empty_rows.empty() ? 0 : 1;
+   uint32_t *cnt = ctx->counters.as<uint32_t>(); // [0] item counter [1] fb count [2] status, [4..7] u64 x2
+   int *status = reinterpret_cast<int *>(cnt + 2);
+   unsigned long long *stats = reinterpret_cast<unsigned long long *>(cnt + 4);
+
+   UNGX_CUDA(ctx, cudaEventRecord(ev[2], s), "event");
+   if (route == UNGX_ROUTE_TENSOR && !plan.items.empty())
+   {
+      UNGX_CUDA(ctx, ctx->gmax.ensure(sizeof(float) * (p.num_groups + 1)), "group norms");
+      UNGX_CUDA(ctx,
+                ungx::launch_group_maxnorm(ctx->xnorm.as<float>(), ctx->ranges.as<uint32_t>(), p.num_groups,
+                                           ctx->gmax.as<float>(), s),
+                "group norm kernel");
+      UNGX_CUDA(ctx, ctx->fb_rows.ensure(sizeof(uint32_t) * std::max<uint64_t>(item_rows, 1)), "fallback list");
+      UNGX_CUDA(ctx, ctx->fb_items.ensure(sizeof(uint32_t) * std::max<uint64_t>(item_rows, 1)), "fallback list");
+      ungx::TcMaps maps;
+      if ((st = make_map(ctx, &maps.a, ctx->Xp.p, ctx->n, ctx->dp, 128)))
+         return st;
+      for (int i = 0; i < 5; ++i)
+         if ((st = make_map(ctx, &maps.b[i], ctx->Xp.p, ctx->n, ctx->dp, 16u << i)))
+            return st;
+      ungx::TcParams tp{};
+      tp.items = ctx->items.as<ungx::WorkItem>();
+      tp.segs = ctx->segs.as<ungx::Segment>();
+      tp.num_items = (uint32_t)plan.items.size();
+      tp.item_counter = cnt + 0;
+      tp.X = ctx->X;
+      tp.xnorm = ctx->xnorm.as<float>();
+      tp.group_maxn2 = ctx->gmax.as<float>();
+      tp.n = ctx->n;
+      tp.d = ctx->d;
+      tp.dp = ctx->dp;
+      tp.k = k;
+      tp.out_ids = d_ids;
+      tp.out_dists = d_dists;
+      tp.fb_rows = ctx->fb_rows.as<uint32_t>();
+      tp.fb_items = ctx->fb_items.as<uint32_t>();
+      tp.fb_count = cnt + 1;
+      tp.counters = stats;
+      tp.status = status;
+      tp.timeout_ns = ctx->device_wait_ns;
+      ungx::tc_certificate_constants(ctx->d, ctx->dp, tp);
+      const uint32_t grid = (uint32_t)std::min<size_t>(plan.items.size(), (size_t)ctx->num_sms);
+      UNGX_CUDA(ctx, ungx::launch_tc(maps, tp, grid, s), "tensor-core kernel launch");
+      UNGX_CUDA(ctx, cudaEventRecord(ev[3], s), "event");
+      // rows the certificate rejected: exact rescan (count read on the device)
+      ungx::ExactParams ep{};
+      ep.items = tp.items;
+      ep.segs = tp.segs;
+      ep.X = ctx->X;
+      ep.d = ctx->d;
+      ep.k = k;
+      ep.rows = tp.fb_rows;
+      ep.row_items = tp.fb_items;
+      ep.count_dev = tp.fb_count;
+      ep.out_ids = d_ids;
+      ep.out_dists = d_dists;
+      UNGX_CUDA(ctx, ungx::launch_exact(ep, (uint32_t)ctx->num_sms * 4, s), "fallback kernel launch");
+      t.gpu_launches += 3;
+   }
+   else if (!plan.items.empty())
+   {
+      std::vector<uint32_t> rows, row_items;
+      rows.reserve(item_rows);
+      row_items.reserve(item_rows);
+      for (uint32_t i = 0; i < plan.items.size(); ++i)
+         for (uint32_t r = 0; r < plan.items[i].row_count; ++r)
+         {
+            rows.push_back(plan.items[i].row_begin + r);
+            row_items.push_back(i);
+         }
+      if ((st = upload(ctx, ctx->rows, rows, "row list")) || (st = upload(ctx, ctx->row_items, row_items, "row list")))
+         return st;
+      UNGX_CUDA(ctx, cudaEventRecord(ev[3], s), "event");
+      ungx::ExactParams ep{};
+      ep.items = ctx->items.as<ungx::WorkItem>();
+      ep.segs = ctx->segs.as<ungx::Segment>();
+      ep.X = ctx->X;
+      ep.d = ctx->d;
+      ep.k = k;
+      ep.rows = ctx->rows.as<uint32_t>();
+      ep.row_items = ctx->row_items.as<uint32_t>();
+      ep.count_host = (uint32_t)rows.size();
+      ep.out_ids = d_ids;
+      ep.out_dists = d_dists;
+      const uint32_t grid = (uint32_t)std::min<uint64_t>((rows.size() + 7) / 8, (uint64_t)ctx->num_sms * 16);
+      UNGX_CUDA(ctx, ungx::launch_exact(ep, std::max(grid, 1u), s), "exact kernel launch");
+      t.gpu_launches += 1;
+   }
+   else
+   {
+      UNGX_CUDA(ctx, cudaEventRecord(ev[3], s), "event");
+   }
+   UNGX_CUDA(ctx, cudaEventRecord(ev[4], s), "event");
+   UNGX_CUDA(ctx, cudaMemcpyAsync(ctx->h_counters, ctx->counters.p, 64, cudaMemcpyDeviceToHost, s), "counters");
+   UNGX_CUDA(ctx, cudaEventRecord(ev[5], s), "event");
+   if ((st = wait_event(ctx, ev[5], "cross-edge kernels")))
+      return st;
+   float a = 0, b = 0, c = 0;
+   cudaEventElapsedTime(&a, ev[0], ev[1]);
+   cudaEventElapsedTime(&b, ev[2], ev[4]);
+   cudaEventElapsedTime(&c, ev[2], ev[3]);
+   t.gpu_h2d_ms += a;
+   t.gpu_kernel_ms += b;
+   if (route == UNGX_ROUTE_TENSOR)
+   {
+      t.tc_kernel_ms += c;
+      float f = 0;
+      cudaEventElapsedTime(&f, ev[3], ev[4]);
+      t.fallback_ms += f;
+   }
+   const int dev_status = reinterpret_cast<const int *>(ctx->h_counters)[2];
+   const unsigned long long *hs = reinterpret_cast<const unsigned long long *>(ctx->h_counters + 4);
+   if (route == UNGX_ROUTE_TENSOR)
+   {
+      t.rows_certified = hs[0];
+      t.rows_fallback = hs[1];
+   }
+   else
+   {
+      t.rows_certified = 0;
+      t.rows_fallback = 0;
+   }
+   if (dev_status != 0)
+      return fail(ctx, dev_status, "tensor-core kernel reported status " + std::to_string(dev_status) +
+                                       " (a bounded device wait expired)");
+   return UNGX_OK;
+}
+} // namespace
+
+extern "C"
+{
+
+const char *ungx_status_string(int status)
+{
+   switch (status)
+   {
+   case UNGX_OK: return "ok";
+   case UNGX_ERR_INVALID_ARG: return "invalid argument";
+   case UNGX_ERR_OOM: return "out of memory";
+   case UNGX_ERR_CUDA: return "CUDA error";
+   case UNGX_ERR_TIMEOUT: return "timeout";
+   case UNGX_ERR_ABORTED: return "aborted";
+   case UNGX_ERR_NO_DEVICE: return "no usable device";
+   case UNGX_ERR_STATE: return "invalid call order";
+   default: return "unknown status";
+   }
+}
+
+const char *ungx_last_error(const ungx_context *ctx) { return ctx ? ctx->err.c_str() : ungx::global_error(); }
+
+int ungx_context_create(int device, ungx_context **out)
+{
+   if (!out)
+      return fail(nullptr, UNGX_ERR_INVALID_ARG, "ungx_context_create: null output");
+   *out = nullptr;
+   int count = 0;
+   cudaError_t e = cudaGetDeviceCount(&count);
+   if (e != cudaSuccess || count == 0)
+   {
+      cudaGetLastError();
+      return fail(nullptr, UNGX_ERR_NO_DEVICE, std::string("no CUDA device: ") + cudaGetErrorString(e));
+   }
+   if (device < 0 || device >= count)
+      return fail(nullptr, UNGX_ERR_INVALID_ARG, "device index out of range");
+   cudaDeviceProp prop{};
+   if ((e = cudaGetDeviceProperties(&prop, device)) != cudaSuccess)
+      return cuda_fail(nullptr, e, "cudaGetDeviceProperties");
+   if (prop.major != 10 || prop.minor != 0)
+      return fail(nullptr, UNGX_ERR_NO_DEVICE,
+                  "device is sm_" + std::to_string(prop.major) + std::to_string(prop.minor) +
+                      "; this build targets sm_100a (B200)");
+   auto ctx = std::make_unique<ungx_context>();
+   ctx->device = device;
+   ctx->num_sms = prop.multiProcessorCount;
+   if ((e = cudaSetDevice(device)) != cudaSuccess)
+      return cuda_fail(nullptr, e, "cudaSetDevice");
+   if ((e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking)) != cudaSuccess)
+      return cuda_fail(nullptr, e, "stream");
+   for (auto &ev : ctx->ev)
+      if ((e = cudaEventCreate(&ev)) != cudaSuccess)
+         return cuda_fail(nullptr, e, "event");
+   if ((e = cudaHostAlloc(&ctx->h_counters, 64, cudaHostAllocDefault)) != cudaSuccess)
+      return cuda_fail(nullptr, e, "pinned counters");
+   void *fn = nullptr;
+   cudaDriverEntryPointQueryResult q{};
+   if ((e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q)) != cudaSuccess ||
+       q != cudaDriverEntryPointSuccess || !fn)
+      return fail(nullptr, UNGX_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+   ctx->encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+   *out = ctx.release();
+   return UNGX_OK;
+}
+
+int ungx_context_destroy(ungx_context *ctx)
+{
+   if (!ctx)
+      return UNGX_OK;
+   cudaSetDevice(ctx->device);
+   if (ctx->stream)
+      cudaStreamSynchronize(ctx->stream);
+   ungx_release_base_vectors(ctx);
+   for (DevBuf *b : {&ctx->items, &ctx->segs, &ctx->empties, &ctx->ranges, &ctx->gmax, &ctx->counters,
+                     &ctx->fb_rows, &ctx->fb_items, &ctx->rows, &ctx->row_items, &ctx->out_ids, &ctx->out_dists,
+                     &ctx->stage[0], &ctx->stage[1]})
+      b->release();
+   for (auto &ev : ctx->ev)
+      if (ev)
+         cudaEventDestroy(ev);
+   if (ctx->h_counters)
+      cudaFreeHost(ctx->h_counters);
+   if (ctx->stream)
+      cudaStreamDestroy(ctx->stream);
+   delete ctx;
+   return UNGX_OK;
+}
+
+int ungx_set_timeout_ms(ungx_context *ctx, uint32_t timeout_ms)
+{
+   if (!ctx || timeout_ms == 0)
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "ungx_set_timeout_ms: bad argument");
+   ctx->timeout_ms = timeout_ms;
+   return UNGX_OK;
+}
+
+int ungx_set_device_wait_limit_ns(ungx_context *ctx, uint64_t limit_ns)
+{
+   if (!ctx || limit_ns == 0)
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "ungx_set_device_wait_limit_ns: bad argument");
+   ctx->device_wait_ns = limit_ns;
+   return UNGX_OK;
+}
+
+int ungx_prepare_base_vectors(ungx_context *ctx, const float *vectors, uint32_t n, uint32_t d, int on_device)
+{
+   if (!ctx)
+      return fail(nullptr, UNGX_ERR_INVALID_ARG, "null context");
+   if (!vectors || n == 0 || d == 0)
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "ungx_prepare_base_vectors: empty or null vectors");
+   UNGX_CUDA(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+   ungx_release_base_vectors(ctx);
+   const auto t0 = std::chrono::steady_clock::now();
+   const uint32_t dp = (d + 31) / 32 * 32;
+   const size_t xbytes = size_t(n) * d * sizeof(float);
+   if (on_device)
+      ctx->X = vectors;
+   else
+   {
+      UNGX_CUDA(ctx, ctx->X_owned.ensure(xbytes), "vector allocation");
+      int st = upload_vectors(ctx, ctx->X_owned.as<float>(), vectors, xbytes);
+      if (st)
+         return st;
+      ctx->X = ctx->X_owned.as<float>();
+   }
+   UNGX_CUDA(ctx, ctx->Xp.ensure(size_t(n) * dp * sizeof(float)), "operand allocation");
+   UNGX_CUDA(ctx, ctx->xnorm.ensure(size_t(n) * sizeof(float)), "norm allocation");
+   UNGX_CUDA(ctx, ctx->mean.ensure(size_t(d) * sizeof(float)), "mean allocation");
+   UNGX_CUDA(ctx, ctx->sums.ensure(size_t(d) * sizeof(double)), "mean allocation");
+   UNGX_CUDA(ctx, ungx::launch_colsum(ctx->X, n, d, ctx->sums.as<double>(), ctx->stream), "column-sum kernel");
+   UNGX_CUDA(ctx,
+             ungx::launch_center(ctx->X, ctx->sums.as<double>(), n, d, dp, ctx->mean.as<float>(), ctx->Xp.as<float>(),
+                                 ctx->xnorm.as<float>(), ctx->stream),
+             "centre kernel");
+   UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[6], ctx->stream), "event");
+   int st = wait_event(ctx, ctx->ev[6], "vector preparation");
+   if (st)
+      return st;
+   ctx->n = n;
+   ctx->d = d;
+   ctx->dp = dp;
+   ctx->have_vectors = true;
+   (void)t0;
+   return UNGX_OK;
+}
+
+int ungx_release_base_vectors(ungx_context *ctx)
+{
+   if (!ctx)
+      return UNGX_ERR_INVALID_ARG;
+   cudaSetDevice(ctx->device);
+   ctx->X_owned.release();
+   ctx->Xp.release();
+   ctx->xnorm.release();
+   ctx->mean.release();
+   ctx->sums.release();
+   ctx->X = nullptr;
+   ctx->have_vectors = false;
+   ctx->n = ctx->d = ctx->dp = 0;
+   return UNGX_OK;
+}
+
+int ungx_cross_edges_generate_device(ungx_context *ctx, const ungx_cross_edge_problem *problem, uint32_t *d_ids,
+                                     float *d_dists, void *stream, ungx_cross_edge_timing *timing)
+{
+   if (!ctx || !problem)
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "null argument");
+   if (!ctx->have_vectors)
+      return fail(ctx, UNGX_ERR_STATE, "call ungx_prepare_base_vectors first");
+   if (problem->num_points != ctx->n || problem->dim != ctx->d)
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "problem n/d differ from the prepared base vectors");
+   if (problem->num_points && !d_ids)
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "null output");
+   UNGX_CUDA(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+   const auto t0 = std::chrono::steady_clock::now();
+   ungx_cross_edge_timing t{};
+   Plan plan;
+   std::string err;
+   int st = ungx::build_plan(*problem, plan, err);
+   if (st)
+      return fail(ctx, st, "invalid problem: " + err);
+   t.plan_ms = ms_since(t0);
+   t.pairs = plan.pairs;
+   cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+   st = run_generate(ctx, *problem, plan, d_ids, d_dists, s, t);
+   t.generate_ms = ms_since(t0);
+   if (timing)
+      *timing = t;
+   return st;
+}
+
+int ungx_cross_edges_generate(ungx_context *ctx, const ungx_cross_edge_problem *problem, uint32_t *out_ids,
+                              float *out_dists, ungx_cross_edge_timing *timing)
+{
+   if (!ctx || !problem)
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "null argument");
+   if (!ctx->have_vectors)
+      return fail(ctx, UNGX_ERR_STATE, "call ungx_prepare_base_vectors first");
+   if (problem->num_points != ctx->n || problem->dim != ctx->d)
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "problem n/d differ from the prepared base vectors");
+   if (problem->num_points && !out_ids)
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "null output");
+   UNGX_CUDA(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+   const auto t0 = std::chrono::steady_clock::now();
+   ungx_cross_edge_timing t{};
+   Plan plan;
+   std::string err;
+   int st = ungx::build_plan(*problem, plan, err);
+   if (st)
+      return fail(ctx, st, "invalid problem: " + err);
+   t.plan_ms = ms_since(t0);
+   t.pairs = plan.pairs;
+   const size_t nk = size_t(problem->num_points) * problem->topk;
+   UNGX_CUDA(ctx, ctx->out_ids.ensure(nk * sizeof(uint32_t)), "output allocation");
+   UNGX_CUDA(ctx, ctx->out_dists.ensure(nk * sizeof(float)), "output allocation");
+   st = run_generate(ctx, *problem, plan, ctx->out_ids.as<uint32_t>(), ctx->out_dists.as<float>(), ctx->stream, t);
+   if (st)
+      return st;
+   // device -> host: whole rows of this shard's work
+   const uint32_t k = problem->topk;
+   UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[6], ctx->stream), "event");
+   auto copy_rows = [&](uint32_t begin, uint32_t count) -> int {
+      const size_t off = size_t(begin) * k, len = size_t(count) * k;
+      UNGX_CUDA(ctx,
+                cudaMemcpyAsync(out_ids + off, ctx->out_ids.as<uint32_t>() + off, len * sizeof(uint32_t),
+                                cudaMemcpyDeviceToHost, ctx->stream),
+                "output copy");
+      if (out_dists)
+         UNGX_CUDA(ctx,
+                   cudaMemcpyAsync(out_dists + off, ctx->out_dists.as<float>() + off, len * sizeof(float),
+                                   cudaMemcpyDeviceToHost, ctx->stream),
+                   "output copy");
+      return UNGX_OK;
+   };
+   if (problem->shard_count <= 1)
+   {
+      if ((st = copy_rows(0, problem->num_points)))
+         return st;
+   }
+   else
+   {
+      // merge adjacent row ranges of this shard into few copies
+      std::vector<ungx::RowRange> rr;
+      for (const auto &it : plan.items)
+         rr.push_back({it.row_begin, it.row_count});
+      rr.insert(rr.end(), plan.empty_rows.begin(), plan.empty_rows.end());
+      std::sort(rr.begin(), rr.end(), [](const ungx::RowRange &a, const ungx::RowRange &b) { return a.begin < b.begin; });
+      for (size_t i = 0; i < rr.size();)
+      {
+         uint32_t b = rr[i].begin, e = rr[i].begin + rr[i].count;
+         size_t j = i + 1;
+         while (j < rr.size() && rr[j].begin == e)
+            e += rr[j++].count;
+         if ((st = copy_rows(b, e - b)))
+            return st;
+         i = j;
+      }
+   }
+   UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[7], ctx->stream), "event");
+   if ((st = wait_event(ctx, ctx->ev[7], "output copy")))
+      return st;
+   float d2h = 0;
+   cudaEventElapsedTime(&d2h, ctx->ev[6], ctx->ev[7]);
+   t.gpu_d2h_ms = d2h;
+   t.generate_ms = ms_since(t0);
+   if (timing)
+      *timing = t;
+   return UNGX_OK;
+}
+
+int ungx_cross_edges_build(ungx_context *ctx, const float *vectors, const ungx_cross_edge_problem *problem,
+                           uint32_t *out_ids, float *out_dists, ungx_cross_edge_timing *timing)
+{
+   if (!ctx || !problem)
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "null argument");
+   const auto t0 = std::chrono::steady_clock::now();
+   int st = ungx_prepare_base_vectors(ctx, vectors, problem->num_points, problem->dim, 0);
+   if (st)
+      return st;
+   const double prep = ms_since(t0);
+   ungx_cross_edge_timing t{};
+   st = ungx_cross_edges_generate(ctx, problem, out_ids, out_dists, &t);
+   ungx_release_base_vectors(ctx);
+   t.prepare_ms = prep;
+   t.generate_ms = ms_since(t0);
+   if (timing)
+      *timing = t;
+   return st;
+}
+
+} // extern "C"

@@ -1,0 +1,66 @@
+// Internal declarations shared by the host (.cpp) and device (.cu) halves of libungx.
+#pragma once
+
+#include <cstdint>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../include/ungx.h"
+
+namespace ungx
+{
+
+// Thread-local message for calls that have no context (label graph, planning).
+void set_global_error(const std::string &msg);
+const char *global_error();
+
+// Run body(i) for i in [0, count) on up to `threads` std::threads, dynamic chunks.
+template <class F>
+void parallel_for(int64_t count, int threads, int64_t chunk, F &&body);
+
+// ------------------------------------------------------------------ planning
+// One unit of device work: <=128 consecutive rows of one source group f, paired
+// with every target group of out(f).  Source-centric, so a row's final top-k is
+// produced by exactly one CTA and written once (no merge, no locks).
+struct WorkItem
+{
+   uint32_t row_begin;
+   uint32_t row_count;  // 1..128
+   uint32_t seg_begin;  // into Plan::segs
+   uint32_t seg_count;
+};
+
+// A target group's contiguous row range (one LNG edge f -> f').
+struct Segment
+{
+   uint32_t x_begin;
+   uint32_t x_count;
+   uint32_t group_id;
+   uint32_t pad;
+};
+
+struct RowRange
+{
+   uint32_t begin, count;
+};
+
+struct Plan
+{
+   std::vector<WorkItem> items;       // this shard's items, longest first
+   std::vector<Segment> segs;
+   std::vector<RowRange> empty_rows;  // this shard's rows that get no candidates
+   uint64_t pairs = 0;                // sum |f|*|f'| over this shard's rows
+   uint64_t padded_cols = 0;          // sum over items of sum roundup16(|f'|)
+   uint32_t max_item_cols = 0;
+};
+
+constexpr uint32_t kRowsPerItem = 128;
+
+// Validates the problem and builds this shard's plan.  Returns UNGX_OK or an error
+// status with a message in `err`.
+int build_plan(const ungx_cross_edge_problem &p, Plan &plan, std::string &err);
+
+} // namespace ungx
+
+#include "ungx_parallel.inl"

@@ -1,0 +1,191 @@
+/*
+ * ungx.h -- C ABI of the B200 UNG cross-group edge builder.
+ *
+ * Drop-in for the cross-edge generation step of UNG index construction in
+ * panjd123/FilterVectorCode_refactor.  Plain pointers and sizes only; every
+ * buffer passed in is owned by the caller and is never freed by the library.
+ * All functions return an int status (UNGX_OK == 0, negative on error) and leave
+ * a message retrievable with ungx_last_error().
+ *
+ * Id spaces follow the reference: vectors are addressed by their REORDERED id
+ * (groups contiguous, group 1 first), exactly as UniNavGraph sees them after
+ * prepare_group_storages_graphs (UNG/codes/src/uni_nav_graph.cpp:148-169).
+ * Groups are numbered 1..G; index 0 of every per-group array is unused.
+ */
+#ifndef UNGX_H
+#define UNGX_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ status */
+enum
+{
+   UNGX_OK = 0,
+   UNGX_ERR_INVALID_ARG = -1,  /* bad size, null pointer, unsupported shape */
+   UNGX_ERR_OOM = -2,          /* device or host allocation failed */
+   UNGX_ERR_CUDA = -3,         /* CUDA runtime / driver error */
+   UNGX_ERR_TIMEOUT = -4,      /* a bounded device wait ran out */
+   UNGX_ERR_ABORTED = -5,      /* a kernel reported an internal consistency error */
+   UNGX_ERR_NO_DEVICE = -6,    /* no usable sm_100 device */
+   UNGX_ERR_STATE = -7         /* call order violated (e.g. no base vectors prepared) */
+};
+
+/* Writeback modes of the reference, CrossEdgeGpuWritebackMode
+ * (UNG/codes/include/ung_cross_edge_config.h:17-22).  The C ABI always emits the
+ * flat layout; the C++ adapter (ungx_ung_adapter.hpp) materialises the others. */
+enum
+{
+   UNGX_WRITEBACK_SEARCH_QUEUE = 0,
+   UNGX_WRITEBACK_ID_VECTOR = 1,
+   UNGX_WRITEBACK_FLAT_ID = 2
+};
+
+/* Route selection for ungx_cross_edges_generate. */
+enum
+{
+   UNGX_ROUTE_AUTO = 0,        /* tensor-core prefilter + exact rerank when k allows, else exact */
+   UNGX_ROUTE_TENSOR = 1,      /* tcgen05 TF32 prefilter + certified exact fp32 rerank */
+   UNGX_ROUTE_EXACT = 2        /* CUDA-core exact scan in the reference's summation order */
+};
+
+typedef struct ungx_context ungx_context;
+typedef struct ungx_label_graph ungx_label_graph;
+
+/* Mirrors CrossEdgeBuildTiming (UNG/codes/include/ung_cross_edge_result.h:15-28)
+ * for the fields this step owns, plus the breakdown of the device work. */
+typedef struct
+{
+   double generate_ms;   /* whole call, host wall clock */
+   double gpu_h2d_ms;    /* host -> device copies (vectors, plan) */
+   double gpu_kernel_ms; /* device time of the generate kernels (CUDA events) */
+   double gpu_d2h_ms;    /* device -> host copies of ids / dists */
+   double plan_ms;       /* host work-item planning */
+   double prepare_ms;    /* centring / rounding / norm kernels */
+   double tc_kernel_ms;  /* tensor-core prefilter kernel alone */
+   double fallback_ms;   /* exact rescan of rows the certificate rejected */
+   uint64_t pairs;       /* sum over LNG edges f->f' of |f|*|f'| (the reference's dim_ops / dim) */
+   uint64_t rows_certified;
+   uint64_t rows_fallback;
+   uint32_t route_used;  /* UNGX_ROUTE_TENSOR or UNGX_ROUTE_EXACT */
+   uint32_t gpu_launches;/* kernels this call launched */
+} ungx_cross_edge_timing;
+
+/* The inputs UniNavGraph::build_cross_edges_generate_gpu_optimized reads
+ * (UNG/codes/include/uni_nav_graph.h:403-407, UNG/codes/src/uni_nav_graph_cross_edges.cpp:334-440). */
+typedef struct
+{
+   uint32_t num_points;        /* n */
+   uint32_t dim;               /* d */
+   uint32_t topk;              /* k = _num_cross_edges */
+   uint32_t num_groups;        /* G */
+   const uint32_t *group_ranges;   /* [2*(G+1)]: group g owns rows [ranges[2g], ranges[2g+1]);
+                                      the memory layout of std::vector<std::pair<IdxType,IdxType>>
+                                      _group_id_to_range */
+   const uint64_t *lng_out_offsets;/* [G+2]: out-neighbours (minimal supersets) of g are */
+   const uint32_t *lng_out_ids;    /*        lng_out_ids[off[g] .. off[g+1]) */
+   const uint8_t *skip_source_group;/* optional [G+1]: non-zero = do not emit cross edges for
+                                      the group's vectors (special-block trivial roots,
+                                      UNG/codes/src/gpu_gemm_topk.cu:399-412); may be NULL */
+   uint32_t route;             /* UNGX_ROUTE_* */
+   uint32_t shard_rank;        /* work-item shard this call computes (0 for one GPU) */
+   uint32_t shard_count;       /* number of shards (1 for one GPU) */
+} ungx_cross_edge_problem;
+
+/* ---------------------------------------------------------------- context */
+int ungx_context_create(int device, ungx_context **out);
+int ungx_context_destroy(ungx_context *ctx);
+const char *ungx_last_error(const ungx_context *ctx);
+const char *ungx_status_string(int status);
+/* Bounded-wait limit (milliseconds) for every host wait on device work. */
+int ungx_set_timeout_ms(ungx_context *ctx, uint32_t timeout_ms);
+/* Limit (nanoseconds, default 4e9) of each spin wait inside the tensor-core kernel
+ * (pipeline barriers between its producer, MMA and epilogue warps).  A wait that
+ * runs out makes the kernel stop issuing work, drain what is in flight, free its
+ * tensor memory and report UNGX_ERR_TIMEOUT; the context stays usable. */
+int ungx_set_device_wait_limit_ns(ungx_context *ctx, uint64_t limit_ns);
+
+/* ------------------------------------------ a4: resident base vectors + norms
+ * Replaces gpu_prepare_all_vectors_on_device
+ * (UNG/codes/src/gpu_cross_edge_resident_vectors.cuh:10-215): one upload of the
+ * reordered n x d fp32 matrix, then the device builds the tensor-core operand
+ * (centred, TF32-rounded, zero-padded to a multiple of 32 columns) and the row
+ * norms.  `vectors_on_device` != 0 means `vectors` is a device pointer that stays
+ * valid until ungx_release_base_vectors (no copy is made of it). */
+int ungx_prepare_base_vectors(ungx_context *ctx, const float *vectors, uint32_t num_points, uint32_t dim,
+                              int vectors_on_device);
+/* Replaces gpu_release_all_vectors_on_device. */
+int ungx_release_base_vectors(ungx_context *ctx);
+
+/* ------------------------------------- a6-a11: the cross-edge generate step
+ * Replaces build_cross_edges_generate_gpu_optimized's device work
+ * (UNG/codes/src/uni_nav_graph_cross_edges.cpp:334-440 and the GPU routes under it,
+ * UNG/codes/src/gpu_gemm_topk.cu:377-970).  For every vector v of every group f
+ * with out(f) non-empty, row v of the output receives the k nearest vectors (squared
+ * L2, the reference's fp32 summation order) over the union of the groups in
+ * out(f), sorted by (distance, id) ascending -- the content of the reference's
+ * SearchQueue after the exact scan.  Slots past the number of candidates, and every
+ * slot of a row whose group has no out-neighbour, hold id UINT32_MAX and distance
+ * +inf (the FlatId writeback sentinel of UNG/codes/src/ung_cross_edge_output_writer.cpp:78-88).
+ *
+ * `out_ids` [n*k] and `out_dists` [n*k] (may be NULL) are HOST buffers.  With
+ * shard_count > 1 only the rows of this shard's work items are written; the other
+ * rows are left untouched. */
+int ungx_cross_edges_generate(ungx_context *ctx, const ungx_cross_edge_problem *problem, uint32_t *out_ids,
+                              float *out_dists, ungx_cross_edge_timing *timing);
+
+/* Same, with DEVICE output buffers on the context's device.  `stream` is a
+ * cudaStream_t (NULL = the context's own stream); the call returns after the
+ * work completed (bounded wait). */
+int ungx_cross_edges_generate_device(ungx_context *ctx, const ungx_cross_edge_problem *problem,
+                                     uint32_t *d_out_ids, float *d_out_dists, void *stream,
+                                     ungx_cross_edge_timing *timing);
+
+/* One call = prepare + generate + release with host buffers: the whole step as
+ * the reference's UniNavGraph calls it. */
+int ungx_cross_edges_build(ungx_context *ctx, const float *vectors, const ungx_cross_edge_problem *problem,
+                           uint32_t *out_ids, float *out_dists, ungx_cross_edge_timing *timing);
+
+/* Rows (reordered vector ids) this shard owns, ascending; `*count` receives the
+ * number.  `rows` may be NULL to query the count only. */
+int ungx_shard_rows(const ungx_cross_edge_problem *problem, uint32_t *rows, uint64_t *count);
+
+/* ---------------------------------------------- a16: grouping + reorder + LNG
+ * build_trie_and_divide_groups (UNG/codes/src/uni_nav_graph_label_graph.cpp:21-43),
+ * the reorder of prepare_group_storages_graphs (UNG/codes/src/uni_nav_graph.cpp:148-169)
+ * and the minimal-superset label navigating graph
+ * (UNG/codes/src/uni_nav_graph_label_graph.cpp:103-206, 851-911).
+ * Labels are CSR: vector i (original id) carries labels[label_offsets[i] .. label_offsets[i+1]),
+ * in any order (they are sorted, as Storage::load_from_file does).  Group ids follow
+ * the first appearance of each exact sorted label sequence. */
+int ungx_label_graph_build(uint32_t num_points, const uint64_t *label_offsets, const uint32_t *labels,
+                           int num_threads, ungx_label_graph **out);
+int ungx_label_graph_destroy(ungx_label_graph *lg);
+uint32_t ungx_label_graph_num_groups(const ungx_label_graph *lg);
+uint64_t ungx_label_graph_num_edges(const ungx_label_graph *lg);
+/* new_to_old [n]; group_ranges [2*(G+1)] as in ungx_cross_edge_problem. */
+int ungx_label_graph_copy_groups(const ungx_label_graph *lg, uint32_t *new_to_old, uint32_t *group_ranges);
+/* out-neighbours (ascending group id within a group): offsets [G+2], ids [num_edges]. */
+int ungx_label_graph_copy_out_neighbors(const ungx_label_graph *lg, uint64_t *offsets, uint32_t *ids);
+/* in-neighbours, ascending source id (uni_nav_graph_label_graph.cpp:889-906). */
+int ungx_label_graph_copy_in_neighbors(const ungx_label_graph *lg, uint64_t *offsets, uint32_t *ids);
+/* label set of each group as CSR: offsets [G+2], labels [offsets[G+1]]. */
+uint64_t ungx_label_graph_num_set_labels(const ungx_label_graph *lg);
+int ungx_label_graph_copy_label_sets(const ungx_label_graph *lg, uint64_t *offsets, uint32_t *labels);
+
+/* ------------------------------------------- a14: CSR of the cross edges
+ * CrossEdgeGraphMaterializationWriter::build_csr_adjacency
+ * (UNG/codes/src/ung_cross_edge_output_writer.cpp:44-66) from the flat output:
+ * row_offsets [n+1], col_indices [row_offsets[n]] (skip UINT32_MAX slots). */
+int ungx_flat_to_csr(const uint32_t *flat_ids, uint32_t num_points, uint32_t topk, uint64_t *row_offsets,
+                     uint32_t *col_indices);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* UNGX_H */

@@ -1,0 +1,172 @@
+"""TEST INFRASTRUCTURE ONLY: ctypes access to the CPU checkers.
+
+* ``_build/libungx_oracle.so`` -- the plain-C restatement (ungx_oracle.c), always built.
+* ``_ref/libungref.so``        -- the reference's own leaf sources (TrieIndex, SearchQueue,
+  FloatL2DistanceHandler) compiled where they lie, plus ref_harness.cpp; present
+  only where the reference tree was available at build time.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg import this.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import c_float, c_int, c_uint8, c_uint32, c_uint64, c_void_p
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "_build", "libungx_oracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libungref.so")
+
+# FloatL2DistanceHandler's rounding in the reference's release build: the 8-lane
+# loop rounds mul and add separately, the tails are fused (bit 1).
+L2_REFERENCE_BUILD = 2
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data
+
+
+class _Lib:
+    def __init__(self, path: str, prefix: str):
+        self.lib = ctypes.CDLL(path)
+        self.prefix = prefix
+        L, P = self.lib, prefix
+        getattr(L, f"{P}label_graph_build").restype = c_void_p
+        getattr(L, f"{P}label_graph_build").argtypes = [c_uint32, c_void_p, c_void_p]
+        getattr(L, f"{P}num_groups").restype = c_uint32
+        getattr(L, f"{P}num_groups").argtypes = [c_void_p]
+        getattr(L, f"{P}copy_groups").argtypes = [c_void_p, c_void_p, c_void_p]
+        getattr(L, f"{P}lng_nnz").restype = c_uint64
+        getattr(L, f"{P}lng_nnz").argtypes = [c_void_p]
+        getattr(L, f"{P}copy_lng_out").argtypes = [c_void_p, c_void_p, c_void_p]
+        getattr(L, f"{P}label_graph_free").argtypes = [c_void_p]
+
+    def label_graph(self, label_offsets: np.ndarray, labels: np.ndarray) -> dict:
+        P = self.prefix
+        label_offsets = np.ascontiguousarray(label_offsets, dtype=np.uint64)
+        labels = np.ascontiguousarray(labels, dtype=np.uint32)
+        n = label_offsets.shape[0] - 1
+        h = getattr(self.lib, f"{P}label_graph_build")(n, _p(label_offsets), _p(labels) if labels.size else None)
+        try:
+            G = getattr(self.lib, f"{P}num_groups")(h)
+            new_to_old = np.empty(n, dtype=np.uint32)
+            first = np.empty(G + 2, dtype=np.uint32)
+            getattr(self.lib, f"{P}copy_groups")(h, _p(new_to_old), _p(first))
+            nnz = getattr(self.lib, f"{P}lng_nnz")(h)
+            off = np.empty(G + 2, dtype=np.uint64)
+            ids = np.empty(max(nnz, 1), dtype=np.uint32)
+            getattr(self.lib, f"{P}copy_lng_out")(h, _p(off), _p(ids))
+        finally:
+            getattr(self.lib, f"{P}label_graph_free")(h)
+        ranges = np.zeros(2 * (G + 1), dtype=np.uint32)
+        ranges[2::2] = first[1:G + 1]
+        ranges[3::2] = first[2:G + 2]
+        return dict(num_groups=G, new_to_old=new_to_old, group_first=first, group_ranges=ranges,
+                    out_offsets=off, out_ids=ids[:nnz])
+
+
+class Oracle(_Lib):
+    """The plain-C restatement."""
+
+    def __init__(self, path: str = ORACLE_SO):
+        super().__init__(path, "orc_")
+        L = self.lib
+        L.orc_l2.restype = c_float
+        L.orc_l2.argtypes = [c_void_p, c_void_p, c_uint32, c_int]
+        L.orc_cross_rows.restype = None
+        L.orc_cross_rows.argtypes = [c_void_p, c_uint32, c_uint32, c_uint32, c_uint32, c_void_p, c_void_p,
+                                     c_void_p, c_void_p, c_uint64, c_int, c_int, c_void_p, c_void_p]
+        L.orc_cross_exact.restype = c_uint64
+        L.orc_cross_exact.argtypes = [c_void_p, c_uint32, c_uint32, c_uint32, c_uint32, c_void_p, c_void_p,
+                                      c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]
+
+    def l2(self, a: np.ndarray, b: np.ndarray, fused: int = L2_REFERENCE_BUILD) -> float:
+        a = np.ascontiguousarray(a, dtype=np.float32)
+        b = np.ascontiguousarray(b, dtype=np.float32)
+        return self.lib.orc_l2(_p(a), _p(b), a.shape[0], fused)
+
+    def cross_exact(self, X: np.ndarray, k: int, group_first: np.ndarray, out_offsets: np.ndarray,
+                    out_ids: np.ndarray, source_mask: np.ndarray | None = None, num_threads: int = 0,
+                    fused: int = L2_REFERENCE_BUILD):
+        X = np.ascontiguousarray(X, dtype=np.float32)
+        n, d = X.shape
+        G = group_first.shape[0] - 2
+        gf = np.ascontiguousarray(group_first, dtype=np.uint32)
+        oo = np.ascontiguousarray(out_offsets, dtype=np.uint64)
+        oi = np.ascontiguousarray(out_ids, dtype=np.uint32)
+        if oi.size == 0:
+            oi = np.zeros(1, dtype=np.uint32)
+        sm = None if source_mask is None else np.ascontiguousarray(source_mask, dtype=np.uint8)
+        ids = np.empty(n * k, dtype=np.uint32)
+        dists = np.empty(n * k, dtype=np.float32)
+        pairs = self.lib.orc_cross_exact(_p(X), n, d, k, G, _p(gf), _p(oo), _p(oi), _p(sm), num_threads, fused,
+                                         _p(ids), _p(dists))
+        return ids, dists, int(pairs)
+
+
+    def cross_rows(self, X: np.ndarray, k: int, group_first: np.ndarray, out_offsets: np.ndarray,
+                   out_ids: np.ndarray, rows: np.ndarray, num_threads: int = 0, fused: int = L2_REFERENCE_BUILD):
+        """Exact top-k of the listed rows only; returns ids/dists of shape [len(rows), k]."""
+        X = np.ascontiguousarray(X, dtype=np.float32)
+        n, d = X.shape
+        G = group_first.shape[0] - 2
+        gf = np.ascontiguousarray(group_first, dtype=np.uint32)
+        oo = np.ascontiguousarray(out_offsets, dtype=np.uint64)
+        oi = np.ascontiguousarray(out_ids, dtype=np.uint32)
+        if oi.size == 0:
+            oi = np.zeros(1, dtype=np.uint32)
+        rows = np.ascontiguousarray(rows, dtype=np.uint32)
+        ids = np.empty((rows.size, k), dtype=np.uint32)
+        dists = np.empty((rows.size, k), dtype=np.float32)
+        self.lib.orc_cross_rows(_p(X), n, d, k, G, _p(gf), _p(oo), _p(oi), _p(rows), rows.size, num_threads,
+                                fused, _p(ids), _p(dists))
+        return ids, dists
+
+
+class Reference(_Lib):
+    """The reference's own compiled code behind ref_harness.cpp."""
+
+    def __init__(self, path: str = REF_SO):
+        super().__init__(path, "ungref_")
+        L = self.lib
+        L.ungref_label_graph_build.restype = c_void_p
+        L.ungref_l2.restype = c_float
+        L.ungref_l2.argtypes = [c_void_p, c_void_p, c_uint32]
+        L.ungref_cross_exact.restype = c_uint64
+        L.ungref_cross_exact.argtypes = [c_void_p, c_uint32, c_uint32, c_uint32, c_uint32, c_void_p, c_void_p,
+                                         c_void_p, c_void_p, c_int, c_void_p, c_void_p]
+
+    def l2(self, a: np.ndarray, b: np.ndarray) -> float:
+        a = np.ascontiguousarray(a, dtype=np.float32)
+        b = np.ascontiguousarray(b, dtype=np.float32)
+        return self.lib.ungref_l2(_p(a), _p(b), a.shape[0])
+
+    def cross_exact(self, X, k, group_first, out_offsets, out_ids, source_mask=None, num_threads: int = 0):
+        X = np.ascontiguousarray(X, dtype=np.float32)
+        n, d = X.shape
+        G = group_first.shape[0] - 2
+        gf = np.ascontiguousarray(group_first, dtype=np.uint32)
+        oo = np.ascontiguousarray(out_offsets, dtype=np.uint64)
+        oi = np.ascontiguousarray(out_ids, dtype=np.uint32)
+        if oi.size == 0:
+            oi = np.zeros(1, dtype=np.uint32)
+        sm = None if source_mask is None else np.ascontiguousarray(source_mask, dtype=np.uint8)
+        ids = np.empty(n * k, dtype=np.uint32)
+        dists = np.empty(n * k, dtype=np.float32)
+        pairs = self.lib.ungref_cross_exact(_p(X), n, d, k, G, _p(gf), _p(oo), _p(oi), _p(sm), num_threads,
+                                            _p(ids), _p(dists))
+        return ids, dists, int(pairs)
+
+
+def oracle() -> Oracle:
+    return Oracle()
+
+
+def reference() -> Reference | None:
+    return Reference() if os.path.exists(REF_SO) else None
+
+
+def lng_sets(out_offsets: np.ndarray, out_ids: np.ndarray, num_groups: int) -> list[frozenset]:
+    return [frozenset(out_ids[out_offsets[g]:out_offsets[g + 1]].tolist()) for g in range(num_groups + 1)]

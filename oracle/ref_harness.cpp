@@ -1,0 +1,263 @@
+// TEST INFRASTRUCTURE ONLY -- never linked into the product library.
+//
+// Harness around the reference's own compiled leaf code (TrieIndex, SearchQueue,
+// FloatL2DistanceHandler) from panjd123/FilterVectorCode_refactor.  It restates,
+// step by step, the UniNavGraph member functions that the cross-edge path reads
+// and runs, so that the reference's numerics and tie rules decide the oracle's
+// answers:
+//
+//   grouping   UNG/codes/src/uni_nav_graph_label_graph.cpp:21-43  (build_trie_and_divide_groups)
+//   reorder    UNG/codes/src/uni_nav_graph.cpp:148-169            (prepare_group_storages_graphs)
+//   LNG        UNG/codes/src/uni_nav_graph_label_graph.cpp:103-206, 851-911
+//              (get_min_super_sets_optimized_bucket + build_label_nav_graph_optimized_phase1)
+//   cross scan UNG/codes/src/uni_nav_graph_cross_edges.cpp:32-57, 154-220
+//              (append_cross_edges_from_target_range + build_cross_edges_generate_cpu_exact_scan)
+//
+// The reference sources themselves are compiled from where they lie by
+// oracle/Makefile into oracle/_ref/; nothing from them is copied here.
+#include <omp.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <limits>
+#include <memory>
+#include <vector>
+
+#include "distance.h"
+#include "search_queue.h"
+#include "trie.h"
+
+using ANNS::IdxType;
+using ANNS::LabelType;
+
+namespace
+{
+struct RefLabelGraph
+{
+   uint32_t num_points = 0;
+   uint32_t num_groups = 0;
+   ANNS::TrieIndex trie;
+   std::vector<std::vector<IdxType>> group_vec_ids;        // [G+1]
+   std::vector<std::vector<LabelType>> group_label_set;    // [G+1]
+   std::vector<uint32_t> new_to_old;                       // [n]
+   std::vector<uint32_t> group_first;                      // [G+2]
+   std::vector<std::vector<IdxType>> out_neighbors;        // [G+1]
+};
+
+// Minimal-superset filter in the bucket order the reference uses
+// (uni_nav_graph_label_graph.cpp:103-206): candidates come from the reference
+// trie's own superset search; they are visited by increasing label-set size and a
+// candidate is kept unless it includes an already kept set.
+void min_super_sets(const RefLabelGraph &g, const std::vector<LabelType> &query, std::vector<IdxType> &out)
+{
+   out.clear();
+   std::vector<std::shared_ptr<ANNS::TrieNode>> cands;
+   g.trie.get_super_set_entrances(query, cands, true, true);
+   if (cands.empty())
+      return;
+   if (cands.size() == 1)
+   {
+      out.push_back(cands[0]->group_id);
+      return;
+   }
+   LabelType min_size = cands[0]->label_set_size, max_size = min_size;
+   for (auto &c : cands)
+   {
+      min_size = std::min(min_size, c->label_set_size);
+      max_size = std::max(max_size, c->label_set_size);
+   }
+   std::vector<const std::vector<LabelType> *> kept;
+   auto consider = [&](const ANNS::TrieNode *c) {
+      const auto &ls = g.group_label_set[c->group_id];
+      bool is_min = true;
+      if (c->label_set_size > min_size)
+         for (auto *m : kept)
+            if (std::includes(ls.begin(), ls.end(), m->begin(), m->end()))
+            {
+               is_min = false;
+               break;
+            }
+      if (is_min)
+      {
+         out.push_back(c->group_id);
+         kept.push_back(&ls);
+      }
+   };
+   if (max_size - min_size <= 256)
+   {
+      std::vector<std::vector<const ANNS::TrieNode *>> buckets(max_size - min_size + 1);
+      for (auto &c : cands)
+         buckets[c->label_set_size - min_size].push_back(c.get());
+      for (auto &b : buckets)
+         for (auto *c : b)
+            consider(c);
+   }
+   else
+   {
+      std::vector<const ANNS::TrieNode *> sorted;
+      for (auto &c : cands)
+         sorted.push_back(c.get());
+      std::sort(sorted.begin(), sorted.end(),
+                [](const ANNS::TrieNode *a, const ANNS::TrieNode *b) { return a->label_set_size < b->label_set_size; });
+      for (auto *c : sorted)
+         consider(c);
+   }
+}
+} // namespace
+
+extern "C"
+{
+
+// Labels arrive as CSR: point i owns labels[label_offsets[i] .. label_offsets[i+1]).
+// Each point's labels are sorted ascending first, as Storage::load_from_file does
+// (UNG/codes/src/storage.cpp:133-146).
+void *ungref_label_graph_build(uint32_t num_points, const uint64_t *label_offsets, const uint32_t *labels)
+{
+   auto *g = new RefLabelGraph();
+   g->num_points = num_points;
+   IdxType next_group_id = 1;
+   std::vector<LabelType> ls;
+   for (uint32_t v = 0; v < num_points; ++v)
+   {
+      ls.assign(labels + label_offsets[v], labels + label_offsets[v + 1]);
+      std::sort(ls.begin(), ls.end());
+      IdxType gid = g->trie.insert(ls, next_group_id);
+      if (gid + 1 > g->group_vec_ids.size())
+      {
+         g->group_vec_ids.resize(gid + 1);
+         g->group_label_set.resize(gid + 1);
+         g->group_label_set[gid] = ls;
+      }
+      g->group_vec_ids[gid].push_back(v);
+   }
+   g->num_groups = next_group_id - 1;
+   g->group_vec_ids.resize(g->num_groups + 1);
+   g->group_label_set.resize(g->num_groups + 1);
+
+   g->new_to_old.resize(num_points);
+   g->group_first.assign(g->num_groups + 2, 0);
+   uint32_t nid = 0;
+   for (uint32_t gid = 1; gid <= g->num_groups; ++gid)
+   {
+      g->group_first[gid] = nid;
+      for (auto old : g->group_vec_ids[gid])
+         g->new_to_old[nid++] = old;
+   }
+   g->group_first[g->num_groups + 1] = nid;
+
+   g->out_neighbors.assign(g->num_groups + 1, {});
+#pragma omp parallel for schedule(dynamic, 64)
+   for (long long gid = 1; gid <= (long long)g->num_groups; ++gid)
+      min_super_sets(*g, g->group_label_set[gid], g->out_neighbors[gid]);
+   return g;
+}
+
+uint32_t ungref_num_groups(void *h) { return static_cast<RefLabelGraph *>(h)->num_groups; }
+
+void ungref_copy_groups(void *h, uint32_t *new_to_old, uint32_t *group_first)
+{
+   auto *g = static_cast<RefLabelGraph *>(h);
+   std::memcpy(new_to_old, g->new_to_old.data(), g->new_to_old.size() * sizeof(uint32_t));
+   std::memcpy(group_first, g->group_first.data(), g->group_first.size() * sizeof(uint32_t));
+}
+
+uint64_t ungref_lng_nnz(void *h)
+{
+   auto *g = static_cast<RefLabelGraph *>(h);
+   uint64_t nnz = 0;
+   for (auto &o : g->out_neighbors)
+      nnz += o.size();
+   return nnz;
+}
+
+// out_offsets has G+2 entries (group 0 is empty); ids are in the reference's order.
+void ungref_copy_lng_out(void *h, uint64_t *out_offsets, uint32_t *out_ids)
+{
+   auto *g = static_cast<RefLabelGraph *>(h);
+   uint64_t pos = 0;
+   out_offsets[0] = 0;
+   for (uint32_t gid = 0; gid <= g->num_groups; ++gid)
+   {
+      out_offsets[gid] = pos;
+      for (auto t : g->out_neighbors[gid])
+         out_ids[pos++] = t;
+   }
+   out_offsets[g->num_groups + 1] = pos;
+}
+
+void ungref_label_graph_free(void *h) { delete static_cast<RefLabelGraph *>(h); }
+
+float ungref_l2(const float *a, const float *b, uint32_t dim)
+{
+   static ANNS::FloatL2DistanceHandler h;
+   return h.compute(reinterpret_cast<const char *>(a), reinterpret_cast<const char *>(b), dim);
+}
+
+// Exact cross-edge scan over the reordered base vectors X[n x d].
+// Groups are 1..G with rows [group_first[g], group_first[g+1]).  LNG out-neighbours
+// come as CSR over groups.  In-neighbours are derived serially in ascending source
+// order (uni_nav_graph_label_graph.cpp:889-906) and the scan order is the
+// reference's: target groups ascending, their in-groups in order, an OpenMP
+// dynamic,1 loop over the source vectors.  When source_mask is non-null only
+// source groups with a non-zero mask entry are scanned (used to time a bounded
+// sample).  Row v of ids/dists receives the queue of point v in queue order;
+// unused slots hold UINT32_MAX / +inf.  Returns the algorithmic pair count
+// (the reference's dim_ops / dim).
+uint64_t ungref_cross_exact(const float *X, uint32_t n, uint32_t d, uint32_t k, uint32_t num_groups,
+                            const uint32_t *group_first, const uint64_t *out_offsets, const uint32_t *out_ids,
+                            const uint8_t *source_mask, int num_threads, uint32_t *ids, float *dists)
+{
+   std::vector<std::vector<IdxType>> in_neighbors(num_groups + 1);
+   for (uint32_t f = 1; f <= num_groups; ++f)
+      for (uint64_t e = out_offsets[f]; e < out_offsets[f + 1]; ++e)
+         in_neighbors[out_ids[e]].push_back(f);
+
+   std::vector<ANNS::SearchQueue> queues(n);
+   for (uint32_t v = 0; v < n; ++v)
+      queues[v].reserve(k);
+   ANNS::FloatL2DistanceHandler dist;
+   if (num_threads > 0)
+      omp_set_num_threads(num_threads);
+   uint64_t pairs = 0;
+   for (uint32_t t = 1; t <= num_groups; ++t)
+   {
+      if (in_neighbors[t].empty())
+         continue;
+      const IdxType tf = group_first[t], ts = group_first[t + 1];
+      if (ts == tf)
+         continue;
+      for (IdxType f : in_neighbors[t])
+      {
+         if (source_mask && !source_mask[f])
+            continue;
+         const IdxType qf = group_first[f], qs = group_first[f + 1];
+         pairs += uint64_t(qs - qf) * uint64_t(ts - tf);
+#pragma omp parallel for schedule(dynamic, 1)
+         for (long long v = qf; v < (long long)qs; ++v)
+         {
+            ANNS::SearchQueue local;
+            local.reserve(k);
+            const char *q = reinterpret_cast<const char *>(X + size_t(v) * d);
+            for (IdxType x = tf; x < ts; ++x)
+               local.insert(x, dist.compute(q, reinterpret_cast<const char *>(X + size_t(x) * d), d));
+            for (int i = 0; i < local.size(); ++i)
+               queues[v].insert(local[i].id, local[i].distance);
+         }
+      }
+   }
+   for (uint32_t v = 0; v < n; ++v)
+   {
+      const auto &q = queues[v];
+      for (uint32_t i = 0; i < k; ++i)
+      {
+         const bool have = i < uint32_t(q.size());
+         ids[size_t(v) * k + i] = have ? q[i].id : std::numeric_limits<uint32_t>::max();
+         dists[size_t(v) * k + i] = have ? q[i].distance : std::numeric_limits<float>::infinity();
+      }
+   }
+   return pairs;
+}
+
+} // extern "C"

@@ -1,0 +1,462 @@
+/*
+ * TEST INFRASTRUCTURE ONLY -- the CPU oracle for the UNG cross-edge build.
+ * Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg load it;
+ * the product library never links or calls it.
+ *
+ * Plain-C restatement of the reference algorithm (panjd123/FilterVectorCode_refactor):
+ *
+ *   orc_l2            FloatL2DistanceHandler::compute, UNG/codes/src/distance.cpp:34-91
+ *                     (8 AVX2 lanes, hi+lo 128-bit fold, 4-wide tail, masked tail,
+ *                     two horizontal adds).  `fused` is a bit mask: bit 0 makes the
+ *                     8-lane loop update one rounding (fma), bit 1 does the same for
+ *                     the 4-wide and masked tails.  The reference's release build
+ *                     (GCC 13, -Ofast -mfma) rounds the loop update twice (mul, add)
+ *                     and fuses the tails: mode ORC_L2_REFERENCE_BUILD = 2, checked
+ *                     bit-for-bit against the compiled reference in the tests.
+ *   orc_queue_insert  SearchQueue::insert, UNG/codes/src/search_queue.cpp:26-53 with
+ *                     the (distance, id) order of UNG/codes/include/search_queue.h:20-22.
+ *   orc_cross_exact   build_cross_edges_generate_cpu_exact_scan +
+ *                     append_cross_edges_from_target_range,
+ *                     UNG/codes/src/uni_nav_graph_cross_edges.cpp:32-57, 154-220.
+ *   orc_label_graph_* build_trie_and_divide_groups (uni_nav_graph_label_graph.cpp:21-43),
+ *                     prepare_group_storages_graphs (uni_nav_graph.cpp:148-169) and the
+ *                     minimal-superset LNG (uni_nav_graph_label_graph.cpp:103-206, 851-911).
+ *                     Out-neighbours are produced as a set (ascending group id); the
+ *                     cross-edge result depends only on the set.
+ *
+ * Compiled with -ffp-contract=off so that every multiply and add rounds exactly
+ * where the restatement says.
+ */
+#include <math.h>
+#include <omp.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+typedef struct
+{
+   uint32_t id;
+   float dist;
+} orc_cand;
+
+static int cmp_u32(const void *a, const void *b);
+
+float orc_l2(const float *a, const float *b, uint32_t dim, int fused)
+{
+   float lane[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+   uint32_t i = 0;
+   while (dim - i >= 8)
+   {
+      for (int j = 0; j < 8; ++j)
+      {
+         const float t = a[i + j] - b[i + j];
+         lane[j] = (fused & 1) ? fmaf(t, t, lane[j]) : lane[j] + t * t;
+      }
+      i += 8;
+   }
+   float s[4];
+   for (int j = 0; j < 4; ++j)
+      s[j] = lane[4 + j] + lane[j];
+   if (dim - i >= 4)
+   {
+      for (int j = 0; j < 4; ++j)
+      {
+         const float t = a[i + j] - b[i + j];
+         s[j] = (fused & 2) ? fmaf(t, t, s[j]) : s[j] + t * t;
+      }
+      i += 4;
+   }
+   if (dim > i)
+   {
+      for (uint32_t j = 0; j < 4; ++j)
+      {
+         const float t = (i + j < dim) ? a[i + j] - b[i + j] : 0.0f;
+         s[j] = (fused & 2) ? fmaf(t, t, s[j]) : s[j] + t * t;
+      }
+   }
+   const float h0 = s[0] + s[1], h1 = s[2] + s[3];
+   return h0 + h1;
+}
+
+static int cand_less(orc_cand x, orc_cand y)
+{
+   return x.dist < y.dist || (x.dist == y.dist && x.id < y.id);
+}
+
+/* q has room for cap + 1 entries, *size <= cap. */
+void orc_queue_insert(orc_cand *q, int32_t *size, int32_t cap, uint32_t id, float dist)
+{
+   orc_cand c = {id, dist};
+   if (*size == cap && cand_less(q[*size - 1], c))
+      return;
+   int32_t lo = 0, hi = *size;
+   while (lo < hi)
+   {
+      int32_t mid = (lo + hi) >> 1;
+      if (cand_less(c, q[mid]))
+         hi = mid;
+      else if (q[mid].id == c.id)
+         return;
+      else
+         lo = mid + 1;
+   }
+   if (lo < cap)
+      memmove(&q[lo + 1], &q[lo], (size_t)(*size - lo) * sizeof(orc_cand));
+   q[lo] = c;
+   if (*size < cap)
+      (*size)++;
+}
+
+/* See ungref_cross_exact in ref_harness.cpp for the argument contract. */
+uint64_t orc_cross_exact(const float *X, uint32_t n, uint32_t d, uint32_t k, uint32_t num_groups,
+                         const uint32_t *group_first, const uint64_t *out_offsets, const uint32_t *out_ids,
+                         const uint8_t *source_mask, int num_threads, int fused, uint32_t *ids, float *dists)
+{
+   /* in-neighbours, ascending source id */
+   uint64_t *in_off = (uint64_t *)calloc((size_t)num_groups + 2, sizeof(uint64_t));
+   uint64_t nnz = out_offsets[num_groups + 1];
+   uint32_t *in_ids = (uint32_t *)malloc((nnz ? nnz : 1) * sizeof(uint32_t));
+   for (uint32_t f = 1; f <= num_groups; ++f)
+      for (uint64_t e = out_offsets[f]; e < out_offsets[f + 1]; ++e)
+         in_off[out_ids[e] + 1]++;
+   for (uint32_t g = 0; g <= num_groups; ++g)
+      in_off[g + 1] += in_off[g];
+   uint64_t *fill = (uint64_t *)malloc(((size_t)num_groups + 1) * sizeof(uint64_t));
+   memcpy(fill, in_off, ((size_t)num_groups + 1) * sizeof(uint64_t));
+   for (uint32_t f = 1; f <= num_groups; ++f)
+      for (uint64_t e = out_offsets[f]; e < out_offsets[f + 1]; ++e)
+         in_ids[fill[out_ids[e]]++] = f;
+   free(fill);
+
+   orc_cand *queues = (orc_cand *)malloc((size_t)n * (k + 1) * sizeof(orc_cand));
+   int32_t *qsize = (int32_t *)calloc(n ? n : 1, sizeof(int32_t));
+   if (num_threads > 0)
+      omp_set_num_threads(num_threads);
+   uint64_t pairs = 0;
+   for (uint32_t t = 1; t <= num_groups; ++t)
+   {
+      const uint32_t tf = group_first[t], ts = group_first[t + 1];
+      if (in_off[t] == in_off[t + 1] || ts == tf)
+         continue;
+      for (uint64_t e = in_off[t]; e < in_off[t + 1]; ++e)
+      {
+         const uint32_t f = in_ids[e];
+         if (source_mask && !source_mask[f])
+            continue;
+         const uint32_t qf = group_first[f], qs = group_first[f + 1];
+         pairs += (uint64_t)(qs - qf) * (uint64_t)(ts - tf);
+#pragma omp parallel for schedule(dynamic, 1)
+         for (long long v = qf; v < (long long)qs; ++v)
+         {
+            orc_cand local[257];
+            orc_cand *loc = k + 1 <= 257 ? local : (orc_cand *)malloc((k + 1) * sizeof(orc_cand));
+            int32_t lsize = 0;
+            const float *q = X + (size_t)v * d;
+            for (uint32_t x = tf; x < ts; ++x)
+               orc_queue_insert(loc, &lsize, (int32_t)k, x, orc_l2(q, X + (size_t)x * d, d, fused));
+            for (int32_t i = 0; i < lsize; ++i)
+               orc_queue_insert(queues + (size_t)v * (k + 1), &qsize[v], (int32_t)k, loc[i].id, loc[i].dist);
+            if (loc != local)
+               free(loc);
+         }
+      }
+   }
+   for (uint32_t v = 0; v < n; ++v)
+      for (uint32_t i = 0; i < k; ++i)
+      {
+         const int have = (int32_t)i < qsize[v];
+         ids[(size_t)v * k + i] = have ? queues[(size_t)v * (k + 1) + i].id : 0xffffffffu;
+         dists[(size_t)v * k + i] = have ? queues[(size_t)v * (k + 1) + i].dist : INFINITY;
+      }
+   free(queues);
+   free(qsize);
+   free(in_off);
+   free(in_ids);
+   return pairs;
+}
+
+/* ---------------- grouping + LNG ---------------- */
+
+typedef struct
+{
+   uint32_t num_points, num_groups;
+   uint32_t *new_to_old;     /* [n] */
+   uint32_t *group_first;    /* [G+2] */
+   uint64_t *set_off;        /* [G+2] label set of group g: set_lab[set_off[g]..set_off[g+1]) */
+   uint32_t *set_lab;
+   uint64_t *out_off;        /* [G+2] */
+   uint32_t *out_ids;
+} orc_label_graph;
+
+static int cmp_u32(const void *a, const void *b)
+{
+   uint32_t x = *(const uint32_t *)a, y = *(const uint32_t *)b;
+   return (x > y) - (x < y);
+}
+
+static uint64_t hash_seq(const uint32_t *s, uint32_t len)
+{
+   uint64_t h = 1469598103934665603ull ^ len;
+   for (uint32_t i = 0; i < len; ++i)
+   {
+      h ^= s[i] + 0x9e3779b97f4a7c15ull;
+      h *= 1099511628211ull;
+   }
+   return h;
+}
+
+/* std::includes over sorted sequences (multiset semantics). */
+static int seq_includes(const uint32_t *a, uint32_t na, const uint32_t *b, uint32_t nb)
+{
+   uint32_t i = 0, j = 0;
+   while (j < nb)
+   {
+      if (i == na || b[j] < a[i])
+         return 0;
+      if (!(a[i] < b[j]))
+         ++j;
+      ++i;
+   }
+   return 1;
+}
+
+void *orc_label_graph_build(uint32_t n, const uint64_t *label_offsets, const uint32_t *labels)
+{
+   orc_label_graph *g = (orc_label_graph *)calloc(1, sizeof(orc_label_graph));
+   g->num_points = n;
+   /* sorted copy of every point's labels */
+   uint64_t total = label_offsets[n];
+   uint32_t *sl = (uint32_t *)malloc((total ? total : 1) * sizeof(uint32_t));
+   memcpy(sl, labels, total * sizeof(uint32_t));
+   for (uint32_t v = 0; v < n; ++v)
+      qsort(sl + label_offsets[v], label_offsets[v + 1] - label_offsets[v], sizeof(uint32_t), cmp_u32);
+
+   /* open-addressing table: label sequence -> group id, first appearance order */
+   uint64_t cap = 16;
+   while (cap < 2ull * n + 16)
+      cap <<= 1;
+   uint32_t *slot_point = (uint32_t *)malloc(cap * sizeof(uint32_t)); /* representative point */
+   uint32_t *slot_group = (uint32_t *)calloc(cap, sizeof(uint32_t));
+   uint32_t *point_group = (uint32_t *)malloc((n ? n : 1) * sizeof(uint32_t));
+   uint32_t *rep = (uint32_t *)malloc(((size_t)n + 2) * sizeof(uint32_t));
+   uint32_t G = 0;
+   for (uint32_t v = 0; v < n; ++v)
+   {
+      const uint32_t *s = sl + label_offsets[v];
+      const uint32_t len = (uint32_t)(label_offsets[v + 1] - label_offsets[v]);
+      uint64_t h = hash_seq(s, len) & (cap - 1);
+      for (;;)
+      {
+         if (slot_group[h] == 0)
+         {
+            slot_group[h] = ++G;
+            slot_point[h] = v;
+            rep[G] = v;
+            point_group[v] = G;
+            break;
+         }
+         const uint32_t r = slot_point[h];
+         const uint32_t rlen = (uint32_t)(label_offsets[r + 1] - label_offsets[r]);
+         if (rlen == len && memcmp(sl + label_offsets[r], s, len * sizeof(uint32_t)) == 0)
+         {
+            point_group[v] = slot_group[h];
+            break;
+         }
+         h = (h + 1) & (cap - 1);
+      }
+   }
+   free(slot_point);
+   free(slot_group);
+   g->num_groups = G;
+
+   /* reorder: groups 1..G concatenated, original order inside a group */
+   g->group_first = (uint32_t *)calloc((size_t)G + 2, sizeof(uint32_t));
+   uint32_t *cnt = (uint32_t *)calloc((size_t)G + 2, sizeof(uint32_t));
+   for (uint32_t v = 0; v < n; ++v)
+      cnt[point_group[v]]++;
+   uint32_t acc = 0;
+   for (uint32_t gid = 1; gid <= G; ++gid)
+   {
+      g->group_first[gid] = acc;
+      acc += cnt[gid];
+   }
+   g->group_first[G + 1] = acc;
+   g->new_to_old = (uint32_t *)malloc((n ? n : 1) * sizeof(uint32_t));
+   memset(cnt, 0, ((size_t)G + 2) * sizeof(uint32_t));
+   for (uint32_t v = 0; v < n; ++v)
+   {
+      const uint32_t gid = point_group[v];
+      g->new_to_old[g->group_first[gid] + cnt[gid]++] = v;
+   }
+   free(cnt);
+   free(point_group);
+
+   /* label set per group */
+   g->set_off = (uint64_t *)calloc((size_t)G + 2, sizeof(uint64_t));
+   for (uint32_t gid = 1; gid <= G; ++gid)
+      g->set_off[gid + 1] = g->set_off[gid] + (label_offsets[rep[gid] + 1] - label_offsets[rep[gid]]);
+   g->set_lab = (uint32_t *)malloc((g->set_off[G + 1] ? g->set_off[G + 1] : 1) * sizeof(uint32_t));
+   for (uint32_t gid = 1; gid <= G; ++gid)
+      memcpy(g->set_lab + g->set_off[gid], sl + label_offsets[rep[gid]],
+             (g->set_off[gid + 1] - g->set_off[gid]) * sizeof(uint32_t));
+   free(rep);
+   free(sl);
+
+   /* groups ordered by label-set size (stable), then minimal strict supersets */
+   uint32_t *by_size = (uint32_t *)malloc(((size_t)G + 1) * sizeof(uint32_t));
+   {
+      uint32_t maxlen = 0;
+      for (uint32_t gid = 1; gid <= G; ++gid)
+      {
+         uint32_t l = (uint32_t)(g->set_off[gid + 1] - g->set_off[gid]);
+         if (l > maxlen)
+            maxlen = l;
+      }
+      uint32_t *bc = (uint32_t *)calloc((size_t)maxlen + 2, sizeof(uint32_t));
+      for (uint32_t gid = 1; gid <= G; ++gid)
+         bc[g->set_off[gid + 1] - g->set_off[gid] + 1]++;
+      for (uint32_t l = 0; l <= maxlen; ++l)
+         bc[l + 1] += bc[l];
+      for (uint32_t gid = 1; gid <= G; ++gid)
+         by_size[bc[g->set_off[gid + 1] - g->set_off[gid]]++] = gid;
+      free(bc);
+   }
+   uint32_t **mins = (uint32_t **)calloc((size_t)G + 1, sizeof(uint32_t *));
+   uint32_t *nmins = (uint32_t *)calloc((size_t)G + 1, sizeof(uint32_t));
+#pragma omp parallel for schedule(dynamic, 16)
+   for (long long fl = 1; fl <= (long long)G; ++fl)
+   {
+      const uint32_t f = (uint32_t)fl;
+      const uint32_t *fs = g->set_lab + g->set_off[f];
+      const uint32_t fn = (uint32_t)(g->set_off[f + 1] - g->set_off[f]);
+      uint32_t *kept = (uint32_t *)malloc(((size_t)G + 1) * sizeof(uint32_t));
+      uint32_t nk = 0;
+      for (uint32_t i = 0; i < G; ++i)
+      {
+         const uint32_t c = by_size[i];
+         if (c == f)
+            continue;
+         const uint32_t *cs = g->set_lab + g->set_off[c];
+         const uint32_t cn = (uint32_t)(g->set_off[c + 1] - g->set_off[c]);
+         if (!seq_includes(cs, cn, fs, fn))
+            continue;
+         int is_min = 1;
+         for (uint32_t m = 0; m < nk && is_min; ++m)
+         {
+            const uint32_t *ms = g->set_lab + g->set_off[kept[m]];
+            const uint32_t mn = (uint32_t)(g->set_off[kept[m] + 1] - g->set_off[kept[m]]);
+            if (mn < cn && seq_includes(cs, cn, ms, mn))
+               is_min = 0;
+         }
+         if (is_min)
+            kept[nk++] = c;
+      }
+      qsort(kept, nk, sizeof(uint32_t), cmp_u32);
+      mins[f] = kept;
+      nmins[f] = nk;
+   }
+   free(by_size);
+   g->out_off = (uint64_t *)calloc((size_t)G + 2, sizeof(uint64_t));
+   for (uint32_t f = 1; f <= G; ++f)
+      g->out_off[f + 1] = g->out_off[f] + nmins[f];
+   g->out_ids = (uint32_t *)malloc((g->out_off[G + 1] ? g->out_off[G + 1] : 1) * sizeof(uint32_t));
+   for (uint32_t f = 1; f <= G; ++f)
+   {
+      memcpy(g->out_ids + g->out_off[f], mins[f], nmins[f] * sizeof(uint32_t));
+      free(mins[f]);
+   }
+   free(mins);
+   free(nmins);
+   return g;
+}
+
+uint32_t orc_num_groups(void *h) { return ((orc_label_graph *)h)->num_groups; }
+
+void orc_copy_groups(void *h, uint32_t *new_to_old, uint32_t *group_first)
+{
+   orc_label_graph *g = (orc_label_graph *)h;
+   memcpy(new_to_old, g->new_to_old, (size_t)g->num_points * sizeof(uint32_t));
+   memcpy(group_first, g->group_first, ((size_t)g->num_groups + 2) * sizeof(uint32_t));
+}
+
+uint64_t orc_lng_nnz(void *h)
+{
+   orc_label_graph *g = (orc_label_graph *)h;
+   return g->out_off[g->num_groups + 1];
+}
+
+void orc_copy_lng_out(void *h, uint64_t *out_offsets, uint32_t *out_ids)
+{
+   orc_label_graph *g = (orc_label_graph *)h;
+   memcpy(out_offsets, g->out_off, ((size_t)g->num_groups + 2) * sizeof(uint64_t));
+   memcpy(out_ids, g->out_ids, g->out_off[g->num_groups + 1] * sizeof(uint32_t));
+}
+
+void orc_label_graph_free(void *h)
+{
+   orc_label_graph *g = (orc_label_graph *)h;
+   if (!g)
+      return;
+   free(g->new_to_old);
+   free(g->group_first);
+   free(g->set_off);
+   free(g->set_lab);
+   free(g->out_off);
+   free(g->out_ids);
+   free(g);
+}
+
+/* Exact cross edges for a list of rows only (same result as orc_cross_exact on those
+ * rows): every target group of the row's source group is scanned into the row's
+ * queue in ascending target-group order, like the reference's outer loop. */
+void orc_cross_rows(const float *X, uint32_t n, uint32_t d, uint32_t k, uint32_t num_groups,
+                    const uint32_t *group_first, const uint64_t *out_offsets, const uint32_t *out_ids,
+                    const uint32_t *rows, uint64_t nrows, int num_threads, int fused, uint32_t *ids, float *dists)
+{
+   (void)n;
+   if (num_threads > 0)
+      omp_set_num_threads(num_threads);
+#pragma omp parallel for schedule(dynamic, 1)
+   for (long long i = 0; i < (long long)nrows; ++i)
+   {
+      const uint32_t v = rows[i];
+      /* source group of v: largest g with group_first[g] <= v and a non-empty range */
+      uint32_t lo = 1, hi = num_groups;
+      while (lo < hi)
+      {
+         uint32_t mid = (lo + hi + 1) / 2;
+         if (group_first[mid] <= v)
+            lo = mid;
+         else
+            hi = mid - 1;
+      }
+      while (lo > 1 && group_first[lo] == group_first[lo + 1])
+         --lo;
+      const uint32_t f = lo;
+      orc_cand *q = (orc_cand *)malloc((k + 1) * sizeof(orc_cand));
+      orc_cand *loc = (orc_cand *)malloc((k + 1) * sizeof(orc_cand));
+      int32_t qs = 0;
+      /* targets in ascending group order */
+      uint64_t nt = out_offsets[f + 1] - out_offsets[f];
+      uint32_t *tg = (uint32_t *)malloc((nt ? nt : 1) * sizeof(uint32_t));
+      memcpy(tg, out_ids + out_offsets[f], nt * sizeof(uint32_t));
+      qsort(tg, nt, sizeof(uint32_t), cmp_u32);
+      for (uint64_t e = 0; e < nt; ++e)
+      {
+         const uint32_t t = tg[e];
+         int32_t ls = 0;
+         for (uint32_t x = group_first[t]; x < group_first[t + 1]; ++x)
+            orc_queue_insert(loc, &ls, (int32_t)k, x, orc_l2(X + (size_t)v * d, X + (size_t)x * d, d, fused));
+         for (int32_t j = 0; j < ls; ++j)
+            orc_queue_insert(q, &qs, (int32_t)k, loc[j].id, loc[j].dist);
+      }
+      for (uint32_t j = 0; j < k; ++j)
+      {
+         ids[(size_t)i * k + j] = (int32_t)j < qs ? q[j].id : 0xffffffffu;
+         dists[(size_t)i * k + j] = (int32_t)j < qs ? q[j].dist : INFINITY;
+      }
+      free(tg);
+      free(q);
+      free(loc);
+   }
+}

@@ -1,0 +1,169 @@
+"""Parity of the B200 cross-edge build against the oracle, through the C ABI.
+
+* golden fixtures (made by the reference's own compiled code): ids and distance bits equal;
+* full-size configuration 2 and scaled configurations 3 / 4: rows sampled across every
+  source-group size are recomputed by the CPU oracle and must match exactly; every
+  row satisfies the size-independent properties (sorted, ids from the union of the
+  out-groups, min(k, |union|) edges, sentinels last);
+* the device-pointer entry point equals the host entry point; sharded calls cover
+  every row exactly once and reproduce the one-shard result;
+* a pipeline wait that runs out returns UNGX_ERR_TIMEOUT and leaves the context usable.
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+from parity import assert_rows_match, check_row_properties
+from filtervectorcode_refactor_b200 import _native as nat
+from filtervectorcode_refactor_b200 import datasets
+from filtervectorcode_refactor_b200.ung import UniNavGraph
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    c = nat.Context(0)
+    yield c
+    c.close()
+
+
+def run_golden(ctx, g, route):
+    n, d = g["Xr"].shape
+    prob = nat.Problem(n, d, g["k"], g["group_ranges"], g["out_offsets"], g["out_ids"], route=route)
+    ids = np.full(n * g["k"], 7, dtype=np.uint32)
+    dists = np.full(n * g["k"], -1, dtype=np.float32)
+    ctx.prepare_base_vectors(g["Xr"], n, d, on_device=False)
+    t = ctx.generate(prob, ids, dists)
+    ctx.release_base_vectors()
+    return ids, dists, t
+
+
+@pytest.mark.parametrize("route", [nat.ROUTE_TENSOR, nat.ROUTE_EXACT])
+def test_golden_parity(ctx, golden, route):
+    if route == nat.ROUTE_TENSOR and golden["k"] > 24:
+        with pytest.raises(nat.UngxError):
+            run_golden(ctx, golden, route)
+        return
+    ids, dists, t = run_golden(ctx, golden, route)
+    assert t.route_used == route
+    assert t.pairs == int(golden["pairs"])
+    assert_rows_match(ids, dists, golden["ids"], golden["dists"], golden["k"])
+
+
+def test_uninavgraph_mirror_end_to_end(golden):
+    """The reference-shaped host API: labels + raw vectors in, SearchQueue content out."""
+    ung = UniNavGraph(num_cross_edges=golden["k"])
+    ung.build(golden["X"], golden["label_offsets"], golden["labels"])
+    try:
+        assert np.array_equal(ung._new_to_old_vec_ids, golden["new_to_old"])
+        assert_rows_match(ung.cross_group_neighbor_flat_ids, ung.cross_group_neighbor_dists, golden["ids"],
+                          golden["dists"], golden["k"])
+        off, cols = ung.cross_edges_csr()
+        assert int(off[-1]) == int((golden["ids"] != 0xFFFFFFFF).sum())
+    finally:
+        ung.close()
+
+
+def test_device_entry_point_matches_host(ctx, golden):
+    import torch
+    n, d = golden["Xr"].shape
+    k = golden["k"]
+    if k > 24:
+        pytest.skip("tensor route needs k <= 24")
+    prob = nat.Problem(n, d, k, golden["group_ranges"], golden["out_offsets"], golden["out_ids"])
+    X = torch.from_numpy(golden["Xr"]).cuda()
+    d_ids = torch.empty(n * k, dtype=torch.int32, device="cuda")
+    d_dists = torch.empty(n * k, dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    ctx.prepare_base_vectors(X.data_ptr(), n, d, on_device=True)
+    ctx.generate_device(prob, d_ids.data_ptr(), d_dists.data_ptr())
+    ctx.release_base_vectors()
+    ids = d_ids.cpu().numpy().view(np.uint32)
+    dists = d_dists.cpu().numpy()
+    assert_rows_match(ids, dists, golden["ids"], golden["dists"], k)
+
+
+def test_shards_cover_rows_once(ctx, golden):
+    n, d = golden["Xr"].shape
+    k = golden["k"]
+    route = nat.ROUTE_TENSOR if k <= 24 else nat.ROUTE_EXACT
+    ids = np.full(n * k, 0xABCDEF, dtype=np.uint32)
+    dists = np.full(n * k, -5, dtype=np.float32)
+    ctx.prepare_base_vectors(golden["Xr"], n, d, on_device=False)
+    seen = np.zeros(n, dtype=np.int64)
+    for r in range(3):
+        prob = nat.Problem(n, d, k, golden["group_ranges"], golden["out_offsets"], golden["out_ids"], route=route,
+                           shard_rank=r, shard_count=3)
+        seen[prob.shard_rows()] += 1
+        ctx.generate(prob, ids, dists)
+    ctx.release_base_vectors()
+    assert np.all(seen == 1)
+    assert_rows_match(ids, dists, golden["ids"], golden["dists"], k)
+
+
+def sample_rows(group_ranges, out_offsets, rng, per_bucket=12, max_rows=400):
+    """Rows drawn across source-group size buckets (singletons .. the largest group)."""
+    gr = group_ranges.reshape(-1, 2).astype(np.int64)
+    sizes = gr[:, 1] - gr[:, 0]
+    has_out = np.diff(out_offsets.astype(np.int64))[:len(sizes)] > 0
+    rows = []
+    for lo in [1, 2, 8, 64, 512, 4096, 32768]:
+        gs = np.nonzero((sizes >= lo) & (sizes < lo * 8) & has_out)[0]
+        if gs.size == 0:
+            continue
+        for g in rng.choice(gs, size=min(per_bucket, gs.size), replace=False):
+            rows.append(int(rng.integers(gr[g, 0], gr[g, 1])))
+    no_out = np.nonzero(~has_out & (sizes > 0))[0]
+    for g in no_out[:5]:
+        rows.append(int(gr[g, 0]))
+    return np.unique(np.array(rows[:max_rows], dtype=np.uint32))
+
+
+@pytest.mark.parametrize("cfg,n", [(2, None), (3, 200_000), (4, 1_000_000)])
+def test_config_scale_parity(ctx, cfg, n):
+    c = datasets.make_config(cfg, seed=0, n=n)
+    lg = nat.LabelGraph(c["label_offsets"], c["labels"])
+    Xr = np.ascontiguousarray(c["X"][lg.new_to_old])
+    N, d, k = Xr.shape[0], Xr.shape[1], c["k"]
+    prob = nat.Problem(N, d, k, lg.group_ranges, lg.out_offsets, lg.out_ids, route=nat.ROUTE_TENSOR)
+    ids = np.empty(N * k, dtype=np.uint32)
+    dists = np.empty(N * k, dtype=np.float32)
+    ctx.prepare_base_vectors(Xr, N, d, on_device=False)
+    t = ctx.generate(prob, ids, dists)
+    ctx.release_base_vectors()
+    rng = np.random.default_rng(cfg)
+    rows = sample_rows(lg.group_ranges, lg.out_offsets, rng, per_bucket=12 if d <= 128 else 5)
+    group_first = np.concatenate([[0], lg.group_ranges[2::2], [lg.group_ranges[-1]]]).astype(np.uint32)
+    o_ids, o_d = O.oracle().cross_rows(Xr, k, group_first, lg.out_offsets, lg.out_ids, rows)
+    full_ids = np.full((N, k), 0xFFFFFFFF, dtype=np.uint32)
+    full_d = np.full((N, k), np.inf, dtype=np.float32)
+    full_ids[rows] = o_ids
+    full_d[rows] = o_d
+    assert_rows_match(ids, dists, full_ids.ravel(), full_d.ravel(), k, rows=rows)
+    prop_rows = np.unique(np.concatenate([rows, rng.integers(0, N, size=2000).astype(np.uint32)]))
+    check_row_properties(ids, dists, k, lg.group_ranges, lg.out_offsets, lg.out_ids, prop_rows)
+    # the certificate must clear nearly every row (the rest are rescanned exactly)
+    assert t.rows_certified + t.rows_fallback > 0
+    assert t.rows_fallback <= 0.01 * (t.rows_certified + t.rows_fallback)
+
+
+def test_wait_timeout_reports_and_context_survives(ctx):
+    g = __import__("conftest").load_golden("cfg2_n6000")
+    n, d = g["Xr"].shape
+    k = g["k"]
+    prob = nat.Problem(n, d, k, g["group_ranges"], g["out_offsets"], g["out_ids"], route=nat.ROUTE_TENSOR)
+    ids = np.empty(n * k, dtype=np.uint32)
+    dists = np.empty(n * k, dtype=np.float32)
+    ctx.prepare_base_vectors(g["Xr"], n, d, on_device=False)
+    try:
+        ctx.set_device_wait_limit_ns(1)
+        with pytest.raises(nat.UngxError) as e:
+            ctx.generate(prob, ids, dists)
+        assert e.value.status == nat.UNGX_ERR_TIMEOUT
+        ctx.set_device_wait_limit_ns(4_000_000_000)
+        ctx.generate(prob, ids, dists)
+        assert_rows_match(ids, dists, g["ids"], g["dists"], k)
+    finally:
+        ctx.set_device_wait_limit_ns(4_000_000_000)
+        ctx.release_base_vectors()

@@ -1,0 +1,58 @@
+"""The product's grouping / reorder / LNG (host C++ in libungx) against the reference goldens."""
+import numpy as np
+import pytest
+
+import oracle as O
+from filtervectorcode_refactor_b200 import _native as nat
+from filtervectorcode_refactor_b200 import datasets
+
+
+def test_label_graph_matches_golden(golden):
+    lg = nat.LabelGraph(golden["label_offsets"], golden["labels"])
+    G = golden["num_groups"]
+    assert lg.num_groups == G
+    assert np.array_equal(lg.new_to_old, golden["new_to_old"])
+    assert np.array_equal(lg.group_ranges, golden["group_ranges"])
+    assert O.lng_sets(lg.out_offsets, lg.out_ids, G) == O.lng_sets(golden["out_offsets"], golden["out_ids"], G)
+    # in-neighbours: transpose of out, each list ascending (reference builds it serially)
+    for t in range(1, G + 1):
+        ins = lg.in_ids[lg.in_offsets[t]:lg.in_offsets[t + 1]]
+        assert np.all(np.diff(ins.astype(np.int64)) > 0)
+        for f in ins:
+            assert t in lg.out_ids[lg.out_offsets[f]:lg.out_offsets[f + 1]]
+
+
+def test_label_sets_are_sorted_sequences():
+    off = np.array([0, 2, 4, 4, 5], dtype=np.uint64)
+    lab = np.array([3, 1, 1, 3, 7], dtype=np.uint32)  # {3,1} and {1,3} are one group; empty set; {7}
+    lg = nat.LabelGraph(off, lab)
+    assert lg.num_groups == 3
+    assert lg.new_to_old.tolist() == [0, 1, 2, 3]
+    assert lg.set_labels.tolist() == [1, 3, 7]
+    # empty set (group 2) has every other group as superset; minimal ones: {1,3} and {7}
+    assert sorted(lg.out_ids[lg.out_offsets[2]:lg.out_offsets[3]].tolist()) == [1, 3]
+    assert lg.out_offsets[2] - lg.out_offsets[1] == 0  # {1,3} has no strict superset
+
+
+def test_label_graph_config2_shape():
+    """Group statistics of the full config-2 label model (seed 0): 21,753 groups,
+    5,316 singletons, 81,611 LNG edges, W = 1.549e10 pairs."""
+    c = datasets.CONFIGS[2]
+    off, lab = datasets.make_labels(c["n"], c["vocab"], c["umin"], c["umax"], c["zipf"], seed=0)
+    lg = nat.LabelGraph(off, lab)
+    sizes = np.diff(lg.group_ranges.reshape(-1, 2), axis=1)[1:, 0].astype(np.int64)
+    assert lg.num_groups == 21753
+    assert int((sizes == 1).sum()) == 5316
+    assert len(lg.out_ids) == 81611
+    W = 0
+    for f in range(1, lg.num_groups + 1):
+        outs = lg.out_ids[lg.out_offsets[f]:lg.out_offsets[f + 1]]
+        W += int(sizes[f - 1]) * int(sizes[outs.astype(np.int64) - 1].sum())
+    assert W == 15487870738 or abs(W - 1.549e10) / 1.549e10 < 1e-3
+
+
+def test_label_graph_rejects_bad_offsets():
+    off = np.array([0, 3, 2], dtype=np.uint64)
+    lab = np.array([1, 2, 3], dtype=np.uint32)
+    with pytest.raises(nat.UngxError):
+        nat.LabelGraph(off, lab)
