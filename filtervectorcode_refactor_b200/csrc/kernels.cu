@@ -35,6 +35,7 @@ constexpr uint32_t kItemSlots = 2;
 constexpr uint32_t kAChunk = 128 * 128; // 128 rows x 32 fp32
 constexpr uint32_t kBChunk = 256 * 128; // up to 256 rows x 32 fp32
 constexpr uint32_t kNoItem = 0xFFFFFFFFu;
+constexpr int kPushBuf = 4; // per-lane buffer of candidates awaiting a merge into the sorted list
 // Limit of the waits that retire work already in flight before the CTA exits
 // (independent of the configurable pipeline wait limit, which tests set tiny).
 constexpr uint64_t kDrainWaitNs = 2000000000ull;
@@ -615,6 +616,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
          const WorkItem w = p.items[idx];
          const bool row_ok = r < w.row_count;
          const bool warp_ok = q * 32u < w.row_count;
+         // Sorted candidate list (key, col) of the KP smallest keys seen, and a
+         // small unsorted buffer of keys that beat the list's threshold as it was
+         // at the last flush.  Pushes are branch-free; the buffer is merged into the
+         // list only when some lane of the warp fills it, so all lanes merge together.
          float key[KP];
          uint32_t col[KP];
 #pragma unroll
@@ -623,6 +628,26 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
             key[i] = INFINITY;
             col[i] = 0xFFFFFFFFu;
          }
+         float bk[kPushBuf];
+         uint32_t bc[kPushBuf];
+#pragma unroll
+         for (int i = 0; i < kPushBuf; ++i)
+         {
+            bk[i] = INFINITY;
+            bc[i] = 0xFFFFFFFFu;
+         }
+         uint32_t nb = 0;
+         float thr = row_ok ? INFINITY : -INFINITY; // rows past the item never take candidates
+         auto flush = [&]() {
+#pragma unroll
+            for (int i = 0; i < kPushBuf; ++i)
+            {
+               insert_key<KP>(key, col, bk[i], bc[i]); // +inf entries leave the list unchanged
+               bk[i] = INFINITY;
+            }
+            nb = 0;
+            thr = row_ok ? key[KP - 1] : -INFINITY;
+         };
          float maxn2 = 0.f;
          uint32_t total = 0;
          for (uint32_t s = 0; s < w.seg_count && ok; ++s)
@@ -635,44 +660,59 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
                const uint32_t valid = min(256u, sg.x_count - t0);
                const uint32_t x0 = sg.x_begin + t0;
                const uint32_t b = tseq & 1u;
+               const uint32_t nchunk = (valid + 31u) >> 5;
+               // norms of this warp's chunks (j = h, h+2, ...), loaded before the wait
+               float nreg[4];
+#pragma unroll
+               for (uint32_t i = 0; i < 4; ++i)
+               {
+                  const uint32_t c = (h + 2u * i) * 32u + lane;
+                  nreg[i] = c < valid ? __ldg(p.xnorm + x0 + c) : INFINITY;
+               }
                if (!ptx::mbar_wait(&acc_full[b], (tseq >> 1) & 1u, abort_word, tmo))
                {
                   ok = false;
                   break;
                }
                ptx::tc_fence_after();
-               const uint32_t nchunk = (valid + 31u) >> 5;
-               for (uint32_t j = h; j < nchunk; j += 2)
+#pragma unroll 1
+               for (uint32_t i = 0; i < 4; ++i)
                {
-                  const uint32_t c = j * 32u + lane;
-                  nrm[lane] = c < valid ? __ldg(p.xnorm + x0 + c) : INFINITY;
+                  const uint32_t j = h + 2u * i;
+                  if (j >= nchunk)
+                     break;
+                  const float nv = i == 0 ? nreg[0] : i == 1 ? nreg[1] : i == 2 ? nreg[2] : nreg[3];
                   __syncwarp();
-                  if (warp_ok)
+                  nrm[lane] = nv;
+                  __syncwarp();
+                  if (!warp_ok)
+                     continue;
+                  uint32_t v[32];
+                  ptx::tmem_ld32(tmem_base + ((q * 32u) << 16) + b * 256u + j * 32u, v);
+                  ptx::tmem_wait_ld();
+                  const uint32_t cbase = x0 + j * 32u;
+#pragma unroll
+                  for (int jj = 0; jj < 32; ++jj)
                   {
-                     uint32_t v[32];
-                     ptx::tmem_ld32(tmem_base + ((q * 32u) << 16) + b * 256u + j * 32u, v);
-                     ptx::tmem_wait_ld();
-                     if (row_ok)
+                     const float kk = __fmaf_rn(-2.0f, __uint_as_float(v[jj]), nrm[jj]);
+                     const bool pass = kk < thr;
+                     if (__any_sync(0xffffffffu, pass))
                      {
-                        float kk[32];
-                        float mn = INFINITY;
 #pragma unroll
-                        for (int jj = 0; jj < 32; ++jj)
+                        for (int m = kPushBuf - 1; m > 0; --m)
                         {
-                           kk[jj] = __fmaf_rn(-2.0f, __uint_as_float(v[jj]), nrm[jj]);
-                           mn = fminf(mn, kk[jj]);
+                           bk[m] = pass ? bk[m - 1] : bk[m];
+                           bc[m] = pass ? bc[m - 1] : bc[m];
                         }
-                        if (mn < key[KP - 1])
-                        {
-#pragma unroll
-                           for (int jj = 0; jj < 32; ++jj)
-                              if (kk[jj] < key[KP - 1])
-                                 insert_key<KP>(key, col, kk[jj], x0 + j * 32u + jj);
-                        }
+                        bk[0] = pass ? kk : bk[0];
+                        bc[0] = pass ? cbase + jj : bc[0];
+                        nb += pass ? 1u : 0u;
+                        if (__any_sync(0xffffffffu, nb == kPushBuf))
+                           flush();
                      }
                   }
-                  __syncwarp();
                }
+               __syncwarp();
                ptx::tc_fence_before();
                __syncwarp();
                if (lane == 0)
@@ -682,6 +722,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
          }
          if (!ok)
             break;
+         flush();
          // ---- merge the two column halves of each row (bounded mbarrier handshake)
          const uint32_t mseq = iseq - 1; // items this warp has finished before this one
          if (h == 1)
@@ -835,13 +876,10 @@ cudaError_t launch_exact_t(const ExactParams &p, uint32_t grid, cudaStream_t s)
 
 int tc_candidates_for_k(uint32_t k)
 {
-   if (k == 0)
+   // the smallest candidate list with at least two entries of slack past k
+   if (k == 0 || k > kTcMaxK)
       return 0;
-   if (k <= 10)
-      return 16;
-   if (k <= kTcMaxK)
-      return 32;
-   return 0;
+   return k + 2 <= 8 ? 8 : k + 2 <= 16 ? 16 : k + 2 <= 24 ? 24 : 32;
 }
 
 bool tc_a_resident(uint32_t dp) { return dp <= 128; }
@@ -923,8 +961,12 @@ cudaError_t launch_tc(const TcMaps &maps, const TcParams &p, uint32_t grid, cuda
 {
    const int kp = tc_candidates_for_k(p.k);
    const bool ares = tc_a_resident(p.dp);
+   if (kp == 8)
+      return ares ? launch_tc_t<8, true>(maps, p, grid, s) : launch_tc_t<8, false>(maps, p, grid, s);
    if (kp == 16)
       return ares ? launch_tc_t<16, true>(maps, p, grid, s) : launch_tc_t<16, false>(maps, p, grid, s);
+   if (kp == 24)
+      return ares ? launch_tc_t<24, true>(maps, p, grid, s) : launch_tc_t<24, false>(maps, p, grid, s);
    if (kp == 32)
       return ares ? launch_tc_t<32, true>(maps, p, grid, s) : launch_tc_t<32, false>(maps, p, grid, s);
    return cudaErrorInvalidValue;

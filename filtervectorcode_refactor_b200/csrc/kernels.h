@@ -52,7 +52,7 @@ struct ExactParams
 };
 
 // Largest k the tensor-core route supports (candidate list of 32 per row).
-constexpr uint32_t kTcMaxK = 24;
+constexpr uint32_t kTcMaxK = 30;
 // Largest k the exact route supports (per-lane list of 128).
 constexpr uint32_t kExactMaxK = 128;
 

@@ -39,7 +39,7 @@ def run_golden(ctx, g, route):
     return ids, dists, t
 
 
-@pytest.mark.parametrize("route", [nat.ROUTE_TENSOR, nat.ROUTE_EXACT])
+@pytest.mark.parametrize("route", [nat.ROUTE_TENSOR, nat.ROUTE_EXACT], ids=["tensor", "exact"])
 def test_golden_parity(ctx, golden, route):
     if route == nat.ROUTE_TENSOR and golden["k"] > 24:
         with pytest.raises(nat.UngxError):
