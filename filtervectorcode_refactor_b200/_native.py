@@ -47,6 +47,7 @@ class CrossEdgeTiming(ctypes.Structure):
         ("plan_ms", c_double),
         ("prepare_ms", c_double),
         ("tc_kernel_ms", c_double),
+        ("rerank_ms", c_double),
         ("fallback_ms", c_double),
         ("pairs", c_uint64),
         ("rows_certified", c_uint64),

@@ -78,9 +78,10 @@ struct ungx_context
    uint32_t n = 0, d = 0, dp = 0;
    // per-call scratch
    DevBuf items, segs, empties, ranges, gmax, counters, fb_rows, fb_items, rows, row_items, out_ids, out_dists;
+   DevBuf cand_key, cand_col;
    DevBuf stage[2];
    uint32_t *h_counters = nullptr; // pinned
-   cudaEvent_t ev[8] = {};
+   cudaEvent_t ev[10] = {};
 };
 
 namespace
@@ -259,10 +260,14 @@ int run_generate(ungx_context *ctx, const ungx_cross_edge_problem &p, const Plan
                 "group norm kernel");
       UNGX_CUDA(ctx, ctx->fb_rows.ensure(sizeof(uint32_t) * std::max<uint64_t>(item_rows, 1)), "fallback list");
       UNGX_CUDA(ctx, ctx->fb_items.ensure(sizeof(uint32_t) * std::max<uint64_t>(item_rows, 1)), "fallback list");
+      // candidate lists [row][2][kp], indexed by the global row
+      const size_t cand = size_t(ctx->n) * 2u * uint32_t(kp);
+      UNGX_CUDA(ctx, ctx->cand_key.ensure(cand * sizeof(float)), "candidate buffer");
+      UNGX_CUDA(ctx, ctx->cand_col.ensure(cand * sizeof(uint32_t)), "candidate buffer");
       ungx::TcMaps maps;
       if ((st = make_map(ctx, &maps.a, ctx->Xp.p, ctx->n, ctx->dp, 128)))
          return st;
-      for (int i = 0; i < 5; ++i)
+      for (int i = 0; i < 4; ++i)
          if ((st = make_map(ctx, &maps.b[i], ctx->Xp.p, ctx->n, ctx->dp, 16u << i)))
             return st;
       ungx::TcParams tp{};
@@ -270,25 +275,35 @@ int run_generate(ungx_context *ctx, const ungx_cross_edge_problem &p, const Plan
       tp.segs = ctx->segs.as<ungx::Segment>();
       tp.num_items = (uint32_t)plan.items.size();
       tp.item_counter = cnt + 0;
-      tp.X = ctx->X;
       tp.xnorm = ctx->xnorm.as<float>();
-      tp.group_maxn2 = ctx->gmax.as<float>();
-      tp.n = ctx->n;
-      tp.d = ctx->d;
       tp.dp = ctx->dp;
-      tp.k = k;
-      tp.out_ids = d_ids;
-      tp.out_dists = d_dists;
-      tp.fb_rows = ctx->fb_rows.as<uint32_t>();
-      tp.fb_items = ctx->fb_items.as<uint32_t>();
-      tp.fb_count = cnt + 1;
-      tp.counters = stats;
+      tp.cand_key = ctx->cand_key.as<float>();
+      tp.cand_col = ctx->cand_col.as<uint32_t>();
       tp.status = status;
       tp.timeout_ns = ctx->device_wait_ns;
-      ungx::tc_certificate_constants(ctx->d, ctx->dp, tp);
       const uint32_t grid = (uint32_t)std::min<size_t>(plan.items.size(), (size_t)ctx->num_sms);
-      UNGX_CUDA(ctx, ungx::launch_tc(maps, tp, grid, s), "tensor-core kernel launch");
+      UNGX_CUDA(ctx, ungx::launch_tc(maps, tp, (uint32_t)kp, grid, s), "tensor-core kernel launch");
       UNGX_CUDA(ctx, cudaEventRecord(ev[3], s), "event");
+      ungx::RerankParams rp{};
+      rp.items = tp.items;
+      rp.segs = tp.segs;
+      rp.item_offset = 0;
+      rp.X = ctx->X;
+      rp.xnorm = tp.xnorm;
+      rp.group_maxn2 = ctx->gmax.as<float>();
+      rp.d = ctx->d;
+      rp.k = k;
+      rp.cand_key = tp.cand_key;
+      rp.cand_col = tp.cand_col;
+      rp.out_ids = d_ids;
+      rp.out_dists = d_dists;
+      rp.fb_rows = ctx->fb_rows.as<uint32_t>();
+      rp.fb_items = ctx->fb_items.as<uint32_t>();
+      rp.fb_count = cnt + 1;
+      rp.counters = stats;
+      ungx::tc_certificate_constants(ctx->d, ctx->dp, rp);
+      UNGX_CUDA(ctx, ungx::launch_rerank(rp, (uint32_t)kp, (uint32_t)plan.items.size(), s), "rerank kernel launch");
+      UNGX_CUDA(ctx, cudaEventRecord(ev[8], s), "event");
       // rows the certificate rejected: exact rescan (count read on the device)
       ungx::ExactParams ep{};
       ep.items = tp.items;
@@ -296,13 +311,13 @@ int run_generate(ungx_context *ctx, const ungx_cross_edge_problem &p, const Plan
       ep.X = ctx->X;
       ep.d = ctx->d;
       ep.k = k;
-      ep.rows = tp.fb_rows;
-      ep.row_items = tp.fb_items;
-      ep.count_dev = tp.fb_count;
+      ep.rows = rp.fb_rows;
+      ep.row_items = rp.fb_items;
+      ep.count_dev = rp.fb_count;
       ep.out_ids = d_ids;
       ep.out_dists = d_dists;
       UNGX_CUDA(ctx, ungx::launch_exact(ep, (uint32_t)ctx->num_sms * 4, s), "fallback kernel launch");
-      t.gpu_launches += 3;
+      t.gpu_launches += 4;
    }
    else if (!plan.items.empty())
    {
@@ -348,11 +363,13 @@ int run_generate(ungx_context *ctx, const ungx_cross_edge_problem &p, const Plan
    cudaEventElapsedTime(&c, ev[2], ev[3]);
    t.gpu_h2d_ms += a;
    t.gpu_kernel_ms += b;
-   if (route == UNGX_ROUTE_TENSOR)
+   if (route == UNGX_ROUTE_TENSOR && !plan.items.empty())
    {
       t.tc_kernel_ms += c;
-      float f = 0;
-      cudaEventElapsedTime(&f, ev[3], ev[4]);
+      float rr = 0, f = 0;
+      cudaEventElapsedTime(&rr, ev[3], ev[8]);
+      cudaEventElapsedTime(&f, ev[8], ev[4]);
+      t.rerank_ms += rr;
       t.fallback_ms += f;
    }
    const int dev_status = reinterpret_cast<const int *>(ctx->h_counters)[2];
@@ -448,7 +465,7 @@ int ungx_context_destroy(ungx_context *ctx)
    ungx_release_base_vectors(ctx);
    for (DevBuf *b : {&ctx->items, &ctx->segs, &ctx->empties, &ctx->ranges, &ctx->gmax, &ctx->counters,
                      &ctx->fb_rows, &ctx->fb_items, &ctx->rows, &ctx->row_items, &ctx->out_ids, &ctx->out_dists,
-                     &ctx->stage[0], &ctx->stage[1]})
+                     &ctx->stage[0], &ctx->stage[1], &ctx->cand_key, &ctx->cand_col})
       b->release();
    for (auto &ev : ctx->ev)
       if (ev)
@@ -484,7 +501,9 @@ int ungx_prepare_base_vectors(ungx_context *ctx, const float *vectors, uint32_t 
    if (!vectors || n == 0 || d == 0)
       return fail(ctx, UNGX_ERR_INVALID_ARG, "ungx_prepare_base_vectors: empty or null vectors");
    UNGX_CUDA(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
-   ungx_release_base_vectors(ctx);
+   // device buffers of an earlier preparation are reused when large enough
+   ctx->have_vectors = false;
+   ctx->X = nullptr;
    const auto t0 = std::chrono::steady_clock::now();
    const uint32_t dp = (d + 31) / 32 * 32;
    const size_t xbytes = size_t(n) * d * sizeof(float);
@@ -655,7 +674,8 @@ int ungx_cross_edges_build(ungx_context *ctx, const float *vectors, const ungx_c
    const double prep = ms_since(t0);
    ungx_cross_edge_timing t{};
    st = ungx_cross_edges_generate(ctx, problem, out_ids, out_dists, &t);
-   ungx_release_base_vectors(ctx);
+   // the device buffers stay allocated in the context for the next build
+   ctx->have_vectors = false;
    t.prepare_ms = prep;
    t.generate_ms = ms_since(t0);
    if (timing)

@@ -2,23 +2,24 @@
 //
 //   colsum / center     resident operand build (a4): mean, centred + TF32-rounded
 //                       copy padded to 32 columns, fp32 row norms.
-//   exact_rows_kernel   CUDA-core exact scan, squared L2 in the reference's fp32
-//                       summation order (FloatL2DistanceHandler::compute,
-//                       UNG/codes/src/distance.cpp:34-91) and its (distance, id)
-//                       queue order (UNG/codes/include/search_queue.h:20-22).
-//                       Route EXACT, and the rescan of rows whose certificate failed.
-//   tc_kernel           the hot path: persistent CTAs pull source-centric work items;
-//                       TMA stages 128-row source tiles and target tiles through a
-//                       4-stage shared-memory ring; one thread issues tcgen05.mma
-//                       kind::tf32 into a double-buffered TMEM accumulator; eight
-//                       epilogue warps read TMEM rows (one thread per source row),
-//                       turn dot products into ||x||^2 - 2 q.x keys and keep a
-//                       register top-KP per row; at the end of the item the KP
-//                       candidates are re-ranked with the exact reference distance
-//                       and a rounding-error certificate proves that no excluded
-//                       column could enter the top-k.  Rows whose certificate fails
-//                       are queued for exact_rows_kernel.  No distance matrix is ever
-//                       written to global memory.
+//   tc_kernel           the hot path.  Persistent CTAs pull source-centric work items
+//                       (<=128 rows of one source group x all its LNG target groups);
+//                       TMA stages the item's source rows once (operand A) and the
+//                       target rows in 128-row tiles through an 8-stage shared-memory
+//                       ring; one thread issues tcgen05.mma kind::tf32 into four
+//                       128-column TMEM accumulators; eight epilogue warps read TMEM
+//                       rows (thread = source row), form the keys ||x||^2 - 2 q.x and
+//                       keep a sorted register top-KP per row and column half.  The two
+//                       lists of every row go to a small candidate buffer; no distance
+//                       matrix reaches global memory.
+//   rerank_kernel       merges a row's two lists, computes the exact reference distance
+//                       of each candidate, sorts by (distance, id), writes the top-k and
+//                       checks a rounding-error certificate that no column outside the
+//                       list could enter the top-k; failing rows are queued.
+//   exact_rows_kernel   CUDA-core exact scan in the reference's fp32 summation order
+//                       (FloatL2DistanceHandler::compute, UNG/codes/src/distance.cpp:34-91)
+//                       with its (distance, id) queue order (UNG/codes/include/search_queue.h:20-22):
+//                       route EXACT, and the rescan of the queued rows.
 #include <cfloat>
 #include <cmath>
 
@@ -30,33 +31,37 @@ namespace ungx
 namespace
 {
 constexpr uint32_t kTcThreads = 320; // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
-constexpr uint32_t kStages = 4;
+constexpr uint32_t kBN = 128;        // target columns per tile / TMEM accumulator
+constexpr uint32_t kAccBufs = 4;     // TMEM accumulators (4 x 128 columns = all 512)
 constexpr uint32_t kItemSlots = 2;
-constexpr uint32_t kAChunk = 128 * 128; // 128 rows x 32 fp32
-constexpr uint32_t kBChunk = 256 * 128; // up to 256 rows x 32 fp32
+constexpr uint32_t kAChunk = 128 * 128; // 128 rows x 32 fp32, 128-byte swizzled
+constexpr uint32_t kBChunk = kBN * 128; // 128 rows x 32 fp32
 constexpr uint32_t kNoItem = 0xFFFFFFFFu;
-constexpr int kPushBuf = 4; // per-lane buffer of candidates awaiting a merge into the sorted list
 // Limit of the waits that retire work already in flight before the CTA exits
 // (independent of the configurable pipeline wait limit, which tests set tiny).
 constexpr uint64_t kDrainWaitNs = 2000000000ull;
 
 struct TcLayout
 {
-   uint32_t a_off, a_bytes, stage_off, stage_bytes, merge_off, norm_off, bar_off, misc_off, total;
+   uint32_t stages, a_off, a_bytes, stage_off, stage_bytes, keys_off, norm_off, bar_off, misc_off, total;
 };
 
-__host__ __device__ inline TcLayout tc_layout(uint32_t dp, bool a_res, uint32_t kp)
+// A resident (dp <= 128): A = dp/32 chunks of 16 KB kept per item, 8 stages of one
+// 16 KB target chunk.  A streamed: 6 stages of (16 KB source + 16 KB target) chunks.
+// Then 4 KB per epilogue warp for a chunk's 32 x 32 keys, the chunk norms, barriers.
+__host__ __device__ inline TcLayout tc_layout(uint32_t dp, bool a_res)
 {
    TcLayout L;
+   L.stages = a_res ? 8u : 6u;
    L.a_off = 0;
    L.a_bytes = a_res ? (dp / 32) * kAChunk : 0;
    L.stage_off = L.a_bytes;
    L.stage_bytes = a_res ? kBChunk : kAChunk + kBChunk;
-   L.merge_off = L.stage_off + kStages * L.stage_bytes;
-   L.norm_off = L.merge_off + 128 * kp * 8;
+   L.keys_off = L.stage_off + L.stages * L.stage_bytes;
+   L.norm_off = L.keys_off + 8 * 32 * 32 * 4;
    L.bar_off = L.norm_off + 8 * 32 * 4;
-   L.misc_off = L.bar_off + 32 * 8;
-   L.total = L.misc_off + 64;
+   L.misc_off = L.bar_off + 40 * 8;
+   L.total = L.misc_off + 128;
    return L;
 }
 
@@ -153,8 +158,9 @@ __device__ __forceinline__ bool pair_less(float d0, uint32_t i0, float d1, uint3
    return d0 < d1 || (d0 == d1 && i0 < i1);
 }
 
-// Sorted insert of (d, id) into an ascending (distance, id) list; caller checked
-// that (d, id) precedes the last entry.  Static indices only (stays in registers).
+// Sorted insert of (d, id) into an ascending (distance, id) list of K entries (the
+// last entry drops out).  Branch-free; an entry that does not precede the last one
+// leaves the list unchanged.  Static indices only, so the list stays in registers.
 template <int K>
 __device__ __forceinline__ void insert_pair(float (&kd)[K], uint32_t (&ki)[K], float d, uint32_t id)
 {
@@ -175,7 +181,8 @@ __device__ __forceinline__ void insert_pair(float (&kd)[K], uint32_t (&ki)[K], f
    }
 }
 
-// Same on prefilter keys alone (their order among equal keys does not matter).
+// Same on prefilter keys alone (their order among equal keys does not matter);
+// inserting +inf is a no-op.
 template <int K>
 __device__ __forceinline__ void insert_key(float (&kd)[K], uint32_t (&ki)[K], float d, uint32_t id)
 {
@@ -353,7 +360,67 @@ __device__ __forceinline__ void raise_abort(volatile int *abort_word, int *statu
 
 __device__ __forceinline__ uint32_t box_index(uint32_t valid)
 {
-   return valid <= 16 ? 0u : valid <= 32 ? 1u : valid <= 64 ? 2u : valid <= 128 ? 3u : 4u;
+   return valid <= 16 ? 0u : valid <= 32 ? 1u : valid <= 64 ? 2u : 3u;
+}
+
+// Walks the 128-column tiles of a work item: segment by segment, 128 columns at a
+// time.  The descriptor of the following segment is always loaded one segment
+// ahead, so crossing into a new segment never waits on global memory.
+struct TileIter
+{
+   const Segment *segs;
+   uint32_t seg, nseg, t0;
+   uint2 cur, nxt; // (x_begin, x_count)
+   __device__ __forceinline__ uint2 load(uint32_t s) const
+   {
+      if (s >= nseg)
+         return make_uint2(0, 0);
+      const uint4 v = __ldg(reinterpret_cast<const uint4 *>(segs + s));
+      return make_uint2(v.x, v.y);
+   }
+   __device__ __forceinline__ void start(const Segment *s, uint32_t begin, uint32_t count)
+   {
+      segs = s + begin;
+      seg = 0;
+      nseg = count;
+      t0 = 0;
+      cur = load(0);
+      nxt = load(1);
+   }
+   __device__ __forceinline__ bool valid_tile() const { return seg < nseg; }
+   __device__ __forceinline__ uint32_t x0() const { return cur.x + t0; }
+   __device__ __forceinline__ uint32_t cols() const { return min(kBN, cur.y - t0); }
+   __device__ __forceinline__ void next()
+   {
+      t0 += kBN;
+      if (t0 >= cur.y)
+      {
+         t0 = 0;
+         ++seg;
+         cur = nxt;
+         nxt = load(seg + 1);
+      }
+   }
+};
+
+// Candidate keys carry, in their 5 lowest mantissa bits, the slot of the entry in a
+// per-thread column array.  A sorted list of such keys is updated with min/max only;
+// the packing moves a key by at most 32 ulp (relative 2^-18), which the certificate
+// accounts for.
+constexpr uint32_t kSlotMask = 31u;
+
+__device__ __forceinline__ float packed_init(int i)
+{
+   return __uint_as_float((0x7F7FFFFFu & ~kSlotMask) | uint32_t(i)); // huge, finite, ascending
+}
+
+template <int K>
+__device__ __forceinline__ void insert_packed(float (&L)[K], float v)
+{
+#pragma unroll
+   for (int i = K - 1; i > 0; --i)
+      L[i] = fmaxf(L[i - 1], fminf(L[i], v));
+   L[0] = fminf(L[0], v);
 }
 
 template <int KP, bool A_RES>
@@ -362,26 +429,26 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
    extern __shared__ uint8_t smem_raw[];
    const uint32_t raw_u32 = ptx::smem_u32(smem_raw);
    uint8_t *smem = smem_raw + (((raw_u32 + 1023u) & ~1023u) - raw_u32);
-   const TcLayout L = tc_layout(p.dp, A_RES, KP);
+   const TcLayout L = tc_layout(p.dp, A_RES);
+   const uint32_t S = L.stages;
    uint8_t *sA = smem + L.a_off;
    uint8_t *sStage = smem + L.stage_off;
-   float2 *sMerge = reinterpret_cast<float2 *>(smem + L.merge_off);
    float *sNorm = reinterpret_cast<float *>(smem + L.norm_off);
    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bar_off);
-   uint64_t *full = bars;
-   uint64_t *empty = bars + kStages;
-   uint64_t *acc_full = bars + 2 * kStages;
-   uint64_t *acc_empty = acc_full + 2;
-   uint64_t *a_full = acc_empty + 2;
-   uint64_t *a_empty = a_full + 1;
-   uint64_t *item_full = a_empty + 1;
-   uint64_t *item_empty = item_full + kItemSlots;
-   uint64_t *done_bar = item_empty + kItemSlots;
-   uint64_t *merge_ready = done_bar + 1; // [4] per TMEM quarter: half 1 published its list
-   uint64_t *merge_done = merge_ready + 4; // [4] per TMEM quarter: half 0 consumed it
+   uint64_t *full = bars;            // [S]
+   uint64_t *empty = bars + 8;       // [S]
+   uint64_t *acc_full = bars + 16;   // [4]
+   uint64_t *acc_empty = bars + 20;  // [4]
+   uint64_t *a_full = bars + 24;
+   uint64_t *a_empty = bars + 25;
+   uint64_t *item_full = bars + 26;  // [2]
+   uint64_t *item_empty = bars + 28; // [2]
+   uint64_t *done_bar = bars + 30;
    volatile uint32_t *item_slot = reinterpret_cast<volatile uint32_t *>(smem + L.misc_off);
    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L.misc_off + 16);
    volatile int *abort_word = reinterpret_cast<volatile int *>(smem + L.misc_off + 32);
+   WorkItem *item_desc = reinterpret_cast<WorkItem *>(smem + L.misc_off + 64); // [kItemSlots]
+   float *sKeys = reinterpret_cast<float *>(smem + L.keys_off);
 
    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
    const uint32_t nch = p.dp / 32;
@@ -389,12 +456,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
 
    if (threadIdx.x == 0)
    {
-      for (uint32_t s = 0; s < kStages; ++s)
+      for (uint32_t s = 0; s < S; ++s)
       {
          ptx::mbar_init(&full[s], 1);
          ptx::mbar_init(&empty[s], 1);
       }
-      for (uint32_t b = 0; b < 2; ++b)
+      for (uint32_t b = 0; b < kAccBufs; ++b)
       {
          ptx::mbar_init(&acc_full[b], 1);
          ptx::mbar_init(&acc_empty[b], 8);
@@ -407,18 +474,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
          ptx::mbar_init(&item_empty[s], 9); // MMA thread + 8 epilogue warps
       }
       ptx::mbar_init(done_bar, 1);
-      for (uint32_t qq = 0; qq < 4; ++qq)
-      {
-         ptx::mbar_init(&merge_ready[qq], 1);
-         ptx::mbar_init(&merge_done[qq], 1);
-      }
       *abort_word = 0;
       ptx::fence_mbar_init();
    }
    if (warp == 0 && lane == 0)
    {
       ptx::prefetch_tmap(&maps.a);
-      for (int i = 0; i < 5; ++i)
+      for (int i = 0; i < 4; ++i)
          ptx::prefetch_tmap(&maps.b[i]);
    }
    if (warp == 1)
@@ -447,12 +509,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
                ok = false;
                break;
             }
+            WorkItem w{};
+            if (idx < p.num_items)
+               w = p.items[idx];
+            item_desc[slot] = w;
             item_slot[slot] = idx < p.num_items ? idx : kNoItem;
             ptx::mbar_arrive(&item_full[slot]);
             ++iseq;
             if (idx >= p.num_items)
                break;
-            const WorkItem w = p.items[idx];
             if (A_RES)
             {
                if (!ptx::mbar_wait(a_empty, (aseq & 1u) ^ 1u, abort_word, tmo))
@@ -465,30 +530,26 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
                   ptx::tma_load_2d(sA + c * kAChunk, &maps.a, a_full, int32_t(c * 32), int32_t(w.row_begin));
                ++aseq;
             }
-            for (uint32_t s = 0; s < w.seg_count && ok; ++s)
+            TileIter ti;
+            for (ti.start(p.segs, w.seg_begin, w.seg_count); ti.valid_tile() && ok; ti.next())
             {
-               const Segment sg = p.segs[w.seg_begin + s];
-               for (uint32_t t0 = 0; t0 < sg.x_count && ok; t0 += 256)
+               const uint32_t bix = box_index(ti.cols());
+               const uint32_t brows = 16u << bix;
+               for (uint32_t c = 0; c < nch; ++c)
                {
-                  const uint32_t valid = min(256u, sg.x_count - t0);
-                  const uint32_t bix = box_index(valid);
-                  const uint32_t brows = 16u << bix;
-                  for (uint32_t c = 0; c < nch; ++c)
+                  const uint32_t st = it % S;
+                  if (!ptx::mbar_wait(&empty[st], ((it / S) & 1u) ^ 1u, abort_word, tmo))
                   {
-                     const uint32_t st = it % kStages;
-                     if (!ptx::mbar_wait(&empty[st], ((it / kStages) & 1u) ^ 1u, abort_word, tmo))
-                     {
-                        ok = false;
-                        break;
-                     }
-                     uint8_t *dst = sStage + st * L.stage_bytes;
-                     ptx::mbar_arrive_expect_tx(&full[st], (A_RES ? 0u : kAChunk) + brows * 128u);
-                     if (!A_RES)
-                        ptx::tma_load_2d(dst, &maps.a, &full[st], int32_t(c * 32), int32_t(w.row_begin));
-                     ptx::tma_load_2d(dst + (A_RES ? 0u : kAChunk), &maps.b[bix], &full[st], int32_t(c * 32),
-                                      int32_t(sg.x_begin + t0));
-                     ++it;
+                     ok = false;
+                     break;
                   }
+                  uint8_t *dst = sStage + st * L.stage_bytes;
+                  ptx::mbar_arrive_expect_tx(&full[st], (A_RES ? 0u : kAChunk) + brows * 128u);
+                  if (!A_RES)
+                     ptx::tma_load_2d(dst, &maps.a, &full[st], int32_t(c * 32), int32_t(w.row_begin));
+                  ptx::tma_load_2d(dst + (A_RES ? 0u : kAChunk), &maps.b[bix], &full[st], int32_t(c * 32),
+                                   int32_t(ti.x0()));
+                  ++it;
                }
             }
             if (!ok)
@@ -498,9 +559,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
          {
             raise_abort(abort_word, p.status, UNGX_ERR_TIMEOUT);
             // drain: every load already issued must land before the CTA exits
-            for (uint32_t st = 0; st < kStages; ++st)
+            for (uint32_t st = 0; st < S; ++st)
             {
-               const uint32_t issued = it / kStages + (st < it % kStages ? 1u : 0u);
+               const uint32_t issued = it / S + (st < it % S ? 1u : 0u);
                if (issued)
                   ptx::mbar_wait(&full[st], (issued - 1) & 1u, nullptr, kDrainWaitNs);
             }
@@ -529,51 +590,47 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
             ++iseq;
             if (idx == kNoItem)
                break;
-            const WorkItem w = p.items[idx];
+            const WorkItem w = item_desc[slot];
             if (A_RES && !ptx::mbar_wait(a_full, aseq & 1u, abort_word, tmo))
             {
                ok = false;
                break;
             }
-            for (uint32_t s = 0; s < w.seg_count && ok; ++s)
+            TileIter ti;
+            for (ti.start(p.segs, w.seg_begin, w.seg_count); ti.valid_tile() && ok; ti.next())
             {
-               const Segment sg = p.segs[w.seg_begin + s];
-               for (uint32_t t0 = 0; t0 < sg.x_count && ok; t0 += 256)
+               const uint32_t b = tseq % kAccBufs;
+               if (!ptx::mbar_wait(&acc_empty[b], ((tseq / kAccBufs) & 1u) ^ 1u, abort_word, tmo))
                {
-                  const uint32_t valid = min(256u, sg.x_count - t0);
-                  const uint32_t b = tseq & 1u;
-                  if (!ptx::mbar_wait(&acc_empty[b], ((tseq >> 1) & 1u) ^ 1u, abort_word, tmo))
+                  ok = false;
+                  break;
+               }
+               ptx::tc_fence_after();
+               const uint32_t N = (ti.cols() + 15u) & ~15u;
+               const uint32_t idesc = ptx::idesc_tf32(128, N);
+               const uint32_t dt = tmem_base + b * kBN;
+               for (uint32_t c = 0; c < nch; ++c)
+               {
+                  const uint32_t st = it % S;
+                  if (!ptx::mbar_wait(&full[st], (it / S) & 1u, abort_word, tmo))
                   {
                      ok = false;
                      break;
                   }
                   ptx::tc_fence_after();
-                  const uint32_t N = min(256u, (valid + 15u) & ~15u);
-                  const uint32_t idesc = ptx::idesc_tf32(128, N);
-                  const uint32_t dt = tmem_base + b * 256u;
-                  for (uint32_t c = 0; c < nch; ++c)
-                  {
-                     const uint32_t st = it % kStages;
-                     if (!ptx::mbar_wait(&full[st], (it / kStages) & 1u, abort_word, tmo))
-                     {
-                        ok = false;
-                        break;
-                     }
-                     ptx::tc_fence_after();
-                     uint8_t *stage = sStage + st * L.stage_bytes;
-                     const uint64_t ad = ptx::sdesc_k_sw128(ptx::smem_u32(A_RES ? sA + c * kAChunk : stage));
-                     const uint64_t bd = ptx::sdesc_k_sw128(ptx::smem_u32(stage + (A_RES ? 0u : kAChunk)));
+                  uint8_t *stage = sStage + st * L.stage_bytes;
+                  const uint64_t ad = ptx::sdesc_k_sw128(ptx::smem_u32(A_RES ? sA + c * kAChunk : stage));
+                  const uint64_t bd = ptx::sdesc_k_sw128(ptx::smem_u32(stage + (A_RES ? 0u : kAChunk)));
 #pragma unroll
-                     for (uint32_t ks = 0; ks < 4; ++ks) // 4 x K=8 per 32-column chunk (+32 B each)
-                        ptx::mma_tf32(dt, ad + 2u * ks, bd + 2u * ks, idesc, (c | ks) != 0u);
-                     ptx::mma_commit(&empty[st]);
-                     ++it;
-                  }
-                  if (!ok)
-                     break;
-                  ptx::mma_commit(&acc_full[b]);
-                  ++tseq;
+                  for (uint32_t ks = 0; ks < 4; ++ks) // 4 x K=8 per 32-column chunk (+32 B each)
+                     ptx::mma_tf32(dt, ad + 2u * ks, bd + 2u * ks, idesc, (c | ks) != 0u);
+                  ptx::mma_commit(&empty[st]);
+                  ++it;
                }
+               if (!ok)
+                  break;
+               ptx::mma_commit(&acc_full[b]);
+               ++tseq;
             }
             if (!ok)
                break;
@@ -595,9 +652,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
    else
    {
       // ------------------------------------------------ epilogue: one thread per source row
-      const uint32_t q = warp & 3u;          // TMEM lane quarter this warp may read
-      const uint32_t h = (warp - 2u) >> 2;   // which half of each tile's 32-column chunks
-      const uint32_t r = q * 32u + lane;     // row inside the work item
+      // Warp w reads TMEM lane quarter w % 4 (rows 32q..32q+31) and, of every 128-column
+      // tile, the 32-column chunks h and h + 2.
+      const uint32_t q = warp & 3u;
+      const uint32_t h = (warp - 2u) >> 2;
+      const uint32_t r = q * 32u + lane;
       float *nrm = sNorm + (warp - 2u) * 32u;
       uint32_t tseq = 0, iseq = 0;
       bool ok = true;
@@ -613,223 +672,104 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
          ++iseq;
          if (idx == kNoItem)
             break;
-         const WorkItem w = p.items[idx];
+         const WorkItem w = item_desc[slot];
          const bool row_ok = r < w.row_count;
          const bool warp_ok = q * 32u < w.row_count;
-         // Sorted candidate list (key, col) of the KP smallest keys seen, and a
-         // small unsorted buffer of keys that beat the list's threshold as it was
-         // at the last flush.  Pushes are branch-free; the buffer is merged into the
-         // list only when some lane of the warp fills it, so all lanes merge together.
-         float key[KP];
-         uint32_t col[KP];
+         float key[KP];      // ascending packed keys (slot in the low bits)
+         uint32_t colv[KP];  // column of each slot (dynamically indexed)
 #pragma unroll
          for (int i = 0; i < KP; ++i)
          {
-            key[i] = INFINITY;
-            col[i] = 0xFFFFFFFFu;
+            key[i] = packed_init(i);
+            colv[i] = 0xFFFFFFFFu;
          }
-         float bk[kPushBuf];
-         uint32_t bc[kPushBuf];
-#pragma unroll
-         for (int i = 0; i < kPushBuf; ++i)
+         float thr = row_ok ? key[KP - 1] : -INFINITY; // rows past the item never take candidates
+         float *kst = sKeys + (warp - 2u) * 1024u;      // 32 lanes x 32 keys, column-swizzled
+         TileIter ti;
+         ti.start(p.segs, w.seg_begin, w.seg_count);
+         // norms of this warp's two chunks of the current tile; the next tile's are
+         // loaded while the current one is processed
+         float n0 = INFINITY, n1 = INFINITY;
+         if (ti.valid_tile())
          {
-            bk[i] = INFINITY;
-            bc[i] = 0xFFFFFFFFu;
+            const uint32_t c0 = h * 32u + lane, c1 = c0 + 64u, v = ti.cols(), x0 = ti.x0();
+            n0 = c0 < v ? __ldg(p.xnorm + x0 + c0) : INFINITY;
+            n1 = c1 < v ? __ldg(p.xnorm + x0 + c1) : INFINITY;
          }
-         uint32_t nb = 0;
-         float thr = row_ok ? INFINITY : -INFINITY; // rows past the item never take candidates
-         auto flush = [&]() {
-#pragma unroll
-            for (int i = 0; i < kPushBuf; ++i)
+         for (; ti.valid_tile(); ++tseq)
+         {
+            const uint32_t valid = ti.cols(), x0 = ti.x0();
+            const float cn0 = n0, cn1 = n1;
+            ti.next();
+            if (ti.valid_tile())
             {
-               insert_key<KP>(key, col, bk[i], bc[i]); // +inf entries leave the list unchanged
-               bk[i] = INFINITY;
+               const uint32_t c0 = h * 32u + lane, c1 = c0 + 64u, v = ti.cols(), nx0 = ti.x0();
+               n0 = c0 < v ? __ldg(p.xnorm + nx0 + c0) : INFINITY;
+               n1 = c1 < v ? __ldg(p.xnorm + nx0 + c1) : INFINITY;
             }
-            nb = 0;
-            thr = row_ok ? key[KP - 1] : -INFINITY;
-         };
-         float maxn2 = 0.f;
-         uint32_t total = 0;
-         for (uint32_t s = 0; s < w.seg_count && ok; ++s)
-         {
-            const Segment sg = p.segs[w.seg_begin + s];
-            maxn2 = fmaxf(maxn2, p.group_maxn2[sg.group_id]);
-            total += sg.x_count;
-            for (uint32_t t0 = 0; t0 < sg.x_count; t0 += 256)
-            {
-               const uint32_t valid = min(256u, sg.x_count - t0);
-               const uint32_t x0 = sg.x_begin + t0;
-               const uint32_t b = tseq & 1u;
-               const uint32_t nchunk = (valid + 31u) >> 5;
-               // norms of this warp's chunks (j = h, h+2, ...), loaded before the wait
-               float nreg[4];
-#pragma unroll
-               for (uint32_t i = 0; i < 4; ++i)
-               {
-                  const uint32_t c = (h + 2u * i) * 32u + lane;
-                  nreg[i] = c < valid ? __ldg(p.xnorm + x0 + c) : INFINITY;
-               }
-               if (!ptx::mbar_wait(&acc_full[b], (tseq >> 1) & 1u, abort_word, tmo))
-               {
-                  ok = false;
-                  break;
-               }
-               ptx::tc_fence_after();
-#pragma unroll 1
-               for (uint32_t i = 0; i < 4; ++i)
-               {
-                  const uint32_t j = h + 2u * i;
-                  if (j >= nchunk)
-                     break;
-                  const float nv = i == 0 ? nreg[0] : i == 1 ? nreg[1] : i == 2 ? nreg[2] : nreg[3];
-                  __syncwarp();
-                  nrm[lane] = nv;
-                  __syncwarp();
-                  if (!warp_ok)
-                     continue;
-                  uint32_t v[32];
-                  ptx::tmem_ld32(tmem_base + ((q * 32u) << 16) + b * 256u + j * 32u, v);
-                  ptx::tmem_wait_ld();
-                  const uint32_t cbase = x0 + j * 32u;
-#pragma unroll
-                  for (int jj = 0; jj < 32; ++jj)
-                  {
-                     const float kk = __fmaf_rn(-2.0f, __uint_as_float(v[jj]), nrm[jj]);
-                     const bool pass = kk < thr;
-                     if (__any_sync(0xffffffffu, pass))
-                     {
-#pragma unroll
-                        for (int m = kPushBuf - 1; m > 0; --m)
-                        {
-                           bk[m] = pass ? bk[m - 1] : bk[m];
-                           bc[m] = pass ? bc[m - 1] : bc[m];
-                        }
-                        bk[0] = pass ? kk : bk[0];
-                        bc[0] = pass ? cbase + jj : bc[0];
-                        nb += pass ? 1u : 0u;
-                        if (__any_sync(0xffffffffu, nb == kPushBuf))
-                           flush();
-                     }
-                  }
-               }
-               __syncwarp();
-               ptx::tc_fence_before();
-               __syncwarp();
-               if (lane == 0)
-                  ptx::mbar_arrive(&acc_empty[b]);
-               ++tseq;
-            }
-         }
-         if (!ok)
-            break;
-         flush();
-         // ---- merge the two column halves of each row (bounded mbarrier handshake)
-         const uint32_t mseq = iseq - 1; // items this warp has finished before this one
-         if (h == 1)
-         {
-            if (!ptx::mbar_wait(&merge_done[q], (mseq & 1u) ^ 1u, abort_word, tmo))
+            const uint32_t b = tseq % kAccBufs;
+            if (!ptx::mbar_wait(&acc_full[b], (tseq / kAccBufs) & 1u, abort_word, tmo))
             {
                ok = false;
                break;
             }
-            if (row_ok)
-            {
-#pragma unroll
-               for (int i = 0; i < KP; ++i)
-                  sMerge[r * KP + i] = make_float2(key[i], __uint_as_float(col[i]));
-            }
-            __syncwarp();
-            if (lane == 0)
-               ptx::mbar_arrive(&merge_ready[q]);
-         }
-         else if (!ptx::mbar_wait(&merge_ready[q], mseq & 1u, abort_word, tmo))
-         {
-            ok = false;
-            break;
-         }
-         bool cert = true;
-         if (h == 0 && row_ok)
-         {
-            for (int i = 0; i < KP; ++i)
-            {
-               const float2 e = sMerge[r * KP + i];
-               if (e.x < key[KP - 1])
-                  insert_key<KP>(key, col, e.x, __float_as_uint(e.y));
-            }
-            // ---- exact rerank of the candidates in the reference's arithmetic
-            const uint32_t row = w.row_begin + r;
-            const uint32_t m = total < uint32_t(KP) ? total : uint32_t(KP);
-            uint32_t cl[KP];
-#pragma unroll
-            for (int i = 0; i < KP; ++i)
-               cl[i] = col[i];
-            float sd[KP];
-            uint32_t si[KP];
-#pragma unroll
-            for (int i = 0; i < KP; ++i)
-            {
-               sd[i] = INFINITY;
-               si[i] = 0xFFFFFFFFu;
-            }
-            const float *qv = p.X + size_t(row) * p.d;
-            const bool vec4 = (p.d & 3u) == 0;
+            ptx::tc_fence_after();
 #pragma unroll 1
-            for (uint32_t i = 0; i < m; ++i)
+            for (uint32_t i = 0; i < 2; ++i)
             {
-               const uint32_t x = cl[i];
-               const float *xv = p.X + size_t(x) * p.d;
-               const float D = vec4 ? ref_l2<true>(qv, xv, p.d) : ref_l2<false>(qv, xv, p.d);
-               if (pair_less(D, x, sd[KP - 1], si[KP - 1]))
-                  insert_pair<KP>(sd, si, D, x);
-            }
-            // ---- certificate: every column outside the list has key >= T, hence
-            // true squared distance >= ||a||^2 + T - bound and reference distance
-            // >= that * (1 - gref); if this exceeds the k-th exact distance no
-            // excluded column can enter the top-k.
-            if (total > uint32_t(KP))
-            {
-               float dk = INFINITY;
+               const uint32_t j = h + 2u * i;
+               if (!warp_ok || j * 32u >= valid)
+                  break;
+               __syncwarp();
+               nrm[lane] = i ? cn1 : cn0;
+               __syncwarp();
+               uint32_t raw[32];
+               ptx::tmem_ld32(tmem_base + ((q * 32u) << 16) + b * kBN + j * 32u, raw);
+               ptx::tmem_wait_ld();
+               uint32_t mask = 0;
 #pragma unroll
-               for (int i = 0; i < KP; ++i)
-                  if (uint32_t(i) == p.k - 1)
-                     dk = sd[i];
-               const double T = (double)key[KP - 1];
-               const double qn = (double)__ldg(p.xnorm + row);
-               const double a2lo = qn * (1.0 - p.gd);
-               const double ahi = sqrt(qn * (1.0 + p.gd));
-               const double bmax = sqrt((double)maxn2 * (1.0 + p.gd));
-               const double bound = (p.c1 * ahi * bmax + p.c2 * bmax * bmax) * (1.0 + 1.0 / 1024.0);
-               const double lhs = (a2lo + T - bound) * (1.0 - p.gref);
-               cert = lhs > (double)dk;
-            }
-#pragma unroll
-            for (int i = 0; i < KP; ++i)
-               if (uint32_t(i) < p.k)
+               for (int jj = 0; jj < 32; ++jj)
                {
-                  p.out_ids[size_t(row) * p.k + i] = si[i];
-                  if (p.out_dists)
-                     p.out_dists[size_t(row) * p.k + i] = sd[i];
+                  const float kk = __fmaf_rn(-2.0f, __uint_as_float(raw[jj]), nrm[jj]);
+                  mask |= (kk < thr) ? (1u << jj) : 0u;
+                  kst[lane * 32u + (uint32_t(jj) ^ lane)] = kk;
                }
-            if (!cert)
-            {
-               const uint32_t pos = atomicAdd(p.fb_count, 1u);
-               p.fb_rows[pos] = row;
-               p.fb_items[pos] = idx;
+               // every lane inserts its passing keys; the loop runs as often as the
+               // busiest lane needs, lanes without a candidate insert +inf (a no-op)
+               const uint32_t cbase = x0 + j * 32u;
+               while (__any_sync(0xffffffffu, mask != 0u))
+               {
+                  const uint32_t jj = mask ? uint32_t(__ffs(mask) - 1) : 0u;
+                  const float kk = kst[lane * 32u + (jj ^ lane)];
+                  const uint32_t ev = __float_as_uint(key[KP - 1]) & kSlotMask; // slot that drops out
+                  const float v = __uint_as_float((__float_as_uint(kk) & ~kSlotMask) | ev);
+                  const bool ins = mask != 0u && v < key[KP - 1];
+                  if (ins)
+                     colv[ev] = cbase + jj;
+                  insert_packed<KP>(key, ins ? v : INFINITY);
+                  mask &= mask - 1u;
+               }
+               thr = row_ok ? key[KP - 1] : -INFINITY;
             }
-         }
-         if (h == 0)
-         {
+            ptx::tc_fence_before();
             __syncwarp();
             if (lane == 0)
-               ptx::mbar_arrive(&merge_done[q]);
-            const uint32_t nrows = __popc(__ballot_sync(0xffffffffu, row_ok));
-            const uint32_t nfail = __popc(__ballot_sync(0xffffffffu, row_ok && !cert));
-            if (lane == 0)
+               ptx::mbar_arrive(&acc_empty[b]);
+         }
+         if (!ok)
+            break;
+         if (row_ok)
+         {
+            float4 *kd = reinterpret_cast<float4 *>(p.cand_key + (size_t(w.row_begin + r) * 2u + h) * KP);
+            uint4 *cd = reinterpret_cast<uint4 *>(p.cand_col + (size_t(w.row_begin + r) * 2u + h) * KP);
+#pragma unroll
+            for (int i = 0; i < KP / 4; ++i)
             {
-               if (nrows - nfail)
-                  atomicAdd(&p.counters[0], (unsigned long long)(nrows - nfail));
-               if (nfail)
-                  atomicAdd(&p.counters[1], (unsigned long long)nfail);
+               kd[i] = make_float4(key[4 * i], key[4 * i + 1], key[4 * i + 2], key[4 * i + 3]);
+               cd[i] = make_uint4(colv[__float_as_uint(key[4 * i]) & kSlotMask],
+                                  colv[__float_as_uint(key[4 * i + 1]) & kSlotMask],
+                                  colv[__float_as_uint(key[4 * i + 2]) & kSlotMask],
+                                  colv[__float_as_uint(key[4 * i + 3]) & kSlotMask]);
             }
          }
          __syncwarp();
@@ -850,10 +790,173 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
    }
 }
 
+// ------------------------------------------------------------------ rerank + certificate
+// One block per work item; TPR threads per row (one or two candidates each), RPB rows
+// per pass.  Keys are the packed prefilter keys: within 2^-17 relative of the fp32 key.
+template <int KP>
+__global__ void __launch_bounds__(256) rerank_kernel(const RerankParams p)
+{
+   constexpr uint32_t TPR = KP <= 16 ? 16u : 32u;
+   constexpr uint32_t RPB = 256u / TPR;
+   __shared__ uint32_t s_col[RPB][KP];
+   __shared__ float s_key[RPB][KP];
+   __shared__ float s_d[RPB][KP];
+   __shared__ double s_lim[RPB];
+   __shared__ float s_maxn2;
+   __shared__ uint32_t s_total;
+   __shared__ unsigned long long s_cnt[2];
+   const WorkItem w = p.items[blockIdx.x];
+   const uint32_t tid = threadIdx.x;
+   if (tid < 32)
+   {
+      float m = 0.f;
+      uint32_t tot = 0;
+      for (uint32_t s = tid; s < w.seg_count; s += 32)
+      {
+         const Segment sg = p.segs[w.seg_begin + s];
+         m = fmaxf(m, p.group_maxn2[sg.group_id]);
+         tot += sg.x_count;
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1)
+      {
+         m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+         tot += __shfl_xor_sync(0xffffffffu, tot, o);
+      }
+      if (tid == 0)
+      {
+         s_maxn2 = m;
+         s_total = tot;
+         s_cnt[0] = s_cnt[1] = 0;
+      }
+   }
+   __syncthreads();
+   const uint32_t total = s_total;
+   const uint32_t m = total < uint32_t(KP) ? total : uint32_t(KP);
+   const uint32_t rl = tid / TPR, sub = tid % TPR;
+   const bool vec4 = (p.d & 3u) == 0;
+   const double pk = 1.0 / 131072.0; // packed-key tolerance, 2^-17 relative
+   const double bmax = sqrt((double)s_maxn2 * (1.0 + p.gd));
+   for (uint32_t base = 0; base < w.row_count; base += RPB)
+   {
+      const uint32_t r = base + rl;
+      const bool ok = r < w.row_count;
+      const uint32_t row = w.row_begin + r;
+      const double qn = ok ? (double)__ldg(p.xnorm + row) : 0.0;
+      const double ahi = sqrt(qn * (1.0 + p.gd));
+      // |key - (||b||^2 - 2 a.b)| <= bound for every column of this row
+      const double bound = (p.c1 * ahi * bmax + p.c2 * bmax * bmax) * (1.0 + 1.0 / 1024.0);
+      if (ok && sub == 0)
+      {
+         float k0[KP];
+         uint32_t c0[KP];
+         const float *kp = p.cand_key + size_t(row) * 2u * KP;
+         const uint32_t *cp = p.cand_col + size_t(row) * 2u * KP;
+#pragma unroll
+         for (int i = 0; i < KP; ++i)
+         {
+            k0[i] = kp[i];
+            c0[i] = cp[i];
+         }
+#pragma unroll 1
+         for (int i = 0; i < KP; ++i)
+            insert_key<KP>(k0, c0, kp[KP + i], cp[KP + i]);
+         float kk = INFINITY;
+#pragma unroll
+         for (int i = 0; i < KP; ++i)
+         {
+            s_key[rl][i] = k0[i];
+            s_col[rl][i] = c0[i];
+            if (uint32_t(i) == p.k - 1)
+               kk = k0[i];
+         }
+         // a candidate whose smallest possible reference distance exceeds the largest
+         // possible one of the k-th candidate cannot enter the top-k: no need to rerank it
+         const double khi = (double)kk + fabs((double)kk) * pk;
+         s_lim[rl] = (khi + qn * (1.0 + p.gd) + bound) * (1.0 + p.gref);
+      }
+      __syncthreads();
+      if (ok)
+      {
+         const float *qv = p.X + size_t(row) * p.d;
+         const double a2lo = qn * (1.0 - p.gd);
+         for (uint32_t i = sub; i < m; i += TPR)
+         {
+            const double kc = (double)s_key[rl][i];
+            const double lo = fmax(0.0, kc - fabs(kc) * pk + a2lo - bound) * (1.0 - p.gref);
+            float D = INFINITY;
+            if (!(lo > s_lim[rl]))
+            {
+               const float *xv = p.X + size_t(s_col[rl][i]) * p.d;
+               D = vec4 ? ref_l2<true>(qv, xv, p.d) : ref_l2<false>(qv, xv, p.d);
+            }
+            s_d[rl][i] = D;
+         }
+      }
+      __syncthreads();
+      if (ok && sub == 0)
+      {
+         float sd[KP];
+         uint32_t si[KP];
+#pragma unroll
+         for (int i = 0; i < KP; ++i)
+         {
+            sd[i] = INFINITY;
+            si[i] = 0xFFFFFFFFu;
+         }
+#pragma unroll 1
+         for (uint32_t i = 0; i < m; ++i)
+            if (s_d[rl][i] != INFINITY)
+               insert_pair<KP>(sd, si, s_d[rl][i], s_col[rl][i]);
+         // certificate: every column outside the list has key >= T (up to the packing
+         // tolerance), hence true squared distance >= ||a||^2 + T - bound and reference
+         // distance >= that * (1 - gref); above the k-th exact distance, no excluded
+         // column can enter the top-k
+         bool cert = true;
+         if (total > uint32_t(KP))
+         {
+            float dk = INFINITY;
+#pragma unroll
+            for (int i = 0; i < KP; ++i)
+               if (uint32_t(i) == p.k - 1)
+                  dk = sd[i];
+            const double Tp = (double)s_key[rl][KP - 1];
+            const double T = Tp - fabs(Tp) * pk;
+            const double a2lo = qn * (1.0 - p.gd);
+            const double lhs = (a2lo + T - bound) * (1.0 - p.gref);
+            cert = lhs > (double)dk;
+         }
+#pragma unroll
+         for (int i = 0; i < KP; ++i)
+            if (uint32_t(i) < p.k)
+            {
+               p.out_ids[size_t(row) * p.k + i] = si[i];
+               if (p.out_dists)
+                  p.out_dists[size_t(row) * p.k + i] = sd[i];
+            }
+         if (!cert)
+         {
+            const uint32_t pos = atomicAdd(p.fb_count, 1u);
+            p.fb_rows[pos] = row;
+            p.fb_items[pos] = blockIdx.x + p.item_offset;
+         }
+         atomicAdd(&s_cnt[cert ? 0 : 1], 1ull);
+      }
+      __syncthreads();
+   }
+   if (tid == 0)
+   {
+      if (s_cnt[0])
+         atomicAdd(&p.counters[0], s_cnt[0]);
+      if (s_cnt[1])
+         atomicAdd(&p.counters[1], s_cnt[1]);
+   }
+}
+
 template <int KP, bool A_RES>
 cudaError_t launch_tc_t(const TcMaps &maps, const TcParams &p, uint32_t grid, cudaStream_t s)
 {
-   const TcLayout L = tc_layout(p.dp, A_RES, KP);
+   const TcLayout L = tc_layout(p.dp, A_RES);
    const size_t smem = L.total + 1024;
    cudaError_t e = cudaFuncSetAttribute(tc_kernel<KP, A_RES>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
    if (e != cudaSuccess)
@@ -876,20 +979,18 @@ cudaError_t launch_exact_t(const ExactParams &p, uint32_t grid, cudaStream_t s)
 
 int tc_candidates_for_k(uint32_t k)
 {
-   // the smallest candidate list with at least two entries of slack past k
+   // the smallest candidate list with at least eight entries of slack past k: with
+   // less slack the certificate rejects a few percent of rows on dense data
    if (k == 0 || k > kTcMaxK)
       return 0;
-   return k + 2 <= 8 ? 8 : k + 2 <= 16 ? 16 : k + 2 <= 24 ? 24 : 32;
+   return k + 8 <= 16 ? 16 : k + 8 <= 24 ? 24 : 32;
 }
 
 bool tc_a_resident(uint32_t dp) { return dp <= 128; }
 
-size_t tc_smem_bytes(uint32_t dp, uint32_t k)
-{
-   return tc_layout(dp, tc_a_resident(dp), (uint32_t)tc_candidates_for_k(k)).total + 1024;
-}
+size_t tc_smem_bytes(uint32_t dp, uint32_t) { return tc_layout(dp, tc_a_resident(dp)).total + 1024; }
 
-void tc_certificate_constants(uint32_t d, uint32_t dp, TcParams &p)
+void tc_certificate_constants(uint32_t d, uint32_t dp, RerankParams &p)
 {
    const double u24 = std::ldexp(1.0, -24);
    // relative error of a TF32-rounded centred value against the exact centred value
@@ -957,12 +1058,9 @@ cudaError_t launch_exact(const ExactParams &p, uint32_t grid, cudaStream_t s)
    return launch_exact_t<128>(p, grid, s);
 }
 
-cudaError_t launch_tc(const TcMaps &maps, const TcParams &p, uint32_t grid, cudaStream_t s)
+cudaError_t launch_tc(const TcMaps &maps, const TcParams &p, uint32_t kp, uint32_t grid, cudaStream_t s)
 {
-   const int kp = tc_candidates_for_k(p.k);
    const bool ares = tc_a_resident(p.dp);
-   if (kp == 8)
-      return ares ? launch_tc_t<8, true>(maps, p, grid, s) : launch_tc_t<8, false>(maps, p, grid, s);
    if (kp == 16)
       return ares ? launch_tc_t<16, true>(maps, p, grid, s) : launch_tc_t<16, false>(maps, p, grid, s);
    if (kp == 24)
@@ -970,6 +1068,21 @@ cudaError_t launch_tc(const TcMaps &maps, const TcParams &p, uint32_t grid, cuda
    if (kp == 32)
       return ares ? launch_tc_t<32, true>(maps, p, grid, s) : launch_tc_t<32, false>(maps, p, grid, s);
    return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_rerank(const RerankParams &p, uint32_t kp, uint32_t num_items, cudaStream_t s)
+{
+   if (num_items == 0)
+      return cudaSuccess;
+   if (kp == 16)
+      rerank_kernel<16><<<num_items, 256, 0, s>>>(p);
+   else if (kp == 24)
+      rerank_kernel<24><<<num_items, 256, 0, s>>>(p);
+   else if (kp == 32)
+      rerank_kernel<32><<<num_items, 256, 0, s>>>(p);
+   else
+      return cudaErrorInvalidValue;
+   return cudaGetLastError();
 }
 
 } // namespace ungx

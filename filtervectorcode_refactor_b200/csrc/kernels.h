@@ -13,27 +13,43 @@ namespace ungx
 struct TcMaps
 {
    CUtensorMap a;     // operand rows, box {32 cols, 128 rows}
-   CUtensorMap b[5];  // operand rows, box {32 cols, 16 << i rows}
+   CUtensorMap b[4];  // operand rows, box {32 cols, 16 << i rows}
 };
 
+// Tensor-core prefilter: per source row, the KP smallest keys ||x||^2 - 2 q.x of each
+// column half, written to cand_key / cand_col [row][2][KP].
 struct TcParams
 {
    const WorkItem *items;
    const Segment *segs;
    uint32_t num_items;
    uint32_t *item_counter;   // zeroed before launch
-   const float *X;           // original reordered vectors [n x d]
    const float *xnorm;       // ||fl(x - mean)||^2, fp32
+   uint32_t dp;
+   float *cand_key;
+   uint32_t *cand_col;
+   int *status;              // 0 or a UNGX_ERR_* code
+   unsigned long long timeout_ns;
+};
+
+// Exact rerank + certificate of the candidates.
+struct RerankParams
+{
+   const WorkItem *items;
+   const Segment *segs;
+   uint32_t item_offset;
+   const float *X;           // original reordered vectors [n x d]
+   const float *xnorm;
    const float *group_maxn2; // [G+1] max xnorm per group
-   uint32_t n, d, dp, k;
+   uint32_t d, k;
+   const float *cand_key;
+   const uint32_t *cand_col;
    uint32_t *out_ids;
    float *out_dists;
    uint32_t *fb_rows;        // rows the certificate rejected
    uint32_t *fb_items;
    uint32_t *fb_count;       // zeroed before launch
    unsigned long long *counters; // [0] certified rows, [1] rejected rows
-   int *status;              // 0 or a UNGX_ERR_* code
-   unsigned long long timeout_ns;
    double c1, c2, gd, gref;  // certificate constants, see tc_certificate_constants
 };
 
@@ -52,14 +68,14 @@ struct ExactParams
 };
 
 // Largest k the tensor-core route supports (candidate list of 32 per row).
-constexpr uint32_t kTcMaxK = 30;
+constexpr uint32_t kTcMaxK = 24;
 // Largest k the exact route supports (per-lane list of 128).
 constexpr uint32_t kExactMaxK = 128;
 
-int tc_candidates_for_k(uint32_t k);              // 16 or 32; 0 = unsupported
+int tc_candidates_for_k(uint32_t k);              // 8, 16, 24 or 32; 0 = unsupported
 bool tc_a_resident(uint32_t dp);                  // A operand kept in smem per item
 size_t tc_smem_bytes(uint32_t dp, uint32_t k);
-void tc_certificate_constants(uint32_t d, uint32_t dp, TcParams &p);
+void tc_certificate_constants(uint32_t d, uint32_t dp, RerankParams &p);
 
 cudaError_t launch_colsum(const float *X, uint32_t n, uint32_t d, double *sums, cudaStream_t s);
 cudaError_t launch_center(const float *X, const double *sums, uint32_t n, uint32_t d, uint32_t dp, float *mean,
@@ -69,6 +85,7 @@ cudaError_t launch_group_maxnorm(const float *xnorm, const uint32_t *ranges, uin
 cudaError_t launch_fill_empty(const RowRange *ranges, uint32_t nranges, uint32_t k, uint32_t *ids, float *dists,
                               cudaStream_t s);
 cudaError_t launch_exact(const ExactParams &p, uint32_t grid_hint, cudaStream_t s);
-cudaError_t launch_tc(const TcMaps &maps, const TcParams &p, uint32_t grid, cudaStream_t s);
+cudaError_t launch_tc(const TcMaps &maps, const TcParams &p, uint32_t kp, uint32_t grid, cudaStream_t s);
+cudaError_t launch_rerank(const RerankParams &p, uint32_t kp, uint32_t num_items, cudaStream_t s);
 
 } // namespace ungx

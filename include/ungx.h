@@ -67,6 +67,7 @@ typedef struct
    double plan_ms;       /* host work-item planning */
    double prepare_ms;    /* centring / rounding / norm kernels */
    double tc_kernel_ms;  /* tensor-core prefilter kernel alone */
+   double rerank_ms;     /* exact rerank + certificate of the candidates */
    double fallback_ms;   /* exact rescan of rows the certificate rejected */
    uint64_t pairs;       /* sum over LNG edges f->f' of |f|*|f'| (the reference's dim_ops / dim) */
    uint64_t rows_certified;
@@ -145,8 +146,10 @@ int ungx_cross_edges_generate_device(ungx_context *ctx, const ungx_cross_edge_pr
                                      uint32_t *d_out_ids, float *d_out_dists, void *stream,
                                      ungx_cross_edge_timing *timing);
 
-/* One call = prepare + generate + release with host buffers: the whole step as
- * the reference's UniNavGraph calls it. */
+/* One call = prepare + generate with host buffers: the whole step as the
+ * reference's UniNavGraph calls it.  The device buffers stay allocated in the
+ * context and are reused by the next call; ungx_release_base_vectors or
+ * ungx_context_destroy frees them. */
 int ungx_cross_edges_build(ungx_context *ctx, const float *vectors, const ungx_cross_edge_problem *problem,
                            uint32_t *out_ids, float *out_dists, ungx_cross_edge_timing *timing);
 
