@@ -29,6 +29,9 @@ ROUTE_EXACT = 2
 
 EMPTY_ID = 0xFFFFFFFF
 
+INJECT_NONE = 0
+INJECT_WITHHOLD_WORK = 1
+
 
 class UngxError(RuntimeError):
     def __init__(self, status: int, message: str):
@@ -86,6 +89,7 @@ _SIGNATURES = [
     ("ungx_status_string", c_char_p, [c_int]),
     ("ungx_set_timeout_ms", c_int, [c_void_p, c_uint32]),
     ("ungx_set_device_wait_limit_ns", c_int, [c_void_p, c_uint64]),
+    ("ungx_set_fault_injection", c_int, [c_void_p, c_uint32]),
     ("ungx_prepare_base_vectors", c_int, [c_void_p, c_void_p, c_uint32, c_uint32, c_int]),
     ("ungx_release_base_vectors", c_int, [c_void_p]),
     ("ungx_cross_edges_generate", c_int,
@@ -237,6 +241,9 @@ class Context:
 
     def set_device_wait_limit_ns(self, ns: int) -> None:
         check(lib.ungx_set_device_wait_limit_ns(self.h, ns), self.h)
+
+    def set_fault_injection(self, flags: int) -> None:
+        check(lib.ungx_set_fault_injection(self.h, flags), self.h)
 
     def prepare_base_vectors(self, vectors, num_points: int, dim: int, on_device: bool) -> None:
         """``vectors`` is a host numpy array, or (on_device=True) an integer device pointer."""

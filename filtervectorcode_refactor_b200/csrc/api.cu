@@ -70,6 +70,7 @@ struct ungx_context
    std::string err;
    uint32_t timeout_ms = 120000;
    uint64_t device_wait_ns = 4000000000ull;
+   uint32_t inject = UNGX_INJECT_NONE;
    PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
    // resident base vectors (a4)
    bool have_vectors = false;
@@ -127,6 +128,9 @@ int wait_event(ungx_context *ctx, cudaEvent_t ev, const char *what)
    }
 }
 
+// Tensor map over the TF32-valued fp32 operand [rows x cols]: boxes of 32 columns
+// (128 bytes, the 128-byte swizzle the MMA descriptors expect) by box_rows rows.
+// Rows past the end read as zero.
 int make_map(ungx_context *ctx, CUtensorMap *map, void *base, uint32_t rows, uint32_t cols, uint32_t box_rows)
 {
    cuuint64_t dims[2] = {cols, rows};
@@ -281,6 +285,7 @@ int run_generate(ungx_context *ctx, const ungx_cross_edge_problem &p, const Plan
       tp.cand_col = ctx->cand_col.as<uint32_t>();
       tp.status = status;
       tp.timeout_ns = ctx->device_wait_ns;
+      tp.inject = ctx->inject;
       const uint32_t grid = (uint32_t)std::min<size_t>(plan.items.size(), (size_t)ctx->num_sms);
       UNGX_CUDA(ctx, ungx::launch_tc(maps, tp, (uint32_t)kp, grid, s), "tensor-core kernel launch");
       UNGX_CUDA(ctx, cudaEventRecord(ev[3], s), "event");
@@ -291,6 +296,8 @@ int run_generate(ungx_context *ctx, const ungx_cross_edge_problem &p, const Plan
       rp.X = ctx->X;
       rp.xnorm = tp.xnorm;
       rp.group_maxn2 = ctx->gmax.as<float>();
+      rp.n = ctx->n;
+      rp.status = status;
       rp.d = ctx->d;
       rp.k = k;
       rp.cand_key = tp.cand_key;
@@ -316,7 +323,7 @@ int run_generate(ungx_context *ctx, const ungx_cross_edge_problem &p, const Plan
       ep.count_dev = rp.fb_count;
       ep.out_ids = d_ids;
       ep.out_dists = d_dists;
-      UNGX_CUDA(ctx, ungx::launch_exact(ep, (uint32_t)ctx->num_sms * 4, s), "fallback kernel launch");
+      UNGX_CUDA(ctx, ungx::launch_exact(ep, (uint32_t)ctx->num_sms * 8, s), "fallback kernel launch");
       t.gpu_launches += 4;
    }
    else if (!plan.items.empty())
@@ -344,7 +351,8 @@ int run_generate(ungx_context *ctx, const ungx_cross_edge_problem &p, const Plan
       ep.count_host = (uint32_t)rows.size();
       ep.out_ids = d_ids;
       ep.out_dists = d_dists;
-      const uint32_t grid = (uint32_t)std::min<uint64_t>((rows.size() + 7) / 8, (uint64_t)ctx->num_sms * 16);
+      // one block per row, persistent over the row list
+      const uint32_t grid = (uint32_t)std::min<uint64_t>(rows.size(), (uint64_t)ctx->num_sms * 8);
       UNGX_CUDA(ctx, ungx::launch_exact(ep, std::max(grid, 1u), s), "exact kernel launch");
       t.gpu_launches += 1;
    }
@@ -491,6 +499,14 @@ int ungx_set_device_wait_limit_ns(ungx_context *ctx, uint64_t limit_ns)
    if (!ctx || limit_ns == 0)
       return fail(ctx, UNGX_ERR_INVALID_ARG, "ungx_set_device_wait_limit_ns: bad argument");
    ctx->device_wait_ns = limit_ns;
+   return UNGX_OK;
+}
+
+int ungx_set_fault_injection(ungx_context *ctx, uint32_t flags)
+{
+   if (!ctx || flags > UNGX_INJECT_WITHHOLD_WORK)
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "ungx_set_fault_injection: bad argument");
+   ctx->inject = flags;
    return UNGX_OK;
 }
 

@@ -1,13 +1,14 @@
 // Device code of the B200 cross-edge builder (sm_100a).
 //
-//   colsum / center     resident operand build (a4): mean, centred + TF32-rounded
+//   colsum / center     resident operand build (a4): mean, centred + BF16-rounded
 //                       copy padded to 32 columns, fp32 row norms.
 //   tc_kernel           the hot path.  Persistent CTAs pull source-centric work items
 //                       (<=128 rows of one source group x all its LNG target groups);
 //                       TMA stages the item's source rows once (operand A) and the
-//                       target rows in 128-row tiles through an 8-stage shared-memory
-//                       ring; one thread issues tcgen05.mma kind::tf32 into four
-//                       128-column TMEM accumulators; eight epilogue warps read TMEM
+//                       target rows in 128-row tiles through a shared-memory ring of
+//                       up to 16 stages; one thread issues tcgen05.mma kind::f16 (bf16
+//                       operands, fp32 accumulate) into four 128-column TMEM
+//                       accumulators; eight epilogue warps read TMEM
 //                       rows (thread = source row), form the keys ||x||^2 - 2 q.x and
 //                       keep a sorted register top-KP per row and column half.  The two
 //                       lists of every row go to a small candidate buffer; no distance
@@ -34,8 +35,11 @@ constexpr uint32_t kTcThreads = 320; // warp 0 TMA, warp 1 MMA, warps 2..9 epilo
 constexpr uint32_t kBN = 128;        // target columns per tile / TMEM accumulator
 constexpr uint32_t kAccBufs = 4;     // TMEM accumulators (4 x 128 columns = all 512)
 constexpr uint32_t kItemSlots = 2;
-constexpr uint32_t kAChunk = 128 * 128; // 128 rows x 32 fp32, 128-byte swizzled
-constexpr uint32_t kBChunk = kBN * 128; // 128 rows x 32 fp32
+constexpr uint32_t kChunkK = 32;          // fp32 columns per K chunk: 128-byte rows
+constexpr uint32_t kAChunk = 128 * 128;   // 128 rows x 32 fp32, 128-byte swizzled
+constexpr uint32_t kBChunk = kBN * 128;   // 128 rows x 32 fp32
+constexpr uint32_t kMaxStages = 16;
+constexpr uint32_t kSmemLimit = 232448;   // per-block opt-in maximum on sm_100
 constexpr uint32_t kNoItem = 0xFFFFFFFFu;
 // Limit of the waits that retire work already in flight before the CTA exits
 // (independent of the configurable pipeline wait limit, which tests set tiny).
@@ -43,28 +47,33 @@ constexpr uint64_t kDrainWaitNs = 2000000000ull;
 
 struct TcLayout
 {
-   uint32_t stages, a_off, a_bytes, stage_off, stage_bytes, keys_off, norm_off, bar_off, misc_off, total;
+   uint32_t stages, a_off, a_bytes, stage_off, stage_bytes, colv_off, norm_off, bar_off, misc_off, total;
 };
 
-// A resident (dp <= 128): A = dp/32 chunks of 16 KB kept per item, 8 stages of one
-// 16 KB target chunk.  A streamed: 6 stages of (16 KB source + 16 KB target) chunks.
-// Then 4 KB per epilogue warp for a chunk's 32 x 32 keys, the chunk norms, barriers.
-__host__ __device__ inline TcLayout tc_layout(uint32_t dp, bool a_res)
+// A resident (dp <= 128): A = dp/32 chunks of 16 KB kept per item, then as many
+// 16 KB target-chunk stages as fit (at most 16).  A streamed: stages of (16 KB
+// source + 16 KB target) chunks.  Then the epilogue's column table (8 warps x KP
+// slots x 32 lanes), the chunk norms, barriers, and the item slots.
+__host__ __device__ inline TcLayout tc_layout(uint32_t dp, bool a_res, uint32_t kp)
 {
    TcLayout L;
-   L.stages = a_res ? 8u : 6u;
    L.a_off = 0;
-   L.a_bytes = a_res ? (dp / 32) * kAChunk : 0;
+   L.a_bytes = a_res ? (dp / kChunkK) * kAChunk : 0;
    L.stage_off = L.a_bytes;
    L.stage_bytes = a_res ? kBChunk : kAChunk + kBChunk;
-   L.keys_off = L.stage_off + L.stages * L.stage_bytes;
-   L.norm_off = L.keys_off + 8 * 32 * 32 * 4;
-   L.bar_off = L.norm_off + 8 * 32 * 4;
-   L.misc_off = L.bar_off + 40 * 8;
-   L.total = L.misc_off + 128;
+   const uint32_t fixed = L.a_bytes + 8u * kp * 32u * 4u + 8u * 32u * 4u + 48u * 8u + 128u + 1024u;
+   const uint32_t fit = fixed < kSmemLimit ? (kSmemLimit - fixed) / L.stage_bytes : 0u;
+   L.stages = fit < kMaxStages ? fit : kMaxStages;
+   L.colv_off = L.stage_off + L.stages * L.stage_bytes;
+   L.norm_off = L.colv_off + 8u * kp * 32u * 4u;
+   L.bar_off = L.norm_off + 8u * 32u * 4u;
+   L.misc_off = L.bar_off + 48u * 8u;
+   L.total = L.misc_off + 128u;
    return L;
 }
 
+// Round to the nearest TF32 value (10 explicit mantissa bits, ties to even), kept
+// in fp32 storage with the 13 low bits zero, so the tensor core reads it exactly.
 __device__ __forceinline__ float tf32_rne(float v)
 {
    uint32_t u = __float_as_uint(v);
@@ -72,6 +81,25 @@ __device__ __forceinline__ float tf32_rne(float v)
       return v;
    u += 0xFFFu + ((u >> 13) & 1u);
    return __uint_as_float(u & 0xFFFFE000u);
+}
+
+// v[j] for a per-thread index j in 0..31, by a 5-level select tree (registers only).
+__device__ __forceinline__ float select32(const float (&v)[32], uint32_t j)
+{
+   float a[16], b[8], c[4], e[2];
+#pragma unroll
+   for (int i = 0; i < 16; ++i)
+      a[i] = (j & 1u) ? v[2 * i + 1] : v[2 * i];
+#pragma unroll
+   for (int i = 0; i < 8; ++i)
+      b[i] = (j & 2u) ? a[2 * i + 1] : a[2 * i];
+#pragma unroll
+   for (int i = 0; i < 4; ++i)
+      c[i] = (j & 4u) ? b[2 * i + 1] : b[2 * i];
+#pragma unroll
+   for (int i = 0; i < 2; ++i)
+      e[i] = (j & 8u) ? c[2 * i + 1] : c[2 * i];
+   return (j & 16u) ? e[1] : e[0];
 }
 
 // Squared L2 in the reference's order: 8 accumulators over i mod 8 with the update
@@ -283,15 +311,17 @@ __global__ void fill_empty_kernel(const RowRange *__restrict__ ranges, uint32_t 
 }
 
 // ------------------------------------------------------------------ exact scan
-// One warp per row: lanes stride over the row's candidate columns keeping a sorted
-// top-KMAX each, then k rounds of a warp arg-min by (distance, id) emit the result.
+// One block (8 warps) per row: the 256 threads stride over the row's candidate
+// columns keeping a sorted top-KMAX each; every warp then emits its own top-k by k
+// rounds of a warp arg-min over (distance, id), and one thread merges the 8 lists.
 template <int KMAX, bool VEC4>
 __global__ void __launch_bounds__(256) exact_rows_kernel(const ExactParams p)
 {
+   __shared__ float s_d[8][KMAX];
+   __shared__ uint32_t s_i[8][KMAX];
    const uint32_t count = p.count_dev ? *(volatile const uint32_t *)p.count_dev : p.count_host;
-   const uint32_t lane = threadIdx.x & 31;
-   const uint32_t nw = (gridDim.x * blockDim.x) >> 5;
-   for (uint32_t w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < count; w += nw)
+   const uint32_t lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+   for (uint32_t w = blockIdx.x; w < count; w += gridDim.x)
    {
       const uint32_t row = p.rows[w];
       const WorkItem it = p.items[p.row_items[w]];
@@ -308,7 +338,7 @@ __global__ void __launch_bounds__(256) exact_rows_kernel(const ExactParams p)
       {
          const Segment sg = p.segs[it.seg_begin + s];
          const uint32_t end = sg.x_begin + sg.x_count;
-         for (uint32_t x = sg.x_begin + lane; x < end; x += 32)
+         for (uint32_t x = sg.x_begin + threadIdx.x; x < end; x += blockDim.x)
          {
             const float D = ref_l2<VEC4>(q, p.X + size_t(x) * p.d, p.d);
             if (pair_less(D, x, bd[KMAX - 1], bi[KMAX - 1]))
@@ -343,11 +373,32 @@ __global__ void __launch_bounds__(256) exact_rows_kernel(const ExactParams p)
          }
          if (lane == 0)
          {
-            p.out_ids[size_t(row) * p.k + o] = mi;
-            if (p.out_dists)
-               p.out_dists[size_t(row) * p.k + o] = (mi == 0xFFFFFFFFu) ? INFINITY : md;
+            s_d[wid][o] = md;
+            s_i[wid][o] = mi;
          }
       }
+      __syncthreads();
+      if (threadIdx.x == 0)
+      {
+#pragma unroll
+         for (int i = 0; i < KMAX; ++i)
+         {
+            bd[i] = INFINITY;
+            bi[i] = 0xFFFFFFFFu;
+         }
+         for (uint32_t wv = 0; wv < 8; ++wv)
+            for (uint32_t o = 0; o < p.k && s_i[wv][o] != 0xFFFFFFFFu; ++o)
+               insert_pair<KMAX>(bd, bi, s_d[wv][o], s_i[wv][o]);
+#pragma unroll
+         for (int i = 0; i < KMAX; ++i)
+            if (uint32_t(i) < p.k)
+            {
+               p.out_ids[size_t(row) * p.k + i] = bi[i];
+               if (p.out_dists)
+                  p.out_dists[size_t(row) * p.k + i] = bd[i];
+            }
+      }
+      __syncthreads();
    }
 }
 
@@ -429,29 +480,29 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
    extern __shared__ uint8_t smem_raw[];
    const uint32_t raw_u32 = ptx::smem_u32(smem_raw);
    uint8_t *smem = smem_raw + (((raw_u32 + 1023u) & ~1023u) - raw_u32);
-   const TcLayout L = tc_layout(p.dp, A_RES);
+   const TcLayout L = tc_layout(p.dp, A_RES, KP);
    const uint32_t S = L.stages;
    uint8_t *sA = smem + L.a_off;
    uint8_t *sStage = smem + L.stage_off;
    float *sNorm = reinterpret_cast<float *>(smem + L.norm_off);
+   uint32_t *sColv = reinterpret_cast<uint32_t *>(smem + L.colv_off);
    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bar_off);
-   uint64_t *full = bars;            // [S]
-   uint64_t *empty = bars + 8;       // [S]
-   uint64_t *acc_full = bars + 16;   // [4]
-   uint64_t *acc_empty = bars + 20;  // [4]
-   uint64_t *a_full = bars + 24;
-   uint64_t *a_empty = bars + 25;
-   uint64_t *item_full = bars + 26;  // [2]
-   uint64_t *item_empty = bars + 28; // [2]
-   uint64_t *done_bar = bars + 30;
+   uint64_t *full = bars;              // [S <= 16]
+   uint64_t *empty = bars + 16;        // [S]
+   uint64_t *acc_full = bars + 32;     // [4]
+   uint64_t *acc_empty = bars + 36;    // [4]
+   uint64_t *a_full = bars + 40;
+   uint64_t *a_empty = bars + 41;
+   uint64_t *item_full = bars + 42;    // [2]
+   uint64_t *item_empty = bars + 44;   // [2]
+   uint64_t *done_bar = bars + 46;
    volatile uint32_t *item_slot = reinterpret_cast<volatile uint32_t *>(smem + L.misc_off);
    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L.misc_off + 16);
    volatile int *abort_word = reinterpret_cast<volatile int *>(smem + L.misc_off + 32);
    WorkItem *item_desc = reinterpret_cast<WorkItem *>(smem + L.misc_off + 64); // [kItemSlots]
-   float *sKeys = reinterpret_cast<float *>(smem + L.keys_off);
 
    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-   const uint32_t nch = p.dp / 32;
+   const uint32_t nch = p.dp / kChunkK;
    const uint64_t tmo = p.timeout_ns;
 
    if (threadIdx.x == 0)
@@ -496,7 +547,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
    if (warp == 0)
    {
       // ------------------------------------------------ TMA producer
-      if (lane == 0)
+      if (lane == 0 && !(p.inject & UNGX_INJECT_WITHHOLD_WORK))
       {
          uint32_t it = 0, iseq = 0, aseq = 0;
          bool ok = true;
@@ -527,7 +578,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
                }
                ptx::mbar_arrive_expect_tx(a_full, nch * kAChunk);
                for (uint32_t c = 0; c < nch; ++c)
-                  ptx::tma_load_2d(sA + c * kAChunk, &maps.a, a_full, int32_t(c * 32), int32_t(w.row_begin));
+                  ptx::tma_load_2d(sA + c * kAChunk, &maps.a, a_full, int32_t(c * kChunkK), int32_t(w.row_begin));
                ++aseq;
             }
             TileIter ti;
@@ -546,8 +597,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
                   uint8_t *dst = sStage + st * L.stage_bytes;
                   ptx::mbar_arrive_expect_tx(&full[st], (A_RES ? 0u : kAChunk) + brows * 128u);
                   if (!A_RES)
-                     ptx::tma_load_2d(dst, &maps.a, &full[st], int32_t(c * 32), int32_t(w.row_begin));
-                  ptx::tma_load_2d(dst + (A_RES ? 0u : kAChunk), &maps.b[bix], &full[st], int32_t(c * 32),
+                     ptx::tma_load_2d(dst, &maps.a, &full[st], int32_t(c * kChunkK), int32_t(w.row_begin));
+                  ptx::tma_load_2d(dst + (A_RES ? 0u : kAChunk), &maps.b[bix], &full[st], int32_t(c * kChunkK),
                                    int32_t(ti.x0()));
                   ++it;
                }
@@ -675,16 +726,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
          const WorkItem w = item_desc[slot];
          const bool row_ok = r < w.row_count;
          const bool warp_ok = q * 32u < w.row_count;
-         float key[KP];      // ascending packed keys (slot in the low bits)
-         uint32_t colv[KP];  // column of each slot (dynamically indexed)
+         float key[KP]; // ascending packed keys (slot in the low bits)
+         // column of each slot: colv[slot * 32 + lane] (bank = lane, conflict-free)
+         uint32_t *colv = sColv + (warp - 2u) * (KP * 32u) + lane;
 #pragma unroll
          for (int i = 0; i < KP; ++i)
          {
             key[i] = packed_init(i);
-            colv[i] = 0xFFFFFFFFu;
+            colv[i * 32] = 0xFFFFFFFFu;
          }
          float thr = row_ok ? key[KP - 1] : -INFINITY; // rows past the item never take candidates
-         float *kst = sKeys + (warp - 2u) * 1024u;      // 32 lanes x 32 keys, column-swizzled
          TileIter ti;
          ti.start(p.segs, w.seg_begin, w.seg_count);
          // norms of this warp's two chunks of the current tile; the next tile's are
@@ -726,13 +777,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
                uint32_t raw[32];
                ptx::tmem_ld32(tmem_base + ((q * 32u) << 16) + b * kBN + j * 32u, raw);
                ptx::tmem_wait_ld();
+               float kv[32];
                uint32_t mask = 0;
 #pragma unroll
                for (int jj = 0; jj < 32; ++jj)
                {
-                  const float kk = __fmaf_rn(-2.0f, __uint_as_float(raw[jj]), nrm[jj]);
-                  mask |= (kk < thr) ? (1u << jj) : 0u;
-                  kst[lane * 32u + (uint32_t(jj) ^ lane)] = kk;
+                  kv[jj] = __fmaf_rn(-2.0f, __uint_as_float(raw[jj]), nrm[jj]);
+                  mask |= (kv[jj] < thr) ? (1u << jj) : 0u;
                }
                // every lane inserts its passing keys; the loop runs as often as the
                // busiest lane needs, lanes without a candidate insert +inf (a no-op)
@@ -740,12 +791,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
                while (__any_sync(0xffffffffu, mask != 0u))
                {
                   const uint32_t jj = mask ? uint32_t(__ffs(mask) - 1) : 0u;
-                  const float kk = kst[lane * 32u + (jj ^ lane)];
+                  const float kk = select32(kv, jj);
                   const uint32_t ev = __float_as_uint(key[KP - 1]) & kSlotMask; // slot that drops out
                   const float v = __uint_as_float((__float_as_uint(kk) & ~kSlotMask) | ev);
                   const bool ins = mask != 0u && v < key[KP - 1];
                   if (ins)
-                     colv[ev] = cbase + jj;
+                     colv[ev * 32u] = cbase + jj;
                   insert_packed<KP>(key, ins ? v : INFINITY);
                   mask &= mask - 1u;
                }
@@ -766,10 +817,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
             for (int i = 0; i < KP / 4; ++i)
             {
                kd[i] = make_float4(key[4 * i], key[4 * i + 1], key[4 * i + 2], key[4 * i + 3]);
-               cd[i] = make_uint4(colv[__float_as_uint(key[4 * i]) & kSlotMask],
-                                  colv[__float_as_uint(key[4 * i + 1]) & kSlotMask],
-                                  colv[__float_as_uint(key[4 * i + 2]) & kSlotMask],
-                                  colv[__float_as_uint(key[4 * i + 3]) & kSlotMask]);
+               cd[i] = make_uint4(colv[(__float_as_uint(key[4 * i]) & kSlotMask) * 32u],
+                                  colv[(__float_as_uint(key[4 * i + 1]) & kSlotMask) * 32u],
+                                  colv[(__float_as_uint(key[4 * i + 2]) & kSlotMask) * 32u],
+                                  colv[(__float_as_uint(key[4 * i + 3]) & kSlotMask) * 32u]);
             }
          }
          __syncwarp();
@@ -805,6 +856,9 @@ __global__ void __launch_bounds__(256) rerank_kernel(const RerankParams p)
    __shared__ float s_maxn2;
    __shared__ uint32_t s_total;
    __shared__ unsigned long long s_cnt[2];
+   // an aborted prefilter left the candidate buffer unwritten: touch nothing
+   if (*reinterpret_cast<const volatile int *>(p.status) != 0)
+      return;
    const WorkItem w = p.items[blockIdx.x];
    const uint32_t tid = threadIdx.x;
    if (tid < 32)
@@ -885,9 +939,10 @@ __global__ void __launch_bounds__(256) rerank_kernel(const RerankParams p)
             const double kc = (double)s_key[rl][i];
             const double lo = fmax(0.0, kc - fabs(kc) * pk + a2lo - bound) * (1.0 - p.gref);
             float D = INFINITY;
-            if (!(lo > s_lim[rl]))
+            const uint32_t c = s_col[rl][i];
+            if (!(lo > s_lim[rl]) && c < p.n) // a column outside the matrix is never read
             {
-               const float *xv = p.X + size_t(s_col[rl][i]) * p.d;
+               const float *xv = p.X + size_t(c) * p.d;
                D = vec4 ? ref_l2<true>(qv, xv, p.d) : ref_l2<false>(qv, xv, p.d);
             }
             s_d[rl][i] = D;
@@ -956,7 +1011,9 @@ __global__ void __launch_bounds__(256) rerank_kernel(const RerankParams p)
 template <int KP, bool A_RES>
 cudaError_t launch_tc_t(const TcMaps &maps, const TcParams &p, uint32_t grid, cudaStream_t s)
 {
-   const TcLayout L = tc_layout(p.dp, A_RES);
+   const TcLayout L = tc_layout(p.dp, A_RES, KP);
+   if (L.stages < 2)
+      return cudaErrorInvalidValue;
    const size_t smem = L.total + 1024;
    cudaError_t e = cudaFuncSetAttribute(tc_kernel<KP, A_RES>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
    if (e != cudaSuccess)
@@ -988,14 +1045,19 @@ int tc_candidates_for_k(uint32_t k)
 
 bool tc_a_resident(uint32_t dp) { return dp <= 128; }
 
-size_t tc_smem_bytes(uint32_t dp, uint32_t) { return tc_layout(dp, tc_a_resident(dp)).total + 1024; }
+size_t tc_smem_bytes(uint32_t dp, uint32_t k)
+{
+   return tc_layout(dp, tc_a_resident(dp), (uint32_t)tc_candidates_for_k(k)).total + 1024;
+}
 
 void tc_certificate_constants(uint32_t d, uint32_t dp, RerankParams &p)
 {
    const double u24 = std::ldexp(1.0, -24);
-   // relative error of a TF32-rounded centred value against the exact centred value
+   // relative error of a TF32-rounded (11-bit significand, nearest-even) centred
+   // value against the exact centred value
    const double ur = u24 + std::ldexp(1.0, -11) * (1.0 + u24);
-   // tensor-core fp32 accumulation, taken 4x looser than one rounding per K=8 step
+   // tf32 x tf32 products are exact in fp32; the tensor-core fp32 accumulation is
+   // taken as 4x looser than one rounding per K=8 step
    const double cacc = (double(dp) / 2.0 + 8.0) * std::ldexp(1.0, -22);
    p.c1 = 4.0 * ur + 2.0 * ur * ur + 2.0 * cacc * (1.0 + ur) * (1.0 + ur) + 2.0 * std::ldexp(1.0, -23);
    p.c2 = (double(d) + 4.0) * u24 + std::ldexp(1.0, -23) + u24;

@@ -30,6 +30,7 @@ struct TcParams
    uint32_t *cand_col;
    int *status;              // 0 or a UNGX_ERR_* code
    unsigned long long timeout_ns;
+   uint32_t inject;          // UNGX_INJECT_* test hook
 };
 
 // Exact rerank + certificate of the candidates.
@@ -41,7 +42,8 @@ struct RerankParams
    const float *X;           // original reordered vectors [n x d]
    const float *xnorm;
    const float *group_maxn2; // [G+1] max xnorm per group
-   uint32_t d, k;
+   uint32_t n, d, k;
+   const int *status;        // the prefilter's status word: non-zero = nothing to rerank
    const float *cand_key;
    const uint32_t *cand_col;
    uint32_t *out_ids;

@@ -70,7 +70,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
    {
       if (mbar_try_wait(bar, parity))
          return true;
-      if ((spin & 63u) == 0)
+      if ((spin & 7u) == 0)
       {
          if (abort_word && *abort_word)
             return false;
@@ -118,7 +118,8 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols)
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// D[tmem] (+)= A[smem] * B[smem]^T, kind::tf32, one CTA.  accumulate = 0 overwrites D.
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::tf32 (fp32 accumulator), one CTA.
+// accumulate = 0 overwrites D.
 __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                          uint32_t accumulate)
 {
@@ -157,9 +158,10 @@ __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.
 
 // Shared-memory matrix descriptor for a K-major operand in the canonical
 // 128-byte-swizzle layout: rows of 128 B (32 fp32), 8-row atoms of 1024 B stacked
-// contiguously.  Fields: start address >> 4 [0,14), leading byte offset >> 4
-// [16,30) (unused for this layout, set to 1), stride byte offset >> 4 [32,46)
-// = 1024 B between 8-row atoms, version 1 [46,48), layout SWIZZLE_128B = 2 [61,64).
+// contiguously (what a TMA load with SWIZZLE_128B and a 128-byte inner box writes).
+// Fields: start address >> 4 [0,14), leading byte offset >> 4 [16,30) (unused for
+// swizzled K-major, set to 1), stride byte offset >> 4 [32,46) = 1024 B between
+// 8-row atoms, version 1 [46,48), layout SWIZZLE_128B = 2 [61,64).
 __device__ __forceinline__ uint64_t sdesc_k_sw128(uint32_t saddr)
 {
    uint64_t d = 0;
@@ -177,11 +179,6 @@ __device__ __forceinline__ uint64_t sdesc_k_sw128(uint32_t saddr)
 __host__ __device__ constexpr uint32_t idesc_tf32(uint32_t M, uint32_t N)
 {
    return (1u << 4) | (2u << 7) | (2u << 10) | ((N >> 3) << 17) | ((M >> 4) << 24);
-}
-
-__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads)
-{
-   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 } // namespace ptx

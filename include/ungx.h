@@ -110,6 +110,17 @@ int ungx_set_timeout_ms(ungx_context *ctx, uint32_t timeout_ms);
  * tensor memory and report UNGX_ERR_TIMEOUT; the context stays usable. */
 int ungx_set_device_wait_limit_ns(ungx_context *ctx, uint64_t limit_ns);
 
+/* Failure-detection test hook.  UNGX_INJECT_WITHHOLD_WORK makes the tensor-core
+ * kernel's producer warp publish no work item, as if it had been lost: the MMA
+ * and epilogue warps' bounded waits run out and the call returns
+ * UNGX_ERR_TIMEOUT without faulting the device.  0 restores normal operation. */
+enum
+{
+   UNGX_INJECT_NONE = 0,
+   UNGX_INJECT_WITHHOLD_WORK = 1
+};
+int ungx_set_fault_injection(ungx_context *ctx, uint32_t flags);
+
 /* ------------------------------------------ a4: resident base vectors + norms
  * Replaces gpu_prepare_all_vectors_on_device
  * (UNG/codes/src/gpu_cross_edge_resident_vectors.cuh:10-215): one upload of the

@@ -157,13 +157,17 @@ def test_wait_timeout_reports_and_context_survives(ctx):
     dists = np.empty(n * k, dtype=np.float32)
     ctx.prepare_base_vectors(g["Xr"], n, d, on_device=False)
     try:
-        ctx.set_device_wait_limit_ns(1)
+        # the producer warp withholds all work: every consumer wait must run out
+        ctx.set_device_wait_limit_ns(20_000_000)
+        ctx.set_fault_injection(nat.INJECT_WITHHOLD_WORK)
         with pytest.raises(nat.UngxError) as e:
             ctx.generate(prob, ids, dists)
         assert e.value.status == nat.UNGX_ERR_TIMEOUT
+        ctx.set_fault_injection(nat.INJECT_NONE)
         ctx.set_device_wait_limit_ns(4_000_000_000)
         ctx.generate(prob, ids, dists)
         assert_rows_match(ids, dists, g["ids"], g["dists"], k)
     finally:
+        ctx.set_fault_injection(nat.INJECT_NONE)
         ctx.set_device_wait_limit_ns(4_000_000_000)
         ctx.release_base_vectors()
