@@ -98,6 +98,8 @@ _SIGNATURES = [
      [c_void_p, POINTER(CrossEdgeProblem), c_void_p, c_void_p, c_void_p, POINTER(CrossEdgeTiming)]),
     ("ungx_cross_edges_build", c_int,
      [c_void_p, c_void_p, POINTER(CrossEdgeProblem), c_void_p, c_void_p, POINTER(CrossEdgeTiming)]),
+    ("ungx_cross_edges_exact_noalloc", c_int,
+     [POINTER(CrossEdgeProblem), c_void_p, c_void_p, c_void_p, c_void_p]),
     ("ungx_shard_rows", c_int, [POINTER(CrossEdgeProblem), c_void_p, POINTER(c_uint64)]),
     ("ungx_label_graph_build", c_int, [c_uint32, c_void_p, c_void_p, c_int, POINTER(c_void_p)]),
     ("ungx_label_graph_destroy", c_int, [c_void_p]),
@@ -272,6 +274,12 @@ class Context:
         check(lib.ungx_cross_edges_build(self.h, _ptr(vectors), ctypes.byref(problem.c), _ptr(out_ids),
                                          _ptr(out_dists), ctypes.byref(t)), self.h)
         return t
+
+
+def cross_edges_exact_noalloc(problem: Problem, d_vectors: int, d_ids: int, d_dists: int | None,
+                              stream: int | None = None) -> None:
+    """ungx_cross_edges_exact_noalloc: device pointers in and out, no device allocation."""
+    check(lib.ungx_cross_edges_exact_noalloc(ctypes.byref(problem.c), d_vectors, d_ids, d_dists, stream))
 
 
 def flat_to_csr(flat_ids: np.ndarray, num_points: int, topk: int) -> tuple[np.ndarray, np.ndarray]:

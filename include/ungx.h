@@ -164,6 +164,26 @@ int ungx_cross_edges_generate_device(ungx_context *ctx, const ungx_cross_edge_pr
 int ungx_cross_edges_build(ungx_context *ctx, const float *vectors, const ungx_cross_edge_problem *problem,
                            uint32_t *out_ids, float *out_dists, ungx_cross_edge_timing *timing);
 
+/* The exact route without any device allocation.  No counterpart in the reference.
+ * For callers that cannot call cudaMalloc when they need the cross edges: code that
+ * is recording a CUDA graph (allocation is not allowed during stream capture), code
+ * whose device memory belongs to another allocator (a framework's caching
+ * allocator, a pool with a hard budget), or a service that must not grow its
+ * device footprint after start-up.  The caller passes the reordered base vectors
+ * (`d_vectors`, device, n x d fp32) and the device outputs (`d_out_ids` [n*k],
+ * `d_out_dists` [n*k] or NULL); the rows' results are those of
+ * ungx_cross_edges_generate with UNGX_ROUTE_EXACT.  The work plan lives in one
+ * 64 MiB __device__ array of the library (held by every GPU that loads it until
+ * the process exits), so the plan must fit: about 8 bytes per source row plus 16
+ * per work item and target segment; larger problems return UNGX_ERR_INVALID_ARG
+ * naming the size.  Runs on the current device and on `stream` (a cudaStream_t,
+ * NULL = the legacy stream); returns after the work finished (bounded wait).  The
+ * first call on each device fetches the array's device address, so make it before
+ * any stream capture.  All calls share the array: calls that overlap on the GPU
+ * race.  Errors are reported through ungx_last_error(NULL). */
+int ungx_cross_edges_exact_noalloc(const ungx_cross_edge_problem *problem, const float *d_vectors,
+                                   uint32_t *d_out_ids, float *d_out_dists, void *stream);
+
 /* Rows (reordered vector ids) this shard owns, ascending; `*count` receives the
  * number.  `rows` may be NULL to query the count only. */
 int ungx_shard_rows(const ungx_cross_edge_problem *problem, uint32_t *rows, uint64_t *count);
