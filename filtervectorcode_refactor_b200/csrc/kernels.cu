@@ -549,7 +549,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
       // ------------------------------------------------ TMA producer
       if (lane == 0 && !(p.inject & UNGX_INJECT_WITHHOLD_WORK))
       {
-         uint32_t it = 0, iseq = 0, aseq = 0;
+         uint32_t it = 0, iseq = 0, aseq = 0, pst = 0, pph = 0;
          bool ok = true;
          for (;;)
          {
@@ -588,19 +588,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
                const uint32_t brows = 16u << bix;
                for (uint32_t c = 0; c < nch; ++c)
                {
-                  const uint32_t st = it % S;
-                  if (!ptx::mbar_wait(&empty[st], ((it / S) & 1u) ^ 1u, abort_word, tmo))
+                  if (!ptx::mbar_wait(&empty[pst], pph ^ 1u, abort_word, tmo))
                   {
                      ok = false;
                      break;
                   }
-                  uint8_t *dst = sStage + st * L.stage_bytes;
-                  ptx::mbar_arrive_expect_tx(&full[st], (A_RES ? 0u : kAChunk) + brows * 128u);
+                  uint8_t *dst = sStage + pst * L.stage_bytes;
+                  ptx::mbar_arrive_expect_tx(&full[pst], (A_RES ? 0u : kAChunk) + brows * 128u);
                   if (!A_RES)
-                     ptx::tma_load_2d(dst, &maps.a, &full[st], int32_t(c * kChunkK), int32_t(w.row_begin));
-                  ptx::tma_load_2d(dst + (A_RES ? 0u : kAChunk), &maps.b[bix], &full[st], int32_t(c * kChunkK),
+                     ptx::tma_load_2d(dst, &maps.a, &full[pst], int32_t(c * kChunkK), int32_t(w.row_begin));
+                  ptx::tma_load_2d(dst + (A_RES ? 0u : kAChunk), &maps.b[bix], &full[pst], int32_t(c * kChunkK),
                                    int32_t(ti.x0()));
                   ++it;
+                  if (++pst == S) // ring position and phase kept without division
+                  {
+                     pst = 0;
+                     pph ^= 1u;
+                  }
                }
             }
             if (!ok)
@@ -627,7 +631,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
       // ------------------------------------------------ MMA issuer
       if (lane == 0)
       {
-         uint32_t it = 0, tseq = 0, iseq = 0, aseq = 0;
+         uint32_t tseq = 0, iseq = 0, aseq = 0, mst = 0, mph = 0;
          bool ok = true;
          for (;;)
          {
@@ -662,21 +666,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
                const uint32_t dt = tmem_base + b * kBN;
                for (uint32_t c = 0; c < nch; ++c)
                {
-                  const uint32_t st = it % S;
-                  if (!ptx::mbar_wait(&full[st], (it / S) & 1u, abort_word, tmo))
+                  if (!ptx::mbar_wait(&full[mst], mph, abort_word, tmo))
                   {
                      ok = false;
                      break;
                   }
                   ptx::tc_fence_after();
-                  uint8_t *stage = sStage + st * L.stage_bytes;
+                  uint8_t *stage = sStage + mst * L.stage_bytes;
                   const uint64_t ad = ptx::sdesc_k_sw128(ptx::smem_u32(A_RES ? sA + c * kAChunk : stage));
                   const uint64_t bd = ptx::sdesc_k_sw128(ptx::smem_u32(stage + (A_RES ? 0u : kAChunk)));
 #pragma unroll
                   for (uint32_t ks = 0; ks < 4; ++ks) // 4 x K=8 per 32-column chunk (+32 B each)
                      ptx::mma_tf32(dt, ad + 2u * ks, bd + 2u * ks, idesc, (c | ks) != 0u);
-                  ptx::mma_commit(&empty[st]);
-                  ++it;
+                  ptx::mma_commit(&empty[mst]);
+                  if (++mst == S)
+                  {
+                     mst = 0;
+                     mph ^= 1u;
+                  }
                }
                if (!ok)
                   break;

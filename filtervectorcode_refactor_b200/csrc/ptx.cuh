@@ -58,25 +58,38 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity)
    return ok != 0;
 }
 
+// Same test, but the thread may be suspended by the hardware for up to `hint_ns`
+// while the phase is incomplete (it resumes as soon as the phase completes), so a
+// waiting thread neither spins nor takes issue slots.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity, uint32_t hint_ns)
+{
+   uint32_t ok;
+   asm volatile("{\n\t.reg .pred p;\n\t"
+                "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+                "selp.u32 %0, 1, 0, p;\n\t}"
+                : "=r"(ok)
+                : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+                : "memory");
+   return ok != 0;
+}
+
 // Bounded wait for the phase with the given parity.  Returns false when the
-// deadline passed or another thread raised the abort word.
+// deadline passed or another thread raised the abort word (both checked each time
+// the thread wakes, at least every 20 us).
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_word,
                                           uint64_t timeout_ns)
 {
    if (mbar_try_wait(bar, parity))
       return true;
    const uint64_t start = globaltimer();
-   for (uint32_t spin = 1;; ++spin)
+   for (;;)
    {
-      if (mbar_try_wait(bar, parity))
+      if (mbar_try_wait_sleep(bar, parity, 20000u))
          return true;
-      if ((spin & 7u) == 0)
-      {
-         if (abort_word && *abort_word)
-            return false;
-         if (globaltimer() - start > timeout_ns)
-            return false;
-      }
+      if (abort_word && *abort_word)
+         return false;
+      if (globaltimer() - start > timeout_ns)
+         return false;
    }
 }
 
