@@ -56,6 +56,34 @@ struct DevBuf
    }
 };
 
+// Page-locked host buffer that grows on demand (cudaHostAlloc).
+struct PinnedBuf
+{
+   void *p = nullptr;
+   size_t bytes = 0;
+   cudaError_t ensure(size_t need)
+   {
+      if (need <= bytes && p)
+         return cudaSuccess;
+      if (p)
+         cudaFreeHost(p);
+      p = nullptr;
+      bytes = 0;
+      const size_t alloc = std::max<size_t>(need, 4096);
+      cudaError_t e = cudaHostAlloc(&p, alloc, cudaHostAllocDefault);
+      if (e == cudaSuccess)
+         bytes = alloc;
+      return e;
+   }
+   void release()
+   {
+      if (p)
+         cudaFreeHost(p);
+      p = nullptr;
+      bytes = 0;
+   }
+};
+
 double ms_since(std::chrono::steady_clock::time_point t0)
 {
    return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
@@ -81,6 +109,8 @@ struct ungx_context
    DevBuf items, segs, empties, ranges, gmax, counters, fb_rows, fb_items, rows, row_items, out_ids, out_dists;
    DevBuf cand_key, cand_col;
    DevBuf stage[2];
+   DevBuf copy_ranges, compact; // a shard's rows gathered for one device -> host copy
+   PinnedBuf host_stage;
    uint32_t *h_counters = nullptr; // pinned
    cudaEvent_t ev[10] = {};
 };
@@ -473,8 +503,10 @@ int ungx_context_destroy(ungx_context *ctx)
    ungx_release_base_vectors(ctx);
    for (DevBuf *b : {&ctx->items, &ctx->segs, &ctx->empties, &ctx->ranges, &ctx->gmax, &ctx->counters,
                      &ctx->fb_rows, &ctx->fb_items, &ctx->rows, &ctx->row_items, &ctx->out_ids, &ctx->out_dists,
-                     &ctx->stage[0], &ctx->stage[1], &ctx->cand_key, &ctx->cand_col})
+                     &ctx->stage[0], &ctx->stage[1], &ctx->cand_key, &ctx->cand_col, &ctx->copy_ranges,
+                     &ctx->compact})
       b->release();
+   ctx->host_stage.release();
    for (auto &ev : ctx->ev)
       if (ev)
          cudaEventDestroy(ev);
@@ -629,46 +661,75 @@ int ungx_cross_edges_generate(ungx_context *ctx, const ungx_cross_edge_problem *
    // device -> host: whole rows of this shard's work
    const uint32_t k = problem->topk;
    UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[6], ctx->stream), "event");
-   auto copy_rows = [&](uint32_t begin, uint32_t count) -> int {
-      const size_t off = size_t(begin) * k, len = size_t(count) * k;
+   if (problem->shard_count <= 1)
+   {
       UNGX_CUDA(ctx,
-                cudaMemcpyAsync(out_ids + off, ctx->out_ids.as<uint32_t>() + off, len * sizeof(uint32_t),
-                                cudaMemcpyDeviceToHost, ctx->stream),
+                cudaMemcpyAsync(out_ids, ctx->out_ids.as<uint32_t>(), nk * sizeof(uint32_t), cudaMemcpyDeviceToHost,
+                                ctx->stream),
                 "output copy");
       if (out_dists)
          UNGX_CUDA(ctx,
-                   cudaMemcpyAsync(out_dists + off, ctx->out_dists.as<float>() + off, len * sizeof(float),
-                                   cudaMemcpyDeviceToHost, ctx->stream),
+                   cudaMemcpyAsync(out_dists, ctx->out_dists.as<float>(), nk * sizeof(float), cudaMemcpyDeviceToHost,
+                                   ctx->stream),
                    "output copy");
-      return UNGX_OK;
-   };
-   if (problem->shard_count <= 1)
-   {
-      if ((st = copy_rows(0, problem->num_points)))
+      UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[7], ctx->stream), "event");
+      if ((st = wait_event(ctx, ctx->ev[7], "output copy")))
          return st;
    }
    else
    {
-      // merge adjacent row ranges of this shard into few copies
+      // a shard's rows are scattered over the id space (one range per work item):
+      // gather them into a compact device buffer, copy it back in one piece and
+      // scatter the ranges on the host
       std::vector<ungx::RowRange> rr;
       for (const auto &it : plan.items)
          rr.push_back({it.row_begin, it.row_count});
       rr.insert(rr.end(), plan.empty_rows.begin(), plan.empty_rows.end());
       std::sort(rr.begin(), rr.end(), [](const ungx::RowRange &a, const ungx::RowRange &b) { return a.begin < b.begin; });
+      std::vector<ungx::CopyRange> cr;
+      uint32_t rows = 0;
       for (size_t i = 0; i < rr.size();)
       {
          uint32_t b = rr[i].begin, e = rr[i].begin + rr[i].count;
          size_t j = i + 1;
          while (j < rr.size() && rr[j].begin == e)
             e += rr[j++].count;
-         if ((st = copy_rows(b, e - b)))
-            return st;
+         cr.push_back({b, rows, e - b, 0});
+         rows += e - b;
          i = j;
       }
+      const size_t cnk = size_t(rows) * k;
+      const size_t id_bytes = cnk * sizeof(uint32_t), d_bytes = out_dists ? cnk * sizeof(float) : 0;
+      UNGX_CUDA(ctx, ctx->copy_ranges.ensure(cr.size() * sizeof(ungx::CopyRange)), "copy-range allocation");
+      UNGX_CUDA(ctx, ctx->compact.ensure(id_bytes + d_bytes), "compact output allocation");
+      UNGX_CUDA(ctx, ctx->host_stage.ensure(id_bytes + d_bytes), "pinned output staging");
+      UNGX_CUDA(ctx,
+                cudaMemcpyAsync(ctx->copy_ranges.p, cr.data(), cr.size() * sizeof(ungx::CopyRange),
+                                cudaMemcpyHostToDevice, ctx->stream),
+                "copy-range upload");
+      uint32_t *c_ids = ctx->compact.as<uint32_t>();
+      float *c_d = out_dists ? reinterpret_cast<float *>(ctx->compact.as<char>() + id_bytes) : nullptr;
+      UNGX_CUDA(ctx,
+                ungx::launch_gather_rows(ctx->copy_ranges.as<ungx::CopyRange>(), (uint32_t)cr.size(), k,
+                                         ctx->out_ids.as<uint32_t>(), out_dists ? ctx->out_dists.as<float>() : nullptr,
+                                         c_ids, c_d, ctx->stream),
+                "row gather kernel");
+      t.gpu_launches += cr.empty() ? 0 : 1;
+      UNGX_CUDA(ctx, cudaMemcpyAsync(ctx->host_stage.p, ctx->compact.p, id_bytes + d_bytes, cudaMemcpyDeviceToHost,
+                                     ctx->stream),
+                "output copy");
+      UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[7], ctx->stream), "event");
+      if ((st = wait_event(ctx, ctx->ev[7], "output copy")))
+         return st;
+      const uint32_t *h_ids = static_cast<const uint32_t *>(ctx->host_stage.p);
+      const float *h_d = reinterpret_cast<const float *>(static_cast<const char *>(ctx->host_stage.p) + id_bytes);
+      ungx::parallel_for((int64_t)cr.size(), 0, 64, [&](int64_t i) {
+         const ungx::CopyRange &c = cr[i];
+         std::memcpy(out_ids + size_t(c.src_row) * k, h_ids + size_t(c.dst_row) * k, size_t(c.count) * k * 4);
+         if (out_dists)
+            std::memcpy(out_dists + size_t(c.src_row) * k, h_d + size_t(c.dst_row) * k, size_t(c.count) * k * 4);
+      });
    }
-   UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[7], ctx->stream), "event");
-   if ((st = wait_event(ctx, ctx->ev[7], "output copy")))
-      return st;
    float d2h = 0;
    cudaEventElapsedTime(&d2h, ctx->ev[6], ctx->ev[7]);
    t.gpu_d2h_ms = d2h;

@@ -86,6 +86,15 @@ cudaError_t launch_group_maxnorm(const float *xnorm, const uint32_t *ranges, uin
                                  cudaStream_t s);
 cudaError_t launch_fill_empty(const RowRange *ranges, uint32_t nranges, uint32_t k, uint32_t *ids, float *dists,
                               cudaStream_t s);
+
+// Rows [src_row, src_row+count) of a row-major n x k output go to rows
+// [dst_row, dst_row+count) of a compact buffer (a shard's rows, copied back at once).
+struct CopyRange
+{
+   uint32_t src_row, dst_row, count, pad;
+};
+cudaError_t launch_gather_rows(const CopyRange *ranges, uint32_t nranges, uint32_t k, const uint32_t *ids,
+                               const float *dists, uint32_t *out_ids, float *out_dists, cudaStream_t s);
 cudaError_t launch_exact(const ExactParams &p, uint32_t grid_hint, cudaStream_t s);
 cudaError_t launch_tc(const TcMaps &maps, const TcParams &p, uint32_t kp, uint32_t grid, cudaStream_t s);
 cudaError_t launch_rerank(const RerankParams &p, uint32_t kp, uint32_t num_items, cudaStream_t s);
