@@ -155,28 +155,17 @@ class ClockSampler:
                 "reasons": sorted(reasons)}
 
 
-def measured_tf32_peak(device) -> float:
-    """cuBLAS TF32 GEMM throughput (8192^3, best of 5) on this GPU, TFLOP/s."""
-    import torch
-    old = torch.backends.cuda.matmul.allow_tf32
-    torch.backends.cuda.matmul.allow_tf32 = True
+def tensor_peak() -> tuple[float, str]:
+    """Dense fp16/bf16 tensor peak of this pool's B200s (TFLOP/s): the driver-measured
+    cuBLAS bf16 GEMM burst figure (the prefilter kernel is timed per launch), else the
+    pool's earlier measurement."""
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
-        a = torch.randn(8192, 8192, device=device)
-        b = torch.randn(8192, 8192, device=device)
-        for _ in range(2):
-            a @ b
-        best = 1e9
-        for _ in range(5):
-            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s.record()
-            a @ b
-            e.record()
-            e.synchronize()
-            best = min(best, s.elapsed_time(e))
-        del a, b
-        return 2 * 8192 ** 3 / (best * 1e-3) / 1e12
-    finally:
-        torch.backends.cuda.matmul.allow_tf32 = old
+        with open(path) as f:
+            v = float(json.load(f)["bf16_tflops"])
+        return v, "of measured (MEASURED_PEAKS.json bf16_tflops, burst; fp16 runs at the bf16 rate)"
+    except Exception:
+        return 1590.0, "of fallback (1.59 PFLOP/s bf16, earlier measurement on this pool)"
 
 
 def run_reference(args, rank, world):
@@ -284,7 +273,7 @@ def run_ours(args, rank, world, local_rank):
     value = flops_total / (ms_step * 1e-3) / 1e12
     tc_ms = statistics.median(t["tc_kernel_ms"] for t in timings)
     shard_pairs = timings[-1]["pairs"]
-    launches = sum(t["gpu_launches"] + 2 for t in timings)  # +2: the operand-build kernels of prepare
+    launches = sum(t["gpu_launches"] + 3 for t in timings)  # +3: the operand-build kernels of prepare
     fallback_rows = timings[-1]["rows_fallback"]
     certified_rows = timings[-1]["rows_certified"]
 
@@ -314,7 +303,7 @@ def run_ours(args, rank, world, local_rank):
            "d2h_bytes_per_step": int(n * k * 8)}
 
     if rank == 0:
-        peak = measured_tf32_peak(dev)
+        peak, peak_source = tensor_peak()
         achieved = 2.0 * d * shard_pairs / (tc_ms * 1e-3) / 1e12
         threads = os.cpu_count() or 1
         _, dt0, p0, _ = cpu_exact_sample(lg, Xr, k, 200_000_000, threads=threads)
@@ -323,18 +312,18 @@ def run_ours(args, rank, world, local_rank):
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "tf32+f32",
+            "scaling": "strong", "vs_baseline": None, "dtype": "f16+f32",
             "data": "synthetic (seeded, BASELINE configs[1] distributions)",
             "config": {"workload": c["name"], "n": n, "d": d, "k": k, "groups": int(lg.num_groups),
                        "lng_edges": int(lg.out_ids.size), "pairs_W": int(W), "flops_per_step": flops_total,
                        "wall_s_per_build": round(ms_step / 1e3, 6), "parallelism": f"item-shards x{world}",
-                       "route": "tcgen05 TF32 prefilter + exact fp32 rerank",
-                       "l2": "inputs larger than L2 (n*d*4 = %d MB base + operand), no flush" % (Xr.nbytes >> 20),
+                       "route": "tcgen05 kind::f16 prefilter (fp16 operand, fp32 accumulate) + exact fp32 rerank",
+                       "l2": "inputs larger than L2 (n*d*4 = %d MB base + fp16 operand), no flush" % (Xr.nbytes >> 20),
                        "rows_certified": int(certified_rows), "rows_rescanned": int(fallback_rows)},
             "gpu_launches": int(launches),
             "roofline": {"bound": "tensor", "kernel": "tc_kernel", "achieved": round(achieved, 2),
                          "peak": round(peak, 1), "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
-                         "peak_source": "cuBLAS TF32 GEMM 8192^3 measured in this run (MEASURED_PEAKS.json has bf16 only)",
+                         "peak_source": peak_source,
                          "traffic": None},
             "cpu_baseline": {"value": round(cpu_rate, 4), "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": kind,
                              "sample": f"{cpu_pairs} of W={W} pairs (stratified source groups), {cpu_dt:.1f} s"},

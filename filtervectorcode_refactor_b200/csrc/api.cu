@@ -103,7 +103,7 @@ struct ungx_context
    // resident base vectors (a4)
    bool have_vectors = false;
    const float *X = nullptr; // device, n x d
-   DevBuf X_owned, Xp, xnorm, mean, sums;
+   DevBuf X_owned, Xh, xnorm, mean, sums, range, scale; // Xh: fp16 operand [n x dp]
    uint32_t n = 0, d = 0, dp = 0;
    // per-call scratch
    DevBuf items, segs, empties, ranges, gmax, counters, fb_rows, fb_items, rows, row_items, out_ids, out_dists;
@@ -158,16 +158,15 @@ int wait_event(ungx_context *ctx, cudaEvent_t ev, const char *what)
    }
 }
 
-// Tensor map over the TF32-valued fp32 operand [rows x cols]: boxes of 32 columns
-// (128 bytes, the 128-byte swizzle the MMA descriptors expect) by box_rows rows.
-// Rows past the end read as zero.
+// Tensor map of the fp16 operand [rows x cols]: boxes of 64 columns (128 bytes,
+// 128-byte swizzle) by box_rows rows; out-of-range elements read as zero.
 int make_map(ungx_context *ctx, CUtensorMap *map, void *base, uint32_t rows, uint32_t cols, uint32_t box_rows)
 {
    cuuint64_t dims[2] = {cols, rows};
-   cuuint64_t strides[1] = {cuuint64_t(cols) * sizeof(float)};
-   cuuint32_t box[2] = {32, box_rows};
+   cuuint64_t strides[1] = {cuuint64_t(cols) * sizeof(uint16_t)};
+   cuuint32_t box[2] = {64, box_rows};
    cuuint32_t estr[2] = {1, 1};
-   const CUresult r = ctx->encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, estr,
+   const CUresult r = ctx->encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, dims, strides, box, estr,
                                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
    if (r != CUDA_SUCCESS)
@@ -295,14 +294,14 @@ int run_generate(ungx_context *ctx, const ungx_cross_edge_problem &p, const Plan
       UNGX_CUDA(ctx, ctx->fb_rows.ensure(sizeof(uint32_t) * std::max<uint64_t>(item_rows, 1)), "fallback list");
       UNGX_CUDA(ctx, ctx->fb_items.ensure(sizeof(uint32_t) * std::max<uint64_t>(item_rows, 1)), "fallback list");
       // candidate lists [row][2][kp], indexed by the global row
-      const size_t cand = size_t(ctx->n) * 2u * uint32_t(kp);
+      const size_t cand = size_t(ctx->n) * ungx::kTcLists * uint32_t(kp);
       UNGX_CUDA(ctx, ctx->cand_key.ensure(cand * sizeof(float)), "candidate buffer");
       UNGX_CUDA(ctx, ctx->cand_col.ensure(cand * sizeof(uint32_t)), "candidate buffer");
       ungx::TcMaps maps;
-      if ((st = make_map(ctx, &maps.a, ctx->Xp.p, ctx->n, ctx->dp, 128)))
+      if ((st = make_map(ctx, &maps.a, ctx->Xh.p, ctx->n, ctx->dp, 128)))
          return st;
-      for (int i = 0; i < 4; ++i)
-         if ((st = make_map(ctx, &maps.b[i], ctx->Xp.p, ctx->n, ctx->dp, 16u << i)))
+      for (uint32_t i = 0; i < ungx::kTcBoxes; ++i)
+         if ((st = make_map(ctx, &maps.b[i], ctx->Xh.p, ctx->n, ctx->dp, 16u * (i + 1u))))
             return st;
       ungx::TcParams tp{};
       tp.items = ctx->items.as<ungx::WorkItem>();
@@ -311,6 +310,7 @@ int run_generate(ungx_context *ctx, const ungx_cross_edge_problem &p, const Plan
       tp.item_counter = cnt + 0;
       tp.xnorm = ctx->xnorm.as<float>();
       tp.dp = ctx->dp;
+      tp.scale = ctx->scale.as<ungx::OperandScale>();
       tp.cand_key = ctx->cand_key.as<float>();
       tp.cand_col = ctx->cand_col.as<uint32_t>();
       tp.status = status;
@@ -338,6 +338,7 @@ int run_generate(ungx_context *ctx, const ungx_cross_edge_problem &p, const Plan
       rp.fb_items = ctx->fb_items.as<uint32_t>();
       rp.fb_count = cnt + 1;
       rp.counters = stats;
+      rp.scale = tp.scale;
       ungx::tc_certificate_constants(ctx->d, ctx->dp, rp);
       UNGX_CUDA(ctx, ungx::launch_rerank(rp, (uint32_t)kp, (uint32_t)plan.items.size(), s), "rerank kernel launch");
       UNGX_CUDA(ctx, cudaEventRecord(ev[8], s), "event");
@@ -553,7 +554,7 @@ int ungx_prepare_base_vectors(ungx_context *ctx, const float *vectors, uint32_t 
    ctx->have_vectors = false;
    ctx->X = nullptr;
    const auto t0 = std::chrono::steady_clock::now();
-   const uint32_t dp = (d + 31) / 32 * 32;
+   const uint32_t dp = ungx::tc_operand_cols(d);
    const size_t xbytes = size_t(n) * d * sizeof(float);
    if (on_device)
       ctx->X = vectors;
@@ -565,14 +566,21 @@ int ungx_prepare_base_vectors(ungx_context *ctx, const float *vectors, uint32_t 
          return st;
       ctx->X = ctx->X_owned.as<float>();
    }
-   UNGX_CUDA(ctx, ctx->Xp.ensure(size_t(n) * dp * sizeof(float)), "operand allocation");
+   UNGX_CUDA(ctx, ctx->Xh.ensure(size_t(n) * dp * sizeof(uint16_t)), "operand allocation");
    UNGX_CUDA(ctx, ctx->xnorm.ensure(size_t(n) * sizeof(float)), "norm allocation");
    UNGX_CUDA(ctx, ctx->mean.ensure(size_t(d) * sizeof(float)), "mean allocation");
    UNGX_CUDA(ctx, ctx->sums.ensure(size_t(d) * sizeof(double)), "mean allocation");
-   UNGX_CUDA(ctx, ungx::launch_colsum(ctx->X, n, d, ctx->sums.as<double>(), ctx->stream), "column-sum kernel");
+   UNGX_CUDA(ctx, ctx->range.ensure(size_t(d) * 2 * sizeof(uint32_t)), "range allocation");
+   UNGX_CUDA(ctx, ctx->scale.ensure(sizeof(ungx::OperandScale)), "scale allocation");
+   UNGX_CUDA(ctx, ungx::launch_colsum(ctx->X, n, d, ctx->sums.as<double>(), ctx->range.as<uint32_t>(), ctx->stream),
+             "column-sum kernel");
    UNGX_CUDA(ctx,
-             ungx::launch_center(ctx->X, ctx->sums.as<double>(), n, d, dp, ctx->mean.as<float>(), ctx->Xp.as<float>(),
-                                 ctx->xnorm.as<float>(), ctx->stream),
+             ungx::launch_scale(ctx->sums.as<double>(), ctx->range.as<uint32_t>(), n, d, ctx->mean.as<float>(),
+                                ctx->scale.as<ungx::OperandScale>(), ctx->stream),
+             "scale kernel");
+   UNGX_CUDA(ctx,
+             ungx::launch_center(ctx->X, ctx->mean.as<float>(), ctx->scale.as<ungx::OperandScale>(), n, d, dp,
+                                 ctx->Xh.as<uint16_t>(), ctx->xnorm.as<float>(), ctx->stream),
              "centre kernel");
    UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[6], ctx->stream), "event");
    int st = wait_event(ctx, ctx->ev[6], "vector preparation");
@@ -592,10 +600,12 @@ int ungx_release_base_vectors(ungx_context *ctx)
       return UNGX_ERR_INVALID_ARG;
    cudaSetDevice(ctx->device);
    ctx->X_owned.release();
-   ctx->Xp.release();
+   ctx->Xh.release();
    ctx->xnorm.release();
    ctx->mean.release();
    ctx->sums.release();
+   ctx->range.release();
+   ctx->scale.release();
    ctx->X = nullptr;
    ctx->have_vectors = false;
    ctx->n = ctx->d = ctx->dp = 0;

@@ -1,19 +1,20 @@
 // Device code of the B200 cross-edge builder (sm_100a).
 //
-//   colsum / center     resident operand build (a4): mean, centred + BF16-rounded
-//                       copy padded to 32 columns, fp32 row norms.
+//   colsum / scale /    resident operand build (a4): column sums and ranges, the mean
+//   center              and a power-of-two scale s, then fp16(s * (x - mean)) padded to
+//                       a multiple of 16 columns and fp32 norms of the centred rows.
 //   tc_kernel           the hot path.  Persistent CTAs pull source-centric work items
-//                       (<=128 rows of one source group x all its LNG target groups);
-//                       TMA stages the item's source rows once (operand A) and the
-//                       target rows in 128-row tiles through a shared-memory ring of
-//                       up to 16 stages; one thread issues tcgen05.mma kind::f16 (bf16
-//                       operands, fp32 accumulate) into four 128-column TMEM
-//                       accumulators; eight epilogue warps read TMEM
-//                       rows (thread = source row), form the keys ||x||^2 - 2 q.x and
-//                       keep a sorted register top-KP per row and column half.  The two
-//                       lists of every row go to a small candidate buffer; no distance
-//                       matrix reaches global memory.
-//   rerank_kernel       merges a row's two lists, computes the exact reference distance
+//                       (<=128 rows of one source group x all its LNG target groups).
+//                       TMA stages fp16 operand chunks (64 columns, 128-byte rows)
+//                       through a shared-memory ring; one thread copies the item's
+//                       source rows into TMEM (tcgen05.cp) and issues tcgen05.mma
+//                       kind::f16 with A in TMEM and the target tile (<= 192 rows) in
+//                       shared memory into two 192-column TMEM accumulators; twelve
+//                       epilogue warps read TMEM rows (thread = source row), form the
+//                       keys ||x||^2 - 2 q.x and keep a sorted register top-KP per row
+//                       and column third.  The three lists of every row go to a small
+//                       candidate buffer; no distance matrix reaches global memory.
+//   rerank_kernel       merges a row's lists, computes the exact reference distance
 //                       of each candidate, sorts by (distance, id), writes the top-k and
 //                       checks a rounding-error certificate that no column outside the
 //                       list could enter the top-k; failing rows are queued.
@@ -23,6 +24,7 @@
 //                       route EXACT, and the rescan of the queued rows.
 #include <cfloat>
 #include <cmath>
+#include <cuda_fp16.h>
 
 #include "kernels.h"
 #include "ptx.cuh"
@@ -31,13 +33,16 @@ namespace ungx
 {
 namespace
 {
-constexpr uint32_t kTcThreads = 320; // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
-constexpr uint32_t kBN = 128;        // target columns per tile / TMEM accumulator
-constexpr uint32_t kAccBufs = 4;     // TMEM accumulators (4 x 128 columns = all 512)
+constexpr uint32_t kEpiWarps = 12;                    // three per TMEM lane quarter
+constexpr uint32_t kTcThreads = 64 + 32 * kEpiWarps;  // warp 0 TMA, warp 1 MMA, 2.. epilogue
+constexpr uint32_t kBN = 192;          // target columns per tile / TMEM accumulator
+constexpr uint32_t kAccBufs = 2;       // TMEM accumulators at columns 128 + 192 b
+constexpr uint32_t kAccCol0 = 128;     // TMEM columns [0, 128): four A slots
+constexpr uint32_t kASlots = 4;        // A slot = 32 TMEM columns = 64 fp16 of K x 128 rows
 constexpr uint32_t kItemSlots = 2;
-constexpr uint32_t kChunkK = 32;          // fp32 columns per K chunk: 128-byte rows
-constexpr uint32_t kAChunk = 128 * 128;   // 128 rows x 32 fp32, 128-byte swizzled
-constexpr uint32_t kBChunk = kBN * 128;   // 128 rows x 32 fp32
+constexpr uint32_t kChunkK = 64;          // fp16 columns per K chunk: 128-byte rows
+constexpr uint32_t kAChunk = 128 * 128;   // 128 rows x 64 fp16, 128-byte swizzled
+constexpr uint32_t kBChunk = kBN * 128;   // 192 rows x 64 fp16
 constexpr uint32_t kMaxStages = 16;
 constexpr uint32_t kSmemLimit = 232448;   // per-block opt-in maximum on sm_100
 constexpr uint32_t kNoItem = 0xFFFFFFFFu;
@@ -47,46 +52,46 @@ constexpr uint64_t kDrainWaitNs = 2000000000ull;
 
 struct TcLayout
 {
-   uint32_t stages, a_off, a_bytes, stage_off, stage_bytes, colv_off, norm_off, bar_off, misc_off, total;
+   uint32_t stages, stage_off, stage_bytes, colv_off, norm_off, bar_off, misc_off, total;
 };
 
-// A resident (dp <= 128): A = dp/32 chunks of 16 KB kept per item, then as many
-// 16 KB target-chunk stages as fit (at most 16).  A streamed: stages of (16 KB
-// source + 16 KB target) chunks.  Then the epilogue's column table (8 warps x KP
-// slots x 32 lanes), the chunk norms, barriers, and the item slots.
+// Stages of the ring: A resident (dp <= 256) -> one 24 KB target chunk per stage, the
+// item's source chunks (16 KB) pass through the same ring once per item; A streamed
+// -> 16 KB source + 24 KB target chunk per stage.  As many stages as fit (at most
+// 16), then the epilogue's column table (12 warps x KP slots x 32 lanes), the chunk
+// norms, barriers, and the item slots.
 __host__ __device__ inline TcLayout tc_layout(uint32_t dp, bool a_res, uint32_t kp)
 {
+   (void)dp;
    TcLayout L;
-   L.a_off = 0;
-   L.a_bytes = a_res ? (dp / kChunkK) * kAChunk : 0;
-   L.stage_off = L.a_bytes;
+   L.stage_off = 0;
    L.stage_bytes = a_res ? kBChunk : kAChunk + kBChunk;
-   const uint32_t fixed = L.a_bytes + 8u * kp * 32u * 4u + 8u * 32u * 4u + 48u * 8u + 128u + 1024u;
+   const uint32_t fixed = kEpiWarps * kp * 32u * 4u + kEpiWarps * 32u * 4u + 48u * 8u + 128u + 1024u;
    const uint32_t fit = fixed < kSmemLimit ? (kSmemLimit - fixed) / L.stage_bytes : 0u;
    L.stages = fit < kMaxStages ? fit : kMaxStages;
    L.colv_off = L.stage_off + L.stages * L.stage_bytes;
-   L.norm_off = L.colv_off + 8u * kp * 32u * 4u;
-   L.bar_off = L.norm_off + 8u * 32u * 4u;
+   L.norm_off = L.colv_off + kEpiWarps * kp * 32u * 4u;
+   L.bar_off = L.norm_off + kEpiWarps * 32u * 4u;
    L.misc_off = L.bar_off + 48u * 8u;
    L.total = L.misc_off + 128u;
    return L;
 }
 
-// Round to the nearest TF32 value (10 explicit mantissa bits, ties to even), kept
-// in fp32 storage with the 13 low bits zero, so the tensor core reads it exactly.
-__device__ __forceinline__ float tf32_rne(float v)
+// Order-preserving map of a float to an unsigned key (for atomic min / max).
+__device__ __forceinline__ uint32_t float_key(float f)
 {
-   uint32_t u = __float_as_uint(v);
-   if ((u & 0x7f800000u) == 0x7f800000u)
-      return v;
-   u += 0xFFFu + ((u >> 13) & 1u);
-   return __uint_as_float(u & 0xFFFFE000u);
+   const uint32_t u = __float_as_uint(f);
+   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key_float(uint32_t k)
+{
+   return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
 }
 
 // v[j] for a per-thread index j in 0..31, by a 5-level select tree (registers only).
-__device__ __forceinline__ float select32(const float (&v)[32], uint32_t j)
+__device__ __forceinline__ uint32_t select32(const uint32_t (&v)[32], uint32_t j)
 {
-   float a[16], b[8], c[4], e[2];
+   uint32_t a[16], b[8], c[4], e[2];
 #pragma unroll
    for (int i = 0; i < 16; ++i)
       a[i] = (j & 1u) ? v[2 * i + 1] : v[2 * i];
@@ -100,6 +105,25 @@ __device__ __forceinline__ float select32(const float (&v)[32], uint32_t j)
    for (int i = 0; i < 2; ++i)
       e[i] = (j & 8u) ? c[2 * i + 1] : c[2 * i];
    return (j & 16u) ? e[1] : e[0];
+}
+
+// Two fp32 lanes per instruction (sm_100 f32x2 arithmetic); each lane rounds exactly
+// like the scalar __fmaf_rn / __fsub_rn.
+__device__ __forceinline__ uint64_t pack2(float lo, float hi)
+{
+   return (uint64_t(__float_as_uint(hi)) << 32) | __float_as_uint(lo);
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c)
+{
+   uint64_t d;
+   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+   return d;
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b)
+{
+   uint64_t d;
+   asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+   return d;
 }
 
 // Squared L2 in the reference's order: 8 accumulators over i mod 8 with the update
@@ -232,43 +256,122 @@ __device__ __forceinline__ void insert_key(float (&kd)[K], uint32_t (&ki)[K], fl
 }
 
 // ------------------------------------------------------------------ prep
+// Column sums (fp64) and column ranges of X over a block of rows; thread = column,
+// four rows in flight per thread.
 __global__ void colsum_kernel(const float *__restrict__ X, uint32_t n, uint32_t d, double *__restrict__ sums,
-                              uint32_t rows_per_block)
+                              uint32_t *__restrict__ range, uint32_t rows_per_block)
 {
    const uint64_t r0 = uint64_t(blockIdx.x) * rows_per_block;
    const uint64_t r1 = (r0 + rows_per_block < n) ? r0 + rows_per_block : uint64_t(n);
    for (uint32_t j = threadIdx.x; j < d; j += blockDim.x)
    {
-      double acc = 0.0;
-      for (uint64_t r = r0; r < r1; ++r)
-         acc += (double)X[r * d + j];
-      atomicAdd(&sums[j], acc);
+      double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
+      float mn = INFINITY, mx = -INFINITY;
+      uint64_t r = r0;
+      for (; r + 4 <= r1; r += 4)
+      {
+         const float v0 = __ldg(X + r * d + j), v1 = __ldg(X + (r + 1) * d + j);
+         const float v2 = __ldg(X + (r + 2) * d + j), v3 = __ldg(X + (r + 3) * d + j);
+         a0 += (double)v0;
+         a1 += (double)v1;
+         a2 += (double)v2;
+         a3 += (double)v3;
+         mn = fminf(fminf(mn, v0), fminf(fminf(v1, v2), v3));
+         mx = fmaxf(fmaxf(mx, v0), fmaxf(fmaxf(v1, v2), v3));
+      }
+      for (; r < r1; ++r)
+      {
+         const float v = __ldg(X + r * d + j);
+         a0 += (double)v;
+         mn = fminf(mn, v);
+         mx = fmaxf(mx, v);
+      }
+      atomicAdd(&sums[j], (a0 + a1) + (a2 + a3));
+      atomicMax(&range[2 * j], ~float_key(mn)); // minimum kept as the complement (zero = none)
+      atomicMax(&range[2 * j + 1], float_key(mx));
    }
 }
 
-__global__ void center_kernel(const float *__restrict__ X, const double *__restrict__ sums, uint32_t n,
-                              uint32_t d, uint32_t dp, float *__restrict__ mean, float *__restrict__ Xp,
-                              float *__restrict__ xnorm)
+// One block: the fp32 mean, the largest centred magnitude m = max_j max(fl(max_j -
+// mean_j), fl(mean_j - min_j)) (rounding is monotone, so no centred element exceeds
+// it), and the scale s = 2^e with 2^14 <= s m < 2^15.
+__global__ void scale_kernel(const double *__restrict__ sums, const uint32_t *__restrict__ range, uint32_t n,
+                             uint32_t d, float *__restrict__ mean, OperandScale *__restrict__ out)
+{
+   __shared__ float s_m[32];
+   float m = 0.f;
+   bool bad = false;
+   for (uint32_t j = threadIdx.x; j < d; j += blockDim.x)
+   {
+      const float mu = (float)(sums[j] / (double)n);
+      mean[j] = mu;
+      const float lo = key_float(~range[2 * j]), hi = key_float(range[2 * j + 1]);
+      const float e = fmaxf(__fsub_rn(hi, mu), __fsub_rn(mu, lo));
+      if (!(e <= FLT_MAX)) // inf or nan in the data
+         bad = true;
+      else
+         m = fmaxf(m, e);
+   }
+   bad = __syncthreads_or(bad);
+   for (int o = 16; o; o >>= 1)
+      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+   if ((threadIdx.x & 31) == 0)
+      s_m[threadIdx.x >> 5] = m;
+   __syncthreads();
+   if (threadIdx.x == 0)
+   {
+      for (uint32_t w = 1; w < (blockDim.x + 31) / 32; ++w)
+         m = fmaxf(m, s_m[w]);
+      int e = 0;
+      int exact_only = bad ? 1 : 0;
+      if (m > 0.f && !bad)
+      {
+         e = 14 - ilogbf(m); // ilogb: floor(log2 m), also for subnormal m
+         if (e > 60)
+            e = 60; // tiny data: keep 1/s^2 a normal float (the certificate sees the loss)
+         if (e < -60)
+         {
+            e = -60;
+            exact_only = 1; // s m would overflow fp16
+         }
+      }
+      OperandScale sc;
+      sc.s = ldexpf(1.f, e);
+      sc.neg2_inv_s2 = -ldexpf(1.f, 1 - 2 * e);
+      sc.inv_s = ldexpf(1.f, -e);
+      sc.exact_only = exact_only;
+      *out = sc;
+   }
+}
+
+// Warp per row: v = fl(x - mean), operand fp16(s v) (saturated; s v is exact), norm
+// = fp32 sum of v^2.  Columns d..dp-1 of the operand are zero.
+__global__ void center_kernel(const float *__restrict__ X, const float *__restrict__ mean,
+                              const OperandScale *__restrict__ scale, uint32_t n, uint32_t d, uint32_t dp,
+                              __half *__restrict__ Xh, float *__restrict__ xnorm)
 {
    extern __shared__ float s_mean[];
    for (uint32_t j = threadIdx.x; j < d; j += blockDim.x)
-      s_mean[j] = (float)(sums[j] / (double)n);
+      s_mean[j] = mean[j];
    __syncthreads();
-   if (blockIdx.x == 0)
-      for (uint32_t j = threadIdx.x; j < d; j += blockDim.x)
-         mean[j] = s_mean[j];
+   const float sc = scale->s;
    const uint32_t lane = threadIdx.x & 31;
    const uint64_t warps = (uint64_t(gridDim.x) * blockDim.x) >> 5;
    for (uint64_t r = (uint64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; r < n; r += warps)
    {
       float acc = 0.f;
-      for (uint32_t j = lane; j < dp; j += 32)
+      for (uint32_t j = 2 * lane; j < dp; j += 64)
       {
-         float v = 0.f;
+         float v0 = 0.f, v1 = 0.f;
          if (j < d)
-            v = __fsub_rn(X[r * d + j], s_mean[j]);
-         Xp[r * dp + j] = tf32_rne(v);
-         acc = __fmaf_rn(v, v, acc);
+            v0 = __fsub_rn(X[r * d + j], s_mean[j]);
+         if (j + 1 < d)
+            v1 = __fsub_rn(X[r * d + j + 1], s_mean[j + 1]);
+         const float w0 = fminf(fmaxf(v0 * sc, -65504.f), 65504.f);
+         const float w1 = fminf(fmaxf(v1 * sc, -65504.f), 65504.f);
+         *reinterpret_cast<__half2 *>(Xh + r * dp + j) = __halves2half2(__float2half_rn(w0), __float2half_rn(w1));
+         acc = __fmaf_rn(v0, v0, acc);
+         acc = __fmaf_rn(v1, v1, acc);
       }
 #pragma unroll
       for (int o = 16; o; o >>= 1)
@@ -423,12 +526,10 @@ __device__ __forceinline__ void raise_abort(volatile int *abort_word, int *statu
    atomicCAS(status, 0, code);
 }
 
-__device__ __forceinline__ uint32_t box_index(uint32_t valid)
-{
-   return valid <= 16 ? 0u : valid <= 32 ? 1u : valid <= 64 ? 2u : 3u;
-}
+// Narrowest target box covering `valid` (1..192) columns: 16 (i + 1) rows.
+__device__ __forceinline__ uint32_t box_index(uint32_t valid) { return (valid + 15u) / 16u - 1u; }
 
-// Walks the 128-column tiles of a work item: segment by segment, 128 columns at a
+// Walks the 192-column tiles of a work item: segment by segment, 192 columns at a
 // time.  The descriptor of the following segment is always loaded one segment
 // ahead, so crossing into a new segment never waits on global memory.
 struct TileIter
@@ -496,27 +597,25 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
    uint8_t *smem = smem_raw + (((raw_u32 + 1023u) & ~1023u) - raw_u32);
    const TcLayout L = tc_layout(p.dp, A_RES, KP);
    const uint32_t S = L.stages;
-   uint8_t *sA = smem + L.a_off;
    uint8_t *sStage = smem + L.stage_off;
    float *sNorm = reinterpret_cast<float *>(smem + L.norm_off);
    uint32_t *sColv = reinterpret_cast<uint32_t *>(smem + L.colv_off);
    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bar_off);
    uint64_t *full = bars;              // [S <= 16]
    uint64_t *empty = bars + 16;        // [S]
-   uint64_t *acc_full = bars + 32;     // [4]
-   uint64_t *acc_empty = bars + 36;    // [4]
-   uint64_t *a_full = bars + 40;
-   uint64_t *a_empty = bars + 41;
-   uint64_t *item_full = bars + 42;    // [2]
-   uint64_t *item_empty = bars + 44;   // [2]
-   uint64_t *done_bar = bars + 46;
+   uint64_t *acc_full = bars + 32;     // [2]
+   uint64_t *acc_empty = bars + 34;    // [2]
+   uint64_t *a_free = bars + 36;       // [4]: MMAs reading A slot s completed
+   uint64_t *item_full = bars + 40;    // [2]
+   uint64_t *item_empty = bars + 42;   // [2]
+   uint64_t *done_bar = bars + 44;
    volatile uint32_t *item_slot = reinterpret_cast<volatile uint32_t *>(smem + L.misc_off);
    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L.misc_off + 16);
    volatile int *abort_word = reinterpret_cast<volatile int *>(smem + L.misc_off + 32);
    WorkItem *item_desc = reinterpret_cast<WorkItem *>(smem + L.misc_off + 64); // [kItemSlots]
 
    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-   const uint32_t nch = p.dp / kChunkK;
+   const uint32_t nch = (p.dp + kChunkK - 1) / kChunkK;
    const uint64_t tmo = p.timeout_ns;
 
    if (threadIdx.x == 0)
@@ -529,14 +628,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
       for (uint32_t b = 0; b < kAccBufs; ++b)
       {
          ptx::mbar_init(&acc_full[b], 1);
-         ptx::mbar_init(&acc_empty[b], 8);
+         ptx::mbar_init(&acc_empty[b], kEpiWarps);
       }
-      ptx::mbar_init(a_full, 1);
-      ptx::mbar_init(a_empty, 1);
+      for (uint32_t s = 0; s < kASlots; ++s)
+         ptx::mbar_init(&a_free[s], 1);
       for (uint32_t s = 0; s < kItemSlots; ++s)
       {
          ptx::mbar_init(&item_full[s], 1);
-         ptx::mbar_init(&item_empty[s], 9); // MMA thread + 8 epilogue warps
+         ptx::mbar_init(&item_empty[s], 1 + kEpiWarps); // MMA thread + epilogue warps
       }
       ptx::mbar_init(done_bar, 1);
       *abort_word = 0;
@@ -545,7 +644,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
    if (warp == 0 && lane == 0)
    {
       ptx::prefetch_tmap(&maps.a);
-      for (int i = 0; i < 4; ++i)
+      for (uint32_t i = 0; i < kTcBoxes; ++i)
          ptx::prefetch_tmap(&maps.b[i]);
    }
    if (warp == 1)
@@ -563,8 +662,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
       // ------------------------------------------------ TMA producer
       if (lane == 0 && !(p.inject & UNGX_INJECT_WITHHOLD_WORK))
       {
-         uint32_t it = 0, iseq = 0, aseq = 0, pst = 0, pph = 0;
+         uint32_t it = 0, iseq = 0, pst = 0, pph = 0;
          bool ok = true;
+         auto next_stage = [&](uint32_t bytes) -> uint8_t * {
+            if (!ptx::mbar_wait(&empty[pst], pph ^ 1u, abort_word, tmo))
+               return nullptr;
+            uint8_t *dst = sStage + pst * L.stage_bytes;
+            ptx::mbar_arrive_expect_tx(&full[pst], bytes);
+            return dst;
+         };
+         auto advance = [&]() {
+            ++it;
+            if (++pst == S) // ring position and phase kept without division
+            {
+               pst = 0;
+               pph ^= 1u;
+            }
+         };
          for (;;)
          {
             const uint32_t idx = atomicAdd(p.item_counter, 1u);
@@ -583,42 +697,36 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
             ++iseq;
             if (idx >= p.num_items)
                break;
-            if (A_RES)
-            {
-               if (!ptx::mbar_wait(a_empty, (aseq & 1u) ^ 1u, abort_word, tmo))
+            if (A_RES) // the item's source chunks, once, through the ring
+               for (uint32_t c = 0; c < nch && ok; ++c)
                {
-                  ok = false;
-                  break;
-               }
-               ptx::mbar_arrive_expect_tx(a_full, nch * kAChunk);
-               for (uint32_t c = 0; c < nch; ++c)
-                  ptx::tma_load_2d(sA + c * kAChunk, &maps.a, a_full, int32_t(c * kChunkK), int32_t(w.row_begin));
-               ++aseq;
-            }
-            TileIter ti;
-            for (ti.start(p.segs, w.seg_begin, w.seg_count); ti.valid_tile() && ok; ti.next())
-            {
-               const uint32_t bix = box_index(ti.cols());
-               const uint32_t brows = 16u << bix;
-               for (uint32_t c = 0; c < nch; ++c)
-               {
-                  if (!ptx::mbar_wait(&empty[pst], pph ^ 1u, abort_word, tmo))
+                  uint8_t *dst = next_stage(kAChunk);
+                  if (!dst)
                   {
                      ok = false;
                      break;
                   }
-                  uint8_t *dst = sStage + pst * L.stage_bytes;
-                  ptx::mbar_arrive_expect_tx(&full[pst], (A_RES ? 0u : kAChunk) + brows * 128u);
+                  ptx::tma_load_2d(dst, &maps.a, &full[pst], int32_t(c * kChunkK), int32_t(w.row_begin));
+                  advance();
+               }
+            TileIter ti;
+            for (ti.start(p.segs, w.seg_begin, w.seg_count); ti.valid_tile() && ok; ti.next())
+            {
+               const uint32_t bix = box_index(ti.cols());
+               const uint32_t brows = 16u * (bix + 1u);
+               for (uint32_t c = 0; c < nch; ++c)
+               {
+                  uint8_t *dst = next_stage((A_RES ? 0u : kAChunk) + brows * 128u);
+                  if (!dst)
+                  {
+                     ok = false;
+                     break;
+                  }
                   if (!A_RES)
                      ptx::tma_load_2d(dst, &maps.a, &full[pst], int32_t(c * kChunkK), int32_t(w.row_begin));
                   ptx::tma_load_2d(dst + (A_RES ? 0u : kAChunk), &maps.b[bix], &full[pst], int32_t(c * kChunkK),
                                    int32_t(ti.x0()));
-                  ++it;
-                  if (++pst == S) // ring position and phase kept without division
-                  {
-                     pst = 0;
-                     pph ^= 1u;
-                  }
+                  advance();
                }
             }
             if (!ok)
@@ -634,8 +742,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
                if (issued)
                   ptx::mbar_wait(&full[st], (issued - 1) & 1u, nullptr, kDrainWaitNs);
             }
-            if (A_RES && aseq)
-               ptx::mbar_wait(a_full, (aseq - 1) & 1u, nullptr, kDrainWaitNs);
          }
       }
       __syncwarp();
@@ -645,8 +751,38 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
       // ------------------------------------------------ MMA issuer
       if (lane == 0)
       {
-         uint32_t tseq = 0, iseq = 0, aseq = 0, mst = 0, mph = 0;
+         uint32_t tseq = 0, iseq = 0, mst = 0, mph = 0;
+         uint32_t apos = 0; // A slots used so far (slot = apos % 4, use count = apos / 4)
          bool ok = true;
+         // acquire the next A slot: the MMAs that read its previous contents completed
+         auto take_slot = [&]() -> int {
+            const uint32_t s = apos % kASlots, u = apos / kASlots;
+            if (u && !ptx::mbar_wait(&a_free[s], (u - 1u) & 1u, abort_word, tmo))
+               return -1;
+            ++apos;
+            return int(s);
+         };
+         auto wait_full = [&]() -> uint8_t * {
+            if (!ptx::mbar_wait(&full[mst], mph, abort_word, tmo))
+               return nullptr;
+            ptx::tc_fence_after();
+            return sStage + mst * L.stage_bytes;
+         };
+         auto release = [&]() {
+            ptx::mma_commit(&empty[mst]);
+            if (++mst == S)
+            {
+               mst = 0;
+               mph ^= 1u;
+            }
+         };
+         // four 128x256b copies: 128 rows x 64 fp16 -> TMEM columns [32 s, 32 s + 32)
+         auto copy_a = [&](const uint8_t *src, uint32_t s) {
+            const uint64_t ad = ptx::sdesc_k_sw128(ptx::smem_u32(src));
+#pragma unroll
+            for (uint32_t ks = 0; ks < 4; ++ks)
+               ptx::tmem_cp_128x256b(tmem_base + s * 32u + ks * 8u, ad + 2u * ks);
+         };
          for (;;)
          {
             const uint32_t slot = iseq % kItemSlots;
@@ -660,62 +796,76 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
             if (idx == kNoItem)
                break;
             const WorkItem w = item_desc[slot];
-            if (A_RES && !ptx::mbar_wait(a_full, aseq & 1u, abort_word, tmo))
-            {
-               ok = false;
-               break;
-            }
+            const uint32_t abase = apos;
+            if (A_RES)
+               for (uint32_t c = 0; c < nch; ++c)
+               {
+                  const int s = take_slot();
+                  const uint8_t *stage = s < 0 ? nullptr : wait_full();
+                  if (!stage)
+                  {
+                     ok = false;
+                     break;
+                  }
+                  copy_a(stage, uint32_t(s));
+                  release();
+               }
             TileIter ti;
             for (ti.start(p.segs, w.seg_begin, w.seg_count); ti.valid_tile() && ok; ti.next())
             {
-               const uint32_t b = tseq % kAccBufs;
-               if (!ptx::mbar_wait(&acc_empty[b], ((tseq / kAccBufs) & 1u) ^ 1u, abort_word, tmo))
+               const uint32_t b = tseq & 1u;
+               if (!ptx::mbar_wait(&acc_empty[b], ((tseq >> 1) & 1u) ^ 1u, abort_word, tmo))
                {
                   ok = false;
                   break;
                }
                ptx::tc_fence_after();
-               const uint32_t N = (ti.cols() + 15u) & ~15u;
-               const uint32_t idesc = ptx::idesc_tf32(128, N);
-               const uint32_t dt = tmem_base + b * kBN;
+               const uint32_t N = 16u * (box_index(ti.cols()) + 1u);
+               const uint32_t idesc = ptx::idesc_f16(128, N);
+               const uint32_t dt = tmem_base + kAccCol0 + b * kBN;
                for (uint32_t c = 0; c < nch; ++c)
                {
-                  if (!ptx::mbar_wait(&full[mst], mph, abort_word, tmo))
+                  int s;
+                  if (A_RES)
+                     s = int((abase + c) % kASlots);
+                  else if ((s = take_slot()) < 0)
                   {
                      ok = false;
                      break;
                   }
-                  ptx::tc_fence_after();
-                  uint8_t *stage = sStage + mst * L.stage_bytes;
-                  const uint64_t ad = ptx::sdesc_k_sw128(ptx::smem_u32(A_RES ? sA + c * kAChunk : stage));
-                  const uint64_t bd = ptx::sdesc_k_sw128(ptx::smem_u32(stage + (A_RES ? 0u : kAChunk)));
-#pragma unroll
-                  for (uint32_t ks = 0; ks < 4; ++ks) // 4 x K=8 per 32-column chunk (+32 B each)
-                     ptx::mma_tf32(dt, ad + 2u * ks, bd + 2u * ks, idesc, (c | ks) != 0u);
-                  ptx::mma_commit(&empty[mst]);
-                  if (++mst == S)
+                  const uint8_t *stage = wait_full();
+                  if (!stage)
                   {
-                     mst = 0;
-                     mph ^= 1u;
+                     ok = false;
+                     break;
                   }
+                  if (!A_RES)
+                     copy_a(stage, uint32_t(s));
+                  const uint64_t bd = ptx::sdesc_k_sw128(ptx::smem_u32(stage + (A_RES ? 0u : kAChunk)));
+                  const uint32_t kleft = p.dp - c * kChunkK; // multiple of 16
+                  const uint32_t ksteps = kleft >= kChunkK ? 4u : kleft / 16u;
+                  const uint32_t at = tmem_base + uint32_t(s) * 32u;
+                  for (uint32_t ks = 0; ks < ksteps; ++ks) // K = 16 per MMA (+32 B, +8 TMEM columns)
+                     ptx::mma_f16_ts(dt, at + ks * 8u, bd + 2u * ks, idesc, (c | ks) != 0u);
+                  release();
+                  if (!A_RES)
+                     ptx::mma_commit(&a_free[s]);
                }
                if (!ok)
                   break;
                ptx::mma_commit(&acc_full[b]);
                ++tseq;
             }
+            if (A_RES) // the item's A slots are free once its MMAs complete
+               for (uint32_t c = 0; c < nch && abase + c < apos; ++c)
+                  ptx::mma_commit(&a_free[(abase + c) % kASlots]);
             if (!ok)
                break;
-            if (A_RES)
-            {
-               ptx::mma_commit(a_empty);
-               ++aseq;
-            }
             ptx::mbar_arrive(&item_empty[slot]);
          }
          if (!ok)
             raise_abort(abort_word, p.status, UNGX_ERR_TIMEOUT);
-         // every MMA issued by this thread (and its arrivals) completes before teardown
+         // every MMA / copy issued by this thread (and its arrivals) completes before teardown
          ptx::mma_commit(done_bar);
          ptx::mbar_wait(done_bar, 0, nullptr, kDrainWaitNs);
       }
@@ -724,12 +874,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
    else
    {
       // ------------------------------------------------ epilogue: one thread per source row
-      // Warp w reads TMEM lane quarter w % 4 (rows 32q..32q+31) and, of every 128-column
-      // tile, the 32-column chunks h and h + 2.
+      // Warp w reads TMEM lane quarter w % 4 (rows 32q..32q+31) and, of every 192-column
+      // tile, the 32-column chunks h and h + 3 (h = 0, 1, 2: its column third).
       const uint32_t q = warp & 3u;
       const uint32_t h = (warp - 2u) >> 2;
       const uint32_t r = q * 32u + lane;
       float *nrm = sNorm + (warp - 2u) * 32u;
+      const float nis = p.scale->neg2_inv_s2; // keys in the unscaled centred domain
       uint32_t tseq = 0, iseq = 0;
       bool ok = true;
       for (;;)
@@ -764,7 +915,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
          float n0 = INFINITY, n1 = INFINITY;
          if (ti.valid_tile())
          {
-            const uint32_t c0 = h * 32u + lane, c1 = c0 + 64u, v = ti.cols(), x0 = ti.x0();
+            const uint32_t c0 = h * 32u + lane, c1 = c0 + 96u, v = ti.cols(), x0 = ti.x0();
             n0 = c0 < v ? __ldg(p.xnorm + x0 + c0) : INFINITY;
             n1 = c1 < v ? __ldg(p.xnorm + x0 + c1) : INFINITY;
          }
@@ -775,12 +926,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
             ti.next();
             if (ti.valid_tile())
             {
-               const uint32_t c0 = h * 32u + lane, c1 = c0 + 64u, v = ti.cols(), nx0 = ti.x0();
+               const uint32_t c0 = h * 32u + lane, c1 = c0 + 96u, v = ti.cols(), nx0 = ti.x0();
                n0 = c0 < v ? __ldg(p.xnorm + nx0 + c0) : INFINITY;
                n1 = c1 < v ? __ldg(p.xnorm + nx0 + c1) : INFINITY;
             }
-            const uint32_t b = tseq % kAccBufs;
-            if (!ptx::mbar_wait(&acc_full[b], (tseq / kAccBufs) & 1u, abort_word, tmo))
+            const uint32_t b = tseq & 1u;
+            if (!ptx::mbar_wait(&acc_full[b], (tseq >> 1) & 1u, abort_word, tmo))
             {
                ok = false;
                break;
@@ -789,37 +940,49 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
 #pragma unroll 1
             for (uint32_t i = 0; i < 2; ++i)
             {
-               const uint32_t j = h + 2u * i;
+               const uint32_t j = h + 3u * i;
                if (!warp_ok || j * 32u >= valid)
                   break;
                __syncwarp();
                nrm[lane] = i ? cn1 : cn0;
                __syncwarp();
                uint32_t raw[32];
-               ptx::tmem_ld32(tmem_base + ((q * 32u) << 16) + b * kBN + j * 32u, raw);
+               ptx::tmem_ld32(tmem_base + ((q * 32u) << 16) + kAccCol0 + b * kBN + j * 32u, raw);
                ptx::tmem_wait_ld();
-               float kv[32];
+               // key = fl(norm + nis * acc); the sign of fl(key - thr) is set exactly when
+               // key < thr (an exact zero difference is +0): element jj goes to bit 31 - jj
+               const float4 *n4 = reinterpret_cast<const float4 *>(nrm);
+               const uint64_t nis2 = pack2(nis, nis), thr2 = pack2(thr, thr);
                uint32_t mask = 0;
 #pragma unroll
-               for (int jj = 0; jj < 32; ++jj)
+               for (int g = 0; g < 8; ++g)
                {
-                  kv[jj] = __fmaf_rn(-2.0f, __uint_as_float(raw[jj]), nrm[jj]);
-                  mask |= (kv[jj] < thr) ? (1u << jj) : 0u;
+                  const float4 nv = n4[g];
+                  const uint64_t k01 = fma2(nis2, pack2(__uint_as_float(raw[4 * g]), __uint_as_float(raw[4 * g + 1])),
+                                            pack2(nv.x, nv.y));
+                  const uint64_t k23 =
+                      fma2(nis2, pack2(__uint_as_float(raw[4 * g + 2]), __uint_as_float(raw[4 * g + 3])),
+                           pack2(nv.z, nv.w));
+                  const uint64_t d01 = sub2(k01, thr2), d23 = sub2(k23, thr2);
+                  mask = __funnelshift_l(uint32_t(d01), mask, 1);
+                  mask = __funnelshift_l(uint32_t(d01 >> 32), mask, 1);
+                  mask = __funnelshift_l(uint32_t(d23), mask, 1);
+                  mask = __funnelshift_l(uint32_t(d23 >> 32), mask, 1);
                }
                // every lane inserts its passing keys; the loop runs as often as the
                // busiest lane needs, lanes without a candidate insert +inf (a no-op)
                const uint32_t cbase = x0 + j * 32u;
                while (__any_sync(0xffffffffu, mask != 0u))
                {
-                  const uint32_t jj = mask ? uint32_t(__ffs(mask) - 1) : 0u;
-                  const float kk = select32(kv, jj);
+                  const uint32_t jj = mask ? uint32_t(__clz(mask)) : 0u;
+                  const float kk = __fmaf_rn(nis, __uint_as_float(select32(raw, jj)), nrm[jj]);
                   const uint32_t ev = __float_as_uint(key[KP - 1]) & kSlotMask; // slot that drops out
                   const float v = __uint_as_float((__float_as_uint(kk) & ~kSlotMask) | ev);
                   const bool ins = mask != 0u && v < key[KP - 1];
                   if (ins)
                      colv[ev * 32u] = cbase + jj;
                   insert_packed<KP>(key, ins ? v : INFINITY);
-                  mask &= mask - 1u;
+                  mask &= ~(0x80000000u >> jj);
                }
                thr = row_ok ? key[KP - 1] : -INFINITY;
             }
@@ -832,8 +995,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
             break;
          if (row_ok)
          {
-            float4 *kd = reinterpret_cast<float4 *>(p.cand_key + (size_t(w.row_begin + r) * 2u + h) * KP);
-            uint4 *cd = reinterpret_cast<uint4 *>(p.cand_col + (size_t(w.row_begin + r) * 2u + h) * KP);
+            float4 *kd = reinterpret_cast<float4 *>(p.cand_key + (size_t(w.row_begin + r) * kTcLists + h) * KP);
+            uint4 *cd = reinterpret_cast<uint4 *>(p.cand_col + (size_t(w.row_begin + r) * kTcLists + h) * KP);
 #pragma unroll
             for (int i = 0; i < KP / 4; ++i)
             {
@@ -865,6 +1028,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
 // ------------------------------------------------------------------ rerank + certificate
 // One block per work item; TPR threads per row (one or two candidates each), RPB rows
 // per pass.  Keys are the packed prefilter keys: within 2^-17 relative of the fp32 key.
+// The row's three lists are merged into its KP smallest keys first.
 template <int KP>
 __global__ void __launch_bounds__(256) rerank_kernel(const RerankParams p)
 {
@@ -912,6 +1076,8 @@ __global__ void __launch_bounds__(256) rerank_kernel(const RerankParams p)
    const bool vec4 = (p.d & 3u) == 0;
    const double pk = 1.0 / 131072.0; // packed-key tolerance, 2^-17 relative
    const double bmax = sqrt((double)s_maxn2 * (1.0 + p.gd));
+   const double inv_s = (double)p.scale->inv_s;
+   const bool exact_only = p.scale->exact_only != 0;
    for (uint32_t base = 0; base < w.row_count; base += RPB)
    {
       const uint32_t r = base + rl;
@@ -920,22 +1086,26 @@ __global__ void __launch_bounds__(256) rerank_kernel(const RerankParams p)
       const double qn = ok ? (double)__ldg(p.xnorm + row) : 0.0;
       const double ahi = sqrt(qn * (1.0 + p.gd));
       // |key - (||b||^2 - 2 a.b)| <= bound for every column of this row
-      const double bound = (p.c1 * ahi * bmax + p.c2 * bmax * bmax) * (1.0 + 1.0 / 1024.0);
+      const double bound =
+          (p.c1 * ahi * bmax + p.c2 * bmax * bmax + p.c3 * inv_s * (ahi + bmax) + p.c4 * inv_s * inv_s) *
+          (1.0 + 1.0 / 1024.0);
       if (ok && sub == 0)
       {
          float k0[KP];
          uint32_t c0[KP];
-         const float *kp = p.cand_key + size_t(row) * 2u * KP;
-         const uint32_t *cp = p.cand_col + size_t(row) * 2u * KP;
+         const float *kp = p.cand_key + size_t(row) * kTcLists * KP;
+         const uint32_t *cp = p.cand_col + size_t(row) * kTcLists * KP;
 #pragma unroll
          for (int i = 0; i < KP; ++i)
          {
             k0[i] = kp[i];
             c0[i] = cp[i];
          }
+         // each list is ascending: stop at its first key past the running maximum
 #pragma unroll 1
-         for (int i = 0; i < KP; ++i)
-            insert_key<KP>(k0, c0, kp[KP + i], cp[KP + i]);
+         for (uint32_t l = 1; l < kTcLists; ++l)
+            for (int i = 0; i < KP && kp[l * KP + i] < k0[KP - 1]; ++i)
+               insert_key<KP>(k0, c0, kp[l * KP + i], cp[l * KP + i]);
          float kk = INFINITY;
 #pragma unroll
          for (int i = 0; i < KP; ++i)
@@ -988,8 +1158,8 @@ __global__ void __launch_bounds__(256) rerank_kernel(const RerankParams p)
          // tolerance), hence true squared distance >= ||a||^2 + T - bound and reference
          // distance >= that * (1 - gref); above the k-th exact distance, no excluded
          // column can enter the top-k
-         bool cert = true;
-         if (total > uint32_t(KP))
+         bool cert = !exact_only;
+         if (cert && total > uint32_t(KP))
          {
             float dk = INFINITY;
 #pragma unroll
@@ -1064,7 +1234,13 @@ int tc_candidates_for_k(uint32_t k)
    return k + 8 <= 16 ? 16 : k + 8 <= 24 ? 24 : 32;
 }
 
-bool tc_a_resident(uint32_t dp) { return dp <= 128; }
+uint32_t tc_operand_cols(uint32_t d)
+{
+   const uint32_t dp = (d + 15u) / 16u * 16u;
+   return dp < kChunkK ? kChunkK : dp;
+}
+
+bool tc_a_resident(uint32_t dp) { return (dp + kChunkK - 1) / kChunkK <= kASlots; }
 
 size_t tc_smem_bytes(uint32_t dp, uint32_t k)
 {
@@ -1074,31 +1250,46 @@ size_t tc_smem_bytes(uint32_t dp, uint32_t k)
 void tc_certificate_constants(uint32_t d, uint32_t dp, RerankParams &p)
 {
    const double u24 = std::ldexp(1.0, -24);
-   // relative error of a TF32-rounded (11-bit significand, nearest-even) centred
-   // value against the exact centred value
+   // relative error of the fp16 operand (11-bit significand, nearest-even; the scale
+   // by a power of two is exact) against the exact centred value, for elements in
+   // the normal fp16 range
    const double ur = u24 + std::ldexp(1.0, -11) * (1.0 + u24);
-   // tf32 x tf32 products are exact in fp32; the tensor-core fp32 accumulation is
-   // taken as 4x looser than one rounding per K=8 step
-   const double cacc = (double(dp) / 2.0 + 8.0) * std::ldexp(1.0, -22);
+   // fp16 x fp16 products are exact in fp32; the tensor-core fp32 accumulation over dp
+   // products is taken as one 2^-23 relative error per product plus 16
+   const double cacc = (double(dp) + 16.0) * std::ldexp(1.0, -23);
    p.c1 = 4.0 * ur + 2.0 * ur * ur + 2.0 * cacc * (1.0 + ur) * (1.0 + ur) + 2.0 * std::ldexp(1.0, -23);
    p.c2 = (double(d) + 4.0) * u24 + std::ldexp(1.0, -23) + u24;
+   // elements below the normal fp16 range carry an absolute error <= 2^-25 in scaled
+   // units: the key moves by at most 2 (1+ur) 2^-25 sqrt(d) (|a| + |b|) / s plus
+   // 2 d 2^-50 / s^2, and the accumulation adds its relative share of both
+   p.c3 = 2.0 * (1.0 + ur) * std::ldexp(1.0, -25) * std::sqrt(double(d)) * (1.0 + cacc) * (1.0 + std::ldexp(1.0, -20));
+   p.c4 = 2.0 * double(d) * std::ldexp(1.0, -50) * (1.0 + cacc) * (1.0 + std::ldexp(1.0, -20));
    p.gd = (double(d) + 6.0) * u24;
    p.gref = (double(d) + 8.0) * u24;
 }
 
-cudaError_t launch_colsum(const float *X, uint32_t n, uint32_t d, double *sums, cudaStream_t s)
+cudaError_t launch_colsum(const float *X, uint32_t n, uint32_t d, double *sums, uint32_t *range, cudaStream_t s)
 {
    cudaError_t e = cudaMemsetAsync(sums, 0, sizeof(double) * d, s);
+   if (e == cudaSuccess)
+      e = cudaMemsetAsync(range, 0, sizeof(uint32_t) * 2 * d, s);
    if (e != cudaSuccess || n == 0)
       return e;
-   const uint32_t rows_per_block = 2048;
+   const uint32_t rows_per_block = 256;
    const uint32_t blocks = (n + rows_per_block - 1) / rows_per_block;
-   colsum_kernel<<<blocks, 256, 0, s>>>(X, n, d, sums, rows_per_block);
+   colsum_kernel<<<blocks, d < 256 ? ((d + 31) / 32) * 32 : 256, 0, s>>>(X, n, d, sums, range, rows_per_block);
    return cudaGetLastError();
 }
 
-cudaError_t launch_center(const float *X, const double *sums, uint32_t n, uint32_t d, uint32_t dp, float *mean,
-                          float *Xp, float *xnorm, cudaStream_t s)
+cudaError_t launch_scale(const double *sums, const uint32_t *range, uint32_t n, uint32_t d, float *mean,
+                         OperandScale *scale, cudaStream_t s)
+{
+   scale_kernel<<<1, 256, 0, s>>>(sums, range, n ? n : 1u, d, mean, scale);
+   return cudaGetLastError();
+}
+
+cudaError_t launch_center(const float *X, const float *mean, const OperandScale *scale, uint32_t n, uint32_t d,
+                          uint32_t dp, uint16_t *Xh, float *xnorm, cudaStream_t s)
 {
    const size_t smem = sizeof(float) * d;
    if (smem > 48 * 1024)
@@ -1108,7 +1299,7 @@ cudaError_t launch_center(const float *X, const double *sums, uint32_t n, uint32
          return e;
    }
    const uint32_t blocks = n ? std::min<uint32_t>((n + 7) / 8, 148 * 16) : 1;
-   center_kernel<<<blocks, 256, smem, s>>>(X, sums, n, d, dp, mean, Xp, xnorm);
+   center_kernel<<<blocks, 256, smem, s>>>(X, mean, scale, n, d, dp, reinterpret_cast<__half *>(Xh), xnorm);
    return cudaGetLastError();
 }
 

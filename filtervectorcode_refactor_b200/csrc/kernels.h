@@ -10,14 +10,31 @@
 namespace ungx
 {
 
+// fp16 operand rows (n x dp, dp a multiple of 16), 128-byte swizzled boxes of 64
+// columns: A = 128 rows, B[i] = 16 (i + 1) rows (the narrowest box covering a tile).
+constexpr uint32_t kTcBoxes = 12;
 struct TcMaps
 {
-   CUtensorMap a;     // operand rows, box {32 cols, 128 rows}
-   CUtensorMap b[4];  // operand rows, box {32 cols, 16 << i rows}
+   CUtensorMap a;
+   CUtensorMap b[kTcBoxes];
 };
 
+// Scale of the fp16 operand: it holds fp16(s * fl(x - mean)) with s = 2^e, chosen
+// from the column ranges so that no element exceeds 2^15 in magnitude.
+struct OperandScale
+{
+   float s;            // 2^e
+   float neg2_inv_s2;  // -2 / s^2 (exact)
+   float inv_s;        // 1 / s
+   int exact_only;     // 1: the data range does not fit the fp16 operand; certify nothing
+};
+
+// Candidate lists per row: one per column third of a tile (three epilogue warps share
+// a TMEM lane quarter).
+constexpr uint32_t kTcLists = 3;
+
 // Tensor-core prefilter: per source row, the KP smallest keys ||x||^2 - 2 q.x of each
-// column half, written to cand_key / cand_col [row][2][KP].
+// column third, written to cand_key / cand_col [row][kTcLists][KP].
 struct TcParams
 {
    const WorkItem *items;
@@ -25,6 +42,7 @@ struct TcParams
    uint32_t num_items;
    uint32_t *item_counter;   // zeroed before launch
    const float *xnorm;       // ||fl(x - mean)||^2, fp32
+   const OperandScale *scale;
    uint32_t dp;
    float *cand_key;
    uint32_t *cand_col;
@@ -52,7 +70,8 @@ struct RerankParams
    uint32_t *fb_items;
    uint32_t *fb_count;       // zeroed before launch
    unsigned long long *counters; // [0] certified rows, [1] rejected rows
-   double c1, c2, gd, gref;  // certificate constants, see tc_certificate_constants
+   const OperandScale *scale;
+   double c1, c2, c3, c4, gd, gref; // certificate constants, see tc_certificate_constants
 };
 
 struct ExactParams
@@ -74,14 +93,21 @@ constexpr uint32_t kTcMaxK = 24;
 // Largest k the exact route supports (per-lane list of 128).
 constexpr uint32_t kExactMaxK = 128;
 
-int tc_candidates_for_k(uint32_t k);              // 8, 16, 24 or 32; 0 = unsupported
-bool tc_a_resident(uint32_t dp);                  // A operand kept in smem per item
+int tc_candidates_for_k(uint32_t k);              // 16, 24 or 32; 0 = unsupported
+uint32_t tc_operand_cols(uint32_t d);             // dp: d rounded up to 16, at least 64
+bool tc_a_resident(uint32_t dp);                  // A operand kept in TMEM per item
 size_t tc_smem_bytes(uint32_t dp, uint32_t k);
 void tc_certificate_constants(uint32_t d, uint32_t dp, RerankParams &p);
 
-cudaError_t launch_colsum(const float *X, uint32_t n, uint32_t d, double *sums, cudaStream_t s);
-cudaError_t launch_center(const float *X, const double *sums, uint32_t n, uint32_t d, uint32_t dp, float *mean,
-                          float *Xp, float *xnorm, cudaStream_t s);
+// Column sums (fp64) and ranges of X; `range` holds, per column, the complement of the
+// minimum's and the maximum's order-preserving integer keys (both zeroed here).
+cudaError_t launch_colsum(const float *X, uint32_t n, uint32_t d, double *sums, uint32_t *range, cudaStream_t s);
+// mean (fp32) and the operand scale from the column sums and ranges.
+cudaError_t launch_scale(const double *sums, const uint32_t *range, uint32_t n, uint32_t d, float *mean,
+                         OperandScale *scale, cudaStream_t s);
+// fp16 operand rows Xh [n x dp] and fp32 norms of the centred rows.
+cudaError_t launch_center(const float *X, const float *mean, const OperandScale *scale, uint32_t n, uint32_t d,
+                          uint32_t dp, uint16_t *Xh, float *xnorm, cudaStream_t s);
 cudaError_t launch_group_maxnorm(const float *xnorm, const uint32_t *ranges, uint32_t G, float *out,
                                  cudaStream_t s);
 cudaError_t launch_fill_empty(const RowRange *ranges, uint32_t nranges, uint32_t k, uint32_t *ids, float *dists,

@@ -131,16 +131,26 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols)
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// D[tmem] (+)= A[smem] * B[smem]^T, kind::tf32 (fp32 accumulator), one CTA.
-// accumulate = 0 overwrites D.
-__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                         uint32_t accumulate)
+// D[tmem] (+)= A[tmem] * B[smem]^T, kind::f16 (fp16 operands, fp32 accumulator),
+// one CTA.  A occupies TMEM lanes 0..127 (row = lane), two fp16 of K per 32-bit
+// column: one K=16 step reads 8 columns from a_tmem.  accumulate = 0 overwrites D.
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate)
 {
    asm volatile("{\n\t.reg .pred p;\n\t"
                 "setp.ne.b32 p, %4, 0;\n\t"
-                "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-                "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+                "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+                "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
                 : "memory");
+}
+
+// Copy 128 rows x 256 bits (16 fp16 of K) from shared memory, described by a matrix
+// descriptor, into TMEM lanes 0..127 at columns [taddr, taddr + 8).  Ordered before
+// the tcgen05.mma this thread issues next; a later copy into the same columns must
+// wait for the MMAs that read them (tcgen05.commit + mbarrier).
+__device__ __forceinline__ void tmem_cp_128x256b(uint32_t taddr, uint64_t sdesc)
+{
+   asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
 }
 
 // Arrive once on `bar` when every tcgen05 op this thread issued so far completed.
@@ -170,7 +180,7 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32])
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // Shared-memory matrix descriptor for a K-major operand in the canonical
-// 128-byte-swizzle layout: rows of 128 B (32 fp32), 8-row atoms of 1024 B stacked
+// 128-byte-swizzle layout: rows of 128 B (64 fp16), 8-row atoms of 1024 B stacked
 // contiguously (what a TMA load with SWIZZLE_128B and a 128-byte inner box writes).
 // Fields: start address >> 4 [0,14), leading byte offset >> 4 [16,30) (unused for
 // swizzled K-major, set to 1), stride byte offset >> 4 [32,46) = 1024 B between
@@ -186,12 +196,12 @@ __device__ __forceinline__ uint64_t sdesc_k_sw128(uint32_t saddr)
    return d;
 }
 
-// Instruction descriptor, kind::tf32, fp32 accumulator, both operands K-major:
-// c_format F32 = 1 at [4,6), a/b format TF32 = 2 at [7,10) / [10,13),
-// N >> 3 at [17,23), M >> 4 at [24,29).
-__host__ __device__ constexpr uint32_t idesc_tf32(uint32_t M, uint32_t N)
+// Instruction descriptor, kind::f16 with fp16 A and B, fp32 accumulator, both
+// operands K-major: c_format F32 = 1 at [4,6), a/b format F16 = 0 at [7,10) /
+// [10,13), N >> 3 at [17,23), M >> 4 at [24,29).
+__host__ __device__ constexpr uint32_t idesc_f16(uint32_t M, uint32_t N)
 {
-   return (1u << 4) | (2u << 7) | (2u << 10) | ((N >> 3) << 17) | ((M >> 4) << 24);
+   return (1u << 4) | ((N >> 3) << 17) | ((M >> 4) << 24);
 }
 
 } // namespace ptx
