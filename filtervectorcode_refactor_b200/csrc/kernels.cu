@@ -34,7 +34,7 @@ namespace ungx
 namespace
 {
 constexpr uint32_t kEpiWarps = 12;                    // three per TMEM lane quarter
-constexpr uint32_t kTcThreads = 64 + 32 * kEpiWarps;  // warp 0 TMA, warp 1 MMA, 2.. epilogue
+constexpr uint32_t kTcThreads = 96 + 32 * kEpiWarps;  // warp 0 TMA, 1 MMA, 2..13 epilogue, 14 MMA (MODE 2)
 constexpr uint32_t kBN = 192;          // target columns per tile / TMEM accumulator
 constexpr uint32_t kAccBufs = 2;       // TMEM accumulators at columns 128 + 192 b
 constexpr uint32_t kAccCol0 = 128;     // TMEM columns [0, 128): four A slots
@@ -589,26 +589,35 @@ __device__ __forceinline__ void insert_packed(float (&L)[K], float v)
    L[0] = fminf(L[0], v);
 }
 
-template <int KP, bool A_RES>
+// MODE 0: A streamed per K chunk (dp > 256), one MMA issuer.
+// MODE 1: A resident per item (128 < dp <= 256), one MMA issuer.
+// MODE 2: A resident (dp <= 128), two MMA issuers (warps 1 and 14) on alternate tiles,
+//         each with its own ring of stages and its own two A slots: one thread's
+//         barrier waits and bookkeeping overlap the other's MMAs (tcgen05.mma issue
+//         hardly queues, and a tile is only dp / 16 MMAs).
+template <int KP, int MODE>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant__ TcMaps maps, const TcParams p)
 {
+   constexpr bool A_RES = MODE >= 1;
+   constexpr bool DUAL = MODE == 2;
+   constexpr uint32_t R = DUAL ? 2u : 1u; // rings of stages
    extern __shared__ uint8_t smem_raw[];
    const uint32_t raw_u32 = ptx::smem_u32(smem_raw);
    uint8_t *smem = smem_raw + (((raw_u32 + 1023u) & ~1023u) - raw_u32);
    const TcLayout L = tc_layout(p.dp, A_RES, KP);
-   const uint32_t S = L.stages;
+   const uint32_t SR = L.stages / R; // stages per ring
    uint8_t *sStage = smem + L.stage_off;
    float *sNorm = reinterpret_cast<float *>(smem + L.norm_off);
    uint32_t *sColv = reinterpret_cast<uint32_t *>(smem + L.colv_off);
    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bar_off);
-   uint64_t *full = bars;              // [S <= 16]
-   uint64_t *empty = bars + 16;        // [S]
+   uint64_t *full = bars;              // [R * SR <= 16], ring r = stages [r SR, r SR + SR)
+   uint64_t *empty = bars + 16;        // [R * SR]
    uint64_t *acc_full = bars + 32;     // [2]
    uint64_t *acc_empty = bars + 34;    // [2]
-   uint64_t *a_free = bars + 36;       // [4]: MMAs reading A slot s completed
+   uint64_t *a_free = bars + 36;       // [4]: MMAs reading A slot s completed (MODE 2: [issuer])
    uint64_t *item_full = bars + 40;    // [2]
    uint64_t *item_empty = bars + 42;   // [2]
-   uint64_t *done_bar = bars + 44;
+   uint64_t *done_bar = bars + 44;     // [2]: one per issuer
    volatile uint32_t *item_slot = reinterpret_cast<volatile uint32_t *>(smem + L.misc_off);
    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L.misc_off + 16);
    volatile int *abort_word = reinterpret_cast<volatile int *>(smem + L.misc_off + 32);
@@ -620,7 +629,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
 
    if (threadIdx.x == 0)
    {
-      for (uint32_t s = 0; s < S; ++s)
+      for (uint32_t s = 0; s < R * SR; ++s)
       {
          ptx::mbar_init(&full[s], 1);
          ptx::mbar_init(&empty[s], 1);
@@ -635,9 +644,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
       for (uint32_t s = 0; s < kItemSlots; ++s)
       {
          ptx::mbar_init(&item_full[s], 1);
-         ptx::mbar_init(&item_empty[s], 1 + kEpiWarps); // MMA thread + epilogue warps
+         ptx::mbar_init(&item_empty[s], R + kEpiWarps); // MMA issuers + epilogue warps
       }
-      ptx::mbar_init(done_bar, 1);
+      ptx::mbar_init(&done_bar[0], 1);
+      ptx::mbar_init(&done_bar[1], 1);
       *abort_word = 0;
       ptx::fence_mbar_init();
    }
@@ -662,21 +672,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
       // ------------------------------------------------ TMA producer
       if (lane == 0 && !(p.inject & UNGX_INJECT_WITHHOLD_WORK))
       {
-         uint32_t it = 0, iseq = 0, pst = 0, pph = 0;
+         uint32_t it[R], pst[R], pph[R]; // per ring: stages issued, position, phase
+         for (uint32_t r = 0; r < R; ++r)
+            it[r] = pst[r] = pph[r] = 0;
+         uint32_t iseq = 0, tseq = 0;
          bool ok = true;
-         auto next_stage = [&](uint32_t bytes) -> uint8_t * {
-            if (!ptx::mbar_wait(&empty[pst], pph ^ 1u, abort_word, tmo))
+         auto next_stage = [&](uint32_t r, uint32_t bytes) -> uint8_t * {
+            const uint32_t g = r * SR + pst[r];
+            if (!ptx::mbar_wait(&empty[g], pph[r] ^ 1u, abort_word, tmo))
                return nullptr;
-            uint8_t *dst = sStage + pst * L.stage_bytes;
-            ptx::mbar_arrive_expect_tx(&full[pst], bytes);
-            return dst;
+            ptx::mbar_arrive_expect_tx(&full[g], bytes);
+            return sStage + g * L.stage_bytes;
          };
-         auto advance = [&]() {
-            ++it;
-            if (++pst == S) // ring position and phase kept without division
+         auto advance = [&](uint32_t r) {
+            ++it[r];
+            if (++pst[r] == SR) // ring position and phase kept without division
             {
-               pst = 0;
-               pph ^= 1u;
+               pst[r] = 0;
+               pph[r] ^= 1u;
             }
          };
          for (;;)
@@ -697,36 +710,40 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
             ++iseq;
             if (idx >= p.num_items)
                break;
-            if (A_RES) // the item's source chunks, once, through the ring
-               for (uint32_t c = 0; c < nch && ok; ++c)
-               {
-                  uint8_t *dst = next_stage(kAChunk);
-                  if (!dst)
+            if (A_RES) // the item's source chunks, once per ring
+               for (uint32_t r = 0; r < R && ok; ++r)
+                  for (uint32_t c = 0; c < nch; ++c)
                   {
-                     ok = false;
-                     break;
+                     uint8_t *dst = next_stage(r, kAChunk);
+                     if (!dst)
+                     {
+                        ok = false;
+                        break;
+                     }
+                     ptx::tma_load_2d(dst, &maps.a, &full[r * SR + pst[r]], int32_t(c * kChunkK),
+                                      int32_t(w.row_begin));
+                     advance(r);
                   }
-                  ptx::tma_load_2d(dst, &maps.a, &full[pst], int32_t(c * kChunkK), int32_t(w.row_begin));
-                  advance();
-               }
             TileIter ti;
-            for (ti.start(p.segs, w.seg_begin, w.seg_count); ti.valid_tile() && ok; ti.next())
+            for (ti.start(p.segs, w.seg_begin, w.seg_count); ti.valid_tile() && ok; ti.next(), ++tseq)
             {
+               const uint32_t r = DUAL ? (tseq & 1u) : 0u;
                const uint32_t bix = box_index(ti.cols());
                const uint32_t brows = 16u * (bix + 1u);
                for (uint32_t c = 0; c < nch; ++c)
                {
-                  uint8_t *dst = next_stage((A_RES ? 0u : kAChunk) + brows * 128u);
+                  uint8_t *dst = next_stage(r, (A_RES ? 0u : kAChunk) + brows * 128u);
                   if (!dst)
                   {
                      ok = false;
                      break;
                   }
+                  uint64_t *fb = &full[r * SR + pst[r]];
                   if (!A_RES)
-                     ptx::tma_load_2d(dst, &maps.a, &full[pst], int32_t(c * kChunkK), int32_t(w.row_begin));
-                  ptx::tma_load_2d(dst + (A_RES ? 0u : kAChunk), &maps.b[bix], &full[pst], int32_t(c * kChunkK),
+                     ptx::tma_load_2d(dst, &maps.a, fb, int32_t(c * kChunkK), int32_t(w.row_begin));
+                  ptx::tma_load_2d(dst + (A_RES ? 0u : kAChunk), &maps.b[bix], fb, int32_t(c * kChunkK),
                                    int32_t(ti.x0()));
-                  advance();
+                  advance(r);
                }
             }
             if (!ok)
@@ -736,25 +753,26 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
          {
             raise_abort(abort_word, p.status, UNGX_ERR_TIMEOUT);
             // drain: every load already issued must land before the CTA exits
-            for (uint32_t st = 0; st < S; ++st)
-            {
-               const uint32_t issued = it / S + (st < it % S ? 1u : 0u);
-               if (issued)
-                  ptx::mbar_wait(&full[st], (issued - 1) & 1u, nullptr, kDrainWaitNs);
-            }
+            for (uint32_t r = 0; r < R; ++r)
+               for (uint32_t st = 0; st < SR; ++st)
+               {
+                  const uint32_t issued = it[r] / SR + (st < it[r] % SR ? 1u : 0u);
+                  if (issued)
+                     ptx::mbar_wait(&full[r * SR + st], (issued - 1) & 1u, nullptr, kDrainWaitNs);
+               }
          }
       }
       __syncwarp();
    }
-   else if (warp == 1)
+   else if (warp == 1 || (DUAL && warp == kEpiWarps + 2u))
    {
-      // ------------------------------------------------ MMA issuer
+      // ------------------------------------------------ MMA issuer(s)
+      const uint32_t m = warp == 1 ? 0u : 1u; // issuer: ring m, accumulator (tile parity) m
       if (lane == 0)
       {
-         uint32_t tseq = 0, iseq = 0, mst = 0, mph = 0;
-         uint32_t apos = 0; // A slots used so far (slot = apos % 4, use count = apos / 4)
+         uint32_t tseq = 0, iseq = 0, mst = 0, mph = 0, items = 0;
+         uint32_t apos = 0; // MODE 0/1: A slots used so far (slot = apos % 4, use count = apos / 4)
          bool ok = true;
-         // acquire the next A slot: the MMAs that read its previous contents completed
          auto take_slot = [&]() -> int {
             const uint32_t s = apos % kASlots, u = apos / kASlots;
             if (u && !ptx::mbar_wait(&a_free[s], (u - 1u) & 1u, abort_word, tmo))
@@ -763,14 +781,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
             return int(s);
          };
          auto wait_full = [&]() -> uint8_t * {
-            if (!ptx::mbar_wait(&full[mst], mph, abort_word, tmo))
+            const uint32_t g = m * SR + mst;
+            if (!ptx::mbar_wait(&full[g], mph, abort_word, tmo))
                return nullptr;
-            ptx::tc_fence_after();
-            return sStage + mst * L.stage_bytes;
+            return sStage + g * L.stage_bytes;
          };
          auto release = [&]() {
-            ptx::mma_commit(&empty[mst]);
-            if (++mst == S)
+            ptx::mma_commit(&empty[m * SR + mst]);
+            if (++mst == SR)
             {
                mst = 0;
                mph ^= 1u;
@@ -797,7 +815,28 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
                break;
             const WorkItem w = item_desc[slot];
             const uint32_t abase = apos;
-            if (A_RES)
+            if (DUAL)
+            {
+               // this issuer's A slots 2m, 2m + 1 are free once its previous item's MMAs completed
+               if (items && !ptx::mbar_wait(&a_free[m], (items - 1u) & 1u, abort_word, tmo))
+               {
+                  ok = false;
+                  break;
+               }
+               for (uint32_t c = 0; c < nch && ok; ++c)
+               {
+                  const uint8_t *stage = wait_full();
+                  if (!stage)
+                  {
+                     ok = false;
+                     break;
+                  }
+                  ptx::tc_fence_after();
+                  copy_a(stage, 2u * m + c);
+                  release();
+               }
+            }
+            else if (A_RES)
                for (uint32_t c = 0; c < nch; ++c)
                {
                   const int s = take_slot();
@@ -807,13 +846,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
                      ok = false;
                      break;
                   }
+                  ptx::tc_fence_after();
                   copy_a(stage, uint32_t(s));
                   release();
                }
             TileIter ti;
-            for (ti.start(p.segs, w.seg_begin, w.seg_count); ti.valid_tile() && ok; ti.next())
+            for (ti.start(p.segs, w.seg_begin, w.seg_count); ti.valid_tile() && ok; ti.next(), ++tseq)
             {
                const uint32_t b = tseq & 1u;
+               if (DUAL && b != m)
+                  continue; // the other issuer's tile
                if (!ptx::mbar_wait(&acc_empty[b], ((tseq >> 1) & 1u) ^ 1u, abort_word, tmo))
                {
                   ok = false;
@@ -823,42 +865,83 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
                const uint32_t N = 16u * (box_index(ti.cols()) + 1u);
                const uint32_t idesc = ptx::idesc_f16(128, N);
                const uint32_t dt = tmem_base + kAccCol0 + b * kBN;
-               for (uint32_t c = 0; c < nch; ++c)
+               if (DUAL)
                {
-                  int s;
-                  if (A_RES)
-                     s = int((abase + c) % kASlots);
-                  else if ((s = take_slot()) < 0)
+                  // dp <= 128: one or two chunks of four K = 16 steps (the last may be partial)
+                  const uint32_t at = tmem_base + 64u * m;
+                  const uint8_t *st0 = wait_full();
+                  if (!st0)
                   {
                      ok = false;
                      break;
                   }
-                  const uint8_t *stage = wait_full();
-                  if (!stage)
-                  {
-                     ok = false;
-                     break;
-                  }
-                  if (!A_RES)
-                     copy_a(stage, uint32_t(s));
-                  const uint64_t bd = ptx::sdesc_k_sw128(ptx::smem_u32(stage + (A_RES ? 0u : kAChunk)));
-                  const uint32_t kleft = p.dp - c * kChunkK; // multiple of 16
-                  const uint32_t ksteps = kleft >= kChunkK ? 4u : kleft / 16u;
-                  const uint32_t at = tmem_base + uint32_t(s) * 32u;
-                  for (uint32_t ks = 0; ks < ksteps; ++ks) // K = 16 per MMA (+32 B, +8 TMEM columns)
-                     ptx::mma_f16_ts(dt, at + ks * 8u, bd + 2u * ks, idesc, (c | ks) != 0u);
+                  const uint64_t bd0 = ptx::sdesc_k_sw128(ptx::smem_u32(st0));
+                  const uint32_t k0 = p.dp >= kChunkK ? 4u : p.dp / 16u;
+                  ptx::mma_f16_ts(dt, at, bd0, idesc, 0u);
+#pragma unroll
+                  for (uint32_t ks = 1; ks < 4; ++ks)
+                     if (ks < k0)
+                        ptx::mma_f16_ts(dt, at + ks * 8u, bd0 + 2u * ks, idesc, 1u);
                   release();
-                  if (!A_RES)
-                     ptx::mma_commit(&a_free[s]);
+                  if (nch > 1)
+                  {
+                     const uint8_t *st1 = wait_full();
+                     if (!st1)
+                     {
+                        ok = false;
+                        break;
+                     }
+                     const uint64_t bd1 = ptx::sdesc_k_sw128(ptx::smem_u32(st1));
+                     const uint32_t k1 = (p.dp - kChunkK) / 16u;
+#pragma unroll
+                     for (uint32_t ks = 0; ks < 4; ++ks)
+                        if (ks < k1)
+                           ptx::mma_f16_ts(dt, at + 32u + ks * 8u, bd1 + 2u * ks, idesc, 1u);
+                     release();
+                  }
                }
+               else
+                  for (uint32_t c = 0; c < nch; ++c)
+                  {
+                     int s;
+                     if (A_RES)
+                        s = int((abase + c) % kASlots);
+                     else if ((s = take_slot()) < 0)
+                     {
+                        ok = false;
+                        break;
+                     }
+                     const uint8_t *stage = wait_full();
+                     if (!stage)
+                     {
+                        ok = false;
+                        break;
+                     }
+                     if (!A_RES)
+                     {
+                        ptx::tc_fence_after();
+                        copy_a(stage, uint32_t(s));
+                     }
+                     const uint64_t bd = ptx::sdesc_k_sw128(ptx::smem_u32(stage + (A_RES ? 0u : kAChunk)));
+                     const uint32_t kleft = p.dp - c * kChunkK; // multiple of 16
+                     const uint32_t ksteps = kleft >= kChunkK ? 4u : kleft / 16u;
+                     const uint32_t at = tmem_base + uint32_t(s) * 32u;
+                     for (uint32_t ks = 0; ks < ksteps; ++ks) // K = 16 per MMA (+32 B, +8 TMEM columns)
+                        ptx::mma_f16_ts(dt, at + ks * 8u, bd + 2u * ks, idesc, (c | ks) != 0u);
+                     release();
+                     if (!A_RES)
+                        ptx::mma_commit(&a_free[s]);
+                  }
                if (!ok)
                   break;
                ptx::mma_commit(&acc_full[b]);
-               ++tseq;
             }
-            if (A_RES) // the item's A slots are free once its MMAs complete
+            if (DUAL)
+               ptx::mma_commit(&a_free[m]);
+            else if (A_RES) // the item's A slots are free once its MMAs complete
                for (uint32_t c = 0; c < nch && abase + c < apos; ++c)
                   ptx::mma_commit(&a_free[(abase + c) % kASlots]);
+            ++items;
             if (!ok)
                break;
             ptx::mbar_arrive(&item_empty[slot]);
@@ -866,10 +949,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
          if (!ok)
             raise_abort(abort_word, p.status, UNGX_ERR_TIMEOUT);
          // every MMA / copy issued by this thread (and its arrivals) completes before teardown
-         ptx::mma_commit(done_bar);
-         ptx::mbar_wait(done_bar, 0, nullptr, kDrainWaitNs);
+         ptx::mma_commit(&done_bar[m]);
+         ptx::mbar_wait(&done_bar[m], 0, nullptr, kDrainWaitNs);
       }
       __syncwarp();
+   }
+   else if (warp == kEpiWarps + 2u)
+   {
+      // spare warp (single-issuer modes)
    }
    else
    {
@@ -1199,18 +1286,28 @@ __global__ void __launch_bounds__(256) rerank_kernel(const RerankParams p)
    }
 }
 
-template <int KP, bool A_RES>
+template <int KP, int MODE>
 cudaError_t launch_tc_t(const TcMaps &maps, const TcParams &p, uint32_t grid, cudaStream_t s)
 {
-   const TcLayout L = tc_layout(p.dp, A_RES, KP);
-   if (L.stages < 2)
+   const TcLayout L = tc_layout(p.dp, MODE >= 1, KP);
+   if (L.stages < (MODE == 2 ? 4u : 2u))
       return cudaErrorInvalidValue;
    const size_t smem = L.total + 1024;
-   cudaError_t e = cudaFuncSetAttribute(tc_kernel<KP, A_RES>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+   cudaError_t e = cudaFuncSetAttribute(tc_kernel<KP, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
    if (e != cudaSuccess)
       return e;
-   tc_kernel<KP, A_RES><<<grid, kTcThreads, smem, s>>>(maps, p);
+   tc_kernel<KP, MODE><<<grid, kTcThreads, smem, s>>>(maps, p);
    return cudaGetLastError();
+}
+
+template <int KP>
+cudaError_t launch_tc_kp(const TcMaps &maps, const TcParams &p, uint32_t grid, cudaStream_t s)
+{
+   if (p.dp <= 2u * kChunkK)
+      return launch_tc_t<KP, 2>(maps, p, grid, s);
+   if (tc_a_resident(p.dp))
+      return launch_tc_t<KP, 1>(maps, p, grid, s);
+   return launch_tc_t<KP, 0>(maps, p, grid, s);
 }
 
 template <int KMAX>
@@ -1343,13 +1440,12 @@ cudaError_t launch_exact(const ExactParams &p, uint32_t grid, cudaStream_t s)
 
 cudaError_t launch_tc(const TcMaps &maps, const TcParams &p, uint32_t kp, uint32_t grid, cudaStream_t s)
 {
-   const bool ares = tc_a_resident(p.dp);
    if (kp == 16)
-      return ares ? launch_tc_t<16, true>(maps, p, grid, s) : launch_tc_t<16, false>(maps, p, grid, s);
+      return launch_tc_kp<16>(maps, p, grid, s);
    if (kp == 24)
-      return ares ? launch_tc_t<24, true>(maps, p, grid, s) : launch_tc_t<24, false>(maps, p, grid, s);
+      return launch_tc_kp<24>(maps, p, grid, s);
    if (kp == 32)
-      return ares ? launch_tc_t<32, true>(maps, p, grid, s) : launch_tc_t<32, false>(maps, p, grid, s);
+      return launch_tc_kp<32>(maps, p, grid, s);
    return cudaErrorInvalidValue;
 }
 

@@ -5,6 +5,8 @@
   source-group size are recomputed by the CPU oracle and must match exactly; every
   row satisfies the size-independent properties (sorted, ids from the union of the
   out-groups, min(k, |union|) edges, sentinels last);
+* every operand width class of the tensor-core kernel (two issuers, one issuer,
+  streamed source rows) matches the oracle on every row;
 * the device-pointer entry point equals the host entry point; sharded calls cover
   every row exactly once and reproduce the one-shard result;
 * a pipeline wait that runs out returns UNGX_ERR_TIMEOUT and leaves the context usable.
@@ -118,6 +120,30 @@ def sample_rows(group_ranges, out_offsets, rng, per_bucket=12, max_rows=400):
     for g in no_out[:5]:
         rows.append(int(gr[g, 0]))
     return np.unique(np.array(rows[:max_rows], dtype=np.uint32))
+
+
+@pytest.mark.parametrize("d,dist", [(64, "normal"), (100, "uniform"), (144, "normal"), (200, "uniform"),
+                                    (256, "normal"), (300, "normal")])
+def test_operand_widths_match_oracle(ctx, d, dist):
+    """Every operand layout of the tensor-core kernel against the oracle, all rows: two MMA
+    issuers with resident source rows (padded width <= 128), one issuer with resident
+    source rows (<= 256), source rows streamed per chunk (> 256)."""
+    n, k = 2500, 6
+    off, lab = datasets.make_labels(n, vocab=12, umin=1, umax=3, zipf=1.1, seed=d)
+    X = datasets.make_vectors(n, d, dist, normalize=False, seed=d)
+    lg = nat.LabelGraph(off, lab)
+    Xr = np.ascontiguousarray(X[lg.new_to_old])
+    prob = nat.Problem(n, d, k, lg.group_ranges, lg.out_offsets, lg.out_ids, route=nat.ROUTE_TENSOR)
+    ids = np.empty(n * k, dtype=np.uint32)
+    dists = np.empty(n * k, dtype=np.float32)
+    ctx.prepare_base_vectors(Xr, n, d, on_device=False)
+    t = ctx.generate(prob, ids, dists)
+    ctx.release_base_vectors()
+    group_first = np.concatenate([[0], lg.group_ranges[2::2], [lg.group_ranges[-1]]]).astype(np.uint32)
+    rows = np.arange(n, dtype=np.uint32)
+    o_ids, o_d = O.oracle().cross_rows(Xr, k, group_first, lg.out_offsets, lg.out_ids, rows)
+    assert_rows_match(ids, dists, o_ids.ravel(), o_d.ravel(), k)
+    assert t.rows_fallback <= 0.01 * (t.rows_certified + t.rows_fallback)
 
 
 @pytest.mark.parametrize("cfg,n", [(2, None), (3, 200_000), (4, 1_000_000)])
