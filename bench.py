@@ -33,6 +33,9 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "UNG cross-edge build TFLOP/s (algorithmic 2*d*W / wall), configs[1]"
+# DRAM bytes (read + write) of one tc_kernel launch on the bench workload, from one ncu
+# capture of this build (profiles/tc_kernel_cfg2.txt); other configurations: not captured.
+TC_TRAFFIC_BYTES = {2: 568_865_792 + 269_338_368}
 
 
 def log(*a):
@@ -324,7 +327,7 @@ def run_ours(args, rank, world, local_rank):
             "roofline": {"bound": "tensor", "kernel": "tc_kernel", "achieved": round(achieved, 2),
                          "peak": round(peak, 1), "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
                          "peak_source": peak_source,
-                         "traffic": None},
+                         "traffic": TC_TRAFFIC_BYTES.get(args.config)},
             "cpu_baseline": {"value": round(cpu_rate, 4), "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": kind,
                              "sample": f"{cpu_pairs} of W={W} pairs (stratified source groups), {cpu_dt:.1f} s"},
             "e2e": e2e,
