@@ -81,6 +81,20 @@ class CrossEdgeProblem(ctypes.Structure):
     ]
 
 
+class AdditionalStats(ctypes.Structure):
+    """Layout of ``ungx_additional_stats``."""
+
+    _fields_ = [
+        ("missing_group_edges", c_uint64),
+        ("query_vectors", c_uint64),
+        ("edges", c_uint64),
+        ("ms", c_double),
+    ]
+
+    def as_dict(self) -> dict:
+        return {name: getattr(self, name) for name, _ in self._fields_}
+
+
 # (name, restype, argtypes) of every exported function, in include/ungx.h order.
 _SIGNATURES = [
     ("ungx_context_create", c_int, [c_int, POINTER(c_void_p)]),
@@ -111,6 +125,12 @@ _SIGNATURES = [
     ("ungx_label_graph_num_set_labels", c_uint64, [c_void_p]),
     ("ungx_label_graph_copy_label_sets", c_int, [c_void_p, c_void_p, c_void_p]),
     ("ungx_flat_to_csr", c_int, [c_void_p, c_uint32, c_uint32, c_void_p, c_void_p]),
+    ("ungx_additional_edges_build", c_int,
+     [c_void_p, POINTER(CrossEdgeProblem), c_void_p, c_void_p, POINTER(AdditionalStats)]),
+    ("ungx_additional_edges_copy", c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+    ("ungx_graph_csr_device", c_int,
+     [c_void_p, c_uint32, c_uint32, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_uint64,
+      POINTER(c_uint64), c_void_p]),
 ]
 
 EXPORTED = [name for name, _, _ in _SIGNATURES]
@@ -274,6 +294,33 @@ class Context:
         check(lib.ungx_cross_edges_build(self.h, _ptr(vectors), ctypes.byref(problem.c), _ptr(out_ids),
                                          _ptr(out_dists), ctypes.byref(t)), self.h)
         return t
+
+
+    def additional_edges(self, problem: Problem, d_cross_ids: int, stream: int | None = None) -> AdditionalStats:
+        """ungx_additional_edges_build on a device cross-edge output [n x k]."""
+        st = AdditionalStats()
+        check(lib.ungx_additional_edges_build(self.h, ctypes.byref(problem.c), d_cross_ids, stream,
+                                              ctypes.byref(st)), self.h)
+        return st
+
+    def additional_edges_copy(self, num_points: int, num_edges: int):
+        """(from_ids, to_ids, point_offsets, point_cols) of the last additional-edge build."""
+        src = np.empty(max(num_edges, 1), dtype=np.uint32)
+        dst = np.empty(max(num_edges, 1), dtype=np.uint32)
+        off = np.empty(num_points + 1, dtype=np.uint64)
+        cols = np.empty(max(num_edges, 1), dtype=np.uint32)
+        check(lib.ungx_additional_edges_copy(self.h, _ptr(src), _ptr(dst), _ptr(off), _ptr(cols)), self.h)
+        return src[:num_edges], dst[:num_edges], off, cols[:num_edges]
+
+    def graph_csr_device(self, num_points: int, topk: int, d_intra_offsets: int | None, d_intra_cols: int | None,
+                         d_cross_ids: int | None, with_additional: bool, d_offsets: int, d_cols: int | None,
+                         cols_capacity: int, stream: int | None = None) -> int:
+        """ungx_graph_csr_device; returns the number of columns written."""
+        total = c_uint64(0)
+        check(lib.ungx_graph_csr_device(self.h, num_points, topk, d_intra_offsets, d_intra_cols, d_cross_ids,
+                                        int(with_additional), d_offsets, d_cols, cols_capacity, ctypes.byref(total),
+                                        stream), self.h)
+        return int(total.value)
 
 
 def cross_edges_exact_noalloc(problem: Problem, d_vectors: int, d_ids: int, d_dists: int | None,

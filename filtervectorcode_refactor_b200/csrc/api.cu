@@ -111,6 +111,12 @@ struct ungx_context
    DevBuf stage[2];
    DevBuf copy_ranges, compact; // a shard's rows gathered for one device -> host copy
    PinnedBuf host_stage;
+   // additional edges and graph emission
+   DevBuf g_ranges, g_out_off, g_out_ids, group_of, reach, add_items, add_segs, add_rows, add_row_items, add_pos,
+       add_res, add_off, add_cols, scan_scratch;
+   uint32_t add_n = 0; // points of the last additional-edge build
+   std::vector<uint32_t> add_from, add_to, add_point_cols;
+   std::vector<uint64_t> add_point_off;
    uint32_t *h_counters = nullptr; // pinned
    cudaEvent_t ev[10] = {};
 };
@@ -505,7 +511,9 @@ int ungx_context_destroy(ungx_context *ctx)
    for (DevBuf *b : {&ctx->items, &ctx->segs, &ctx->empties, &ctx->ranges, &ctx->gmax, &ctx->counters,
                      &ctx->fb_rows, &ctx->fb_items, &ctx->rows, &ctx->row_items, &ctx->out_ids, &ctx->out_dists,
                      &ctx->stage[0], &ctx->stage[1], &ctx->cand_key, &ctx->cand_col, &ctx->copy_ranges,
-                     &ctx->compact})
+                     &ctx->compact, &ctx->g_ranges, &ctx->g_out_off, &ctx->g_out_ids, &ctx->group_of, &ctx->reach,
+                     &ctx->add_items, &ctx->add_segs, &ctx->add_rows, &ctx->add_row_items, &ctx->add_pos,
+                     &ctx->add_res, &ctx->add_off, &ctx->add_cols, &ctx->scan_scratch})
       b->release();
    ctx->host_stage.release();
    for (auto &ev : ctx->ev)
@@ -768,6 +776,233 @@ int ungx_cross_edges_build(ungx_context *ctx, const float *vectors, const ungx_c
    if (timing)
       *timing = t;
    return st;
+}
+
+int ungx_additional_edges_build(ungx_context *ctx, const ungx_cross_edge_problem *problem, const uint32_t *d_cross_ids,
+                                void *stream, ungx_additional_stats *stats)
+{
+   if (!ctx || !problem)
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "null argument");
+   if (!ctx->have_vectors)
+      return fail(ctx, UNGX_ERR_STATE, "call ungx_prepare_base_vectors first");
+   const uint32_t n = problem->num_points, k = problem->topk, G = problem->num_groups;
+   if (n != ctx->n || problem->dim != ctx->d)
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "problem n/d differ from the prepared base vectors");
+   if (n && !d_cross_ids)
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "null cross-edge ids");
+   if (k == 0 || k > ungx::kExactMaxK)
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "k must be 1 .. " + std::to_string(ungx::kExactMaxK));
+   if (G && (!problem->group_ranges || !problem->lng_out_offsets))
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "null group ranges or LNG offsets");
+   const auto t0 = std::chrono::steady_clock::now();
+   UNGX_CUDA(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+   const uint32_t *R = problem->group_ranges;
+   const uint64_t *OO = problem->lng_out_offsets;
+   const uint64_t nnz = G ? OO[G + 1] : 0;
+   if (nnz && !problem->lng_out_ids)
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "null LNG out ids");
+   for (uint32_t g = 1; g <= G; ++g)
+      if (R[2 * g] > R[2 * g + 1] || R[2 * g + 1] > n)
+         return fail(ctx, UNGX_ERR_INVALID_ARG, "group range outside 0..num_points");
+   for (uint64_t e = 0; e < nnz; ++e)
+      if (problem->lng_out_ids[e] == 0 || problem->lng_out_ids[e] > G)
+         return fail(ctx, UNGX_ERR_INVALID_ARG, "lng_out_ids holds a group id outside 1..G");
+   // the caller's cross-edge output is complete before this context's stream reads it
+   cudaStream_t us = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+   if (us != ctx->stream)
+   {
+      UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[9], us), "event");
+      UNGX_CUDA(ctx, cudaStreamWaitEvent(ctx->stream, ctx->ev[9], 0), "stream wait");
+   }
+   cudaStream_t s = ctx->stream;
+   // 1. which LNG edges do the cross edges reach
+   std::vector<uint32_t> ranges(2 * size_t(G + 1));
+   if (G)
+      std::memcpy(ranges.data(), R, ranges.size() * sizeof(uint32_t));
+   std::vector<uint64_t> out_off(OO, OO + (G ? G + 2 : 0));
+   std::vector<uint32_t> out_ids(problem->lng_out_ids, problem->lng_out_ids + nnz);
+   int st;
+   if ((st = upload(ctx, ctx->g_ranges, ranges, "group ranges")) ||
+       (st = upload(ctx, ctx->g_out_off, out_off, "LNG upload")) ||
+       (st = upload(ctx, ctx->g_out_ids, out_ids, "LNG upload")))
+      return st;
+   UNGX_CUDA(ctx, ctx->group_of.ensure(size_t(std::max(n, 1u)) * sizeof(uint32_t)), "group map");
+   UNGX_CUDA(ctx, ctx->reach.ensure(std::max<uint64_t>(nnz, 1)), "edge flags");
+   UNGX_CUDA(ctx, cudaMemsetAsync(ctx->reach.p, 0, std::max<uint64_t>(nnz, 1), s), "edge flags");
+   UNGX_CUDA(ctx, ungx::launch_group_of(ctx->g_ranges.as<uint32_t>(), G, n, ctx->group_of.as<uint32_t>(), s),
+             "group map kernel");
+   if (G)
+      UNGX_CUDA(ctx,
+                ungx::launch_mark_reached(d_cross_ids, n, k, ctx->group_of.as<uint32_t>(), G,
+                                          ctx->g_out_off.as<uint64_t>(), ctx->g_out_ids.as<uint32_t>(),
+                                          ctx->reach.as<uint8_t>(), s),
+                "edge marking kernel");
+   std::vector<uint8_t> reached(nnz);
+   if (nnz)
+      UNGX_CUDA(ctx, cudaMemcpyAsync(reached.data(), ctx->reach.p, nnz, cudaMemcpyDeviceToHost, s), "edge flags");
+   UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[6], s), "event");
+   if ((st = wait_event(ctx, ctx->ev[6], "edge marking")))
+      return st;
+   // 2. the reference's loop over missing edges, as a list of (vector, target) queries:
+   //    each vector of f adds m = min(|f'|, k/2) edges, until k were added (|f| caps it)
+   const uint32_t kh = k / 2;
+   std::vector<ungx::WorkItem> items;
+   std::vector<ungx::Segment> segs;
+   std::vector<uint32_t> rows, row_items, pos;
+   ungx_additional_stats sx{};
+   for (uint32_t f = 1; f <= G; ++f)
+   {
+      const uint32_t qf = R[2 * f], qs = R[2 * f + 1];
+      for (uint64_t e = OO[f]; e < OO[f + 1]; ++e)
+      {
+         if (reached[e])
+            continue;
+         const uint32_t t = out_ids[e];
+         const uint32_t tsize = R[2 * t + 1] - R[2 * t];
+         ++sx.missing_group_edges;
+         const uint32_t m = std::min(tsize, kh);
+         if (m == 0)
+         {
+            sx.query_vectors += qs - qf; // the reference's loop scans every vector, adding nothing
+            continue;
+         }
+         const uint32_t q = std::min<uint32_t>(qs - qf, (k + m - 1) / m);
+         sx.query_vectors += q;
+         const uint32_t item = (uint32_t)items.size();
+         items.push_back({qf, q, (uint32_t)segs.size(), 1u});
+         segs.push_back({R[2 * t], tsize, t, 0u});
+         for (uint32_t i = 0; i < q; ++i)
+         {
+            rows.push_back(qf + i);
+            row_items.push_back(item);
+            pos.push_back((uint32_t)pos.size());
+         }
+      }
+   }
+   // 3. exact top-(k/2) of every query, in the reference's distance and order
+   const uint32_t nq = (uint32_t)rows.size();
+   std::vector<uint32_t> res(size_t(nq) * std::max(kh, 1u));
+   if (nq)
+   {
+      if ((st = upload(ctx, ctx->add_items, items, "query plan")) || (st = upload(ctx, ctx->add_segs, segs, "query plan")) ||
+          (st = upload(ctx, ctx->add_rows, rows, "query plan")) ||
+          (st = upload(ctx, ctx->add_row_items, row_items, "query plan")) ||
+          (st = upload(ctx, ctx->add_pos, pos, "query plan")))
+         return st;
+      UNGX_CUDA(ctx, ctx->add_res.ensure(res.size() * sizeof(uint32_t)), "query results");
+      ungx::ExactParams ep{};
+      ep.items = ctx->add_items.as<ungx::WorkItem>();
+      ep.segs = ctx->add_segs.as<ungx::Segment>();
+      ep.X = ctx->X;
+      ep.d = ctx->d;
+      ep.k = kh;
+      ep.rows = ctx->add_rows.as<uint32_t>();
+      ep.row_items = ctx->add_row_items.as<uint32_t>();
+      ep.count_host = nq;
+      ep.out_ids = ctx->add_res.as<uint32_t>();
+      ep.out_pos = ctx->add_pos.as<uint32_t>();
+      UNGX_CUDA(ctx, ungx::launch_exact(ep, std::min<uint32_t>(nq, (uint32_t)ctx->num_sms * 8), s),
+                "additional-edge kernel");
+      UNGX_CUDA(ctx, cudaMemcpyAsync(res.data(), ctx->add_res.p, res.size() * sizeof(uint32_t),
+                                     cudaMemcpyDeviceToHost, s),
+                "query results");
+      UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[6], s), "event");
+      if ((st = wait_event(ctx, ctx->ev[6], "additional edges")))
+         return st;
+   }
+   // 4. (from, to) in the reference's order, and the same edges per point
+   ctx->add_from.clear();
+   ctx->add_to.clear();
+   for (uint32_t i = 0; i < nq; ++i)
+      for (uint32_t r = 0; r < kh; ++r)
+      {
+         const uint32_t id = res[size_t(i) * kh + r];
+         if (id == 0xFFFFFFFFu)
+            break;
+         ctx->add_from.push_back(rows[i]);
+         ctx->add_to.push_back(id);
+      }
+   ctx->add_n = n;
+   ctx->add_point_off.assign(size_t(n) + 1, 0);
+   for (uint32_t v : ctx->add_from)
+      ++ctx->add_point_off[size_t(v) + 1];
+   for (uint32_t v = 0; v < n; ++v)
+      ctx->add_point_off[size_t(v) + 1] += ctx->add_point_off[v];
+   ctx->add_point_cols.resize(ctx->add_from.size());
+   {
+      std::vector<uint64_t> fill(ctx->add_point_off.begin(), ctx->add_point_off.end() - 1);
+      for (size_t i = 0; i < ctx->add_from.size(); ++i)
+         ctx->add_point_cols[fill[ctx->add_from[i]]++] = ctx->add_to[i];
+   }
+   if ((st = upload(ctx, ctx->add_off, ctx->add_point_off, "additional-edge CSR")) ||
+       (st = upload(ctx, ctx->add_cols, ctx->add_point_cols, "additional-edge CSR")))
+      return st;
+   UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[6], s), "event");
+   if ((st = wait_event(ctx, ctx->ev[6], "additional-edge CSR")))
+      return st;
+   sx.edges = ctx->add_from.size();
+   sx.ms = ms_since(t0);
+   if (stats)
+      *stats = sx;
+   return UNGX_OK;
+}
+
+int ungx_additional_edges_copy(const ungx_context *ctx, uint32_t *from_ids, uint32_t *to_ids, uint64_t *point_offsets,
+                               uint32_t *point_cols)
+{
+   if (!ctx)
+      return UNGX_ERR_INVALID_ARG;
+   const size_t m = ctx->add_from.size();
+   if (from_ids && m)
+      std::memcpy(from_ids, ctx->add_from.data(), m * sizeof(uint32_t));
+   if (to_ids && m)
+      std::memcpy(to_ids, ctx->add_to.data(), m * sizeof(uint32_t));
+   if (point_offsets && !ctx->add_point_off.empty())
+      std::memcpy(point_offsets, ctx->add_point_off.data(), ctx->add_point_off.size() * sizeof(uint64_t));
+   if (point_cols && m)
+      std::memcpy(point_cols, ctx->add_point_cols.data(), m * sizeof(uint32_t));
+   return UNGX_OK;
+}
+
+int ungx_graph_csr_device(ungx_context *ctx, uint32_t num_points, uint32_t topk, const uint64_t *d_intra_offsets,
+                          const uint32_t *d_intra_cols, const uint32_t *d_cross_ids, int with_additional,
+                          uint64_t *d_offsets, uint32_t *d_cols, uint64_t cols_capacity, uint64_t *num_cols,
+                          void *stream)
+{
+   if (!ctx || !d_offsets || !num_cols)
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "null argument");
+   if (d_intra_offsets && !d_intra_cols)
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "intra offsets without columns");
+   if (d_cross_ids && topk == 0)
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "cross edges with topk = 0");
+   if (with_additional && ctx->add_n != num_points)
+      return fail(ctx, UNGX_ERR_STATE, "no additional edges built for this num_points");
+   UNGX_CUDA(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+   cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+   const uint64_t *add_off = with_additional ? ctx->add_off.as<uint64_t>() : nullptr;
+   const uint32_t *add_cols = with_additional ? ctx->add_cols.as<uint32_t>() : nullptr;
+   UNGX_CUDA(ctx, ctx->scan_scratch.ensure(ungx::csr_scan_scratch_bytes(num_points)), "scan scratch");
+   UNGX_CUDA(ctx, ungx::launch_graph_degrees(num_points, topk, d_intra_offsets, d_cross_ids, add_off, d_offsets, s),
+             "degree kernel");
+   UNGX_CUDA(ctx, ungx::launch_exclusive_scan_u64(d_offsets, num_points + 1, ctx->scan_scratch.p, s), "scan kernels");
+   uint64_t total = 0;
+   UNGX_CUDA(ctx, cudaMemcpyAsync(ctx->h_counters, d_offsets + num_points, sizeof(uint64_t), cudaMemcpyDeviceToHost, s),
+             "total");
+   UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[6], s), "event");
+   int st;
+   if ((st = wait_event(ctx, ctx->ev[6], "graph degrees")))
+      return st;
+   std::memcpy(&total, ctx->h_counters, sizeof(uint64_t));
+   *num_cols = total;
+   if (total > cols_capacity || (total && !d_cols))
+      return fail(ctx, UNGX_ERR_INVALID_ARG,
+                  "graph needs " + std::to_string(total) + " columns, capacity " + std::to_string(cols_capacity));
+   UNGX_CUDA(ctx,
+             ungx::launch_graph_fill(num_points, topk, d_intra_offsets, d_intra_cols, d_cross_ids, add_off, add_cols,
+                                     d_offsets, d_cols, s),
+             "fill kernel");
+   UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[6], s), "event");
+   return wait_event(ctx, ctx->ev[6], "graph emission");
 }
 
 } // extern "C"

@@ -506,13 +506,14 @@ __global__ void __launch_bounds__(256) exact_rows_kernel(const ExactParams p)
          for (uint32_t wv = 0; wv < 8; ++wv)
             for (uint32_t o = 0; o < p.k && s_i[wv][o] != 0xFFFFFFFFu; ++o)
                insert_pair<KMAX>(bd, bi, s_d[wv][o], s_i[wv][o]);
+         const size_t slot = p.out_pos ? size_t(p.out_pos[w]) : size_t(row);
 #pragma unroll
          for (int i = 0; i < KMAX; ++i)
             if (uint32_t(i) < p.k)
             {
-               p.out_ids[size_t(row) * p.k + i] = bi[i];
+               p.out_ids[slot * p.k + i] = bi[i];
                if (p.out_dists)
-                  p.out_dists[size_t(row) * p.k + i] = bd[i];
+                  p.out_dists[slot * p.k + i] = bd[i];
             }
       }
       __syncthreads();

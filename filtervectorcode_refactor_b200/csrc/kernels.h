@@ -86,6 +86,7 @@ struct ExactParams
    uint32_t count_host;       // number of rows when count_dev is NULL
    uint32_t *out_ids;
    float *out_dists;
+   const uint32_t *out_pos;   // output row of each listed row, or NULL for the row itself
 };
 
 // Largest k the tensor-core route supports (candidate list of 32 per row).
@@ -122,6 +123,25 @@ struct CopyRange
 cudaError_t launch_gather_rows(const CopyRange *ranges, uint32_t nranges, uint32_t k, const uint32_t *ids,
                                const float *dists, uint32_t *out_ids, float *out_dists, cudaStream_t s);
 cudaError_t launch_exact(const ExactParams &p, uint32_t grid_hint, cudaStream_t s);
+
+// ---- graph assembly (graph.cu)
+// group_of[v] = group of row v (1..G), G + 1 for rows outside every group.
+cudaError_t launch_group_of(const uint32_t *ranges, uint32_t G, uint32_t n, uint32_t *group_of, cudaStream_t s);
+// flags[e] = 1 for every LNG edge f -> g (e in f's out list) that some row of f
+// reaches through its cross edges; flags zeroed by the caller.
+cudaError_t launch_mark_reached(const uint32_t *cross_ids, uint32_t n, uint32_t k, const uint32_t *group_of,
+                                uint32_t G, const uint64_t *out_offsets, const uint32_t *out_ids, uint8_t *flags,
+                                cudaStream_t s);
+// Per point: intra-group edges (optional CSR), then its cross edges up to the first
+// sentinel, then its additional edges (optional CSR): degree, exclusive scan into
+// offsets[n + 1], then the columns.  scratch: >= csr_scan_scratch_bytes(n) bytes.
+size_t csr_scan_scratch_bytes(uint32_t n);
+cudaError_t launch_graph_degrees(uint32_t n, uint32_t k, const uint64_t *intra_off, const uint32_t *cross_ids,
+                                 const uint64_t *add_off, uint64_t *offsets, cudaStream_t s);
+cudaError_t launch_exclusive_scan_u64(uint64_t *data, uint32_t count, void *scratch, cudaStream_t s);
+cudaError_t launch_graph_fill(uint32_t n, uint32_t k, const uint64_t *intra_off, const uint32_t *intra_cols,
+                              const uint32_t *cross_ids, const uint64_t *add_off, const uint32_t *add_cols,
+                              const uint64_t *offsets, uint32_t *cols, cudaStream_t s);
 cudaError_t launch_tc(const TcMaps &maps, const TcParams &p, uint32_t kp, uint32_t grid, cudaStream_t s);
 cudaError_t launch_rerank(const RerankParams &p, uint32_t kp, uint32_t num_items, cudaStream_t s);
 

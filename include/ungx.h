@@ -218,6 +218,51 @@ int ungx_label_graph_copy_label_sets(const ungx_label_graph *lg, uint64_t *offse
 int ungx_flat_to_csr(const uint32_t *flat_ids, uint32_t num_points, uint32_t topk, uint64_t *row_offsets,
                      uint32_t *col_indices);
 
+/* ------------------------------------------- additional edges (exact variant)
+ * Replaces UniNavGraph::build_cross_edges_generate_additional with
+ * UngAdditionalEdgesImpl::CpuExactScan (UNG/codes/src/uni_nav_graph_cross_edges.cpp:442-596).
+ * From a finished cross-edge output `d_cross_ids` (device, [n x k], UINT32_MAX = empty):
+ * every LNG edge f -> f' that no cross edge of f's vectors reaches gets, from f's
+ * vectors in ascending order, the first k/2 entries of each vector's exact top-k over
+ * f' (reference distance, (distance, id) order) until k edges were added for that f'.
+ * Uses the base vectors of ungx_prepare_base_vectors.  The edges stay in the context
+ * (copy them with ungx_additional_edges_copy, or emit them with ungx_graph_csr_device). */
+typedef struct ungx_additional_stats
+{
+   uint64_t missing_group_edges; /* LNG edges no cross edge realises */
+   uint64_t query_vectors;       /* source vectors scanned for them (the reference's count) */
+   uint64_t edges;               /* additional edges */
+   double ms;                    /* wall time of the call */
+} ungx_additional_stats;
+
+int ungx_additional_edges_build(ungx_context *ctx, const ungx_cross_edge_problem *problem, const uint32_t *d_cross_ids,
+                                void *stream, ungx_additional_stats *stats);
+
+/* The last build's edges, host buffers, any of them NULL to skip:
+ *   from_ids / to_ids [edges]: (from, to) pairs in the reference's materialised order
+ *     (source group ascending; per group its LNG out-groups in order, vectors
+ *     ascending, queue rank), the list append_materialized_additional_edges
+ *     (UNG/codes/src/ung_cross_edge_output_writer.cpp:30-42) appends;
+ *   point_offsets [n+1] / point_cols [edges]: the same edges per source point. */
+int ungx_additional_edges_copy(const ungx_context *ctx, uint32_t *from_ids, uint32_t *to_ids, uint64_t *point_offsets,
+                               uint32_t *point_cols);
+
+/* ------------------------------------------- device emission of the whole graph
+ * No single reference counterpart: the per-point adjacency the reference assembles on
+ * the host (intra-group edges offset to global ids, UNG/codes/src/uni_nav_graph.cpp:285-297;
+ * then cross edges in queue order and additional edges,
+ * UNG/codes/src/ung_cross_edge_output_writer.cpp:17-42), emitted as CSR in device memory
+ * for NeighborList64 / CSR consumers (UNG/include/graph.h:18-250).
+ * Inputs, all device pointers, NULL to leave a part out: d_intra_offsets [n+1] +
+ * d_intra_cols (global ids); d_cross_ids [n x k]; with_additional != 0 appends the
+ * context's last additional edges.  Outputs: d_offsets [n+1]; d_cols with room for
+ * cols_capacity ids.  *num_cols receives the total; when it exceeds cols_capacity the
+ * call returns UNGX_ERR_INVALID_ARG and writes no column. */
+int ungx_graph_csr_device(ungx_context *ctx, uint32_t num_points, uint32_t topk, const uint64_t *d_intra_offsets,
+                          const uint32_t *d_intra_cols, const uint32_t *d_cross_ids, int with_additional,
+                          uint64_t *d_offsets, uint32_t *d_cols, uint64_t cols_capacity, uint64_t *num_cols,
+                          void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -67,6 +67,23 @@ class _Lib:
                     out_offsets=off, out_ids=ids[:nnz])
 
 
+    def _additional(self, fn, X, k, group_first, out_offsets, out_ids, cross_ids, *extra):
+        X = np.ascontiguousarray(X, dtype=np.float32)
+        n, d = X.shape
+        G = group_first.shape[0] - 2
+        gf = np.ascontiguousarray(group_first, dtype=np.uint32)
+        oo = np.ascontiguousarray(out_offsets, dtype=np.uint64)
+        oi = np.ascontiguousarray(out_ids, dtype=np.uint32)
+        if oi.size == 0:
+            oi = np.zeros(1, dtype=np.uint32)
+        ci = np.ascontiguousarray(cross_ids, dtype=np.uint32).reshape(-1)
+        count = fn(_p(X), n, d, k, G, _p(gf), _p(oo), _p(oi), _p(ci), *extra, 0, None, None)
+        src = np.empty(max(count, 1), dtype=np.uint32)
+        dst = np.empty(max(count, 1), dtype=np.uint32)
+        fn(_p(X), n, d, k, G, _p(gf), _p(oo), _p(oi), _p(ci), *extra, count, _p(src), _p(dst))
+        return src[:count], dst[:count]
+
+
 class Oracle(_Lib):
     """The plain-C restatement."""
 
@@ -81,6 +98,14 @@ class Oracle(_Lib):
         L.orc_cross_exact.restype = c_uint64
         L.orc_cross_exact.argtypes = [c_void_p, c_uint32, c_uint32, c_uint32, c_uint32, c_void_p, c_void_p,
                                       c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]
+        L.orc_additional_edges.restype = c_uint64
+        L.orc_additional_edges.argtypes = [c_void_p, c_uint32, c_uint32, c_uint32, c_uint32, c_void_p, c_void_p,
+                                           c_void_p, c_void_p, c_int, c_uint64, c_void_p, c_void_p]
+
+    def additional_edges(self, X, k, group_first, out_offsets, out_ids, cross_ids, fused: int = L2_REFERENCE_BUILD):
+        """(from, to) additional edges in the reference's materialised order."""
+        return self._additional(self.lib.orc_additional_edges, X, k, group_first, out_offsets, out_ids, cross_ids,
+                                fused)
 
     def l2(self, a: np.ndarray, b: np.ndarray, fused: int = L2_REFERENCE_BUILD) -> float:
         a = np.ascontiguousarray(a, dtype=np.float32)
@@ -137,6 +162,13 @@ class Reference(_Lib):
         L.ungref_cross_exact.restype = c_uint64
         L.ungref_cross_exact.argtypes = [c_void_p, c_uint32, c_uint32, c_uint32, c_uint32, c_void_p, c_void_p,
                                          c_void_p, c_void_p, c_int, c_void_p, c_void_p]
+        L.ungref_additional_edges.restype = c_uint64
+        L.ungref_additional_edges.argtypes = [c_void_p, c_uint32, c_uint32, c_uint32, c_uint32, c_void_p,
+                                              c_void_p, c_void_p, c_void_p, c_uint64, c_void_p, c_void_p]
+
+    def additional_edges(self, X, k, group_first, out_offsets, out_ids, cross_ids):
+        """(from, to) additional edges in the reference's materialised order."""
+        return self._additional(self.lib.ungref_additional_edges, X, k, group_first, out_offsets, out_ids, cross_ids)
 
     def l2(self, a: np.ndarray, b: np.ndarray) -> float:
         a = np.ascontiguousarray(a, dtype=np.float32)

@@ -12,6 +12,8 @@
 //              (get_min_super_sets_optimized_bucket + build_label_nav_graph_optimized_phase1)
 //   cross scan UNG/codes/src/uni_nav_graph_cross_edges.cpp:32-57, 154-220
 //              (append_cross_edges_from_target_range + build_cross_edges_generate_cpu_exact_scan)
+//   additional UNG/codes/src/uni_nav_graph_cross_edges.cpp:442-596
+//              (build_cross_edges_generate_additional, exact variant)
 //
 // The reference sources themselves are compiled from where they lie by
 // oracle/Makefile into oracle/_ref/; nothing from them is copied here.
@@ -258,6 +260,73 @@ uint64_t ungref_cross_exact(const float *X, uint32_t n, uint32_t d, uint32_t k, 
       }
    }
    return pairs;
+}
+
+// Additional edges, exact variant (UngAdditionalEdgesImpl::CpuExactScan), restating
+// UniNavGraph::build_cross_edges_generate_additional
+// (UNG/codes/src/uni_nav_graph_cross_edges.cpp:442-596) around the reference's own
+// SearchQueue and FloatL2DistanceHandler.  cross_ids is the flat cross-edge output
+// [n x k] (UINT32_MAX = empty slot).  For every group f, the groups its vectors'
+// cross edges reach are marked; every LNG out-group f' of f that is not marked gets
+// edges from f's vectors in ascending order, each contributing the first k/2 entries
+// of its exact top-k over f', until k edges were added for that f'.  The (from, to)
+// pairs come out in the reference's materialised order (group ascending; per group
+// its out-groups in LNG order, vectors ascending, queue rank).  Returns the pair
+// count; the pairs are written only when the count does not exceed cap.
+uint64_t ungref_additional_edges(const float *X, uint32_t n, uint32_t d, uint32_t k, uint32_t num_groups,
+                                 const uint32_t *group_first, const uint64_t *out_offsets, const uint32_t *out_ids,
+                                 const uint32_t *cross_ids, uint64_t cap, uint32_t *from_ids, uint32_t *to_ids)
+{
+   std::vector<uint32_t> group_of(n, num_groups + 1);
+   for (uint32_t g = 1; g <= num_groups; ++g)
+      for (uint32_t v = group_first[g]; v < group_first[g + 1]; ++v)
+         group_of[v] = g;
+   std::vector<std::pair<uint32_t, uint32_t>> edges;
+   std::vector<uint32_t> connected(size_t(num_groups) + 2, 0);
+   ANNS::FloatL2DistanceHandler dist;
+   uint32_t epoch = 0;
+   for (uint32_t f = 1; f <= num_groups; ++f)
+   {
+      ++epoch;
+      const uint32_t qf = group_first[f], qs = group_first[f + 1];
+      for (uint32_t v = qf; v < qs; ++v)
+         for (uint32_t j = 0; j < k; ++j)
+         {
+            const uint32_t id = cross_ids[size_t(v) * k + j];
+            if (id == std::numeric_limits<uint32_t>::max())
+               continue;
+            const uint32_t g = group_of[id];
+            if (g <= num_groups)
+               connected[g] = epoch;
+         }
+      for (uint64_t e = out_offsets[f]; e < out_offsets[f + 1]; ++e)
+      {
+         const uint32_t t = out_ids[e];
+         if (t <= num_groups && connected[t] == epoch)
+            continue;
+         uint32_t cnt = 0;
+         for (uint32_t v = qf; v < qs && cnt < k; ++v)
+         {
+            ANNS::SearchQueue local;
+            local.reserve(k);
+            const char *q = reinterpret_cast<const char *>(X + size_t(v) * d);
+            for (uint32_t x = group_first[t]; x < group_first[t + 1]; ++x)
+               local.insert(x, dist.compute(q, reinterpret_cast<const char *>(X + size_t(x) * d), d));
+            for (int r = 0; r < local.size() && r < int(k / 2); ++r)
+            {
+               edges.emplace_back(v, local[r].id);
+               ++cnt;
+            }
+         }
+      }
+   }
+   if (edges.size() <= cap)
+      for (size_t i = 0; i < edges.size(); ++i)
+      {
+         from_ids[i] = edges[i].first;
+         to_ids[i] = edges[i].second;
+      }
+   return edges.size();
 }
 
 } // extern "C"

@@ -460,3 +460,67 @@ void orc_cross_rows(const float *X, uint32_t n, uint32_t d, uint32_t k, uint32_t
       free(loc);
    }
 }
+
+/* Additional edges, exact variant: the restatement of
+ * UniNavGraph::build_cross_edges_generate_additional
+ * (UNG/codes/src/uni_nav_graph_cross_edges.cpp:442-596) that ungref_additional_edges
+ * in ref_harness.cpp runs on the reference's own SearchQueue and distance.  Same
+ * contract: (from, to) pairs in the reference's materialised order, count returned,
+ * pairs written only when the count does not exceed cap. */
+uint64_t orc_additional_edges(const float *X, uint32_t n, uint32_t d, uint32_t k, uint32_t num_groups,
+                              const uint32_t *group_first, const uint64_t *out_offsets, const uint32_t *out_ids,
+                              const uint32_t *cross_ids, int fused, uint64_t cap, uint32_t *from_ids,
+                              uint32_t *to_ids)
+{
+   uint32_t *group_of = (uint32_t *)malloc((n ? n : 1) * sizeof(uint32_t));
+   for (uint32_t v = 0; v < n; ++v)
+      group_of[v] = num_groups + 1;
+   for (uint32_t g = 1; g <= num_groups; ++g)
+      for (uint32_t v = group_first[g]; v < group_first[g + 1]; ++v)
+         group_of[v] = g;
+   uint32_t *connected = (uint32_t *)calloc((size_t)num_groups + 2, sizeof(uint32_t));
+   orc_cand *loc = (orc_cand *)malloc(((size_t)k + 1) * sizeof(orc_cand));
+   uint64_t count = 0;
+   uint32_t epoch = 0;
+   for (uint32_t f = 1; f <= num_groups; ++f)
+   {
+      ++epoch;
+      const uint32_t qf = group_first[f], qs = group_first[f + 1];
+      for (uint32_t v = qf; v < qs; ++v)
+         for (uint32_t j = 0; j < k; ++j)
+         {
+            const uint32_t id = cross_ids[(size_t)v * k + j];
+            if (id == 0xffffffffu)
+               continue;
+            if (group_of[id] <= num_groups)
+               connected[group_of[id]] = epoch;
+         }
+      for (uint64_t e = out_offsets[f]; e < out_offsets[f + 1]; ++e)
+      {
+         const uint32_t t = out_ids[e];
+         if (t <= num_groups && connected[t] == epoch)
+            continue;
+         uint32_t cnt = 0;
+         for (uint32_t v = qf; v < qs && cnt < k; ++v)
+         {
+            int32_t ls = 0;
+            for (uint32_t x = group_first[t]; x < group_first[t + 1]; ++x)
+               orc_queue_insert(loc, &ls, (int32_t)k, x, orc_l2(X + (size_t)v * d, X + (size_t)x * d, d, fused));
+            for (int32_t r = 0; r < ls && r < (int32_t)(k / 2); ++r)
+            {
+               if (count < cap)
+               {
+                  from_ids[count] = v;
+                  to_ids[count] = loc[r].id;
+               }
+               ++count;
+               ++cnt;
+            }
+         }
+      }
+   }
+   free(loc);
+   free(connected);
+   free(group_of);
+   return count;
+}

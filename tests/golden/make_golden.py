@@ -11,8 +11,9 @@ that has the reference sources:
 
 Each fixture stores how to regenerate its inputs (seeded generator parameters, or the
 small input arrays themselves), a digest of the inputs, and the reference's outputs:
-group order, reorder map, LNG out-neighbour sets, and the cross-edge ids and
-distances of every vector.
+group order, reorder map, LNG out-neighbour sets, the cross-edge ids and distances of
+every vector, and the additional edges (build_cross_edges_generate_additional, exact
+variant) as (from, to) pairs in the reference's order.
 """
 from __future__ import annotations
 
@@ -76,11 +77,13 @@ def make_one(ref, name, X, off, lab, k, extra):
     lg = ref.label_graph(off, lab)
     Xr = X[lg["new_to_old"]]
     ids, dists, pairs = ref.cross_exact(Xr, k, lg["group_first"], lg["out_offsets"], lg["out_ids"])
+    add_from, add_to = ref.additional_edges(Xr, k, lg["group_first"], lg["out_offsets"], lg["out_ids"], ids)
     np.savez_compressed(
         os.path.join(HERE, name + ".npz"), k=k, input_digest=digest(X, off, lab), new_to_old=lg["new_to_old"],
         group_first=lg["group_first"], out_offsets=lg["out_offsets"], out_ids=lg["out_ids"], ids=ids,
-        dists=dists, pairs=pairs, **extra)
-    print(name, "n", X.shape[0], "d", X.shape[1], "G", lg["num_groups"], "E", len(lg["out_ids"]), "pairs", pairs)
+        dists=dists, pairs=pairs, add_from=add_from, add_to=add_to, **extra)
+    print(name, "n", X.shape[0], "d", X.shape[1], "G", lg["num_groups"], "E", len(lg["out_ids"]), "pairs", pairs,
+          "additional", add_from.size)
 
 
 def main():

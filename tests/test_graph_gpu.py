@@ -1,0 +1,105 @@
+"""Additional edges and device-side graph emission, through the C ABI.
+
+* ungx_additional_edges_build on the device cross-edge output reproduces the
+  reference's additional edges (exact variant of build_cross_edges_generate_additional,
+  golden fixtures made by the reference's compiled code): the (from, to) list in the
+  reference's order, and the same edges per point;
+* ungx_graph_csr_device emits, per point, intra-group edges, then cross edges in queue
+  order, then additional edges, equal to the same adjacency assembled on the host;
+* a column buffer that is too small is refused without writing.
+"""
+import numpy as np
+import pytest
+
+from filtervectorcode_refactor_b200 import _native as nat
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    c = nat.Context(0)
+    yield c
+    c.close()
+
+
+def cross_on_device(ctx, g):
+    n, d = g["Xr"].shape
+    k = g["k"]
+    route = nat.ROUTE_TENSOR if k <= 24 else nat.ROUTE_EXACT
+    prob = nat.Problem(n, d, k, g["group_ranges"], g["out_offsets"], g["out_ids"], route=route)
+    ctx.prepare_base_vectors(g["Xr"], n, d, on_device=False)
+    d_ids = torch.empty((n, k), dtype=torch.int32, device="cuda")
+    d_dists = torch.empty((n, k), dtype=torch.float32, device="cuda")
+    ctx.generate_device(prob, d_ids.data_ptr(), d_dists.data_ptr())
+    torch.cuda.synchronize()
+    return prob, d_ids
+
+
+def test_additional_edges_match_golden(ctx, golden):
+    prob, d_ids = cross_on_device(ctx, golden)
+    n = golden["Xr"].shape[0]
+    assert np.array_equal(d_ids.cpu().numpy().view(np.uint32).ravel(), golden["ids"])
+    st = ctx.additional_edges(prob, d_ids.data_ptr())
+    src, dst, off, cols = ctx.additional_edges_copy(n, int(st.edges))
+    ctx.release_base_vectors()
+    assert np.array_equal(src, golden["add_from"])
+    assert np.array_equal(dst, golden["add_to"])
+    # per point: the same edges, in list order
+    exp_off = np.zeros(n + 1, dtype=np.uint64)
+    np.add.at(exp_off, golden["add_from"].astype(np.int64) + 1, 1)
+    exp_off = np.cumsum(exp_off).astype(np.uint64)
+    assert np.array_equal(off, exp_off)
+    order = np.argsort(golden["add_from"], kind="stable")
+    assert np.array_equal(cols, golden["add_to"][order])
+    assert st.edges == golden["add_from"].size
+    assert st.missing_group_edges >= (1 if st.edges else 0)
+
+
+def test_graph_csr_device_matches_host_assembly(ctx, golden):
+    prob, d_ids = cross_on_device(ctx, golden)
+    n = golden["Xr"].shape[0]
+    k = golden["k"]
+    st = ctx.additional_edges(prob, d_ids.data_ptr())
+    _, _, add_off, add_cols = ctx.additional_edges_copy(n, int(st.edges))
+    ctx.release_base_vectors()
+    rng = np.random.default_rng(n)
+    deg = rng.integers(0, 6, size=n)
+    intra_off = np.zeros(n + 1, dtype=np.uint64)
+    intra_off[1:] = np.cumsum(deg)
+    intra_cols = rng.integers(0, n, size=int(intra_off[-1])).astype(np.uint32)
+    ids = golden["ids"].reshape(n, k)
+    expected = []
+    for v in range(n):
+        row = list(intra_cols[intra_off[v]:intra_off[v + 1]])
+        row += [x for x in ids[v] if x != 0xFFFFFFFF]
+        row += list(add_cols[add_off[v]:add_off[v + 1]])
+        expected.append(row)
+    exp_off = np.zeros(n + 1, dtype=np.uint64)
+    exp_off[1:] = np.cumsum([len(r) for r in expected])
+    exp_cols = np.array([x for r in expected for x in r], dtype=np.uint32)
+
+    d_intra_off = torch.from_numpy(intra_off.view(np.int64)).cuda()
+    d_intra_cols = torch.from_numpy(intra_cols.view(np.int32) if intra_cols.size else np.zeros(1, np.int32)).cuda()
+    d_off = torch.empty(n + 1, dtype=torch.int64, device="cuda")
+    cap = int(exp_off[-1])
+    d_cols = torch.empty(max(cap, 1), dtype=torch.int32, device="cuda")
+    # too small a column buffer is refused
+    if cap:
+        with pytest.raises(nat.UngxError):
+            ctx.graph_csr_device(n, k, d_intra_off.data_ptr(), d_intra_cols.data_ptr(), d_ids.data_ptr(), True,
+                                 d_off.data_ptr(), d_cols.data_ptr(), cap - 1)
+    total = ctx.graph_csr_device(n, k, d_intra_off.data_ptr(), d_intra_cols.data_ptr(), d_ids.data_ptr(), True,
+                                 d_off.data_ptr(), d_cols.data_ptr(), cap)
+    assert total == cap
+    assert np.array_equal(d_off.cpu().numpy().view(np.uint64), exp_off)
+    assert np.array_equal(d_cols.cpu().numpy().view(np.uint32)[:cap], exp_cols)
+    # cross edges alone: the CSR of build_csr_adjacency
+    total2 = ctx.graph_csr_device(n, k, None, None, d_ids.data_ptr(), False, d_off.data_ptr(), d_cols.data_ptr(),
+                                  cap)
+    h_off, h_cols = nat.flat_to_csr(golden["ids"], n, k)
+    assert total2 == int(h_off[-1])
+    assert np.array_equal(d_off.cpu().numpy().view(np.uint64), h_off)
+    assert np.array_equal(d_cols.cpu().numpy().view(np.uint32)[:total2], h_cols)

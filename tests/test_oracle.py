@@ -46,6 +46,24 @@ def test_reference_harness_reproduces_golden(golden):
     assert np.array_equal(ids, golden["ids"])
 
 
+def test_oracle_additional_edges_match_golden(golden):
+    """Additional edges (the exact variant of build_cross_edges_generate_additional):
+    the C restatement reproduces the reference harness's (from, to) list in order."""
+    src, dst = O.oracle().additional_edges(golden["Xr"], golden["k"], golden["group_first"], golden["out_offsets"],
+                                           golden["out_ids"], golden["ids"])
+    assert np.array_equal(src, golden["add_from"])
+    assert np.array_equal(dst, golden["add_to"])
+
+
+def test_reference_harness_reproduces_golden_additional_edges(golden):
+    ref = O.reference()
+    if ref is None:
+        pytest.skip("reference build (oracle/_ref) not present on this machine")
+    src, dst = ref.additional_edges(golden["Xr"], golden["k"], golden["group_first"], golden["out_offsets"],
+                                    golden["out_ids"], golden["ids"])
+    assert np.array_equal(src, golden["add_from"]) and np.array_equal(dst, golden["add_to"])
+
+
 def test_planted_mistake_is_caught(golden):
     """A mistake planted in the oracle's output (on the CPU) must fail the comparison
     the GPU tests use."""
