@@ -95,6 +95,20 @@ class AdditionalStats(ctypes.Structure):
         return {name: getattr(self, name) for name, _ in self._fields_}
 
 
+class ExactKnnConfig(ctypes.Structure):
+    """Layout of ``ungx_exact_knn_config``."""
+
+    _fields_ = [
+        ("candidate_k", c_uint32),
+        ("final_degree", c_uint32),
+        ("head_keep", c_uint32),
+        ("anchor_tail", c_uint32),
+        ("anchor_slots", c_uint32),
+        ("bidir_anchor", c_uint32),
+        ("graph_stride", c_uint32),
+    ]
+
+
 # (name, restype, argtypes) of every exported function, in include/ungx.h order.
 _SIGNATURES = [
     ("ungx_context_create", c_int, [c_int, POINTER(c_void_p)]),
@@ -131,6 +145,9 @@ _SIGNATURES = [
     ("ungx_graph_csr_device", c_int,
      [c_void_p, c_uint32, c_uint32, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_uint64,
       POINTER(c_uint64), c_void_p]),
+    ("ungx_exact_knn_default_config", None, [c_uint32, c_uint32, POINTER(ExactKnnConfig)]),
+    ("ungx_exact_knn_graph_device", c_int,
+     [c_void_p, c_uint32, c_void_p, POINTER(ExactKnnConfig), c_void_p, c_void_p, c_void_p, POINTER(c_double)]),
 ]
 
 EXPORTED = [name for name, _, _ in _SIGNATURES]
@@ -312,6 +329,15 @@ class Context:
         check(lib.ungx_additional_edges_copy(self.h, _ptr(src), _ptr(dst), _ptr(off), _ptr(cols)), self.h)
         return src[:num_edges], dst[:num_edges], off, cols[:num_edges]
 
+    def exact_knn_graph_device(self, group_ranges: np.ndarray, cfg: ExactKnnConfig, d_graph: int,
+                               d_entry_points: int | None = None, stream: int | None = None) -> float:
+        """ungx_exact_knn_graph_device; group_ranges is [2 * groups] (first, end); returns kernel ms."""
+        r = np.ascontiguousarray(group_ranges, dtype=np.uint32)
+        ms = c_double(0.0)
+        check(lib.ungx_exact_knn_graph_device(self.h, r.size // 2, _ptr(r) if r.size else None, ctypes.byref(cfg),
+                                              d_graph, d_entry_points, stream, ctypes.byref(ms)), self.h)
+        return ms.value
+
     def graph_csr_device(self, num_points: int, topk: int, d_intra_offsets: int | None, d_intra_cols: int | None,
                          d_cross_ids: int | None, with_additional: bool, d_offsets: int, d_cols: int | None,
                          cols_capacity: int, stream: int | None = None) -> int:
@@ -321,6 +347,12 @@ class Context:
                                         int(with_additional), d_offsets, d_cols, cols_capacity, ctypes.byref(total),
                                         stream), self.h)
         return int(total.value)
+
+
+def exact_knn_default_config(candidate_k: int, final_degree: int) -> ExactKnnConfig:
+    cfg = ExactKnnConfig()
+    lib.ungx_exact_knn_default_config(candidate_k, final_degree, ctypes.byref(cfg))
+    return cfg
 
 
 def cross_edges_exact_noalloc(problem: Problem, d_vectors: int, d_ids: int, d_dists: int | None,

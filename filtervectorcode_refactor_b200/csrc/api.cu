@@ -113,7 +113,7 @@ struct ungx_context
    PinnedBuf host_stage;
    // additional edges and graph emission
    DevBuf g_ranges, g_out_off, g_out_ids, group_of, reach, add_items, add_segs, add_rows, add_row_items, add_pos,
-       add_res, add_off, add_cols, scan_scratch;
+       add_res, add_off, add_cols, scan_scratch, knn_ranges, knn_base, knn_tasks;
    uint32_t add_n = 0; // points of the last additional-edge build
    std::vector<uint32_t> add_from, add_to, add_point_cols;
    std::vector<uint64_t> add_point_off;
@@ -513,7 +513,8 @@ int ungx_context_destroy(ungx_context *ctx)
                      &ctx->stage[0], &ctx->stage[1], &ctx->cand_key, &ctx->cand_col, &ctx->copy_ranges,
                      &ctx->compact, &ctx->g_ranges, &ctx->g_out_off, &ctx->g_out_ids, &ctx->group_of, &ctx->reach,
                      &ctx->add_items, &ctx->add_segs, &ctx->add_rows, &ctx->add_row_items, &ctx->add_pos,
-                     &ctx->add_res, &ctx->add_off, &ctx->add_cols, &ctx->scan_scratch})
+                     &ctx->add_res, &ctx->add_off, &ctx->add_cols, &ctx->scan_scratch, &ctx->knn_ranges,
+                     &ctx->knn_base, &ctx->knn_tasks})
       b->release();
    ctx->host_stage.release();
    for (auto &ev : ctx->ev)
@@ -1003,6 +1004,90 @@ int ungx_graph_csr_device(ungx_context *ctx, uint32_t num_points, uint32_t topk,
              "fill kernel");
    UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[6], s), "event");
    return wait_event(ctx, ctx->ev[6], "graph emission");
+}
+
+void ungx_exact_knn_default_config(uint32_t candidate_k, uint32_t final_degree, ungx_exact_knn_config *cfg)
+{
+   if (!cfg)
+      return;
+   ungx_exact_knn_config c{};
+   c.candidate_k = candidate_k <= final_degree ? final_degree + 1 : candidate_k;
+   c.final_degree = final_degree;
+   c.head_keep = final_degree > 8 ? final_degree - 8 : final_degree;
+   c.anchor_tail = 1;
+   c.anchor_slots = 0;
+   c.bidir_anchor = 0;
+   c.graph_stride = final_degree + 1;
+   *cfg = c;
+}
+
+int ungx_exact_knn_graph_device(ungx_context *ctx, uint32_t num_groups, const uint32_t *group_ranges,
+                                const ungx_exact_knn_config *cfg, uint32_t *d_graph, uint32_t *d_entry_points,
+                                void *stream, double *kernel_ms)
+{
+   if (!ctx || !cfg || (num_groups && (!group_ranges || !d_graph)))
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "null argument");
+   if (!ctx->have_vectors)
+      return fail(ctx, UNGX_ERR_STATE, "call ungx_prepare_base_vectors first");
+   if (ctx->d > ungx::kKnnMaxDim)
+      return fail(ctx, UNGX_ERR_INVALID_ARG,
+                  "exact kNN seeding supports dim <= " + std::to_string(ungx::kKnnMaxDim));
+   if (cfg->graph_stride < cfg->final_degree + 1)
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "graph_stride must be at least final_degree + 1");
+   std::vector<uint32_t> ranges(group_ranges, group_ranges + 2 * size_t(num_groups));
+   std::vector<uint64_t> base(num_groups);
+   uint64_t rows = 0;
+   for (uint32_t g = 0; g < num_groups; ++g)
+   {
+      if (ranges[2 * g] > ranges[2 * g + 1] || ranges[2 * g + 1] > ctx->n)
+         return fail(ctx, UNGX_ERR_INVALID_ARG, "group range outside the base vectors");
+      base[g] = rows;
+      rows += ranges[2 * g + 1] - ranges[2 * g];
+   }
+   UNGX_CUDA(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+   if (num_groups == 0)
+      return UNGX_OK;
+   const size_t ntask = ungx::knn_task_count(ranges.data(), num_groups);
+   std::vector<uint32_t> tasks(2 * std::max<size_t>(ntask, 1));
+   ungx::knn_tasks(ranges.data(), num_groups, tasks.data());
+   int st;
+   if ((st = upload(ctx, ctx->knn_ranges, ranges, "kNN upload")) || (st = upload(ctx, ctx->knn_base, base, "kNN upload")) ||
+       (st = upload(ctx, ctx->knn_tasks, tasks, "kNN upload")))
+      return st;
+   cudaStream_t us = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+   cudaStream_t s = ctx->stream;
+   if (us != s)
+   {
+      UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[9], us), "event");
+      UNGX_CUDA(ctx, cudaStreamWaitEvent(s, ctx->ev[9], 0), "stream wait");
+   }
+   ungx::KnnParams kp{};
+   kp.X = ctx->X;
+   kp.d = ctx->d;
+   kp.dpad = (ctx->d + 3) / 4 * 4;
+   kp.ranges = ctx->knn_ranges.as<uint32_t>();
+   kp.base = ctx->knn_base.as<uint64_t>();
+   kp.candidate_k = cfg->candidate_k;
+   kp.final_degree = cfg->final_degree;
+   kp.head_keep = cfg->head_keep;
+   kp.anchor_tail = cfg->anchor_tail;
+   kp.anchor_slots = cfg->anchor_slots;
+   kp.bidir_anchor = cfg->bidir_anchor;
+   kp.graph_stride = cfg->graph_stride;
+   kp.graph = d_graph;
+   kp.entry_points = d_entry_points;
+   UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[0], s), "event");
+   UNGX_CUDA(ctx, ungx::launch_exact_knn(kp, ctx->knn_tasks.as<uint32_t>(), (uint32_t)ntask, s), "kNN kernel launch");
+   UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[1], s), "event");
+   if ((st = wait_event(ctx, ctx->ev[1], "exact kNN seeding")))
+      return st;
+   if (kernel_ms)
+   {
+      float ms = 0;
+      cudaEventElapsedTime(&ms, ctx->ev[0], ctx->ev[1]);
+      *kernel_ms = ms;
+   }
+   return UNGX_OK;
 }
 
 } // extern "C"

@@ -124,6 +124,23 @@ cudaError_t launch_gather_rows(const CopyRange *ranges, uint32_t nranges, uint32
                                const float *dists, uint32_t *out_ids, float *out_dists, cudaStream_t s);
 cudaError_t launch_exact(const ExactParams &p, uint32_t grid_hint, cudaStream_t s);
 
+// ---- exact kNN graph seeding (knn.cu)
+struct KnnParams
+{
+   const float *X;             // base vectors [* x d]
+   uint32_t d, dpad;           // dpad = d rounded up to 4
+   const uint32_t *ranges;     // [2 * groups]: rows [first, end) of each group
+   const uint64_t *base;       // [groups]: output row of each group's first point
+   uint32_t candidate_k, final_degree, head_keep, anchor_tail, anchor_slots, bidir_anchor, graph_stride;
+   uint32_t *graph;            // [points x graph_stride]
+   uint32_t *entry_points;     // [groups] or NULL
+};
+constexpr uint32_t kKnnMaxDim = 352; // both 64-row tiles hold every dimension in shared memory
+size_t knn_smem_bytes(uint32_t d);
+size_t knn_task_count(const uint32_t *ranges, uint32_t num_groups);
+void knn_tasks(const uint32_t *ranges, uint32_t num_groups, uint32_t *tasks); // [2 * count]: (group, first row)
+cudaError_t launch_exact_knn(const KnnParams &p, const uint32_t *d_tasks, uint32_t num_tasks, cudaStream_t s);
+
 // ---- graph assembly (graph.cu)
 // group_of[v] = group of row v (1..G), G + 1 for rows outside every group.
 cudaError_t launch_group_of(const uint32_t *ranges, uint32_t G, uint32_t n, uint32_t *group_of, cudaStream_t s);

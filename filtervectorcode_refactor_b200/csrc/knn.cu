@@ -1,0 +1,314 @@
+// Large-group intra-graph exact kNN seeding on the device (sm_100a): the role of
+// batched_exact_knn_graph_kernel (UNG/codes/src/tagore_graph_builder.cu:650-795) with
+// the host defaults of make_fast_exact_batch_config
+// (UNG/codes/src/tagore_cuda_config.cpp:23-45).
+//
+// Every point of a group keeps its cand_degree = min(64, K - 1, n - 1) nearest other
+// points of the group, then writes one row [degree, local ids...] in the head / ring
+// anchor / tail layout.  The distance is the reference's: built with --use_fast_math
+// (UNG/codes/src/CMakeLists.txt:79-80), a 128-thread block sums per-thread partials
+// acc = fma(diff, diff, acc) over dims t, t+128, ... by a __shfl_down tree inside each
+// warp and (w0 + w2) + (w1 + w3) across the warps; every add, sub and fma flushes
+// subnormals (.ftz).  A warp's shuffle tree is a balanced binary tree whose in-order
+// leaves are the lanes in 5-bit bit-reversed order, so it is evaluated here as a
+// recursive tree over those leaves, for a 4 x 2 block of (row, candidate) pairs per
+// thread at once (register tiling; each shared-memory load feeds two to four pairs).
+//
+// Layout of a block (256 threads): 64 source rows x 32 candidates per step, both tiles
+// transposed in shared memory ([dim][64]); distances of the step go to a shared tile,
+// then one thread per row inserts them in ascending candidate order into the row's
+// sorted list (strict <, the reference's tie rule), kept in shared memory.
+#include <algorithm>
+#include <cfloat>
+
+#include "kernels.h"
+
+namespace ungx
+{
+namespace
+{
+constexpr int kKnnRows = 64;     // source rows per block
+constexpr int kKnnCands = 32;    // candidates per step
+constexpr int kKnnThreads = 256; // 16 x 16 threads, 4 x 2 pairs each
+constexpr int kKnnMax = 64;      // longest candidate list
+constexpr int kLd = kKnnCands + 1;     // distance tile row stride
+constexpr int kLl = kKnnMax + 1;       // list row stride
+
+__device__ __forceinline__ float add_ftz(float a, float b)
+{
+   float r;
+   asm("add.ftz.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+   return r;
+}
+__device__ __forceinline__ float sub_ftz(float a, float b)
+{
+   float r;
+   asm("sub.ftz.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+   return r;
+}
+__device__ __forceinline__ float fma_ftz(float a, float b, float c)
+{
+   float r;
+   asm("fma.rn.ftz.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+   return r;
+}
+
+__host__ __device__ constexpr int bitrev5(int k)
+{
+   return ((k & 1) << 4) | ((k & 2) << 2) | (k & 4) | ((k & 8) >> 2) | ((k & 16) >> 4);
+}
+
+// Partial of thread t of the reference's block for the 4 x 2 pairs: fma chain over
+// dims t, t + 128, ... (zero when t >= d).
+__device__ __forceinline__ void leaf(float (&out)[8], const float *sq, const float *sx, int t, uint32_t d, int r0,
+                                     int c0)
+{
+#pragma unroll
+   for (int i = 0; i < 8; ++i)
+      out[i] = 0.0f;
+   for (uint32_t dim = t; dim < d; dim += 128)
+   {
+      const float4 q = *reinterpret_cast<const float4 *>(sq + dim * kKnnRows + r0);
+      const float2 x = *reinterpret_cast<const float2 *>(sx + dim * kKnnCands + c0);
+      const float qa[4] = {q.x, q.y, q.z, q.w}, xa[2] = {x.x, x.y};
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+         for (int b = 0; b < 2; ++b)
+         {
+            const float diff = sub_ftz(qa[a], xa[b]);
+            out[a * 2 + b] = fma_ftz(diff, diff, out[a * 2 + b]);
+         }
+   }
+}
+
+// The shuffle tree of warp J over in-order leaves [LO, LO + SIZE).
+template <int J, int LO, int SIZE>
+__device__ __forceinline__ void warp_tree(float (&out)[8], const float *sq, const float *sx, uint32_t d, int r0,
+                                          int c0)
+{
+   if constexpr (SIZE == 1)
+      leaf(out, sq, sx, 32 * J + bitrev5(LO), d, r0, c0);
+   else
+   {
+      float l[8], r[8];
+      warp_tree<J, LO, SIZE / 2>(l, sq, sx, d, r0, c0);
+      warp_tree<J, LO + SIZE / 2, SIZE / 2>(r, sq, sx, d, r0, c0);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+         out[i] = add_ftz(l[i], r[i]);
+   }
+}
+
+struct KnnTask
+{
+   uint32_t group, row0;
+};
+
+__global__ void __launch_bounds__(kKnnThreads) exact_knn_kernel(const KnnParams p, const KnnTask *__restrict__ tasks)
+{
+   extern __shared__ float smem_f[];
+   float *sq = smem_f;                            // [d][64] source rows
+   float *sx = sq + size_t(p.dpad) * kKnnRows;    // [d][64] candidates
+   float *sd = sx + size_t(p.dpad) * kKnnCands;   // [64][33] distances of the step
+   float *ld = sd + kKnnRows * kLd;               // [64][65] list distances
+   uint32_t *li = reinterpret_cast<uint32_t *>(ld + kKnnRows * kLl); // [64][65] list ids
+
+   const KnnTask task = tasks[blockIdx.x];
+   const uint32_t first = p.ranges[2 * task.group], n = p.ranges[2 * task.group + 1] - first;
+   const uint32_t tid = threadIdx.x;
+   uint32_t cand = p.candidate_k > 0 ? p.candidate_k - 1 : 0;
+   cand = min(cand, uint32_t(kKnnMax));
+   cand = min(cand, n > 0 ? n - 1 : 0u);
+   if (task.row0 == 0 && tid == 0 && p.entry_points)
+      p.entry_points[task.group] = 0;
+
+   // source rows, transposed; rows past the group read as zero
+   for (uint32_t idx = tid; idx < uint32_t(kKnnRows) * p.dpad; idx += kKnnThreads)
+   {
+      const uint32_t r = idx % kKnnRows, dim = idx / kKnnRows;
+      const uint32_t row = task.row0 + r;
+      sq[dim * kKnnRows + r] = (row < n && dim < p.d) ? p.X[size_t(first + row) * p.d + dim] : 0.0f;
+   }
+   for (uint32_t idx = tid; idx < uint32_t(kKnnRows) * kLl; idx += kKnnThreads)
+   {
+      ld[idx] = FLT_MAX;
+      li[idx] = 0xFFFFFFFFu;
+   }
+   const int tr = int(tid / 16u), tc = int(tid % 16u);
+   const int r0 = tr * 4, c0 = tc * 2;
+   for (uint32_t x0 = 0; x0 < n; x0 += kKnnCands)
+   {
+      __syncthreads(); // previous step's candidate tile and distances are consumed
+      for (uint32_t idx = tid; idx < uint32_t(kKnnCands) * p.dpad; idx += kKnnThreads)
+      {
+         const uint32_t c = idx % kKnnCands, dim = idx / kKnnCands;
+         const uint32_t x = x0 + c;
+         sx[dim * kKnnCands + c] = (x < n && dim < p.d) ? p.X[size_t(first + x) * p.d + dim] : 0.0f;
+      }
+      __syncthreads();
+      float s02[8], s13[8], w[8];
+      warp_tree<0, 0, 32>(s02, sq, sx, p.d, r0, c0);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+         s13[i] = 0.0f;
+      if (p.d > 32)
+         warp_tree<1, 0, 32>(s13, sq, sx, p.d, r0, c0);
+      if (p.d > 64)
+      {
+         warp_tree<2, 0, 32>(w, sq, sx, p.d, r0, c0);
+#pragma unroll
+         for (int i = 0; i < 8; ++i)
+            s02[i] = add_ftz(s02[i], w[i]);
+      }
+      if (p.d > 96)
+      {
+         warp_tree<3, 0, 32>(w, sq, sx, p.d, r0, c0);
+#pragma unroll
+         for (int i = 0; i < 8; ++i)
+            s13[i] = add_ftz(s13[i], w[i]);
+      }
+      // a skipped warp total is +0, and every partial is +0 or normal: adding it changes nothing
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+         for (int b = 0; b < 2; ++b)
+            sd[(r0 + a) * kLd + c0 + b] = add_ftz(s02[a * 2 + b], s13[a * 2 + b]);
+      __syncthreads();
+      // one thread per row: the step's candidates in ascending order, the reference's insert
+      if (tid < uint32_t(kKnnRows) && task.row0 + tid < n && cand > 0)
+      {
+         const uint32_t self = task.row0 + tid;
+         float *rd = ld + tid * kLl;
+         uint32_t *ri = li + tid * kLl;
+         const uint32_t cend = min(uint32_t(kKnnCands), n - x0);
+         for (uint32_t c = 0; c < cend; ++c)
+         {
+            const uint32_t x = x0 + c;
+            if (x == self)
+               continue;
+            const float dist = sd[tid * kLd + c];
+            if (!(dist < rd[cand - 1]))
+               continue;
+            uint32_t pos = cand;
+            while (pos > 0 && dist < rd[pos - 1])
+            {
+               if (pos < cand)
+               {
+                  rd[pos] = rd[pos - 1];
+                  ri[pos] = ri[pos - 1];
+               }
+               --pos;
+            }
+            rd[pos] = dist;
+            ri[pos] = x;
+         }
+      }
+   }
+   __syncthreads();
+   // the row layout: head, ring anchors, tail, padding with the point itself
+   if (tid < uint32_t(kKnnRows) && task.row0 + tid < n)
+   {
+      const uint32_t s = task.row0 + tid;
+      const uint32_t *top = li + tid * kLl;
+      uint32_t *row = p.graph + size_t(p.base[task.group] + s) * p.graph_stride;
+      const uint32_t out_degree = min(p.final_degree, cand);
+      row[0] = out_degree;
+      uint32_t write = 0;
+      if (out_degree > 0)
+      {
+         const uint32_t near_limit = min(out_degree, min(p.head_keep, p.final_degree));
+         for (; write < near_limit; ++write)
+            row[1 + write] = top[write];
+         const uint32_t remaining = p.final_degree > write ? p.final_degree - write : 0;
+         const uint32_t anchor_limit =
+             p.anchor_tail ? (p.anchor_slots == 0 ? remaining : min(p.anchor_slots, remaining)) : 0;
+         if (anchor_limit > 0 && n > 1)
+            for (uint32_t t = 0; t < anchor_limit && write < out_degree; ++t)
+            {
+               const uint32_t hop = max(1u, uint32_t((uint64_t(t + 1) * n) / (anchor_limit + 1)));
+               const bool backward = p.bidir_anchor && (t & 1u);
+               uint32_t c = backward ? (s + n - (hop % n)) % n : (s + hop) % n;
+               for (uint32_t retry = 0; retry < n && write < out_degree;
+                    ++retry, c = backward ? (c + n - 1) % n : (c + 1) % n)
+               {
+                  if (c == s)
+                     continue;
+                  bool dup = false;
+                  for (uint32_t q = 0; q < write; ++q)
+                     if (row[1 + q] == c)
+                     {
+                        dup = true;
+                        break;
+                     }
+                  if (!dup)
+                  {
+                     row[1 + write++] = c;
+                     break;
+                  }
+               }
+            }
+         const uint32_t tail_start = near_limit;
+         const uint32_t tail_count = cand > tail_start ? cand - tail_start : 0;
+         const uint32_t step = tail_count > remaining && remaining > 0 ? (tail_count + remaining - 1) / remaining : 1;
+         for (uint32_t sc = tail_start; sc < cand && write < out_degree; sc += step)
+            row[1 + write++] = top[sc];
+         for (uint32_t sc = tail_start; sc < cand && write < out_degree; ++sc)
+         {
+            const uint32_t c = top[sc];
+            bool dup = false;
+            for (uint32_t q = 0; q < write; ++q)
+               if (row[1 + q] == c)
+               {
+                  dup = true;
+                  break;
+               }
+            if (!dup)
+               row[1 + write++] = c;
+         }
+      }
+      for (uint32_t j = out_degree; j + 1 < p.graph_stride; ++j)
+         row[1 + j] = s;
+   }
+}
+} // namespace
+
+size_t knn_smem_bytes(uint32_t d)
+{
+   const uint32_t dpad = (d + 3) / 4 * 4;
+   return (size_t(dpad) * (kKnnRows + kKnnCands) + kKnnRows * kLd + 2 * kKnnRows * kLl) * sizeof(float);
+}
+
+size_t knn_task_count(const uint32_t *ranges, uint32_t num_groups)
+{
+   size_t t = 0;
+   for (uint32_t g = 0; g < num_groups; ++g)
+      t += (ranges[2 * g + 1] - ranges[2 * g] + kKnnRows - 1) / kKnnRows;
+   return t;
+}
+
+void knn_tasks(const uint32_t *ranges, uint32_t num_groups, uint32_t *tasks)
+{
+   size_t i = 0;
+   for (uint32_t g = 0; g < num_groups; ++g)
+      for (uint32_t r = 0; r < ranges[2 * g + 1] - ranges[2 * g]; r += kKnnRows)
+      {
+         tasks[2 * i] = g;
+         tasks[2 * i + 1] = r;
+         ++i;
+      }
+}
+
+cudaError_t launch_exact_knn(const KnnParams &p, const uint32_t *d_tasks, uint32_t num_tasks, cudaStream_t s)
+{
+   if (num_tasks == 0)
+      return cudaSuccess;
+   const size_t smem = knn_smem_bytes(p.d);
+   cudaError_t e = cudaFuncSetAttribute(exact_knn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+   if (e != cudaSuccess)
+      return e;
+   exact_knn_kernel<<<num_tasks, kKnnThreads, smem, s>>>(p, reinterpret_cast<const KnnTask *>(d_tasks));
+   return cudaGetLastError();
+}
+
+} // namespace ungx

@@ -49,7 +49,7 @@ enum
 enum
 {
    UNGX_ROUTE_AUTO = 0,        /* tensor-core prefilter + exact rerank when k allows, else exact */
-   UNGX_ROUTE_TENSOR = 1,      /* tcgen05 TF32 prefilter + certified exact fp32 rerank */
+   UNGX_ROUTE_TENSOR = 1,      /* tcgen05 fp16 prefilter + certified exact fp32 rerank */
    UNGX_ROUTE_EXACT = 2        /* CUDA-core exact scan in the reference's summation order */
 };
 
@@ -125,8 +125,8 @@ int ungx_set_fault_injection(ungx_context *ctx, uint32_t flags);
  * Replaces gpu_prepare_all_vectors_on_device
  * (UNG/codes/src/gpu_cross_edge_resident_vectors.cuh:10-215): one upload of the
  * reordered n x d fp32 matrix, then the device builds the tensor-core operand
- * (centred, TF32-rounded, zero-padded to a multiple of 32 columns) and the row
- * norms.  `vectors_on_device` != 0 means `vectors` is a device pointer that stays
+ * (centred, scaled by a power of two, rounded to fp16, zero-padded to a multiple of
+ * 16 columns) and the row norms.  `vectors_on_device` != 0 means `vectors` is a device pointer that stays
  * valid until ungx_release_base_vectors (no copy is made of it). */
 int ungx_prepare_base_vectors(ungx_context *ctx, const float *vectors, uint32_t num_points, uint32_t dim,
                               int vectors_on_device);
@@ -262,6 +262,37 @@ int ungx_graph_csr_device(ungx_context *ctx, uint32_t num_points, uint32_t topk,
                           const uint32_t *d_intra_cols, const uint32_t *d_cross_ids, int with_additional,
                           uint64_t *d_offsets, uint32_t *d_cols, uint64_t cols_capacity, uint64_t *num_cols,
                           void *stream);
+
+/* ------------------------------------------- a15: large-group exact kNN seeding
+ * batched_exact_knn_graph_kernel with the defaults of make_fast_exact_batch_config
+ * (UNG/codes/src/tagore_graph_builder.cu:650-795, UNG/codes/src/tagore_cuda_config.cpp:23-45),
+ * the intra-group graph seed of the groups below UNG_FAST_GRNND_BATCH_EXACT_NX.
+ * Each point of a group keeps its min(64, K - 1, n - 1) nearest other points of the
+ * group (the reference's fp32 distance of its 128-thread kernel built with
+ * --use_fast_math, strict-< insertion in ascending local id), then writes one row of
+ * graph_stride uint32: [degree, local ids in head / ring-anchor / tail order, padding
+ * with its own local id]. */
+typedef struct ungx_exact_knn_config
+{
+   uint32_t candidate_k;  /* K (UNG_TAGORE_K, 64); raised to final_degree + 1 when not above it */
+   uint32_t final_degree; /* degree of a row (the graph's max degree) */
+   uint32_t head_keep;    /* nearest entries kept first */
+   uint32_t anchor_tail;  /* 1: ring anchors fill the remaining slots */
+   uint32_t anchor_slots; /* 0: all remaining slots */
+   uint32_t bidir_anchor; /* 1: every second anchor walks backwards */
+   uint32_t graph_stride; /* row length in uint32, at least final_degree + 1 */
+} ungx_exact_knn_config;
+
+/* The reference's defaults for K and a degree (environment overrides not read). */
+void ungx_exact_knn_default_config(uint32_t candidate_k, uint32_t final_degree, ungx_exact_knn_config *cfg);
+
+/* Groups g = 0 .. num_groups-1 are rows [group_ranges[2g], group_ranges[2g+1]) of the
+ * base vectors of ungx_prepare_base_vectors (any dim up to 352).  d_graph (device):
+ * one row per point, groups in the given order; d_entry_points (device, may be NULL):
+ * 0 per group, as the reference writes.  *kernel_ms (may be NULL): device time. */
+int ungx_exact_knn_graph_device(ungx_context *ctx, uint32_t num_groups, const uint32_t *group_ranges,
+                                const ungx_exact_knn_config *cfg, uint32_t *d_graph, uint32_t *d_entry_points,
+                                void *stream, double *kernel_ms);
 
 #ifdef __cplusplus
 }

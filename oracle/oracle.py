@@ -98,9 +98,34 @@ class Oracle(_Lib):
         L.orc_cross_exact.restype = c_uint64
         L.orc_cross_exact.argtypes = [c_void_p, c_uint32, c_uint32, c_uint32, c_uint32, c_void_p, c_void_p,
                                       c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]
+        L.orc_block_l2.restype = c_float
+        L.orc_block_l2.argtypes = [c_void_p, c_void_p, c_uint32]
+        L.orc_exact_knn_graph.restype = None
+        L.orc_exact_knn_graph.argtypes = [c_void_p, c_uint32, c_uint32, c_void_p, c_uint32, c_uint32, c_uint32,
+                                          c_uint32, c_uint32, c_uint32, c_uint32, c_int, c_void_p, c_void_p]
         L.orc_additional_edges.restype = c_uint64
         L.orc_additional_edges.argtypes = [c_void_p, c_uint32, c_uint32, c_uint32, c_uint32, c_void_p, c_void_p,
                                            c_void_p, c_void_p, c_int, c_uint64, c_void_p, c_void_p]
+
+    def block_l2(self, a: np.ndarray, b: np.ndarray) -> float:
+        """The distance of the reference's 128-thread kNN kernel (fast-math fp32)."""
+        a = np.ascontiguousarray(a, dtype=np.float32)
+        b = np.ascontiguousarray(b, dtype=np.float32)
+        return self.lib.orc_block_l2(_p(a), _p(b), a.shape[0])
+
+    def exact_knn_graph(self, X: np.ndarray, group_ranges: np.ndarray, candidate_k: int, final_degree: int,
+                        head_keep: int, anchor_tail: int, anchor_slots: int, bidir_anchor: int, graph_stride: int,
+                        num_threads: int = 0):
+        """Rows [points x graph_stride] and entry points of the exact kNN seeding restatement."""
+        X = np.ascontiguousarray(X, dtype=np.float32)
+        r = np.ascontiguousarray(group_ranges, dtype=np.uint32)
+        G = r.size // 2
+        pts = int(np.sum(r[1::2].astype(np.int64) - r[0::2]))
+        graph = np.zeros((max(pts, 1), graph_stride), dtype=np.uint32)
+        entry = np.zeros(max(G, 1), dtype=np.uint32)
+        self.lib.orc_exact_knn_graph(_p(X), X.shape[1], G, _p(r), candidate_k, final_degree, head_keep, anchor_tail,
+                                     anchor_slots, bidir_anchor, graph_stride, num_threads, _p(graph), _p(entry))
+        return graph[:pts], entry[:G]
 
     def additional_edges(self, X, k, group_first, out_offsets, out_ids, cross_ids, fused: int = L2_REFERENCE_BUILD):
         """(from, to) additional edges in the reference's materialised order."""

@@ -524,3 +524,187 @@ uint64_t orc_additional_edges(const float *X, uint32_t n, uint32_t d, uint32_t k
    free(group_of);
    return count;
 }
+
+/* ---------------- large-group intra-graph exact kNN seeding ----------------
+ * Restatement of batched_exact_knn_graph_kernel (the default 128-thread block
+ * variant) and of its host defaults, UNG/codes/src/tagore_graph_builder.cu:650-795
+ * and make_fast_exact_batch_config (UNG/codes/src/tagore_cuda_config.cpp:23-45).
+ * PARITY UNPINNED: that source includes the external Tagore_src.cuh, which is not
+ * present, so the reference cannot be built or run here; this restatement was made
+ * by reading the kernel.  The reference is compiled with --use_fast_math
+ * (UNG/codes/src/CMakeLists.txt:79-80): every fp32 add, sub and fma flushes
+ * subnormal inputs and results to zero, and `acc += diff * diff` is one fma.
+ *
+ * Distance of (src, dst): thread t of 128 accumulates acc = fma(diff, diff, acc) over
+ * dims t, t+128, ... ; each warp sums its 32 partials by __shfl_down (offsets 16..1),
+ * then warp 0 sums the four warp totals the same way: (w0 + w2) + (w1 + w3). */
+static inline float ftz(float x) { return fabsf(x) < 1.17549435e-38f ? copysignf(0.0f, x) : x; }
+static inline float add_ftz(float a, float b) { return ftz(ftz(a) + ftz(b)); }
+static inline float sub_ftz(float a, float b) { return ftz(ftz(a) - ftz(b)); }
+static inline float fma_ftz(float a, float b, float c) { return ftz(fmaf(ftz(a), ftz(b), ftz(c))); }
+
+static float warp_tree32(const float *p)
+{
+   float v[32];
+   for (int i = 0; i < 32; ++i)
+      v[i] = p[i];
+   for (int off = 16; off > 0; off >>= 1)
+      for (int i = 0; i < off; ++i)
+         v[i] = add_ftz(v[i], v[i + off]);
+   return v[0];
+}
+
+float orc_block_l2(const float *a, const float *b, uint32_t dim)
+{
+   float part[128];
+   for (uint32_t t = 0; t < 128; ++t)
+   {
+      float acc = 0.0f;
+      for (uint32_t d = t; d < dim; d += 128)
+      {
+         const float diff = sub_ftz(a[d], b[d]);
+         acc = fma_ftz(diff, diff, acc);
+      }
+      part[t] = acc;
+   }
+   const float w0 = warp_tree32(part), w1 = warp_tree32(part + 32), w2 = warp_tree32(part + 64),
+               w3 = warp_tree32(part + 96);
+   return add_ftz(add_ftz(w0, w2), add_ftz(w1, w3));
+}
+
+/* One point's output row (graph_stride uint32: [degree, local ids..., padding]) from
+ * its candidate list top_idx[0 .. cand_degree); the head / anchor / tail layout. */
+static void knn_row_layout(uint32_t *row, const uint32_t *top_idx, uint32_t cand_degree, uint32_t n,
+                           uint32_t local_src, uint32_t final_degree, uint32_t head_keep, uint32_t anchor_tail,
+                           uint32_t anchor_slots, uint32_t bidir_anchor, uint32_t graph_stride)
+{
+   const uint32_t out_degree = final_degree < cand_degree ? final_degree : cand_degree;
+   row[0] = out_degree;
+   if (out_degree > 0)
+   {
+      uint32_t near_limit = head_keep < final_degree ? head_keep : final_degree;
+      if (out_degree < near_limit)
+         near_limit = out_degree;
+      uint32_t write = 0;
+      for (; write < near_limit; ++write)
+         row[1 + write] = top_idx[write];
+      const uint32_t remaining = final_degree > write ? final_degree - write : 0;
+      const uint32_t anchor_limit =
+          anchor_tail ? (anchor_slots == 0 ? remaining : (anchor_slots < remaining ? anchor_slots : remaining)) : 0;
+      if (anchor_limit > 0 && n > 1)
+      {
+         for (uint32_t t = 0; t < anchor_limit && write < out_degree; ++t)
+         {
+            uint32_t hop = (uint32_t)(((uint64_t)(t + 1) * n) / (anchor_limit + 1));
+            if (hop < 1)
+               hop = 1;
+            const int backward = bidir_anchor && (t & 1u);
+            uint32_t cand = backward ? (local_src + n - (hop % n)) % n : (local_src + hop) % n;
+            for (uint32_t retry = 0; retry < n && write < out_degree;
+                 ++retry, cand = backward ? (cand + n - 1) % n : (cand + 1) % n)
+            {
+               if (cand == local_src)
+                  continue;
+               int dup = 0;
+               for (uint32_t p = 0; p < write; ++p)
+                  if (row[1 + p] == cand)
+                  {
+                     dup = 1;
+                     break;
+                  }
+               if (!dup)
+               {
+                  row[1 + write++] = cand;
+                  break;
+               }
+            }
+         }
+      }
+      const uint32_t tail_start = near_limit;
+      const uint32_t tail_count = cand_degree > tail_start ? cand_degree - tail_start : 0;
+      const uint32_t step = tail_count > remaining && remaining > 0 ? (tail_count + remaining - 1) / remaining : 1;
+      for (uint32_t s = tail_start; s < cand_degree && write < out_degree; s += step)
+         row[1 + write++] = top_idx[s];
+      for (uint32_t s = tail_start; s < cand_degree && write < out_degree; ++s)
+      {
+         const uint32_t cand = top_idx[s];
+         int dup = 0;
+         for (uint32_t p = 0; p < write; ++p)
+            if (row[1 + p] == cand)
+            {
+               dup = 1;
+               break;
+            }
+         if (!dup)
+            row[1 + write++] = cand;
+      }
+   }
+   for (uint32_t j = out_degree; j + 1 < graph_stride; ++j)
+      row[1 + j] = local_src;
+}
+
+/* Groups g = 0 .. num_groups-1 are rows [ranges[2g], ranges[2g+1]) of X [* x d];
+ * graph receives one row of graph_stride uint32 per point, groups in order (local ids);
+ * entry_points[g] = 0.  candidate_k is the K of the reference (cand_degree =
+ * min(64, K - 1, n - 1)). */
+void orc_exact_knn_graph(const float *X, uint32_t d, uint32_t num_groups, const uint32_t *ranges,
+                         uint32_t candidate_k, uint32_t final_degree, uint32_t head_keep, uint32_t anchor_tail,
+                         uint32_t anchor_slots, uint32_t bidir_anchor, uint32_t graph_stride, int num_threads,
+                         uint32_t *graph, uint32_t *entry_points)
+{
+   uint64_t *base = (uint64_t *)malloc(((size_t)num_groups + 1) * sizeof(uint64_t));
+   base[0] = 0;
+   for (uint32_t g = 0; g < num_groups; ++g)
+      base[g + 1] = base[g] + (ranges[2 * g + 1] - ranges[2 * g]);
+   if (num_threads > 0)
+      omp_set_num_threads(num_threads);
+   for (uint32_t g = 0; g < num_groups; ++g)
+   {
+      const uint32_t first = ranges[2 * g], n = ranges[2 * g + 1] - ranges[2 * g];
+      if (n == 0)
+         continue; /* no point writes anything (the reference refuses empty groups) */
+      if (entry_points)
+         entry_points[g] = 0;
+      uint32_t cand_degree = candidate_k > 0 ? candidate_k - 1 : 0;
+      if (cand_degree > 64)
+         cand_degree = 64;
+      if (cand_degree > n - 1)
+         cand_degree = n - 1;
+#pragma omp parallel for schedule(dynamic, 16)
+      for (long long s = 0; s < (long long)n; ++s)
+      {
+         uint32_t top_idx[64];
+         float top_dist[64];
+         for (int i = 0; i < 64; ++i)
+         {
+            top_idx[i] = 0xffffffffu;
+            top_dist[i] = 3.402823466e+38f;
+         }
+         const float *src = X + (size_t)(first + s) * d;
+         for (uint32_t x = 0; x < n; ++x)
+         {
+            if (x == (uint32_t)s)
+               continue;
+            const float dist = orc_block_l2(src, X + (size_t)(first + x) * d, d);
+            if (cand_degree > 0 && dist < top_dist[cand_degree - 1])
+            {
+               uint32_t pos = cand_degree;
+               while (pos > 0 && dist < top_dist[pos - 1])
+               {
+                  if (pos < cand_degree)
+                  {
+                     top_dist[pos] = top_dist[pos - 1];
+                     top_idx[pos] = top_idx[pos - 1];
+                  }
+                  --pos;
+               }
+               top_dist[pos] = dist;
+               top_idx[pos] = x;
+            }
+         }
+         knn_row_layout(graph + (size_t)(base[g] + s) * graph_stride, top_idx, cand_degree, n, (uint32_t)s,
+                        final_degree, head_keep, anchor_tail, anchor_slots, bidir_anchor, graph_stride);
+      }
+   }
+   free(base);
+}

@@ -1,0 +1,82 @@
+"""Exact kNN graph seeding on the device (ungx_exact_knn_graph_device) against the
+oracle restatement, bit for bit: every row (degree, local ids in the head / anchor /
+tail layout, padding) and the entry points, over group sizes from 1 to above the
+64-row block, dimensions that are and are not multiples of 4 / 32 / 128, data with
+exact duplicates (ties broken by local id), and several layout configurations."""
+import numpy as np
+import pytest
+
+import oracle as O
+from filtervectorcode_refactor_b200 import _native as nat
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+SIZES = [1, 2, 5, 33, 64, 65, 100, 300, 1100]
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    c = nat.Context(0)
+    yield c
+    c.close()
+
+
+def make_groups(d, seed):
+    rng = np.random.default_rng(seed)
+    n = sum(SIZES) + 7
+    X = rng.standard_normal((n, d)).astype(np.float32)
+    X[200:230] = X[205]                        # duplicates: equal distances, order by id
+    X[::11] = np.round(X[::11] * 2) / 2        # coarse rows: more equal distances
+    ranges, at = [], 3                         # a few leading rows outside every group
+    for s in SIZES:
+        ranges += [at, at + s]
+        at += s
+    return X, np.array(ranges, dtype=np.uint32)
+
+
+CONFIGS = {
+    "default": lambda: nat.exact_knn_default_config(64, 32),
+    "small_k": lambda: _cfg(20, 16, 10, 1, 3, 1, 17),
+    "no_anchor": lambda: _cfg(40, 24, 24, 0, 0, 0, 30),
+    "stride_k": lambda: _cfg(64, 32, 24, 1, 0, 0, 64),
+}
+
+
+def _cfg(k, deg, head, tail, slots, bidir, stride):
+    c = nat.ExactKnnConfig()
+    c.candidate_k, c.final_degree, c.head_keep, c.anchor_tail = k, deg, head, tail
+    c.anchor_slots, c.bidir_anchor, c.graph_stride = slots, bidir, stride
+    return c
+
+
+@pytest.mark.parametrize("d", [13, 96, 128, 200])
+@pytest.mark.parametrize("name", list(CONFIGS))
+def test_exact_knn_graph_matches_oracle(ctx, d, name):
+    X, ranges = make_groups(d, seed=d)
+    cfg = CONFIGS[name]()
+    pts = int(np.sum(ranges[1::2].astype(np.int64) - ranges[0::2]))
+    ctx.prepare_base_vectors(X, X.shape[0], d, on_device=False)
+    d_graph = torch.full((pts, cfg.graph_stride), 7, dtype=torch.int32, device="cuda")
+    d_entry = torch.full((ranges.size // 2,), 9, dtype=torch.int32, device="cuda")
+    ctx.exact_knn_graph_device(ranges, cfg, d_graph.data_ptr(), d_entry.data_ptr())
+    ctx.release_base_vectors()
+    got = d_graph.cpu().numpy().view(np.uint32)
+    exp, exp_entry = O.oracle().exact_knn_graph(X, ranges, cfg.candidate_k, cfg.final_degree, cfg.head_keep,
+                                                cfg.anchor_tail, cfg.anchor_slots, cfg.bidir_anchor,
+                                                cfg.graph_stride)
+    assert np.array_equal(d_entry.cpu().numpy().view(np.uint32), exp_entry)
+    bad = np.nonzero(np.any(got != exp, axis=1))[0]
+    assert bad.size == 0, f"{bad.size} rows differ; first {bad[0]}: got {got[bad[0]].tolist()} " \
+                          f"expected {exp[bad[0]].tolist()}"
+
+
+def test_dimension_limit_is_refused(ctx):
+    X = np.zeros((10, 400), dtype=np.float32)
+    ctx.prepare_base_vectors(X, 10, 400, on_device=False)
+    cfg = nat.exact_knn_default_config(64, 32)
+    d_graph = torch.zeros((10, 33), dtype=torch.int32, device="cuda")
+    with pytest.raises(nat.UngxError):
+        ctx.exact_knn_graph_device(np.array([0, 10], dtype=np.uint32), cfg, d_graph.data_ptr())
+    ctx.release_base_vectors()
