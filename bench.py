@@ -337,6 +337,99 @@ def run_ours(args, rank, world, local_rank):
     ctx.close()
 
 
+def run_graph_stages(args):
+    """--stage graph (one GPU): the path's graph stages after the cross edges, each timed
+    on the device over the configuration's synthetic workload:
+      * exact kNN seeding of the groups in the reference's adaptive exact range
+        (65 .. 4096 points; K = 64, degree 32, make_fast_exact_batch_config defaults);
+      * additional edges (exact variant) from the cross-edge output;
+      * whole-graph CSR emission (kNN rows as intra edges + cross + additional)."""
+    import torch
+    from filtervectorcode_refactor_b200 import _native as nat
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    torch.cuda.set_device(0)
+    c, lg, Xr, W = load_workload(args.config)
+    n, d, k = Xr.shape[0], Xr.shape[1], c["k"]
+    ctx = nat.Context(0)
+    X = torch.from_numpy(Xr).cuda()
+    ctx.prepare_base_vectors(X.data_ptr(), n, d, on_device=True)
+    gr = lg.group_ranges.reshape(-1, 2)[1:].astype(np.int64)
+    sizes = gr[:, 1] - gr[:, 0]
+    sel = np.nonzero((sizes > 64) & (sizes <= 4096))[0]
+    ranges = gr[sel].astype(np.uint32).ravel()
+    pts = int(sizes[sel].sum())
+    pairs = int(np.sum(sizes[sel] * (sizes[sel] - 1)))
+    cfg = nat.exact_knn_default_config(64, 32)
+    d_graph = torch.empty((max(pts, 1), cfg.graph_stride), dtype=torch.int32, device="cuda")
+    for _ in range(args.warmup):
+        ctx.exact_knn_graph_device(ranges, cfg, d_graph.data_ptr())
+    knn_ms = statistics.median(ctx.exact_knn_graph_device(ranges, cfg, d_graph.data_ptr())
+                               for _ in range(max(args.steps, 1)))
+    # CPU: the oracle restatement (the reference's seeding cannot be built) on a group sample
+    rng = np.random.default_rng(0)
+    order = rng.permutation(sel.size)
+    take, acc = [], 0
+    budget = 2e8 * max(args.cpu_seconds, 1.0) / 15.0
+    for i in order:
+        take.append(sel[i])
+        acc += int(sizes[sel[i]] * (sizes[sel[i]] - 1))
+        if acc > budget:
+            break
+    sr = gr[np.sort(np.array(take, dtype=np.int64))].astype(np.uint32).ravel()
+    t0 = time.perf_counter()
+    O.oracle().exact_knn_graph(Xr, sr, 64, 32, 24, 1, 0, 0, 33)
+    cpu_dt = time.perf_counter() - t0
+    # cross edges on the device, then additional edges and the CSR
+    prob = nat.Problem(n, d, k, lg.group_ranges, lg.out_offsets, lg.out_ids, route=nat.ROUTE_AUTO)
+    d_ids = torch.empty((n, k), dtype=torch.int32, device="cuda")
+    d_dists = torch.empty((n, k), dtype=torch.float32, device="cuda")
+    ctx.generate_device(prob, d_ids.data_ptr(), d_dists.data_ptr())
+    torch.cuda.synchronize()
+    add = [ctx.additional_edges(prob, d_ids.data_ptr()) for _ in range(max(args.warmup, 1) + 1)][-1]
+    # intra edges = the kNN rows of the seeded groups (global ids), other points none
+    g = d_graph[:pts].cpu().numpy().view(np.uint32)
+    deg = np.zeros(n, dtype=np.int64)
+    rows = np.concatenate([np.arange(a, b) for a, b in gr[sel]]) if sel.size else np.zeros(0, np.int64)
+    firsts = np.concatenate([np.full(b - a, a) for a, b in gr[sel]]) if sel.size else np.zeros(0, np.int64)
+    deg[rows] = g[:, 0]
+    intra_off = np.zeros(n + 1, dtype=np.uint64)
+    intra_off[1:] = np.cumsum(deg)
+    cols = np.zeros(max(int(intra_off[-1]), 1), dtype=np.uint32)
+    if rows.size:  # rows ascend, so the row-major selection lands in CSR order
+        keep = np.arange(g.shape[1] - 1)[None, :] < g[:, :1].astype(np.int64)
+        cols[:int(intra_off[-1])] = (g[:, 1:].astype(np.int64) + firsts[:, None])[keep].astype(np.uint32)
+    d_io = torch.from_numpy(intra_off.view(np.int64)).cuda()
+    d_ic = torch.from_numpy(cols.view(np.int32)).cuda()
+    cap = int(intra_off[-1]) + n * k + int(add.edges)
+    d_off = torch.empty(n + 1, dtype=torch.int64, device="cuda")
+    d_cols = torch.empty(max(cap, 1), dtype=torch.int32, device="cuda")
+    csr = []
+    for i in range(max(args.warmup, 1) + max(args.steps, 1)):
+        t1 = time.perf_counter()
+        total = ctx.graph_csr_device(n, k, d_io.data_ptr(), d_ic.data_ptr(), d_ids.data_ptr(), True,
+                                     d_off.data_ptr(), d_cols.data_ptr(), cap)
+        csr.append((time.perf_counter() - t1) * 1e3)
+    csr_ms = statistics.median(csr[max(args.warmup, 1):])
+    csr_bytes = (n + 1) * 8 * 2 + n * k * 4 + int(intra_off[-1]) * 4 * 2 + int(add.edges) * 4 * 2 + total * 4
+    line = {
+        "metric": "UNG graph stages after the cross edges (exact kNN seeding, additional edges, CSR emission)",
+        "config": {"workload": c["name"], "n": n, "d": d, "k": k},
+        "knn_seeding": {"groups": int(sel.size), "points": pts, "pairs": pairs, "ms": round(knn_ms, 3),
+                        "tflops_algorithmic": round(2.0 * d * pairs / (knn_ms * 1e-3) / 1e12, 3),
+                        "cpu_baseline": {"kind": "port", "cores": os.cpu_count(),
+                                         "sample_pairs": int(acc), "seconds": round(cpu_dt, 2),
+                                         "tflops": round(2.0 * d * acc / cpu_dt / 1e12, 4)}},
+        "additional_edges": {"missing_group_edges": int(add.missing_group_edges),
+                             "query_vectors": int(add.query_vectors), "edges": int(add.edges),
+                             "ms_wall": round(add.ms, 3)},
+        "csr_emission": {"columns": int(total), "ms_wall": round(csr_ms, 3),
+                         "gbs_algorithmic": round(csr_bytes / (csr_ms * 1e-3) / 1e9, 1)},
+    }
+    print(json.dumps(line), flush=True)
+    ctx.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -346,7 +439,12 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
                     help="CPU work of the cpu_baseline sample (seconds on this host)")
+    ap.add_argument("--stage", default="cross", choices=["cross", "graph"],
+                    help="cross: the cross-edge build (the benchmark line); graph: the later graph stages")
     args = ap.parse_args()
+    if args.stage == "graph":
+        run_graph_stages(args)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

@@ -16,8 +16,11 @@
 //
 // Layout of a block (256 threads): 64 source rows x 32 candidates per step, both tiles
 // transposed in shared memory ([dim][64]); distances of the step go to a shared tile,
-// then one thread per row inserts them in ascending candidate order into the row's
-// sorted list (strict <, the reference's tie rule), kept in shared memory.
+// all threads test them against their row's current last entry, then one thread per
+// row inserts the passing ones in ascending candidate order into the row's sorted list
+// (strict <, the reference's tie rule), kept in shared memory.  The tree code is one
+// 8-leaf subtree body looped over the 16 (warp, subtree) positions: a kernel of a few
+// hundred instructions (a fully unrolled tree missed the instruction cache).
 #include <algorithm>
 #include <cfloat>
 
@@ -53,11 +56,6 @@ __device__ __forceinline__ float fma_ftz(float a, float b, float c)
    return r;
 }
 
-__host__ __device__ constexpr int bitrev5(int k)
-{
-   return ((k & 1) << 4) | ((k & 2) << 2) | (k & 4) | ((k & 8) >> 2) | ((k & 16) >> 4);
-}
-
 // Partial of thread t of the reference's block for the 4 x 2 pairs: fma chain over
 // dims t, t + 128, ... (zero when t >= d).
 __device__ __forceinline__ void leaf(float (&out)[8], const float *sq, const float *sx, int t, uint32_t d, int r0,
@@ -82,22 +80,56 @@ __device__ __forceinline__ void leaf(float (&out)[8], const float *sq, const flo
    }
 }
 
-// The shuffle tree of warp J over in-order leaves [LO, LO + SIZE).
-template <int J, int LO, int SIZE>
-__device__ __forceinline__ void warp_tree(float (&out)[8], const float *sq, const float *sx, uint32_t d, int r0,
-                                          int c0)
+__host__ __device__ constexpr int bitrev3(int k) { return ((k & 1) << 2) | (k & 2) | ((k & 4) >> 2); }
+
+// Balanced tree over the in-order leaves [LO, LO + SIZE) of one 8-leaf subtree whose
+// leaf i sits at dimension offset base + 4 bitrev3(i) (in-order leaf 8 g + i of a warp
+// is lane bitrev5(8 g + i) = 4 bitrev3(i) + bitrev2(g)).
+template <int LO, int SIZE>
+__device__ __forceinline__ void sub_tree(float (&out)[8], const float *sq, const float *sx, int base, uint32_t d,
+                                         int r0, int c0)
 {
    if constexpr (SIZE == 1)
-      leaf(out, sq, sx, 32 * J + bitrev5(LO), d, r0, c0);
+      leaf(out, sq, sx, base + 4 * bitrev3(LO), d, r0, c0);
    else
    {
       float l[8], r[8];
-      warp_tree<J, LO, SIZE / 2>(l, sq, sx, d, r0, c0);
-      warp_tree<J, LO + SIZE / 2, SIZE / 2>(r, sq, sx, d, r0, c0);
+      sub_tree<LO, SIZE / 2>(l, sq, sx, base, d, r0, c0);
+      sub_tree<LO + SIZE / 2, SIZE / 2>(r, sq, sx, base, d, r0, c0);
 #pragma unroll
       for (int i = 0; i < 8; ++i)
          out[i] = add_ftz(l[i], r[i]);
    }
+}
+
+// The shuffle tree of warp j (lanes / dims 32 j ..): ((S0 + S1) + (S2 + S3)) over its
+// four in-order 8-leaf subtrees g, each at dims 32 j + bitrev2(g) + 4 bitrev3(i).  The
+// subtree body is shared by all 16 (warp, subtree) uses: small code.
+__device__ __forceinline__ void warp_tree(float (&out)[8], const float *sq, const float *sx, int j, uint32_t d,
+                                          int r0, int c0)
+{
+   float a[8], b[8];
+#pragma unroll 1
+   for (int g = 0; g < 4; ++g) // a = S0 + S1, b = S2 + S3 (g is uniform: no divergence)
+   {
+      float t[8];
+      sub_tree<0, 8>(t, sq, sx, 32 * j + ((g & 1) << 1 | (g >> 1)), d, r0, c0);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+      {
+         if (g == 0)
+            a[i] = t[i];
+         else if (g == 1)
+            a[i] = add_ftz(a[i], t[i]);
+         else if (g == 2)
+            b[i] = t[i];
+         else
+            b[i] = add_ftz(b[i], t[i]);
+      }
+   }
+#pragma unroll
+   for (int i = 0; i < 8; ++i)
+      out[i] = add_ftz(a[i], b[i]);
 }
 
 struct KnnTask
@@ -137,6 +169,8 @@ __global__ void __launch_bounds__(kKnnThreads) exact_knn_kernel(const KnnParams 
    }
    const int tr = int(tid / 16u), tc = int(tid % 16u);
    const int r0 = tr * 4, c0 = tc * 2;
+   __shared__ __align__(4) uint8_t pass[kKnnThreads]; // per row: 4 bytes = its 32 candidates
+   uint32_t fill = 0;                                // entries in this thread's row list (tid < 64)
    for (uint32_t x0 = 0; x0 < n; x0 += kKnnCands)
    {
       __syncthreads(); // previous step's candidate tile and distances are consumed
@@ -147,26 +181,29 @@ __global__ void __launch_bounds__(kKnnThreads) exact_knn_kernel(const KnnParams 
          sx[dim * kKnnCands + c] = (x < n && dim < p.d) ? p.X[size_t(first + x) * p.d + dim] : 0.0f;
       }
       __syncthreads();
-      float s02[8], s13[8], w[8];
-      warp_tree<0, 0, 32>(s02, sq, sx, p.d, r0, c0);
+      // (w0 + w2) + (w1 + w3); a warp block past d is +0 and is skipped
+      float s02[8], s13[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i)
-         s13[i] = 0.0f;
-      if (p.d > 32)
-         warp_tree<1, 0, 32>(s13, sq, sx, p.d, r0, c0);
-      if (p.d > 64)
+         s02[i] = s13[i] = 0.0f;
+      const int nj = int(min(p.d, 128u) + 31u) / 32;
+#pragma unroll 1
+      for (int j = 0; j < nj; ++j)
       {
-         warp_tree<2, 0, 32>(w, sq, sx, p.d, r0, c0);
+         float w[8];
+         warp_tree(w, sq, sx, j, p.d, r0, c0);
 #pragma unroll
          for (int i = 0; i < 8; ++i)
-            s02[i] = add_ftz(s02[i], w[i]);
-      }
-      if (p.d > 96)
-      {
-         warp_tree<3, 0, 32>(w, sq, sx, p.d, r0, c0);
-#pragma unroll
-         for (int i = 0; i < 8; ++i)
-            s13[i] = add_ftz(s13[i], w[i]);
+         {
+            if (j == 0)
+               s02[i] = w[i];
+            else if (j == 1)
+               s13[i] = w[i];
+            else if (j == 2)
+               s02[i] = add_ftz(s02[i], w[i]);
+            else
+               s13[i] = add_ftz(s13[i], w[i]);
+         }
       }
       // a skipped warp total is +0, and every partial is +0 or normal: adding it changes nothing
 #pragma unroll
@@ -175,22 +212,43 @@ __global__ void __launch_bounds__(kKnnThreads) exact_knn_kernel(const KnnParams 
          for (int b = 0; b < 2; ++b)
             sd[(r0 + a) * kLd + c0 + b] = add_ftz(s02[a * 2 + b], s13[a * 2 + b]);
       __syncthreads();
-      // one thread per row: the step's candidates in ascending order, the reference's insert
+      // all threads: which of the step's candidates beat their row's current last entry
+      // (4 threads per row, 8 candidates each; a looser test than the insert's own)
+      {
+         const uint32_t row = tid >> 2, part = tid & 3u;
+         const uint32_t cend = min(uint32_t(kKnnCands), n - x0);
+         uint32_t m = 0;
+         if (task.row0 + row < n && cand > 0)
+         {
+            const float thr = ld[row * kLl + cand - 1];
+#pragma unroll
+            for (uint32_t i = 0; i < 8; ++i)
+            {
+               const uint32_t c = part * 8u + i;
+               if (c < cend && x0 + c != task.row0 + row && sd[row * kLd + c] < thr)
+                  m |= 1u << i;
+            }
+         }
+         pass[tid] = uint8_t(m);
+      }
+      __syncthreads();
+      // one thread per row: the passing candidates in ascending order, the reference's
+      // insert (started at the list's fill: the empty tail holds FLT_MAX / UINT32_MAX)
       if (tid < uint32_t(kKnnRows) && task.row0 + tid < n && cand > 0)
       {
-         const uint32_t self = task.row0 + tid;
          float *rd = ld + tid * kLl;
          uint32_t *ri = li + tid * kLl;
-         const uint32_t cend = min(uint32_t(kKnnCands), n - x0);
-         for (uint32_t c = 0; c < cend; ++c)
+         uint32_t m = *reinterpret_cast<const uint32_t *>(pass + 4 * tid);
+         while (m)
          {
+            const uint32_t c = __ffs(m) - 1;
+            m &= m - 1u;
             const uint32_t x = x0 + c;
-            if (x == self)
-               continue;
             const float dist = sd[tid * kLd + c];
             if (!(dist < rd[cand - 1]))
                continue;
-            uint32_t pos = cand;
+            uint32_t pos = min(fill, cand);
+            fill = min(fill + 1u, cand);
             while (pos > 0 && dist < rd[pos - 1])
             {
                if (pos < cand)
