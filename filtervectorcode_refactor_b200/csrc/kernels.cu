@@ -1325,11 +1325,13 @@ cudaError_t launch_exact_t(const ExactParams &p, uint32_t grid, cudaStream_t s)
 
 int tc_candidates_for_k(uint32_t k)
 {
-   // the smallest candidate list with at least eight entries of slack past k: with
-   // less slack the certificate rejects a few percent of rows on dense data
+   // 16 entries up to k = 8, else 32: the certificate needs slack past k, more of it
+   // for larger k and high-dimensional data (configuration 3, k = 16, d = 960: with 24
+   // entries 0.47 % of rows fail and their exact rescan costs 3x the prefilter; with 32,
+   // none fail)
    if (k == 0 || k > kTcMaxK)
       return 0;
-   return k + 8 <= 16 ? 16 : k + 8 <= 24 ? 24 : 32;
+   return k <= 8 ? 16 : 32;
 }
 
 uint32_t tc_operand_cols(uint32_t d)
@@ -1443,8 +1445,6 @@ cudaError_t launch_tc(const TcMaps &maps, const TcParams &p, uint32_t kp, uint32
 {
    if (kp == 16)
       return launch_tc_kp<16>(maps, p, grid, s);
-   if (kp == 24)
-      return launch_tc_kp<24>(maps, p, grid, s);
    if (kp == 32)
       return launch_tc_kp<32>(maps, p, grid, s);
    return cudaErrorInvalidValue;
@@ -1456,8 +1456,6 @@ cudaError_t launch_rerank(const RerankParams &p, uint32_t kp, uint32_t num_items
       return cudaSuccess;
    if (kp == 16)
       rerank_kernel<16><<<num_items, 256, 0, s>>>(p);
-   else if (kp == 24)
-      rerank_kernel<24><<<num_items, 256, 0, s>>>(p);
    else if (kp == 32)
       rerank_kernel<32><<<num_items, 256, 0, s>>>(p);
    else

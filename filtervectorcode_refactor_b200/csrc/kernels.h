@@ -94,7 +94,7 @@ constexpr uint32_t kTcMaxK = 24;
 // Largest k the exact route supports (per-lane list of 128).
 constexpr uint32_t kExactMaxK = 128;
 
-int tc_candidates_for_k(uint32_t k);              // 16, 24 or 32; 0 = unsupported
+int tc_candidates_for_k(uint32_t k);              // 16 or 32; 0 = unsupported
 uint32_t tc_operand_cols(uint32_t d);             // dp: d rounded up to 16, at least 64
 bool tc_a_resident(uint32_t dp);                  // A operand kept in TMEM per item
 size_t tc_smem_bytes(uint32_t dp, uint32_t k);
