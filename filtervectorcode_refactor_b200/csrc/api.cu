@@ -92,6 +92,7 @@ double ms_since(std::chrono::steady_clock::time_point t0)
 
 struct ungx_context
 {
+   Plan plan; // the last generate call's plan and the planner's working storage
    int device = 0;
    int num_sms = 148;
    cudaStream_t stream = nullptr;
@@ -300,7 +301,7 @@ int run_generate(ungx_context *ctx, const ungx_cross_edge_problem &p, const Plan
       UNGX_CUDA(ctx, ctx->fb_rows.ensure(sizeof(uint32_t) * std::max<uint64_t>(item_rows, 1)), "fallback list");
       UNGX_CUDA(ctx, ctx->fb_items.ensure(sizeof(uint32_t) * std::max<uint64_t>(item_rows, 1)), "fallback list");
       // candidate lists [row][2][kp], indexed by the global row
-      const size_t cand = size_t(ctx->n) * ungx::kTcLists * uint32_t(kp);
+      const size_t cand = size_t(ctx->n) * ungx::kTcLists * uint32_t(ungx::tc_list_depth(kp));
       UNGX_CUDA(ctx, ctx->cand_key.ensure(cand * sizeof(float)), "candidate buffer");
       UNGX_CUDA(ctx, ctx->cand_col.ensure(cand * sizeof(uint32_t)), "candidate buffer");
       ungx::TcMaps maps;
@@ -635,7 +636,7 @@ int ungx_cross_edges_generate_device(ungx_context *ctx, const ungx_cross_edge_pr
    UNGX_CUDA(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
    const auto t0 = std::chrono::steady_clock::now();
    ungx_cross_edge_timing t{};
-   Plan plan;
+   Plan &plan = ctx->plan; // reused: its buffers keep their capacity across calls
    std::string err;
    int st = ungx::build_plan(*problem, plan, err);
    if (st)
@@ -664,7 +665,7 @@ int ungx_cross_edges_generate(ungx_context *ctx, const ungx_cross_edge_problem *
    UNGX_CUDA(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
    const auto t0 = std::chrono::steady_clock::now();
    ungx_cross_edge_timing t{};
-   Plan plan;
+   Plan &plan = ctx->plan; // reused: its buffers keep their capacity across calls
    std::string err;
    int st = ungx::build_plan(*problem, plan, err);
    if (st)

@@ -58,7 +58,7 @@ struct TcLayout
 // Stages of the ring: A resident (dp <= 256) -> one 24 KB target chunk per stage, the
 // item's source chunks (16 KB) pass through the same ring once per item; A streamed
 // -> 16 KB source + 24 KB target chunk per stage.  As many stages as fit (at most
-// 16), then the epilogue's column table (12 warps x KP slots x 32 lanes), the chunk
+// 16), then the epilogue's column table (12 warps x list-depth slots x 32 lanes), the chunk
 // norms, barriers, and the item slots.
 __host__ __device__ inline TcLayout tc_layout(uint32_t dp, bool a_res, uint32_t kp)
 {
@@ -66,11 +66,12 @@ __host__ __device__ inline TcLayout tc_layout(uint32_t dp, bool a_res, uint32_t 
    TcLayout L;
    L.stage_off = 0;
    L.stage_bytes = a_res ? kBChunk : kAChunk + kBChunk;
-   const uint32_t fixed = kEpiWarps * kp * 32u * 4u + kEpiWarps * 32u * 4u + 48u * 8u + 128u + 1024u;
+   const uint32_t kd = uint32_t(tc_list_depth(int(kp)));
+   const uint32_t fixed = kEpiWarps * kd * 32u * 4u + kEpiWarps * 32u * 4u + 48u * 8u + 128u + 1024u;
    const uint32_t fit = fixed < kSmemLimit ? (kSmemLimit - fixed) / L.stage_bytes : 0u;
    L.stages = fit < kMaxStages ? fit : kMaxStages;
    L.colv_off = L.stage_off + L.stages * L.stage_bytes;
-   L.norm_off = L.colv_off + kEpiWarps * kp * 32u * 4u;
+   L.norm_off = L.colv_off + kEpiWarps * kd * 32u * 4u;
    L.bar_off = L.norm_off + kEpiWarps * 32u * 4u;
    L.misc_off = L.bar_off + 48u * 8u;
    L.total = L.misc_off + 128u;
@@ -986,16 +987,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
          const WorkItem w = item_desc[slot];
          const bool row_ok = r < w.row_count;
          const bool warp_ok = q * 32u < w.row_count;
-         float key[KP]; // ascending packed keys (slot in the low bits)
+         constexpr int KD = tc_list_depth(KP);
+         float key[KD]; // ascending packed keys (slot in the low bits)
          // column of each slot: colv[slot * 32 + lane] (bank = lane, conflict-free)
-         uint32_t *colv = sColv + (warp - 2u) * (KP * 32u) + lane;
+         uint32_t *colv = sColv + (warp - 2u) * (KD * 32u) + lane;
 #pragma unroll
-         for (int i = 0; i < KP; ++i)
+         for (int i = 0; i < KD; ++i)
          {
             key[i] = packed_init(i);
             colv[i * 32] = 0xFFFFFFFFu;
          }
-         float thr = row_ok ? key[KP - 1] : -INFINITY; // rows past the item never take candidates
+         float thr = row_ok ? key[KD - 1] : -INFINITY; // rows past the item never take candidates
          TileIter ti;
          ti.start(p.segs, w.seg_begin, w.seg_count);
          // norms of this warp's two chunks of the current tile; the next tile's are
@@ -1064,15 +1066,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
                {
                   const uint32_t jj = mask ? uint32_t(__clz(mask)) : 0u;
                   const float kk = __fmaf_rn(nis, __uint_as_float(select32(raw, jj)), nrm[jj]);
-                  const uint32_t ev = __float_as_uint(key[KP - 1]) & kSlotMask; // slot that drops out
+                  const uint32_t ev = __float_as_uint(key[KD - 1]) & kSlotMask; // slot that drops out
                   const float v = __uint_as_float((__float_as_uint(kk) & ~kSlotMask) | ev);
-                  const bool ins = mask != 0u && v < key[KP - 1];
+                  const bool ins = mask != 0u && v < key[KD - 1];
                   if (ins)
                      colv[ev * 32u] = cbase + jj;
-                  insert_packed<KP>(key, ins ? v : INFINITY);
+                  insert_packed<KD>(key, ins ? v : INFINITY);
                   mask &= ~(0x80000000u >> jj);
                }
-               thr = row_ok ? key[KP - 1] : -INFINITY;
+               thr = row_ok ? key[KD - 1] : -INFINITY;
             }
             ptx::tc_fence_before();
             __syncwarp();
@@ -1083,10 +1085,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
             break;
          if (row_ok)
          {
-            float4 *kd = reinterpret_cast<float4 *>(p.cand_key + (size_t(w.row_begin + r) * kTcLists + h) * KP);
-            uint4 *cd = reinterpret_cast<uint4 *>(p.cand_col + (size_t(w.row_begin + r) * kTcLists + h) * KP);
+            float4 *kd = reinterpret_cast<float4 *>(p.cand_key + (size_t(w.row_begin + r) * kTcLists + h) * KD);
+            uint4 *cd = reinterpret_cast<uint4 *>(p.cand_col + (size_t(w.row_begin + r) * kTcLists + h) * KD);
 #pragma unroll
-            for (int i = 0; i < KP / 4; ++i)
+            for (int i = 0; i < KD / 4; ++i)
             {
                kd[i] = make_float4(key[4 * i], key[4 * i + 1], key[4 * i + 2], key[4 * i + 3]);
                cd[i] = make_uint4(colv[(__float_as_uint(key[4 * i]) & kSlotMask) * 32u],
@@ -1121,11 +1123,13 @@ template <int KP>
 __global__ void __launch_bounds__(256) rerank_kernel(const RerankParams p)
 {
    constexpr uint32_t TPR = KP <= 16 ? 16u : 32u;
+   constexpr int KD = tc_list_depth(KP); // depth of each of the row's lists
    constexpr uint32_t RPB = 256u / TPR;
    __shared__ uint32_t s_col[RPB][KP];
    __shared__ float s_key[RPB][KP];
    __shared__ float s_d[RPB][KP];
    __shared__ double s_lim[RPB];
+   __shared__ float s_lmin[RPB];
    __shared__ float s_maxn2;
    __shared__ uint32_t s_total;
    __shared__ unsigned long long s_cnt[2];
@@ -1181,19 +1185,25 @@ __global__ void __launch_bounds__(256) rerank_kernel(const RerankParams p)
       {
          float k0[KP];
          uint32_t c0[KP];
-         const float *kp = p.cand_key + size_t(row) * kTcLists * KP;
-         const uint32_t *cp = p.cand_col + size_t(row) * kTcLists * KP;
+         const float *kp = p.cand_key + size_t(row) * kTcLists * KD;
+         const uint32_t *cp = p.cand_col + size_t(row) * kTcLists * KD;
 #pragma unroll
          for (int i = 0; i < KP; ++i)
          {
-            k0[i] = kp[i];
-            c0[i] = cp[i];
+            k0[i] = i < KD ? kp[i] : INFINITY;
+            c0[i] = i < KD ? cp[i] : 0xFFFFFFFFu;
          }
-         // each list is ascending: stop at its first key past the running maximum
+         // each list is ascending: stop at its first key past the running maximum; a
+         // column a list dropped has a key at least that list's last one
+         float lmin = kp[KD - 1];
 #pragma unroll 1
          for (uint32_t l = 1; l < kTcLists; ++l)
-            for (int i = 0; i < KP && kp[l * KP + i] < k0[KP - 1]; ++i)
-               insert_key<KP>(k0, c0, kp[l * KP + i], cp[l * KP + i]);
+         {
+            lmin = fminf(lmin, kp[l * KD + KD - 1]);
+            for (int i = 0; i < KD && kp[l * KD + i] < k0[KP - 1]; ++i)
+               insert_key<KP>(k0, c0, kp[l * KD + i], cp[l * KD + i]);
+         }
+         s_lmin[rl] = lmin;
          float kk = INFINITY;
 #pragma unroll
          for (int i = 0; i < KP; ++i)
@@ -1242,19 +1252,21 @@ __global__ void __launch_bounds__(256) rerank_kernel(const RerankParams p)
          for (uint32_t i = 0; i < m; ++i)
             if (s_d[rl][i] != INFINITY)
                insert_pair<KP>(sd, si, s_d[rl][i], s_col[rl][i]);
-         // certificate: every column outside the list has key >= T (up to the packing
-         // tolerance), hence true squared distance >= ||a||^2 + T - bound and reference
-         // distance >= that * (1 - gref); above the k-th exact distance, no excluded
-         // column can enter the top-k
+         // certificate: every column outside the list has key >= T = min(merged KP-th
+         // key, every list's last key) (up to the packing tolerance), hence true squared
+         // distance >= ||a||^2 + T - bound and reference distance >= that * (1 - gref);
+         // above the k-th exact distance, no excluded column can enter the top-k.  With
+         // at most KD columns no list dropped any.
          bool cert = !exact_only;
-         if (cert && total > uint32_t(KP))
+         if (cert && total > uint32_t(KD))
          {
+            const float Tb = fminf(s_key[rl][KP - 1], s_lmin[rl]);
             float dk = INFINITY;
 #pragma unroll
             for (int i = 0; i < KP; ++i)
                if (uint32_t(i) == p.k - 1)
                   dk = sd[i];
-            const double Tp = (double)s_key[rl][KP - 1];
+            const double Tp = (double)Tb;
             const double T = Tp - fabs(Tp) * pk;
             const double a2lo = qn * (1.0 - p.gd);
             const double lhs = (a2lo + T - bound) * (1.0 - p.gref);

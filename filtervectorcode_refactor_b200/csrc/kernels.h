@@ -33,8 +33,16 @@ struct OperandScale
 // a TMEM lane quarter).
 constexpr uint32_t kTcLists = 3;
 
-// Tensor-core prefilter: per source row, the KP smallest keys ||x||^2 - 2 q.x of each
-// column third, written to cand_key / cand_col [row][kTcLists][KP].
+// Depth of each list for a merged candidate list of kp entries.  The rerank certifies
+// against min(merged kp-th key, every list's last key), so a list may be shallower
+// than kp: three lists of 12 lose nothing against three of 16 unless 12 of a row's
+// nearest keys fall in one column third.  Shallower lists take fewer insertions, each
+// cheaper, in the prefilter's epilogue (its bottleneck).  kp = 32 keeps full lists.
+__host__ __device__ constexpr int tc_list_depth(int kp) { return kp == 16 ? 12 : kp; }
+
+// Tensor-core prefilter: per source row, the tc_list_depth(KP) smallest keys
+// ||x||^2 - 2 q.x of each column third, written to cand_key / cand_col
+// [row][kTcLists][tc_list_depth(KP)].
 struct TcParams
 {
    const WorkItem *items;

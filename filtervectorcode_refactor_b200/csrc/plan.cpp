@@ -19,7 +19,11 @@ namespace ungx
 
 int build_plan(const ungx_cross_edge_problem &p, Plan &plan, std::string &err)
 {
-   plan = Plan();
+   plan.items.clear();
+   plan.segs.clear();
+   plan.empty_rows.clear();
+   plan.pairs = plan.padded_cols = 0;
+   plan.max_item_cols = 0;
    const uint32_t n = p.num_points, G = p.num_groups;
    if (p.dim == 0 || p.topk == 0)
    {
@@ -63,76 +67,158 @@ int build_plan(const ungx_cross_edge_problem &p, Plan &plan, std::string &err)
          return UNGX_ERR_INVALID_ARG;
       }
 
-   struct Cand
-   {
-      WorkItem item;
-      uint64_t cost;
-      uint64_t pairs;
+   // Pass 1, per source group f: its non-empty targets (segments), their columns and
+   // the item cost (MMA columns, 16-granular, plus ~32 columns of per-tile overhead).
+   // Pass 2 writes segments and items at offsets from prefix sums, so both passes can
+   // run over groups in parallel and the result equals the sequential construction.
+   plan.g_nseg.assign(size_t(G) + 1, 0u);
+   plan.g_item0.assign(size_t(G) + 2, 0u);
+   plan.g_seg0.assign(size_t(G) + 2, 0u);
+   plan.g_cols.assign(size_t(G) + 1, 0u);
+   plan.g_cost.assign(size_t(G) + 1, 0u);
+   const bool par = nnz > 262144 || G > 65536; // thread start-up costs more on small plans
+   auto over_groups = [&](auto &&body) {
+      if (par)
+         parallel_for(int64_t(G), 0, 4096, [&](int64_t i) { body(uint32_t(i) + 1u); });
+      else
+         for (uint32_t f = 1; f <= G; ++f)
+            body(f);
    };
-   std::vector<Cand> all;
-   std::vector<std::pair<RowRange, uint32_t>> empties; // (range, group)
-   for (uint32_t f = 1; f <= G; ++f)
-   {
+   over_groups([&](uint32_t f) {
       const uint32_t a = p.group_ranges[2 * f], b = p.group_ranges[2 * f + 1];
-      if (a == b)
-         continue;
-      if (p.skip_source_group && p.skip_source_group[f])
-      {
-         empties.push_back({{a, b - a}, f});
-         continue;
-      }
-      const uint32_t seg_begin = (uint32_t)plan.segs.size();
-      uint64_t cols = 0, cost_cols = 0;
+      if (a == b || (p.skip_source_group && p.skip_source_group[f]))
+         return;
+      uint32_t ns = 0;
+      uint64_t cols = 0, cost = 0;
       for (uint64_t e = p.lng_out_offsets[f]; e < p.lng_out_offsets[f + 1]; ++e)
       {
          const uint32_t t = p.lng_out_ids[e];
          const uint32_t ta = p.group_ranges[2 * t], tb = p.group_ranges[2 * t + 1];
          if (ta == tb)
             continue;
-         plan.segs.push_back({ta, tb - ta, t, 0});
+         ++ns;
          cols += tb - ta;
-         // MMA columns (16-granular) plus a per-tile overhead of ~32 columns
          const uint64_t full = (tb - ta) / 256, rem = (tb - ta) % 256;
-         cost_cols += full * (256 + 32) + (rem ? ((rem + 15) / 16) * 16 + 32 : 0);
+         cost += full * (256 + 32) + (rem ? ((rem + 15) / 16) * 16 + 32 : 0);
       }
-      const uint32_t seg_count = (uint32_t)plan.segs.size() - seg_begin;
-      if (seg_count == 0)
-      {
-         empties.push_back({{a, b - a}, f});
-         continue;
-      }
-      for (uint32_t r = a; r < b; r += kRowsPerItem)
-      {
-         const uint32_t cnt = std::min(kRowsPerItem, b - r);
-         all.push_back({{r, cnt, seg_begin, seg_count}, cost_cols, uint64_t(cnt) * cols});
-      }
-      plan.max_item_cols = (uint32_t)std::max<uint64_t>(plan.max_item_cols, cols);
-   }
-   // longest processing time first; ties broken by row for determinism
-   std::stable_sort(all.begin(), all.end(), [](const Cand &x, const Cand &y) {
-      if (x.cost != y.cost)
-         return x.cost > y.cost;
-      return x.item.row_begin < y.item.row_begin;
+      plan.g_nseg[f] = ns;
+      plan.g_cols[f] = cols;
+      plan.g_cost[f] = cost;
    });
+   uint64_t nsegs = 0, nitems = 0;
+   for (uint32_t f = 1; f <= G; ++f)
+   {
+      plan.g_seg0[f] = uint32_t(nsegs);
+      plan.g_item0[f] = uint32_t(nitems);
+      if (plan.g_nseg[f])
+      {
+         const uint32_t rows = p.group_ranges[2 * f + 1] - p.group_ranges[2 * f];
+         nsegs += plan.g_nseg[f];
+         nitems += (rows + kRowsPerItem - 1) / kRowsPerItem;
+         plan.max_item_cols = (uint32_t)std::max<uint64_t>(plan.max_item_cols, plan.g_cols[f]);
+      }
+   }
+   if (nsegs > UINT32_MAX || nitems > UINT32_MAX)
+   {
+      err = "plan exceeds 2^32 segments or items";
+      return UNGX_ERR_INVALID_ARG;
+   }
+   plan.segs.resize(nsegs);
+   plan.all.resize(nitems);
+   plan.key.resize(nitems);
+   plan.item_pairs.resize(nitems);
+   over_groups([&](uint32_t f) {
+      const uint32_t ns = plan.g_nseg[f];
+      if (!ns)
+         return;
+      const uint32_t seg_begin = plan.g_seg0[f];
+      Segment *sg = plan.segs.data() + seg_begin;
+      for (uint64_t e = p.lng_out_offsets[f]; e < p.lng_out_offsets[f + 1]; ++e)
+      {
+         const uint32_t t = p.lng_out_ids[e];
+         const uint32_t ta = p.group_ranges[2 * t], tb = p.group_ranges[2 * t + 1];
+         if (ta != tb)
+            *sg++ = {ta, tb - ta, t, 0};
+      }
+      const uint32_t a = p.group_ranges[2 * f], b = p.group_ranges[2 * f + 1];
+      uint32_t i = plan.g_item0[f];
+      for (uint32_t r = a; r < b; r += kRowsPerItem, ++i)
+      {
+         plan.all[i] = {r, std::min(kRowsPerItem, b - r), seg_begin, ns};
+         plan.key[i] = plan.g_cost[f];
+         plan.item_pairs[i] = uint64_t(plan.all[i].row_count) * plan.g_cols[f];
+      }
+   });
+
+   // Longest processing time first, ties by first row: a stable LSD radix sort, first
+   // by row (skipped when the groups' rows already ascend) and then by descending cost.
+   const uint32_t N = uint32_t(nitems);
+   plan.order.resize(N);
+   plan.order2.resize(N);
+   std::iota(plan.order.begin(), plan.order.end(), 0u);
+   auto radix = [&](auto &&digit_of, int bits) {
+      constexpr int kDigit = 11;
+      std::vector<uint32_t> hist(size_t(1) << kDigit);
+      for (int shift = 0; shift < bits; shift += kDigit)
+      {
+         std::fill(hist.begin(), hist.end(), 0u);
+         for (uint32_t i = 0; i < N; ++i)
+            ++hist[(digit_of(plan.order[i]) >> shift) & ((1u << kDigit) - 1u)];
+         uint32_t sum = 0;
+         for (auto &h : hist)
+         {
+            const uint32_t c = h;
+            h = sum;
+            sum += c;
+         }
+         for (uint32_t i = 0; i < N; ++i)
+         {
+            const uint32_t o = plan.order[i];
+            plan.order2[hist[(digit_of(o) >> shift) & ((1u << kDigit) - 1u)]++] = o;
+         }
+         plan.order.swap(plan.order2);
+      }
+   };
+   bool rows_ascend = true;
+   for (uint32_t i = 1; i < N && rows_ascend; ++i)
+      rows_ascend = plan.all[i - 1].row_begin < plan.all[i].row_begin;
+   if (!rows_ascend)
+      radix([&](uint32_t o) { return uint64_t(plan.all[o].row_begin); }, 32);
+   uint64_t max_cost = 0;
+   for (uint32_t i = 0; i < N; ++i)
+      max_cost = std::max(max_cost, plan.key[i]);
+   int cost_bits = 0;
+   while (cost_bits < 64 && (max_cost >> cost_bits))
+      ++cost_bits;
+   radix([&](uint32_t o) { return max_cost - plan.key[o]; }, cost_bits);
+
+   // greedy assignment to the least-loaded shard, in that order
    const uint32_t S = p.shard_count;
    std::vector<uint64_t> load(S, 0);
-   for (const Cand &c : all)
+   plan.items.reserve(S == 1 ? N : N / S + 1);
+   for (uint32_t i = 0; i < N; ++i)
    {
+      const uint32_t o = plan.order[i];
       uint32_t best = 0;
       for (uint32_t s = 1; s < S; ++s)
          if (load[s] < load[best])
             best = s;
-      load[best] += c.cost + 1;
+      load[best] += plan.key[o] + 1;
       if (best == p.shard_rank)
       {
-         plan.items.push_back(c.item);
-         plan.pairs += c.pairs;
-         plan.padded_cols += c.cost;
+         const WorkItem &it = plan.all[o];
+         plan.items.push_back(it);
+         plan.pairs += plan.item_pairs[o];
+         plan.padded_cols += plan.key[o];
       }
    }
-   for (const auto &e : empties)
-      if (e.second % S == p.shard_rank)
-         plan.empty_rows.push_back(e.first);
+   // rows with no candidates: skipped source groups and groups without targets
+   for (uint32_t f = 1; f <= G; ++f)
+   {
+      const uint32_t a = p.group_ranges[2 * f], b = p.group_ranges[2 * f + 1];
+      if (a != b && plan.g_nseg[f] == 0 && f % S == p.shard_rank)
+         plan.empty_rows.push_back({a, b - a});
+   }
    return UNGX_OK;
 }
 

@@ -53,6 +53,12 @@ struct Plan
    uint64_t pairs = 0;                // sum |f|*|f'| over this shard's rows
    uint64_t padded_cols = 0;          // sum over items of sum roundup16(|f'|)
    uint32_t max_item_cols = 0;
+   // working storage of build_plan, kept so that a reused Plan allocates nothing
+   std::vector<uint64_t> g_cols, g_cost;            // per group: target columns, cost
+   std::vector<uint32_t> g_nseg, g_seg0, g_item0;   // per group: segments, offsets
+   std::vector<WorkItem> all;                       // every shard's items, group order
+   std::vector<uint64_t> key, item_pairs;           // per item: cost (sort key), pairs
+   std::vector<uint32_t> order, order2;             // item permutation
 };
 
 constexpr uint32_t kRowsPerItem = 128;
