@@ -234,28 +234,6 @@ __device__ __forceinline__ void insert_pair(float (&kd)[K], uint32_t (&ki)[K], f
    }
 }
 
-// Same on prefilter keys alone (their order among equal keys does not matter);
-// inserting +inf is a no-op.
-template <int K>
-__device__ __forceinline__ void insert_key(float (&kd)[K], uint32_t (&ki)[K], float d, uint32_t id)
-{
-#pragma unroll
-   for (int i = K - 1; i > 0; --i)
-   {
-      const bool prev = d < kd[i - 1];
-      const bool here = d < kd[i];
-      const float nd = prev ? kd[i - 1] : (here ? d : kd[i]);
-      const uint32_t ni = prev ? ki[i - 1] : (here ? id : ki[i]);
-      kd[i] = nd;
-      ki[i] = ni;
-   }
-   if (d < kd[0])
-   {
-      kd[0] = d;
-      ki[0] = id;
-   }
-}
-
 // ------------------------------------------------------------------ prep
 // Column sums (fp64) and column ranges of X over a block of rows; thread = column,
 // four rows in flight per thread.
@@ -1116,20 +1094,25 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
 }
 
 // ------------------------------------------------------------------ rerank + certificate
-// One block per work item; TPR threads per row (one or two candidates each), RPB rows
-// per pass.  Keys are the packed prefilter keys: within 2^-17 relative of the fp32 key.
-// The row's three lists are merged into its KP smallest keys first.
+// One block per work item.  A row belongs to a group of KP lanes (a half warp for
+// KP = 16, a warp for KP = 32) that never waits on the rest of the block:
+//   1. the lanes rank the row's 3 x KD list entries (packed prefilter keys, within
+//      2^-17 relative of the fp32 key) by counting over shuffles, ties by entry index,
+//      and the KP smallest go to one lane each (the merged list);
+//   2. each lane computes the exact reference distance of its candidate unless its
+//      key shows it cannot reach the top-k;
+//   3. the lanes rank their (distance, id) pairs the same way and write the first k;
+//   4. the certificate is evaluated by every lane, recorded by lane 0.
 template <int KP>
-__global__ void __launch_bounds__(256) rerank_kernel(const RerankParams p)
+__global__ void __launch_bounds__(256, 3) rerank_kernel(const RerankParams p)
 {
-   constexpr uint32_t TPR = KP <= 16 ? 16u : 32u;
-   constexpr int KD = tc_list_depth(KP); // depth of each of the row's lists
-   constexpr uint32_t RPB = 256u / TPR;
-   __shared__ uint32_t s_col[RPB][KP];
-   __shared__ float s_key[RPB][KP];
-   __shared__ float s_d[RPB][KP];
-   __shared__ double s_lim[RPB];
-   __shared__ float s_lmin[RPB];
+   constexpr uint32_t TPR = KP;           // lanes per row
+   constexpr int KD = tc_list_depth(KP);  // depth of each of the row's lists
+   constexpr int NE = int(kTcLists) * KD; // list entries per row
+   constexpr int EPL = (NE + int(TPR) - 1) / int(TPR);
+   constexpr uint32_t RPB = 256u / TPR; // rows in flight per block
+   static_assert(TPR == 16 || TPR == 32, "a row group is a half warp or a warp");
+   __shared__ uint2 s_slot[RPB][KP]; // merged list: (key bits, column) by rank
    __shared__ float s_maxn2;
    __shared__ uint32_t s_total;
    __shared__ unsigned long long s_cnt[2];
@@ -1163,133 +1146,133 @@ __global__ void __launch_bounds__(256) rerank_kernel(const RerankParams p)
    }
    __syncthreads();
    const uint32_t total = s_total;
-   const uint32_t m = total < uint32_t(KP) ? total : uint32_t(KP);
-   const uint32_t rl = tid / TPR, sub = tid % TPR;
+   const uint32_t grp = tid / TPR, j = tid % TPR;
+   const uint32_t gmask = TPR == 32u ? 0xffffffffu : (0xffffu << (tid & 16u));
    const bool vec4 = (p.d & 3u) == 0;
    const double pk = 1.0 / 131072.0; // packed-key tolerance, 2^-17 relative
    const double bmax = sqrt((double)s_maxn2 * (1.0 + p.gd));
    const double inv_s = (double)p.scale->inv_s;
    const bool exact_only = p.scale->exact_only != 0;
-   for (uint32_t base = 0; base < w.row_count; base += RPB)
+   const uint32_t k = p.k;
+   uint32_t n_cert = 0, n_fail = 0;
+   for (uint32_t r = grp; r < w.row_count; r += RPB)
    {
-      const uint32_t r = base + rl;
-      const bool ok = r < w.row_count;
       const uint32_t row = w.row_begin + r;
-      const double qn = ok ? (double)__ldg(p.xnorm + row) : 0.0;
+      const float *kp = p.cand_key + size_t(row) * NE;
+      const uint32_t *cp = p.cand_col + size_t(row) * NE;
+      float ek[EPL];
+      uint32_t ec[EPL];
+#pragma unroll
+      for (int e = 0; e < EPL; ++e)
+      {
+         const int idx = int(j) + e * int(TPR);
+         ek[e] = idx < NE ? kp[idx] : INFINITY;
+         ec[e] = idx < NE ? cp[idx] : 0xFFFFFFFFu;
+      }
+      // 1. rank among the NE entries: (key, entry index) order
+      uint32_t rk[EPL];
+#pragma unroll
+      for (int e = 0; e < EPL; ++e)
+         rk[e] = 0;
+#pragma unroll
+      for (int src = 0; src < NE; ++src)
+      {
+         const float v = __shfl_sync(gmask, ek[src / int(TPR)], src % int(TPR), TPR);
+#pragma unroll
+         for (int e = 0; e < EPL; ++e)
+            rk[e] += (v < ek[e] || (v == ek[e] && src < int(j) + e * int(TPR))) ? 1u : 0u;
+      }
+      // a column a list dropped has a key at least that list's last one
+      float lmin = INFINITY;
+#pragma unroll
+      for (int l = 0; l < int(kTcLists); ++l)
+      {
+         const int src = l * KD + KD - 1;
+         lmin = fminf(lmin, __shfl_sync(gmask, ek[src / int(TPR)], src % int(TPR), TPR));
+      }
+#pragma unroll
+      for (int e = 0; e < EPL; ++e)
+         if (rk[e] < uint32_t(KP))
+            s_slot[grp][rk[e]] = make_uint2(__float_as_uint(ek[e]), ec[e]);
+      __syncwarp(gmask);
+      const uint2 mine = s_slot[grp][j];
+      __syncwarp(gmask);
+      const float key = __uint_as_float(mine.x);
+      const float kk = __shfl_sync(gmask, key, k - 1u, TPR);      // k-th merged key
+      const float klast = __shfl_sync(gmask, key, TPR - 1u, TPR); // KP-th merged key
+
+      const double qn = (double)__ldg(p.xnorm + row);
       const double ahi = sqrt(qn * (1.0 + p.gd));
       // |key - (||b||^2 - 2 a.b)| <= bound for every column of this row
       const double bound =
           (p.c1 * ahi * bmax + p.c2 * bmax * bmax + p.c3 * inv_s * (ahi + bmax) + p.c4 * inv_s * inv_s) *
           (1.0 + 1.0 / 1024.0);
-      if (ok && sub == 0)
-      {
-         float k0[KP];
-         uint32_t c0[KP];
-         const float *kp = p.cand_key + size_t(row) * kTcLists * KD;
-         const uint32_t *cp = p.cand_col + size_t(row) * kTcLists * KD;
-#pragma unroll
-         for (int i = 0; i < KP; ++i)
-         {
-            k0[i] = i < KD ? kp[i] : INFINITY;
-            c0[i] = i < KD ? cp[i] : 0xFFFFFFFFu;
-         }
-         // each list is ascending: stop at its first key past the running maximum; a
-         // column a list dropped has a key at least that list's last one
-         float lmin = kp[KD - 1];
-#pragma unroll 1
-         for (uint32_t l = 1; l < kTcLists; ++l)
-         {
-            lmin = fminf(lmin, kp[l * KD + KD - 1]);
-            for (int i = 0; i < KD && kp[l * KD + i] < k0[KP - 1]; ++i)
-               insert_key<KP>(k0, c0, kp[l * KD + i], cp[l * KD + i]);
-         }
-         s_lmin[rl] = lmin;
-         float kk = INFINITY;
-#pragma unroll
-         for (int i = 0; i < KP; ++i)
-         {
-            s_key[rl][i] = k0[i];
-            s_col[rl][i] = c0[i];
-            if (uint32_t(i) == p.k - 1)
-               kk = k0[i];
-         }
-         // a candidate whose smallest possible reference distance exceeds the largest
-         // possible one of the k-th candidate cannot enter the top-k: no need to rerank it
-         const double khi = (double)kk + fabs((double)kk) * pk;
-         s_lim[rl] = (khi + qn * (1.0 + p.gd) + bound) * (1.0 + p.gref);
-      }
-      __syncthreads();
-      if (ok)
+      // 2. a candidate whose smallest possible reference distance exceeds the largest
+      // possible one of the k-th candidate cannot enter the top-k: it is not reranked
+      const double khi = (double)kk + fabs((double)kk) * pk;
+      const double lim = (khi + qn * (1.0 + p.gd) + bound) * (1.0 + p.gref);
+      const double a2lo = qn * (1.0 - p.gd);
+      const double kc = (double)key;
+      const double lo = fmax(0.0, kc - fabs(kc) * pk + a2lo - bound) * (1.0 - p.gref);
+      float D = INFINITY;
+      if (!(lo > lim) && mine.y < p.n) // a column outside the matrix is never read
       {
          const float *qv = p.X + size_t(row) * p.d;
-         const double a2lo = qn * (1.0 - p.gd);
-         for (uint32_t i = sub; i < m; i += TPR)
-         {
-            const double kc = (double)s_key[rl][i];
-            const double lo = fmax(0.0, kc - fabs(kc) * pk + a2lo - bound) * (1.0 - p.gref);
-            float D = INFINITY;
-            const uint32_t c = s_col[rl][i];
-            if (!(lo > s_lim[rl]) && c < p.n) // a column outside the matrix is never read
-            {
-               const float *xv = p.X + size_t(c) * p.d;
-               D = vec4 ? ref_l2<true>(qv, xv, p.d) : ref_l2<false>(qv, xv, p.d);
-            }
-            s_d[rl][i] = D;
-         }
+         const float *xv = p.X + size_t(mine.y) * p.d;
+         D = vec4 ? ref_l2<true>(qv, xv, p.d) : ref_l2<false>(qv, xv, p.d);
       }
-      __syncthreads();
-      if (ok && sub == 0)
+      const uint32_t id = D != INFINITY ? mine.y : 0xFFFFFFFFu; // not reranked: an empty slot
+      // 3. rank of (D, id) among the row's candidates, ties by lane; the first k are the row
+      uint32_t orank = 0;
+#pragma unroll
+      for (int src = 0; src < int(TPR); ++src)
       {
-         float sd[KP];
-         uint32_t si[KP];
-#pragma unroll
-         for (int i = 0; i < KP; ++i)
-         {
-            sd[i] = INFINITY;
-            si[i] = 0xFFFFFFFFu;
-         }
-#pragma unroll 1
-         for (uint32_t i = 0; i < m; ++i)
-            if (s_d[rl][i] != INFINITY)
-               insert_pair<KP>(sd, si, s_d[rl][i], s_col[rl][i]);
-         // certificate: every column outside the list has key >= T = min(merged KP-th
-         // key, every list's last key) (up to the packing tolerance), hence true squared
-         // distance >= ||a||^2 + T - bound and reference distance >= that * (1 - gref);
-         // above the k-th exact distance, no excluded column can enter the top-k.  With
-         // at most KD columns no list dropped any.
-         bool cert = !exact_only;
-         if (cert && total > uint32_t(KD))
-         {
-            const float Tb = fminf(s_key[rl][KP - 1], s_lmin[rl]);
-            float dk = INFINITY;
-#pragma unroll
-            for (int i = 0; i < KP; ++i)
-               if (uint32_t(i) == p.k - 1)
-                  dk = sd[i];
-            const double Tp = (double)Tb;
-            const double T = Tp - fabs(Tp) * pk;
-            const double a2lo = qn * (1.0 - p.gd);
-            const double lhs = (a2lo + T - bound) * (1.0 - p.gref);
-            cert = lhs > (double)dk;
-         }
-#pragma unroll
-         for (int i = 0; i < KP; ++i)
-            if (uint32_t(i) < p.k)
-            {
-               p.out_ids[size_t(row) * p.k + i] = si[i];
-               if (p.out_dists)
-                  p.out_dists[size_t(row) * p.k + i] = sd[i];
-            }
+         const float d2 = __shfl_sync(gmask, D, src, TPR);
+         const uint32_t i2 = __shfl_sync(gmask, id, src, TPR);
+         orank += (pair_less(d2, i2, D, id) || (d2 == D && i2 == id && src < int(j))) ? 1u : 0u;
+      }
+      if (orank < k)
+      {
+         p.out_ids[size_t(row) * k + orank] = id;
+         if (p.out_dists)
+            p.out_dists[size_t(row) * k + orank] = D;
+      }
+      // 4. certificate: every column outside the merged list has key >= T = min(KP-th
+      // merged key, every list's last key) (up to the packing tolerance), hence true
+      // squared distance >= ||a||^2 + T - bound and reference distance >= that *
+      // (1 - gref); above the k-th exact distance, no excluded column can enter the
+      // top-k.  With at most KD columns no list dropped any.
+      const uint32_t at_k = __ballot_sync(gmask, orank == k - 1u) >> (TPR == 32u ? 0u : (tid & 16u));
+      const float dk = __shfl_sync(gmask, D, __ffs(at_k) - 1, TPR);
+      bool cert = !exact_only;
+      if (cert && total > uint32_t(KD))
+      {
+         const double Tp = (double)fminf(klast, lmin);
+         const double T = Tp - fabs(Tp) * pk;
+         const double lhs = (a2lo + T - bound) * (1.0 - p.gref);
+         cert = lhs > (double)dk;
+      }
+      if (j == 0)
+      {
          if (!cert)
          {
             const uint32_t pos = atomicAdd(p.fb_count, 1u);
             p.fb_rows[pos] = row;
             p.fb_items[pos] = blockIdx.x + p.item_offset;
+            ++n_fail;
          }
-         atomicAdd(&s_cnt[cert ? 0 : 1], 1ull);
+         else
+            ++n_cert;
       }
-      __syncthreads();
    }
+   if (j == 0)
+   {
+      if (n_cert)
+         atomicAdd(&s_cnt[0], (unsigned long long)n_cert);
+      if (n_fail)
+         atomicAdd(&s_cnt[1], (unsigned long long)n_fail);
+   }
+   __syncthreads();
    if (tid == 0)
    {
       if (s_cnt[0])
