@@ -16,11 +16,12 @@
 //
 // Layout of a block (256 threads): 64 source rows x 32 candidates per step, both tiles
 // transposed in shared memory ([dim][64]); distances of the step go to a shared tile,
-// all threads test them against their row's current last entry, then one thread per
-// row inserts the passing ones in ascending candidate order into the row's sorted list
-// (strict <, the reference's tie rule), kept in shared memory.  The tree code is one
-// 8-leaf subtree body looped over the 16 (warp, subtree) positions: a kernel of a few
-// hundred instructions (a fully unrolled tree missed the instruction cache).
+// then each warp updates the sorted lists of 8 rows (kept in shared memory): the
+// candidates that beat a row's last entry are inserted in ascending candidate order
+// (strict <, the reference's tie rule), a ballot giving the position and a one-lane
+// shift moving the tail, so that all 32 lanes work on one row's insert.  The tree code
+// is one 8-leaf subtree body looped over the 16 (warp, subtree) positions: a kernel of
+// a few hundred instructions (a fully unrolled tree missed the instruction cache).
 #include <algorithm>
 #include <cfloat>
 
@@ -155,13 +156,28 @@ __global__ void __launch_bounds__(kKnnThreads) exact_knn_kernel(const KnnParams 
    if (task.row0 == 0 && tid == 0 && p.entry_points)
       p.entry_points[task.group] = 0;
 
-   // source rows, transposed; rows past the group read as zero
-   for (uint32_t idx = tid; idx < uint32_t(kKnnRows) * p.dpad; idx += kKnnThreads)
-   {
-      const uint32_t r = idx % kKnnRows, dim = idx / kKnnRows;
-      const uint32_t row = task.row0 + r;
-      sq[dim * kKnnRows + r] = (row < n && dim < p.d) ? p.X[size_t(first + row) * p.d + dim] : 0.0f;
-   }
+   // source rows, transposed; rows past the group read as zero.  With d % 4 == 0 each
+   // thread reads four consecutive dims of a row (16-byte loads) and the stores of a
+   // warp go to 32 consecutive rows of a dim (conflict-free).
+   const bool vec4 = (p.d & 3u) == 0;
+   if (vec4)
+      for (uint32_t idx = tid; idx < uint32_t(kKnnRows) * (p.dpad / 4u); idx += kKnnThreads)
+      {
+         const uint32_t r = idx % kKnnRows, d4 = idx / kKnnRows, row = task.row0 + r;
+         const float4 v = row < n ? __ldg(reinterpret_cast<const float4 *>(p.X + size_t(first + row) * p.d) + d4)
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+         sq[(4 * d4 + 0) * kKnnRows + r] = v.x;
+         sq[(4 * d4 + 1) * kKnnRows + r] = v.y;
+         sq[(4 * d4 + 2) * kKnnRows + r] = v.z;
+         sq[(4 * d4 + 3) * kKnnRows + r] = v.w;
+      }
+   else
+      for (uint32_t idx = tid; idx < uint32_t(kKnnRows) * p.dpad; idx += kKnnThreads)
+      {
+         const uint32_t r = idx % kKnnRows, dim = idx / kKnnRows;
+         const uint32_t row = task.row0 + r;
+         sq[dim * kKnnRows + r] = (row < n && dim < p.d) ? p.X[size_t(first + row) * p.d + dim] : 0.0f;
+      }
    for (uint32_t idx = tid; idx < uint32_t(kKnnRows) * kLl; idx += kKnnThreads)
    {
       ld[idx] = FLT_MAX;
@@ -169,17 +185,28 @@ __global__ void __launch_bounds__(kKnnThreads) exact_knn_kernel(const KnnParams 
    }
    const int tr = int(tid / 16u), tc = int(tid % 16u);
    const int r0 = tr * 4, c0 = tc * 2;
-   __shared__ __align__(4) uint8_t pass[kKnnThreads]; // per row: 4 bytes = its 32 candidates
-   uint32_t fill = 0;                                // entries in this thread's row list (tid < 64)
+   const uint32_t warp = tid >> 5, lane = tid & 31u;
    for (uint32_t x0 = 0; x0 < n; x0 += kKnnCands)
    {
       __syncthreads(); // previous step's candidate tile and distances are consumed
-      for (uint32_t idx = tid; idx < uint32_t(kKnnCands) * p.dpad; idx += kKnnThreads)
-      {
-         const uint32_t c = idx % kKnnCands, dim = idx / kKnnCands;
-         const uint32_t x = x0 + c;
-         sx[dim * kKnnCands + c] = (x < n && dim < p.d) ? p.X[size_t(first + x) * p.d + dim] : 0.0f;
-      }
+      if (vec4)
+         for (uint32_t idx = tid; idx < uint32_t(kKnnCands) * (p.dpad / 4u); idx += kKnnThreads)
+         {
+            const uint32_t c = idx % kKnnCands, d4 = idx / kKnnCands, x = x0 + c;
+            const float4 v = x < n ? __ldg(reinterpret_cast<const float4 *>(p.X + size_t(first + x) * p.d) + d4)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+            sx[(4 * d4 + 0) * kKnnCands + c] = v.x;
+            sx[(4 * d4 + 1) * kKnnCands + c] = v.y;
+            sx[(4 * d4 + 2) * kKnnCands + c] = v.z;
+            sx[(4 * d4 + 3) * kKnnCands + c] = v.w;
+         }
+      else
+         for (uint32_t idx = tid; idx < uint32_t(kKnnCands) * p.dpad; idx += kKnnThreads)
+         {
+            const uint32_t c = idx % kKnnCands, dim = idx / kKnnCands;
+            const uint32_t x = x0 + c;
+            sx[dim * kKnnCands + c] = (x < n && dim < p.d) ? p.X[size_t(first + x) * p.d + dim] : 0.0f;
+         }
       __syncthreads();
       // (w0 + w2) + (w1 + w3); a warp block past d is +0 and is skipped
       float s02[8], s13[8];
@@ -212,56 +239,60 @@ __global__ void __launch_bounds__(kKnnThreads) exact_knn_kernel(const KnnParams 
          for (int b = 0; b < 2; ++b)
             sd[(r0 + a) * kLd + c0 + b] = add_ftz(s02[a * 2 + b], s13[a * 2 + b]);
       __syncthreads();
-      // all threads: which of the step's candidates beat their row's current last entry
-      // (4 threads per row, 8 candidates each; a looser test than the insert's own)
-      {
-         const uint32_t row = tid >> 2, part = tid & 3u;
-         const uint32_t cend = min(uint32_t(kKnnCands), n - x0);
-         uint32_t m = 0;
-         if (task.row0 + row < n && cand > 0)
+      // The reference's insert, one warp per row (8 rows per warp): the row's step
+      // candidates that beat its last entry are taken in ascending local id; each goes
+      // after every entry <= its distance (strict <), the last entry dropping out.  The
+      // list's empty tail holds FLT_MAX / UINT32_MAX, so a distance of FLT_MAX or more
+      // never enters.  Lane l holds entries l and l + 32 while the row is updated.
+      if (cand > 0)
+#pragma unroll 1
+         for (uint32_t i = 0; i < uint32_t(kKnnRows) / (kKnnThreads / 32u); ++i)
          {
-            const float thr = ld[row * kLl + cand - 1];
-#pragma unroll
-            for (uint32_t i = 0; i < 8; ++i)
-            {
-               const uint32_t c = part * 8u + i;
-               if (c < cend && x0 + c != task.row0 + row && sd[row * kLd + c] < thr)
-                  m |= 1u << i;
-            }
-         }
-         pass[tid] = uint8_t(m);
-      }
-      __syncthreads();
-      // one thread per row: the passing candidates in ascending order, the reference's
-      // insert (started at the list's fill: the empty tail holds FLT_MAX / UINT32_MAX)
-      if (tid < uint32_t(kKnnRows) && task.row0 + tid < n && cand > 0)
-      {
-         float *rd = ld + tid * kLl;
-         uint32_t *ri = li + tid * kLl;
-         uint32_t m = *reinterpret_cast<const uint32_t *>(pass + 4 * tid);
-         while (m)
-         {
-            const uint32_t c = __ffs(m) - 1;
-            m &= m - 1u;
-            const uint32_t x = x0 + c;
-            const float dist = sd[tid * kLd + c];
-            if (!(dist < rd[cand - 1]))
+            const uint32_t r = warp * (uint32_t(kKnnRows) / (kKnnThreads / 32u)) + i;
+            const uint32_t s = task.row0 + r;
+            if (s >= n)
+               break;
+            const uint32_t x = x0 + lane;
+            const float dist = sd[r * kLd + lane];
+            uint32_t m = __ballot_sync(0xffffffffu, x < n && x != s && dist < ld[r * kLl + cand - 1]);
+            if (!m)
                continue;
-            uint32_t pos = min(fill, cand);
-            fill = min(fill + 1u, cand);
-            while (pos > 0 && dist < rd[pos - 1])
+            float e0 = ld[r * kLl + lane], e1 = ld[r * kLl + 32u + lane];
+            uint32_t i0 = li[r * kLl + lane], i1 = li[r * kLl + 32u + lane];
+            const uint32_t lc = (cand - 1u) & 31u;
+            while (m)
             {
-               if (pos < cand)
+               const uint32_t b = __ffs(m) - 1u;
+               m &= m - 1u;
+               const float nd = __shfl_sync(0xffffffffu, dist, b);
+               const float last = __shfl_sync(0xffffffffu, cand > 32u ? e1 : e0, lc);
+               if (!(nd < last))
+                  continue;
+               const uint32_t pos = __popc(__ballot_sync(0xffffffffu, lane < cand && e0 <= nd)) +
+                                    __popc(__ballot_sync(0xffffffffu, lane + 32u < cand && e1 <= nd));
+               const float u0 = __shfl_up_sync(0xffffffffu, e0, 1), u1 = __shfl_up_sync(0xffffffffu, e1, 1);
+               const uint32_t v0 = __shfl_up_sync(0xffffffffu, i0, 1), v1 = __shfl_up_sync(0xffffffffu, i1, 1);
+               const float t31 = __shfl_sync(0xffffffffu, e0, 31);
+               const uint32_t j31 = __shfl_sync(0xffffffffu, i0, 31);
+               const float p1 = lane ? u1 : t31;
+               const uint32_t q1 = lane ? v1 : j31;
+               const uint32_t nid = x0 + b;
+               if (lane >= pos)
                {
-                  rd[pos] = rd[pos - 1];
-                  ri[pos] = ri[pos - 1];
+                  e0 = lane == pos ? nd : u0;
+                  i0 = lane == pos ? nid : v0;
                }
-               --pos;
+               if (lane + 32u >= pos)
+               {
+                  e1 = lane + 32u == pos ? nd : p1;
+                  i1 = lane + 32u == pos ? nid : q1;
+               }
             }
-            rd[pos] = dist;
-            ri[pos] = x;
+            ld[r * kLl + lane] = e0;
+            ld[r * kLl + 32u + lane] = e1;
+            li[r * kLl + lane] = i0;
+            li[r * kLl + 32u + lane] = i1;
          }
-      }
    }
    __syncthreads();
    // the row layout: head, ring anchors, tail, padding with the point itself
