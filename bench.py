@@ -35,7 +35,7 @@ sys.path.insert(0, ROOT)
 METRIC = "UNG cross-edge build TFLOP/s (algorithmic 2*d*W / wall), configs[1]"
 # DRAM bytes (read + write) of one tc_kernel launch on the bench workload, from one ncu
 # capture of this build (profiles/tc_kernel_cfg2.txt); other configurations: not captured.
-TC_TRAFFIC_BYTES = {2: 568_865_792 + 269_338_368}
+TC_TRAFFIC_BYTES = {2: 556_360_704 + 202_750_976}
 
 
 def log(*a):
