@@ -114,10 +114,10 @@ struct ungx_context
    PinnedBuf host_stage;
    // additional edges and graph emission
    DevBuf g_ranges, g_out_off, g_out_ids, group_of, reach, add_items, add_segs, add_rows, add_row_items, add_pos,
-       add_res, add_off, add_cols, scan_scratch, knn_ranges, knn_base, knn_tasks;
-   uint32_t add_n = 0; // points of the last additional-edge build
-   std::vector<uint32_t> add_from, add_to, add_point_cols;
-   std::vector<uint64_t> add_point_off;
+       add_res, add_off, add_cols, add_qoff, add_loff, add_from, add_to, add_stats, scan_scratch, knn_ranges, knn_base,
+       knn_tasks;
+   uint32_t add_n = 0;     // points of the last additional-edge build
+   uint64_t add_edges = 0; // its edges
    uint32_t *h_counters = nullptr; // pinned
    cudaEvent_t ev[10] = {};
 };
@@ -514,7 +514,8 @@ int ungx_context_destroy(ungx_context *ctx)
                      &ctx->stage[0], &ctx->stage[1], &ctx->cand_key, &ctx->cand_col, &ctx->copy_ranges,
                      &ctx->compact, &ctx->g_ranges, &ctx->g_out_off, &ctx->g_out_ids, &ctx->group_of, &ctx->reach,
                      &ctx->add_items, &ctx->add_segs, &ctx->add_rows, &ctx->add_row_items, &ctx->add_pos,
-                     &ctx->add_res, &ctx->add_off, &ctx->add_cols, &ctx->scan_scratch, &ctx->knn_ranges,
+                     &ctx->add_res, &ctx->add_off, &ctx->add_cols, &ctx->add_qoff, &ctx->add_loff, &ctx->add_from,
+                     &ctx->add_to, &ctx->add_stats, &ctx->scan_scratch, &ctx->knn_ranges,
                      &ctx->knn_base, &ctx->knn_tasks})
       b->release();
    ctx->host_stage.release();
@@ -818,15 +819,16 @@ int ungx_additional_edges_build(ungx_context *ctx, const ungx_cross_edge_problem
    }
    cudaStream_t s = ctx->stream;
    // 1. which LNG edges do the cross edges reach
-   std::vector<uint32_t> ranges(2 * size_t(G + 1));
-   if (G)
-      std::memcpy(ranges.data(), R, ranges.size() * sizeof(uint32_t));
-   std::vector<uint64_t> out_off(OO, OO + (G ? G + 2 : 0));
-   std::vector<uint32_t> out_ids(problem->lng_out_ids, problem->lng_out_ids + nnz);
+   auto up = [&](DevBuf &b, const void *src, size_t bytes, const char *what) -> int {
+      UNGX_CUDA(ctx, b.ensure(std::max<size_t>(bytes, 8)), what);
+      if (bytes)
+         UNGX_CUDA(ctx, cudaMemcpyAsync(b.p, src, bytes, cudaMemcpyHostToDevice, s), what);
+      return UNGX_OK;
+   };
    int st;
-   if ((st = upload(ctx, ctx->g_ranges, ranges, "group ranges")) ||
-       (st = upload(ctx, ctx->g_out_off, out_off, "LNG upload")) ||
-       (st = upload(ctx, ctx->g_out_ids, out_ids, "LNG upload")))
+   if ((st = up(ctx->g_ranges, R, 2 * (size_t(G) + 1) * sizeof(uint32_t), "group ranges")) ||
+       (st = up(ctx->g_out_off, OO, (G ? size_t(G) + 2 : 0) * sizeof(uint64_t), "LNG upload")) ||
+       (st = up(ctx->g_out_ids, problem->lng_out_ids, nnz * sizeof(uint32_t), "LNG upload")))
       return st;
    UNGX_CUDA(ctx, ctx->group_of.ensure(size_t(std::max(n, 1u)) * sizeof(uint32_t)), "group map");
    UNGX_CUDA(ctx, ctx->reach.ensure(std::max<uint64_t>(nnz, 1)), "edge flags");
@@ -839,59 +841,59 @@ int ungx_additional_edges_build(ungx_context *ctx, const ungx_cross_edge_problem
                                           ctx->g_out_off.as<uint64_t>(), ctx->g_out_ids.as<uint32_t>(),
                                           ctx->reach.as<uint8_t>(), s),
                 "edge marking kernel");
-   std::vector<uint8_t> reached(nnz);
-   if (nnz)
-      UNGX_CUDA(ctx, cudaMemcpyAsync(reached.data(), ctx->reach.p, nnz, cudaMemcpyDeviceToHost, s), "edge flags");
-   UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[6], s), "event");
-   if ((st = wait_event(ctx, ctx->ev[6], "edge marking")))
-      return st;
-   // 2. the reference's loop over missing edges, as a list of (vector, target) queries:
-   //    each vector of f adds m = min(|f'|, k/2) edges, until k were added (|f| caps it)
+   // 2. the reference's loop over missing edges, as (vector, target) queries: each
+   //    vector of f adds m = min(|f'|, k/2) edges, until k were added (|f| caps it);
+   //    queries numbered in the reference's order by a scan over the edges
    const uint32_t kh = k / 2;
-   std::vector<ungx::WorkItem> items;
-   std::vector<ungx::Segment> segs;
-   std::vector<uint32_t> rows, row_items, pos;
+   UNGX_CUDA(ctx, ctx->add_qoff.ensure((nnz + 1) * sizeof(uint64_t)), "query offsets");
+   UNGX_CUDA(ctx, ctx->add_stats.ensure(4 * sizeof(unsigned long long)), "counters");
+   UNGX_CUDA(ctx, cudaMemsetAsync(ctx->add_qoff.p, 0, (nnz + 1) * sizeof(uint64_t), s), "query offsets");
+   UNGX_CUDA(ctx, cudaMemsetAsync(ctx->add_stats.p, 0, 4 * sizeof(unsigned long long), s), "counters");
+   UNGX_CUDA(ctx, ctx->scan_scratch.ensure(ungx::csr_scan_scratch_bytes((uint32_t)std::max<uint64_t>(nnz + 1, n + 1))),
+             "scan scratch");
+   uint64_t *qoff = ctx->add_qoff.as<uint64_t>();
+   unsigned long long *cnt = ctx->add_stats.as<unsigned long long>();
+   UNGX_CUDA(ctx,
+             ungx::launch_add_edge_queries(ctx->g_ranges.as<uint32_t>(), G, ctx->g_out_off.as<uint64_t>(),
+                                           ctx->g_out_ids.as<uint32_t>(), ctx->reach.as<uint8_t>(), k, qoff, cnt, s),
+             "query count kernel");
+   UNGX_CUDA(ctx, ungx::launch_exclusive_scan_u64(qoff, (uint32_t)(nnz + 1), ctx->scan_scratch.p, s), "query scan");
+   UNGX_CUDA(ctx, cudaMemcpyAsync(cnt + 2, qoff + nnz, sizeof(uint64_t), cudaMemcpyDeviceToDevice, s), "query count");
+   unsigned long long hc[3] = {0, 0, 0};
+   UNGX_CUDA(ctx, cudaMemcpyAsync(hc, cnt, sizeof(hc), cudaMemcpyDeviceToHost, s), "query count");
+   UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[6], s), "event");
+   if ((st = wait_event(ctx, ctx->ev[6], "query count")))
+      return st;
    ungx_additional_stats sx{};
-   for (uint32_t f = 1; f <= G; ++f)
-   {
-      const uint32_t qf = R[2 * f], qs = R[2 * f + 1];
-      for (uint64_t e = OO[f]; e < OO[f + 1]; ++e)
-      {
-         if (reached[e])
-            continue;
-         const uint32_t t = out_ids[e];
-         const uint32_t tsize = R[2 * t + 1] - R[2 * t];
-         ++sx.missing_group_edges;
-         const uint32_t m = std::min(tsize, kh);
-         if (m == 0)
-         {
-            sx.query_vectors += qs - qf; // the reference's loop scans every vector, adding nothing
-            continue;
-         }
-         const uint32_t q = std::min<uint32_t>(qs - qf, (k + m - 1) / m);
-         sx.query_vectors += q;
-         const uint32_t item = (uint32_t)items.size();
-         items.push_back({qf, q, (uint32_t)segs.size(), 1u});
-         segs.push_back({R[2 * t], tsize, t, 0u});
-         for (uint32_t i = 0; i < q; ++i)
-         {
-            rows.push_back(qf + i);
-            row_items.push_back(item);
-            pos.push_back((uint32_t)pos.size());
-         }
-      }
-   }
+   sx.missing_group_edges = hc[0];
+   sx.query_vectors = hc[1];
+   if (hc[2] > UINT32_MAX)
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "more than 2^32 additional-edge queries");
+   const uint32_t nq = (uint32_t)hc[2];
+   UNGX_CUDA(ctx, ctx->scan_scratch.ensure(ungx::csr_scan_scratch_bytes(std::max<uint32_t>(nq + 1u, n + 1u))),
+             "scan scratch");
    // 3. exact top-(k/2) of every query, in the reference's distance and order
-   const uint32_t nq = (uint32_t)rows.size();
-   std::vector<uint32_t> res(size_t(nq) * std::max(kh, 1u));
-   if (nq)
+   UNGX_CUDA(ctx, ctx->add_items.ensure(std::max<uint64_t>(nnz, 1) * sizeof(ungx::WorkItem)), "query plan");
+   UNGX_CUDA(ctx, ctx->add_segs.ensure(std::max<uint64_t>(nnz, 1) * sizeof(ungx::Segment)), "query plan");
+   UNGX_CUDA(ctx, ctx->add_rows.ensure(size_t(std::max(nq, 1u)) * sizeof(uint32_t)), "query plan");
+   UNGX_CUDA(ctx, ctx->add_row_items.ensure(size_t(std::max(nq, 1u)) * sizeof(uint32_t)), "query plan");
+   UNGX_CUDA(ctx, ctx->add_pos.ensure(size_t(std::max(nq, 1u)) * sizeof(uint32_t)), "query plan");
+   const size_t cap = size_t(std::max(nq, 1u)) * std::max(kh, 1u); // entries at most
+   UNGX_CUDA(ctx, ctx->add_res.ensure(cap * sizeof(uint32_t)), "query results");
+   UNGX_CUDA(ctx, ctx->add_loff.ensure((size_t(nq) + 1) * sizeof(uint64_t)), "edge offsets");
+   UNGX_CUDA(ctx, ctx->add_from.ensure(cap * sizeof(uint32_t)), "edge list");
+   UNGX_CUDA(ctx, ctx->add_to.ensure(cap * sizeof(uint32_t)), "edge list");
+   UNGX_CUDA(ctx, ctx->add_off.ensure((size_t(n) + 1) * sizeof(uint64_t)), "edge offsets");
+   UNGX_CUDA(ctx, ctx->add_cols.ensure(cap * sizeof(uint32_t)), "edge columns");
+   UNGX_CUDA(ctx, cudaMemsetAsync(ctx->add_loff.p, 0, sizeof(uint64_t), s), "edge offsets");
+   if (nq && kh)
    {
-      if ((st = upload(ctx, ctx->add_items, items, "query plan")) || (st = upload(ctx, ctx->add_segs, segs, "query plan")) ||
-          (st = upload(ctx, ctx->add_rows, rows, "query plan")) ||
-          (st = upload(ctx, ctx->add_row_items, row_items, "query plan")) ||
-          (st = upload(ctx, ctx->add_pos, pos, "query plan")))
-         return st;
-      UNGX_CUDA(ctx, ctx->add_res.ensure(res.size() * sizeof(uint32_t)), "query results");
+      UNGX_CUDA(ctx,
+                ungx::launch_add_query_fill(ctx->g_ranges.as<uint32_t>(), G, ctx->g_out_off.as<uint64_t>(),
+                                            ctx->g_out_ids.as<uint32_t>(), qoff, ctx->add_items.as<ungx::WorkItem>(),
+                                            ctx->add_segs.as<ungx::Segment>(), ctx->add_rows.as<uint32_t>(),
+                                            ctx->add_row_items.as<uint32_t>(), ctx->add_pos.as<uint32_t>(), s),
+                "query fill kernel");
       ungx::ExactParams ep{};
       ep.items = ctx->add_items.as<ungx::WorkItem>();
       ep.segs = ctx->add_segs.as<ungx::Segment>();
@@ -905,44 +907,28 @@ int ungx_additional_edges_build(ungx_context *ctx, const ungx_cross_edge_problem
       ep.out_pos = ctx->add_pos.as<uint32_t>();
       UNGX_CUDA(ctx, ungx::launch_exact(ep, std::min<uint32_t>(nq, (uint32_t)ctx->num_sms * 8), s),
                 "additional-edge kernel");
-      UNGX_CUDA(ctx, cudaMemcpyAsync(res.data(), ctx->add_res.p, res.size() * sizeof(uint32_t),
-                                     cudaMemcpyDeviceToHost, s),
-                "query results");
-      UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[6], s), "event");
-      if ((st = wait_event(ctx, ctx->ev[6], "additional edges")))
-         return st;
+      // 4. (from, to) in the reference's order, and the same edges per point
+      UNGX_CUDA(ctx,
+                ungx::launch_add_list(ctx->add_res.as<uint32_t>(), ctx->add_rows.as<uint32_t>(), nq, kh,
+                                      ctx->add_loff.as<uint64_t>(), ctx->add_from.as<uint32_t>(),
+                                      ctx->add_to.as<uint32_t>(), ctx->scan_scratch.p, s),
+                "edge list kernel");
    }
-   // 4. (from, to) in the reference's order, and the same edges per point
-   ctx->add_from.clear();
-   ctx->add_to.clear();
-   for (uint32_t i = 0; i < nq; ++i)
-      for (uint32_t r = 0; r < kh; ++r)
-      {
-         const uint32_t id = res[size_t(i) * kh + r];
-         if (id == 0xFFFFFFFFu)
-            break;
-         ctx->add_from.push_back(rows[i]);
-         ctx->add_to.push_back(id);
-      }
-   ctx->add_n = n;
-   ctx->add_point_off.assign(size_t(n) + 1, 0);
-   for (uint32_t v : ctx->add_from)
-      ++ctx->add_point_off[size_t(v) + 1];
-   for (uint32_t v = 0; v < n; ++v)
-      ctx->add_point_off[size_t(v) + 1] += ctx->add_point_off[v];
-   ctx->add_point_cols.resize(ctx->add_from.size());
-   {
-      std::vector<uint64_t> fill(ctx->add_point_off.begin(), ctx->add_point_off.end() - 1);
-      for (size_t i = 0; i < ctx->add_from.size(); ++i)
-         ctx->add_point_cols[fill[ctx->add_from[i]]++] = ctx->add_to[i];
-   }
-   if ((st = upload(ctx, ctx->add_off, ctx->add_point_off, "additional-edge CSR")) ||
-       (st = upload(ctx, ctx->add_cols, ctx->add_point_cols, "additional-edge CSR")))
-      return st;
+   UNGX_CUDA(ctx,
+             ungx::launch_add_points(ctx->g_ranges.as<uint32_t>(), nq && kh ? G : 0u, n, k,
+                                     ctx->g_out_off.as<uint64_t>(), qoff, ctx->add_loff.as<uint64_t>(),
+                                     ctx->add_to.as<uint32_t>(), ctx->add_off.as<uint64_t>(),
+                                     ctx->add_cols.as<uint32_t>(), ctx->scan_scratch.p, s),
+             "per-point edge kernel");
+   uint64_t edges = 0;
+   UNGX_CUDA(ctx, cudaMemcpyAsync(&edges, ctx->add_loff.as<uint64_t>() + nq, sizeof(uint64_t), cudaMemcpyDeviceToHost, s),
+             "edge count");
    UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[6], s), "event");
-   if ((st = wait_event(ctx, ctx->ev[6], "additional-edge CSR")))
+   if ((st = wait_event(ctx, ctx->ev[6], "additional edges")))
       return st;
-   sx.edges = ctx->add_from.size();
+   ctx->add_n = n;
+   ctx->add_edges = edges;
+   sx.edges = edges;
    sx.ms = ms_since(t0);
    if (stats)
       *stats = sx;
@@ -954,15 +940,24 @@ int ungx_additional_edges_copy(const ungx_context *ctx, uint32_t *from_ids, uint
 {
    if (!ctx)
       return UNGX_ERR_INVALID_ARG;
-   const size_t m = ctx->add_from.size();
-   if (from_ids && m)
-      std::memcpy(from_ids, ctx->add_from.data(), m * sizeof(uint32_t));
-   if (to_ids && m)
-      std::memcpy(to_ids, ctx->add_to.data(), m * sizeof(uint32_t));
-   if (point_offsets && !ctx->add_point_off.empty())
-      std::memcpy(point_offsets, ctx->add_point_off.data(), ctx->add_point_off.size() * sizeof(uint64_t));
-   if (point_cols && m)
-      std::memcpy(point_cols, ctx->add_point_cols.data(), m * sizeof(uint32_t));
+   if (cudaSetDevice(ctx->device) != cudaSuccess)
+      return UNGX_ERR_CUDA;
+   const size_t m = ctx->add_edges;
+   const struct
+   {
+      void *dst;
+      const DevBuf *src;
+      size_t bytes;
+   } parts[4] = {{from_ids, &ctx->add_from, m * sizeof(uint32_t)},
+                 {to_ids, &ctx->add_to, m * sizeof(uint32_t)},
+                 {point_offsets, &ctx->add_off, ctx->add_n ? (size_t(ctx->add_n) + 1) * sizeof(uint64_t) : 0},
+                 {point_cols, &ctx->add_cols, m * sizeof(uint32_t)}};
+   for (const auto &pt : parts)
+      if (pt.dst && pt.bytes && cudaMemcpy(pt.dst, pt.src->p, pt.bytes, cudaMemcpyDeviceToHost) != cudaSuccess)
+      {
+         ungx::set_global_error("ungx_additional_edges_copy: device to host copy failed");
+         return UNGX_ERR_CUDA;
+      }
    return UNGX_OK;
 }
 

@@ -214,6 +214,148 @@ __global__ void graph_fill_kernel(uint32_t n, uint32_t k, const uint64_t *__rest
    }
 }
 
+// ------------------------------------------------------------------ additional edges
+// The reference's loop over LNG edges f -> f' that no cross edge reaches
+// (UNG/codes/src/uni_nav_graph_cross_edges.cpp:442-596) as device passes over the edges
+// of each source group, in the reference's order (groups ascending, out-groups in
+// order, vectors ascending).  Only the first k vectors of a group can get edges.
+
+// Thread per source group: q_e queries for each unreached edge e (each vector of f adds
+// m = min(|f'|, k/2) edges, so ceil(k / m) vectors, |f| at most), 0 otherwise; the
+// reference's counters of missing edges and scanned vectors.
+__global__ void add_edge_queries_kernel(const uint32_t *__restrict__ ranges, uint32_t G,
+                                        const uint64_t *__restrict__ out_off, const uint32_t *__restrict__ out_ids,
+                                        const uint8_t *__restrict__ reached, uint32_t k, uint64_t *__restrict__ qcnt,
+                                        unsigned long long *__restrict__ stats)
+{
+   unsigned long long miss = 0, scanned = 0;
+   for (uint32_t f = blockIdx.x * blockDim.x + threadIdx.x + 1; f <= G; f += gridDim.x * blockDim.x)
+   {
+      const uint32_t fs = ranges[2 * f + 1] - ranges[2 * f];
+      for (uint64_t e = out_off[f]; e < out_off[f + 1]; ++e)
+      {
+         uint64_t q = 0;
+         if (!reached[e])
+         {
+            const uint32_t t = out_ids[e];
+            const uint32_t m = min(ranges[2 * t + 1] - ranges[2 * t], k / 2u);
+            ++miss;
+            if (m == 0)
+               scanned += fs; // the reference scans every vector of f, adding nothing
+            else
+            {
+               q = min(fs, (k + m - 1u) / m);
+               scanned += q;
+            }
+         }
+         qcnt[e] = q;
+      }
+   }
+#pragma unroll
+   for (int o = 16; o; o >>= 1)
+   {
+      miss += __shfl_xor_sync(0xffffffffu, miss, o);
+      scanned += __shfl_xor_sync(0xffffffffu, scanned, o);
+   }
+   if ((threadIdx.x & 31u) == 0 && (miss | scanned))
+   {
+      atomicAdd(&stats[0], miss);
+      atomicAdd(&stats[1], scanned);
+   }
+}
+
+// Thread per source group: edge e's queries are rows qf .. qf + q_e - 1 at qoff[e]: a
+// work item (rows, one target segment) per edge and the per-query row, item and slot.
+__global__ void add_query_fill_kernel(const uint32_t *__restrict__ ranges, uint32_t G,
+                                      const uint64_t *__restrict__ out_off, const uint32_t *__restrict__ out_ids,
+                                      const uint64_t *__restrict__ qoff, WorkItem *__restrict__ items,
+                                      Segment *__restrict__ segs, uint32_t *__restrict__ rows,
+                                      uint32_t *__restrict__ row_items, uint32_t *__restrict__ pos)
+{
+   for (uint32_t f = blockIdx.x * blockDim.x + threadIdx.x + 1; f <= G; f += gridDim.x * blockDim.x)
+   {
+      const uint32_t qf = ranges[2 * f];
+      for (uint64_t e = out_off[f]; e < out_off[f + 1]; ++e)
+      {
+         const uint32_t q = uint32_t(qoff[e + 1] - qoff[e]);
+         if (q == 0)
+            continue;
+         const uint32_t t = out_ids[e];
+         items[e] = {qf, q, uint32_t(e), 1u};
+         segs[e] = {ranges[2 * t], ranges[2 * t + 1] - ranges[2 * t], t, 0u};
+         for (uint32_t i = 0; i < q; ++i)
+         {
+            const uint32_t w = uint32_t(qoff[e]) + i;
+            rows[w] = qf + i;
+            row_items[w] = uint32_t(e);
+            pos[w] = w;
+         }
+      }
+   }
+}
+
+// Per query: the entries of its top-(k/2) before the first empty slot.
+__global__ void add_count_kernel(const uint32_t *__restrict__ res, uint32_t nq, uint32_t kh, uint64_t *__restrict__ lcnt)
+{
+   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < nq; i += gridDim.x * blockDim.x)
+   {
+      uint32_t c = 0;
+      while (c < kh && res[size_t(i) * kh + c] != 0xFFFFFFFFu)
+         ++c;
+      lcnt[i] = c;
+   }
+}
+
+// Per query: its entries into the (from, to) list at loff[i].
+__global__ void add_list_kernel(const uint32_t *__restrict__ res, const uint32_t *__restrict__ rows, uint32_t nq,
+                                uint32_t kh, const uint64_t *__restrict__ loff, uint32_t *__restrict__ from,
+                                uint32_t *__restrict__ to)
+{
+   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < nq; i += gridDim.x * blockDim.x)
+   {
+      const uint64_t a = loff[i], c = loff[i + 1] - a;
+      for (uint32_t r = 0; r < c; ++r)
+      {
+         from[a + r] = rows[i];
+         to[a + r] = res[size_t(i) * kh + r];
+      }
+   }
+}
+
+// Thread per (source group f, vector t < k): vector v = qf + t's entries over f's edges
+// in order.  COUNT: their number into deg[v]; else: the entries at off[v].
+template <bool COUNT>
+__global__ void add_point_kernel(const uint32_t *__restrict__ ranges, uint32_t G, uint32_t k,
+                                 const uint64_t *__restrict__ out_off, const uint64_t *__restrict__ qoff,
+                                 const uint64_t *__restrict__ loff, const uint32_t *__restrict__ to,
+                                 uint64_t *__restrict__ deg_or_off, uint32_t *__restrict__ cols)
+{
+   const uint64_t total = uint64_t(G) * k;
+   for (uint64_t idx = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+        idx += uint64_t(gridDim.x) * blockDim.x)
+   {
+      const uint32_t f = uint32_t(idx / k) + 1u, t = uint32_t(idx % k);
+      const uint32_t qf = ranges[2 * f];
+      if (t >= ranges[2 * f + 1] - qf)
+         continue;
+      const uint32_t v = qf + t;
+      uint64_t c = 0, w = COUNT ? 0 : deg_or_off[v];
+      for (uint64_t e = out_off[f]; e < out_off[f + 1]; ++e)
+      {
+         if (qoff[e + 1] - qoff[e] <= t)
+            continue;
+         const uint64_t i = qoff[e] + t;
+         if (COUNT)
+            c += loff[i + 1] - loff[i];
+         else
+            for (uint64_t j = loff[i]; j < loff[i + 1]; ++j)
+               cols[w++] = to[j];
+      }
+      if (COUNT)
+         deg_or_off[v] = c;
+   }
+}
+
 uint32_t grid_for(uint64_t work, uint32_t threads)
 {
    const uint64_t g = (work + threads - 1) / threads;
@@ -259,6 +401,57 @@ cudaError_t launch_exclusive_scan_u64(uint64_t *data, uint32_t count, void *scra
    scan_tiles_kernel<<<tiles, kScanThreads, 0, s>>>(data, count, sums);
    scan_sums_kernel<<<1, 1024, 0, s>>>(sums, tiles);
    scan_add_kernel<<<tiles, 256, 0, s>>>(data, count, sums);
+   return cudaGetLastError();
+}
+
+cudaError_t launch_add_edge_queries(const uint32_t *ranges, uint32_t G, const uint64_t *out_off, const uint32_t *out_ids,
+                                    const uint8_t *reached, uint32_t k, uint64_t *qcnt, unsigned long long *stats,
+                                    cudaStream_t s)
+{
+   if (G == 0)
+      return cudaSuccess;
+   add_edge_queries_kernel<<<grid_for(G, 128), 128, 0, s>>>(ranges, G, out_off, out_ids, reached, k, qcnt, stats);
+   return cudaGetLastError();
+}
+
+cudaError_t launch_add_query_fill(const uint32_t *ranges, uint32_t G, const uint64_t *out_off, const uint32_t *out_ids,
+                                  const uint64_t *qoff, WorkItem *items, Segment *segs, uint32_t *rows,
+                                  uint32_t *row_items, uint32_t *pos, cudaStream_t s)
+{
+   if (G == 0)
+      return cudaSuccess;
+   add_query_fill_kernel<<<grid_for(G, 128), 128, 0, s>>>(ranges, G, out_off, out_ids, qoff, items, segs, rows,
+                                                          row_items, pos);
+   return cudaGetLastError();
+}
+
+cudaError_t launch_add_list(const uint32_t *res, const uint32_t *rows, uint32_t nq, uint32_t kh, uint64_t *loff,
+                            uint32_t *from, uint32_t *to, void *scratch, cudaStream_t s)
+{
+   if (nq == 0)
+      return cudaSuccess;
+   add_count_kernel<<<grid_for(nq, 256), 256, 0, s>>>(res, nq, kh, loff);
+   cudaError_t e = cudaMemsetAsync(loff + nq, 0, sizeof(uint64_t), s);
+   if (e == cudaSuccess)
+      e = launch_exclusive_scan_u64(loff, nq + 1, scratch, s);
+   if (e != cudaSuccess)
+      return e;
+   add_list_kernel<<<grid_for(nq, 256), 256, 0, s>>>(res, rows, nq, kh, loff, from, to);
+   return cudaGetLastError();
+}
+
+cudaError_t launch_add_points(const uint32_t *ranges, uint32_t G, uint32_t n, uint32_t k, const uint64_t *out_off,
+                              const uint64_t *qoff, const uint64_t *loff, const uint32_t *to, uint64_t *off,
+                              uint32_t *cols, void *scratch, cudaStream_t s)
+{
+   cudaError_t e = cudaMemsetAsync(off, 0, (size_t(n) + 1) * sizeof(uint64_t), s);
+   if (e != cudaSuccess || G == 0)
+      return e;
+   const uint32_t grid = grid_for(uint64_t(G) * k, 256);
+   add_point_kernel<true><<<grid, 256, 0, s>>>(ranges, G, k, out_off, qoff, loff, to, off, cols);
+   if ((e = launch_exclusive_scan_u64(off, n + 1, scratch, s)) != cudaSuccess)
+      return e;
+   add_point_kernel<false><<<grid, 256, 0, s>>>(ranges, G, k, out_off, qoff, loff, to, off, cols);
    return cudaGetLastError();
 }
 

@@ -164,6 +164,23 @@ size_t csr_scan_scratch_bytes(uint32_t n);
 cudaError_t launch_graph_degrees(uint32_t n, uint32_t k, const uint64_t *intra_off, const uint32_t *cross_ids,
                                  const uint64_t *add_off, uint64_t *offsets, cudaStream_t s);
 cudaError_t launch_exclusive_scan_u64(uint64_t *data, uint32_t count, void *scratch, cudaStream_t s);
+// Additional edges (the reference's rule for unreached LNG edges), device passes:
+// per edge its query count into qcnt[nnz] and the counters stats[0] (missing edges),
+// stats[1] (vectors the reference scans); after an exclusive scan of qcnt into qoff,
+// the work items / segments (indexed by edge) and per query its row, item and slot;
+// after the exact top-(k/2), the (from, to) list at loff (nq + 1 entries, scanned
+// here); the same edges per point: off[n + 1] and cols.
+cudaError_t launch_add_edge_queries(const uint32_t *ranges, uint32_t G, const uint64_t *out_off, const uint32_t *out_ids,
+                                    const uint8_t *reached, uint32_t k, uint64_t *qcnt, unsigned long long *stats,
+                                    cudaStream_t s);
+cudaError_t launch_add_query_fill(const uint32_t *ranges, uint32_t G, const uint64_t *out_off, const uint32_t *out_ids,
+                                  const uint64_t *qoff, WorkItem *items, Segment *segs, uint32_t *rows,
+                                  uint32_t *row_items, uint32_t *pos, cudaStream_t s);
+cudaError_t launch_add_list(const uint32_t *res, const uint32_t *rows, uint32_t nq, uint32_t kh, uint64_t *loff,
+                            uint32_t *from, uint32_t *to, void *scratch, cudaStream_t s);
+cudaError_t launch_add_points(const uint32_t *ranges, uint32_t G, uint32_t n, uint32_t k, const uint64_t *out_off,
+                              const uint64_t *qoff, const uint64_t *loff, const uint32_t *to, uint64_t *off,
+                              uint32_t *cols, void *scratch, cudaStream_t s);
 cudaError_t launch_graph_fill(uint32_t n, uint32_t k, const uint64_t *intra_off, const uint32_t *intra_cols,
                               const uint32_t *cross_ids, const uint64_t *add_off, const uint32_t *add_cols,
                               const uint64_t *offsets, uint32_t *cols, cudaStream_t s);
