@@ -12,6 +12,7 @@
 
 #include <algorithm>
 #include <chrono>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <string>
@@ -115,7 +116,7 @@ struct ungx_context
    // additional edges and graph emission
    DevBuf g_ranges, g_out_off, g_out_ids, group_of, reach, add_items, add_segs, add_rows, add_row_items, add_pos,
        add_res, add_off, add_cols, add_qoff, add_loff, add_from, add_to, add_stats, scan_scratch, knn_ranges, knn_base,
-       knn_tasks;
+       knn_tasks, knn_dist, knn_dbase, knn_tiles, knn_rows;
    uint32_t add_n = 0;     // points of the last additional-edge build
    uint64_t add_edges = 0; // its edges
    uint32_t *h_counters = nullptr; // pinned
@@ -516,7 +517,8 @@ int ungx_context_destroy(ungx_context *ctx)
                      &ctx->add_items, &ctx->add_segs, &ctx->add_rows, &ctx->add_row_items, &ctx->add_pos,
                      &ctx->add_res, &ctx->add_off, &ctx->add_cols, &ctx->add_qoff, &ctx->add_loff, &ctx->add_from,
                      &ctx->add_to, &ctx->add_stats, &ctx->scan_scratch, &ctx->knn_ranges,
-                     &ctx->knn_base, &ctx->knn_tasks})
+                     &ctx->knn_base, &ctx->knn_tasks, &ctx->knn_dist, &ctx->knn_dbase, &ctx->knn_tiles,
+                     &ctx->knn_rows})
       b->release();
    ctx->host_stage.release();
    for (auto &ev : ctx->ev)
@@ -1043,12 +1045,8 @@ int ungx_exact_knn_graph_device(ungx_context *ctx, uint32_t num_groups, const ui
    UNGX_CUDA(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
    if (num_groups == 0)
       return UNGX_OK;
-   const size_t ntask = ungx::knn_task_count(ranges.data(), num_groups);
-   std::vector<uint32_t> tasks(2 * std::max<size_t>(ntask, 1));
-   ungx::knn_tasks(ranges.data(), num_groups, tasks.data());
    int st;
-   if ((st = upload(ctx, ctx->knn_ranges, ranges, "kNN upload")) || (st = upload(ctx, ctx->knn_base, base, "kNN upload")) ||
-       (st = upload(ctx, ctx->knn_tasks, tasks, "kNN upload")))
+   if ((st = upload(ctx, ctx->knn_ranges, ranges, "kNN upload")) || (st = upload(ctx, ctx->knn_base, base, "kNN upload")))
       return st;
    cudaStream_t us = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
    cudaStream_t s = ctx->stream;
@@ -1072,8 +1070,86 @@ int ungx_exact_knn_graph_device(ungx_context *ctx, uint32_t num_groups, const ui
    kp.graph_stride = cfg->graph_stride;
    kp.graph = d_graph;
    kp.entry_points = d_entry_points;
+   uint32_t max_n = 0;
+   for (uint32_t g = 0; g < num_groups; ++g)
+      max_n = std::max(max_n, ranges[2 * g + 1] - ranges[2 * g]);
+   // limits of the two-phase path; the environment may lower them (tests reach the
+   // fused kernel and several batches with small groups that way)
+   auto env_u64 = [](const char *name, uint64_t def) {
+      const char *v = std::getenv(name);
+      return v && *v ? std::strtoull(v, nullptr, 10) : def;
+   };
+   const uint64_t dist_max_n = env_u64("UNGX_KNN_DIST_MAX_N", ungx::kKnnDistMaxN);
+   const uint64_t batch_entries = std::max<uint64_t>(1, env_u64("UNGX_KNN_BATCH_ENTRIES", ungx::kKnnDistBatch));
    UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[0], s), "event");
-   UNGX_CUDA(ctx, ungx::launch_exact_knn(kp, ctx->knn_tasks.as<uint32_t>(), (uint32_t)ntask, s), "kNN kernel launch");
+   if (max_n > std::min<uint64_t>(dist_max_n, ungx::kKnnDistMaxN))
+   {
+      // fused kernel: one block per 64 rows of a group, every candidate of the group
+      const size_t ntask = ungx::knn_task_count(ranges.data(), num_groups);
+      std::vector<uint32_t> tasks(2 * std::max<size_t>(ntask, 1));
+      ungx::knn_tasks(ranges.data(), num_groups, tasks.data());
+      if ((st = upload(ctx, ctx->knn_tasks, tasks, "kNN upload")))
+         return st;
+      UNGX_CUDA(ctx, ungx::launch_exact_knn(kp, ctx->knn_tasks.as<uint32_t>(), (uint32_t)ntask, s),
+                "kNN kernel launch");
+   }
+   else
+   {
+      // two-phase path, groups in batches of at most kKnnDistBatch matrix entries (a
+      // batch restarts the matrix offsets at 0): the tiles on and above each group's
+      // diagonal, then its rows in pieces of 32
+      std::vector<uint64_t> dbase(num_groups, 0);
+      std::vector<uint32_t> batch_end;
+      uint64_t dmax = 0;
+      for (uint32_t g0 = 0; g0 < num_groups;)
+      {
+         uint64_t used = 0;
+         uint32_t g1 = g0;
+         for (; g1 < num_groups; ++g1)
+         {
+            const uint64_t n = ranges[2 * g1 + 1] - ranges[2 * g1];
+            if (g1 > g0 && used + n * n > batch_entries)
+               break;
+            dbase[g1] = used;
+            used += n * n;
+         }
+         dmax = std::max(dmax, used);
+         batch_end.push_back(g1);
+         g0 = g1;
+      }
+      UNGX_CUDA(ctx, ctx->knn_dist.ensure(std::max<uint64_t>(dmax, 1) * sizeof(float)), "kNN distance matrix");
+      if ((st = upload(ctx, ctx->knn_dbase, dbase, "kNN upload")))
+         return st;
+      kp.dist = ctx->knn_dist.as<float>();
+      kp.dbase = ctx->knn_dbase.as<uint64_t>();
+      std::vector<uint32_t> tiles, rowt;
+      uint32_t g0 = 0;
+      for (const uint32_t g1 : batch_end)
+      {
+         tiles.clear();
+         rowt.clear();
+         for (uint32_t g = g0; g < g1; ++g)
+         {
+            const uint32_t n = ranges[2 * g + 1] - ranges[2 * g];
+            const uint32_t T = (n + 63) / 64;
+            for (uint32_t bi = 0; bi < T; ++bi)
+               for (uint32_t bj = bi; bj < T; ++bj)
+                  tiles.insert(tiles.end(), {g, bi, bj});
+            for (uint32_t r = 0; r < n; r += 32)
+               rowt.insert(rowt.end(), {g, r});
+         }
+         // the previous batch's kernels are done with the task lists and the matrix
+         UNGX_CUDA(ctx, cudaStreamSynchronize(s), "kNN batch");
+         if ((st = upload(ctx, ctx->knn_tiles, tiles, "kNN upload")) ||
+             (st = upload(ctx, ctx->knn_rows, rowt, "kNN upload")))
+            return st;
+         UNGX_CUDA(ctx,
+                   ungx::launch_knn_two_phase(kp, ctx->knn_tiles.as<uint32_t>(), (uint32_t)(tiles.size() / 3),
+                                              ctx->knn_rows.as<uint32_t>(), (uint32_t)(rowt.size() / 2), s),
+                   "kNN kernel launch");
+         g0 = g1;
+      }
+   }
    UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[1], s), "event");
    if ((st = wait_event(ctx, ctx->ev[1], "exact kNN seeding")))
       return st;

@@ -142,12 +142,23 @@ struct KnnParams
    uint32_t candidate_k, final_degree, head_keep, anchor_tail, anchor_slots, bidir_anchor, graph_stride;
    uint32_t *graph;            // [points x graph_stride]
    uint32_t *entry_points;     // [groups] or NULL
+   float *dist;                // two-phase path: the groups' distance matrices, [n_g x n_g] each
+   const uint64_t *dbase;      // [groups]: offset of group g's matrix in dist
 };
 constexpr uint32_t kKnnMaxDim = 352; // both 64-row tiles hold every dimension in shared memory
+// Groups of at most kKnnDistMaxN points take the two-phase path (symmetric distance
+// matrix, then a warp per row), in batches of at most kKnnDistBatch matrix entries;
+// a call with a larger group takes the fused kernel (one block per 64 rows).
+constexpr uint32_t kKnnDistMaxN = 8192;
+constexpr uint64_t kKnnDistBatch = 1ull << 30;
 size_t knn_smem_bytes(uint32_t d);
 size_t knn_task_count(const uint32_t *ranges, uint32_t num_groups);
 void knn_tasks(const uint32_t *ranges, uint32_t num_groups, uint32_t *tasks); // [2 * count]: (group, first row)
 cudaError_t launch_exact_knn(const KnnParams &p, const uint32_t *d_tasks, uint32_t num_tasks, cudaStream_t s);
+// Two-phase path: tiles [3 * num_tiles] = (group, row tile, column tile >= row tile) of
+// 64 x 64; rows [2 * num_rows] = (group, first row) of 32-row pieces.
+cudaError_t launch_knn_two_phase(const KnnParams &p, const uint32_t *d_tiles, uint32_t num_tiles,
+                                 const uint32_t *d_rows, uint32_t num_rows, cudaStream_t s);
 
 // ---- graph assembly (graph.cu)
 // group_of[v] = group of row v (1..G), G + 1 for rows outside every group.

@@ -133,6 +133,71 @@ __device__ __forceinline__ void warp_tree(float (&out)[8], const float *sq, cons
       out[i] = add_ftz(a[i], b[i]);
 }
 
+// One output row: [degree, head, ring anchors, tail, dedupe tail], padded with the point
+// itself (the reference's layout of batched_exact_knn_graph_kernel's epilogue).
+__device__ void write_row(const KnnParams &p, uint32_t group, uint32_t n, uint32_t s, uint32_t cand,
+                          const uint32_t *top)
+{
+   uint32_t *row = p.graph + size_t(p.base[group] + s) * p.graph_stride;
+   const uint32_t out_degree = min(p.final_degree, cand);
+   row[0] = out_degree;
+   uint32_t write = 0;
+   if (out_degree > 0)
+   {
+      const uint32_t near_limit = min(out_degree, min(p.head_keep, p.final_degree));
+      for (; write < near_limit; ++write)
+         row[1 + write] = top[write];
+      const uint32_t remaining = p.final_degree > write ? p.final_degree - write : 0;
+      const uint32_t anchor_limit =
+          p.anchor_tail ? (p.anchor_slots == 0 ? remaining : min(p.anchor_slots, remaining)) : 0;
+      if (anchor_limit > 0 && n > 1)
+         for (uint32_t t = 0; t < anchor_limit && write < out_degree; ++t)
+         {
+            const uint32_t hop = max(1u, uint32_t((uint64_t(t + 1) * n) / (anchor_limit + 1)));
+            const bool backward = p.bidir_anchor && (t & 1u);
+            uint32_t c = backward ? (s + n - (hop % n)) % n : (s + hop) % n;
+            for (uint32_t retry = 0; retry < n && write < out_degree;
+                 ++retry, c = backward ? (c + n - 1) % n : (c + 1) % n)
+            {
+               if (c == s)
+                  continue;
+               bool dup = false;
+               for (uint32_t q = 0; q < write; ++q)
+                  if (row[1 + q] == c)
+                  {
+                     dup = true;
+                     break;
+                  }
+               if (!dup)
+               {
+                  row[1 + write++] = c;
+                  break;
+               }
+            }
+         }
+      const uint32_t tail_start = near_limit;
+      const uint32_t tail_count = cand > tail_start ? cand - tail_start : 0;
+      const uint32_t step = tail_count > remaining && remaining > 0 ? (tail_count + remaining - 1) / remaining : 1;
+      for (uint32_t sc = tail_start; sc < cand && write < out_degree; sc += step)
+         row[1 + write++] = top[sc];
+      for (uint32_t sc = tail_start; sc < cand && write < out_degree; ++sc)
+      {
+         const uint32_t c = top[sc];
+         bool dup = false;
+         for (uint32_t q = 0; q < write; ++q)
+            if (row[1 + q] == c)
+            {
+               dup = true;
+               break;
+            }
+         if (!dup)
+            row[1 + write++] = c;
+      }
+   }
+   for (uint32_t j = out_degree; j + 1 < p.graph_stride; ++j)
+      row[1 + j] = s;
+}
+
 struct KnnTask
 {
    uint32_t group, row0;
@@ -297,69 +362,194 @@ __global__ void __launch_bounds__(kKnnThreads) exact_knn_kernel(const KnnParams 
    __syncthreads();
    // the row layout: head, ring anchors, tail, padding with the point itself
    if (tid < uint32_t(kKnnRows) && task.row0 + tid < n)
-   {
-      const uint32_t s = task.row0 + tid;
-      const uint32_t *top = li + tid * kLl;
-      uint32_t *row = p.graph + size_t(p.base[task.group] + s) * p.graph_stride;
-      const uint32_t out_degree = min(p.final_degree, cand);
-      row[0] = out_degree;
-      uint32_t write = 0;
-      if (out_degree > 0)
+      write_row(p, task.group, n, task.row0 + tid, cand, li + tid * kLl);
+}
+
+// ------------------------------------------------------------------ two-phase path
+// The reference's block distance is symmetric bit for bit: swapping the two points
+// negates every difference (exact in IEEE arithmetic, flush-to-zero included) and
+// fma(-x, -x, acc) == fma(x, x, acc), so the leaves, the tree and the sum are the same.
+// Phase 1 therefore evaluates only the 64 x 64 tiles on and above the diagonal of each
+// group's distance matrix and writes every value at (i, j) and (j, i); phase 2 gives
+// each row to a warp, which scans the row in ascending candidate order with the
+// reference's insert.
+
+struct KnnTile
+{
+   uint32_t group, bi, bj; // rows 64 bi .., columns 64 bj .., bj >= bi
+};
+
+__global__ void __launch_bounds__(kKnnThreads) knn_dist_kernel(const KnnParams p, const KnnTile *__restrict__ tiles)
+{
+   extern __shared__ float smem_f[];
+   float *sq = smem_f;                          // [d][64] source rows
+   float *sx = sq + size_t(p.dpad) * kKnnRows;  // [d][32] candidates
+   float *sd = sx + size_t(p.dpad) * kKnnCands; // [64][33] distances of the step
+   const KnnTile task = tiles[blockIdx.x];
+   const uint32_t first = p.ranges[2 * task.group], n = p.ranges[2 * task.group + 1] - first;
+   const uint32_t row0 = task.bi * kKnnRows, col0 = task.bj * kKnnRows;
+   float *D = p.dist + p.dbase[task.group]; // [n][n]
+   const uint32_t tid = threadIdx.x;
+   const bool vec4 = (p.d & 3u) == 0;
+   if (vec4)
+      for (uint32_t idx = tid; idx < uint32_t(kKnnRows) * (p.dpad / 4u); idx += kKnnThreads)
       {
-         const uint32_t near_limit = min(out_degree, min(p.head_keep, p.final_degree));
-         for (; write < near_limit; ++write)
-            row[1 + write] = top[write];
-         const uint32_t remaining = p.final_degree > write ? p.final_degree - write : 0;
-         const uint32_t anchor_limit =
-             p.anchor_tail ? (p.anchor_slots == 0 ? remaining : min(p.anchor_slots, remaining)) : 0;
-         if (anchor_limit > 0 && n > 1)
-            for (uint32_t t = 0; t < anchor_limit && write < out_degree; ++t)
-            {
-               const uint32_t hop = max(1u, uint32_t((uint64_t(t + 1) * n) / (anchor_limit + 1)));
-               const bool backward = p.bidir_anchor && (t & 1u);
-               uint32_t c = backward ? (s + n - (hop % n)) % n : (s + hop) % n;
-               for (uint32_t retry = 0; retry < n && write < out_degree;
-                    ++retry, c = backward ? (c + n - 1) % n : (c + 1) % n)
-               {
-                  if (c == s)
-                     continue;
-                  bool dup = false;
-                  for (uint32_t q = 0; q < write; ++q)
-                     if (row[1 + q] == c)
-                     {
-                        dup = true;
-                        break;
-                     }
-                  if (!dup)
-                  {
-                     row[1 + write++] = c;
-                     break;
-                  }
-               }
-            }
-         const uint32_t tail_start = near_limit;
-         const uint32_t tail_count = cand > tail_start ? cand - tail_start : 0;
-         const uint32_t step = tail_count > remaining && remaining > 0 ? (tail_count + remaining - 1) / remaining : 1;
-         for (uint32_t sc = tail_start; sc < cand && write < out_degree; sc += step)
-            row[1 + write++] = top[sc];
-         for (uint32_t sc = tail_start; sc < cand && write < out_degree; ++sc)
+         const uint32_t r = idx % kKnnRows, d4 = idx / kKnnRows, row = row0 + r;
+         const float4 v = row < n ? __ldg(reinterpret_cast<const float4 *>(p.X + size_t(first + row) * p.d) + d4)
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+         sq[(4 * d4 + 0) * kKnnRows + r] = v.x;
+         sq[(4 * d4 + 1) * kKnnRows + r] = v.y;
+         sq[(4 * d4 + 2) * kKnnRows + r] = v.z;
+         sq[(4 * d4 + 3) * kKnnRows + r] = v.w;
+      }
+   else
+      for (uint32_t idx = tid; idx < uint32_t(kKnnRows) * p.dpad; idx += kKnnThreads)
+      {
+         const uint32_t r = idx % kKnnRows, dim = idx / kKnnRows, row = row0 + r;
+         sq[dim * kKnnRows + r] = (row < n && dim < p.d) ? p.X[size_t(first + row) * p.d + dim] : 0.0f;
+      }
+   const int r0 = int(tid / 16u) * 4, c0 = int(tid % 16u) * 2;
+   for (uint32_t step = 0; step < 2; ++step)
+   {
+      const uint32_t x0 = col0 + step * kKnnCands;
+      if (x0 >= n)
+         break;
+      __syncthreads(); // the previous step's candidates and distances are consumed
+      if (vec4)
+         for (uint32_t idx = tid; idx < uint32_t(kKnnCands) * (p.dpad / 4u); idx += kKnnThreads)
          {
-            const uint32_t c = top[sc];
-            bool dup = false;
-            for (uint32_t q = 0; q < write; ++q)
-               if (row[1 + q] == c)
-               {
-                  dup = true;
-                  break;
-               }
-            if (!dup)
-               row[1 + write++] = c;
+            const uint32_t c = idx % kKnnCands, d4 = idx / kKnnCands, x = x0 + c;
+            const float4 v = x < n ? __ldg(reinterpret_cast<const float4 *>(p.X + size_t(first + x) * p.d) + d4)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+            sx[(4 * d4 + 0) * kKnnCands + c] = v.x;
+            sx[(4 * d4 + 1) * kKnnCands + c] = v.y;
+            sx[(4 * d4 + 2) * kKnnCands + c] = v.z;
+            sx[(4 * d4 + 3) * kKnnCands + c] = v.w;
+         }
+      else
+         for (uint32_t idx = tid; idx < uint32_t(kKnnCands) * p.dpad; idx += kKnnThreads)
+         {
+            const uint32_t c = idx % kKnnCands, dim = idx / kKnnCands, x = x0 + c;
+            sx[dim * kKnnCands + c] = (x < n && dim < p.d) ? p.X[size_t(first + x) * p.d + dim] : 0.0f;
+         }
+      __syncthreads();
+      float s02[8], s13[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+         s02[i] = s13[i] = 0.0f;
+      const int nj = int(min(p.d, 128u) + 31u) / 32;
+#pragma unroll 1
+      for (int j = 0; j < nj; ++j)
+      {
+         float w[8];
+         warp_tree(w, sq, sx, j, p.d, r0, c0);
+#pragma unroll
+         for (int i = 0; i < 8; ++i)
+         {
+            if (j == 0)
+               s02[i] = w[i];
+            else if (j == 1)
+               s13[i] = w[i];
+            else if (j == 2)
+               s02[i] = add_ftz(s02[i], w[i]);
+            else
+               s13[i] = add_ftz(s13[i], w[i]);
          }
       }
-      for (uint32_t j = out_degree; j + 1 < p.graph_stride; ++j)
-         row[1 + j] = s;
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+         for (int b = 0; b < 2; ++b)
+            sd[(r0 + a) * kLd + c0 + b] = add_ftz(s02[a * 2 + b], s13[a * 2 + b]);
+      __syncthreads();
+      // (i, j): 32-column row pieces; (j, i) off the diagonal: 64-row column pieces
+      for (uint32_t idx = tid; idx < uint32_t(kKnnRows) * kKnnCands; idx += kKnnThreads)
+      {
+         const uint32_t r = idx / kKnnCands, c = idx % kKnnCands, row = row0 + r, col = x0 + c;
+         if (row < n && col < n)
+            D[size_t(row) * n + col] = sd[r * kLd + c];
+      }
+      if (task.bi != task.bj)
+         for (uint32_t idx = tid; idx < uint32_t(kKnnRows) * kKnnCands; idx += kKnnThreads)
+         {
+            const uint32_t r = idx % kKnnRows, c = idx / kKnnRows, row = row0 + r, col = x0 + c;
+            if (row < n && col < n)
+               D[size_t(col) * n + row] = sd[r * kLd + c];
+         }
    }
 }
+
+constexpr int kRowWarps = 4; // warps per block of the row pass, 32 rows each
+
+// Phase 2: a warp per 32 rows of a group.  Each row's list (lane l: entries l and
+// l + 32) takes the row's candidates in ascending order; then every lane lays out one
+// of the warp's rows (head, ring anchors, tail, padding with the point itself).
+__global__ void __launch_bounds__(kRowWarps * 32) knn_rows_kernel(const KnnParams p, const KnnTask *__restrict__ tasks,
+                                                                   uint32_t num_tasks)
+{
+   __shared__ uint32_t s_top[kRowWarps][32][kKnnMax];
+   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+   const uint32_t ti = blockIdx.x * kRowWarps + warp;
+   if (ti >= num_tasks)
+      return;
+   const KnnTask task = tasks[ti];
+   const uint32_t first = p.ranges[2 * task.group], n = p.ranges[2 * task.group + 1] - first;
+   uint32_t cand = p.candidate_k > 0 ? p.candidate_k - 1 : 0;
+   cand = min(cand, uint32_t(kKnnMax));
+   cand = min(cand, n > 0 ? n - 1 : 0u);
+   if (task.row0 == 0 && lane == 0 && p.entry_points)
+      p.entry_points[task.group] = 0;
+   const float *D = p.dist + p.dbase[task.group];
+   const uint32_t lc = cand > 0 ? (cand - 1u) & 31u : 0u;
+   for (uint32_t rr = 0; rr < 32u && task.row0 + rr < n; ++rr)
+   {
+      const uint32_t s = task.row0 + rr;
+      float e0 = FLT_MAX, e1 = FLT_MAX;
+      uint32_t i0 = 0xFFFFFFFFu, i1 = 0xFFFFFFFFu;
+      if (cand > 0)
+         for (uint32_t x0 = 0; x0 < n; x0 += 32u)
+         {
+            const uint32_t x = x0 + lane;
+            const float dist = x < n ? D[size_t(s) * n + x] : FLT_MAX;
+            const float last0 = __shfl_sync(0xffffffffu, cand > 32u ? e1 : e0, lc);
+            uint32_t m = __ballot_sync(0xffffffffu, x < n && x != s && dist < last0);
+            while (m)
+            {
+               const uint32_t b = __ffs(m) - 1u;
+               m &= m - 1u;
+               const float nd = __shfl_sync(0xffffffffu, dist, b);
+               const float last = __shfl_sync(0xffffffffu, cand > 32u ? e1 : e0, lc);
+               if (!(nd < last))
+                  continue;
+               const uint32_t pos = __popc(__ballot_sync(0xffffffffu, lane < cand && e0 <= nd)) +
+                                    __popc(__ballot_sync(0xffffffffu, lane + 32u < cand && e1 <= nd));
+               const float u0 = __shfl_up_sync(0xffffffffu, e0, 1), u1 = __shfl_up_sync(0xffffffffu, e1, 1);
+               const uint32_t v0 = __shfl_up_sync(0xffffffffu, i0, 1), v1 = __shfl_up_sync(0xffffffffu, i1, 1);
+               const float t31 = __shfl_sync(0xffffffffu, e0, 31);
+               const uint32_t j31 = __shfl_sync(0xffffffffu, i0, 31);
+               const float p1 = lane ? u1 : t31;
+               const uint32_t q1 = lane ? v1 : j31;
+               const uint32_t nid = x0 + b;
+               if (lane >= pos)
+               {
+                  e0 = lane == pos ? nd : u0;
+                  i0 = lane == pos ? nid : v0;
+               }
+               if (lane + 32u >= pos)
+               {
+                  e1 = lane + 32u == pos ? nd : p1;
+                  i1 = lane + 32u == pos ? nid : q1;
+               }
+            }
+         }
+      s_top[warp][rr][lane] = i0;
+      s_top[warp][rr][32u + lane] = i1;
+   }
+   __syncwarp();
+   if (task.row0 + lane < n)
+      write_row(p, task.group, n, task.row0 + lane, cand, s_top[warp][lane]);
+}
+
 } // namespace
 
 size_t knn_smem_bytes(uint32_t d)
@@ -397,6 +587,26 @@ cudaError_t launch_exact_knn(const KnnParams &p, const uint32_t *d_tasks, uint32
    if (e != cudaSuccess)
       return e;
    exact_knn_kernel<<<num_tasks, kKnnThreads, smem, s>>>(p, reinterpret_cast<const KnnTask *>(d_tasks));
+   return cudaGetLastError();
+}
+
+cudaError_t launch_knn_two_phase(const KnnParams &p, const uint32_t *d_tiles, uint32_t num_tiles,
+                                 const uint32_t *d_rows, uint32_t num_rows, cudaStream_t s)
+{
+   if (num_tiles)
+   {
+      const uint32_t dpad = (p.d + 3) / 4 * 4;
+      const size_t smem = (size_t(dpad) * (kKnnRows + kKnnCands) + kKnnRows * kLd) * sizeof(float);
+      cudaError_t e = cudaFuncSetAttribute(knn_dist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess)
+         return e;
+      knn_dist_kernel<<<num_tiles, kKnnThreads, smem, s>>>(p, reinterpret_cast<const KnnTile *>(d_tiles));
+      if ((e = cudaGetLastError()) != cudaSuccess)
+         return e;
+   }
+   if (num_rows)
+      knn_rows_kernel<<<(num_rows + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, s>>>(
+          p, reinterpret_cast<const KnnTask *>(d_rows), num_rows);
    return cudaGetLastError();
 }
 

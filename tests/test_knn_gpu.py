@@ -80,3 +80,16 @@ def test_dimension_limit_is_refused(ctx):
     with pytest.raises(nat.UngxError):
         ctx.exact_knn_graph_device(np.array([0, 10], dtype=np.uint32), cfg, d_graph.data_ptr())
     ctx.release_base_vectors()
+
+
+# The two-phase path in many batches (every group in its own batch) and the fused
+# kernel (taken for groups above the two-phase limit) give the same rows.
+PATHS = {"batched": ("UNGX_KNN_BATCH_ENTRIES", "20000"), "fused": ("UNGX_KNN_DIST_MAX_N", "0")}
+
+
+@pytest.mark.parametrize("d", [13, 128])
+@pytest.mark.parametrize("name", ["default", "small_k"])
+@pytest.mark.parametrize("path", list(PATHS))
+def test_exact_knn_paths_match_oracle(ctx, monkeypatch, d, name, path):
+    monkeypatch.setenv(*PATHS[path])
+    test_exact_knn_graph_matches_oracle(ctx, d, name)
