@@ -108,7 +108,8 @@ struct ungx_context
    DevBuf X_owned, Xh, xnorm, mean, sums, range, scale; // Xh: fp16 operand [n x dp]
    uint32_t n = 0, d = 0, dp = 0;
    // per-call scratch
-   DevBuf items, segs, empties, ranges, gmax, counters, fb_rows, fb_items, rows, row_items, out_ids, out_dists;
+   DevBuf items, segs, empties, ranges, gmax, norm_chunks, counters, fb_rows, fb_items, rows, row_items, out_ids,
+       out_dists;
    DevBuf cand_key, cand_col;
    DevBuf stage[2];
    DevBuf copy_ranges, compact; // a shard's rows gathered for one device -> host copy
@@ -295,8 +296,11 @@ int run_generate(ungx_context *ctx, const ungx_cross_edge_problem &p, const Plan
    if (route == UNGX_ROUTE_TENSOR && !plan.items.empty())
    {
       UNGX_CUDA(ctx, ctx->gmax.ensure(sizeof(float) * (p.num_groups + 1)), "group norms");
+      if ((st = upload(ctx, ctx->norm_chunks, plan.norm_chunks, "plan upload")))
+         return st;
       UNGX_CUDA(ctx,
-                ungx::launch_group_maxnorm(ctx->xnorm.as<float>(), ctx->ranges.as<uint32_t>(), p.num_groups,
+                ungx::launch_group_maxnorm(ctx->xnorm.as<float>(), ctx->norm_chunks.as<uint32_t>(),
+                                           (uint32_t)(plan.norm_chunks.size() / 3), p.num_groups,
                                            ctx->gmax.as<float>(), s),
                 "group norm kernel");
       UNGX_CUDA(ctx, ctx->fb_rows.ensure(sizeof(uint32_t) * std::max<uint64_t>(item_rows, 1)), "fallback list");
@@ -510,7 +514,7 @@ int ungx_context_destroy(ungx_context *ctx)
    if (ctx->stream)
       cudaStreamSynchronize(ctx->stream);
    ungx_release_base_vectors(ctx);
-   for (DevBuf *b : {&ctx->items, &ctx->segs, &ctx->empties, &ctx->ranges, &ctx->gmax, &ctx->counters,
+   for (DevBuf *b : {&ctx->items, &ctx->segs, &ctx->empties, &ctx->ranges, &ctx->gmax, &ctx->norm_chunks, &ctx->counters,
                      &ctx->fb_rows, &ctx->fb_items, &ctx->rows, &ctx->row_items, &ctx->out_ids, &ctx->out_dists,
                      &ctx->stage[0], &ctx->stage[1], &ctx->cand_key, &ctx->cand_col, &ctx->copy_ranges,
                      &ctx->compact, &ctx->g_ranges, &ctx->g_out_off, &ctx->g_out_ids, &ctx->group_of, &ctx->reach,

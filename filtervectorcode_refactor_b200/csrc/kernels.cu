@@ -360,22 +360,25 @@ __global__ void center_kernel(const float *__restrict__ X, const float *__restri
    }
 }
 
-__global__ void group_maxnorm_kernel(const float *__restrict__ xnorm, const uint32_t *__restrict__ ranges, uint32_t G,
-                                     float *__restrict__ out)
+// Warp per chunk (group, first row, rows <= 4096) of a group's rows: the chunk's largest
+// norm into out[group] by an integer max on the float bits (norms are >= 0; out zeroed
+// by the caller).  Chunks keep one large group from serialising on a single warp.
+__global__ void group_maxnorm_kernel(const float *__restrict__ xnorm, const uint32_t *__restrict__ chunks,
+                                     uint32_t nchunks, float *__restrict__ out)
 {
    const uint32_t lane = threadIdx.x & 31;
    const uint32_t warps = (gridDim.x * blockDim.x) >> 5;
-   for (uint32_t g = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; g <= G; g += warps)
+   for (uint32_t c = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; c < nchunks; c += warps)
    {
+      const uint32_t g = chunks[3 * c], a = chunks[3 * c + 1], b = a + chunks[3 * c + 2];
       float m = 0.f;
-      if (g > 0)
-         for (uint32_t r = ranges[2 * g] + lane; r < ranges[2 * g + 1]; r += 32)
-            m = fmaxf(m, xnorm[r]);
+      for (uint32_t r = a + lane; r < b; r += 32)
+         m = fmaxf(m, xnorm[r]);
 #pragma unroll
       for (int o = 16; o; o >>= 1)
          m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
       if (lane == 0)
-         out[g] = m;
+         atomicMax(reinterpret_cast<int *>(out + g), __float_as_int(m));
    }
 }
 
@@ -1398,10 +1401,14 @@ cudaError_t launch_center(const float *X, const float *mean, const OperandScale 
    return cudaGetLastError();
 }
 
-cudaError_t launch_group_maxnorm(const float *xnorm, const uint32_t *ranges, uint32_t G, float *out, cudaStream_t s)
+cudaError_t launch_group_maxnorm(const float *xnorm, const uint32_t *chunks, uint32_t nchunks, uint32_t G, float *out,
+                                 cudaStream_t s)
 {
-   const uint32_t blocks = std::min<uint32_t>((G + 1 + 7) / 8, 148 * 16);
-   group_maxnorm_kernel<<<blocks, 256, 0, s>>>(xnorm, ranges, G, out);
+   cudaError_t e = cudaMemsetAsync(out, 0, sizeof(float) * (size_t(G) + 1), s);
+   if (e != cudaSuccess || nchunks == 0)
+      return e;
+   const uint32_t blocks = std::min<uint32_t>((nchunks + 7) / 8, 148 * 16);
+   group_maxnorm_kernel<<<blocks, 256, 0, s>>>(xnorm, chunks, nchunks, out);
    return cudaGetLastError();
 }
 

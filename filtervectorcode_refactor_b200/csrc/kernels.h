@@ -117,7 +117,7 @@ cudaError_t launch_scale(const double *sums, const uint32_t *range, uint32_t n, 
 // fp16 operand rows Xh [n x dp] and fp32 norms of the centred rows.
 cudaError_t launch_center(const float *X, const float *mean, const OperandScale *scale, uint32_t n, uint32_t d,
                           uint32_t dp, uint16_t *Xh, float *xnorm, cudaStream_t s);
-cudaError_t launch_group_maxnorm(const float *xnorm, const uint32_t *ranges, uint32_t G, float *out,
+cudaError_t launch_group_maxnorm(const float *xnorm, const uint32_t *chunks, uint32_t nchunks, uint32_t G, float *out,
                                  cudaStream_t s);
 cudaError_t launch_fill_empty(const RowRange *ranges, uint32_t nranges, uint32_t k, uint32_t *ids, float *dists,
                               cudaStream_t s);

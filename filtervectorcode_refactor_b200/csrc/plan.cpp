@@ -212,12 +212,16 @@ int build_plan(const ungx_cross_edge_problem &p, Plan &plan, std::string &err)
          plan.padded_cols += plan.key[o];
       }
    }
-   // rows with no candidates: skipped source groups and groups without targets
+   // rows with no candidates: skipped source groups and groups without targets; and
+   // every group's rows in chunks for the per-group norm maxima
+   plan.norm_chunks.clear();
    for (uint32_t f = 1; f <= G; ++f)
    {
       const uint32_t a = p.group_ranges[2 * f], b = p.group_ranges[2 * f + 1];
       if (a != b && plan.g_nseg[f] == 0 && f % S == p.shard_rank)
          plan.empty_rows.push_back({a, b - a});
+      for (uint32_t r = a; r < b; r += 4096u)
+         plan.norm_chunks.insert(plan.norm_chunks.end(), {f, r, std::min(4096u, b - r)});
    }
    return UNGX_OK;
 }

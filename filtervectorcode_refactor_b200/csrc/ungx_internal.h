@@ -59,6 +59,7 @@ struct Plan
    std::vector<WorkItem> all;                       // every shard's items, group order
    std::vector<uint64_t> key, item_pairs;           // per item: cost (sort key), pairs
    std::vector<uint32_t> order, order2;             // item permutation
+   std::vector<uint32_t> norm_chunks;               // (group, first row, rows <= 4096) of every group
 };
 
 constexpr uint32_t kRowsPerItem = 128;
