@@ -133,6 +133,98 @@ __device__ __forceinline__ void warp_tree(float (&out)[8], const float *sq, cons
       out[i] = add_ftz(a[i], b[i]);
 }
 
+// The same sums on packed pairs (sm_100 f32x2 arithmetic: each half rounds and
+// flushes exactly like the scalar instruction): pair P[b][h] holds rows 2h, 2h + 1 of
+// the thread's 4 x 2 block against candidate b, so a leaf is four packed subtractions
+// and four packed FMAs instead of eight of each.
+__device__ __forceinline__ uint64_t pk2(float lo, float hi)
+{
+   return (uint64_t(__float_as_uint(hi)) << 32) | __float_as_uint(lo);
+}
+__device__ __forceinline__ uint64_t sub2_ftz(uint64_t a, uint64_t b)
+{
+   uint64_t d;
+   asm("sub.rn.ftz.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+   return d;
+}
+__device__ __forceinline__ uint64_t add2_ftz(uint64_t a, uint64_t b)
+{
+   uint64_t d;
+   asm("add.rn.ftz.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+   return d;
+}
+__device__ __forceinline__ uint64_t fma2_ftz(uint64_t a, uint64_t b, uint64_t c)
+{
+   uint64_t d;
+   asm("fma.rn.ftz.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+   return d;
+}
+
+__device__ __forceinline__ void leaf2(uint64_t (&out)[4], const float *sq, const float *sx, int t, uint32_t d, int r0,
+                                     int c0)
+{
+#pragma unroll
+   for (int i = 0; i < 4; ++i)
+      out[i] = 0;
+   for (uint32_t dim = t; dim < d; dim += 128)
+   {
+      const float4 q = *reinterpret_cast<const float4 *>(sq + dim * kKnnRows + r0);
+      const float2 x = *reinterpret_cast<const float2 *>(sx + dim * kKnnCands + c0);
+      const uint64_t q01 = pk2(q.x, q.y), q23 = pk2(q.z, q.w);
+      const uint64_t x0 = pk2(x.x, x.x), x1 = pk2(x.y, x.y);
+      const uint64_t d00 = sub2_ftz(q01, x0), d01 = sub2_ftz(q23, x0);
+      const uint64_t d10 = sub2_ftz(q01, x1), d11 = sub2_ftz(q23, x1);
+      out[0] = fma2_ftz(d00, d00, out[0]);
+      out[1] = fma2_ftz(d01, d01, out[1]);
+      out[2] = fma2_ftz(d10, d10, out[2]);
+      out[3] = fma2_ftz(d11, d11, out[3]);
+   }
+}
+
+template <int LO, int SIZE>
+__device__ __forceinline__ void sub_tree2(uint64_t (&out)[4], const float *sq, const float *sx, int base, uint32_t d,
+                                          int r0, int c0)
+{
+   if constexpr (SIZE == 1)
+      leaf2(out, sq, sx, base + 4 * bitrev3(LO), d, r0, c0);
+   else
+   {
+      uint64_t l[4], r[4];
+      sub_tree2<LO, SIZE / 2>(l, sq, sx, base, d, r0, c0);
+      sub_tree2<LO + SIZE / 2, SIZE / 2>(r, sq, sx, base, d, r0, c0);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+         out[i] = add2_ftz(l[i], r[i]);
+   }
+}
+
+__device__ __forceinline__ void warp_tree2(uint64_t (&out)[4], const float *sq, const float *sx, int j, uint32_t d,
+                                           int r0, int c0)
+{
+   uint64_t a[4], b[4];
+#pragma unroll 1
+   for (int g = 0; g < 4; ++g) // a = S0 + S1, b = S2 + S3
+   {
+      uint64_t t[4];
+      sub_tree2<0, 8>(t, sq, sx, 32 * j + ((g & 1) << 1 | (g >> 1)), d, r0, c0);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+      {
+         if (g == 0)
+            a[i] = t[i];
+         else if (g == 1)
+            a[i] = add2_ftz(a[i], t[i]);
+         else if (g == 2)
+            b[i] = t[i];
+         else
+            b[i] = add2_ftz(b[i], t[i]);
+      }
+   }
+#pragma unroll
+   for (int i = 0; i < 4; ++i)
+      out[i] = add2_ftz(a[i], b[i]);
+}
+
 // One output row: [degree, head, ring anchors, tail, dedupe tail], padded with the point
 // itself (the reference's layout of batched_exact_knn_graph_kernel's epilogue).
 __device__ void write_row(const KnnParams &p, uint32_t group, uint32_t n, uint32_t s, uint32_t cand,
@@ -433,34 +525,40 @@ __global__ void __launch_bounds__(kKnnThreads) knn_dist_kernel(const KnnParams p
             sx[dim * kKnnCands + c] = (x < n && dim < p.d) ? p.X[size_t(first + x) * p.d + dim] : 0.0f;
          }
       __syncthreads();
-      float s02[8], s13[8];
+      // (w0 + w2) + (w1 + w3); a warp block past d is +0 and is skipped
+      uint64_t s02[4], s13[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
-         s02[i] = s13[i] = 0.0f;
+      for (int i = 0; i < 4; ++i)
+         s02[i] = s13[i] = 0;
       const int nj = int(min(p.d, 128u) + 31u) / 32;
 #pragma unroll 1
       for (int j = 0; j < nj; ++j)
       {
-         float w[8];
-         warp_tree(w, sq, sx, j, p.d, r0, c0);
+         uint64_t w[4];
+         warp_tree2(w, sq, sx, j, p.d, r0, c0);
 #pragma unroll
-         for (int i = 0; i < 8; ++i)
+         for (int i = 0; i < 4; ++i)
          {
             if (j == 0)
                s02[i] = w[i];
             else if (j == 1)
                s13[i] = w[i];
             else if (j == 2)
-               s02[i] = add_ftz(s02[i], w[i]);
+               s02[i] = add2_ftz(s02[i], w[i]);
             else
-               s13[i] = add_ftz(s13[i], w[i]);
+               s13[i] = add2_ftz(s13[i], w[i]);
          }
       }
+      // pair P[b][h]: rows 2h (low half), 2h + 1 (high half), candidate b
 #pragma unroll
-      for (int a = 0; a < 4; ++a)
+      for (int b = 0; b < 2; ++b)
 #pragma unroll
-         for (int b = 0; b < 2; ++b)
-            sd[(r0 + a) * kLd + c0 + b] = add_ftz(s02[a * 2 + b], s13[a * 2 + b]);
+         for (int h = 0; h < 2; ++h)
+         {
+            const uint64_t v = add2_ftz(s02[b * 2 + h], s13[b * 2 + h]);
+            sd[(r0 + 2 * h) * kLd + c0 + b] = __uint_as_float(uint32_t(v));
+            sd[(r0 + 2 * h + 1) * kLd + c0 + b] = __uint_as_float(uint32_t(v >> 32));
+         }
       __syncthreads();
       // (i, j): 32-column row pieces; (j, i) off the diagonal: 64-row column pieces
       for (uint32_t idx = tid; idx < uint32_t(kKnnRows) * kKnnCands; idx += kKnnThreads)
