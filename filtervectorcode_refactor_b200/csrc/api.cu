@@ -941,8 +941,8 @@ int ungx_additional_edges_build(ungx_context *ctx, const ungx_cross_edge_problem
       ep.count_host = nq;
       ep.out_ids = ctx->add_res.as<uint32_t>();
       ep.out_pos = ctx->add_pos.as<uint32_t>();
-      UNGX_CUDA(ctx, ungx::launch_exact(ep, std::min<uint32_t>(nq, (uint32_t)ctx->num_sms * 8), s),
-                "additional-edge kernel");
+      ep.warp_per_row = 1; // a query scans one target group
+      UNGX_CUDA(ctx, ungx::launch_exact(ep, (uint32_t)ctx->num_sms * 16, s), "additional-edge kernel");
       // 4. (from, to) in the reference's order, and the same edges per point
       UNGX_CUDA(ctx,
                 ungx::launch_add_list(ctx->add_res.as<uint32_t>(), ctx->add_rows.as<uint32_t>(), nq, kh,

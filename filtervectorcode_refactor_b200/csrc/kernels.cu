@@ -502,6 +502,77 @@ __global__ void __launch_bounds__(256) exact_rows_kernel(const ExactParams p)
    }
 }
 
+// A warp per row, for rows whose candidate columns are few (the additional-edge
+// queries scan one target group each): lanes stride over the columns keeping a sorted
+// top-KMAX each, then k rounds of a warp arg-min over (distance, id) give the row's
+// top-k in order, written by lane 0.  No block barrier.
+template <int KMAX, bool VEC4>
+__global__ void __launch_bounds__(256) exact_rows_warp_kernel(const ExactParams p)
+{
+   const uint32_t count = p.count_dev ? *(volatile const uint32_t *)p.count_dev : p.count_host;
+   const uint32_t lane = threadIdx.x & 31;
+   const uint32_t per_block = blockDim.x >> 5;
+   for (uint32_t w = blockIdx.x * per_block + (threadIdx.x >> 5); w < count; w += gridDim.x * per_block)
+   {
+      const uint32_t row = p.rows[w];
+      const WorkItem it = p.items[p.row_items[w]];
+      float bd[KMAX];
+      uint32_t bi[KMAX];
+#pragma unroll
+      for (int i = 0; i < KMAX; ++i)
+      {
+         bd[i] = INFINITY;
+         bi[i] = 0xFFFFFFFFu;
+      }
+      const float *q = p.X + size_t(row) * p.d;
+      for (uint32_t s = 0; s < it.seg_count; ++s)
+      {
+         const Segment sg = p.segs[it.seg_begin + s];
+         const uint32_t end = sg.x_begin + sg.x_count;
+         for (uint32_t x = sg.x_begin + lane; x < end; x += 32)
+         {
+            const float D = ref_l2<VEC4>(q, p.X + size_t(x) * p.d, p.d);
+            if (pair_less(D, x, bd[KMAX - 1], bi[KMAX - 1]))
+               insert_pair<KMAX>(bd, bi, D, x);
+         }
+      }
+      const size_t slot = p.out_pos ? size_t(p.out_pos[w]) : size_t(row);
+      for (uint32_t o = 0; o < p.k; ++o)
+      {
+         float md = bd[0];
+         uint32_t mi = bi[0];
+#pragma unroll
+         for (int off = 16; off; off >>= 1)
+         {
+            const float od = __shfl_xor_sync(0xffffffffu, md, off);
+            const uint32_t oi = __shfl_xor_sync(0xffffffffu, mi, off);
+            if (pair_less(od, oi, md, mi))
+            {
+               md = od;
+               mi = oi;
+            }
+         }
+         if (mi != 0xFFFFFFFFu && bi[0] == mi)
+         {
+#pragma unroll
+            for (int i = 0; i < KMAX - 1; ++i)
+            {
+               bd[i] = bd[i + 1];
+               bi[i] = bi[i + 1];
+            }
+            bd[KMAX - 1] = INFINITY;
+            bi[KMAX - 1] = 0xFFFFFFFFu;
+         }
+         if (lane == 0)
+         {
+            p.out_ids[slot * p.k + o] = mi;
+            if (p.out_dists)
+               p.out_dists[slot * p.k + o] = md;
+         }
+      }
+   }
+}
+
 // ------------------------------------------------------------------ tensor-core path
 __device__ __forceinline__ void raise_abort(volatile int *abort_word, int *status, int code)
 {
@@ -1312,6 +1383,16 @@ cudaError_t launch_tc_kp(const TcMaps &maps, const TcParams &p, uint32_t grid, c
 template <int KMAX>
 cudaError_t launch_exact_t(const ExactParams &p, uint32_t grid, cudaStream_t s)
 {
+   if (p.warp_per_row && KMAX <= 16)
+   {
+      // eight rows per block
+      const uint32_t g = p.count_dev ? grid : std::max(1u, std::min(grid, (p.count_host + 7u) / 8u));
+      if ((p.d & 3u) == 0)
+         exact_rows_warp_kernel<KMAX <= 16 ? KMAX : 16, true><<<g, 256, 0, s>>>(p);
+      else
+         exact_rows_warp_kernel<KMAX <= 16 ? KMAX : 16, false><<<g, 256, 0, s>>>(p);
+      return cudaGetLastError();
+   }
    if ((p.d & 3u) == 0)
       exact_rows_kernel<KMAX, true><<<grid, 256, 0, s>>>(p);
    else

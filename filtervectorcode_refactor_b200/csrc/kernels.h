@@ -95,6 +95,7 @@ struct ExactParams
    uint32_t *out_ids;
    float *out_dists;
    const uint32_t *out_pos;   // output row of each listed row, or NULL for the row itself
+   uint32_t warp_per_row;     // 1: a warp per row (short target lists, k <= 16), else a block
 };
 
 // Largest k the tensor-core route supports (candidate list of 32 per row).

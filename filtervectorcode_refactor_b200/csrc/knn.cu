@@ -160,9 +160,39 @@ __device__ __forceinline__ uint64_t fma2_ftz(uint64_t a, uint64_t b, uint64_t c)
    return d;
 }
 
+__device__ __forceinline__ uint64_t mul2_ftz(uint64_t a, uint64_t b)
+{
+   uint64_t d;
+   asm("mul.rn.ftz.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+   return d;
+}
+
 __device__ __forceinline__ void leaf2(uint64_t (&out)[4], const float *sq, const float *sx, int t, uint32_t d, int r0,
                                      int c0)
 {
+   if (d <= 128u) // one dimension per leaf: fma(x, x, +0) == mul(x, x) for a square
+   {
+      if (uint32_t(t) < d)
+      {
+         const float4 q = *reinterpret_cast<const float4 *>(sq + t * kKnnRows + r0);
+         const float2 x = *reinterpret_cast<const float2 *>(sx + t * kKnnCands + c0);
+         const uint64_t q01 = pk2(q.x, q.y), q23 = pk2(q.z, q.w);
+         const uint64_t x0 = pk2(x.x, x.x), x1 = pk2(x.y, x.y);
+         const uint64_t d00 = sub2_ftz(q01, x0), d01 = sub2_ftz(q23, x0);
+         const uint64_t d10 = sub2_ftz(q01, x1), d11 = sub2_ftz(q23, x1);
+         out[0] = mul2_ftz(d00, d00);
+         out[1] = mul2_ftz(d01, d01);
+         out[2] = mul2_ftz(d10, d10);
+         out[3] = mul2_ftz(d11, d11);
+      }
+      else
+      {
+#pragma unroll
+         for (int i = 0; i < 4; ++i)
+            out[i] = 0;
+      }
+      return;
+   }
 #pragma unroll
    for (int i = 0; i < 4; ++i)
       out[i] = 0;
