@@ -607,6 +607,12 @@ __global__ void __launch_bounds__(kKnnThreads) knn_dist_kernel(const KnnParams p
    }
 }
 
+// (distance, id) order of the reference's lists; an empty slot (+inf, UINT32_MAX) is last
+__device__ __forceinline__ bool pair_less_knn(float d0, uint32_t i0, float d1, uint32_t i1)
+{
+   return d0 < d1 || (d0 == d1 && i0 < i1);
+}
+
 constexpr int kRowWarps = 4; // warps per block of the row pass, 32 rows each
 
 // Phase 2: a warp per 32 rows of a group.  Each row's list (lane l: entries l and
@@ -635,7 +641,76 @@ __global__ void __launch_bounds__(kRowWarps * 32) knn_rows_kernel(const KnnParam
       float e0 = FLT_MAX, e1 = FLT_MAX;
       uint32_t i0 = 0xFFFFFFFFu, i1 = 0xFFFFFFFFu;
       if (cand > 0)
-         for (uint32_t x0 = 0; x0 < n; x0 += 32u)
+      {
+         // Columns 0..63 at once.  Inserting candidates in ascending id with strict <
+         // keeps the cand smallest by (distance, id) of those with a distance below
+         // FLT_MAX, so the warp sorts the 64 by (distance, id) (bitonic, element l and
+         // l + 32 in lane l) and keeps the first cand; the rest of the list holds
+         // FLT_MAX / UINT32_MAX as the reference's does.
+         {
+            const uint32_t xa = lane, xb = lane + 32u;
+            float da = xa < n ? D[size_t(s) * n + xa] : INFINITY;
+            float db = xb < n ? D[size_t(s) * n + xb] : INFINITY;
+            uint32_t ia = xa, ib = xb;
+            if (!(xa < n && xa != s && da < FLT_MAX))
+            {
+               da = INFINITY;
+               ia = 0xFFFFFFFFu;
+            }
+            if (!(xb < n && xb != s && db < FLT_MAX))
+            {
+               db = INFINITY;
+               ib = 0xFFFFFFFFu;
+            }
+#pragma unroll
+            for (uint32_t k = 2; k <= 64; k <<= 1)
+#pragma unroll
+               for (uint32_t j = k >> 1; j > 0; j >>= 1)
+               {
+                  if (j == 32)
+                  {
+                     // partner of element l is l + 32, in the same lane; k == 64: ascending
+                     if (pair_less_knn(db, ib, da, ia))
+                     {
+                        const float td = da;
+                        const uint32_t ti = ia;
+                        da = db;
+                        ia = ib;
+                        db = td;
+                        ib = ti;
+                     }
+                     continue;
+                  }
+                  const bool lower = (lane & j) == 0;
+                  {
+                     const float od = __shfl_xor_sync(0xffffffffu, da, j);
+                     const uint32_t oi = __shfl_xor_sync(0xffffffffu, ia, j);
+                     const bool asc = (lane & k) == 0;
+                     const bool o_less = pair_less_knn(od, oi, da, ia);
+                     if (lower == asc ? o_less : !o_less)
+                     {
+                        da = od;
+                        ia = oi;
+                     }
+                  }
+                  {
+                     const float od = __shfl_xor_sync(0xffffffffu, db, j);
+                     const uint32_t oi = __shfl_xor_sync(0xffffffffu, ib, j);
+                     const bool asc = ((lane + 32u) & k) == 0;
+                     const bool o_less = pair_less_knn(od, oi, db, ib);
+                     if (lower == asc ? o_less : !o_less)
+                     {
+                        db = od;
+                        ib = oi;
+                     }
+                  }
+               }
+            e0 = lane < cand && ia != 0xFFFFFFFFu ? da : FLT_MAX;
+            i0 = lane < cand && ia != 0xFFFFFFFFu ? ia : 0xFFFFFFFFu;
+            e1 = lane + 32u < cand && ib != 0xFFFFFFFFu ? db : FLT_MAX;
+            i1 = lane + 32u < cand && ib != 0xFFFFFFFFu ? ib : 0xFFFFFFFFu;
+         }
+         for (uint32_t x0 = 64; x0 < n; x0 += 32u)
          {
             const uint32_t x = x0 + lane;
             const float dist = x < n ? D[size_t(s) * n + x] : FLT_MAX;
@@ -670,6 +745,7 @@ __global__ void __launch_bounds__(kRowWarps * 32) knn_rows_kernel(const KnnParam
                }
             }
          }
+      }
       s_top[warp][rr][lane] = i0;
       s_top[warp][rr][32u + lane] = i1;
    }
