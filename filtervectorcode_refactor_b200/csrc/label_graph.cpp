@@ -118,10 +118,72 @@ void build_lng(ungx_label_graph &g, int threads)
    for (uint32_t f = 1; f <= G; ++f)
       max_len = std::max(max_len, set_len(f));
 
+   // label sets of at most 64 distinct labels without repeats: the inverted lists carry
+   // each group's label mask, so the superset test is a sequential scan of 8-byte words
+   const bool fast = !has_dup && W == 1;
+   std::vector<uint64_t> inv_mask(fast ? inv.size() : 0);
+   if (fast)
+      for (size_t j = 0; j < inv.size(); ++j)
+         inv_mask[j] = masks[inv[j]];
    std::vector<std::vector<uint32_t>> outs(G + 1);
    parallel_for(G, threads, 64, [&](int64_t i) {
       const uint32_t f = (uint32_t)i + 1;
       const uint32_t flen = set_len(f);
+      if (fast)
+      {
+         // candidates: strict supersets among the groups holding f's rarest label, in
+         // the reference's visiting order (label-set length, then group id); a candidate
+         // is kept unless a kept shorter one is included in it
+         const uint64_t mf = masks[f];
+         uint64_t best_n = UINT64_MAX, best_off = 0;
+         for (uint64_t j = g.set_off[f]; j < g.set_off[f + 1]; ++j)
+         {
+            const uint32_t l = dense[j];
+            if (inv_off[l + 1] - inv_off[l] < best_n)
+            {
+               best_n = inv_off[l + 1] - inv_off[l];
+               best_off = inv_off[l];
+            }
+         }
+         std::vector<std::pair<uint32_t, uint32_t>> sup; // (length, group)
+         if (best_n == UINT64_MAX) // the empty set: every other group is a superset
+         {
+            for (uint32_t c = 1; c <= G; ++c)
+               if (c != f)
+                  sup.push_back({set_len(c), c});
+         }
+         else
+            for (uint64_t j = best_off; j < best_off + best_n; ++j)
+            {
+               const uint64_t m = inv_mask[j];
+               if ((m & mf) == mf && m != mf)
+                  sup.push_back({(uint32_t)__builtin_popcountll(m), inv[j]});
+            }
+         std::sort(sup.begin(), sup.end());
+         std::vector<uint32_t> kept;
+         std::vector<uint64_t> kept_mask;
+         std::vector<uint32_t> kept_len;
+         for (const auto &lc : sup)
+         {
+            const uint64_t mc = masks[lc.second];
+            bool is_min = true;
+            for (size_t q = 0; q < kept.size(); ++q)
+               if (kept_len[q] < lc.first && (mc & kept_mask[q]) == kept_mask[q])
+               {
+                  is_min = false;
+                  break;
+               }
+            if (is_min)
+            {
+               kept.push_back(lc.second);
+               kept_mask.push_back(mc);
+               kept_len.push_back(lc.first);
+            }
+         }
+         std::sort(kept.begin(), kept.end());
+         outs[f].swap(kept);
+         return;
+      }
       // candidate source list: the inverted list of f's rarest label
       const uint32_t *lst = all_groups.data();
       uint64_t lst_n = G;
@@ -212,14 +274,27 @@ int ungx_label_graph_build(uint32_t n, const uint64_t *label_offsets, const uint
          std::sort(b, e);
          h[v] = hash_seq(b, (uint32_t)(e - b));
       });
-      // first-appearance group ids (serial: the order is the definition)
-      uint64_t cap = 64;
-      while (cap < 2ull * n + 64)
-         cap <<= 1;
+      // first-appearance group ids (serial: the order is the definition).  The open
+      // addressing table holds the groups, not the points: it starts small and doubles
+      // at half load, so it stays cache-resident when groups are far fewer than points.
+      uint64_t cap = 1024;
       std::vector<uint32_t> slot_rep(cap), slot_gid(cap, 0);
       std::vector<uint32_t> point_gid(n), rep;
       rep.push_back(0);
       uint32_t G = 0;
+      auto grow = [&]() {
+         cap <<= 1;
+         slot_rep.assign(cap, 0);
+         slot_gid.assign(cap, 0);
+         for (uint32_t gid = 1; gid <= G; ++gid)
+         {
+            uint64_t q = h[rep[gid]] & (cap - 1);
+            while (slot_gid[q] != 0)
+               q = (q + 1) & (cap - 1);
+            slot_gid[q] = gid;
+            slot_rep[q] = rep[gid];
+         }
+      };
       for (uint32_t v = 0; v < n; ++v)
       {
          const uint32_t len = (uint32_t)(label_offsets[v + 1] - label_offsets[v]);
@@ -233,6 +308,8 @@ int ungx_label_graph_build(uint32_t n, const uint64_t *label_offsets, const uint
                slot_rep[p] = v;
                rep.push_back(v);
                point_gid[v] = G;
+               if (2ull * G > cap)
+                  grow();
                break;
             }
             const uint32_t r = slot_rep[p];
