@@ -139,6 +139,7 @@ _SIGNATURES = [
     ("ungx_label_graph_num_set_labels", c_uint64, [c_void_p]),
     ("ungx_label_graph_copy_label_sets", c_int, [c_void_p, c_void_p, c_void_p]),
     ("ungx_flat_to_csr", c_int, [c_void_p, c_uint32, c_uint32, c_void_p, c_void_p]),
+    ("ungx_graph_save_text", c_int, [c_char_p, c_uint32, c_void_p, c_void_p]),
     ("ungx_additional_edges_build", c_int,
      [c_void_p, POINTER(CrossEdgeProblem), c_void_p, c_void_p, POINTER(AdditionalStats)]),
     ("ungx_additional_edges_copy", c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
@@ -359,6 +360,13 @@ def cross_edges_exact_noalloc(problem: Problem, d_vectors: int, d_ids: int, d_di
                               stream: int | None = None) -> None:
     """ungx_cross_edges_exact_noalloc: device pointers in and out, no device allocation."""
     check(lib.ungx_cross_edges_exact_noalloc(ctypes.byref(problem.c), d_vectors, d_ids, d_dists, stream))
+
+
+def graph_save_text(path: str, offsets: np.ndarray, cols: np.ndarray) -> None:
+    """Write a CSR adjacency in the reference's graph text format (ungx_graph_save_text)."""
+    offsets = np.ascontiguousarray(offsets, dtype=np.uint64)
+    cols = np.ascontiguousarray(cols, dtype=np.uint32)
+    check(lib.ungx_graph_save_text(os.fsencode(path), offsets.size - 1, _ptr(offsets), _ptr(cols)))
 
 
 def flat_to_csr(flat_ids: np.ndarray, num_points: int, topk: int) -> tuple[np.ndarray, np.ndarray]:

@@ -218,6 +218,13 @@ int ungx_label_graph_copy_label_sets(const ungx_label_graph *lg, uint64_t *offse
 int ungx_flat_to_csr(const uint32_t *flat_ids, uint32_t num_points, uint32_t topk, uint64_t *row_offsets,
                      uint32_t *col_indices);
 
+/* ------------------------------------------- the graph in the reference's text format
+ * ANNS::Graph::save (UNG/codes/include/graph.h:207-216), the <prefix>graph file of
+ * UniNavGraph::save (UNG/codes/src/uni_nav_graph_io.cpp:383-386), from a host CSR:
+ * for each point v, "v " then "c " for each column of row v in order, then '\n'.
+ * Returns UNGX_ERR_INVALID_ARG for a null or non-monotone argument or a file error. */
+int ungx_graph_save_text(const char *path, uint32_t num_points, const uint64_t *offsets, const uint32_t *cols);
+
 /* ------------------------------------------- additional edges (exact variant)
  * Replaces UniNavGraph::build_cross_edges_generate_additional with
  * UngAdditionalEdgesImpl::CpuExactScan (UNG/codes/src/uni_nav_graph_cross_edges.cpp:442-596).

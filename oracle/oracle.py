@@ -195,6 +195,15 @@ class Reference(_Lib):
         """(from, to) additional edges in the reference's materialised order."""
         return self._additional(self.lib.ungref_additional_edges, X, k, group_first, out_offsets, out_ids, cross_ids)
 
+    def graph_save_text(self, path: str, offsets: np.ndarray, cols: np.ndarray) -> None:
+        """The CSR rows written by the reference's ANNS::Graph::save (graph.h:207-216)."""
+        off = np.ascontiguousarray(offsets, dtype=np.uint64)
+        c = np.ascontiguousarray(cols, dtype=np.uint32)
+        if c.size == 0:
+            c = np.zeros(1, dtype=np.uint32)
+        self.lib.ungref_graph_save_text.argtypes = [ctypes.c_char_p, c_uint32, c_void_p, c_void_p]
+        self.lib.ungref_graph_save_text(os.fsencode(path), off.size - 1, _p(off), _p(c))
+
     def l2(self, a: np.ndarray, b: np.ndarray) -> float:
         a = np.ascontiguousarray(a, dtype=np.float32)
         b = np.ascontiguousarray(b, dtype=np.float32)

@@ -28,6 +28,7 @@
 #include <vector>
 
 #include "distance.h"
+#include "graph.h"
 #include "search_queue.h"
 #include "trie.h"
 
@@ -329,4 +330,18 @@ uint64_t ungref_additional_edges(const float *X, uint32_t n, uint32_t d, uint32_
    return edges.size();
 }
 
+
+// The reference's own graph writer: the CSR rows pushed into an ANNS::Graph
+// (NeighborList per point) and written by Graph::save (UNG/codes/include/graph.h:207-216).
+int ungref_graph_save_text(const char *path, uint32_t num_points, const uint64_t *offsets, const uint32_t *cols)
+{
+   ANNS::Graph g(num_points);
+   for (uint32_t v = 0; v < num_points; ++v)
+      for (uint64_t e = offsets[v]; e < offsets[v + 1]; ++e)
+         g.neighbors[v].push_back(cols[e]);
+   std::string fn(path);
+   g.save(fn);
+   g.clean();
+   return 0;
+}
 } // extern "C"
