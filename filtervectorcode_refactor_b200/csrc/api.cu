@@ -126,7 +126,7 @@ struct ungx_context
    uint32_t add_n = 0;     // points of the last additional-edge build
    uint64_t add_edges = 0; // its edges
    uint32_t *h_counters = nullptr; // pinned
-   cudaEvent_t ev[10] = {};
+   cudaEvent_t ev[11] = {}; // ev[10]: end of the last vector preparation
 };
 
 namespace
@@ -167,8 +167,9 @@ int wait_event(ungx_context *ctx, cudaEvent_t ev, const char *what)
          return cuda_fail(ctx, e, what);
       if (ms_since(t0) > ctx->timeout_ms)
          return fail(ctx, UNGX_ERR_TIMEOUT, std::string(what) + ": device work exceeded the timeout");
-      if (spin > 64)
-         std::this_thread::sleep_for(std::chrono::microseconds(50));
+      // spin for the first 2 ms (short kernels), then sleep in 20 us slices
+      if (spin > 64 && ms_since(t0) > 2.0)
+         std::this_thread::sleep_for(std::chrono::microseconds(20));
    }
 }
 
@@ -271,6 +272,8 @@ int run_generate(ungx_context *ctx, const ungx_cross_edge_problem &p, const Plan
    t.gpu_launches = 0;
 
    cudaEvent_t *ev = ctx->ev;
+   if (s != ctx->stream) // the operand is prepared on the context's stream
+      UNGX_CUDA(ctx, cudaStreamWaitEvent(s, ev[10], 0), "stream wait");
    UNGX_CUDA(ctx, cudaEventRecord(ev[0], s), "event");
    // plan upload
    std::vector<uint32_t> ranges(2 * size_t(p.num_groups + 1));
@@ -604,10 +607,11 @@ int ungx_prepare_base_vectors(ungx_context *ctx, const float *vectors, uint32_t 
              ungx::launch_center(ctx->X, ctx->mean.as<float>(), ctx->scale.as<ungx::OperandScale>(), n, d, dp,
                                  ctx->Xh.as<uint16_t>(), ctx->xnorm.as<float>(), ctx->stream),
              "centre kernel");
-   UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[6], ctx->stream), "event");
-   int st = wait_event(ctx, ctx->ev[6], "vector preparation");
-   if (st)
-      return st;
+   // The preparation kernels run on while the caller goes on (a generate call plans on
+   // the host meanwhile); work on the context's stream follows them in order, work on
+   // another stream waits for this event, and a fault in them surfaces at that work's
+   // wait.  Device vectors stay valid until ungx_release_base_vectors in any case.
+   UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[10], ctx->stream), "event");
    ctx->n = n;
    ctx->d = d;
    ctx->dp = dp;
