@@ -501,7 +501,7 @@ struct KnnTile
    uint32_t group, bi, bj; // rows 64 bi .., columns 64 bj .., bj >= bi
 };
 
-__global__ void __launch_bounds__(kKnnThreads) knn_dist_kernel(const KnnParams p, const KnnTile *__restrict__ tiles)
+__global__ void __launch_bounds__(kKnnThreads, 3) knn_dist_kernel(const KnnParams p, const KnnTile *__restrict__ tiles)
 {
    extern __shared__ float smem_f[];
    float *sq = smem_f;                          // [d][64] source rows
@@ -710,10 +710,27 @@ __global__ void __launch_bounds__(kRowWarps * 32) knn_rows_kernel(const KnnParam
             e1 = lane + 32u < cand && ib != 0xFFFFFFFFu ? db : FLT_MAX;
             i1 = lane + 32u < cand && ib != 0xFFFFFFFFu ? ib : 0xFFFFFFFFu;
          }
-         for (uint32_t x0 = 64; x0 < n; x0 += 32u)
+         // the row's distances are loaded four 32-column steps ahead of their use
+         float pf[4];
+#pragma unroll
+         for (int j = 0; j < 4; ++j)
          {
+            const uint32_t xj = 64u + 32u * uint32_t(j) + lane;
+            pf[j] = xj < n ? D[size_t(s) * n + xj] : FLT_MAX;
+         }
+         for (uint32_t xb = 64; xb < n; xb += 128u)
+#pragma unroll
+         for (int j = 0; j < 4; ++j)
+         {
+            const uint32_t x0 = xb + 32u * uint32_t(j);
+            if (x0 >= n)
+               break;
             const uint32_t x = x0 + lane;
-            const float dist = x < n ? D[size_t(s) * n + x] : FLT_MAX;
+            const float dist = pf[j];
+            {
+               const uint32_t xn = x + 128u;
+               pf[j] = xn < n ? D[size_t(s) * n + xn] : FLT_MAX;
+            }
             const float last0 = __shfl_sync(0xffffffffu, cand > 32u ? e1 : e0, lc);
             uint32_t m = __ballot_sync(0xffffffffu, x < n && x != s && dist < last0);
             while (m)
