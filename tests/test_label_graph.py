@@ -56,3 +56,32 @@ def test_label_graph_rejects_bad_offsets():
     lab = np.array([1, 2, 3], dtype=np.uint32)
     with pytest.raises(nat.UngxError):
         nat.LabelGraph(off, lab)
+
+
+@pytest.mark.parametrize("vocab", [30, 100])
+def test_label_graph_matches_reference_trie(vocab):
+    """Both LNG paths against the reference's own TrieIndex build (oracle/_ref): label
+    sets of up to 64 distinct labels take the mask scan, larger vocabularies the general
+    inclusion test; empty label sets included."""
+    ref = O.reference()
+    if ref is None:
+        pytest.skip("the reference harness (oracle/_ref) is not built")
+    rng = np.random.default_rng(vocab)
+    n = 20000
+    sizes = rng.integers(0, 5, n)
+    off = np.zeros(n + 1, dtype=np.uint64)
+    off[1:] = np.cumsum(sizes)
+    weights = 1.0 / np.arange(1, vocab + 1) ** 1.1
+    weights /= weights.sum()
+    lab = []
+    for s in sizes:
+        lab.extend(rng.choice(vocab, size=int(s), replace=False, p=weights).tolist())
+    lab = np.array(lab, dtype=np.uint32)
+    lg = nat.LabelGraph(off, lab)
+    exp = ref.label_graph(off, lab)
+    G = exp["num_groups"]
+    assert np.array_equal(np.asarray(lg.new_to_old), exp["new_to_old"])
+    assert np.array_equal(np.asarray(lg.group_ranges), exp["group_ranges"])
+    got_sets = O.lng_sets(np.asarray(lg.out_offsets), np.asarray(lg.out_ids), G)
+    exp_sets = O.lng_sets(exp["out_offsets"], exp["out_ids"], G)
+    assert got_sets == exp_sets
