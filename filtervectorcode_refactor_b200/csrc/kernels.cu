@@ -11,9 +11,10 @@
 //                       kind::f16 with A in TMEM and the target tile (<= 192 rows) in
 //                       shared memory into two 192-column TMEM accumulators; twelve
 //                       epilogue warps read TMEM rows (thread = source row), form the
-//                       keys ||x||^2 - 2 q.x and keep a sorted register top-KP per row
-//                       and column third.  The three lists of every row go to a small
-//                       candidate buffer; no distance matrix reaches global memory.
+//                       keys ||x||^2 - 2 q.x and keep a sorted register list per row
+//                       and column third (tc_list_depth(KP) keys).  The three lists of
+//                       every row go to a small candidate buffer; no distance matrix
+//                       reaches global memory.
 //   rerank_kernel       merges a row's lists, computes the exact reference distance
 //                       of each candidate, sorts by (distance, id), writes the top-k and
 //                       checks a rounding-error certificate that no column outside the
@@ -21,7 +22,8 @@
 //   exact_rows_kernel   CUDA-core exact scan in the reference's fp32 summation order
 //                       (FloatL2DistanceHandler::compute, UNG/codes/src/distance.cpp:34-91)
 //                       with its (distance, id) queue order (UNG/codes/include/search_queue.h:20-22):
-//                       route EXACT, and the rescan of the queued rows.
+//                       route EXACT, and the rescan of the queued rows (a block per row);
+//                       exact_rows_warp_kernel, a warp per row, for short target lists.
 #include <cfloat>
 #include <cmath>
 #include <cuda_fp16.h>
