@@ -86,6 +86,27 @@ def test_device_entry_point_matches_host(ctx, golden):
     assert_rows_match(ids, dists, golden["ids"], golden["dists"], k)
 
 
+
+def test_device_entry_point_on_caller_stream(ctx, golden):
+    """Generate on the caller's own stream straight after preparation: the preparation
+    kernels run on the context's stream and the call must wait for them."""
+    import torch
+    n, d = golden["Xr"].shape
+    k = golden["k"]
+    if k > 24:
+        pytest.skip("tensor route needs k <= 24")
+    prob = nat.Problem(n, d, k, golden["group_ranges"], golden["out_offsets"], golden["out_ids"])
+    X = torch.from_numpy(golden["Xr"]).cuda()
+    d_ids = torch.empty(n * k, dtype=torch.int32, device="cuda")
+    d_dists = torch.empty(n * k, dtype=torch.float32, device="cuda")
+    s = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    ctx.prepare_base_vectors(X.data_ptr(), n, d, on_device=True)
+    ctx.generate_device(prob, d_ids.data_ptr(), d_dists.data_ptr(), s.cuda_stream)
+    s.synchronize()
+    ctx.release_base_vectors()
+    assert_rows_match(d_ids.cpu().numpy().view(np.uint32), d_dists.cpu().numpy(), golden["ids"], golden["dists"], k)
+
 def test_shards_cover_rows_once(ctx, golden):
     n, d = golden["Xr"].shape
     k = golden["k"]
