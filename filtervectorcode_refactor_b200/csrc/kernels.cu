@@ -1180,7 +1180,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
 //   3. the lanes rank their (distance, id) pairs the same way and write the first k;
 //   4. the certificate is evaluated by every lane, recorded by lane 0.
 template <int KP>
-__global__ void __launch_bounds__(256, 3) rerank_kernel(const RerankParams p)
+__global__ void __launch_bounds__(256, 4) rerank_kernel(const RerankParams p)
 {
    constexpr uint32_t TPR = KP;           // lanes per row
    constexpr int KD = tc_list_depth(KP);  // depth of each of the row's lists
