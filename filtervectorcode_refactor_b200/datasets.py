@@ -26,6 +26,12 @@ CONFIGS = {
             dist="normal", normalize=False, k=6),
 }
 
+# Configuration 5: the configuration-2 index searched by nq queries, each with a
+# label set of 1-2 labels from the same Zipf(1.0) over 30 (containment filter);
+# greedy search L = 100, top-10.
+QUERIES = dict(nq=10_240, d=128, vocab=30, umin=1, umax=2, zipf=1.0, dist="normal", normalize=False,
+               L=100, K=10, num_entry_points=16)
+
 
 def make_labels(n: int, vocab: int, umin: int, umax: int, zipf: float, seed: int,
                 chunk: int = 1 << 19) -> tuple[np.ndarray, np.ndarray]:
@@ -71,4 +77,17 @@ def make_config(cfg: int, seed: int = 0, n: int | None = None) -> dict:
     off, lab = make_labels(c["n"], c["vocab"], c["umin"], c["umax"], c["zipf"], seed)
     X = make_vectors(c["n"], c["d"], c["dist"], c["normalize"], seed)
     c.update(label_offsets=off, labels=lab, X=X, seed=seed)
+    return c
+
+
+def make_queries(seed: int = 0, nq: int | None = None) -> dict:
+    """Configuration-5 queries: vectors from ``default_rng([seed, 2])``, label sets from
+    the label stream seeded ``seed + 1_000_003``."""
+    c = dict(QUERIES)
+    if nq is not None:
+        c["nq"] = nq
+    off, lab = make_labels(c["nq"], c["vocab"], c["umin"], c["umax"], c["zipf"], seed + 1_000_003)
+    rng = np.random.default_rng([seed, 2])
+    Q = rng.standard_normal((c["nq"], c["d"]), dtype=np.float32)
+    c.update(label_offsets=off, labels=lab, Q=Q, seed=seed)
     return c

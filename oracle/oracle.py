@@ -98,6 +98,12 @@ class Oracle(_Lib):
         L.orc_cross_exact.restype = c_uint64
         L.orc_cross_exact.argtypes = [c_void_p, c_uint32, c_uint32, c_uint32, c_uint32, c_void_p, c_void_p,
                                       c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]
+        L.orc_ung_search.restype = None
+        L.orc_ung_search.argtypes = [c_void_p, c_uint32, c_uint32, c_void_p, c_void_p, c_void_p, c_uint32, c_void_p,
+                                     c_void_p, c_uint32, c_uint32, c_int, c_int, c_void_p, c_void_p]
+        L.orc_filtered_scan.restype = None
+        L.orc_filtered_scan.argtypes = [c_void_p, c_uint32, c_void_p, c_void_p, c_uint32, c_void_p, c_void_p,
+                                        c_uint32, c_int, c_int, c_void_p, c_void_p]
         L.orc_block_l2.restype = c_float
         L.orc_block_l2.argtypes = [c_void_p, c_void_p, c_uint32]
         L.orc_exact_knn_graph.restype = None
@@ -131,6 +137,30 @@ class Oracle(_Lib):
         """(from, to) additional edges in the reference's materialised order."""
         return self._additional(self.lib.orc_additional_edges, X, k, group_first, out_offsets, out_ids, cross_ids,
                                 fused)
+
+    def ung_search(self, X, offsets, cols, Q, entry_offsets, entry_ids, L: int, K: int, num_threads: int = 0):
+        """Greedy search of every query over the CSR graph: ids [nq x K] and distance counts [nq]."""
+        X, off, c, Q, eo, ei = _search_args(X, offsets, cols, Q, entry_offsets, entry_ids)
+        nq = Q.shape[0]
+        ids = np.empty(max(nq * K, 1), dtype=np.uint32)
+        cmps = np.empty(max(nq, 1), dtype=np.uint32)
+        self.lib.orc_ung_search(_p(X), X.shape[0], X.shape[1], _p(off), _p(c), _p(Q), nq, _p(eo), _p(ei), L, K,
+                                L2_REFERENCE_BUILD, num_threads, _p(ids), _p(cmps))
+        return ids[:nq * K].reshape(nq, K), cmps[:nq]
+
+    def filtered_scan(self, X, group_first, Q, target_offsets, target_ids, K: int, num_threads: int = 0):
+        """Filtered brute-force ground truth: ids and distances [nq x K]."""
+        X = np.ascontiguousarray(X, dtype=np.float32)
+        Q = np.ascontiguousarray(Q, dtype=np.float32)
+        gf = np.ascontiguousarray(group_first, dtype=np.uint32)
+        to = np.ascontiguousarray(target_offsets, dtype=np.uint64)
+        ti = np.ascontiguousarray(target_ids if len(target_ids) else [0], dtype=np.uint32)
+        nq = Q.shape[0]
+        ids = np.empty(max(nq * K, 1), dtype=np.uint32)
+        dists = np.empty(max(nq * K, 1), dtype=np.float32)
+        self.lib.orc_filtered_scan(_p(X), X.shape[1], _p(gf), _p(Q), nq, _p(to), _p(ti), K, L2_REFERENCE_BUILD,
+                                   num_threads, _p(ids), _p(dists))
+        return ids[:nq * K].reshape(nq, K), dists[:nq * K].reshape(nq, K)
 
     def l2(self, a: np.ndarray, b: np.ndarray, fused: int = L2_REFERENCE_BUILD) -> float:
         a = np.ascontiguousarray(a, dtype=np.float32)
@@ -190,6 +220,34 @@ class Reference(_Lib):
         L.ungref_additional_edges.restype = c_uint64
         L.ungref_additional_edges.argtypes = [c_void_p, c_uint32, c_uint32, c_uint32, c_uint32, c_void_p,
                                               c_void_p, c_void_p, c_void_p, c_uint64, c_void_p, c_void_p]
+        L.ungref_ung_search.restype = None
+        L.ungref_ung_search.argtypes = [c_void_p, c_uint32, c_uint32, c_void_p, c_void_p, c_void_p, c_uint32,
+                                        c_void_p, c_void_p, c_uint32, c_uint32, c_void_p]
+        L.ungref_filtered_scan.restype = None
+        L.ungref_filtered_scan.argtypes = [c_void_p, c_uint32, c_void_p, c_void_p, c_uint32, c_void_p, c_void_p,
+                                           c_uint32, c_void_p, c_void_p]
+
+    def ung_search(self, X, offsets, cols, Q, entry_offsets, entry_ids, L: int, K: int):
+        """iterate_to_fixed_point over the reference's SearchQueue (single thread): ids [nq x K]."""
+        X, off, c, Q, eo, ei = _search_args(X, offsets, cols, Q, entry_offsets, entry_ids)
+        nq = Q.shape[0]
+        ids = np.empty(max(nq * K, 1), dtype=np.uint32)
+        self.lib.ungref_ung_search(_p(X), X.shape[0], X.shape[1], _p(off), _p(c), _p(Q), nq, _p(eo), _p(ei), L, K,
+                                   _p(ids))
+        return ids[:nq * K].reshape(nq, K)
+
+    def filtered_scan(self, X, group_first, Q, target_offsets, target_ids, K: int):
+        """FilteredScan::answer_one_query over the reference's SearchQueue: ids and distances [nq x K]."""
+        X = np.ascontiguousarray(X, dtype=np.float32)
+        Q = np.ascontiguousarray(Q, dtype=np.float32)
+        gf = np.ascontiguousarray(group_first, dtype=np.uint32)
+        to = np.ascontiguousarray(target_offsets, dtype=np.uint64)
+        ti = np.ascontiguousarray(target_ids if len(target_ids) else [0], dtype=np.uint32)
+        nq = Q.shape[0]
+        ids = np.empty(max(nq * K, 1), dtype=np.uint32)
+        dists = np.empty(max(nq * K, 1), dtype=np.float32)
+        self.lib.ungref_filtered_scan(_p(X), X.shape[1], _p(gf), _p(Q), nq, _p(to), _p(ti), K, _p(ids), _p(dists))
+        return ids[:nq * K].reshape(nq, K), dists[:nq * K].reshape(nq, K)
 
     def additional_edges(self, X, k, group_first, out_offsets, out_ids, cross_ids):
         """(from, to) additional edges in the reference's materialised order."""
@@ -236,3 +294,89 @@ def reference() -> Reference | None:
 
 def lng_sets(out_offsets: np.ndarray, out_ids: np.ndarray, num_groups: int) -> list[frozenset]:
     return [frozenset(out_ids[out_offsets[g]:out_offsets[g + 1]].tolist()) for g in range(num_groups + 1)]
+
+
+def _search_args(X, offsets, cols, Q, entry_offsets, entry_ids):
+    X = np.ascontiguousarray(X, dtype=np.float32)
+    off = np.ascontiguousarray(offsets, dtype=np.uint64)
+    c = np.ascontiguousarray(cols if len(cols) else [0], dtype=np.uint32)
+    Q = np.ascontiguousarray(Q, dtype=np.float32)
+    eo = np.ascontiguousarray(entry_offsets, dtype=np.uint64)
+    ei = np.ascontiguousarray(entry_ids if len(entry_ids) else [0], dtype=np.uint32)
+    return X, off, c, Q, eo, ei
+
+
+def query_groups(set_offsets: np.ndarray, set_labels: np.ndarray, query_offsets: np.ndarray,
+                 query_labels: np.ndarray):
+    """Per query label set, over the base groups 1..G and their sorted label sets:
+
+    * the containment targets, every group whose set includes the query's (ascending
+      group id): the groups FilteredScan scans (filtered_scan.cpp:131-154);
+    * the minimal ones among them, no other target's set strictly inside theirs: the
+      entry groups of a containment query (get_min_super_sets with avoid_self false,
+      UNG/codes/src/uni_nav_graph_label_graph.cpp:45-54; get_entry_points,
+      UNG/codes/src/uni_nav_graph_search_backend.cpp:169-198).
+
+    Returned as two CSR pairs (offsets uint64 [nq+1], group ids uint32)."""
+    G = set_offsets.shape[0] - 2
+    sets = [frozenset(set_labels[set_offsets[g]:set_offsets[g + 1]].tolist()) for g in range(G + 1)]
+    labels = sorted(set().union(*sets[1:], set(query_labels.tolist())))
+    bit = {lab: 1 << i for i, lab in enumerate(labels)}
+    masks = [sum(bit[x] for x in s) for s in sets]
+    nq = query_offsets.shape[0] - 1
+    t_off, t_ids, m_off, m_ids = [0], [], [0], []
+    for q in range(nq):
+        qm = sum(bit[x] for x in query_labels[query_offsets[q]:query_offsets[q + 1]].tolist())
+        tg = [g for g in range(1, G + 1) if masks[g] & qm == qm]
+        tm = [masks[g] for g in tg]
+        mins = [g for g, m in zip(tg, tm) if not any(o != m and o & m == o for o in tm)]
+        t_ids += tg
+        m_ids += mins
+        t_off.append(len(t_ids))
+        m_off.append(len(m_ids))
+    return (np.array(t_off, dtype=np.uint64), np.array(t_ids, dtype=np.uint32),
+            np.array(m_off, dtype=np.uint64), np.array(m_ids, dtype=np.uint32))
+
+
+def entry_points(group_first: np.ndarray, group_entry: np.ndarray, entry_offsets: np.ndarray,
+                 entry_groups: np.ndarray, num_entry_points: int = 16, seed: int = 0):
+    """Entry vectors of every query, get_entry_points_given_group_id
+    (UNG/codes/src/uni_nav_graph_search_backend.cpp:200-228) per entry group in order:
+    a group of at most num_entry_points vectors gives all of them; a larger one gives its
+    entry point, then for i = 1 .. num_entry_points-1 the vector first + i whenever the
+    random draw of that step hits a vector not drawn before (the reference appends
+    first + i, not the drawn vector).  The reference draws with the C library's rand(),
+    shared by its search threads; here each query has its own seeded generator.
+    group_entry holds each group's entry point as a local index (0 .. size-1)."""
+    nq = entry_offsets.shape[0] - 1
+    off, ids = [0], []
+    for q in range(nq):
+        rng = np.random.default_rng([seed, q])
+        marked = set()
+        for g in entry_groups[entry_offsets[q]:entry_offsets[q + 1]].tolist():
+            first, last = int(group_first[g]), int(group_first[g + 1])
+            size = last - first
+            if size <= num_entry_points:
+                ids += range(first, last)
+                continue
+            ep = first + int(group_entry[g])
+            marked.add(ep)
+            ids.append(ep)
+            draws = rng.integers(0, size, size=num_entry_points - 1)
+            for i in range(1, num_entry_points):
+                r = first + int(draws[i - 1])
+                if r not in marked:
+                    marked.add(r)
+                    ids.append(first + i)
+        off.append(len(ids))
+    return np.array(off, dtype=np.uint64), np.array(ids, dtype=np.uint32)
+
+
+def recall_at_k(result_ids: np.ndarray, truth_ids: np.ndarray) -> float:
+    """Mean over queries of |result ∩ truth| / |truth| (truth without empty slots)."""
+    tot, hit = 0, 0
+    for r, t in zip(result_ids, truth_ids):
+        ts = set(t.tolist()) - {0xFFFFFFFF}
+        tot += len(ts)
+        hit += len(ts & set(r.tolist()))
+    return hit / max(tot, 1)

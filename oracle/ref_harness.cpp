@@ -14,6 +14,8 @@
 //              (append_cross_edges_from_target_range + build_cross_edges_generate_cpu_exact_scan)
 //   additional UNG/codes/src/uni_nav_graph_cross_edges.cpp:442-596
 //              (build_cross_edges_generate_additional, exact variant)
+//   search     UNG/codes/src/uni_nav_graph_search_backend.cpp:242-283 (iterate_to_fixed_point)
+//   truth      UNG/codes/src/filtered_scan.cpp:157-194          (FilteredScan::answer_one_query)
 //
 // The reference sources themselves are compiled from where they lie by
 // oracle/Makefile into oracle/_ref/; nothing from them is copied here.
@@ -343,5 +345,70 @@ int ungref_graph_save_text(const char *path, uint32_t num_points, const uint64_t
    g.save(fn);
    g.clean();
    return 0;
+}
+
+// Greedy search of a built index, step for step iterate_to_fixed_point over the
+// reference's own SearchQueue (capacity L, expanded flags) and distance handler:
+// the given entry points, then the closest unexpanded candidate is expanded and every
+// unvisited neighbour inserted, until none is left.  Result: the queue's first K ids.
+void ungref_ung_search(const float *X, uint32_t n, uint32_t d, const uint64_t *offsets, const uint32_t *cols,
+                       const float *Q, uint32_t nq, const uint64_t *entry_offsets, const uint32_t *entry_ids,
+                       uint32_t L, uint32_t K, uint32_t *ids)
+{
+   ANNS::FloatL2DistanceHandler dist;
+   const char *base = reinterpret_cast<const char *>(X);
+   const size_t row = size_t(d) * sizeof(float);
+   std::vector<uint8_t> visited(n);
+   ANNS::SearchQueue sq;
+   sq.reserve(int32_t(L));
+   for (uint32_t qi = 0; qi < nq; ++qi)
+   {
+      const char *query = reinterpret_cast<const char *>(Q + size_t(qi) * d);
+      sq.clear();
+      std::fill(visited.begin(), visited.end(), 0);
+      for (uint64_t e = entry_offsets[qi]; e < entry_offsets[qi + 1]; ++e)
+         sq.insert(entry_ids[e], dist.compute(query, base + entry_ids[e] * row, d));
+      while (sq.has_unexpanded_node())
+      {
+         const IdxType u = sq.get_closest_unexpanded().id;
+         for (uint64_t j = offsets[u]; j < offsets[u + 1]; ++j)
+         {
+            const IdxType w = cols[j];
+            if (visited[w])
+               continue;
+            visited[w] = 1;
+            sq.insert(w, dist.compute(query, base + w * row, d));
+         }
+      }
+      for (uint32_t r = 0; r < K; ++r)
+         ids[size_t(qi) * K + r] = int32_t(r) < sq.size() ? sq[r].id : UINT32_MAX;
+   }
+}
+
+// Filtered ground truth: every vector of the query's target groups into a
+// reference SearchQueue of capacity K, groups in the given order.
+void ungref_filtered_scan(const float *X, uint32_t d, const uint32_t *group_first, const float *Q, uint32_t nq,
+                          const uint64_t *target_offsets, const uint32_t *target_ids, uint32_t K, uint32_t *ids,
+                          float *dists)
+{
+   ANNS::FloatL2DistanceHandler dist;
+   const char *base = reinterpret_cast<const char *>(X);
+   const size_t row = size_t(d) * sizeof(float);
+#pragma omp parallel for schedule(dynamic, 1)
+   for (int64_t qi = 0; qi < int64_t(nq); ++qi)
+   {
+      const char *query = reinterpret_cast<const char *>(Q + size_t(qi) * d);
+      ANNS::SearchQueue sq;
+      sq.reserve(int32_t(K));
+      for (uint64_t t = target_offsets[qi]; t < target_offsets[qi + 1]; ++t)
+         for (uint32_t x = group_first[target_ids[t]]; x < group_first[target_ids[t] + 1]; ++x)
+            sq.insert(x, dist.compute(query, base + x * row, d));
+      for (uint32_t r = 0; r < K; ++r)
+      {
+         const bool have = int32_t(r) < sq.size();
+         ids[size_t(qi) * K + r] = have ? sq[r].id : UINT32_MAX;
+         dists[size_t(qi) * K + r] = have ? sq[r].distance : std::numeric_limits<float>::infinity();
+      }
+   }
 }
 } // extern "C"

@@ -708,3 +708,143 @@ void orc_exact_knn_graph(const float *X, uint32_t d, uint32_t num_groups, const 
    }
    free(base);
 }
+
+/* ------------------------------------------------------------------ filtered search
+ * Downstream check of a built index (benchmark configuration 5): UNG greedy search
+ * over a CSR graph, and the brute-force filtered ground truth.
+ *
+ *   orc_ung_search      UniNavGraph::iterate_to_fixed_point,
+ *                       UNG/codes/src/uni_nav_graph_search_backend.cpp:242-283, with the
+ *                       expanded-flag queue of SearchQueue (search_queue.cpp:26-69):
+ *                       capacity L, the closest unexpanded candidate is expanded, every
+ *                       unvisited neighbour is inserted; the result is the first K
+ *                       entries.  Entry points come from the caller (one list per query).
+ *   orc_filtered_scan   FilteredScan::answer_one_query, UNG/codes/src/filtered_scan.cpp:
+ *                       157-194: every vector of the target groups into a queue of K.
+ *
+ * Ids are the reordered ids of X throughout. */
+typedef struct
+{
+   uint32_t id;
+   float dist;
+   uint8_t expanded;
+} orc_scand;
+
+static void orc_squeue_insert(orc_scand *q, int32_t *size, int32_t cap, int32_t *cur, uint32_t id, float dist)
+{
+   orc_cand c = {id, dist};
+   if (*size == cap)
+   {
+      orc_cand last = {q[*size - 1].id, q[*size - 1].dist};
+      if (cand_less(last, c))
+         return;
+   }
+   int32_t lo = 0, hi = *size;
+   while (lo < hi)
+   {
+      int32_t mid = (lo + hi) >> 1;
+      orc_cand m = {q[mid].id, q[mid].dist};
+      if (cand_less(c, m))
+         hi = mid;
+      else if (m.id == c.id)
+         return;
+      else
+         lo = mid + 1;
+   }
+   if (lo < cap)
+      memmove(&q[lo + 1], &q[lo], (size_t)(*size - lo) * sizeof(orc_scand));
+   q[lo].id = id;
+   q[lo].dist = dist;
+   q[lo].expanded = 0;
+   if (*size < cap)
+      (*size)++;
+   if (lo < *cur)
+      *cur = lo;
+}
+
+/* Per query q: entries entry_ids[entry_offsets[q] .. entry_offsets[q+1]), search queue
+ * of capacity L (L >= K), result ids[q*K .. +K) (UINT32_MAX where the queue holds fewer)
+ * and the number of distance computations per query in cmps (may be NULL). */
+void orc_ung_search(const float *X, uint32_t n, uint32_t d, const uint64_t *offsets, const uint32_t *cols,
+                    const float *Q, uint32_t nq, const uint64_t *entry_offsets, const uint32_t *entry_ids,
+                    uint32_t L, uint32_t K, int fused, int num_threads, uint32_t *ids, uint32_t *cmps)
+{
+   if (num_threads > 0)
+      omp_set_num_threads(num_threads);
+#pragma omp parallel
+   {
+      orc_scand *q = (orc_scand *)malloc(sizeof(orc_scand) * ((size_t)L + 1));
+      uint32_t *stamp = (uint32_t *)calloc(n ? n : 1, sizeof(uint32_t));
+      uint32_t epoch = 0;
+#pragma omp for schedule(dynamic, 16)
+      for (int64_t qi = 0; qi < (int64_t)nq; ++qi)
+      {
+         const float *qv = Q + (size_t)qi * d;
+         int32_t size = 0, cur = 0;
+         uint32_t ncmp = 0;
+         ++epoch; /* a fresh visited set per query (clear_visited_set) */
+         for (uint64_t e = entry_offsets[qi]; e < entry_offsets[qi + 1]; ++e)
+         {
+            const uint32_t v = entry_ids[e];
+            orc_squeue_insert(q, &size, (int32_t)L, &cur, v, orc_l2(qv, X + (size_t)v * d, d, fused));
+            ++ncmp;
+         }
+         while (cur < size)
+         {
+            const int32_t pre = cur;
+            q[cur].expanded = 1;
+            while (cur < size && q[cur].expanded)
+               ++cur;
+            const uint32_t u = q[pre].id;
+            for (uint64_t j = offsets[u]; j < offsets[u + 1]; ++j)
+            {
+               const uint32_t w = cols[j];
+               if (stamp[w] == epoch)
+                  continue;
+               stamp[w] = epoch;
+               orc_squeue_insert(q, &size, (int32_t)L, &cur, w, orc_l2(qv, X + (size_t)w * d, d, fused));
+               ++ncmp;
+            }
+         }
+         for (uint32_t r = 0; r < K; ++r)
+            ids[(size_t)qi * K + r] = (int32_t)r < size ? q[r].id : UINT32_MAX;
+         if (cmps)
+            cmps[qi] = ncmp;
+      }
+      free(q);
+      free(stamp);
+   }
+}
+
+/* Per query q: the K nearest vectors over the row ranges of its target groups,
+ * target_ids[target_offsets[q] .. target_offsets[q+1]) (group ids 1..G, rows
+ * [group_first[g], group_first[g+1])), in that order.  ids/dists [nq x K]. */
+void orc_filtered_scan(const float *X, uint32_t d, const uint32_t *group_first, const float *Q, uint32_t nq,
+                       const uint64_t *target_offsets, const uint32_t *target_ids, uint32_t K, int fused,
+                       int num_threads, uint32_t *ids, float *dists)
+{
+   if (num_threads > 0)
+      omp_set_num_threads(num_threads);
+#pragma omp parallel
+   {
+      orc_cand *q = (orc_cand *)malloc(sizeof(orc_cand) * ((size_t)K + 1));
+#pragma omp for schedule(dynamic, 1)
+      for (int64_t qi = 0; qi < (int64_t)nq; ++qi)
+      {
+         const float *qv = Q + (size_t)qi * d;
+         int32_t size = 0;
+         for (uint64_t t = target_offsets[qi]; t < target_offsets[qi + 1]; ++t)
+         {
+            const uint32_t g = target_ids[t];
+            for (uint32_t x = group_first[g]; x < group_first[g + 1]; ++x)
+               orc_queue_insert(q, &size, (int32_t)K, x, orc_l2(qv, X + (size_t)x * d, d, fused));
+         }
+         for (uint32_t r = 0; r < K; ++r)
+         {
+            ids[(size_t)qi * K + r] = (int32_t)r < size ? q[r].id : UINT32_MAX;
+            dists[(size_t)qi * K + r] = (int32_t)r < size ? q[r].dist : INFINITY;
+         }
+      }
+      free(q);
+   }
+}
