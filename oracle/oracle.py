@@ -319,23 +319,36 @@ def query_groups(set_offsets: np.ndarray, set_labels: np.ndarray, query_offsets:
 
     Returned as two CSR pairs (offsets uint64 [nq+1], group ids uint32)."""
     G = set_offsets.shape[0] - 2
-    sets = [frozenset(set_labels[set_offsets[g]:set_offsets[g + 1]].tolist()) for g in range(G + 1)]
-    labels = sorted(set().union(*sets[1:], set(query_labels.tolist())))
-    bit = {lab: 1 << i for i, lab in enumerate(labels)}
-    masks = [sum(bit[x] for x in s) for s in sets]
-    nq = query_offsets.shape[0] - 1
+    so = set_offsets.astype(np.int64)
+    qo = query_offsets.astype(np.int64)
+    labels = np.unique(np.concatenate([set_labels, query_labels]).astype(np.int64))
+    if labels.size > 63:
+        raise ValueError("query_groups handles at most 63 distinct labels")
+    pos = np.searchsorted(labels, set_labels.astype(np.int64))
+    owner = np.repeat(np.arange(G + 1), np.diff(so))
+    masks = np.zeros(G + 1, dtype=np.int64)
+    np.bitwise_or.at(masks, owner, np.left_shift(np.int64(1), pos))
+    qpos = np.searchsorted(labels, query_labels.astype(np.int64))
+    nq = qo.shape[0] - 1
     t_off, t_ids, m_off, m_ids = [0], [], [0], []
+    exact = {int(m): g for g, m in enumerate(masks.tolist()) if g > 0}
     for q in range(nq):
-        qm = sum(bit[x] for x in query_labels[query_offsets[q]:query_offsets[q + 1]].tolist())
-        tg = [g for g in range(1, G + 1) if masks[g] & qm == qm]
-        tm = [masks[g] for g in tg]
-        mins = [g for g, m in zip(tg, tm) if not any(o != m and o & m == o for o in tm)]
-        t_ids += tg
-        m_ids += mins
-        t_off.append(len(t_ids))
-        m_off.append(len(m_ids))
-    return (np.array(t_off, dtype=np.uint64), np.array(t_ids, dtype=np.uint32),
-            np.array(m_off, dtype=np.uint64), np.array(m_ids, dtype=np.uint32))
+        qm = 0
+        for p in qpos[qo[q]:qo[q + 1]].tolist():
+            qm |= 1 << p
+        tg = np.nonzero((masks[1:] & qm) == qm)[0] + 1
+        if qm in exact:                     # the query's own set is a group: the only minimal one
+            mins = np.array([exact[qm]])
+        else:
+            tm = masks[tg]
+            inner = ((tm[None, :] & tm[:, None]) == tm[None, :]) & (tm[None, :] != tm[:, None])
+            mins = tg[~inner.any(axis=1)]
+        t_ids.append(tg)
+        m_ids.append(mins)
+        t_off.append(t_off[-1] + tg.size)
+        m_off.append(m_off[-1] + mins.size)
+    cat = lambda parts: np.concatenate(parts).astype(np.uint32) if parts else np.zeros(0, np.uint32)
+    return np.array(t_off, dtype=np.uint64), cat(t_ids), np.array(m_off, dtype=np.uint64), cat(m_ids)
 
 
 def entry_points(group_first: np.ndarray, group_entry: np.ndarray, entry_offsets: np.ndarray,

@@ -41,44 +41,54 @@ def intra_csr(graph_rows: np.ndarray, case: dict):
     return off, glob[mask].astype(np.uint32)
 
 
-def oracle_graph(case: dict):
-    """The whole index graph from the CPU oracle: CSR offsets, columns, and the groups'
-    entry points (local index per group 0..G, 0 unused)."""
-    orc = O.oracle()
-    cfg = knn_config()
-    rows, entry = orc.exact_knn_graph(case["Xr"], case["group_ranges"][2:], cfg.candidate_k, cfg.final_degree,
-                                      cfg.head_keep, cfg.anchor_tail, cfg.anchor_slots, cfg.bidir_anchor,
-                                      cfg.graph_stride)
-    i_off, i_cols = intra_csr(rows, case)
-    n, k = case["n"], case["k"]
-    ids, _, _ = orc.cross_exact(case["Xr"], k, case["group_first"], case["out_offsets"], case["out_ids"])
-    src, dst = orc.additional_edges(case["Xr"], k, case["group_first"], case["out_offsets"], case["out_ids"], ids)
-    cross = ids.reshape(n, k)
-    order = np.argsort(src, kind="stable")
-    a_off = np.zeros(n + 1, dtype=np.int64)
-    a_off[1:] = np.cumsum(np.bincount(src, minlength=n))
-    a_dst = dst[order]
-    rows_out = []
-    for v in range(n):
-        r = i_cols[i_off[v]:i_off[v + 1]].tolist()
-        r += [x for x in cross[v].tolist() if x != 0xFFFFFFFF]
-        r += a_dst[a_off[v]:a_off[v + 1]].tolist()
-        rows_out.append(r)
+def assemble_graph(n: int, intra_off, intra_cols, cross_ids: np.ndarray, add_from, add_to):
+    """Per point: intra-group edges, cross edges in queue order (empty slots dropped),
+    additional edges in list order, as CSR (offsets uint64 [n+1], columns uint32)."""
+    k = cross_ids.size // n
+    cross = cross_ids.reshape(n, k)
+    valid = cross != 0xFFFFFFFF
+    intra_pt = np.repeat(np.arange(n, dtype=np.int64), np.diff(intra_off.astype(np.int64)))
+    cross_pt = np.nonzero(valid)[0].astype(np.int64)
+    keys = np.concatenate([3 * intra_pt, 3 * cross_pt + 1, 3 * add_from.astype(np.int64) + 2])
+    vals = np.concatenate([intra_cols, cross[valid], add_to]).astype(np.uint32)
+    order = np.argsort(keys, kind="stable")
     off = np.zeros(n + 1, dtype=np.uint64)
-    off[1:] = np.cumsum([len(r) for r in rows_out])
-    cols = np.fromiter((x for r in rows_out for x in r), dtype=np.uint32, count=int(off[-1]))
+    off[1:] = np.cumsum(np.bincount(keys // 3, minlength=n))
+    return off, vals[order]
+
+
+def oracle_graph(case: dict, intra_rows=None, lib=None):
+    """The whole index graph from the CPU checkers: CSR offsets, columns, and the
+    groups' entry points (local index per group 0..G, 0 unused).  Cross and additional
+    edges come from ``lib`` (the C restatement by default; ``oracle.reference()`` for the
+    reference's own compiled code).  ``intra_rows`` replaces the oracle's kNN seeding
+    with given [degree, local ids ...] rows (entry points then 0, as the seeding writes)."""
+    lib = lib or O.oracle()
+    if intra_rows is None:
+        cfg = knn_config()
+        intra_rows, entry = O.oracle().exact_knn_graph(case["Xr"], case["group_ranges"][2:], cfg.candidate_k,
+                                                       cfg.final_degree, cfg.head_keep, cfg.anchor_tail,
+                                                       cfg.anchor_slots, cfg.bidir_anchor, cfg.graph_stride)
+    else:
+        entry = np.zeros(case["num_groups"], dtype=np.uint32)
+    i_off, i_cols = intra_csr(intra_rows, case)
+    n, k = case["n"], case["k"]
+    ids, _, _ = lib.cross_exact(case["Xr"], k, case["group_first"], case["out_offsets"], case["out_ids"])
+    src, dst = lib.additional_edges(case["Xr"], k, case["group_first"], case["out_offsets"], case["out_ids"], ids)
+    off, cols = assemble_graph(n, i_off, i_cols, ids, src, dst)
     group_entry = np.zeros(case["num_groups"] + 1, dtype=np.uint32)
     group_entry[1:] = entry
     return off, cols, group_entry
 
 
-def search_recall(case: dict, offsets, cols, group_entry):
+def search_recall(case: dict, offsets, cols, group_entry, truth=None):
     """Greedy search of every query (oracle restatement) and recall@K against the
-    filtered brute-force truth: (recall, result ids, truth ids)."""
+    filtered brute-force truth (computed unless given): (recall, result ids, truth ids)."""
     orc = O.oracle()
     eo, ei = O.entry_points(case["group_first"], group_entry, case["min_offsets"], case["min_ids"], case["E"],
                             seed=case["seed"])
     res, _ = orc.ung_search(case["Xr"], offsets, cols, case["Q"], eo, ei, case["L"], case["K"])
-    gt, _ = orc.filtered_scan(case["Xr"], case["group_first"], case["Q"], case["target_offsets"],
-                              case["target_ids"], case["K"])
-    return O.recall_at_k(res, gt), res, gt
+    if truth is None:
+        truth, _ = orc.filtered_scan(case["Xr"], case["group_first"], case["Q"], case["target_offsets"],
+                                     case["target_ids"], case["K"])
+    return O.recall_at_k(res, truth), res, truth
