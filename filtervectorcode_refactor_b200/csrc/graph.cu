@@ -181,6 +181,9 @@ __global__ void scan_add_kernel(uint64_t *__restrict__ data, uint32_t count, con
 }
 
 // Warp per point: intra edges, cross edges up to the first sentinel, additional edges.
+// The point's offsets and its first 32 cross slots are loaded together up front (one
+// slot per lane); the cross count is the position of the first sentinel, found by a
+// ballot instead of a serial walk of the row.
 __global__ void graph_fill_kernel(uint32_t n, uint32_t k, const uint64_t *__restrict__ intra_off,
                                   const uint32_t *__restrict__ intra_cols, const uint32_t *__restrict__ cross_ids,
                                   const uint64_t *__restrict__ add_off, const uint32_t *__restrict__ add_cols,
@@ -191,26 +194,35 @@ __global__ void graph_fill_kernel(uint32_t n, uint32_t k, const uint64_t *__rest
    for (uint64_t v = (uint64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; v < n; v += warps)
    {
       uint64_t w = offsets[v];
+      const uint64_t ia = intra_off ? intra_off[v] : 0, ib = intra_off ? intra_off[v + 1] : 0;
+      const uint64_t aa = add_off ? add_off[v] : 0, ab = add_off ? add_off[v + 1] : 0;
+      const uint32_t x0 = cross_ids && lane < k ? cross_ids[v * k + lane] : 0xFFFFFFFFu;
       if (intra_off)
       {
-         const uint64_t a = intra_off[v], b = intra_off[v + 1];
-         for (uint64_t i = a + lane; i < b; i += 32)
-            cols[w + (i - a)] = intra_cols[i];
-         w += b - a;
+         for (uint64_t i = ia + lane; i < ib; i += 32)
+            cols[w + (i - ia)] = intra_cols[i];
+         w += ib - ia;
       }
       if (cross_ids)
       {
-         const uint32_t c = cross_count(cross_ids, uint32_t(v), k);
-         for (uint32_t i = lane; i < c; i += 32)
-            cols[w + i] = cross_ids[v * k + i];
-         w += c;
+         uint32_t x = x0;
+         for (uint32_t base = 0;; base += 32) // warp-uniform: every lane sees the same ballot
+         {
+            const uint32_t empty = __ballot_sync(0xffffffffu, x == 0xFFFFFFFFu);
+            const uint32_t cnt = empty ? uint32_t(__ffs(empty) - 1) : 32u;
+            if (lane < cnt)
+               cols[w + base + lane] = x;
+            if (cnt < 32 || base + 32 >= k)
+            {
+               w += base + cnt;
+               break;
+            }
+            x = base + 32 + lane < k ? cross_ids[v * k + base + 32 + lane] : 0xFFFFFFFFu;
+         }
       }
       if (add_off)
-      {
-         const uint64_t a = add_off[v], b = add_off[v + 1];
-         for (uint64_t i = a + lane; i < b; i += 32)
-            cols[w + (i - a)] = add_cols[i];
-      }
+         for (uint64_t i = aa + lane; i < ab; i += 32)
+            cols[w + (i - aa)] = add_cols[i];
    }
 }
 
