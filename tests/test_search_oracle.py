@@ -100,3 +100,19 @@ def test_recall_counts_truth_slots():
     res = np.array([[1, 2, 3], [4, 5, 6]], dtype=np.uint32)
     gt = np.array([[3, 2, 9], [4, 0xFFFFFFFF, 0xFFFFFFFF]], dtype=np.uint32)
     assert O.recall_at_k(res, gt) == pytest.approx(3 / 4)
+
+
+def test_assemble_graph_order():
+    """Per point: intra edges, cross edges up to the first empty slot, additional edges
+    in list order; points without edges get empty rows."""
+    from search_case import assemble_graph
+    S = 0xFFFFFFFF
+    n, k = 4, 3
+    intra_off = np.array([0, 2, 2, 3, 3], dtype=np.uint64)
+    intra_cols = np.array([7, 8, 9], dtype=np.uint32)
+    cross = np.array([[1, 2, S], [S, S, S], [3, S, S], [4, 5, 6]], dtype=np.uint32).ravel()
+    add_from = np.array([3, 0, 3], dtype=np.uint32)
+    add_to = np.array([10, 11, 12], dtype=np.uint32)
+    off, cols = assemble_graph(n, intra_off, intra_cols, cross, add_from, add_to)
+    rows = [cols[off[v]:off[v + 1]].tolist() for v in range(n)]
+    assert rows == [[7, 8, 1, 2, 11], [], [9, 3], [4, 5, 6, 10, 12]]
