@@ -119,30 +119,47 @@ void build_lng(ungx_label_graph &g, int threads)
       max_len = std::max(max_len, set_len(f));
 
    // label sets of at most 64 distinct labels without repeats: the inverted lists carry
-   // each group's label mask, so the superset test is a sequential scan of 8-byte words
+   // each group's label mask, so the superset test is a sequential scan of 8-byte words.
+   // Each list is ordered by (set length, group id), the reference's visiting order, so
+   // a group scans only the entries longer than its own set and they come out in that
+   // order; a group of the longest length scans nothing.
    const bool fast = !has_dup && W == 1;
    std::vector<uint64_t> inv_mask(fast ? inv.size() : 0);
+   std::vector<uint32_t> inv_len(fast ? inv.size() : 0);
    if (fast)
+   {
+      parallel_for(L, threads, 1, [&](int64_t l) {
+         std::stable_sort(inv.begin() + inv_off[l], inv.begin() + inv_off[l + 1],
+                          [&](uint32_t a, uint32_t b) { return set_len(a) < set_len(b); });
+      });
       for (size_t j = 0; j < inv.size(); ++j)
+      {
          inv_mask[j] = masks[inv[j]];
+         inv_len[j] = set_len(inv[j]);
+      }
+   }
    std::vector<std::vector<uint32_t>> outs(G + 1);
    parallel_for(G, threads, 64, [&](int64_t i) {
       const uint32_t f = (uint32_t)i + 1;
       const uint32_t flen = set_len(f);
       if (fast)
       {
-         // candidates: strict supersets among the groups holding f's rarest label, in
+         // candidates: strict supersets among the groups holding one of f's labels, in
          // the reference's visiting order (label-set length, then group id); a candidate
          // is kept unless a kept shorter one is included in it
+         // candidates: the entries longer than f's set in the list, among f's labels,
+         // that has the fewest of them
          const uint64_t mf = masks[f];
          uint64_t best_n = UINT64_MAX, best_off = 0;
          for (uint64_t j = g.set_off[f]; j < g.set_off[f + 1]; ++j)
          {
             const uint32_t l = dense[j];
-            if (inv_off[l + 1] - inv_off[l] < best_n)
+            const uint32_t *lb = inv_len.data() + inv_off[l], *le = inv_len.data() + inv_off[l + 1];
+            const uint64_t a = inv_off[l] + (std::upper_bound(lb, le, flen) - lb);
+            if (inv_off[l + 1] - a < best_n)
             {
-               best_n = inv_off[l + 1] - inv_off[l];
-               best_off = inv_off[l];
+               best_n = inv_off[l + 1] - a;
+               best_off = a;
             }
          }
          std::vector<std::pair<uint32_t, uint32_t>> sup; // (length, group)
@@ -151,15 +168,17 @@ void build_lng(ungx_label_graph &g, int threads)
             for (uint32_t c = 1; c <= G; ++c)
                if (c != f)
                   sup.push_back({set_len(c), c});
+            std::sort(sup.begin(), sup.end());
          }
          else
+         {
             for (uint64_t j = best_off; j < best_off + best_n; ++j)
             {
                const uint64_t m = inv_mask[j];
-               if ((m & mf) == mf && m != mf)
-                  sup.push_back({(uint32_t)__builtin_popcountll(m), inv[j]});
+               if ((m & mf) == mf)
+                  sup.push_back({inv_len[j], inv[j]});
             }
-         std::sort(sup.begin(), sup.end());
+         }
          std::vector<uint32_t> kept;
          std::vector<uint64_t> kept_mask;
          std::vector<uint32_t> kept_len;
@@ -276,48 +295,55 @@ int ungx_label_graph_build(uint32_t n, const uint64_t *label_offsets, const uint
       });
       // first-appearance group ids (serial: the order is the definition).  The open
       // addressing table holds the groups, not the points: it starts small and doubles
-      // at half load, so it stays cache-resident when groups are far fewer than points.
+      // at half load.  Each slot keeps its group's hash, and each group's sorted labels
+      // are appended to a compact per-group store as the group is created, so a probe
+      // reads only the table and that store (cache-resident when groups are far fewer
+      // than points), never another point's arrays.
       uint64_t cap = 1024;
-      std::vector<uint32_t> slot_rep(cap), slot_gid(cap, 0);
-      std::vector<uint32_t> point_gid(n), rep;
-      rep.push_back(0);
+      std::vector<uint64_t> slot_hash(cap, 0);
+      std::vector<uint32_t> slot_gid(cap, 0);
+      std::vector<uint32_t> point_gid(n);
+      std::vector<uint64_t> group_hash(1, 0), gset_off(2, 0); // group g's labels: [gset_off[g], gset_off[g+1])
+      std::vector<uint32_t> gset;
       uint32_t G = 0;
       auto grow = [&]() {
          cap <<= 1;
-         slot_rep.assign(cap, 0);
+         slot_hash.assign(cap, 0);
          slot_gid.assign(cap, 0);
          for (uint32_t gid = 1; gid <= G; ++gid)
          {
-            uint64_t q = h[rep[gid]] & (cap - 1);
+            uint64_t q = group_hash[gid] & (cap - 1);
             while (slot_gid[q] != 0)
                q = (q + 1) & (cap - 1);
             slot_gid[q] = gid;
-            slot_rep[q] = rep[gid];
+            slot_hash[q] = group_hash[gid];
          }
       };
       for (uint32_t v = 0; v < n; ++v)
       {
          const uint32_t len = (uint32_t)(label_offsets[v + 1] - label_offsets[v]);
          const uint32_t *s = sl.data() + label_offsets[v];
-         uint64_t p = h[v] & (cap - 1);
+         const uint64_t hv = h[v];
+         uint64_t p = hv & (cap - 1);
          for (;;)
          {
-            if (slot_gid[p] == 0)
+            const uint32_t gid = slot_gid[p];
+            if (gid == 0)
             {
                slot_gid[p] = ++G;
-               slot_rep[p] = v;
-               rep.push_back(v);
+               slot_hash[p] = hv;
+               group_hash.push_back(hv);
+               gset.insert(gset.end(), s, s + len);
+               gset_off.push_back(gset.size());
                point_gid[v] = G;
                if (2ull * G > cap)
                   grow();
                break;
             }
-            const uint32_t r = slot_rep[p];
-            const uint32_t rlen = (uint32_t)(label_offsets[r + 1] - label_offsets[r]);
-            if (h[r] == h[v] && rlen == len &&
-                std::memcmp(sl.data() + label_offsets[r], s, len * sizeof(uint32_t)) == 0)
+            if (slot_hash[p] == hv && gset_off[gid + 1] - gset_off[gid] == len &&
+                std::memcmp(gset.data() + gset_off[gid], s, len * sizeof(uint32_t)) == 0)
             {
-               point_gid[v] = slot_gid[p];
+               point_gid[v] = gid;
                break;
             }
             p = (p + 1) & (cap - 1);
@@ -342,14 +368,9 @@ int ungx_label_graph_build(uint32_t n, const uint64_t *label_offsets, const uint
          for (uint32_t v = 0; v < n; ++v)
             g->new_to_old[fill[point_gid[v]]++] = v;
       }
-      // group label sets
-      g->set_off.assign(G + 2, 0);
-      for (uint32_t gid = 1; gid <= G; ++gid)
-         g->set_off[gid + 1] = g->set_off[gid] + (label_offsets[rep[gid] + 1] - label_offsets[rep[gid]]);
-      g->set_labels.resize(g->set_off[G + 1]);
-      for (uint32_t gid = 1; gid <= G; ++gid)
-         std::copy(sl.begin() + label_offsets[rep[gid]], sl.begin() + label_offsets[rep[gid] + 1],
-                   g->set_labels.begin() + g->set_off[gid]);
+      // group label sets: the store the grouping pass filled
+      g->set_off = std::move(gset_off);
+      g->set_labels = std::move(gset);
       build_lng(*g, threads);
       *out = g.release();
       return UNGX_OK;
