@@ -85,3 +85,26 @@ def test_label_graph_matches_reference_trie(vocab):
     got_sets = O.lng_sets(np.asarray(lg.out_offsets), np.asarray(lg.out_ids), G)
     exp_sets = O.lng_sets(exp["out_offsets"], exp["out_ids"], G)
     assert got_sets == exp_sets
+
+
+def test_out_list_order_changes_only_row_order_of_additional_edges(golden):
+    """The library returns each LNG out list in ascending group id; the reference keeps
+    the order its trie search found them in (a breadth-first walk over hash-map children,
+    uni_nav_graph_label_graph.cpp:103-206 and trie.cpp:78-143), which it never sorts.
+    Cross edges depend only on the sets.  Additional edges follow the out-list order
+    given to them: with either order the same (from, to) edges come out, and each
+    point gets the same set, so a greedy search over the graph is unchanged."""
+    from filtervectorcode_refactor_b200 import _native as nat
+    g = golden
+    G, k, n = g["num_groups"], g["k"], g["Xr"].shape[0]
+    lg = nat.LabelGraph(g["label_offsets"], g["labels"])
+    assert O.lng_sets(lg.out_offsets, lg.out_ids, G) == O.lng_sets(g["out_offsets"], g["out_ids"], G)
+    for f in range(1, G + 1):
+        row = lg.out_ids[lg.out_offsets[f]:lg.out_offsets[f + 1]]
+        assert np.all(row[1:] > row[:-1])
+    orc = O.oracle()
+    ref_order = orc.additional_edges(g["Xr"], k, g["group_first"], g["out_offsets"], g["out_ids"], g["ids"])
+    lib_order = orc.additional_edges(g["Xr"], k, g["group_first"], lg.out_offsets, lg.out_ids, g["ids"])
+    assert np.array_equal(ref_order[0], g["add_from"]) and np.array_equal(ref_order[1], g["add_to"])
+    pairs = lambda s, t: sorted(zip(s.tolist(), t.tolist()))
+    assert pairs(*ref_order) == pairs(*lib_order)

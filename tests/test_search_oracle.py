@@ -116,3 +116,16 @@ def test_assemble_graph_order():
     off, cols = assemble_graph(n, intra_off, intra_cols, cross, add_from, add_to)
     rows = [cols[off[v]:off[v + 1]].tolist() for v in range(n)]
     assert rows == [[7, 8, 1, 2, 11], [], [9, 3], [4, 5, 6, 10, 12]]
+
+
+def test_search_ignores_column_order_within_rows(case, graph):
+    """One expansion inserts all of a node's unvisited neighbours before the next one
+    starts, and the bounded queue keeps the best L of what it has seen, so the result
+    does not depend on the order of a row's columns (e.g. of its additional edges)."""
+    off, cols, ge = graph
+    rev = cols.copy()
+    for v in range(case["n"]):
+        rev[off[v]:off[v + 1]] = cols[off[v]:off[v + 1]][::-1]
+    r1, res1, _ = search_recall(case, off, cols, ge)
+    r2, res2, _ = search_recall(case, off, rev, ge)
+    assert np.array_equal(res1, res2) and r1 == r2
