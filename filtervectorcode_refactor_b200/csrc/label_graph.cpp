@@ -60,6 +60,60 @@ inline uint64_t hash_seq(const uint32_t *s, uint32_t len)
    return h ^ (h >> 31);
 }
 
+// Groups by exact label sequence, numbered 1.. in the order they are first added.
+// Open addressing over the groups (not the points): it starts small and doubles at
+// half load.  Each slot keeps its group's hash, and each group's labels go to a compact
+// store when the group is created, so a probe reads only the table and that store.
+struct GroupTable
+{
+   uint64_t cap = 1024;
+   std::vector<uint64_t> slot_hash = std::vector<uint64_t>(1024, 0);
+   std::vector<uint32_t> slot_gid = std::vector<uint32_t>(1024, 0);
+   std::vector<uint64_t> hash = std::vector<uint64_t>(1, 0); // per group, index 0 unused
+   std::vector<uint64_t> set_off = std::vector<uint64_t>(2, 0); // group g: [set_off[g], set_off[g+1])
+   std::vector<uint32_t> set;
+   uint32_t count = 0;
+
+   uint32_t find_or_add(uint64_t h, const uint32_t *s, uint32_t len)
+   {
+      uint64_t p = h & (cap - 1);
+      for (;;)
+      {
+         const uint32_t gid = slot_gid[p];
+         if (gid == 0)
+         {
+            slot_gid[p] = ++count;
+            slot_hash[p] = h;
+            hash.push_back(h);
+            set.insert(set.end(), s, s + len);
+            set_off.push_back(set.size());
+            if (2ull * count > cap)
+               grow();
+            return count;
+         }
+         if (slot_hash[p] == h && set_off[gid + 1] - set_off[gid] == len &&
+             std::memcmp(set.data() + set_off[gid], s, len * sizeof(uint32_t)) == 0)
+            return gid;
+         p = (p + 1) & (cap - 1);
+      }
+   }
+
+   void grow()
+   {
+      cap <<= 1;
+      slot_hash.assign(cap, 0);
+      slot_gid.assign(cap, 0);
+      for (uint32_t gid = 1; gid <= count; ++gid)
+      {
+         uint64_t q = hash[gid] & (cap - 1);
+         while (slot_gid[q] != 0)
+            q = (q + 1) & (cap - 1);
+         slot_gid[q] = gid;
+         slot_hash[q] = hash[gid];
+      }
+   }
+};
+
 void build_lng(ungx_label_graph &g, int threads)
 {
    const uint32_t G = g.num_groups;
@@ -293,62 +347,42 @@ int ungx_label_graph_build(uint32_t n, const uint64_t *label_offsets, const uint
          std::sort(b, e);
          h[v] = hash_seq(b, (uint32_t)(e - b));
       });
-      // first-appearance group ids (serial: the order is the definition).  The open
-      // addressing table holds the groups, not the points: it starts small and doubles
-      // at half load.  Each slot keeps its group's hash, and each group's sorted labels
-      // are appended to a compact per-group store as the group is created, so a probe
-      // reads only the table and that store (cache-resident when groups are far fewer
-      // than points), never another point's arrays.
-      uint64_t cap = 1024;
-      std::vector<uint64_t> slot_hash(cap, 0);
-      std::vector<uint32_t> slot_gid(cap, 0);
+      // first-appearance group ids.  The order is the definition, so the points are cut
+      // into contiguous chunks, each numbered by its own table in parallel (local ids in
+      // first-appearance order within the chunk), and the chunks' groups are then added
+      // to one table in chunk order and local-id order: a group first seen at point v
+      // gets its id after every group first seen before v, as in one serial pass.
       std::vector<uint32_t> point_gid(n);
-      std::vector<uint64_t> group_hash(1, 0), gset_off(2, 0); // group g's labels: [gset_off[g], gset_off[g+1])
-      std::vector<uint32_t> gset;
-      uint32_t G = 0;
-      auto grow = [&]() {
-         cap <<= 1;
-         slot_hash.assign(cap, 0);
-         slot_gid.assign(cap, 0);
-         for (uint32_t gid = 1; gid <= G; ++gid)
-         {
-            uint64_t q = group_hash[gid] & (cap - 1);
-            while (slot_gid[q] != 0)
-               q = (q + 1) & (cap - 1);
-            slot_gid[q] = gid;
-            slot_hash[q] = group_hash[gid];
-         }
-      };
-      for (uint32_t v = 0; v < n; ++v)
+      const int hw = threads > 0 ? threads : (int)std::max(1u, std::thread::hardware_concurrency());
+      const uint32_t nchunks = n >= (1u << 18) ? (uint32_t)std::min<int64_t>(hw, n >> 16) : 1u;
+      std::vector<GroupTable> local(nchunks);
+      auto chunk_lo = [&](uint32_t c) { return (uint32_t)((uint64_t)n * c / nchunks); };
+      parallel_for(nchunks, threads, 1, [&](int64_t c) {
+         GroupTable &t = local[c];
+         for (uint32_t v = chunk_lo((uint32_t)c); v < chunk_lo((uint32_t)c + 1); ++v)
+            point_gid[v] = t.find_or_add(h[v], sl.data() + label_offsets[v],
+                                         (uint32_t)(label_offsets[v + 1] - label_offsets[v]));
+      });
+      GroupTable global;
+      std::vector<std::vector<uint32_t>> to_global(nchunks);
+      for (uint32_t c = 0; c < nchunks; ++c)
       {
-         const uint32_t len = (uint32_t)(label_offsets[v + 1] - label_offsets[v]);
-         const uint32_t *s = sl.data() + label_offsets[v];
-         const uint64_t hv = h[v];
-         uint64_t p = hv & (cap - 1);
-         for (;;)
-         {
-            const uint32_t gid = slot_gid[p];
-            if (gid == 0)
-            {
-               slot_gid[p] = ++G;
-               slot_hash[p] = hv;
-               group_hash.push_back(hv);
-               gset.insert(gset.end(), s, s + len);
-               gset_off.push_back(gset.size());
-               point_gid[v] = G;
-               if (2ull * G > cap)
-                  grow();
-               break;
-            }
-            if (slot_hash[p] == hv && gset_off[gid + 1] - gset_off[gid] == len &&
-                std::memcmp(gset.data() + gset_off[gid], s, len * sizeof(uint32_t)) == 0)
-            {
-               point_gid[v] = gid;
-               break;
-            }
-            p = (p + 1) & (cap - 1);
-         }
+         const GroupTable &t = local[c];
+         to_global[c].resize(t.count + 1, 0);
+         for (uint32_t lg = 1; lg <= t.count; ++lg)
+            to_global[c][lg] = global.find_or_add(t.hash[lg], t.set.data() + t.set_off[lg],
+                                                  (uint32_t)(t.set_off[lg + 1] - t.set_off[lg]));
       }
+      if (nchunks > 1)
+         parallel_for(nchunks, threads, 1, [&](int64_t c) {
+            const std::vector<uint32_t> &m = to_global[c];
+            for (uint32_t v = chunk_lo((uint32_t)c); v < chunk_lo((uint32_t)c + 1); ++v)
+               point_gid[v] = m[point_gid[v]];
+         });
+      local.clear();
+      const uint32_t G = global.count;
+      std::vector<uint64_t> gset_off = std::move(global.set_off);
+      std::vector<uint32_t> gset = std::move(global.set);
       g->num_groups = G;
       // reorder
       std::vector<uint32_t> first(G + 2, 0);

@@ -108,3 +108,26 @@ def test_out_list_order_changes_only_row_order_of_additional_edges(golden):
     assert np.array_equal(ref_order[0], g["add_from"]) and np.array_equal(ref_order[1], g["add_to"])
     pairs = lambda s, t: sorted(zip(s.tolist(), t.tolist()))
     assert pairs(*ref_order) == pairs(*lib_order)
+
+
+@pytest.mark.parametrize("threads", [1, 3, 8])
+def test_chunked_grouping_matches_serial_oracle(threads):
+    """Above 2^18 points the grouping runs in parallel chunks merged in order; the
+    group ids, reorder and LNG must equal a serial first-appearance pass, including
+    empty label sets and groups whose first point sits late in a chunk."""
+    from filtervectorcode_refactor_b200 import _native as nat
+    rng = np.random.default_rng(threads)
+    n = 300_000
+    u = rng.integers(0, 4, size=n)                 # 0 = empty label set
+    u[-5:] = 3                                     # new groups at the very end
+    off = np.zeros(n + 1, dtype=np.uint64)
+    off[1:] = np.cumsum(u)
+    lab = np.concatenate([np.sort(rng.choice(12, size=c, replace=False)) + 1 for c in u]).astype(np.uint32)
+    lab[-3:] = [20, 21, 22]                        # a label set only the last point has
+    lg = nat.LabelGraph(off, lab, num_threads=threads)
+    exp = O.oracle().label_graph(off, lab)
+    G = exp["num_groups"]
+    assert lg.num_groups == G
+    assert np.array_equal(lg.new_to_old, exp["new_to_old"])
+    assert np.array_equal(lg.group_ranges, exp["group_ranges"])
+    assert O.lng_sets(lg.out_offsets, lg.out_ids, G) == O.lng_sets(exp["out_offsets"], exp["out_ids"], G)
