@@ -81,11 +81,10 @@ class UniNavGraph:
         self._new_to_old_vec_ids = self._lg.new_to_old
         self._base = np.ascontiguousarray(vectors[self._new_to_old_vec_ids], dtype=np.float32)
         self._dim = self._base.shape[1]
-        gid = np.zeros(self._num_points, dtype=np.uint32)
-        r = self._group_id_to_range
-        for g in range(1, self._num_groups + 1):
-            gid[r[g, 0]:r[g, 1]] = g
-        self._new_vec_id_to_group_id = gid
+        # groups 1..G hold consecutive row ranges that cover every row
+        r = self._group_id_to_range.astype(np.int64)
+        self._new_vec_id_to_group_id = np.repeat(np.arange(1, self._num_groups + 1, dtype=np.uint32),
+                                                 r[1:, 1] - r[1:, 0])
 
     def build_label_nav_graph(self) -> None:
         self._label_nav_graph = LabelNavGraph(self._lg.out_offsets, self._lg.out_ids,

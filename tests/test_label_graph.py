@@ -131,3 +131,24 @@ def test_chunked_grouping_matches_serial_oracle(threads):
     assert np.array_equal(lg.new_to_old, exp["new_to_old"])
     assert np.array_equal(lg.group_ranges, exp["group_ranges"])
     assert O.lng_sets(lg.out_offsets, lg.out_ids, G) == O.lng_sets(exp["out_offsets"], exp["out_ids"], G)
+
+
+def test_uninavgraph_mirror_host_steps(golden):
+    """The host half of the UniNavGraph mirror: groups, reorder, the row -> group map
+    and the LNG view, against the golden (the reference's grouping and trie)."""
+    from filtervectorcode_refactor_b200.ung import UniNavGraph
+    g = golden
+    ung = UniNavGraph(num_cross_edges=g["k"])
+    ung.build_trie_and_divide_groups(g["label_offsets"], g["labels"])
+    ung.prepare_group_storages_graphs(g["X"])
+    ung.build_label_nav_graph()
+    assert np.array_equal(ung._new_to_old_vec_ids, g["new_to_old"])
+    assert np.array_equal(ung._base, g["Xr"])
+    gf = g["group_first"].astype(np.int64)
+    exp = np.zeros(g["Xr"].shape[0], dtype=np.uint32)
+    for f in range(1, g["num_groups"] + 1):
+        exp[gf[f]:gf[f + 1]] = f
+    assert np.array_equal(ung._new_vec_id_to_group_id, exp)
+    for f in range(1, g["num_groups"] + 1):
+        assert set(ung._label_nav_graph.out_neighbors(f).tolist()) == \
+            set(g["out_ids"][g["out_offsets"][f]:g["out_offsets"][f + 1]].tolist())
