@@ -95,6 +95,24 @@ class AdditionalStats(ctypes.Structure):
         return {name: getattr(self, name) for name, _ in self._fields_}
 
 
+class CrossGroupStats(ctypes.Structure):
+    """Layout of ``ungx_cross_group_stats``."""
+
+    _fields_ = [
+        ("cross", CrossEdgeTiming),
+        ("additional", AdditionalStats),
+        ("cross_edges", c_uint64),
+        ("num_cols", c_uint64),
+        ("merge_ms", c_double),
+        ("total_ms", c_double),
+    ]
+
+
+BUILD_ADDITIONAL = 1
+BUILD_INTRA_LOCAL_IDS = 2
+BUILD_VECTORS_ON_DEVICE = 4
+
+
 class ExactKnnConfig(ctypes.Structure):
     """Layout of ``ungx_exact_knn_config``."""
 
@@ -146,6 +164,10 @@ _SIGNATURES = [
     ("ungx_graph_csr_device", c_int,
      [c_void_p, c_uint32, c_uint32, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_uint64,
       POINTER(c_uint64), c_void_p]),
+    ("ungx_build_cross_group_edges", c_int,
+     [c_void_p, c_void_p, POINTER(CrossEdgeProblem), c_void_p, c_void_p, c_uint32, c_void_p, c_void_p,
+      POINTER(CrossGroupStats)]),
+    ("ungx_graph_copy", c_int, [c_void_p, c_void_p, c_void_p]),
     ("ungx_exact_knn_default_config", None, [c_uint32, c_uint32, POINTER(ExactKnnConfig)]),
     ("ungx_exact_knn_graph_device", c_int,
      [c_void_p, c_uint32, c_void_p, POINTER(ExactKnnConfig), c_void_p, c_void_p, c_void_p, POINTER(c_double)]),
@@ -329,6 +351,29 @@ class Context:
         cols = np.empty(max(num_edges, 1), dtype=np.uint32)
         check(lib.ungx_additional_edges_copy(self.h, _ptr(src), _ptr(dst), _ptr(off), _ptr(cols)), self.h)
         return src[:num_edges], dst[:num_edges], off, cols[:num_edges]
+
+    def build_cross_group_edges(self, vectors, problem: Problem, intra_offsets: np.ndarray | None = None,
+                                intra_cols: np.ndarray | None = None, flags: int = BUILD_ADDITIONAL,
+                                out_ids: np.ndarray | None = None, out_dists: np.ndarray | None = None
+                                ) -> CrossGroupStats:
+        """ungx_build_cross_group_edges: ``vectors`` is a host array, or an integer device
+        pointer with BUILD_VECTORS_ON_DEVICE in ``flags``."""
+        st = CrossGroupStats()
+        vp = vectors if (flags & BUILD_VECTORS_ON_DEVICE) else _ptr(vectors)
+        io = None if intra_offsets is None else np.ascontiguousarray(intra_offsets, dtype=np.uint64)
+        ic = None if intra_cols is None else np.ascontiguousarray(intra_cols, dtype=np.uint32)
+        if ic is not None and ic.size == 0:
+            ic = np.zeros(1, dtype=np.uint32)
+        check(lib.ungx_build_cross_group_edges(self.h, vp, ctypes.byref(problem.c), _ptr(io), _ptr(ic), flags,
+                                               _ptr(out_ids), _ptr(out_dists), ctypes.byref(st)), self.h)
+        return st
+
+    def graph_copy(self, num_points: int, num_cols: int) -> tuple[np.ndarray, np.ndarray]:
+        """(offsets [n+1], cols) of the last ungx_build_cross_group_edges call."""
+        off = np.empty(num_points + 1, dtype=np.uint64)
+        cols = np.empty(max(num_cols, 1), dtype=np.uint32)
+        check(lib.ungx_graph_copy(self.h, _ptr(off), _ptr(cols)))
+        return off, cols[:num_cols]
 
     def exact_knn_graph_device(self, group_ranges: np.ndarray, cfg: ExactKnnConfig, d_graph: int,
                                d_entry_points: int | None = None, stream: int | None = None) -> float:

@@ -125,6 +125,10 @@ struct ungx_context
        knn_tasks, knn_dist, knn_dbase, knn_tiles, knn_rows;
    uint32_t add_n = 0;     // points of the last additional-edge build
    uint64_t add_edges = 0; // its edges
+   // merged adjacency of the last ungx_build_cross_group_edges call
+   DevBuf intra_off, intra_cols, graph_off, graph_cols;
+   uint32_t graph_n = 0;
+   uint64_t graph_nnz = 0;
    uint32_t *h_counters = nullptr; // pinned
    cudaEvent_t ev[11] = {}; // ev[10]: end of the last vector preparation
 };
@@ -530,7 +534,7 @@ int ungx_context_destroy(ungx_context *ctx)
                      &ctx->add_res, &ctx->add_off, &ctx->add_cols, &ctx->add_qoff, &ctx->add_loff, &ctx->add_from,
                      &ctx->add_to, &ctx->add_stats, &ctx->scan_scratch, &ctx->knn_ranges,
                      &ctx->knn_base, &ctx->knn_tasks, &ctx->knn_dist, &ctx->knn_dbase, &ctx->knn_tiles,
-                     &ctx->knn_rows})
+                     &ctx->knn_rows, &ctx->intra_off, &ctx->intra_cols, &ctx->graph_off, &ctx->graph_cols})
       b->release();
    ctx->host_stage.release();
    for (auto &ev : ctx->ev)
@@ -1040,6 +1044,153 @@ int ungx_graph_csr_device(ungx_context *ctx, uint32_t num_points, uint32_t topk,
              "fill kernel");
    UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[6], s), "event");
    return wait_event(ctx, ctx->ev[6], "graph emission");
+}
+
+int ungx_build_cross_group_edges(ungx_context *ctx, const float *vectors, const ungx_cross_edge_problem *problem,
+                                 const uint64_t *intra_offsets, const uint32_t *intra_cols, uint32_t flags,
+                                 uint32_t *out_ids, float *out_dists, ungx_cross_group_stats *stats)
+{
+   if (!ctx || !problem || !vectors)
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "null argument");
+   if (flags & ~uint32_t(UNGX_BUILD_ADDITIONAL | UNGX_BUILD_INTRA_LOCAL_IDS | UNGX_BUILD_VECTORS_ON_DEVICE))
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "unknown build flag");
+   if (problem->shard_count > 1)
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "ungx_build_cross_group_edges builds the whole graph: shard_count must be 1");
+   if (intra_offsets && !intra_cols)
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "intra offsets without columns");
+   const uint32_t n = problem->num_points, k = problem->topk, G = problem->num_groups;
+   if (n == 0 || k == 0)
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "empty problem");
+   if (intra_offsets)
+   {
+      if (intra_offsets[0] != 0)
+         return fail(ctx, UNGX_ERR_INVALID_ARG, "intra_offsets[0] must be 0");
+      for (uint32_t v = 0; v < n; ++v)
+         if (intra_offsets[v + 1] < intra_offsets[v])
+            return fail(ctx, UNGX_ERR_INVALID_ARG, "intra_offsets must not decrease");
+   }
+   const auto t0 = std::chrono::steady_clock::now();
+   ungx_cross_group_stats sx{};
+   // 1. cross edges: plan on a host thread while the vectors are uploaded and prepared
+   int pst = 0;
+   std::string perr;
+   double pms = 0;
+   std::thread planner([&] {
+      const auto a = std::chrono::steady_clock::now();
+      pst = ungx::build_plan(*problem, ctx->plan, perr);
+      pms = ms_since(a);
+   });
+   int st = ungx_prepare_base_vectors(ctx, vectors, n, problem->dim, (flags & UNGX_BUILD_VECTORS_ON_DEVICE) ? 1 : 0);
+   planner.join();
+   if (st)
+      return st;
+   if (pst)
+      return fail(ctx, pst, "invalid problem: " + perr);
+   ungx_cross_edge_timing &t = sx.cross;
+   t.plan_ms = pms;
+   t.pairs = ctx->plan.pairs;
+   const size_t nk = size_t(n) * k;
+   UNGX_CUDA(ctx, ctx->out_ids.ensure(nk * sizeof(uint32_t)), "output allocation");
+   UNGX_CUDA(ctx, ctx->out_dists.ensure(nk * sizeof(float)), "output allocation");
+   uint32_t *d_ids = ctx->out_ids.as<uint32_t>();
+   if ((st = run_generate(ctx, *problem, ctx->plan, d_ids, ctx->out_dists.as<float>(), ctx->stream, t)))
+      return st;
+   t.generate_ms = ms_since(t0);
+   // 2. additional edges from the device cross edges
+   if (flags & UNGX_BUILD_ADDITIONAL)
+   {
+      if ((st = ungx_additional_edges_build(ctx, problem, d_ids, nullptr, &sx.additional)))
+         return st;
+   }
+   else
+      ctx->add_n = 0;
+   // 3 + 4. intra-group edges (offset to global ids), cross, additional: one CSR
+   const auto tm = std::chrono::steady_clock::now();
+   cudaStream_t s = ctx->stream;
+   const uint64_t intra_nnz = intra_offsets ? intra_offsets[n] : 0;
+   const uint64_t *d_ioff = nullptr;
+   const uint32_t *d_icols = nullptr, *d_group_of = nullptr, *d_ranges = nullptr;
+   if (intra_offsets)
+   {
+      UNGX_CUDA(ctx, ctx->intra_off.ensure((size_t(n) + 1) * sizeof(uint64_t)), "intra offsets");
+      UNGX_CUDA(ctx, ctx->intra_cols.ensure(std::max<uint64_t>(intra_nnz, 1) * sizeof(uint32_t)), "intra columns");
+      UNGX_CUDA(ctx, cudaMemcpyAsync(ctx->intra_off.p, intra_offsets, (size_t(n) + 1) * sizeof(uint64_t),
+                                     cudaMemcpyHostToDevice, s),
+                "intra upload");
+      if (intra_nnz)
+         UNGX_CUDA(ctx, cudaMemcpyAsync(ctx->intra_cols.p, intra_cols, intra_nnz * sizeof(uint32_t),
+                                        cudaMemcpyHostToDevice, s),
+                   "intra upload");
+      d_ioff = ctx->intra_off.as<uint64_t>();
+      d_icols = ctx->intra_cols.as<uint32_t>();
+      if (flags & UNGX_BUILD_INTRA_LOCAL_IDS)
+      {
+         UNGX_CUDA(ctx, ctx->g_ranges.ensure(2 * (size_t(G) + 1) * sizeof(uint32_t)), "group ranges");
+         if (G)
+            UNGX_CUDA(ctx, cudaMemcpyAsync(ctx->g_ranges.p, problem->group_ranges, 2 * (size_t(G) + 1) * sizeof(uint32_t),
+                                           cudaMemcpyHostToDevice, s),
+                      "group ranges");
+         UNGX_CUDA(ctx, ctx->group_of.ensure(size_t(n) * sizeof(uint32_t)), "group map");
+         UNGX_CUDA(ctx, ungx::launch_group_of(ctx->g_ranges.as<uint32_t>(), G, n, ctx->group_of.as<uint32_t>(), s),
+                   "group map kernel");
+         d_group_of = ctx->group_of.as<uint32_t>();
+         d_ranges = ctx->g_ranges.as<uint32_t>();
+      }
+   }
+   const bool with_add = (flags & UNGX_BUILD_ADDITIONAL) != 0;
+   const uint64_t *add_off = with_add ? ctx->add_off.as<uint64_t>() : nullptr;
+   const uint32_t *add_cols = with_add ? ctx->add_cols.as<uint32_t>() : nullptr;
+   UNGX_CUDA(ctx, ctx->graph_off.ensure((size_t(n) + 1) * sizeof(uint64_t)), "graph offsets");
+   uint64_t *g_off = ctx->graph_off.as<uint64_t>();
+   UNGX_CUDA(ctx, ctx->scan_scratch.ensure(ungx::csr_scan_scratch_bytes(n)), "scan scratch");
+   UNGX_CUDA(ctx, ungx::launch_graph_degrees(n, k, d_ioff, d_ids, add_off, g_off, s), "degree kernel");
+   UNGX_CUDA(ctx, ungx::launch_exclusive_scan_u64(g_off, n + 1, ctx->scan_scratch.p, s), "scan kernels");
+   UNGX_CUDA(ctx, cudaMemcpyAsync(ctx->h_counters, g_off + n, sizeof(uint64_t), cudaMemcpyDeviceToHost, s), "total");
+   UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[6], s), "event");
+   if ((st = wait_event(ctx, ctx->ev[6], "graph degrees")))
+      return st;
+   uint64_t total = 0;
+   std::memcpy(&total, ctx->h_counters, sizeof(uint64_t));
+   UNGX_CUDA(ctx, ctx->graph_cols.ensure(std::max<uint64_t>(total, 1) * sizeof(uint32_t)), "graph columns");
+   UNGX_CUDA(ctx,
+             ungx::launch_graph_fill(n, k, d_ioff, d_icols, d_ids, add_off, add_cols, g_off,
+                                     ctx->graph_cols.as<uint32_t>(), s, d_group_of, d_ranges),
+             "fill kernel");
+   // the flat cross edges, when asked for
+   if (out_ids)
+      UNGX_CUDA(ctx, cudaMemcpyAsync(out_ids, d_ids, nk * sizeof(uint32_t), cudaMemcpyDeviceToHost, s), "output copy");
+   if (out_dists)
+      UNGX_CUDA(ctx, cudaMemcpyAsync(out_dists, ctx->out_dists.p, nk * sizeof(float), cudaMemcpyDeviceToHost, s),
+                "output copy");
+   UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[6], s), "event");
+   if ((st = wait_event(ctx, ctx->ev[6], "graph emission")))
+      return st;
+   ctx->graph_n = n;
+   ctx->graph_nnz = total;
+   sx.num_cols = total;
+   sx.cross_edges = total - intra_nnz - (with_add ? sx.additional.edges : 0);
+   sx.merge_ms = ms_since(tm);
+   sx.total_ms = ms_since(t0);
+   if (stats)
+      *stats = sx;
+   return UNGX_OK;
+}
+
+int ungx_graph_copy(const ungx_context *ctx, uint64_t *offsets, uint32_t *cols)
+{
+   if (!ctx)
+      return fail(nullptr, UNGX_ERR_INVALID_ARG, "null context");
+   if (ctx->graph_n == 0)
+      return fail(nullptr, UNGX_ERR_STATE, "ungx_graph_copy: no merged graph built in this context");
+   if (cudaSetDevice(ctx->device) != cudaSuccess)
+      return fail(nullptr, UNGX_ERR_CUDA, "ungx_graph_copy: cudaSetDevice failed");
+   if (offsets && cudaMemcpy(offsets, ctx->graph_off.p, (size_t(ctx->graph_n) + 1) * sizeof(uint64_t),
+                             cudaMemcpyDeviceToHost) != cudaSuccess)
+      return fail(nullptr, UNGX_ERR_CUDA, "ungx_graph_copy: device to host copy failed");
+   if (cols && ctx->graph_nnz &&
+       cudaMemcpy(cols, ctx->graph_cols.p, ctx->graph_nnz * sizeof(uint32_t), cudaMemcpyDeviceToHost) != cudaSuccess)
+      return fail(nullptr, UNGX_ERR_CUDA, "ungx_graph_copy: device to host copy failed");
+   return UNGX_OK;
 }
 
 void ungx_exact_knn_default_config(uint32_t candidate_k, uint32_t final_degree, ungx_exact_knn_config *cfg)

@@ -184,8 +184,12 @@ __global__ void scan_add_kernel(uint64_t *__restrict__ data, uint32_t count, con
 // The point's offsets and its first 32 cross slots are loaded together up front (one
 // slot per lane); the cross count is the position of the first sentinel, found by a
 // ballot instead of a serial walk of the row.
+// With group_of / ranges given, intra columns are group-local ids and get the first
+// row of the point's group added (add_offset_for_uni_nav_graph,
+// UNG/codes/src/uni_nav_graph.cpp:285-297).
 __global__ void graph_fill_kernel(uint32_t n, uint32_t k, const uint64_t *__restrict__ intra_off,
-                                  const uint32_t *__restrict__ intra_cols, const uint32_t *__restrict__ cross_ids,
+                                  const uint32_t *__restrict__ intra_cols, const uint32_t *__restrict__ group_of,
+                                  const uint32_t *__restrict__ ranges, const uint32_t *__restrict__ cross_ids,
                                   const uint64_t *__restrict__ add_off, const uint32_t *__restrict__ add_cols,
                                   const uint64_t *__restrict__ offsets, uint32_t *__restrict__ cols)
 {
@@ -199,8 +203,9 @@ __global__ void graph_fill_kernel(uint32_t n, uint32_t k, const uint64_t *__rest
       const uint32_t x0 = cross_ids && lane < k ? cross_ids[v * k + lane] : 0xFFFFFFFFu;
       if (intra_off)
       {
+         const uint32_t shift = group_of ? ranges[2 * group_of[v]] : 0u;
          for (uint64_t i = ia + lane; i < ib; i += 32)
-            cols[w + (i - ia)] = intra_cols[i];
+            cols[w + (i - ia)] = intra_cols[i] + shift;
          w += ib - ia;
       }
       if (cross_ids)
@@ -469,12 +474,13 @@ cudaError_t launch_add_points(const uint32_t *ranges, uint32_t G, uint32_t n, ui
 
 cudaError_t launch_graph_fill(uint32_t n, uint32_t k, const uint64_t *intra_off, const uint32_t *intra_cols,
                               const uint32_t *cross_ids, const uint64_t *add_off, const uint32_t *add_cols,
-                              const uint64_t *offsets, uint32_t *cols, cudaStream_t s)
+                              const uint64_t *offsets, uint32_t *cols, cudaStream_t s, const uint32_t *group_of,
+                              const uint32_t *ranges)
 {
    if (n == 0)
       return cudaSuccess;
-   graph_fill_kernel<<<grid_for(uint64_t(n) * 32, 256), 256, 0, s>>>(n, k, intra_off, intra_cols, cross_ids, add_off,
-                                                                      add_cols, offsets, cols);
+   graph_fill_kernel<<<grid_for(uint64_t(n) * 32, 256), 256, 0, s>>>(n, k, intra_off, intra_cols, group_of, ranges,
+                                                                      cross_ids, add_off, add_cols, offsets, cols);
    return cudaGetLastError();
 }
 

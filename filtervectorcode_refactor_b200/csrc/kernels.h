@@ -193,9 +193,11 @@ cudaError_t launch_add_list(const uint32_t *res, const uint32_t *rows, uint32_t 
 cudaError_t launch_add_points(const uint32_t *ranges, uint32_t G, uint32_t n, uint32_t k, const uint64_t *out_off,
                               const uint64_t *qoff, const uint64_t *loff, const uint32_t *to, uint64_t *off,
                               uint32_t *cols, void *scratch, cudaStream_t s);
+// group_of / ranges (optional): intra columns are group-local; row v's get ranges[2 group_of[v]] added.
 cudaError_t launch_graph_fill(uint32_t n, uint32_t k, const uint64_t *intra_off, const uint32_t *intra_cols,
                               const uint32_t *cross_ids, const uint64_t *add_off, const uint32_t *add_cols,
-                              const uint64_t *offsets, uint32_t *cols, cudaStream_t s);
+                              const uint64_t *offsets, uint32_t *cols, cudaStream_t s,
+                              const uint32_t *group_of = nullptr, const uint32_t *ranges = nullptr);
 cudaError_t launch_tc(const TcMaps &maps, const TcParams &p, uint32_t kp, uint32_t grid, cudaStream_t s);
 cudaError_t launch_rerank(const RerankParams &p, uint32_t kp, uint32_t num_items, cudaStream_t s);
 

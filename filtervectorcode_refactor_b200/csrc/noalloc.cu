@@ -1,23 +1,27 @@
 // The exact cross-edge route for callers that cannot allocate device memory.
 //
 // Some callers cannot call cudaMalloc at the moment they need the cross edges:
-// a caller recording a CUDA graph (allocation is not permitted while a stream is
-// being captured), a caller whose device memory is owned by another allocator
-// (a framework's caching allocator, a pool with a hard budget) and must not see
-// foreign allocations, or a service that must not grow its device footprint after
-// start-up.  ungx_cross_edges_exact_noalloc serves them: the caller passes the
+// a caller whose device memory is owned by another allocator (a framework's
+// caching allocator, a pool with a hard budget) that must not see foreign
+// allocations, or a service that must not grow its device footprint once it is
+// serving.  ungx_cross_edges_exact_noalloc serves them: the caller passes the
 // device-resident base vectors and device output buffers, and the work plan the
 // kernels read (work items, target segments, the row list, the rows without
 // targets) goes into one fixed scratch array that this file owns.
 //
-// The array is a file-scope __device__ variable of kScratchBytes (64 MiB): every
-// GPU that loads this library holds it until the process exits.  Host code cannot
-// use its name as a device address, so the address is fetched once per device
-// with cudaGetSymbolAddress, with that device current.
+// The array is a file-scope __device__ variable of kScratchBytes (64 MiB).  It
+// belongs to the library's device module, which the CUDA runtime loads on a device
+// at the library's first use there (lazily, with CUDA_MODULE_LOADING=LAZY, at the
+// first cudaGetSymbolAddress or kernel launch); the device then holds it until the
+// process exits.  Host code cannot use its name as a device address, so the
+// address is fetched once per device with cudaGetSymbolAddress, with that device
+// current, by the first call on the device.
 //
 // Nothing in the array has to start at zero: each call overwrites every byte its
 // kernels read.  Every call shares the one array, so calls that overlap on the GPU
-// (on different streams, or from different host threads) race on it.
+// (on different streams, or from different host threads) race on it.  A call that
+// returns UNGX_ERR_TIMEOUT may leave its copies and kernels running on the array;
+// the caller synchronises the stream before calling again.
 #include <cuda_runtime.h>
 
 #include <algorithm>

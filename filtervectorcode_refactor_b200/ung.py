@@ -8,13 +8,16 @@ Method names, argument meaning and call order follow ``ANNS::UniNavGraph``
     build_label_nav_graph             uni_nav_graph_label_graph.cpp:836-911
     build_cross_group_edges           uni_nav_graph_cross_edges.cpp:613-913
       build_cross_edges_generate_gpu_optimized   :334-440
+      build_cross_edges_generate_additional      :442-596 (exact variant)
+      add_offset_for_uni_nav_graph               uni_nav_graph.cpp:285-297
+      merge_cross_edges_to_graph (+ additional)  :598-611
 
 All computation runs in ``libungx.so`` (grouping and LNG on the host in C++, the
 cross-edge top-k on the B200).  Error behaviour: the reference's GPU seam returns
 ``false`` on failure and ``build_cross_group_edges`` then falls back to a CPU path
 unless ``UNG_CROSS_EDGE_GPU_STRICT=1`` (cross_edges.cpp:775-789).  This library has
 no CPU path, so the seam returns ``False`` (with ``last_error`` set) and
-``build_cross_group_edges`` always raises, i.e. it behaves as the strict mode.
+``build_cross_group_edges`` raises, i.e. it behaves as the strict mode.
 """
 from __future__ import annotations
 
@@ -126,9 +129,41 @@ class UniNavGraph:
         ds = self.cross_group_neighbor_dists[point * k:(point + 1) * k]
         return [(int(i), float(x)) for i, x in zip(ids, ds) if i != nat.EMPTY_ID]
 
-    def build_cross_group_edges(self) -> None:
-        if not self.build_cross_edges_generate_gpu_optimized():
-            raise RuntimeError("GPU cross-edge generation failed (no CPU path in this library): " + self.last_error)
+    def build_cross_group_edges(self, intra_offsets: np.ndarray | None = None, intra_cols: np.ndarray | None = None,
+                                intra_ids_are_global: bool = False, additional_edges: bool = True) -> None:
+        """UniNavGraph::build_cross_group_edges (uni_nav_graph_cross_edges.cpp:613-913) in one
+        library call (ungx_build_cross_group_edges): the GPU cross edges, the exact
+        additional edges, add_offset_for_uni_nav_graph on the intra-group graph (CSR over
+        reordered points, group-local ids unless ``intra_ids_are_global``) and the merge.
+        Fills ``cross_group_neighbor_flat_ids`` / ``_dists`` and the merged adjacency
+        ``graph_offsets`` / ``graph_cols`` (per point: intra edges, cross edges nearest
+        first, additional edges).  Raises on failure: the library has no CPU path, so
+        this is the reference's strict mode."""
+        try:
+            if self._ctx is None:
+                self._ctx = nat.Context(self._device)
+            n, k = self._num_points, self._num_cross_edges
+            self.cross_group_neighbor_flat_ids = np.full(n * k, nat.EMPTY_ID, dtype=np.uint32)
+            self.cross_group_neighbor_dists = np.full(n * k, np.inf, dtype=np.float32)
+            flags = nat.BUILD_ADDITIONAL if additional_edges else 0
+            if intra_offsets is not None and not intra_ids_are_global:
+                flags |= nat.BUILD_INTRA_LOCAL_IDS
+            st = self._ctx.build_cross_group_edges(self._base, self._problem(), intra_offsets, intra_cols, flags,
+                                                   self.cross_group_neighbor_flat_ids,
+                                                   self.cross_group_neighbor_dists)
+            self.graph_offsets, self.graph_cols = self._ctx.graph_copy(n, int(st.num_cols))
+        except nat.UngxError as e:
+            self.last_error = str(e)
+            raise RuntimeError("GPU cross-group edge build failed (no CPU path in this library): " + str(e)) from e
+        d = st.cross.as_dict()
+        self.timing.generate_ms += d["generate_ms"]
+        self.timing.gpu_h2d_ms += d["gpu_h2d_ms"]
+        self.timing.gpu_kernel_ms += d["gpu_kernel_ms"]
+        self.timing.gpu_d2h_ms += d["gpu_d2h_ms"]
+        self.timing.merge_cross_ms += st.merge_ms
+        self.timing.detail = dict(d, additional=st.additional.as_dict(), cross_edges=int(st.cross_edges),
+                                  num_cols=int(st.num_cols), total_ms=st.total_ms)
+        self.additional_edge_count = int(st.additional.edges)
 
     def cross_edges_csr(self) -> tuple[np.ndarray, np.ndarray]:
         """CrossEdgeGraphMaterializationWriter::build_csr_adjacency

@@ -165,22 +165,29 @@ int ungx_cross_edges_build(ungx_context *ctx, const float *vectors, const ungx_c
                            uint32_t *out_ids, float *out_dists, ungx_cross_edge_timing *timing);
 
 /* The exact route without any device allocation.  No counterpart in the reference.
- * For callers that cannot call cudaMalloc when they need the cross edges: code that
- * is recording a CUDA graph (allocation is not allowed during stream capture), code
+ * For callers that cannot call cudaMalloc when they need the cross edges: code
  * whose device memory belongs to another allocator (a framework's caching
- * allocator, a pool with a hard budget), or a service that must not grow its
- * device footprint after start-up.  The caller passes the reordered base vectors
- * (`d_vectors`, device, n x d fp32) and the device outputs (`d_out_ids` [n*k],
- * `d_out_dists` [n*k] or NULL); the rows' results are those of
- * ungx_cross_edges_generate with UNGX_ROUTE_EXACT.  The work plan lives in one
- * 64 MiB __device__ array of the library (held by every GPU that loads it until
- * the process exits), so the plan must fit: about 8 bytes per source row plus 16
- * per work item and target segment; larger problems return UNGX_ERR_INVALID_ARG
- * naming the size.  Runs on the current device and on `stream` (a cudaStream_t,
- * NULL = the legacy stream); returns after the work finished (bounded wait).  The
- * first call on each device fetches the array's device address, so make it before
- * any stream capture.  All calls share the array: calls that overlap on the GPU
- * race.  Errors are reported through ungx_last_error(NULL). */
+ * allocator, a pool with a hard budget, where a foreign cudaMalloc would be
+ * invisible to that allocator's accounting or could fail against its limit), or a
+ * service that must not grow its device footprint once it is serving.  The caller
+ * passes the reordered base vectors (`d_vectors`, device, n x d fp32) and the
+ * device outputs (`d_out_ids` [n*k], `d_out_dists` [n*k] or NULL); the rows'
+ * results are those of ungx_cross_edges_generate with UNGX_ROUTE_EXACT.  The work
+ * plan lives in one 64 MiB __device__ array of the library, so the plan must fit:
+ * about 8 bytes per source row plus 16 per work item and target segment; larger
+ * problems return UNGX_ERR_INVALID_ARG naming the size.  The array is part of the
+ * library's device module, which the CUDA runtime loads on a device at the first
+ * use of the library there (with lazy module loading, at the first call of this
+ * entry point or of any kernel of the library); from then on that device holds it
+ * until the process exits.  A caller that needs a fixed footprint makes one call
+ * (any small problem) at start-up on every device it will use.  That first call on
+ * a device also fetches the array's device address (cudaGetSymbolAddress, with
+ * the device current).  Runs on the current device and on `stream` (a
+ * cudaStream_t, NULL = the legacy stream); returns after the work finished
+ * (bounded wait of 10 minutes).  All calls share the array: calls that overlap on
+ * the GPU race.  After UNGX_ERR_TIMEOUT the copies and kernels of that call may
+ * still be using the array: synchronise `stream` before the next call.  Errors are
+ * reported through ungx_last_error(NULL). */
 int ungx_cross_edges_exact_noalloc(const ungx_cross_edge_problem *problem, const float *d_vectors,
                                    uint32_t *d_out_ids, float *d_out_dists, void *stream);
 
@@ -269,6 +276,51 @@ int ungx_graph_csr_device(ungx_context *ctx, uint32_t num_points, uint32_t topk,
                           const uint32_t *d_intra_cols, const uint32_t *d_cross_ids, int with_additional,
                           uint64_t *d_offsets, uint32_t *d_cols, uint64_t cols_capacity, uint64_t *num_cols,
                           void *stream);
+
+/* ------------------------------------------- a1: the whole cross-group edge step
+ * UniNavGraph::build_cross_group_edges (UNG/codes/src/uni_nav_graph_cross_edges.cpp:613-913)
+ * with the GPU generate route, the exact additional edges and the merge, in one call
+ * whose intermediates stay in device memory:
+ *   1. the cross edges (as ungx_cross_edges_build);
+ *   2. with UNGX_BUILD_ADDITIONAL, the additional edges (as ungx_additional_edges_build,
+ *      build_cross_edges_generate_additional with CpuExactScan, :442-596);
+ *   3. add_offset_for_uni_nav_graph (UNG/codes/src/uni_nav_graph.cpp:285-297): with
+ *      UNGX_BUILD_INTRA_LOCAL_IDS the intra-group columns are group-local ids and get the
+ *      first row of the point's group added;
+ *   4. merge_cross_edges_to_graph + merge_additional_edges_to_graph (:598-611,
+ *      UNG/codes/src/ung_cross_edge_output_writer.cpp:17-42): per point, its intra-group
+ *      edges, its cross edges nearest first, then its additional edges, as CSR.
+ * `vectors`: the reordered n x d fp32 rows, host memory (device memory with
+ * UNGX_BUILD_VECTORS_ON_DEVICE).  `intra_offsets` [n+1] / `intra_cols` (host, NULL = no
+ * intra-group edges): the graph of each group.  `out_ids` / `out_dists` (host [n*k], each
+ * may be NULL): the flat cross edges as ungx_cross_edges_generate writes them.  The
+ * merged adjacency stays in the context: *num_cols in `stats` gives its size, and
+ * ungx_graph_copy copies it out.  The base vectors stay prepared afterwards (for
+ * ungx_exact_knn_graph_device, say) until ungx_release_base_vectors. */
+enum
+{
+   UNGX_BUILD_ADDITIONAL = 1,
+   UNGX_BUILD_INTRA_LOCAL_IDS = 2,
+   UNGX_BUILD_VECTORS_ON_DEVICE = 4
+};
+
+typedef struct ungx_cross_group_stats
+{
+   ungx_cross_edge_timing cross;     /* the generate step */
+   ungx_additional_stats additional; /* zero without UNGX_BUILD_ADDITIONAL */
+   uint64_t cross_edges;             /* non-empty cross-edge slots */
+   uint64_t num_cols;                /* columns of the merged adjacency */
+   double merge_ms;                  /* intra upload + offset + CSR emission (wall) */
+   double total_ms;                  /* the whole call (wall) */
+} ungx_cross_group_stats;
+
+int ungx_build_cross_group_edges(ungx_context *ctx, const float *vectors, const ungx_cross_edge_problem *problem,
+                                 const uint64_t *intra_offsets, const uint32_t *intra_cols, uint32_t flags,
+                                 uint32_t *out_ids, float *out_dists, ungx_cross_group_stats *stats);
+
+/* The merged adjacency of the last ungx_build_cross_group_edges call, host buffers:
+ * offsets [n+1], cols [num_cols]; either may be NULL. */
+int ungx_graph_copy(const ungx_context *ctx, uint64_t *offsets, uint32_t *cols);
 
 /* ------------------------------------------- a15: large-group exact kNN seeding
  * batched_exact_knn_graph_kernel with the defaults of make_fast_exact_batch_config

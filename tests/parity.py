@@ -41,6 +41,53 @@ def assert_rows_match(ids, dists, ref_ids, ref_dists, k, rows=None):
             f"got {ids[i].tolist()} {dists[i].tolist()} expected {ref_ids[i].tolist()} {ref_dists[i].tolist()}")
 
 
+def row_groups(group_ranges, n):
+    """Group id (1..G) of every row; 0 for rows outside every group."""
+    gr = group_ranges.reshape(-1, 2).astype(np.int64)
+    sizes = gr[1:, 1] - gr[1:, 0]
+    rg = np.zeros(n, dtype=np.int64)
+    rows = np.repeat(np.arange(1, gr.shape[0]), sizes)
+    starts = np.repeat(gr[1:, 0], sizes)
+    rg[starts + (np.arange(rows.size) - np.repeat(np.cumsum(sizes) - sizes, sizes))] = rows
+    return rg
+
+
+def check_row_properties_fast(ids, dists, k, group_ranges, out_offsets, out_ids, rows):
+    """check_row_properties over many rows at once (vectorised); returns the number of
+    rows checked."""
+    gr = group_ranges.reshape(-1, 2).astype(np.int64)
+    G = gr.shape[0] - 1
+    sizes = gr[:, 1] - gr[:, 0]
+    oo = out_offsets.astype(np.int64)
+    oi = out_ids.astype(np.int64)
+    n = ids.size // k
+    rg = row_groups(group_ranges, n)
+    src = np.repeat(np.arange(G + 1), np.diff(oo[:G + 2]))
+    union = np.zeros(G + 1, dtype=np.int64)
+    np.add.at(union, src, sizes[oi])
+    edge_keys = np.unique(src * (G + 1) + oi)
+    rows = np.asarray(rows, dtype=np.int64)
+    I = ids.reshape(-1, k)[rows].astype(np.int64)
+    D = dists.reshape(-1, k)[rows]
+    f = rg[rows]
+    want = np.minimum(k, union[f])
+    valid = I != 0xFFFFFFFF
+    expect = np.arange(k)[None, :] < want[:, None]
+    bad = np.nonzero(np.any(valid != expect, axis=1))[0]
+    assert bad.size == 0, f"row {rows[bad[0]]}: ids {I[bad[0]].tolist()} want {want[bad[0]]} edges"
+    assert np.all(np.isfinite(D[valid])) and np.all(np.isinf(D[~valid]))
+    pair = valid[:, 1:] & valid[:, :-1]
+    order = (D[:, 1:] > D[:, :-1]) | ((D[:, 1:] == D[:, :-1]) & (I[:, 1:] > I[:, :-1]))
+    bad = np.nonzero(np.any(pair & ~order, axis=1))[0]
+    assert bad.size == 0, f"row {rows[bad[0]]} not sorted: {I[bad[0]].tolist()} {D[bad[0]].tolist()}"
+    tg = np.where(valid, rg[np.where(valid, I, 0)], 0)
+    keys = f[:, None] * (G + 1) + tg
+    member = np.isin(keys, edge_keys) | ~valid
+    bad = np.nonzero(~np.all(member, axis=1))[0]
+    assert bad.size == 0, f"row {rows[bad[0]]}: an id outside the union of its out-groups {I[bad[0]].tolist()}"
+    return rows.size
+
+
 def check_row_properties(ids, dists, k, group_ranges, out_offsets, out_ids, rows):
     """Size-independent properties of any output row: sorted by (distance, id),
     ids drawn from the union of the row's LNG out-groups, sentinels only at the end,

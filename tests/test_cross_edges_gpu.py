@@ -1,9 +1,10 @@
 """Parity of the B200 cross-edge build against the oracle, through the C ABI.
 
 * golden fixtures (made by the reference's own compiled code): ids and distance bits equal;
-* full-size configuration 2 and scaled configurations 3 / 4: rows sampled across every
-  source-group size are recomputed by the CPU oracle and must match exactly; every
-  row satisfies the size-independent properties (sorted, ids from the union of the
+* configurations 2, 3 and 4 at their full size: >= 2,000 rows stratified over every
+  source-group size, the largest source group and the rows whose targets include the
+  largest group are recomputed by the CPU oracle and must match exactly; every row
+  satisfies the size-independent properties (sorted, ids from the union of the
   out-groups, min(k, |union|) edges, sentinels last);
 * every operand width class of the tensor-core kernel (two issuers, one issuer,
   streamed source rows) matches the oracle on every row;
@@ -15,7 +16,7 @@ import numpy as np
 import pytest
 
 import oracle as O
-from parity import assert_rows_match, check_row_properties
+from parity import assert_rows_match, check_row_properties_fast
 from filtervectorcode_refactor_b200 import _native as nat
 from filtervectorcode_refactor_b200 import datasets
 from filtervectorcode_refactor_b200.ung import UniNavGraph
@@ -63,6 +64,9 @@ def test_uninavgraph_mirror_end_to_end(golden):
                           golden["dists"], golden["k"])
         off, cols = ung.cross_edges_csr()
         assert int(off[-1]) == int((golden["ids"] != 0xFFFFFFFF).sum())
+        # build_cross_group_edges also merged the additional edges after each point's cross edges
+        assert int(ung.graph_offsets[-1]) == int(off[-1]) + golden["add_from"].size
+        assert ung.additional_edge_count == golden["add_from"].size
     finally:
         ung.close()
 
@@ -125,24 +129,6 @@ def test_shards_cover_rows_once(ctx, golden):
     assert_rows_match(ids, dists, golden["ids"], golden["dists"], k)
 
 
-def sample_rows(group_ranges, out_offsets, rng, per_bucket=12, max_rows=400):
-    """Rows drawn across source-group size buckets (singletons .. the largest group)."""
-    gr = group_ranges.reshape(-1, 2).astype(np.int64)
-    sizes = gr[:, 1] - gr[:, 0]
-    has_out = np.diff(out_offsets.astype(np.int64))[:len(sizes)] > 0
-    rows = []
-    for lo in [1, 2, 8, 64, 512, 4096, 32768]:
-        gs = np.nonzero((sizes >= lo) & (sizes < lo * 8) & has_out)[0]
-        if gs.size == 0:
-            continue
-        for g in rng.choice(gs, size=min(per_bucket, gs.size), replace=False):
-            rows.append(int(rng.integers(gr[g, 0], gr[g, 1])))
-    no_out = np.nonzero(~has_out & (sizes > 0))[0]
-    for g in no_out[:5]:
-        rows.append(int(gr[g, 0]))
-    return np.unique(np.array(rows[:max_rows], dtype=np.uint32))
-
-
 @pytest.mark.parametrize("d,dist", [(64, "normal"), (100, "uniform"), (144, "normal"), (200, "uniform"),
                                     (256, "normal"), (300, "normal")])
 def test_operand_widths_match_oracle(ctx, d, dist):
@@ -167,30 +153,76 @@ def test_operand_widths_match_oracle(ctx, d, dist):
     assert t.rows_fallback <= 0.01 * (t.rows_certified + t.rows_fallback)
 
 
-@pytest.mark.parametrize("cfg,n", [(2, None), (3, 200_000), (4, 1_000_000)])
-def test_config_scale_parity(ctx, cfg, n):
-    c = datasets.make_config(cfg, seed=0, n=n)
+def stratified_rows(group_ranges, out_offsets, out_ids, rng, total=2000):
+    """Rows for the full-size checks: every source-group size bucket (singletons .. the
+    largest group), the largest source group itself, rows whose targets include the
+    largest group, groups without targets, then random rows of groups with targets
+    up to `total`."""
+    gr = group_ranges.reshape(-1, 2).astype(np.int64)
+    sizes = gr[:, 1] - gr[:, 0]
+    G = gr.shape[0] - 1
+    oo = out_offsets.astype(np.int64)
+    has_out = np.zeros(G + 1, dtype=bool)
+    has_out[:G + 1] = np.diff(oo[:G + 2]) > 0
+    has_out[0] = False
+    pick = lambda g, m: rng.integers(gr[g, 0], gr[g, 1], size=m)
+    rows = []
+    for lo in [1, 2, 8, 64, 512, 4096, 32768, 262144]:
+        gs = np.nonzero((sizes >= lo) & (sizes < lo * 8) & has_out)[0]
+        for g in rng.choice(gs, size=min(40, gs.size), replace=False) if gs.size else []:
+            rows.append(pick(g, 3))
+    src = np.nonzero(has_out)[0]
+    rows.append(pick(src[np.argmax(sizes[src])], 60))                 # the largest source group
+    big = int(np.argmax(sizes[1:])) + 1                               # the largest group
+    owners = np.repeat(np.arange(G + 1), np.diff(oo[:G + 2]))
+    into_big = np.unique(owners[out_ids.astype(np.int64) == big])
+    for g in rng.choice(into_big, size=min(60, into_big.size), replace=False) if into_big.size else []:
+        rows.append(pick(g, 4))                                       # rows whose targets hold it
+    for g in np.nonzero(~has_out & (sizes > 0))[0][:20]:
+        rows.append(pick(g, 1))                                       # rows without targets
+    rows = np.unique(np.concatenate(rows))
+    w = np.where(has_out, sizes, 0).astype(np.float64)
+    while rows.size < total:
+        need = total - rows.size
+        g = rng.choice(G + 1, size=need, p=w / w.sum())
+        rows = np.unique(np.concatenate([rows, gr[g, 0] + (rng.random(need) * sizes[g]).astype(np.int64)]))
+    return rows.astype(np.uint32)
+
+
+def full_size_case(cfg):
+    c = datasets.make_config(cfg, seed=0)
     lg = nat.LabelGraph(c["label_offsets"], c["labels"])
-    Xr = np.ascontiguousarray(c["X"][lg.new_to_old])
+    Xr = datasets.reorder_rows(c["X"], lg.new_to_old)
+    del c["X"]
+    return c, lg, Xr
+
+
+@pytest.mark.parametrize("cfg", [2, 3, 4])
+def test_full_size_configuration_parity(ctx, cfg):
+    """Configurations 2 (1M x 128), 3 (1M x 960, k = 16) and 4 (10M x 96) at their full
+    size through the C ABI: >= 2,000 stratified rows equal to the oracle's exact scan in
+    ids and distance bits, >= 100,000 rows (here every row) with the size-independent
+    properties, and the certificate clearing nearly every row."""
+    c, lg, Xr = full_size_case(cfg)
     N, d, k = Xr.shape[0], Xr.shape[1], c["k"]
+    assert N == datasets.CONFIGS[cfg]["n"]
     prob = nat.Problem(N, d, k, lg.group_ranges, lg.out_offsets, lg.out_ids, route=nat.ROUTE_TENSOR)
     ids = np.empty(N * k, dtype=np.uint32)
     dists = np.empty(N * k, dtype=np.float32)
     ctx.prepare_base_vectors(Xr, N, d, on_device=False)
     t = ctx.generate(prob, ids, dists)
     ctx.release_base_vectors()
-    rng = np.random.default_rng(cfg)
-    rows = sample_rows(lg.group_ranges, lg.out_offsets, rng, per_bucket=12 if d <= 128 else 5)
+    print(f"config {cfg}: rows_certified={t.rows_certified} rows_fallback={t.rows_fallback} "
+          f"tc_ms={t.tc_kernel_ms:.1f} pairs={t.pairs}")
+    rng = np.random.default_rng(100 + cfg)
+    rows = stratified_rows(lg.group_ranges, lg.out_offsets, lg.out_ids, rng)
+    assert rows.size >= 2000
     group_first = np.concatenate([[0], lg.group_ranges[2::2], [lg.group_ranges[-1]]]).astype(np.uint32)
     o_ids, o_d = O.oracle().cross_rows(Xr, k, group_first, lg.out_offsets, lg.out_ids, rows)
-    full_ids = np.full((N, k), 0xFFFFFFFF, dtype=np.uint32)
-    full_d = np.full((N, k), np.inf, dtype=np.float32)
-    full_ids[rows] = o_ids
-    full_d[rows] = o_d
-    assert_rows_match(ids, dists, full_ids.ravel(), full_d.ravel(), k, rows=rows)
-    prop_rows = np.unique(np.concatenate([rows, rng.integers(0, N, size=2000).astype(np.uint32)]))
-    check_row_properties(ids, dists, k, lg.group_ranges, lg.out_offsets, lg.out_ids, prop_rows)
-    # the certificate must clear nearly every row (the rest are rescanned exactly)
+    assert_rows_match(ids.reshape(N, k)[rows], dists.reshape(N, k)[rows], o_ids, o_d, k)
+    checked = check_row_properties_fast(ids, dists, k, lg.group_ranges, lg.out_offsets, lg.out_ids,
+                                        np.arange(N))
+    assert checked >= 100_000
     assert t.rows_certified + t.rows_fallback > 0
     assert t.rows_fallback <= 0.01 * (t.rows_certified + t.rows_fallback)
 

@@ -6,12 +6,15 @@
   reference's order, and the same edges per point;
 * ungx_graph_csr_device emits, per point, intra-group edges, then cross edges in queue
   order, then additional edges, equal to the same adjacency assembled on the host;
-* a column buffer that is too small is refused without writing.
+* a column buffer that is too small is refused without writing;
+* ungx_build_cross_group_edges (generate, additional edges, add_offset and merge in one
+  call) equals the reference's per-point adjacency assembled from the fixtures.
 """
 import numpy as np
 import pytest
 
 from filtervectorcode_refactor_b200 import _native as nat
+from graph_case import expected_merged_graph, local_intra_graph
 
 pytestmark = pytest.mark.gpu
 
@@ -103,3 +106,49 @@ def test_graph_csr_device_matches_host_assembly(ctx, golden):
     assert total2 == int(h_off[-1])
     assert np.array_equal(d_off.cpu().numpy().view(np.uint64), h_off)
     assert np.array_equal(d_cols.cpu().numpy().view(np.uint32)[:total2], h_cols)
+
+
+@pytest.mark.parametrize("additional", [True, False], ids=["with_additional", "cross_only"])
+def test_build_cross_group_edges_one_call(ctx, golden, additional):
+    """ungx_build_cross_group_edges (the whole build_cross_group_edges step: generate,
+    additional edges, add_offset, merge) equals the reference's per-point adjacency
+    assembled from the golden fixtures."""
+    n, d = golden["Xr"].shape
+    k = golden["k"]
+    route = nat.ROUTE_TENSOR if k <= 24 else nat.ROUTE_EXACT
+    prob = nat.Problem(n, d, k, golden["group_ranges"], golden["out_offsets"], golden["out_ids"], route=route)
+    intra_off, intra_cols = local_intra_graph(golden, n)
+    flags = nat.BUILD_INTRA_LOCAL_IDS | (nat.BUILD_ADDITIONAL if additional else 0)
+    ids = np.empty(n * k, dtype=np.uint32)
+    dists = np.empty(n * k, dtype=np.float32)
+    st = ctx.build_cross_group_edges(golden["Xr"], prob, intra_off, intra_cols, flags, ids, dists)
+    off, cols = ctx.graph_copy(n, int(st.num_cols))
+    ctx.release_base_vectors()
+    assert np.array_equal(ids, golden["ids"])
+    assert np.array_equal(dists.view(np.uint32), golden["dists"].view(np.uint32))
+    e_off, e_cols = expected_merged_graph(golden, intra_off, intra_cols, additional)
+    assert np.array_equal(off, e_off)
+    assert np.array_equal(cols, e_cols)
+    assert st.cross_edges == int((golden["ids"] != 0xFFFFFFFF).sum())
+    assert st.additional.edges == (golden["add_from"].size if additional else 0)
+
+
+def test_build_cross_group_edges_device_vectors_global_ids(ctx, golden):
+    """Vectors already in device memory and intra columns that are global ids (no offset)."""
+    n, d = golden["Xr"].shape
+    k = golden["k"]
+    if k > 24:
+        pytest.skip("tensor route needs k <= 24")
+    prob = nat.Problem(n, d, k, golden["group_ranges"], golden["out_offsets"], golden["out_ids"])
+    intra_off, intra_local = local_intra_graph(golden, n + 1)
+    first = golden["group_first"].astype(np.int64)
+    grp = np.searchsorted(first[1:], np.arange(n), side="right")
+    intra_global = (intra_local + np.repeat(first[grp], np.diff(intra_off.astype(np.int64)))).astype(np.uint32)
+    X = torch.from_numpy(golden["Xr"]).cuda()
+    torch.cuda.synchronize()
+    st = ctx.build_cross_group_edges(X.data_ptr(), prob, intra_off, intra_global,
+                                     nat.BUILD_ADDITIONAL | nat.BUILD_VECTORS_ON_DEVICE)
+    off, cols = ctx.graph_copy(n, int(st.num_cols))
+    ctx.release_base_vectors()
+    e_off, e_cols = expected_merged_graph(golden, intra_off, intra_local, True)
+    assert np.array_equal(off, e_off) and np.array_equal(cols, e_cols)

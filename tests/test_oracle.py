@@ -75,3 +75,50 @@ def test_planted_mistake_is_caught(golden):
     ids[row * k] ^= 1
     with pytest.raises(AssertionError):
         assert_rows_match(ids, dists, golden["ids"], golden["dists"], k)
+
+
+@pytest.mark.parametrize("name", __import__("adversarial").CASES)
+def test_oracle_matches_reference_on_certificate_edge_cases(name):
+    """The certificate's adversarial inputs (huge norm spans, fp16-subnormal operands,
+    an element beyond fp16's range with +inf distances, a large offset, ties): the C
+    restatement equals the reference's own compiled exact scan on every row."""
+    from adversarial import make_case
+    X, k, first, ranges, off, ids = make_case(name)
+    o_ids, o_d, o_pairs = O.oracle().cross_exact(X, k, first, off, ids)
+    assert o_pairs > 0
+    ref = O.reference()
+    if ref is None:
+        pytest.skip("reference build (oracle/_ref) not present on this machine")
+    r_ids, r_d, r_pairs = ref.cross_exact(X, k, first, off, ids)
+    assert r_pairs == o_pairs
+    assert np.array_equal(r_ids, o_ids)
+    assert np.array_equal(r_d.view(np.uint32), o_d.view(np.uint32))
+
+
+def test_row_property_checkers_agree_and_catch_mistakes(golden):
+    """The vectorised size-independent row checker accepts every golden row, as the
+    per-row one does, and rejects planted mistakes (an unsorted row, an id outside the
+    row's out-groups, a missing edge)."""
+    from parity import check_row_properties, check_row_properties_fast
+    k = golden["k"]
+    ids, d = golden["ids"].copy(), golden["dists"].copy()
+    n = ids.size // k
+    args = (k, golden["group_ranges"], golden["out_offsets"], golden["out_ids"])
+    assert check_row_properties_fast(ids, d, *args, np.arange(n)) == n
+    check_row_properties(ids, d, *args, np.arange(min(n, 300)))
+    full = np.nonzero(np.all(ids.reshape(-1, k) != 0xFFFFFFFF, axis=1))[0]
+    r = int(full[0])
+    for plant in ("swap", "foreign", "missing"):
+        i2, d2 = ids.copy().reshape(-1, k), d.copy().reshape(-1, k)
+        if plant == "swap":
+            i2[r, [0, 1]] = i2[r, [1, 0]]
+            d2[r, [0, 1]] = d2[r, [1, 0]]
+            if d2[r, 0] == d2[r, 1]:
+                continue
+        elif plant == "foreign":
+            i2[r, k - 1] = r  # the row itself: never in its own out-groups
+        else:
+            i2[r, k - 1] = 0xFFFFFFFF
+            d2[r, k - 1] = np.inf
+        with pytest.raises(AssertionError):
+            check_row_properties_fast(i2.ravel(), d2.ravel(), *args, np.array([r]))

@@ -1,11 +1,14 @@
 """ungx_cross_edges_exact_noalloc: the exact route for callers that cannot allocate
-device memory (code recording a CUDA graph, code whose device memory belongs to
-another allocator, services with a fixed device footprint).
+device memory (code whose device memory belongs to another allocator, services
+whose device footprint must not grow while they serve).
 
 Through the C ABI, two calls in a row of the no-allocation entry point must give
 the same rows as the existing entry point (ungx_cross_edges_generate, exact route),
 ids equal and distance bits equal, the same tolerance as every other parity test
-here.  This file is collected last so that a failure here cannot hide others.
+here.  The device's free memory must not change across those calls (the first call
+on the device, which may load the library's module, comes before the measurement),
+and one of them runs on a non-default stream.  This file is collected last so that
+a failure here cannot hide others.
 """
 import numpy as np
 import pytest
@@ -33,15 +36,27 @@ def test_noalloc_matches_existing_entry_point(name):
     # the caller owns every device buffer; the entry point allocates none
     torch.cuda.set_device(0)
     X = torch.from_numpy(g["Xr"]).cuda()
-    for call in range(2):
-        ids = torch.full((n * k,), -7, dtype=torch.int32, device="cuda")
-        dists = torch.full((n * k,), -3.0, dtype=torch.float32, device="cuda")
+    ids = torch.empty((n * k,), dtype=torch.int32, device="cuda")
+    dists = torch.empty((n * k,), dtype=torch.float32, device="cuda")
+    side = torch.cuda.Stream()
+    # a first call on this device (it may load the library's module with its array)
+    nat.cross_edges_exact_noalloc(prob, X.data_ptr(), ids.data_ptr(), dists.data_ptr())
+    torch.cuda.synchronize()
+    free_before = torch.cuda.mem_get_info(0)[0]
+    results = []
+    for call, stream in enumerate([None, side]):
+        ids.fill_(-7)
+        dists.fill_(-3.0)
         torch.cuda.synchronize()
-        nat.cross_edges_exact_noalloc(prob, X.data_ptr(), ids.data_ptr(), dists.data_ptr())
-        got_ids = ids.cpu().numpy().view(np.uint32)
-        got_d = dists.cpu().numpy()
+        nat.cross_edges_exact_noalloc(prob, X.data_ptr(), ids.data_ptr(), dists.data_ptr(),
+                                      None if stream is None else stream.cuda_stream)
+        torch.cuda.synchronize()
+        results.append((ids.cpu().numpy().view(np.uint32).copy(), dists.cpu().numpy().copy()))
+    free_after = torch.cuda.mem_get_info(0)[0]
+    assert free_after == free_before, f"device free memory changed by {free_before - free_after} bytes"
+    for got_ids, got_d in results:
         assert_rows_match(got_ids, got_d, ref_ids, ref_d, k)
-    assert_rows_match(got_ids, got_d, g["ids"], g["dists"], k)
+    assert_rows_match(results[-1][0], results[-1][1], g["ids"], g["dists"], k)
 
 
 def test_noalloc_rejects_plans_beyond_its_scratch():
