@@ -108,6 +108,42 @@ class CrossGroupStats(ctypes.Structure):
     ]
 
 
+class DistTiming(ctypes.Structure):
+    """Layout of ``ungx_dist_timing``."""
+
+    _fields_ = [
+        ("cross", CrossEdgeTiming),
+        ("upload_ms", c_double),
+        ("replicate_ms", c_double),
+        ("prepare_ms", c_double),
+        ("gather_ms", c_double),
+        ("d2h_ms", c_double),
+        ("total_ms", c_double),
+        ("shard_rows", c_uint64),
+        ("shard_cost", c_uint64),
+        ("shard_cost_max", c_uint64),
+        ("shard_cost_total", c_uint64),
+        ("world_size", c_uint32),
+        ("rank", c_uint32),
+        ("plan_reused", c_uint32),
+        ("gpu_launches", c_uint32),
+    ]
+
+    def as_dict(self) -> dict:
+        d = {name: getattr(self, name) for name, _ in self._fields_ if name != "cross"}
+        d["cross"] = self.cross.as_dict()
+        return d
+
+
+class CommId(ctypes.Structure):
+    """Layout of ``ungx_comm_id`` (an NCCL unique id)."""
+
+    _fields_ = [("internal", ctypes.c_char * 128)]
+
+
+DIST_DEVICE_VECTORS = 1
+DIST_DEVICE_OUTPUT = 2
+
 BUILD_ADDITIONAL = 1
 BUILD_INTRA_LOCAL_IDS = 2
 BUILD_VECTORS_ON_DEVICE = 4
@@ -147,6 +183,12 @@ _SIGNATURES = [
     ("ungx_cross_edges_exact_noalloc", c_int,
      [POINTER(CrossEdgeProblem), c_void_p, c_void_p, c_void_p, c_void_p]),
     ("ungx_shard_rows", c_int, [POINTER(CrossEdgeProblem), c_void_p, POINTER(c_uint64)]),
+    ("ungx_comm_id_create", c_int, [POINTER(CommId)]),
+    ("ungx_comm_init", c_int, [c_void_p, POINTER(CommId), c_int, c_int]),
+    ("ungx_comm_destroy", c_int, [c_void_p]),
+    ("ungx_dist_slice", c_int, [c_uint32, c_uint32, c_uint32, POINTER(c_uint32), POINTER(c_uint32)]),
+    ("ungx_cross_edges_build_distributed", c_int,
+     [c_void_p, c_void_p, c_uint32, POINTER(CrossEdgeProblem), c_void_p, c_void_p, POINTER(DistTiming)]),
     ("ungx_label_graph_build", c_int, [c_uint32, c_void_p, c_void_p, c_int, POINTER(c_void_p)]),
     ("ungx_label_graph_destroy", c_int, [c_void_p]),
     ("ungx_label_graph_num_groups", c_uint32, [c_void_p]),
@@ -336,6 +378,32 @@ class Context:
         return t
 
 
+    def comm_init(self, comm_id: bytes, world_size: int, rank: int) -> None:
+        """ungx_comm_init: join the NCCL communicator of ``comm_id`` (from comm_id_create)."""
+        if len(comm_id) != ctypes.sizeof(CommId):
+            raise ValueError("a communicator id has 128 bytes")
+        cid = CommId()
+        ctypes.memmove(ctypes.addressof(cid), comm_id, len(comm_id))
+        check(lib.ungx_comm_init(self.h, ctypes.byref(cid), world_size, rank), self.h)
+
+    def comm_destroy(self) -> None:
+        check(lib.ungx_comm_destroy(self.h), self.h)
+
+    def build_distributed(self, vectors, problem: Problem, out_ids, out_dists, flags: int = 0) -> DistTiming:
+        """ungx_cross_edges_build_distributed.  ``vectors``: this rank's slice (host array,
+        rows of dist_slice), or an integer device pointer to the whole matrix with
+        DIST_DEVICE_VECTORS.  ``out_ids`` / ``out_dists``: host arrays, or integer device
+        pointers with DIST_DEVICE_OUTPUT (rank 0 only; other ranks may pass None)."""
+        t = DistTiming()
+        vp = vectors if (flags & DIST_DEVICE_VECTORS) else _ptr(vectors)
+        if flags & DIST_DEVICE_OUTPUT:
+            oi, od = out_ids, out_dists
+        else:
+            oi, od = _ptr(out_ids), _ptr(out_dists)
+        check(lib.ungx_cross_edges_build_distributed(self.h, vp, flags, ctypes.byref(problem.c), oi, od,
+                                                     ctypes.byref(t)), self.h)
+        return t
+
     def additional_edges(self, problem: Problem, d_cross_ids: int, stream: int | None = None) -> AdditionalStats:
         """ungx_additional_edges_build on a device cross-edge output [n x k]."""
         st = AdditionalStats()
@@ -405,6 +473,20 @@ def cross_edges_exact_noalloc(problem: Problem, d_vectors: int, d_ids: int, d_di
                               stream: int | None = None) -> None:
     """ungx_cross_edges_exact_noalloc: device pointers in and out, no device allocation."""
     check(lib.ungx_cross_edges_exact_noalloc(ctypes.byref(problem.c), d_vectors, d_ids, d_dists, stream))
+
+
+def comm_id_create() -> bytes:
+    """ungx_comm_id_create: a new NCCL unique id (128 bytes) for ungx_comm_init."""
+    cid = CommId()
+    check(lib.ungx_comm_id_create(ctypes.byref(cid)))
+    return ctypes.string_at(ctypes.addressof(cid), ctypes.sizeof(cid))
+
+
+def dist_slice(num_points: int, world_size: int, rank: int) -> tuple[int, int]:
+    """(first row, row count) that ``rank`` passes from host memory to build_distributed."""
+    a, c = c_uint32(), c_uint32()
+    check(lib.ungx_dist_slice(num_points, world_size, rank, ctypes.byref(a), ctypes.byref(c)))
+    return a.value, c.value
 
 
 def graph_save_text(path: str, offsets: np.ndarray, cols: np.ndarray) -> None:

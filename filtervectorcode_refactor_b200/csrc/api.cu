@@ -19,6 +19,7 @@
 #include <thread>
 
 #include "kernels.h"
+#include "nccl_dl.h"
 #include "ungx_internal.h"
 
 using ungx::Plan;
@@ -91,9 +92,33 @@ double ms_since(std::chrono::steady_clock::time_point t0)
 }
 } // namespace
 
+// The problem a cached plan was made for; a call whose arrays are byte-identical (and
+// whose shard is the same) reuses the plan and its device copy.
+struct PlanKey
+{
+   uint32_t n = 0, G = 0, rank = 0, count = 0;
+   bool skip = false;
+   std::vector<uint32_t> ranges, ids;
+   std::vector<uint64_t> off;
+   std::vector<uint8_t> skipv;
+};
+
 struct ungx_context
 {
    Plan plan; // the last generate call's plan and the planner's working storage
+   PlanKey plan_key;
+   bool plan_valid = false;     // `plan` was made for `plan_key`
+   bool plan_on_device = false; // its arrays are in items / segs / empties / ranges / norm_chunks
+   // every shard's rows as runs (multi-GPU gather), for the cached plan
+   std::vector<std::vector<ungx::CopyRange>> runs;
+   std::vector<uint32_t> run_rows;
+   bool runs_valid = false;
+   // multi-GPU: communicator of this context's device
+   const ungx::NcclApi *nccl = nullptr;
+   ncclComm_t comm = nullptr;
+   int world = 1, rank = 0;
+   DevBuf own_runs, all_runs, recv;
+   cudaEvent_t dev_ev[8] = {};
    // a plan made while ungx_cross_edges_build uploaded the vectors, for that problem
    const ungx_cross_edge_problem *preplanned = nullptr;
    int preplan_status = 0;
@@ -255,6 +280,64 @@ int upload(ungx_context *ctx, DevBuf &buf, const std::vector<T> &v, const char *
    return UNGX_OK;
 }
 
+bool same_problem(const PlanKey &k, const ungx_cross_edge_problem &p)
+{
+   if (k.n != p.num_points || k.G != p.num_groups || k.rank != p.shard_rank || k.count != p.shard_count ||
+       k.skip != (p.skip_source_group != nullptr))
+      return false;
+   const size_t G = p.num_groups;
+   if (G == 0)
+      return true;
+   if (std::memcmp(k.ranges.data(), p.group_ranges, 2 * (G + 1) * sizeof(uint32_t)) ||
+       std::memcmp(k.off.data(), p.lng_out_offsets, (G + 2) * sizeof(uint64_t)))
+      return false;
+   const uint64_t nnz = p.lng_out_offsets[G + 1];
+   if (k.ids.size() != nnz || (nnz && std::memcmp(k.ids.data(), p.lng_out_ids, nnz * sizeof(uint32_t))))
+      return false;
+   return !k.skip || !std::memcmp(k.skipv.data(), p.skip_source_group, G + 1);
+}
+
+// The context's plan for `p`: reused when the problem's arrays and shard equal the
+// cached plan's, built (and the key stored) otherwise.
+int ensure_plan(ungx_context *ctx, const ungx_cross_edge_problem &p, bool &reused, std::string &err)
+{
+   reused = false;
+   if (p.dim == 0 || p.topk == 0)
+   {
+      err = "dim and topk must be positive";
+      return UNGX_ERR_INVALID_ARG;
+   }
+   if (ctx->plan_valid && same_problem(ctx->plan_key, p))
+   {
+      reused = true;
+      return UNGX_OK;
+   }
+   ctx->plan_valid = false;
+   ctx->plan_on_device = false;
+   ctx->runs_valid = false;
+   const int st = ungx::build_plan(p, ctx->plan, err);
+   if (st != UNGX_OK)
+      return st;
+   PlanKey &k = ctx->plan_key;
+   const size_t G = p.num_groups;
+   k.n = p.num_points;
+   k.G = p.num_groups;
+   k.rank = p.shard_rank;
+   k.count = p.shard_count;
+   k.skip = p.skip_source_group != nullptr;
+   if (G)
+   {
+      k.ranges.assign(p.group_ranges, p.group_ranges + 2 * (G + 1));
+      k.off.assign(p.lng_out_offsets, p.lng_out_offsets + G + 2);
+      const uint64_t nnz = p.lng_out_offsets[G + 1];
+      k.ids.assign(p.lng_out_ids, p.lng_out_ids + nnz);
+      if (k.skip)
+         k.skipv.assign(p.skip_source_group, p.skip_source_group + G + 1);
+   }
+   ctx->plan_valid = true;
+   return UNGX_OK;
+}
+
 // The device half of generate: plan upload, kernels, counters.  Outputs are device
 // pointers.  Fills `timing` with device times.
 int run_generate(ungx_context *ctx, const ungx_cross_edge_problem &p, const Plan &plan, uint32_t *d_ids,
@@ -279,16 +362,22 @@ int run_generate(ungx_context *ctx, const ungx_cross_edge_problem &p, const Plan
    if (s != ctx->stream) // the operand is prepared on the context's stream
       UNGX_CUDA(ctx, cudaStreamWaitEvent(s, ev[10], 0), "stream wait");
    UNGX_CUDA(ctx, cudaEventRecord(ev[0], s), "event");
-   // plan upload
-   std::vector<uint32_t> ranges(2 * size_t(p.num_groups + 1));
-   if (p.num_groups)
-      std::memcpy(ranges.data(), p.group_ranges, ranges.size() * sizeof(uint32_t));
+   // plan upload (once per plan: the arrays stay on the device while the plan is reused)
+   const bool cached = ctx->plan_on_device && &plan == &ctx->plan;
    int st;
-   if ((st = upload(ctx, ctx->items, plan.items, "plan upload")) ||
-       (st = upload(ctx, ctx->segs, plan.segs, "plan upload")) ||
-       (st = upload(ctx, ctx->empties, plan.empty_rows, "plan upload")) ||
-       (st = upload(ctx, ctx->ranges, ranges, "plan upload")))
-      return st;
+   if (!cached)
+   {
+      std::vector<uint32_t> ranges(2 * size_t(p.num_groups + 1));
+      if (p.num_groups)
+         std::memcpy(ranges.data(), p.group_ranges, ranges.size() * sizeof(uint32_t));
+      if ((st = upload(ctx, ctx->items, plan.items, "plan upload")) ||
+          (st = upload(ctx, ctx->segs, plan.segs, "plan upload")) ||
+          (st = upload(ctx, ctx->empties, plan.empty_rows, "plan upload")) ||
+          (st = upload(ctx, ctx->ranges, ranges, "plan upload")) ||
+          (st = upload(ctx, ctx->norm_chunks, plan.norm_chunks, "plan upload")))
+         return st;
+      ctx->plan_on_device = &plan == &ctx->plan;
+   }
    uint64_t item_rows = 0;
    for (const auto &it : plan.items)
       item_rows += it.row_count;
@@ -308,8 +397,6 @@ int run_generate(ungx_context *ctx, const ungx_cross_edge_problem &p, const Plan
    if (route == UNGX_ROUTE_TENSOR && !plan.items.empty())
    {
       UNGX_CUDA(ctx, ctx->gmax.ensure(sizeof(float) * (p.num_groups + 1)), "group norms");
-      if ((st = upload(ctx, ctx->norm_chunks, plan.norm_chunks, "plan upload")))
-         return st;
       UNGX_CUDA(ctx,
                 ungx::launch_group_maxnorm(ctx->xnorm.as<float>(), ctx->norm_chunks.as<uint32_t>(),
                                            (uint32_t)(plan.norm_chunks.size() / 3), p.num_groups,
@@ -506,6 +593,9 @@ int ungx_context_create(int device, ungx_context **out)
    for (auto &ev : ctx->ev)
       if ((e = cudaEventCreate(&ev)) != cudaSuccess)
          return cuda_fail(nullptr, e, "event");
+   for (auto &ev : ctx->dev_ev)
+      if ((e = cudaEventCreate(&ev)) != cudaSuccess)
+         return cuda_fail(nullptr, e, "event");
    if ((e = cudaHostAlloc(&ctx->h_counters, 64, cudaHostAllocDefault)) != cudaSuccess)
       return cuda_fail(nullptr, e, "pinned counters");
    void *fn = nullptr;
@@ -525,6 +615,7 @@ int ungx_context_destroy(ungx_context *ctx)
    cudaSetDevice(ctx->device);
    if (ctx->stream)
       cudaStreamSynchronize(ctx->stream);
+   ungx_comm_destroy(ctx);
    ungx_release_base_vectors(ctx);
    for (DevBuf *b : {&ctx->items, &ctx->segs, &ctx->empties, &ctx->ranges, &ctx->gmax, &ctx->norm_chunks, &ctx->counters,
                      &ctx->fb_rows, &ctx->fb_items, &ctx->rows, &ctx->row_items, &ctx->out_ids, &ctx->out_dists,
@@ -534,10 +625,14 @@ int ungx_context_destroy(ungx_context *ctx)
                      &ctx->add_res, &ctx->add_off, &ctx->add_cols, &ctx->add_qoff, &ctx->add_loff, &ctx->add_from,
                      &ctx->add_to, &ctx->add_stats, &ctx->scan_scratch, &ctx->knn_ranges,
                      &ctx->knn_base, &ctx->knn_tasks, &ctx->knn_dist, &ctx->knn_dbase, &ctx->knn_tiles,
-                     &ctx->knn_rows, &ctx->intra_off, &ctx->intra_cols, &ctx->graph_off, &ctx->graph_cols})
+                     &ctx->knn_rows, &ctx->intra_off, &ctx->intra_cols, &ctx->graph_off, &ctx->graph_cols,
+                     &ctx->own_runs, &ctx->all_runs, &ctx->recv})
       b->release();
    ctx->host_stage.release();
    for (auto &ev : ctx->ev)
+      if (ev)
+         cudaEventDestroy(ev);
+   for (auto &ev : ctx->dev_ev)
       if (ev)
          cudaEventDestroy(ev);
    if (ctx->h_counters)
@@ -658,7 +753,8 @@ int ungx_cross_edges_generate_device(ungx_context *ctx, const ungx_cross_edge_pr
    ungx_cross_edge_timing t{};
    Plan &plan = ctx->plan; // reused: its buffers keep their capacity across calls
    std::string err;
-   int st = ungx::build_plan(*problem, plan, err);
+   bool reused = false;
+   int st = ensure_plan(ctx, *problem, reused, err);
    if (st)
       return fail(ctx, st, "invalid problem: " + err);
    t.plan_ms = ms_since(t0);
@@ -697,7 +793,8 @@ int ungx_cross_edges_generate(ungx_context *ctx, const ungx_cross_edge_problem *
    }
    else
    {
-      st = ungx::build_plan(*problem, plan, err);
+      bool reused = false;
+      st = ensure_plan(ctx, *problem, reused, err);
       t.plan_ms = ms_since(t0);
    }
    if (st)
@@ -802,7 +899,8 @@ int ungx_cross_edges_build(ungx_context *ctx, const float *vectors, const ungx_c
    double pms = 0;
    std::thread planner([&] {
       const auto a = std::chrono::steady_clock::now();
-      pst = ungx::build_plan(*problem, ctx->plan, perr);
+      bool reused = false;
+      pst = ensure_plan(ctx, *problem, reused, perr);
       pms = ms_since(a);
    });
    int st = ungx_prepare_base_vectors(ctx, vectors, problem->num_points, problem->dim, 0);
@@ -1046,6 +1144,301 @@ int ungx_graph_csr_device(ungx_context *ctx, uint32_t num_points, uint32_t topk,
    return wait_event(ctx, ctx->ev[6], "graph emission");
 }
 
+int ungx_comm_id_create(ungx_comm_id *id)
+{
+   static_assert(sizeof(ungx_comm_id) == sizeof(ncclUniqueId), "ungx_comm_id holds an ncclUniqueId");
+   if (!id)
+      return fail(nullptr, UNGX_ERR_INVALID_ARG, "ungx_comm_id_create: null id");
+   std::string err;
+   const ungx::NcclApi *api = ungx::nccl_api(err);
+   if (!api)
+      return fail(nullptr, UNGX_ERR_STATE, err);
+   ncclUniqueId u;
+   const ncclResult_t r = api->GetUniqueId(&u);
+   if (r != ncclSuccess)
+      return fail(nullptr, UNGX_ERR_CUDA, std::string("ncclGetUniqueId: ") + api->GetErrorString(r));
+   std::memcpy(id, &u, sizeof(u));
+   return UNGX_OK;
+}
+
+int ungx_comm_init(ungx_context *ctx, const ungx_comm_id *id, int world_size, int rank)
+{
+   if (!ctx || !id)
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "ungx_comm_init: null argument");
+   if (world_size < 1 || rank < 0 || rank >= world_size)
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "ungx_comm_init: rank must be in 0 .. world_size-1");
+   std::string err;
+   const ungx::NcclApi *api = ungx::nccl_api(err);
+   if (!api)
+      return fail(ctx, UNGX_ERR_STATE, err);
+   ungx_comm_destroy(ctx);
+   UNGX_CUDA(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+   ncclUniqueId u;
+   std::memcpy(&u, id, sizeof(u));
+   ncclComm_t comm = nullptr;
+   const ncclResult_t r = api->CommInitRank(&comm, world_size, u, rank);
+   if (r != ncclSuccess)
+      return fail(ctx, UNGX_ERR_CUDA, std::string("ncclCommInitRank: ") + api->GetErrorString(r));
+   ctx->nccl = api;
+   ctx->comm = comm;
+   ctx->world = world_size;
+   ctx->rank = rank;
+   return UNGX_OK;
+}
+
+int ungx_comm_destroy(ungx_context *ctx)
+{
+   if (!ctx)
+      return UNGX_ERR_INVALID_ARG;
+   if (ctx->comm)
+   {
+      cudaSetDevice(ctx->device);
+      ctx->nccl->CommDestroy(ctx->comm);
+   }
+   ctx->comm = nullptr;
+   ctx->world = 1;
+   ctx->rank = 0;
+   return UNGX_OK;
+}
+
+int ungx_dist_slice(uint32_t num_points, uint32_t world_size, uint32_t rank, uint32_t *first, uint32_t *count)
+{
+   if (!first || !count || world_size == 0 || rank >= world_size)
+      return fail(nullptr, UNGX_ERR_INVALID_ARG, "ungx_dist_slice: bad argument");
+   const uint64_t per = (uint64_t(num_points) + world_size - 1) / world_size;
+   const uint64_t a = std::min<uint64_t>(num_points, per * rank);
+   *first = uint32_t(a);
+   *count = uint32_t(std::min<uint64_t>(per, num_points - a));
+   return UNGX_OK;
+}
+
+int ungx_cross_edges_build_distributed(ungx_context *ctx, const float *vectors, uint32_t flags,
+                                       const ungx_cross_edge_problem *problem, uint32_t *out_ids, float *out_dists,
+                                       ungx_dist_timing *timing)
+{
+   if (!ctx || !problem)
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "null argument");
+   if (flags & ~uint32_t(UNGX_DIST_DEVICE_VECTORS | UNGX_DIST_DEVICE_OUTPUT))
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "unknown flag");
+   const int world = ctx->comm ? ctx->world : 1, rank = ctx->comm ? ctx->rank : 0;
+   const uint32_t n = problem->num_points, d = problem->dim, k = problem->topk;
+   if (n == 0 || d == 0 || k == 0)
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "empty problem");
+   uint32_t first = 0, cnt = 0;
+   ungx_dist_slice(n, uint32_t(world), uint32_t(rank), &first, &cnt);
+   if (!vectors && ((flags & UNGX_DIST_DEVICE_VECTORS) || cnt))
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "null vectors");
+   if (rank == 0 && !out_ids)
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "rank 0 needs out_ids");
+   UNGX_CUDA(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+   const auto t0 = std::chrono::steady_clock::now();
+   ungx_dist_timing T{};
+   T.world_size = uint32_t(world);
+   T.rank = uint32_t(rank);
+   ungx_cross_edge_problem pr = *problem;
+   pr.shard_rank = uint32_t(rank);
+   pr.shard_count = uint32_t(world);
+   cudaStream_t s = ctx->stream;
+   cudaEvent_t *E = ctx->dev_ev;
+   // plan on a host thread (or find the previous one reusable) while the vectors go up
+   int pst = 0;
+   bool reused = false;
+   std::string perr;
+   double pms = 0;
+   std::thread planner([&] {
+      const auto a = std::chrono::steady_clock::now();
+      pst = ensure_plan(ctx, pr, reused, perr);
+      pms = ms_since(a);
+   });
+   auto join_fail = [&](int code) {
+      planner.join();
+      return code;
+   };
+   const float *X = vectors;
+   if (cudaEventRecord(E[0], s) != cudaSuccess)
+      return join_fail(fail(ctx, UNGX_ERR_CUDA, "event"));
+   if (!(flags & UNGX_DIST_DEVICE_VECTORS))
+   {
+      // this rank's slice into its place, then every slice to every rank over NVLink
+      const size_t per = (size_t(n) + world - 1) / world;
+      cudaError_t e = ctx->X_owned.ensure(per * world * d * sizeof(float));
+      if (e != cudaSuccess)
+         return join_fail(cuda_fail(ctx, e, "vector allocation"));
+      float *Xo = ctx->X_owned.as<float>();
+      if (cnt)
+      {
+         const int st = upload_vectors(ctx, Xo + size_t(first) * d, vectors, size_t(cnt) * d * sizeof(float));
+         if (st)
+            return join_fail(st);
+      }
+      cudaEventRecord(E[1], s);
+      if (world > 1)
+      {
+         const ncclResult_t r = ctx->nccl->AllGather(Xo + size_t(rank) * per * d, Xo, per * d, ncclFloat32, ctx->comm, s);
+         if (r != ncclSuccess)
+            return join_fail(fail(ctx, UNGX_ERR_CUDA, std::string("ncclAllGather: ") + ctx->nccl->GetErrorString(r)));
+      }
+      X = Xo;
+   }
+   else
+      cudaEventRecord(E[1], s);
+   cudaEventRecord(E[2], s);
+   int st = ungx_prepare_base_vectors(ctx, X, n, d, 1);
+   if (st)
+      return join_fail(st);
+   cudaEventRecord(E[3], s);
+   planner.join();
+   if (pst)
+      return fail(ctx, pst, "invalid problem: " + perr);
+   T.plan_reused = reused ? 1u : 0u;
+   T.cross.plan_ms = pms;
+   T.cross.pairs = ctx->plan.pairs;
+   // this rank's shard: straight into rank 0's device output when it has one
+   const size_t nk = size_t(n) * k;
+   const bool direct = rank == 0 && (flags & UNGX_DIST_DEVICE_OUTPUT);
+   UNGX_CUDA(ctx, ctx->out_ids.ensure(nk * sizeof(uint32_t)), "output allocation");
+   UNGX_CUDA(ctx, ctx->out_dists.ensure(nk * sizeof(float)), "output allocation");
+   uint32_t *d_ids = direct ? out_ids : ctx->out_ids.as<uint32_t>();
+   float *d_dists = direct && out_dists ? out_dists : ctx->out_dists.as<float>();
+   if ((st = run_generate(ctx, pr, ctx->plan, d_ids, d_dists, s, T.cross)))
+      return st;
+   T.gpu_launches = T.cross.gpu_launches + 3; // + the operand kernels
+   // every shard's rows to rank 0: [ids | dists] of a shard's rows in ascending row order
+   UNGX_CUDA(ctx, cudaEventRecord(E[4], s), "event");
+   if (!ctx->runs_valid)
+   {
+      ungx::shard_runs(pr, ctx->plan, ctx->runs, ctx->run_rows);
+      std::vector<ungx::CopyRange> all;
+      uint32_t base = 0;
+      for (int r = 1; r < world; ++r)
+      {
+         for (ungx::CopyRange c : ctx->runs[r])
+         {
+            c.dst_row += base;
+            all.push_back(c);
+         }
+         base += ctx->run_rows[r];
+      }
+      if ((st = upload(ctx, ctx->own_runs, ctx->runs[rank], "run upload")) || (st = upload(ctx, ctx->all_runs, all, "run upload")))
+         return st;
+      ctx->runs_valid = true;
+   }
+   T.shard_rows = ctx->run_rows[rank];
+   T.shard_cost = ctx->plan.shard_load[rank];
+   for (int r = 0; r < world; ++r)
+   {
+      T.shard_cost_max = std::max<uint64_t>(T.shard_cost_max, ctx->plan.shard_load[r]);
+      T.shard_cost_total += ctx->plan.shard_load[r];
+   }
+   if (world > 1)
+   {
+      const ungx::NcclApi *api = ctx->nccl;
+      ncclResult_t r = ncclSuccess;
+      if (rank != 0)
+      {
+         const size_t rows = ctx->run_rows[rank];
+         UNGX_CUDA(ctx, ctx->compact.ensure(std::max<size_t>(rows, 1) * k * 2 * sizeof(uint32_t)), "compact output");
+         uint32_t *c_ids = ctx->compact.as<uint32_t>();
+         float *c_d = reinterpret_cast<float *>(c_ids + rows * k);
+         UNGX_CUDA(ctx,
+                   ungx::launch_gather_rows(ctx->own_runs.as<ungx::CopyRange>(), uint32_t(ctx->runs[rank].size()), k,
+                                            d_ids, d_dists, c_ids, c_d, s),
+                   "row gather kernel");
+         T.gpu_launches += ctx->runs[rank].empty() ? 0 : 1;
+         if (rows)
+         {
+            r = api->GroupStart();
+            if (r == ncclSuccess)
+               r = api->Send(c_ids, rows * k, ncclUint32, 0, ctx->comm, s);
+            if (r == ncclSuccess)
+               r = api->Send(c_d, rows * k, ncclFloat32, 0, ctx->comm, s);
+            const ncclResult_t r2 = api->GroupEnd();
+            r = r == ncclSuccess ? r2 : r;
+         }
+      }
+      else
+      {
+         size_t others = 0;
+         for (int q = 1; q < world; ++q)
+            others += ctx->run_rows[q];
+         UNGX_CUDA(ctx, ctx->recv.ensure(std::max<size_t>(others, 1) * k * 2 * sizeof(uint32_t)), "receive buffer");
+         uint32_t *r_ids = ctx->recv.as<uint32_t>();
+         float *r_d = reinterpret_cast<float *>(r_ids + others * k);
+         r = api->GroupStart();
+         size_t base = 0;
+         for (int q = 1; q < world && r == ncclSuccess; ++q)
+         {
+            const size_t rows = ctx->run_rows[q];
+            if (rows)
+            {
+               r = api->Recv(r_ids + base * k, rows * k, ncclUint32, q, ctx->comm, s);
+               if (r == ncclSuccess)
+                  r = api->Recv(r_d + base * k, rows * k, ncclFloat32, q, ctx->comm, s);
+            }
+            base += rows;
+         }
+         const ncclResult_t r2 = api->GroupEnd();
+         r = r == ncclSuccess ? r2 : r;
+         if (r == ncclSuccess)
+         {
+            size_t nall = 0;
+            for (int q = 1; q < world; ++q)
+               nall += ctx->runs[q].size();
+            UNGX_CUDA(ctx,
+                      ungx::launch_scatter_rows(ctx->all_runs.as<ungx::CopyRange>(), uint32_t(nall), k, r_ids, r_d,
+                                                d_ids, d_dists, s),
+                      "row scatter kernel");
+            T.gpu_launches += nall ? 1 : 0;
+         }
+      }
+      if (r != ncclSuccess)
+         return fail(ctx, UNGX_ERR_CUDA, std::string("NCCL gather: ") + api->GetErrorString(r));
+   }
+   UNGX_CUDA(ctx, cudaEventRecord(E[5], s), "event");
+   if (rank == 0)
+   {
+      if (!(flags & UNGX_DIST_DEVICE_OUTPUT))
+      {
+         UNGX_CUDA(ctx, cudaMemcpyAsync(out_ids, d_ids, nk * sizeof(uint32_t), cudaMemcpyDeviceToHost, s), "output copy");
+         if (out_dists)
+            UNGX_CUDA(ctx, cudaMemcpyAsync(out_dists, d_dists, nk * sizeof(float), cudaMemcpyDeviceToHost, s),
+                      "output copy");
+      }
+      else if (out_dists && d_dists != out_dists)
+         UNGX_CUDA(ctx, cudaMemcpyAsync(out_dists, d_dists, nk * sizeof(float), cudaMemcpyDeviceToDevice, s),
+                   "output copy");
+   }
+   UNGX_CUDA(ctx, cudaEventRecord(E[6], s), "event");
+   if ((st = wait_event(ctx, E[6], "distributed build")))
+   {
+      if (st == UNGX_ERR_TIMEOUT && ctx->comm)
+      {
+         // a peer that never arrives: release this rank's NCCL kernels
+         ctx->nccl->CommAbort(ctx->comm);
+         ctx->comm = nullptr;
+         ctx->world = 1;
+         ctx->rank = 0;
+      }
+      return st;
+   }
+   float a = 0;
+   cudaEventElapsedTime(&a, E[0], E[1]);
+   T.upload_ms = a;
+   cudaEventElapsedTime(&a, E[1], E[2]);
+   T.replicate_ms = a;
+   cudaEventElapsedTime(&a, E[2], E[3]);
+   T.prepare_ms = a;
+   cudaEventElapsedTime(&a, E[4], E[5]);
+   T.gather_ms = a;
+   cudaEventElapsedTime(&a, E[5], E[6]);
+   T.d2h_ms = a;
+   T.total_ms = ms_since(t0);
+   T.cross.generate_ms = T.total_ms;
+   if (timing)
+      *timing = T;
+   return UNGX_OK;
+}
+
 int ungx_build_cross_group_edges(ungx_context *ctx, const float *vectors, const ungx_cross_edge_problem *problem,
                                  const uint64_t *intra_offsets, const uint32_t *intra_cols, uint32_t flags,
                                  uint32_t *out_ids, float *out_dists, ungx_cross_group_stats *stats)
@@ -1077,7 +1470,8 @@ int ungx_build_cross_group_edges(ungx_context *ctx, const float *vectors, const 
    double pms = 0;
    std::thread planner([&] {
       const auto a = std::chrono::steady_clock::now();
-      pst = ungx::build_plan(*problem, ctx->plan, perr);
+      bool reused = false;
+      pst = ensure_plan(ctx, *problem, reused, perr);
       pms = ms_since(a);
    });
    int st = ungx_prepare_base_vectors(ctx, vectors, n, problem->dim, (flags & UNGX_BUILD_VECTORS_ON_DEVICE) ? 1 : 0);

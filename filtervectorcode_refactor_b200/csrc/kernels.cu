@@ -411,6 +411,20 @@ __global__ void gather_rows_kernel(const CopyRange *__restrict__ ranges, uint32_
    }
 }
 
+__global__ void scatter_rows_kernel(const CopyRange *__restrict__ ranges, uint32_t k, const uint32_t *__restrict__ ids,
+                                    const float *__restrict__ dists, uint32_t *__restrict__ out_ids,
+                                    float *__restrict__ out_dists)
+{
+   const CopyRange r = ranges[blockIdx.x];
+   const uint64_t dst = uint64_t(r.src_row) * k, src = uint64_t(r.dst_row) * k, cnt = uint64_t(r.count) * k;
+   for (uint64_t i = threadIdx.x; i < cnt; i += blockDim.x)
+   {
+      out_ids[dst + i] = ids[src + i];
+      if (dists)
+         out_dists[dst + i] = dists[src + i];
+   }
+}
+
 // ------------------------------------------------------------------ exact scan
 // One block (8 warps) per row: the 256 threads stride over the row's candidate
 // columns keeping a sorted top-KMAX each; every warp then emits its own top-k by k
@@ -1510,6 +1524,15 @@ cudaError_t launch_gather_rows(const CopyRange *ranges, uint32_t nranges, uint32
    if (nranges == 0)
       return cudaSuccess;
    gather_rows_kernel<<<nranges, 256, 0, s>>>(ranges, k, ids, dists, out_ids, out_dists);
+   return cudaGetLastError();
+}
+
+cudaError_t launch_scatter_rows(const CopyRange *ranges, uint32_t nranges, uint32_t k, const uint32_t *ids,
+                                const float *dists, uint32_t *out_ids, float *out_dists, cudaStream_t s)
+{
+   if (nranges == 0)
+      return cudaSuccess;
+   scatter_rows_kernel<<<nranges, 256, 0, s>>>(ranges, k, ids, dists, out_ids, out_dists);
    return cudaGetLastError();
 }
 

@@ -123,14 +123,13 @@ cudaError_t launch_group_maxnorm(const float *xnorm, const uint32_t *chunks, uin
 cudaError_t launch_fill_empty(const RowRange *ranges, uint32_t nranges, uint32_t k, uint32_t *ids, float *dists,
                               cudaStream_t s);
 
-// Rows [src_row, src_row+count) of a row-major n x k output go to rows
-// [dst_row, dst_row+count) of a compact buffer (a shard's rows, copied back at once).
-struct CopyRange
-{
-   uint32_t src_row, dst_row, count, pad;
-};
+// CopyRange (ungx_internal.h): a shard's rows into a compact buffer, and back.
 cudaError_t launch_gather_rows(const CopyRange *ranges, uint32_t nranges, uint32_t k, const uint32_t *ids,
                                const float *dists, uint32_t *out_ids, float *out_dists, cudaStream_t s);
+// The reverse of launch_gather_rows: compact rows [dst_row, +count) of (ids, dists) go back
+// to rows [src_row, +count) of the n x k output.
+cudaError_t launch_scatter_rows(const CopyRange *ranges, uint32_t nranges, uint32_t k, const uint32_t *ids,
+                                const float *dists, uint32_t *out_ids, float *out_dists, cudaStream_t s);
 cudaError_t launch_exact(const ExactParams &p, uint32_t grid_hint, cudaStream_t s);
 
 // ---- exact kNN graph seeding (knn.cu)

@@ -194,7 +194,9 @@ int build_plan(const ungx_cross_edge_problem &p, Plan &plan, std::string &err)
 
    // greedy assignment to the least-loaded shard, in that order
    const uint32_t S = p.shard_count;
-   std::vector<uint64_t> load(S, 0);
+   std::vector<uint64_t> &load = plan.shard_load;
+   load.assign(S, 0);
+   plan.item_shard.resize(N);
    plan.items.reserve(S == 1 ? N : N / S + 1);
    for (uint32_t i = 0; i < N; ++i)
    {
@@ -204,6 +206,7 @@ int build_plan(const ungx_cross_edge_problem &p, Plan &plan, std::string &err)
          if (load[s] < load[best])
             best = s;
       load[best] += plan.key[o] + 1;
+      plan.item_shard[o] = best;
       if (best == p.shard_rank)
       {
          const WorkItem &it = plan.all[o];
@@ -224,6 +227,49 @@ int build_plan(const ungx_cross_edge_problem &p, Plan &plan, std::string &err)
          plan.norm_chunks.insert(plan.norm_chunks.end(), {f, r, std::min(4096u, b - r)});
    }
    return UNGX_OK;
+}
+
+void shard_runs(const ungx_cross_edge_problem &p, const Plan &plan, std::vector<std::vector<CopyRange>> &runs,
+                std::vector<uint32_t> &rows)
+{
+   const uint32_t S = p.shard_count, G = p.num_groups;
+   runs.assign(S, {});
+   rows.assign(S, 0u);
+   // (first row, rows, shard) of every item and every group without targets
+   struct Piece
+   {
+      uint32_t begin, count, shard;
+   };
+   std::vector<Piece> pieces;
+   pieces.reserve(plan.all.size() + G);
+   for (uint32_t f = 1; f <= G; ++f)
+   {
+      const uint32_t a = p.group_ranges[2 * f], b = p.group_ranges[2 * f + 1];
+      if (a == b)
+         continue;
+      if (plan.g_nseg[f] == 0)
+      {
+         pieces.push_back({a, b - a, f % S});
+         continue;
+      }
+      const uint32_t i0 = plan.g_item0[f], ni = (b - a + kRowsPerItem - 1) / kRowsPerItem;
+      for (uint32_t i = i0; i < i0 + ni; ++i)
+         pieces.push_back({plan.all[i].row_begin, plan.all[i].row_count, plan.item_shard[i]});
+   }
+   bool ascend = true;
+   for (size_t i = 1; i < pieces.size() && ascend; ++i)
+      ascend = pieces[i - 1].begin < pieces[i].begin;
+   if (!ascend)
+      std::sort(pieces.begin(), pieces.end(), [](const Piece &x, const Piece &y) { return x.begin < y.begin; });
+   for (const Piece &pc : pieces)
+   {
+      auto &r = runs[pc.shard];
+      if (!r.empty() && r.back().src_row + r.back().count == pc.begin)
+         r.back().count += pc.count;
+      else
+         r.push_back({pc.begin, rows[pc.shard], pc.count, 0});
+      rows[pc.shard] += pc.count;
+   }
 }
 
 } // namespace ungx

@@ -45,6 +45,13 @@ struct RowRange
    uint32_t begin, count;
 };
 
+// Rows [src_row, src_row+count) of a row-major n x k output go to rows
+// [dst_row, dst_row+count) of a compact buffer (a shard's rows, copied at once).
+struct CopyRange
+{
+   uint32_t src_row, dst_row, count, pad;
+};
+
 struct Plan
 {
    std::vector<WorkItem> items;       // this shard's items, longest first
@@ -60,6 +67,8 @@ struct Plan
    std::vector<uint64_t> key, item_pairs;           // per item: cost (sort key), pairs
    std::vector<uint32_t> order, order2;             // item permutation
    std::vector<uint32_t> norm_chunks;               // (group, first row, rows <= 4096) of every group
+   std::vector<uint32_t> item_shard;                // per item of `all`: its shard
+   std::vector<uint64_t> shard_load;                // per shard: its LPT cost
 };
 
 constexpr uint32_t kRowsPerItem = 128;
@@ -67,6 +76,13 @@ constexpr uint32_t kRowsPerItem = 128;
 // Validates the problem and builds this shard's plan.  Returns UNGX_OK or an error
 // status with a message in `err`.
 int build_plan(const ungx_cross_edge_problem &p, Plan &plan, std::string &err);
+
+// Every shard's rows (work items and rows without targets) in ascending row order, as
+// runs of consecutive rows: runs[s][i].src_row is the run's first row, dst_row its
+// position in shard s's compact order; rows[s] is the shard's row count.  `plan` is
+// build_plan's result for any shard of p.shard_count.
+void shard_runs(const ungx_cross_edge_problem &p, const Plan &plan, std::vector<std::vector<CopyRange>> &runs,
+                std::vector<uint32_t> &rows);
 
 } // namespace ungx
 

@@ -195,6 +195,68 @@ int ungx_cross_edges_exact_noalloc(const ungx_cross_edge_problem *problem, const
  * number.  `rows` may be NULL to query the count only. */
 int ungx_shard_rows(const ungx_cross_edge_problem *problem, uint32_t *rows, uint64_t *count);
 
+/* ---------------------------------------------- multi-GPU: one process per GPU
+ * No counterpart in the reference, which builds on one GPU.  The LNG group pairs are
+ * sharded across the GPUs of one box (each rank computes the work items of its shard,
+ * longest first, over the whole problem), the base vectors are replicated over
+ * NVLink, and rank 0 gathers every shard's rows with NCCL send / receive.  NCCL is
+ * loaded at the first of these calls (libnccl.so.2, the copy already in the process
+ * when there is one).
+ *
+ * Rank 0 makes an id with ungx_comm_id_create and hands its bytes to every rank by its
+ * own means (a file, a socket, MPI, a framework's store); every rank then calls
+ * ungx_comm_init on a context of its own GPU.  A context without a communicator runs
+ * ungx_cross_edges_build_distributed as a world of one. */
+typedef struct ungx_comm_id
+{
+   char internal[128];
+} ungx_comm_id;
+
+int ungx_comm_id_create(ungx_comm_id *id);
+int ungx_comm_init(ungx_context *ctx, const ungx_comm_id *id, int world_size, int rank);
+int ungx_comm_destroy(ungx_context *ctx);
+
+/* The rows of the reordered base matrix that rank `rank` passes from host memory:
+ * [*first, *first + *count), a balanced split of n rows over world_size ranks. */
+int ungx_dist_slice(uint32_t num_points, uint32_t world_size, uint32_t rank, uint32_t *first, uint32_t *count);
+
+enum
+{
+   UNGX_DIST_DEVICE_VECTORS = 1, /* `vectors`: the whole n x d matrix in this rank's device memory */
+   UNGX_DIST_DEVICE_OUTPUT = 2   /* rank 0's out_ids / out_dists are device pointers on its GPU */
+};
+
+typedef struct ungx_dist_timing
+{
+   ungx_cross_edge_timing cross; /* this rank's generate step (plan_ms: planning or its reuse check) */
+   double upload_ms;             /* host -> device copy of this rank's slice (device time) */
+   double replicate_ms;          /* NCCL all-gather of the slices over NVLink */
+   double prepare_ms;            /* the tensor-core operand and norms */
+   double gather_ms;             /* compaction, NCCL send / receive, scatter on rank 0 */
+   double d2h_ms;                /* rank 0: the whole output to host memory */
+   double total_ms;              /* the whole call (wall) */
+   uint64_t shard_rows;          /* rows this rank computed */
+   uint64_t shard_cost;          /* its shard's cost (the planner's padded target columns) */
+   uint64_t shard_cost_max;      /* the largest shard cost over all ranks */
+   uint64_t shard_cost_total;    /* the sum over ranks */
+   uint32_t world_size, rank;
+   uint32_t plan_reused;         /* 1: the plan of the previous call was reused (same problem arrays) */
+   uint32_t gpu_launches;        /* kernels this call launched on this rank */
+} ungx_dist_timing;
+
+/* The cross-edge build over every rank of the context's communicator; every rank calls
+ * it with the same problem (its shard fields are ignored).  `vectors`: this rank's
+ * slice of the reordered rows (ungx_dist_slice) in host memory, or with
+ * UNGX_DIST_DEVICE_VECTORS the whole matrix in device memory.  Rank 0 receives the
+ * whole output in out_ids [n*k] (required) and out_dists [n*k] (may be NULL) -- host
+ * buffers, or device buffers with UNGX_DIST_DEVICE_OUTPUT; the other ranks' outputs
+ * are ignored.  The plan is reused across calls while the problem's arrays stay the
+ * same.  A device wait that runs out aborts the communicator (UNGX_ERR_TIMEOUT); a
+ * new ungx_comm_init is then needed. */
+int ungx_cross_edges_build_distributed(ungx_context *ctx, const float *vectors, uint32_t flags,
+                                       const ungx_cross_edge_problem *problem, uint32_t *out_ids, float *out_dists,
+                                       ungx_dist_timing *timing);
+
 /* ---------------------------------------------- a16: grouping + reorder + LNG
  * build_trie_and_divide_groups (UNG/codes/src/uni_nav_graph_label_graph.cpp:21-43),
  * the reorder of prepare_group_storages_graphs (UNG/codes/src/uni_nav_graph.cpp:148-169)
