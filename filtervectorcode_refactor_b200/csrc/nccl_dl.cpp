@@ -3,6 +3,8 @@
 
 #include <dlfcn.h>
 
+#include <cstdlib>
+
 #include <mutex>
 
 namespace ungx
@@ -15,13 +17,25 @@ const NcclApi *nccl_api(std::string &err)
    static bool ok = false;
    static std::string load_err;
    std::call_once(once, [] {
-      void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
-      if (!h)
-         h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+      // UNGX_NCCL_LIBRARY names the library to use; otherwise the copy already in the
+      // process (a framework's), else libnccl.so.2 from the loader's search path
+      const char *path = std::getenv("UNGX_NCCL_LIBRARY");
+      void *h = nullptr;
+      if (path && *path)
+         h = dlopen(path, RTLD_NOW | RTLD_GLOBAL);
+      else
+      {
+         h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL | RTLD_NOLOAD);
+         if (!h)
+            h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+         if (!h)
+            h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+      }
       if (!h)
       {
          const char *e = dlerror();
-         load_err = std::string("NCCL is not loadable (libnccl.so.2): ") + (e ? e : "unknown error");
+         load_err = std::string("NCCL is not loadable (") + (path && *path ? path : "libnccl.so.2") +
+                    "): " + (e ? e : "unknown error");
          return;
       }
       bool all = true;

@@ -2,9 +2,12 @@
 //
 // libungx.so does not link NCCL: single-GPU callers never need it, and a process that
 // already loaded an NCCL (a framework's copy, say) must not get a second one.  The
-// first multi-GPU call dlopen()s "libnccl.so.2" -- which returns the copy already in
-// the process when there is one -- and resolves the functions below.  Types and
-// constants come from nccl.h; the library's own ABI never exposes them.
+// first multi-GPU call dlopen()s $UNGX_NCCL_LIBRARY when set, else the "libnccl.so.2"
+// already in the process, else "libnccl.so.2" from the loader's search path, and
+// resolves the functions below.  Only one libnccl.so.2 can live in a process: a
+// framework that brings its own (and needs its newer symbols) is loaded before the
+// first multi-GPU call.  Types and constants come from nccl.h; the library's own ABI
+// never exposes them.
 #pragma once
 
 #include <nccl.h>

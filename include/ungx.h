@@ -200,8 +200,10 @@ int ungx_shard_rows(const ungx_cross_edge_problem *problem, uint32_t *rows, uint
  * sharded across the GPUs of one box (each rank computes the work items of its shard,
  * longest first, over the whole problem), the base vectors are replicated over
  * NVLink, and rank 0 gathers every shard's rows with NCCL send / receive.  NCCL is
- * loaded at the first of these calls (libnccl.so.2, the copy already in the process
- * when there is one).
+ * loaded at the first of these calls: $UNGX_NCCL_LIBRARY when set, else the
+ * libnccl.so.2 already in the process, else libnccl.so.2 from the loader's path.  One
+ * libnccl.so.2 lives in a process, so a framework that brings its own NCCL (PyTorch,
+ * say) is loaded before that first call.
  *
  * Rank 0 makes an id with ungx_comm_id_create and hands its bytes to every rank by its
  * own means (a file, a socket, MPI, a framework's store); every rank then calls

@@ -73,6 +73,7 @@ def _rank_main(rank, world, comm_id, case, device_vectors, out_q):
     """One rank of a multi-GPU build (a spawned process with its own GPU)."""
     try:
         import numpy as np  # noqa: F811
+        import torch  # its NCCL first: the library then uses the copy already loaded
         from filtervectorcode_refactor_b200 import _native as nat  # noqa: F811
         Xr, k, ranges, off, ids_lng = case
         n, d = Xr.shape
@@ -85,7 +86,6 @@ def _rank_main(rank, world, comm_id, case, device_vectors, out_q):
         timings = []
         for _ in range(2):
             if device_vectors:
-                import torch
                 torch.cuda.set_device(rank)
                 X = torch.from_numpy(Xr).cuda()
                 torch.cuda.synchronize()
