@@ -4,6 +4,9 @@
 * ``_ref/libungref.so``        -- the reference's own leaf sources (TrieIndex, SearchQueue,
   FloatL2DistanceHandler) compiled where they lie, plus ref_harness.cpp; present
   only where the reference tree was available at build time.
+* ``_ref/libungref_knn.so``    -- the reference's GPU exact kNN seeding
+  (tagore_graph_builder.cu compiled where it lies) behind knn_ref_harness.cpp; it runs
+  on the GPU, so only GPU tests call it.
 
 Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg import this.
 """
@@ -18,6 +21,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "_build", "libungx_oracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libungref.so")
+REF_KNN_SO = os.path.join(HERE, "_ref", "libungref_knn.so")
 
 # FloatL2DistanceHandler's rounding in the reference's release build: the 8-lane
 # loop rounds mul and add separately, the tails are fused (bit 1).
@@ -282,6 +286,38 @@ class Reference(_Lib):
         pairs = self.lib.ungref_cross_exact(_p(X), n, d, k, G, _p(gf), _p(oo), _p(oi), _p(sm), num_threads,
                                             _p(ids), _p(dists))
         return ids, dists, int(pairs)
+
+
+class ReferenceKnn:
+    """The reference's own GPU exact kNN seeding: build_tagore_vamana_cuda_batch routed to
+    build_fast_exact_cuda_batch / batched_exact_knn_graph_kernel
+    (UNG/codes/src/tagore_graph_builder.cu:650-795, 1058-1340)."""
+
+    def __init__(self, path: str = REF_KNN_SO):
+        self.lib = ctypes.CDLL(path)
+        self.lib.ungref_knn_batch.restype = c_int
+        self.lib.ungref_knn_batch.argtypes = [c_void_p, c_uint32, c_uint32, c_void_p] + [c_uint32] * 7 + \
+            [c_void_p, c_void_p]
+
+    def exact_knn_graph(self, X: np.ndarray, group_ranges: np.ndarray, candidate_k: int, final_degree: int,
+                        head_keep: int, anchor_tail: int, anchor_slots: int, bidir_anchor: int, graph_stride: int):
+        """Rows [points x graph_stride] and entry points, groups = row ranges of X (their rows
+        are passed to the reference concatenated in group order)."""
+        r = np.ascontiguousarray(group_ranges, dtype=np.uint32)
+        sizes = (r[1::2].astype(np.int64) - r[0::2]).astype(np.uint32)
+        data = np.ascontiguousarray(np.concatenate([X[a:b] for a, b in zip(r[0::2], r[1::2])]), dtype=np.float32)
+        pts = int(sizes.sum())
+        graph = np.zeros((max(pts, 1), graph_stride), dtype=np.uint32)
+        entry = np.zeros(max(sizes.size, 1), dtype=np.uint32)
+        st = self.lib.ungref_knn_batch(_p(data), X.shape[1], sizes.size, _p(sizes), candidate_k, final_degree, head_keep,
+                                       anchor_tail, anchor_slots, bidir_anchor, graph_stride, _p(graph), _p(entry))
+        if st != 0:
+            raise RuntimeError(f"reference kNN batch failed with status {st}")
+        return graph[:pts], entry[:sizes.size]
+
+
+def reference_knn() -> ReferenceKnn | None:
+    return ReferenceKnn() if os.path.exists(REF_KNN_SO) else None
 
 
 def oracle() -> Oracle:

@@ -1,8 +1,14 @@
 """Exact kNN graph seeding on the device (ungx_exact_knn_graph_device) against the
-oracle restatement, bit for bit: every row (degree, local ids in the head / anchor /
-tail layout, padding) and the entry points, over group sizes from 1 to above the
-64-row block, dimensions that are and are not multiples of 4 / 32 / 128, data with
-exact duplicates (ties broken by local id), and several layout configurations."""
+reference's own GPU kernel and the oracle restatement, bit for bit: every row (degree,
+local ids in the head / anchor / tail layout, padding) and the entry points, over group
+sizes from 1 to above the 64-row block, dimensions that are and are not multiples of
+4 / 32 / 128, data with exact duplicates (ties broken by local id), and several layout
+configurations.
+
+The pin: oracle/_ref/libungref_knn.so is the reference's tagore_graph_builder.cu
+compiled where it lies (with its --use_fast_math), run through its public batch entry
+point on the exact route (batched_exact_knn_graph_kernel); the device rows must equal
+its rows, and the C restatement must too."""
 import numpy as np
 import pytest
 
@@ -70,6 +76,23 @@ def test_exact_knn_graph_matches_oracle(ctx, d, name):
     bad = np.nonzero(np.any(got != exp, axis=1))[0]
     assert bad.size == 0, f"{bad.size} rows differ; first {bad[0]}: got {got[bad[0]].tolist()} " \
                           f"expected {exp[bad[0]].tolist()}"
+    return X, ranges, cfg, got
+
+
+@pytest.mark.parametrize("d", [13, 96, 128, 200])
+@pytest.mark.parametrize("name", list(CONFIGS))
+def test_exact_knn_graph_matches_reference_kernel(ctx, d, name):
+    """The device rows and the oracle's equal the reference's own GPU kernel's rows."""
+    ref = O.reference_knn()
+    if ref is None:
+        pytest.skip("oracle/_ref/libungref_knn.so is not built (the reference tree was absent at build time)")
+    X, ranges, cfg, got = test_exact_knn_graph_matches_oracle(ctx, d, name)
+    exp, exp_entry = ref.exact_knn_graph(X, ranges, cfg.candidate_k, cfg.final_degree, cfg.head_keep,
+                                         cfg.anchor_tail, cfg.anchor_slots, cfg.bidir_anchor, cfg.graph_stride)
+    assert np.all(exp_entry == 0)
+    bad = np.nonzero(np.any(got != exp, axis=1))[0]
+    assert bad.size == 0, f"{bad.size} rows differ from the reference kernel; first {bad[0]}: " \
+                          f"got {got[bad[0]].tolist()} reference {exp[bad[0]].tolist()}"
 
 
 def test_dimension_limit_is_refused(ctx):

@@ -1,10 +1,11 @@
 """The exact kNN seeding restatement (oracle side, CPU).
 
-The reference's seeding kernel cannot be built here (its file includes an absent
-external source), so its parity is unpinned.  What can be pinned on the CPU: the
-distance order of its 128-thread block, restated independently with numpy (for
-d <= 128 every per-thread partial is one rounded square, and fp32 numpy arithmetic
-rounds like the device), and the row layout rules on small hand-checked cases."""
+The reference's seeding kernel runs only on a GPU: the GPU tests pin this restatement
+and the device path to it (tests/test_knn_gpu.py, oracle/_ref/libungref_knn.so).  What
+is checked here, on the CPU: the distance order of its 128-thread block, restated
+independently with numpy (for d <= 128 every per-thread partial is one rounded square,
+and fp32 numpy arithmetic rounds like the device), and the row layout rules on small
+hand-checked cases."""
 import numpy as np
 import pytest
 
