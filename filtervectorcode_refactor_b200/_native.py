@@ -57,10 +57,12 @@ class CrossEdgeTiming(ctypes.Structure):
         ("rows_fallback", c_uint64),
         ("route_used", c_uint32),
         ("gpu_launches", c_uint32),
+        ("passes", c_uint32),
+        ("reserved", c_uint32),
     ]
 
     def as_dict(self) -> dict:
-        return {name: getattr(self, name) for name, _ in self._fields_}
+        return {name: getattr(self, name) for name, _ in self._fields_ if name != "reserved"}
 
 
 class CrossEdgeProblem(ctypes.Structure):
@@ -172,6 +174,8 @@ _SIGNATURES = [
     ("ungx_set_timeout_ms", c_int, [c_void_p, c_uint32]),
     ("ungx_set_device_wait_limit_ns", c_int, [c_void_p, c_uint64]),
     ("ungx_set_fault_injection", c_int, [c_void_p, c_uint32]),
+    ("ungx_set_device_memory_limit", c_int, [c_void_p, c_uint64]),
+    ("ungx_resident_bytes", c_uint64, [c_uint32, c_uint32, c_uint32]),
     ("ungx_prepare_base_vectors", c_int, [c_void_p, c_void_p, c_uint32, c_uint32, c_int]),
     ("ungx_release_base_vectors", c_int, [c_void_p]),
     ("ungx_cross_edges_generate", c_int,
@@ -346,6 +350,11 @@ class Context:
     def set_device_wait_limit_ns(self, ns: int) -> None:
         check(lib.ungx_set_device_wait_limit_ns(self.h, ns), self.h)
 
+    def set_device_memory_limit(self, nbytes: int) -> None:
+        """Device budget of build(); 0 = the free device memory.  Above it, build() takes
+        the capacity path (passes over pairs of row slices)."""
+        check(lib.ungx_set_device_memory_limit(self.h, nbytes), self.h)
+
     def set_fault_injection(self, flags: int) -> None:
         check(lib.ungx_set_fault_injection(self.h, flags), self.h)
 
@@ -473,6 +482,11 @@ def cross_edges_exact_noalloc(problem: Problem, d_vectors: int, d_ids: int, d_di
                               stream: int | None = None) -> None:
     """ungx_cross_edges_exact_noalloc: device pointers in and out, no device allocation."""
     check(lib.ungx_cross_edges_exact_noalloc(ctypes.byref(problem.c), d_vectors, d_ids, d_dists, stream))
+
+
+def resident_bytes(num_points: int, dim: int, topk: int) -> int:
+    """ungx_resident_bytes: device bytes of a resident build of this size."""
+    return int(lib.ungx_resident_bytes(num_points, dim, topk))
 
 
 def comm_id_create() -> bytes:

@@ -130,6 +130,8 @@ struct ungx_context
    std::string err;
    uint32_t timeout_ms = 120000;
    uint64_t device_wait_ns = 4000000000ull;
+   uint64_t mem_limit = 0; // device budget of ungx_cross_edges_build (0: free memory)
+   DevBuf pass_x, pass_ids, pass_dists, pass_ranges; // capacity path
    uint32_t inject = UNGX_INJECT_NONE;
    PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
    // resident base vectors (a4)
@@ -539,6 +541,205 @@ int run_generate(ungx_context *ctx, const ungx_cross_edge_problem &p, const Plan
                                        " (a bounded device wait expired)");
    return UNGX_OK;
 }
+// Device bytes per point of the resident path: base vectors, tensor-core operand, norm,
+// candidate lists, outputs and fallback lists.
+uint64_t bytes_per_point(uint32_t d, uint32_t k)
+{
+   const uint64_t dp = ungx::tc_operand_cols(d);
+   const int kp = ungx::tc_candidates_for_k(k);
+   const uint64_t lists = kp ? uint64_t(ungx::kTcLists) * uint64_t(ungx::tc_list_depth(kp)) * 8u : 0u;
+   return 4ull * d + 2 * dp + 4 + lists + 8ull * k + 8;
+}
+
+// The device budget of ungx_cross_edges_build: the set limit, else the free device memory
+// plus what the context already holds (its buffers are reused by the call).
+uint64_t device_budget(ungx_context *ctx)
+{
+   if (ctx->mem_limit)
+      return ctx->mem_limit;
+   size_t fr = 0, tot = 0;
+   if (cudaMemGetInfo(&fr, &tot) != cudaSuccess)
+   {
+      cudaGetLastError();
+      return UINT64_MAX;
+   }
+   uint64_t held = 0;
+   for (const DevBuf *b : {&ctx->X_owned, &ctx->Xh, &ctx->xnorm, &ctx->cand_key, &ctx->cand_col, &ctx->out_ids,
+                           &ctx->out_dists, &ctx->fb_rows, &ctx->fb_items, &ctx->pass_x, &ctx->pass_ids,
+                           &ctx->pass_dists})
+      held += b->bytes;
+   return uint64_t(double(fr) * 0.92) + held;
+}
+
+// The capacity path of ungx_cross_edges_build (the reference's X-side streaming,
+// UNG/codes/src/uni_nav_graph_cross_edges.cpp:402-418): rows in slices of m, one pass per
+// (source slice i, target slice j) that some LNG edge needs, two slices on the device.  A
+// pass is an ordinary generate over a sub-problem of the pass buffer (rows of slice i,
+// then those of slice j): each group's rows in slice i are a source group whose targets
+// are its LNG out-groups' rows in slice j.  Its exact per-row top-k is merged into the
+// running top-k by (distance, id), so the result equals the resident one.
+int run_passes(ungx_context *ctx, const float *vectors, const ungx_cross_edge_problem &p, uint64_t budget,
+               uint32_t *out_ids, float *out_dists, ungx_cross_edge_timing &t)
+{
+   const uint32_t n = p.num_points, d = p.dim, k = p.topk, G = p.num_groups;
+   if (k > ungx::kMergeMaxK)
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "capacity path supports k <= " + std::to_string(ungx::kMergeMaxK));
+   const uint64_t per = bytes_per_point(d, k);
+   const uint64_t fixed = uint64_t(n) * k * 8 + (uint64_t(64) << 20);
+   const uint64_t m64 = budget > fixed ? (budget - fixed) / (2 * per) : 0;
+   if (m64 < 256)
+      return fail(ctx, UNGX_ERR_OOM,
+                  "device memory budget of " + std::to_string(budget) + " bytes holds less than two slices of 256 rows");
+   const uint32_t m = uint32_t(std::min<uint64_t>(m64, n));
+   const uint32_t S = (n + m - 1) / m;
+   cudaStream_t s = ctx->stream;
+   const size_t nk = size_t(n) * k;
+   UNGX_CUDA(ctx, ctx->out_ids.ensure(nk * sizeof(uint32_t)), "output allocation");
+   UNGX_CUDA(ctx, ctx->out_dists.ensure(nk * sizeof(float)), "output allocation");
+   UNGX_CUDA(ctx, ctx->pass_x.ensure(size_t(2) * m * d * sizeof(float)), "pass buffer");
+   UNGX_CUDA(ctx, ctx->pass_ids.ensure(size_t(2) * m * k * sizeof(uint32_t)), "pass outputs");
+   UNGX_CUDA(ctx, ctx->pass_dists.ensure(size_t(2) * m * k * sizeof(float)), "pass outputs");
+   uint32_t *g_ids = ctx->out_ids.as<uint32_t>(), *p_ids = ctx->pass_ids.as<uint32_t>();
+   float *g_d = ctx->out_dists.as<float>(), *p_d = ctx->pass_dists.as<float>();
+   float *X = ctx->pass_x.as<float>();
+   // sentinel rows: the running result [0, n) once, the pass outputs [0, 2m) before each pass
+   std::vector<ungx::RowRange> fill;
+   for (uint32_t r = 0; r < n; r += 65536)
+      fill.push_back({r, std::min<uint32_t>(65536, n - r)});
+   const uint32_t n_global_ranges = uint32_t(fill.size());
+   for (uint32_t r = 0; r < 2 * m; r += 65536)
+      fill.push_back({r, std::min<uint32_t>(65536, 2 * m - r)});
+   const uint32_t n_pass_ranges = uint32_t(fill.size()) - n_global_ranges;
+   int st;
+   if ((st = upload(ctx, ctx->pass_ranges, fill, "fill ranges")))
+      return st;
+   const ungx::RowRange *d_fill = ctx->pass_ranges.as<ungx::RowRange>();
+   UNGX_CUDA(ctx, ungx::launch_fill_empty(d_fill, n_global_ranges, k, g_ids, g_d, s), "fill kernel");
+   const uint32_t *R = p.group_ranges;
+   const uint64_t *OO = p.lng_out_offsets;
+   const uint32_t *OI = p.lng_out_ids;
+   auto overlaps = [&](uint32_t g, uint32_t a, uint32_t b) { return R[2 * g] < b && R[2 * g + 1] > a && R[2 * g] < R[2 * g + 1]; };
+   std::vector<uint32_t> tgt_id(size_t(G) + 1, 0u);
+   std::vector<uint8_t> need(S);
+   t.passes = 0;
+   for (uint32_t i = 0; i < S; ++i)
+   {
+      const uint32_t si = i * m, ei = std::min(n, si + m), ni = ei - si;
+      std::vector<uint32_t> src_groups;
+      std::fill(need.begin(), need.end(), uint8_t(0));
+      for (uint32_t g = 1; g <= G; ++g)
+         if (overlaps(g, si, ei))
+         {
+            src_groups.push_back(g);
+            if (p.skip_source_group && p.skip_source_group[g])
+               continue;
+            for (uint64_t e = OO[g]; e < OO[g + 1]; ++e)
+            {
+               const uint32_t ta = R[2 * OI[e]], tb = R[2 * OI[e] + 1];
+               if (ta < tb)
+                  for (uint32_t j = ta / m; j <= (tb - 1) / m; ++j)
+                     need[j] = 1;
+            }
+         }
+      if ((st = upload_vectors(ctx, X, vectors + size_t(si) * d, size_t(ni) * d * sizeof(float))))
+         return st;
+      for (uint32_t j = 0; j < S; ++j)
+      {
+         if (!need[j])
+            continue;
+         const uint32_t sj = j * m, ej = std::min(n, sj + m), nj = ej - sj;
+         const uint32_t nbuf = j == i ? ni : ni + nj;
+         if (j != i && (st = upload_vectors(ctx, X + size_t(ni) * d, vectors + size_t(sj) * d,
+                                            size_t(nj) * d * sizeof(float))))
+            return st;
+         // the pass's sub-problem over the buffer rows
+         std::vector<uint32_t> ranges(2, 0u), ids;
+         std::vector<uint64_t> off(1, 0u);
+         auto piece = [&](uint32_t g, uint32_t a, uint32_t b, uint32_t base) {
+            ranges.push_back(base + std::max(R[2 * g], a) - a);
+            ranges.push_back(base + std::min(R[2 * g + 1], b) - a);
+         };
+         std::vector<uint32_t> tgt_groups;
+         if (j == i)
+         {
+            for (size_t q = 0; q < src_groups.size(); ++q)
+               tgt_id[src_groups[q]] = uint32_t(q + 1);
+         }
+         else
+         {
+            for (uint32_t g = 1; g <= G; ++g)
+               if (overlaps(g, sj, ej))
+               {
+                  tgt_groups.push_back(g);
+                  tgt_id[g] = uint32_t(src_groups.size() + tgt_groups.size());
+               }
+         }
+         for (uint32_t g : src_groups)
+         {
+            piece(g, si, ei, 0);
+            off.push_back(ids.size());
+            if (!(p.skip_source_group && p.skip_source_group[g]))
+               for (uint64_t e = OO[g]; e < OO[g + 1]; ++e)
+                  if (tgt_id[OI[e]])
+                     ids.push_back(tgt_id[OI[e]]);
+         }
+         for (uint32_t g : tgt_groups)
+         {
+            piece(g, sj, ej, ni);
+            off.push_back(ids.size());
+         }
+         off.push_back(ids.size()); // off[q] = first out id of group q (1..), off[0] = 0
+         for (uint32_t g : src_groups)
+            tgt_id[g] = 0;
+         for (uint32_t g : tgt_groups)
+            tgt_id[g] = 0;
+         ungx_cross_edge_problem sub{};
+         sub.num_points = nbuf;
+         sub.dim = d;
+         sub.topk = k;
+         sub.num_groups = uint32_t(src_groups.size() + tgt_groups.size());
+         sub.group_ranges = ranges.data();
+         sub.lng_out_offsets = off.data();
+         sub.lng_out_ids = ids.empty() ? nullptr : ids.data();
+         sub.route = p.route;
+         sub.shard_rank = 0;
+         sub.shard_count = 1;
+         if ((st = ungx_prepare_base_vectors(ctx, X, nbuf, d, 1)))
+            return st;
+         bool reused = false;
+         std::string err;
+         if ((st = ensure_plan(ctx, sub, reused, err)))
+            return fail(ctx, st, "capacity pass: " + err);
+         UNGX_CUDA(ctx, ungx::launch_fill_empty(d_fill + n_global_ranges, n_pass_ranges, k, p_ids, p_d, s),
+                   "fill kernel");
+         ungx_cross_edge_timing tp{};
+         if ((st = run_generate(ctx, sub, ctx->plan, p_ids, p_d, s, tp)))
+            return st;
+         UNGX_CUDA(ctx, ungx::launch_merge_pass(p_ids, p_d, ni, k, si, ni, j == i ? si : sj, g_ids, g_d, s),
+                   "merge kernel");
+         t.gpu_h2d_ms += tp.gpu_h2d_ms;
+         t.gpu_kernel_ms += tp.gpu_kernel_ms;
+         t.tc_kernel_ms += tp.tc_kernel_ms;
+         t.rerank_ms += tp.rerank_ms;
+         t.fallback_ms += tp.fallback_ms;
+         t.rows_certified += tp.rows_certified;
+         t.rows_fallback += tp.rows_fallback;
+         t.gpu_launches += tp.gpu_launches + 3 + 2; // + the operand kernels, the fill and the merge
+         t.pairs += ctx->plan.pairs;
+         t.route_used = tp.route_used;
+         ++t.passes;
+      }
+   }
+   UNGX_CUDA(ctx, cudaMemcpyAsync(out_ids, g_ids, nk * sizeof(uint32_t), cudaMemcpyDeviceToHost, s), "output copy");
+   if (out_dists)
+      UNGX_CUDA(ctx, cudaMemcpyAsync(out_dists, g_d, nk * sizeof(float), cudaMemcpyDeviceToHost, s), "output copy");
+   UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[7], s), "event");
+   if ((st = wait_event(ctx, ctx->ev[7], "output copy")))
+      return st;
+   ctx->plan_valid = false; // the context's plan belongs to the last pass's sub-problem
+   ctx->plan_on_device = false;
+   return UNGX_OK;
+}
 } // namespace
 
 extern "C"
@@ -626,7 +827,8 @@ int ungx_context_destroy(ungx_context *ctx)
                      &ctx->add_to, &ctx->add_stats, &ctx->scan_scratch, &ctx->knn_ranges,
                      &ctx->knn_base, &ctx->knn_tasks, &ctx->knn_dist, &ctx->knn_dbase, &ctx->knn_tiles,
                      &ctx->knn_rows, &ctx->intra_off, &ctx->intra_cols, &ctx->graph_off, &ctx->graph_cols,
-                     &ctx->own_runs, &ctx->all_runs, &ctx->recv})
+                     &ctx->own_runs, &ctx->all_runs, &ctx->recv, &ctx->pass_x, &ctx->pass_ids, &ctx->pass_dists,
+                     &ctx->pass_ranges})
       b->release();
    ctx->host_stage.release();
    for (auto &ev : ctx->ev)
@@ -656,6 +858,19 @@ int ungx_set_device_wait_limit_ns(ungx_context *ctx, uint64_t limit_ns)
    if (!ctx || limit_ns == 0)
       return fail(ctx, UNGX_ERR_INVALID_ARG, "ungx_set_device_wait_limit_ns: bad argument");
    ctx->device_wait_ns = limit_ns;
+   return UNGX_OK;
+}
+
+uint64_t ungx_resident_bytes(uint32_t num_points, uint32_t dim, uint32_t topk)
+{
+   return uint64_t(num_points) * bytes_per_point(dim, topk) + (uint64_t(64) << 20);
+}
+
+int ungx_set_device_memory_limit(ungx_context *ctx, uint64_t bytes)
+{
+   if (!ctx)
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "ungx_set_device_memory_limit: null context");
+   ctx->mem_limit = bytes;
    return UNGX_OK;
 }
 
@@ -893,6 +1108,32 @@ int ungx_cross_edges_build(ungx_context *ctx, const float *vectors, const ungx_c
    if (!ctx || !problem)
       return fail(ctx, UNGX_ERR_INVALID_ARG, "null argument");
    const auto t0 = std::chrono::steady_clock::now();
+   UNGX_CUDA(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+   // the capacity path when the resident footprint exceeds the device budget
+   const ungx_cross_edge_problem &P = *problem;
+   auto passes = [&](uint64_t budget) -> int {
+      ungx_cross_edge_timing t{};
+      std::string err;
+      ungx::Plan probe; // validates the problem (sizes, ranges, group ids) before any pass
+      int st = ungx::build_plan(P, probe, err);
+      if (st)
+         return fail(ctx, st, "invalid problem: " + err);
+      if (!vectors || !out_ids)
+         return fail(ctx, UNGX_ERR_INVALID_ARG, "null vectors or output");
+      st = run_passes(ctx, vectors, P, budget, out_ids, out_dists, t);
+      ctx->have_vectors = false;
+      t.generate_ms = ms_since(t0);
+      if (timing)
+         *timing = t;
+      return st;
+   };
+   if (P.shard_count <= 1 && P.num_points && P.dim && P.topk)
+   {
+      const uint64_t need = ungx_resident_bytes(P.num_points, P.dim, P.topk);
+      const uint64_t budget = device_budget(ctx);
+      if (need > budget)
+         return passes(budget);
+   }
    // the host plans while the vectors go to the device (planning reads only the problem)
    int pst = 0;
    std::string perr;
@@ -905,6 +1146,20 @@ int ungx_cross_edges_build(ungx_context *ctx, const float *vectors, const ungx_c
    });
    int st = ungx_prepare_base_vectors(ctx, vectors, problem->num_points, problem->dim, 0);
    planner.join();
+   auto retry_on_oom = [&]() -> int {
+      // a resident attempt that ran out of device memory: free the context's large
+      // buffers and take the capacity path with what is free now
+      ctx->preplanned = nullptr;
+      cudaStreamSynchronize(ctx->stream);
+      cudaGetLastError();
+      for (DevBuf *b : {&ctx->X_owned, &ctx->Xh, &ctx->xnorm, &ctx->cand_key, &ctx->cand_col, &ctx->out_ids,
+                        &ctx->out_dists, &ctx->fb_rows, &ctx->fb_items})
+         b->release();
+      ctx->have_vectors = false;
+      return passes(device_budget(ctx));
+   };
+   if (st == UNGX_ERR_OOM && P.shard_count <= 1)
+      return retry_on_oom();
    if (st)
       return st;
    ctx->preplanned = problem;
@@ -914,6 +1169,9 @@ int ungx_cross_edges_build(ungx_context *ctx, const float *vectors, const ungx_c
    const double prep = ms_since(t0);
    ungx_cross_edge_timing t{};
    st = ungx_cross_edges_generate(ctx, problem, out_ids, out_dists, &t);
+   if (st == UNGX_ERR_OOM && P.shard_count <= 1)
+      return retry_on_oom();
+   t.passes = 1;
    // the device buffers stay allocated in the context for the next build
    ctx->have_vectors = false;
    t.prepare_ms = prep;

@@ -425,6 +425,59 @@ __global__ void scatter_rows_kernel(const CopyRange *__restrict__ ranges, uint32
    }
 }
 
+// Thread per source row of a pass (capacity path): the pass's top-k of the row (ids
+// are rows of the pass buffer) merged with the row's running top-k over the earlier
+// passes (global ids), both sorted by (distance, id); the k smallest go back to the
+// running list.  Buffer row c is global row base_src + c below split, base_tgt +
+// (c - split) from there.
+template <int KM>
+__global__ void merge_pass_kernel(const uint32_t *__restrict__ pass_ids, const float *__restrict__ pass_dists,
+                                  uint32_t rows, uint32_t k, uint32_t base_src, uint32_t split, uint32_t base_tgt,
+                                  uint32_t *__restrict__ ids, float *__restrict__ dists)
+{
+   for (uint32_t r = blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += gridDim.x * blockDim.x)
+   {
+      const uint64_t po = uint64_t(r) * k, go = uint64_t(base_src + r) * k;
+      uint32_t a = 0, b = 0;
+      uint32_t out_i[KM];
+      float out_d[KM];
+      for (uint32_t o = 0; o < k; ++o)
+      {
+         uint32_t pi = 0xFFFFFFFFu, gi = 0xFFFFFFFFu;
+         float pd = INFINITY, gd = INFINITY;
+         if (a < k && pass_ids[po + a] != 0xFFFFFFFFu)
+         {
+            const uint32_t c = pass_ids[po + a];
+            pi = c < split ? base_src + c : base_tgt + (c - split);
+            pd = pass_dists[po + a];
+         }
+         if (b < k && ids[go + b] != 0xFFFFFFFFu)
+         {
+            gi = ids[go + b];
+            gd = dists[go + b];
+         }
+         if (pi != 0xFFFFFFFFu && (gi == 0xFFFFFFFFu || pair_less(pd, pi, gd, gi)))
+         {
+            out_i[o] = pi;
+            out_d[o] = pd;
+            ++a;
+         }
+         else
+         {
+            out_i[o] = gi;
+            out_d[o] = gd;
+            if (gi != 0xFFFFFFFFu)
+               ++b;
+         }
+      }
+      for (uint32_t o = 0; o < k; ++o)
+      {
+         ids[go + o] = out_i[o];
+         dists[go + o] = out_d[o];
+      }
+   }
+}
+
 // ------------------------------------------------------------------ exact scan
 // One block (8 warps) per row: the 256 threads stride over the row's candidate
 // columns keeping a sorted top-KMAX each; every warp then emits its own top-k by k
@@ -1524,6 +1577,25 @@ cudaError_t launch_gather_rows(const CopyRange *ranges, uint32_t nranges, uint32
    if (nranges == 0)
       return cudaSuccess;
    gather_rows_kernel<<<nranges, 256, 0, s>>>(ranges, k, ids, dists, out_ids, out_dists);
+   return cudaGetLastError();
+}
+
+cudaError_t launch_merge_pass(const uint32_t *pass_ids, const float *pass_dists, uint32_t rows, uint32_t k,
+                              uint32_t base_src, uint32_t split, uint32_t base_tgt, uint32_t *ids, float *dists,
+                              cudaStream_t s)
+{
+   if (rows == 0)
+      return cudaSuccess;
+   if (k > kMergeMaxK)
+      return cudaErrorInvalidValue;
+   const uint32_t blocks = std::min<uint32_t>((rows + 255) / 256, 148 * 8);
+   if (k <= 8)
+      merge_pass_kernel<8><<<blocks, 256, 0, s>>>(pass_ids, pass_dists, rows, k, base_src, split, base_tgt, ids, dists);
+   else if (k <= 32)
+      merge_pass_kernel<32><<<blocks, 256, 0, s>>>(pass_ids, pass_dists, rows, k, base_src, split, base_tgt, ids, dists);
+   else
+      merge_pass_kernel<kMergeMaxK>
+          <<<blocks, 256, 0, s>>>(pass_ids, pass_dists, rows, k, base_src, split, base_tgt, ids, dists);
    return cudaGetLastError();
 }
 

@@ -130,6 +130,13 @@ cudaError_t launch_gather_rows(const CopyRange *ranges, uint32_t nranges, uint32
 // to rows [src_row, +count) of the n x k output.
 cudaError_t launch_scatter_rows(const CopyRange *ranges, uint32_t nranges, uint32_t k, const uint32_t *ids,
                                 const float *dists, uint32_t *out_ids, float *out_dists, cudaStream_t s);
+// Capacity path: merge a pass's per-row top-k (ids = rows of the pass buffer: [0, split)
+// are global rows base_src.., the rest base_tgt..) into the running global top-k of rows
+// base_src .. base_src + rows.  k <= kMergeMaxK.
+constexpr uint32_t kMergeMaxK = 128;
+cudaError_t launch_merge_pass(const uint32_t *pass_ids, const float *pass_dists, uint32_t rows, uint32_t k,
+                              uint32_t base_src, uint32_t split, uint32_t base_tgt, uint32_t *ids, float *dists,
+                              cudaStream_t s);
 cudaError_t launch_exact(const ExactParams &p, uint32_t grid_hint, cudaStream_t s);
 
 // ---- exact kNN graph seeding (knn.cu)

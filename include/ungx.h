@@ -74,6 +74,8 @@ typedef struct
    uint64_t rows_fallback;
    uint32_t route_used;  /* UNGX_ROUTE_TENSOR or UNGX_ROUTE_EXACT */
    uint32_t gpu_launches;/* kernels this call launched */
+   uint32_t passes;      /* 1: the whole problem resident; more: the capacity path's passes */
+   uint32_t reserved;
 } ungx_cross_edge_timing;
 
 /* The inputs UniNavGraph::build_cross_edges_generate_gpu_optimized reads
@@ -109,6 +111,13 @@ int ungx_set_timeout_ms(ungx_context *ctx, uint32_t timeout_ms);
  * runs out makes the kernel stop issuing work, drain what is in flight, free its
  * tensor memory and report UNGX_ERR_TIMEOUT; the context stays usable. */
 int ungx_set_device_wait_limit_ns(ungx_context *ctx, uint64_t limit_ns);
+/* Device memory budget (bytes) of ungx_cross_edges_build; 0 (the default) = the free
+ * device memory at the time of the call.  A problem above it takes the capacity path. */
+int ungx_set_device_memory_limit(ungx_context *ctx, uint64_t bytes);
+/* Device bytes ungx_cross_edges_build needs to hold a problem of n points resident
+ * (the estimate it compares with the budget); the capacity path needs about
+ * n*k*8 + 64 MiB plus two slices of this per-point size. */
+uint64_t ungx_resident_bytes(uint32_t num_points, uint32_t dim, uint32_t topk);
 
 /* Failure-detection test hook.  UNGX_INJECT_WITHHOLD_WORK makes the tensor-core
  * kernel's producer warp publish no work item, as if it had been lost: the MMA
@@ -160,7 +169,16 @@ int ungx_cross_edges_generate_device(ungx_context *ctx, const ungx_cross_edge_pr
 /* One call = prepare + generate with host buffers: the whole step as the
  * reference's UniNavGraph calls it.  The device buffers stay allocated in the
  * context and are reused by the next call; ungx_release_base_vectors or
- * ungx_context_destroy frees them. */
+ * ungx_context_destroy frees them.
+ *
+ * Capacity path (the reference's X-side streaming, UNG/codes/src/uni_nav_graph_cross_edges.cpp:402-418,
+ * UNG/codes/src/gpu_cross_edge_x_streaming.cuh:12-404): when the resident footprint
+ * (base vectors, tensor-core operand, norms, candidate lists, outputs) exceeds the
+ * context's device memory limit, or a resident attempt runs out of device memory, the
+ * rows are cut into slices and the call runs one pass per (source slice, target slice)
+ * holding two slices on the device; each pass's exact per-row top-k is merged into the
+ * running top-k by (distance, id), so the rows equal the resident result.
+ * timing->passes reports the number of passes (1 = resident). */
 int ungx_cross_edges_build(ungx_context *ctx, const float *vectors, const ungx_cross_edge_problem *problem,
                            uint32_t *out_ids, float *out_dists, ungx_cross_edge_timing *timing);
 

@@ -60,6 +60,11 @@ def _cfg(k, deg, head, tail, slots, bidir, stride):
 @pytest.mark.parametrize("d", [13, 96, 128, 200])
 @pytest.mark.parametrize("name", list(CONFIGS))
 def test_exact_knn_graph_matches_oracle(ctx, d, name):
+    run_against_oracle(ctx, d, name)
+
+
+def run_against_oracle(ctx, d, name):
+    """Device rows of one case, checked against the C restatement; returns the case."""
     X, ranges = make_groups(d, seed=d)
     cfg = CONFIGS[name]()
     pts = int(np.sum(ranges[1::2].astype(np.int64) - ranges[0::2]))
@@ -86,7 +91,7 @@ def test_exact_knn_graph_matches_reference_kernel(ctx, d, name):
     ref = O.reference_knn()
     if ref is None:
         pytest.skip("oracle/_ref/libungref_knn.so is not built (the reference tree was absent at build time)")
-    X, ranges, cfg, got = test_exact_knn_graph_matches_oracle(ctx, d, name)
+    X, ranges, cfg, got = run_against_oracle(ctx, d, name)
     exp, exp_entry = ref.exact_knn_graph(X, ranges, cfg.candidate_k, cfg.final_degree, cfg.head_keep,
                                          cfg.anchor_tail, cfg.anchor_slots, cfg.bidir_anchor, cfg.graph_stride)
     assert np.all(exp_entry == 0)
@@ -115,4 +120,4 @@ PATHS = {"batched": ("UNGX_KNN_BATCH_ENTRIES", "20000"), "fused": ("UNGX_KNN_DIS
 @pytest.mark.parametrize("path", list(PATHS))
 def test_exact_knn_paths_match_oracle(ctx, monkeypatch, d, name, path):
     monkeypatch.setenv(*PATHS[path])
-    test_exact_knn_graph_matches_oracle(ctx, d, name)
+    run_against_oracle(ctx, d, name)

@@ -122,3 +122,10 @@ def test_row_property_checkers_agree_and_catch_mistakes(golden):
             d2[r, k - 1] = np.inf
         with pytest.raises(AssertionError):
             check_row_properties_fast(i2.ravel(), d2.ravel(), *args, np.array([r]))
+
+
+def test_reference_knn_library_loads():
+    """The reference's GPU kNN seeding checker links completely (it runs only in GPU tests)."""
+    if not __import__("os").path.exists(O.REF_KNN_SO):
+        pytest.skip("oracle/_ref/libungref_knn.so not built on this machine")
+    assert O.reference_knn() is not None
