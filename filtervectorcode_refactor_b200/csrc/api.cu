@@ -587,9 +587,9 @@ int run_passes(ungx_context *ctx, const float *vectors, const ungx_cross_edge_pr
    const uint64_t per = bytes_per_point(d, k);
    const uint64_t fixed = uint64_t(n) * k * 8 + (uint64_t(64) << 20);
    const uint64_t m64 = budget > fixed ? (budget - fixed) / (2 * per) : 0;
-   if (m64 < 256)
+   if (m64 < 16)
       return fail(ctx, UNGX_ERR_OOM,
-                  "device memory budget of " + std::to_string(budget) + " bytes holds less than two slices of 256 rows");
+                  "device memory budget of " + std::to_string(budget) + " bytes holds less than two slices of 16 rows");
    const uint32_t m = uint32_t(std::min<uint64_t>(m64, n));
    const uint32_t S = (n + m - 1) / m;
    cudaStream_t s = ctx->stream;
