@@ -507,10 +507,18 @@ def run_graph_stages(args):
     pairs = int(np.sum(sizes[sel] * (sizes[sel] - 1)))
     cfg = nat.exact_knn_default_config(64, 32)
     d_graph = torch.empty((max(pts, 1), cfg.graph_stride), dtype=torch.int32, device="cuda")
-    for _ in range(args.warmup):
-        ctx.exact_knn_graph_device(ranges, cfg, d_graph.data_ptr())
-    knn_ms = statistics.median(ctx.exact_knn_graph_device(ranges, cfg, d_graph.data_ptr())
-                               for _ in range(max(args.steps, 1)))
+    knn = {}
+    for route_name, route in (("exact", nat.ROUTE_EXACT), ("tensor", nat.ROUTE_TENSOR)):
+        cfg.route = route
+        for _ in range(args.warmup):
+            ctx.exact_knn_graph_device(ranges, cfg, d_graph.data_ptr())
+        knn[route_name] = statistics.median(ctx.exact_knn_graph_device(ranges, cfg, d_graph.data_ptr())
+                                            for _ in range(max(args.steps, 1)))
+        if route_name == "exact":
+            exact_rows = d_graph[:pts].clone()
+    knn_rejected = ctx.knn_rejected_rows()
+    knn_equal = bool(torch.equal(exact_rows, d_graph[:pts]))
+    knn_ms = knn["tensor"]
     # CPU: the oracle restatement (the reference's seeding cannot be built) on a group sample
     rng = np.random.default_rng(0)
     order = rng.permutation(sel.size)
@@ -561,6 +569,9 @@ def run_graph_stages(args):
         "metric": "UNG graph stages after the cross edges (exact kNN seeding, additional edges, CSR emission)",
         "config": {"workload": c["name"], "n": n, "d": d, "k": k},
         "knn_seeding": {"groups": int(sel.size), "points": pts, "pairs": pairs, "ms": round(knn_ms, 3),
+                        "route": "tcgen05 fp16 self-join prefilter + the reference's distance for 96 candidates",
+                        "rows_rejected": int(knn_rejected), "exact_route_ms": round(knn["exact"], 3),
+                        "routes_equal": knn_equal,
                         "tflops_algorithmic": round(2.0 * d * pairs / (knn_ms * 1e-3) / 1e12, 3),
                         "cpu_baseline": {"kind": "port", "cores": os.cpu_count(),
                                          "sample_pairs": int(acc), "seconds": round(cpu_dt, 2),

@@ -162,6 +162,7 @@ class ExactKnnConfig(ctypes.Structure):
         ("anchor_slots", c_uint32),
         ("bidir_anchor", c_uint32),
         ("graph_stride", c_uint32),
+        ("route", c_uint32),
     ]
 
 
@@ -215,6 +216,7 @@ _SIGNATURES = [
       POINTER(CrossGroupStats)]),
     ("ungx_graph_copy", c_int, [c_void_p, c_void_p, c_void_p]),
     ("ungx_exact_knn_default_config", None, [c_uint32, c_uint32, POINTER(ExactKnnConfig)]),
+    ("ungx_exact_knn_rejected_rows", c_uint64, [c_void_p]),
     ("ungx_exact_knn_graph_device", c_int,
      [c_void_p, c_uint32, c_void_p, POINTER(ExactKnnConfig), c_void_p, c_void_p, c_void_p, POINTER(c_double)]),
 ]
@@ -460,6 +462,10 @@ class Context:
         check(lib.ungx_exact_knn_graph_device(self.h, r.size // 2, _ptr(r) if r.size else None, ctypes.byref(cfg),
                                               d_graph, d_entry_points, stream, ctypes.byref(ms)), self.h)
         return ms.value
+
+    def knn_rejected_rows(self) -> int:
+        """Rows of the last tensor-route kNN seeding that the exact kernel rewrote."""
+        return int(lib.ungx_exact_knn_rejected_rows(self.h))
 
     def graph_csr_device(self, num_points: int, topk: int, d_intra_offsets: int | None, d_intra_cols: int | None,
                          d_cross_ids: int | None, with_additional: bool, d_offsets: int, d_cols: int | None,

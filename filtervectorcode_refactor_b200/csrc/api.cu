@@ -132,6 +132,8 @@ struct ungx_context
    uint64_t device_wait_ns = 4000000000ull;
    uint64_t mem_limit = 0; // device budget of ungx_cross_edges_build (0: free memory)
    DevBuf pass_x, pass_ids, pass_dists, pass_ranges; // capacity path
+   Plan knn_plan; // tensor-core kNN seeding: items of the groups' self-joins
+   DevBuf knn_items, knn_segs, knn_chunks, knn_gmax, knn_fb, knn_cnt;
    uint32_t inject = UNGX_INJECT_NONE;
    PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
    // resident base vectors (a4)
@@ -150,6 +152,7 @@ struct ungx_context
    DevBuf g_ranges, g_out_off, g_out_ids, group_of, reach, add_items, add_segs, add_rows, add_row_items, add_pos,
        add_res, add_off, add_cols, add_qoff, add_loff, add_from, add_to, add_stats, scan_scratch, knn_ranges, knn_base,
        knn_tasks, knn_dist, knn_dbase, knn_tiles, knn_rows;
+   uint64_t knn_rejected = 0; // rows the last tensor-route kNN seeding sent to the exact kernel
    uint32_t add_n = 0;     // points of the last additional-edge build
    uint64_t add_edges = 0; // its edges
    // merged adjacency of the last ungx_build_cross_group_edges call
@@ -740,6 +743,140 @@ int run_passes(ungx_context *ctx, const float *vectors, const ungx_cross_edge_pr
    ctx->plan_on_device = false;
    return UNGX_OK;
 }
+// The tensor-core route of the exact kNN seeding: tc_kernel over the groups' self-joins
+// (items of <= 128 rows of a group, the group itself the only target, the diagonal
+// excluded; lists of 32 per column third), the rerank in the reference's distance with
+// its certificate, then the exact fused kernel for the 64-row blocks holding a rejected
+// row.  Every row is written by the rerank; the fused kernel rewrites rejected blocks.
+int run_knn_tensor(ungx_context *ctx, const std::vector<uint32_t> &ranges, uint32_t num_groups,
+                   const ungx::KnnParams &kp, cudaStream_t s, uint32_t &rejected)
+{
+   rejected = 0;
+   // the self-join problem: group g (1-based) = the caller's group g - 1, out(g) = {g}
+   std::vector<uint32_t> sr(2 * (size_t(num_groups) + 1), 0u), sid(num_groups);
+   std::vector<uint64_t> so(size_t(num_groups) + 2, 0u);
+   for (uint32_t g = 0; g < num_groups; ++g)
+   {
+      sr[2 * (g + 1)] = ranges[2 * g];
+      sr[2 * (g + 1) + 1] = ranges[2 * g + 1];
+      so[g + 1] = g;
+      sid[g] = g + 1;
+   }
+   so[num_groups + 1] = num_groups;
+   ungx_cross_edge_problem sp{};
+   sp.num_points = ctx->n;
+   sp.dim = ctx->d;
+   sp.topk = 24;
+   sp.num_groups = num_groups;
+   sp.group_ranges = sr.data();
+   sp.lng_out_offsets = so.data();
+   sp.lng_out_ids = sid.data();
+   sp.route = UNGX_ROUTE_TENSOR;
+   sp.shard_rank = 0;
+   sp.shard_count = 1;
+   std::string err;
+   ungx::Plan &plan = ctx->knn_plan;
+   int st = ungx::build_plan(sp, plan, err);
+   if (st)
+      return fail(ctx, st, "kNN plan: " + err);
+   if (plan.items.empty())
+      return UNGX_OK;
+   if ((st = upload(ctx, ctx->knn_items, plan.items, "kNN plan")) || (st = upload(ctx, ctx->knn_segs, plan.segs, "kNN plan")) ||
+       (st = upload(ctx, ctx->knn_chunks, plan.norm_chunks, "kNN plan")))
+      return st;
+   constexpr int kp_lists = 32;
+   UNGX_CUDA(ctx, ctx->knn_gmax.ensure(sizeof(float) * (size_t(num_groups) + 1)), "group norms");
+   UNGX_CUDA(ctx,
+             ungx::launch_group_maxnorm(ctx->xnorm.as<float>(), ctx->knn_chunks.as<uint32_t>(),
+                                        (uint32_t)(plan.norm_chunks.size() / 3), num_groups, ctx->knn_gmax.as<float>(), s),
+             "group norm kernel");
+   const size_t cand = size_t(ctx->n) * ungx::kTcLists * uint32_t(ungx::tc_list_depth(kp_lists));
+   UNGX_CUDA(ctx, ctx->cand_key.ensure(cand * sizeof(float)), "candidate buffer");
+   UNGX_CUDA(ctx, ctx->cand_col.ensure(cand * sizeof(uint32_t)), "candidate buffer");
+   uint64_t item_rows = 0;
+   for (const auto &it : plan.items)
+      item_rows += it.row_count;
+   UNGX_CUDA(ctx, ctx->knn_fb.ensure(2 * sizeof(uint32_t) * std::max<uint64_t>(item_rows, 1)), "fallback list");
+   UNGX_CUDA(ctx, ctx->knn_cnt.ensure(64), "counters");
+   UNGX_CUDA(ctx, cudaMemsetAsync(ctx->knn_cnt.p, 0, 64, s), "counters");
+   uint32_t *cnt = ctx->knn_cnt.as<uint32_t>(); // [0] item counter [1] fb count [2] status, [4..7] u64 x2
+   ungx::TcMaps maps;
+   if ((st = make_map(ctx, &maps.a, ctx->Xh.p, ctx->n, ctx->dp, 128)))
+      return st;
+   for (uint32_t i = 0; i < ungx::kTcBoxes; ++i)
+      if ((st = make_map(ctx, &maps.b[i], ctx->Xh.p, ctx->n, ctx->dp, 16u * (i + 1u))))
+         return st;
+   ungx::TcParams tp{};
+   tp.items = ctx->knn_items.as<ungx::WorkItem>();
+   tp.segs = ctx->knn_segs.as<ungx::Segment>();
+   tp.num_items = (uint32_t)plan.items.size();
+   tp.item_counter = cnt + 0;
+   tp.xnorm = ctx->xnorm.as<float>();
+   tp.dp = ctx->dp;
+   tp.scale = ctx->scale.as<ungx::OperandScale>();
+   tp.cand_key = ctx->cand_key.as<float>();
+   tp.cand_col = ctx->cand_col.as<uint32_t>();
+   tp.status = reinterpret_cast<int *>(cnt + 2);
+   tp.timeout_ns = ctx->device_wait_ns;
+   tp.inject = ctx->inject;
+   tp.exclude_self = 1;
+   const uint32_t grid = (uint32_t)std::min<size_t>(plan.items.size(), (size_t)ctx->num_sms);
+   UNGX_CUDA(ctx, ungx::launch_tc(maps, tp, (uint32_t)kp_lists, grid, s), "kNN tensor-core kernel launch");
+   ungx::KnnRerankParams rp{};
+   rp.p = kp;
+   rp.items = tp.items;
+   rp.segs = tp.segs;
+   rp.cand_key = tp.cand_key;
+   rp.cand_col = tp.cand_col;
+   rp.xnorm = tp.xnorm;
+   rp.group_maxn2 = ctx->knn_gmax.as<float>();
+   rp.scale = tp.scale;
+   rp.status = tp.status;
+   ungx::RerankParams cc{};
+   ungx::tc_certificate_constants(ctx->d, ctx->dp, cc);
+   rp.c1 = cc.c1;
+   rp.c2 = cc.c2;
+   rp.c3 = cc.c3;
+   rp.c4 = cc.c4;
+   rp.gd = cc.gd;
+   // the reference's block distance: one rounding in the difference, at most ceil(d/128)
+   // fused updates per partial, 7 levels of additions; flushed subnormals add at most
+   // (d + 128) 2^-126 in absolute terms
+   rp.gref = (16.0 + 2.0 * ((ctx->d + 127) / 128)) * std::ldexp(1.0, -24);
+   rp.abs_err = (double(ctx->d) + 128.0) * std::ldexp(1.0, -126) * 2.0;
+   rp.fb_rows = ctx->knn_fb.as<uint32_t>();
+   rp.fb_count = cnt + 1;
+   rp.counters = reinterpret_cast<unsigned long long *>(cnt + 4);
+   UNGX_CUDA(ctx, ungx::launch_knn_rerank(rp, (uint32_t)plan.items.size(), s), "kNN rerank launch");
+   // rejected rows: read back (count, rows), rewrite their 64-row blocks exactly
+   uint32_t hc[3] = {0, 0, 0};
+   UNGX_CUDA(ctx, cudaMemcpyAsync(hc, cnt, sizeof(hc), cudaMemcpyDeviceToHost, s), "kNN counters");
+   UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[2], s), "event");
+   if ((st = wait_event(ctx, ctx->ev[2], "kNN tensor route")))
+      return st;
+   if (hc[2] != 0)
+      return fail(ctx, (int)hc[2], "kNN tensor-core kernel reported status " + std::to_string((int)hc[2]));
+   rejected = hc[1];
+   if (rejected)
+   {
+      std::vector<uint32_t> fb(2 * size_t(rejected));
+      UNGX_CUDA(ctx, cudaMemcpy(fb.data(), ctx->knn_fb.p, fb.size() * sizeof(uint32_t), cudaMemcpyDeviceToHost),
+                "kNN fallback rows");
+      std::vector<uint64_t> keys(rejected);
+      for (uint32_t i = 0; i < rejected; ++i)
+         keys[i] = (uint64_t(fb[2 * i]) << 32) | (fb[2 * i + 1] / 64u * 64u);
+      std::sort(keys.begin(), keys.end());
+      keys.erase(std::unique(keys.begin(), keys.end()), keys.end());
+      std::vector<uint32_t> tasks;
+      for (uint64_t k2 : keys)
+         tasks.insert(tasks.end(), {uint32_t(k2 >> 32), uint32_t(k2)});
+      if ((st = upload(ctx, ctx->knn_tasks, tasks, "kNN fallback tasks")))
+         return st;
+      UNGX_CUDA(ctx, ungx::launch_exact_knn(kp, ctx->knn_tasks.as<uint32_t>(), (uint32_t)(tasks.size() / 2), s),
+                "kNN fallback kernel");
+   }
+   return UNGX_OK;
+}
 } // namespace
 
 extern "C"
@@ -828,7 +965,8 @@ int ungx_context_destroy(ungx_context *ctx)
                      &ctx->knn_base, &ctx->knn_tasks, &ctx->knn_dist, &ctx->knn_dbase, &ctx->knn_tiles,
                      &ctx->knn_rows, &ctx->intra_off, &ctx->intra_cols, &ctx->graph_off, &ctx->graph_cols,
                      &ctx->own_runs, &ctx->all_runs, &ctx->recv, &ctx->pass_x, &ctx->pass_ids, &ctx->pass_dists,
-                     &ctx->pass_ranges})
+                     &ctx->pass_ranges, &ctx->knn_items, &ctx->knn_segs, &ctx->knn_chunks, &ctx->knn_gmax,
+                     &ctx->knn_fb, &ctx->knn_cnt})
       b->release();
    ctx->host_stage.release();
    for (auto &ev : ctx->ev)
@@ -1857,8 +1995,11 @@ void ungx_exact_knn_default_config(uint32_t candidate_k, uint32_t final_degree, 
    c.anchor_slots = 0;
    c.bidir_anchor = 0;
    c.graph_stride = final_degree + 1;
+   c.route = UNGX_ROUTE_AUTO;
    *cfg = c;
 }
+
+uint64_t ungx_exact_knn_rejected_rows(const ungx_context *ctx) { return ctx ? ctx->knn_rejected : 0; }
 
 int ungx_exact_knn_graph_device(ungx_context *ctx, uint32_t num_groups, const uint32_t *group_ranges,
                                 const ungx_exact_knn_config *cfg, uint32_t *d_graph, uint32_t *d_entry_points,
@@ -1873,6 +2014,8 @@ int ungx_exact_knn_graph_device(ungx_context *ctx, uint32_t num_groups, const ui
                   "exact kNN seeding supports dim <= " + std::to_string(ungx::kKnnMaxDim));
    if (cfg->graph_stride < cfg->final_degree + 1)
       return fail(ctx, UNGX_ERR_INVALID_ARG, "graph_stride must be at least final_degree + 1");
+   if (cfg->route != UNGX_ROUTE_AUTO && cfg->route != UNGX_ROUTE_TENSOR && cfg->route != UNGX_ROUTE_EXACT)
+      return fail(ctx, UNGX_ERR_INVALID_ARG, "unknown kNN route");
    std::vector<uint32_t> ranges(group_ranges, group_ranges + 2 * size_t(num_groups));
    std::vector<uint64_t> base(num_groups);
    uint64_t rows = 0;
@@ -1923,7 +2066,16 @@ int ungx_exact_knn_graph_device(ungx_context *ctx, uint32_t num_groups, const ui
    const uint64_t dist_max_n = env_u64("UNGX_KNN_DIST_MAX_N", ungx::kKnnDistMaxN);
    const uint64_t batch_entries = std::max<uint64_t>(1, env_u64("UNGX_KNN_BATCH_ENTRIES", ungx::kKnnDistBatch));
    UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[0], s), "event");
-   if (max_n > std::min<uint64_t>(dist_max_n, ungx::kKnnDistMaxN))
+   ctx->knn_rejected = 0;
+   const uint32_t route = cfg->route == UNGX_ROUTE_AUTO ? uint32_t(UNGX_ROUTE_TENSOR) : cfg->route;
+   if (route == UNGX_ROUTE_TENSOR)
+   {
+      uint32_t rejected = 0;
+      if ((st = run_knn_tensor(ctx, ranges, num_groups, kp, s, rejected)))
+         return st;
+      ctx->knn_rejected = rejected;
+   }
+   else if (max_n > std::min<uint64_t>(dist_max_n, ungx::kKnnDistMaxN))
    {
       // fused kernel: one block per 64 rows of a group, every candidate of the group
       const size_t ntask = ungx::knn_task_count(ranges.data(), num_groups);

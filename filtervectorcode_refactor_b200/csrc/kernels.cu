@@ -1183,6 +1183,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
                // every lane inserts its passing keys; the loop runs as often as the
                // busiest lane needs, lanes without a candidate insert +inf (a no-op)
                const uint32_t cbase = x0 + j * 32u;
+               if (p.exclude_self) // self-join: the row's own column never passes
+               {
+                  const uint32_t off = w.row_begin + r - cbase;
+                  if (off < 32u)
+                     mask &= ~(0x80000000u >> off);
+               }
                while (__any_sync(0xffffffffu, mask != 0u))
                {
                   const uint32_t jj = mask ? uint32_t(__clz(mask)) : 0u;

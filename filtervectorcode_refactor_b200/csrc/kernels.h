@@ -57,6 +57,7 @@ struct TcParams
    int *status;              // 0 or a UNGX_ERR_* code
    unsigned long long timeout_ns;
    uint32_t inject;          // UNGX_INJECT_* test hook
+   uint32_t exclude_self;    // 1: a row never takes its own column (self-join of a group)
 };
 
 // Exact rerank + certificate of the candidates.
@@ -166,6 +167,30 @@ cudaError_t launch_exact_knn(const KnnParams &p, const uint32_t *d_tasks, uint32
 // 64 x 64; rows [2 * num_rows] = (group, first row) of 32-row pieces.
 cudaError_t launch_knn_two_phase(const KnnParams &p, const uint32_t *d_tiles, uint32_t num_tiles,
                                  const uint32_t *d_rows, uint32_t num_rows, cudaStream_t s);
+
+// Tensor-core route of the seeding: tc_kernel (lists of 32 per column third, the
+// diagonal excluded) over a plan whose items are 128-row blocks of each group with the
+// group itself as the only target; then this rerank, a block per item: each row's 96
+// list entries get the reference's distance, the cand smallest by (distance, local id)
+// are laid out, and the certificate decides whether a column outside the lists could
+// have entered (then the row is queued in fb_rows for the exact kernel).
+struct KnnRerankParams
+{
+   KnnParams p;              // layout, output rows, group ranges (groups 0-based)
+   const WorkItem *items;    // the tensor-core plan's items; segment group id = group + 1
+   const Segment *segs;
+   const float *cand_key;    // [row][3][32] (global rows of X)
+   const uint32_t *cand_col;
+   const float *xnorm;
+   const float *group_maxn2; // [groups + 1], index = group + 1
+   const OperandScale *scale;
+   const int *status;        // the prefilter's status word: non-zero = nothing to do
+   double c1, c2, c3, c4, gd, gref, abs_err;
+   uint32_t *fb_rows;        // rows the certificate rejected: (group, local row) pairs
+   uint32_t *fb_count;
+   unsigned long long *counters; // [0] certified rows, [1] rejected rows
+};
+cudaError_t launch_knn_rerank(const KnnRerankParams &p, uint32_t num_items, cudaStream_t s);
 
 // ---- graph assembly (graph.cu)
 // group_of[v] = group of row v (1..G), G + 1 for rows outside every group.

@@ -771,7 +771,200 @@ __global__ void __launch_bounds__(kRowWarps * 32) knn_rows_kernel(const KnnParam
       write_row(p, task.group, n, task.row0 + lane, cand, s_top[warp][lane]);
 }
 
+// ------------------------------------------------------------------ tensor-core route
+// The reference's distance of one (a, b) pair evaluated by one thread: the partial of
+// block thread t is the fma chain over dims t, t + 128, ... (zero past d), each warp of
+// 32 partials is reduced by the __shfl_down tree (offsets 16 .. 1), and the warp sums
+// are added as (w0 + w2) + (w1 + w3); every operation flushes subnormals.  `a` is in
+// shared memory (the row of the warp), `b` in global memory.
+__device__ float block_l2_thread(const float *__restrict__ a, const float *__restrict__ b, uint32_t d)
+{
+   float w[4];
+#pragma unroll 1
+   for (int j = 0; j < 4; ++j)
+   {
+      float v[32];
+#pragma unroll
+      for (int l = 0; l < 32; ++l)
+      {
+         float acc = 0.0f;
+         for (uint32_t dim = uint32_t(32 * j + l); dim < d; dim += 128)
+         {
+            const float diff = sub_ftz(a[dim], __ldg(b + dim));
+            acc = fma_ftz(diff, diff, acc);
+         }
+         v[l] = acc;
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+         for (int i = 0; i < off; ++i)
+            v[i] = add_ftz(v[i], v[i + off]);
+      w[j] = v[0];
+   }
+   return add_ftz(add_ftz(w[0], w[2]), add_ftz(w[1], w[3]));
+}
+
+constexpr int kRrWarps = 4;         // a block per work item: 4 warps x 32 rows
+constexpr int kRrLists = 3;         // the prefilter's lists per row (column thirds)
+constexpr int kRrDepth = 32;        // entries per list
+constexpr int kRrEntries = kRrLists * kRrDepth;
+constexpr int kRrMaxDim = 352;      // shared-memory row of each warp
+
+// A block per work item (<= 128 rows of one group); warp w ranks rows 32 w .. 32 w + 31
+// one after the other, then every lane lays out one of them.  Per row: the 96 list
+// entries (lane l: l, l + 32, l + 64) get the reference's distance; the cand smallest by
+// (distance, local id) below FLT_MAX are the row's list (the reference's strict-<
+// inserts in ascending id from FLT_MAX keep exactly those).  Certificate: every column
+// outside the lists has a prefilter key >= T, the smallest last key of a full list, so
+// its reference distance is at least ((|a|^2 + T - bound)(1 - gref) - abs_err); when that
+// exceeds the cand-th distance no such column can enter.  A row whose lists are all
+// short saw every column.  Rejected rows are queued for the exact kernel.
+__global__ void __launch_bounds__(kRrWarps * 32) knn_rerank_kernel(const KnnRerankParams rp)
+{
+   __shared__ uint32_t s_top[kRrWarps][32][kKnnMax];
+   __shared__ float s_a[kRrWarps][kRrMaxDim];
+   if (*reinterpret_cast<const volatile int *>(rp.status) != 0)
+      return; // an aborted prefilter left the lists unwritten
+   const KnnParams &p = rp.p;
+   const WorkItem w = rp.items[blockIdx.x];
+   const Segment sg = rp.segs[w.seg_begin];
+   const uint32_t group = sg.group_id - 1u;
+   const uint32_t first = p.ranges[2 * group], n = p.ranges[2 * group + 1] - first;
+   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+   uint32_t cand = p.candidate_k > 0 ? p.candidate_k - 1 : 0;
+   cand = min(cand, uint32_t(kKnnMax));
+   cand = min(cand, n > 0 ? n - 1 : 0u);
+   if (w.row_begin == first && threadIdx.x == 0 && p.entry_points)
+      p.entry_points[group] = 0;
+   const double pk = 1.0 / 131072.0; // packed-key tolerance, 2^-17 relative
+   const double bmax = sqrt((double)rp.group_maxn2[sg.group_id] * (1.0 + rp.gd));
+   const double inv_s = (double)rp.scale->inv_s;
+   const bool exact_only = rp.scale->exact_only != 0;
+   uint32_t n_cert = 0, n_fail = 0;
+   const uint32_t r0 = warp * 32u;
+   for (uint32_t rr = 0; rr < 32u && r0 + rr < w.row_count; ++rr)
+   {
+      const uint32_t row = w.row_begin + r0 + rr; // global row of X
+      const uint32_t s = row - first;             // local row
+      __syncwarp();
+      for (uint32_t dim = lane; dim < p.d; dim += 32)
+         s_a[warp][dim] = p.X[size_t(row) * p.d + dim];
+      __syncwarp();
+      const float *kp = rp.cand_key + size_t(row) * kRrEntries;
+      const uint32_t *cp = rp.cand_col + size_t(row) * kRrEntries;
+      float D[kRrLists];
+      uint32_t id[kRrLists];
+      float T = INFINITY; // smallest last key of a full list
+#pragma unroll
+      for (int e = 0; e < kRrLists; ++e)
+      {
+         const uint32_t c = cp[lane + 32u * e];
+         id[e] = 0xFFFFFFFFu;
+         D[e] = INFINITY;
+         if (c < p.ranges[2 * group + 1] && c >= first && c != row)
+         {
+            const float dd = block_l2_thread(s_a[warp], p.X + size_t(c) * p.d, p.d);
+            if (dd < FLT_MAX)
+            {
+               D[e] = dd;
+               id[e] = c - first;
+            }
+         }
+         // list e ends at entry 32 e + 31 (lane 31): full when that slot holds a column
+         const uint32_t last_c = __shfl_sync(0xffffffffu, c, 31);
+         const float last_k = __shfl_sync(0xffffffffu, kp[lane + 32u * e], 31);
+         if (last_c != 0xFFFFFFFFu)
+            T = fminf(T, last_k);
+      }
+      // rank of each entry by (distance, local id); empty entries (+inf, UINT32_MAX) last
+      uint32_t rk[kRrLists] = {0u, 0u, 0u};
+#pragma unroll 1
+      for (int src = 0; src < 32; ++src)
+#pragma unroll
+         for (int f = 0; f < kRrLists; ++f)
+         {
+            const float d2 = __shfl_sync(0xffffffffu, D[f], src);
+            const uint32_t i2 = __shfl_sync(0xffffffffu, id[f], src);
+#pragma unroll
+            for (int e = 0; e < kRrLists; ++e)
+               rk[e] += pair_less_knn(d2, i2, D[e], id[e]) ? 1u : 0u;
+         }
+      uint32_t nvalid = 0, have_k = 0;
+      float dk = INFINITY;
+#pragma unroll
+      for (int e = 0; e < kRrLists; ++e)
+      {
+         const bool valid = id[e] != 0xFFFFFFFFu;
+         nvalid += __popc(__ballot_sync(0xffffffffu, valid));
+         if (valid && rk[e] < cand)
+            s_top[warp][rr][rk[e]] = id[e];
+         const uint32_t at = __ballot_sync(0xffffffffu, valid && cand > 0 && rk[e] == cand - 1u);
+         if (at)
+         {
+            have_k = 1;
+            dk = __shfl_sync(0xffffffffu, D[e], __ffs(at) - 1);
+         }
+      }
+      for (uint32_t q = nvalid + lane; q < cand; q += 32)
+         s_top[warp][rr][q] = 0xFFFFFFFFu; // the reference's unfilled list slots
+      // certificate (warp-uniform)
+      bool cert;
+      if (cand == 0)
+         cert = true; // nothing to rank
+      else if (exact_only)
+         cert = false; // keys of data outside the fp16 operand's range prove nothing
+      else if (T == INFINITY)
+         cert = true; // no list filled up, so none dropped a column: every column was ranked
+      else if (!have_k)
+         cert = false;
+      else
+      {
+         const double qn = (double)__ldg(rp.xnorm + row);
+         const double ahi = sqrt(qn * (1.0 + rp.gd));
+         const double bound = (rp.c1 * ahi * bmax + rp.c2 * bmax * bmax + rp.c3 * inv_s * (ahi + bmax) +
+                               rp.c4 * inv_s * inv_s) *
+                              (1.0 + 1.0 / 1024.0);
+         const double Tp = (double)T - fabs((double)T) * pk;
+         const double lhs = (qn * (1.0 - rp.gd) + Tp - bound) * (1.0 - rp.gref) - rp.abs_err;
+         cert = lhs > (double)dk;
+      }
+      if (lane == 0)
+      {
+         if (cert)
+            ++n_cert;
+         else
+         {
+            const uint32_t pos = atomicAdd(rp.fb_count, 1u);
+            rp.fb_rows[2 * pos] = group;
+            rp.fb_rows[2 * pos + 1] = s;
+            ++n_fail;
+         }
+      }
+   }
+   __syncwarp();
+   if (r0 + lane < w.row_count)
+      write_row(p, group, n, w.row_begin + r0 + lane - first, cand, s_top[warp][lane]);
+   if (lane == 0)
+   {
+      if (n_cert)
+         atomicAdd(&rp.counters[0], (unsigned long long)n_cert);
+      if (n_fail)
+         atomicAdd(&rp.counters[1], (unsigned long long)n_fail);
+   }
+}
+
 } // namespace
+
+cudaError_t launch_knn_rerank(const KnnRerankParams &p, uint32_t num_items, cudaStream_t s)
+{
+   if (num_items == 0)
+      return cudaSuccess;
+   if (p.p.d > uint32_t(kRrMaxDim))
+      return cudaErrorInvalidValue;
+   knn_rerank_kernel<<<num_items, kRrWarps * 32, 0, s>>>(p);
+   return cudaGetLastError();
+}
 
 size_t knn_smem_bytes(uint32_t d)
 {

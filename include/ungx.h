@@ -422,10 +422,19 @@ typedef struct ungx_exact_knn_config
    uint32_t anchor_slots; /* 0: all remaining slots */
    uint32_t bidir_anchor; /* 1: every second anchor walks backwards */
    uint32_t graph_stride; /* row length in uint32, at least final_degree + 1 */
+   uint32_t route;        /* UNGX_ROUTE_TENSOR (AUTO): tcgen05 fp16 prefilter of each group's
+                             self-join keeping 96 candidates per point, the reference's
+                             distance for those, a certificate that no other point could
+                             enter, the exact kernel for the 64-row blocks it rejects;
+                             UNGX_ROUTE_EXACT: the reference's distance for every pair */
 } ungx_exact_knn_config;
 
-/* The reference's defaults for K and a degree (environment overrides not read). */
+/* The reference's defaults for K and a degree (environment overrides not read);
+ * route UNGX_ROUTE_AUTO. */
 void ungx_exact_knn_default_config(uint32_t candidate_k, uint32_t final_degree, ungx_exact_knn_config *cfg);
+/* Rows of the last ungx_exact_knn_graph_device call (tensor route) whose certificate
+ * failed, rewritten by the exact kernel. */
+uint64_t ungx_exact_knn_rejected_rows(const ungx_context *ctx);
 
 /* Groups g = 0 .. num_groups-1 are rows [group_ranges[2g], group_ranges[2g+1]) of the
  * base vectors of ungx_prepare_base_vectors (any dim up to 352).  d_graph (device):

@@ -57,21 +57,28 @@ def _cfg(k, deg, head, tail, slots, bidir, stride):
     return c
 
 
+ROUTES = {"tensor": nat.ROUTE_TENSOR, "exact": nat.ROUTE_EXACT}
+
+
 @pytest.mark.parametrize("d", [13, 96, 128, 200])
 @pytest.mark.parametrize("name", list(CONFIGS))
-def test_exact_knn_graph_matches_oracle(ctx, d, name):
-    run_against_oracle(ctx, d, name)
+@pytest.mark.parametrize("route", list(ROUTES))
+def test_exact_knn_graph_matches_oracle(ctx, d, name, route):
+    run_against_oracle(ctx, d, name, ROUTES[route])
 
 
-def run_against_oracle(ctx, d, name):
+def run_against_oracle(ctx, d, name, route=nat.ROUTE_AUTO):
     """Device rows of one case, checked against the C restatement; returns the case."""
     X, ranges = make_groups(d, seed=d)
     cfg = CONFIGS[name]()
+    cfg.route = route
     pts = int(np.sum(ranges[1::2].astype(np.int64) - ranges[0::2]))
     ctx.prepare_base_vectors(X, X.shape[0], d, on_device=False)
     d_graph = torch.full((pts, cfg.graph_stride), 7, dtype=torch.int32, device="cuda")
     d_entry = torch.full((ranges.size // 2,), 9, dtype=torch.int32, device="cuda")
     ctx.exact_knn_graph_device(ranges, cfg, d_graph.data_ptr(), d_entry.data_ptr())
+    if route == nat.ROUTE_TENSOR:
+        print(f"kNN tensor route d={d} {name}: {ctx.knn_rejected_rows()} rows rejected")
     ctx.release_base_vectors()
     got = d_graph.cpu().numpy().view(np.uint32)
     exp, exp_entry = O.oracle().exact_knn_graph(X, ranges, cfg.candidate_k, cfg.final_degree, cfg.head_keep,
@@ -86,12 +93,13 @@ def run_against_oracle(ctx, d, name):
 
 @pytest.mark.parametrize("d", [13, 96, 128, 200])
 @pytest.mark.parametrize("name", list(CONFIGS))
-def test_exact_knn_graph_matches_reference_kernel(ctx, d, name):
-    """The device rows and the oracle's equal the reference's own GPU kernel's rows."""
+@pytest.mark.parametrize("route", list(ROUTES))
+def test_exact_knn_graph_matches_reference_kernel(ctx, d, name, route):
+    """The device rows (both routes) and the oracle's equal the reference's own GPU kernel's rows."""
     ref = O.reference_knn()
     if ref is None:
         pytest.skip("oracle/_ref/libungref_knn.so is not built (the reference tree was absent at build time)")
-    X, ranges, cfg, got = run_against_oracle(ctx, d, name)
+    X, ranges, cfg, got = run_against_oracle(ctx, d, name, ROUTES[route])
     exp, exp_entry = ref.exact_knn_graph(X, ranges, cfg.candidate_k, cfg.final_degree, cfg.head_keep,
                                          cfg.anchor_tail, cfg.anchor_slots, cfg.bidir_anchor, cfg.graph_stride)
     assert np.all(exp_entry == 0)
@@ -120,4 +128,32 @@ PATHS = {"batched": ("UNGX_KNN_BATCH_ENTRIES", "20000"), "fused": ("UNGX_KNN_DIS
 @pytest.mark.parametrize("path", list(PATHS))
 def test_exact_knn_paths_match_oracle(ctx, monkeypatch, d, name, path):
     monkeypatch.setenv(*PATHS[path])
-    run_against_oracle(ctx, d, name)
+    run_against_oracle(ctx, d, name, nat.ROUTE_EXACT)
+
+
+@pytest.mark.parametrize("d", [64, 128])
+def test_tensor_route_large_groups_match_oracle(ctx, d):
+    """Groups of 2,000 and 9,000 points (above the exact route's matrix limit) on the tensor
+    route: rows equal the oracle's; the certificate clears nearly every row."""
+    rng = np.random.default_rng(77 + d)
+    sizes = [2000, 9000, 300]
+    X = rng.standard_normal((sum(sizes), d)).astype(np.float32)
+    X /= np.linalg.norm(X, axis=1, keepdims=True)
+    ranges, at = [], 0
+    for sz in sizes:
+        ranges += [at, at + sz]
+        at += sz
+    ranges = np.array(ranges, dtype=np.uint32)
+    cfg = nat.exact_knn_default_config(64, 32)
+    pts = X.shape[0]
+    ctx.prepare_base_vectors(X, pts, d, on_device=False)
+    d_graph = torch.zeros((pts, cfg.graph_stride), dtype=torch.int32, device="cuda")
+    ctx.exact_knn_graph_device(ranges, cfg, d_graph.data_ptr())
+    rejected = ctx.knn_rejected_rows()
+    ctx.release_base_vectors()
+    got = d_graph.cpu().numpy().view(np.uint32)
+    exp, _ = O.oracle().exact_knn_graph(X, ranges, cfg.candidate_k, cfg.final_degree, cfg.head_keep,
+                                        cfg.anchor_tail, cfg.anchor_slots, cfg.bidir_anchor, cfg.graph_stride)
+    bad = np.nonzero(np.any(got != exp, axis=1))[0]
+    assert bad.size == 0, f"{bad.size} rows differ; first {bad[0]}"
+    assert rejected <= 0.01 * pts
