@@ -841,6 +841,16 @@ __global__ void __launch_bounds__(kRrWarps * 32) knn_rerank_kernel(const KnnRera
    const double bmax = sqrt((double)rp.group_maxn2[sg.group_id] * (1.0 + rp.gd));
    const double inv_s = (double)rp.scale->inv_s;
    const bool exact_only = rp.scale->exact_only != 0;
+   // columns each list saw: the group's columns in tiles of 192 from its first row, chunks
+   // of 32; list h takes chunks h and h + 3 of every tile (the row itself is excluded)
+   uint32_t seen[kRrLists] = {0u, 0u, 0u};
+   for (uint32_t t0 = 0; t0 < n; t0 += 192u)
+#pragma unroll
+      for (uint32_t c = 0; c < 6u; ++c)
+      {
+         const uint32_t a = t0 + 32u * c;
+         seen[c % 3u] += a < n ? min(32u, n - a) : 0u;
+      }
    uint32_t n_cert = 0, n_fail = 0;
    const uint32_t r0 = warp * 32u;
    for (uint32_t rr = 0; rr < 32u && r0 + rr < w.row_count; ++rr)
@@ -855,7 +865,8 @@ __global__ void __launch_bounds__(kRrWarps * 32) knn_rerank_kernel(const KnnRera
       const uint32_t *cp = rp.cand_col + size_t(row) * kRrEntries;
       float D[kRrLists];
       uint32_t id[kRrLists];
-      float T = INFINITY; // smallest last key of a full list
+      float T = INFINITY; // smallest last key of a list that dropped a column
+      const uint32_t self_list = ((s % 192u) / 32u) % 3u;
 #pragma unroll
       for (int e = 0; e < kRrLists; ++e)
       {
@@ -871,10 +882,10 @@ __global__ void __launch_bounds__(kRrWarps * 32) knn_rerank_kernel(const KnnRera
                id[e] = c - first;
             }
          }
-         // list e ends at entry 32 e + 31 (lane 31): full when that slot holds a column
-         const uint32_t last_c = __shfl_sync(0xffffffffu, c, 31);
+         // list e (entries 32 e .. 32 e + 31, ascending keys) dropped a column only when it
+         // saw more than 32 (every column it dropped has a key >= its last one)
          const float last_k = __shfl_sync(0xffffffffu, kp[lane + 32u * e], 31);
-         if (last_c != 0xFFFFFFFFu)
+         if (seen[e] - (uint32_t(e) == self_list ? 1u : 0u) > uint32_t(kRrDepth))
             T = fminf(T, last_k);
       }
       // rank of each entry by (distance, local id); empty entries (+inf, UINT32_MAX) last
@@ -915,7 +926,7 @@ __global__ void __launch_bounds__(kRrWarps * 32) knn_rerank_kernel(const KnnRera
       else if (exact_only)
          cert = false; // keys of data outside the fp16 operand's range prove nothing
       else if (T == INFINITY)
-         cert = true; // no list filled up, so none dropped a column: every column was ranked
+         cert = true; // no list dropped a column: every column was ranked
       else if (!have_k)
          cert = false;
       else
