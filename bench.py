@@ -519,6 +519,20 @@ def run_graph_stages(args):
     knn_rejected = ctx.knn_rejected_rows()
     knn_equal = bool(torch.equal(exact_rows, d_graph[:pts]))
     knn_ms = knn["tensor"]
+    del exact_rows
+    # every group above 64 points, the largest included (the role the reference gives to
+    # GNN descent above its exact-batch size): the tensor route, exact and certified
+    big = np.nonzero(sizes > 64)[0]
+    big_ranges = gr[big].astype(np.uint32).ravel()
+    big_pts = int(sizes[big].sum())
+    big_pairs = int(np.sum(sizes[big] * (sizes[big] - 1)))
+    cfg.route = nat.ROUTE_TENSOR
+    g_big = torch.empty((max(big_pts, 1), cfg.graph_stride), dtype=torch.int32, device="cuda")
+    ctx.exact_knn_graph_device(big_ranges, cfg, g_big.data_ptr())
+    big_ms = statistics.median(ctx.exact_knn_graph_device(big_ranges, cfg, g_big.data_ptr())
+                               for _ in range(max(min(args.steps, 3), 1)))
+    big_rejected = ctx.knn_rejected_rows()
+    del g_big
     # CPU: the oracle restatement (the reference's seeding cannot be built) on a group sample
     rng = np.random.default_rng(0)
     order = rng.permutation(sel.size)
@@ -576,6 +590,10 @@ def run_graph_stages(args):
                         "cpu_baseline": {"kind": "port", "cores": os.cpu_count(),
                                          "sample_pairs": int(acc), "seconds": round(cpu_dt, 2),
                                          "tflops": round(2.0 * d * acc / cpu_dt / 1e12, 4)}},
+        "knn_seeding_all_groups": {"groups": int(big.size), "points": big_pts, "pairs": big_pairs,
+                                   "largest_group": int(sizes[big].max()) if big.size else 0,
+                                   "ms": round(big_ms, 3), "rows_rejected": int(big_rejected),
+                                   "tflops_algorithmic": round(2.0 * d * big_pairs / (big_ms * 1e-3) / 1e12, 3)},
         "additional_edges": {"missing_group_edges": int(add.missing_group_edges),
                              "query_vectors": int(add.query_vectors), "edges": int(add.edges),
                              "ms_wall": round(add.ms, 3)},

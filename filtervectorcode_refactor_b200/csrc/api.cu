@@ -746,8 +746,8 @@ int run_passes(ungx_context *ctx, const float *vectors, const ungx_cross_edge_pr
 // The tensor-core route of the exact kNN seeding: tc_kernel over the groups' self-joins
 // (items of <= 128 rows of a group, the group itself the only target, the diagonal
 // excluded; lists of 32 per column third), the rerank in the reference's distance with
-// its certificate, then the exact fused kernel for the 64-row blocks holding a rejected
-// row.  Every row is written by the rerank; the fused kernel rewrites rejected blocks.
+// its certificate, then the exact kernel for the rows it rejected.  Every row is written
+// by the rerank; the fallback rewrites the rejected ones.
 int run_knn_tensor(ungx_context *ctx, const std::vector<uint32_t> &ranges, uint32_t num_groups,
                    const ungx::KnnParams &kp, cudaStream_t s, uint32_t &rejected)
 {
@@ -857,24 +857,10 @@ int run_knn_tensor(ungx_context *ctx, const std::vector<uint32_t> &ranges, uint3
    if (hc[2] != 0)
       return fail(ctx, (int)hc[2], "kNN tensor-core kernel reported status " + std::to_string((int)hc[2]));
    rejected = hc[1];
+   // the rejected rows, each recomputed exactly by a warp (the list of (group, row) pairs
+   // stays on the device)
    if (rejected)
-   {
-      std::vector<uint32_t> fb(2 * size_t(rejected));
-      UNGX_CUDA(ctx, cudaMemcpy(fb.data(), ctx->knn_fb.p, fb.size() * sizeof(uint32_t), cudaMemcpyDeviceToHost),
-                "kNN fallback rows");
-      std::vector<uint64_t> keys(rejected);
-      for (uint32_t i = 0; i < rejected; ++i)
-         keys[i] = (uint64_t(fb[2 * i]) << 32) | (fb[2 * i + 1] / 64u * 64u);
-      std::sort(keys.begin(), keys.end());
-      keys.erase(std::unique(keys.begin(), keys.end()), keys.end());
-      std::vector<uint32_t> tasks;
-      for (uint64_t k2 : keys)
-         tasks.insert(tasks.end(), {uint32_t(k2 >> 32), uint32_t(k2)});
-      if ((st = upload(ctx, ctx->knn_tasks, tasks, "kNN fallback tasks")))
-         return st;
-      UNGX_CUDA(ctx, ungx::launch_exact_knn(kp, ctx->knn_tasks.as<uint32_t>(), (uint32_t)(tasks.size() / 2), s),
-                "kNN fallback kernel");
-   }
+      UNGX_CUDA(ctx, ungx::launch_knn_fallback_rows(kp, ctx->knn_fb.as<uint32_t>(), rejected, s), "kNN fallback kernel");
    return UNGX_OK;
 }
 } // namespace

@@ -965,7 +965,86 @@ __global__ void __launch_bounds__(kRrWarps * 32) knn_rerank_kernel(const KnnRera
    }
 }
 
+// Rows the certificate rejected, a warp per row: every column of the row's group gets
+// the reference's distance (lane l: columns x0 + l of each 32-column step), and the
+// passing columns of a step are inserted in ascending id with the reference's strict <
+// against the list's last entry (FLT_MAX at first): a ballot gives the position, one
+// shuffle moves the tail.  Then the row is laid out as every other row.
+__global__ void __launch_bounds__(kRrWarps * 32) knn_fallback_rows_kernel(const KnnParams p,
+                                                                        const uint32_t *__restrict__ rows,
+                                                                        uint32_t count)
+{
+   __shared__ uint32_t s_top[kRrWarps][kKnnMax];
+   __shared__ float s_a[kRrWarps][kRrMaxDim];
+   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+   const uint32_t wi = blockIdx.x * kRrWarps + warp;
+   if (wi >= count)
+      return;
+   const uint32_t group = rows[2 * wi], s = rows[2 * wi + 1];
+   const uint32_t first = p.ranges[2 * group], n = p.ranges[2 * group + 1] - first;
+   uint32_t cand = p.candidate_k > 0 ? p.candidate_k - 1 : 0;
+   cand = min(cand, uint32_t(kKnnMax));
+   cand = min(cand, n > 0 ? n - 1 : 0u);
+   for (uint32_t dim = lane; dim < p.d; dim += 32)
+      s_a[warp][dim] = p.X[size_t(first + s) * p.d + dim];
+   __syncwarp();
+   float e0 = FLT_MAX, e1 = FLT_MAX; // list entries lane and lane + 32
+   uint32_t i0 = 0xFFFFFFFFu, i1 = 0xFFFFFFFFu;
+   const uint32_t lc = cand > 0 ? (cand - 1u) & 31u : 0u;
+   if (cand > 0)
+      for (uint32_t x0 = 0; x0 < n; x0 += 32u)
+      {
+         const uint32_t x = x0 + lane;
+         const float dist = x < n && x != s ? block_l2_thread(s_a[warp], p.X + size_t(first + x) * p.d, p.d) : FLT_MAX;
+         const float last0 = __shfl_sync(0xffffffffu, cand > 32u ? e1 : e0, lc);
+         uint32_t m = __ballot_sync(0xffffffffu, dist < last0);
+         while (m)
+         {
+            const uint32_t b = __ffs(m) - 1u;
+            m &= m - 1u;
+            const float nd = __shfl_sync(0xffffffffu, dist, b);
+            const float last = __shfl_sync(0xffffffffu, cand > 32u ? e1 : e0, lc);
+            if (!(nd < last))
+               continue;
+            const uint32_t pos = __popc(__ballot_sync(0xffffffffu, lane < cand && e0 <= nd)) +
+                                 __popc(__ballot_sync(0xffffffffu, lane + 32u < cand && e1 <= nd));
+            const float u0 = __shfl_up_sync(0xffffffffu, e0, 1), u1 = __shfl_up_sync(0xffffffffu, e1, 1);
+            const uint32_t v0 = __shfl_up_sync(0xffffffffu, i0, 1), v1 = __shfl_up_sync(0xffffffffu, i1, 1);
+            const float t31 = __shfl_sync(0xffffffffu, e0, 31);
+            const uint32_t j31 = __shfl_sync(0xffffffffu, i0, 31);
+            const float p1 = lane ? u1 : t31;
+            const uint32_t q1 = lane ? v1 : j31;
+            const uint32_t nid = x0 + b;
+            if (lane >= pos)
+            {
+               e0 = lane == pos ? nd : u0;
+               i0 = lane == pos ? nid : v0;
+            }
+            if (lane + 32u >= pos)
+            {
+               e1 = lane + 32u == pos ? nd : p1;
+               i1 = lane + 32u == pos ? nid : q1;
+            }
+         }
+      }
+   s_top[warp][lane] = lane < cand ? i0 : 0xFFFFFFFFu;
+   s_top[warp][32u + lane] = lane + 32u < cand ? i1 : 0xFFFFFFFFu;
+   __syncwarp();
+   if (lane == 0)
+      write_row(p, group, n, s, cand, s_top[warp]);
+}
+
 } // namespace
+
+cudaError_t launch_knn_fallback_rows(const KnnParams &p, const uint32_t *d_rows, uint32_t count, cudaStream_t s)
+{
+   if (count == 0)
+      return cudaSuccess;
+   if (p.d > uint32_t(kRrMaxDim))
+      return cudaErrorInvalidValue;
+   knn_fallback_rows_kernel<<<(count + kRrWarps - 1) / kRrWarps, kRrWarps * 32, 0, s>>>(p, d_rows, count);
+   return cudaGetLastError();
+}
 
 cudaError_t launch_knn_rerank(const KnnRerankParams &p, uint32_t num_items, cudaStream_t s)
 {
