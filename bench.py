@@ -517,6 +517,7 @@ def run_graph_stages(args):
         if route_name == "exact":
             exact_rows = d_graph[:pts].clone()
     knn_rejected = ctx.knn_rejected_rows()
+    knn_phases = {k: round(v, 3) for k, v in ctx.knn_phase_ms().items()}
     knn_equal = bool(torch.equal(exact_rows, d_graph[:pts]))
     knn_ms = knn["tensor"]
     del exact_rows
@@ -532,6 +533,7 @@ def run_graph_stages(args):
     big_ms = statistics.median(ctx.exact_knn_graph_device(big_ranges, cfg, g_big.data_ptr())
                                for _ in range(max(min(args.steps, 3), 1)))
     big_rejected = ctx.knn_rejected_rows()
+    big_phases = {k: round(v, 3) for k, v in ctx.knn_phase_ms().items()}
     del g_big
     # CPU: the oracle restatement (the reference's seeding cannot be built) on a group sample
     rng = np.random.default_rng(0)
@@ -584,7 +586,8 @@ def run_graph_stages(args):
         "config": {"workload": c["name"], "n": n, "d": d, "k": k},
         "knn_seeding": {"groups": int(sel.size), "points": pts, "pairs": pairs, "ms": round(knn_ms, 3),
                         "route": "tcgen05 fp16 self-join prefilter + the reference's distance for 96 candidates",
-                        "rows_rejected": int(knn_rejected), "exact_route_ms": round(knn["exact"], 3),
+                        "rows_rejected": int(knn_rejected), "phases_ms": knn_phases,
+                        "exact_route_ms": round(knn["exact"], 3),
                         "routes_equal": knn_equal,
                         "tflops_algorithmic": round(2.0 * d * pairs / (knn_ms * 1e-3) / 1e12, 3),
                         "cpu_baseline": {"kind": "port", "cores": os.cpu_count(),
@@ -593,6 +596,7 @@ def run_graph_stages(args):
         "knn_seeding_all_groups": {"groups": int(big.size), "points": big_pts, "pairs": big_pairs,
                                    "largest_group": int(sizes[big].max()) if big.size else 0,
                                    "ms": round(big_ms, 3), "rows_rejected": int(big_rejected),
+                                   "phases_ms": big_phases,
                                    "tflops_algorithmic": round(2.0 * d * big_pairs / (big_ms * 1e-3) / 1e12, 3)},
         "additional_edges": {"missing_group_edges": int(add.missing_group_edges),
                              "query_vectors": int(add.query_vectors), "edges": int(add.edges),

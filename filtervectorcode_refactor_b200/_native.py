@@ -217,6 +217,7 @@ _SIGNATURES = [
     ("ungx_graph_copy", c_int, [c_void_p, c_void_p, c_void_p]),
     ("ungx_exact_knn_default_config", None, [c_uint32, c_uint32, POINTER(ExactKnnConfig)]),
     ("ungx_exact_knn_rejected_rows", c_uint64, [c_void_p]),
+    ("ungx_exact_knn_phase_ms", None, [c_void_p, POINTER(c_double)]),
     ("ungx_exact_knn_graph_device", c_int,
      [c_void_p, c_uint32, c_void_p, POINTER(ExactKnnConfig), c_void_p, c_void_p, c_void_p, POINTER(c_double)]),
 ]
@@ -466,6 +467,13 @@ class Context:
     def knn_rejected_rows(self) -> int:
         """Rows of the last tensor-route kNN seeding that the exact kernel rewrote."""
         return int(lib.ungx_exact_knn_rejected_rows(self.h))
+
+    def knn_phase_ms(self) -> dict:
+        """Device time of the last kNN seeding by phase (prefilter, rerank, fallback: the
+        tensor route's; whole: the call)."""
+        out = (c_double * 4)()
+        lib.ungx_exact_knn_phase_ms(self.h, out)
+        return {"prefilter": out[0], "rerank": out[1], "fallback": out[2], "whole": out[3]}
 
     def graph_csr_device(self, num_points: int, topk: int, d_intra_offsets: int | None, d_intra_cols: int | None,
                          d_cross_ids: int | None, with_additional: bool, d_offsets: int, d_cols: int | None,

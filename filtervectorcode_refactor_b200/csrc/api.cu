@@ -153,6 +153,7 @@ struct ungx_context
        add_res, add_off, add_cols, add_qoff, add_loff, add_from, add_to, add_stats, scan_scratch, knn_ranges, knn_base,
        knn_tasks, knn_dist, knn_dbase, knn_tiles, knn_rows;
    uint64_t knn_rejected = 0; // rows the last tensor-route kNN seeding sent to the exact kernel
+   double knn_phase_ms[4] = {}; // last kNN seeding: prefilter, rerank, fallback, whole call
    uint32_t add_n = 0;     // points of the last additional-edge build
    uint64_t add_edges = 0; // its edges
    // merged adjacency of the last ungx_build_cross_group_edges call
@@ -821,7 +822,9 @@ int run_knn_tensor(ungx_context *ctx, const std::vector<uint32_t> &ranges, uint3
    tp.inject = ctx->inject;
    tp.exclude_self = 1;
    const uint32_t grid = (uint32_t)std::min<size_t>(plan.items.size(), (size_t)ctx->num_sms);
+   UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[3], s), "event");
    UNGX_CUDA(ctx, ungx::launch_tc(maps, tp, (uint32_t)kp_lists, grid, s), "kNN tensor-core kernel launch");
+   UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[4], s), "event");
    ungx::KnnRerankParams rp{};
    rp.p = kp;
    rp.items = tp.items;
@@ -857,8 +860,14 @@ int run_knn_tensor(ungx_context *ctx, const std::vector<uint32_t> &ranges, uint3
    if (hc[2] != 0)
       return fail(ctx, (int)hc[2], "kNN tensor-core kernel reported status " + std::to_string((int)hc[2]));
    rejected = hc[1];
+   float a = 0.f, b = 0.f;
+   cudaEventElapsedTime(&a, ctx->ev[3], ctx->ev[4]);
+   cudaEventElapsedTime(&b, ctx->ev[4], ctx->ev[2]);
+   ctx->knn_phase_ms[0] = a;
+   ctx->knn_phase_ms[1] = b;
    // the rejected rows, each recomputed exactly by a warp (the list of (group, row) pairs
    // stays on the device)
+   UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[5], s), "event");
    if (rejected)
       UNGX_CUDA(ctx, ungx::launch_knn_fallback_rows(kp, ctx->knn_fb.as<uint32_t>(), rejected, s), "kNN fallback kernel");
    return UNGX_OK;
@@ -1987,6 +1996,14 @@ void ungx_exact_knn_default_config(uint32_t candidate_k, uint32_t final_degree, 
 
 uint64_t ungx_exact_knn_rejected_rows(const ungx_context *ctx) { return ctx ? ctx->knn_rejected : 0; }
 
+void ungx_exact_knn_phase_ms(const ungx_context *ctx, double out[4])
+{
+   if (!out)
+      return;
+   for (int i = 0; i < 4; ++i)
+      out[i] = ctx ? ctx->knn_phase_ms[i] : 0.0;
+}
+
 int ungx_exact_knn_graph_device(ungx_context *ctx, uint32_t num_groups, const uint32_t *group_ranges,
                                 const ungx_exact_knn_config *cfg, uint32_t *d_graph, uint32_t *d_entry_points,
                                 void *stream, double *kernel_ms)
@@ -2053,6 +2070,8 @@ int ungx_exact_knn_graph_device(ungx_context *ctx, uint32_t num_groups, const ui
    const uint64_t batch_entries = std::max<uint64_t>(1, env_u64("UNGX_KNN_BATCH_ENTRIES", ungx::kKnnDistBatch));
    UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[0], s), "event");
    ctx->knn_rejected = 0;
+   for (double &v : ctx->knn_phase_ms)
+      v = 0.0;
    const uint32_t route = cfg->route == UNGX_ROUTE_AUTO ? uint32_t(UNGX_ROUTE_TENSOR) : cfg->route;
    if (route == UNGX_ROUTE_TENSOR)
    {
@@ -2132,12 +2151,17 @@ int ungx_exact_knn_graph_device(ungx_context *ctx, uint32_t num_groups, const ui
    UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[1], s), "event");
    if ((st = wait_event(ctx, ctx->ev[1], "exact kNN seeding")))
       return st;
-   if (kernel_ms)
+   float ms = 0;
+   cudaEventElapsedTime(&ms, ctx->ev[0], ctx->ev[1]);
+   if (route == UNGX_ROUTE_TENSOR)
    {
-      float ms = 0;
-      cudaEventElapsedTime(&ms, ctx->ev[0], ctx->ev[1]);
-      *kernel_ms = ms;
+      float f = 0;
+      cudaEventElapsedTime(&f, ctx->ev[5], ctx->ev[1]);
+      ctx->knn_phase_ms[2] = f;
    }
+   ctx->knn_phase_ms[3] = ms;
+   if (kernel_ms)
+      *kernel_ms = ms;
    return UNGX_OK;
 }
 

@@ -425,7 +425,8 @@ typedef struct ungx_exact_knn_config
    uint32_t route;        /* UNGX_ROUTE_TENSOR (AUTO): tcgen05 fp16 prefilter of each group's
                              self-join keeping 96 candidates per point, the reference's
                              distance for those, a certificate that no other point could
-                             enter, the exact kernel for the 64-row blocks it rejects;
+                             enter, the exact kernel (a warp per row) for the rows it
+                             rejects;
                              UNGX_ROUTE_EXACT: the reference's distance for every pair */
 } ungx_exact_knn_config;
 
@@ -435,6 +436,10 @@ void ungx_exact_knn_default_config(uint32_t candidate_k, uint32_t final_degree, 
 /* Rows of the last ungx_exact_knn_graph_device call (tensor route) whose certificate
  * failed, rewritten by the exact kernel. */
 uint64_t ungx_exact_knn_rejected_rows(const ungx_context *ctx);
+/* Device time (CUDA events, ms) of the last ungx_exact_knn_graph_device call: out[0] the
+ * tensor route's prefilter kernel, out[1] its rerank and certificate, out[2] the exact
+ * kernel for the rejected rows (all 0 on the exact route), out[3] the whole call. */
+void ungx_exact_knn_phase_ms(const ungx_context *ctx, double out[4]);
 
 /* Groups g = 0 .. num_groups-1 are rows [group_ranges[2g], group_ranges[2g+1]) of the
  * base vectors of ungx_prepare_base_vectors (any dim up to 352).  d_graph (device):
