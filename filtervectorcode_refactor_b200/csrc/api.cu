@@ -133,7 +133,7 @@ struct ungx_context
    uint64_t mem_limit = 0; // device budget of ungx_cross_edges_build (0: free memory)
    DevBuf pass_x, pass_ids, pass_dists, pass_ranges; // capacity path
    Plan knn_plan; // tensor-core kNN seeding: items of the groups' self-joins
-   DevBuf knn_items, knn_segs, knn_chunks, knn_gmax, knn_fb, knn_cnt;
+   DevBuf knn_items, knn_segs, knn_chunks, knn_gmax, knn_fb, knn_fbt, knn_cnt;
    uint32_t inject = UNGX_INJECT_NONE;
    PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
    // resident base vectors (a4)
@@ -865,11 +865,38 @@ int run_knn_tensor(ungx_context *ctx, const std::vector<uint32_t> &ranges, uint3
    cudaEventElapsedTime(&b, ctx->ev[4], ctx->ev[2]);
    ctx->knn_phase_ms[0] = a;
    ctx->knn_phase_ms[1] = b;
-   // the rejected rows, each recomputed exactly by a warp (the list of (group, row) pairs
-   // stays on the device)
-   UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[5], s), "event");
+   // the rejected rows, recomputed exactly: the (group, row) list sorted by group and cut
+   // into tasks of a few rows of one group, which share every staged column tile
    if (rejected)
-      UNGX_CUDA(ctx, ungx::launch_knn_fallback_rows(kp, ctx->knn_fb.as<uint32_t>(), rejected, s), "kNN fallback kernel");
+   {
+      std::vector<uint64_t> fb(rejected);
+      UNGX_CUDA(ctx, cudaMemcpy(fb.data(), ctx->knn_fb.p, size_t(rejected) * 8u, cudaMemcpyDeviceToHost),
+                "kNN fallback list");
+      // each pair reads as group | row << 32 (little-endian): order by (group, row)
+      for (uint64_t &v : fb)
+         v = (v << 32) | (v >> 32);
+      std::sort(fb.begin(), fb.end());
+      std::vector<uint32_t> rows(2 * size_t(rejected)), tasks;
+      const uint32_t per = ungx::knn_fallback_rows_per_task();
+      for (size_t i = 0; i < fb.size(); ++i)
+      {
+         rows[2 * i] = uint32_t(fb[i] >> 32);
+         rows[2 * i + 1] = uint32_t(fb[i]);
+         if (i == 0 || rows[2 * i] != rows[2 * i - 2] || tasks.back() == per)
+            tasks.insert(tasks.end(), {uint32_t(i), 0u});
+         ++tasks.back();
+      }
+      if ((st = upload(ctx, ctx->knn_fb, rows, "kNN fallback list")) ||
+          (st = upload(ctx, ctx->knn_fbt, tasks, "kNN fallback tasks")))
+         return st;
+      UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[5], s), "event");
+      UNGX_CUDA(ctx,
+                ungx::launch_knn_fallback_rows(kp, ctx->knn_fb.as<uint32_t>(), ctx->knn_fbt.as<uint32_t>(),
+                                               (uint32_t)(tasks.size() / 2), s),
+                "kNN fallback kernel");
+   }
+   else
+      UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[5], s), "event");
    return UNGX_OK;
 }
 } // namespace
@@ -961,7 +988,7 @@ int ungx_context_destroy(ungx_context *ctx)
                      &ctx->knn_rows, &ctx->intra_off, &ctx->intra_cols, &ctx->graph_off, &ctx->graph_cols,
                      &ctx->own_runs, &ctx->all_runs, &ctx->recv, &ctx->pass_x, &ctx->pass_ids, &ctx->pass_dists,
                      &ctx->pass_ranges, &ctx->knn_items, &ctx->knn_segs, &ctx->knn_chunks, &ctx->knn_gmax,
-                     &ctx->knn_fb, &ctx->knn_cnt})
+                     &ctx->knn_fb, &ctx->knn_fbt, &ctx->knn_cnt})
       b->release();
    ctx->host_stage.release();
    for (auto &ev : ctx->ev)

@@ -191,9 +191,12 @@ struct KnnRerankParams
    unsigned long long *counters; // [0] certified rows, [1] rejected rows
 };
 cudaError_t launch_knn_rerank(const KnnRerankParams &p, uint32_t num_items, cudaStream_t s);
-// The exact seeding of single rows, a warp per (group, local row) pair of d_rows
-// [2 * count]: the rows the rerank's certificate rejected.
-cudaError_t launch_knn_fallback_rows(const KnnParams &p, const uint32_t *d_rows, uint32_t count, cudaStream_t s);
+// The exact seeding of the rows the rerank's certificate rejected: d_rows [2 * count]
+// (group, local row) pairs sorted by group; d_tasks [2 * num_tasks] = (first pair,
+// pairs) with at most knn_fallback_rows_per_task() pairs of one group each.
+uint32_t knn_fallback_rows_per_task();
+cudaError_t launch_knn_fallback_rows(const KnnParams &p, const uint32_t *d_rows, const uint32_t *d_tasks,
+                                     uint32_t num_tasks, cudaStream_t s);
 
 // ---- graph assembly (graph.cu)
 // group_of[v] = group of row v (1..G), G + 1 for rows outside every group.

@@ -772,66 +772,184 @@ __global__ void __launch_bounds__(kRowWarps * 32) knn_rows_kernel(const KnnParam
 }
 
 // ------------------------------------------------------------------ tensor-core route
-// The reference's distance of one (a, b) pair evaluated by one thread: the partial of
-// block thread t is the fma chain over dims t, t + 128, ... (zero past d), each warp of
-// 32 partials is reduced by the __shfl_down tree (offsets 16 .. 1), and the warp sums
-// are added as (w0 + w2) + (w1 + w3); every operation flushes subnormals.  `a` is in
-// shared memory (the row of the warp), `b` in global memory.
-__device__ float block_l2_thread(const float *__restrict__ a, const float *__restrict__ b, uint32_t d)
+// Distances of one query row to 32 gathered candidate rows (lane l: candidate l), in
+// the reference's block summation.  The candidates' dimensions of reference warp j
+// (dims 32 j + l + 128 c, c < C) pass through a double-buffered per-warp stage in
+// shared memory, filled by cp.async: a row segment of 32 floats is 128 contiguous bytes
+// whatever rows are gathered, so the loads are coalesced, and nothing waits on them
+// while the previous stage is summed.  The stage's row stride is 32 C + 2 floats, so
+// that the 8-byte reads of a half warp (lane l: its own candidate's row) hit 32
+// distinct banks.  Lane l evaluates the 32 partials of reference warp j for its
+// candidate as 16 packed f32x2 pairs: the fma chains over c, the first one from a zero
+// accumulator as in the reference, then the __shfl_down tree (offsets 16 .. 2 are
+// packed adds of pairs m and m + off / 2; offset 1 adds the two halves), and the warp
+// sums as (w0 + w2) + (w1 + w3).  Padding past d is zero: 0 - 0 = +0 and fma(+0, +0,
+// acc) = acc for acc >= +0, so the padded sums equal the reference's.  The zero
+// accumulator is a register the compiler cannot prove zero: a packed square written as
+// a multiply (or an fma of a known zero) followed by the tree's first packed add was
+// contracted by ptxas into one fma, one rounding fewer than the reference's, which
+// moved about one distance in eight by an ulp.
+__device__ __forceinline__ void cp_async8(float *dst, const float *src, uint32_t bytes)
 {
-   float w[4];
-#pragma unroll 1
-   for (int j = 0; j < 4; ++j)
-   {
-      float v[32];
-#pragma unroll
-      for (int l = 0; l < 32; ++l)
-      {
-         float acc = 0.0f;
-         for (uint32_t dim = uint32_t(32 * j + l); dim < d; dim += 128)
-         {
-            const float diff = sub_ftz(a[dim], __ldg(b + dim));
-            acc = fma_ftz(diff, diff, acc);
-         }
-         v[l] = acc;
-      }
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1)
-#pragma unroll
-         for (int i = 0; i < off; ++i)
-            v[i] = add_ftz(v[i], v[i + off]);
-      w[j] = v[0];
-   }
-   return add_ftz(add_ftz(w[0], w[2]), add_ftz(w[1], w[3]));
+   asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+                "l"(__cvta_generic_to_global(src)), "r"(bytes)
+                : "memory");
 }
+__device__ __forceinline__ void cp_async4(float *dst, const float *src, uint32_t bytes)
+{
+   asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+                "l"(__cvta_generic_to_global(src)), "r"(bytes)
+                : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait()
+{
+   asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+constexpr uint32_t kNoRow = 0xFFFFFFFFu;
+
+// C = ceil(d / 128) segments per partial; PAIRS: 8-byte copies (d even and X 8-byte
+// aligned), else 4-byte copies.
+template <int C, bool PAIRS>
+struct WarpDist
+{
+   static constexpr int kLd = 32 * C + 2;  // stage row stride (floats)
+   static constexpr int kStage = 32 * kLd; // one buffer
+   static constexpr int kQ = 128 * C;      // the query row, zero padded
+   static constexpr int kWarpFloats = 2 * kStage + 2 * kQ;
+
+   float *st; // [2][32][kLd]
+   float *sq; // [2][kQ]
+   const float *X;
+   uint32_t d;
+   uint64_t zero; // packed (+0, +0), not known to the compiler as a constant
+
+   // Copies of reference warp j's dimensions of candidate rows shfl(row, r) into stage buf.
+   __device__ __forceinline__ void issue(uint32_t buf, uint32_t row, uint32_t j, uint32_t lane) const
+   {
+      float *dst = st + buf * kStage;
+      if constexpr (PAIRS)
+      {
+#pragma unroll
+         for (int i = 0; i < 16 * C; ++i)
+         {
+            const uint32_t e = lane + 32u * i;
+            const uint32_t r = e / (16u * C), q = e % (16u * C), c = q / 16u, m = q % 16u;
+            const uint32_t rr = __shfl_sync(0xffffffffu, row, r);
+            const uint32_t dim = 32u * j + 128u * c + 2u * m;
+            const bool ok = rr != kNoRow && dim < d;
+            cp_async8(dst + r * kLd + c * 32u + 2u * m, ok ? X + size_t(rr) * d + dim : X, ok ? 8u : 0u);
+         }
+      }
+      else
+      {
+#pragma unroll 8
+         for (int i = 0; i < 32 * C; ++i)
+         {
+            const uint32_t e = lane + 32u * i;
+            const uint32_t r = e / (32u * C), q = e % (32u * C), c = q / 32u, l = q % 32u;
+            const uint32_t rr = __shfl_sync(0xffffffffu, row, r);
+            const uint32_t dim = 32u * j + 128u * c + l;
+            const bool ok = rr != kNoRow && dim < d;
+            cp_async4(dst + r * kLd + c * 32u + l, ok ? X + size_t(rr) * d + dim : X, ok ? 4u : 0u);
+         }
+      }
+   }
+
+   // The query row into buffer qb (zero padded to kQ).
+   __device__ __forceinline__ void issue_query(uint32_t qb, uint32_t row, uint32_t lane) const
+   {
+      float *dst = sq + qb * kQ;
+      if constexpr (PAIRS)
+      {
+#pragma unroll
+         for (int i = 0; i < 2 * C; ++i)
+         {
+            const uint32_t dim = 2u * (lane + 32u * i);
+            const bool ok = dim < d;
+            cp_async8(dst + dim, ok ? X + size_t(row) * d + dim : X, ok ? 8u : 0u);
+         }
+      }
+      else
+      {
+#pragma unroll
+         for (int i = 0; i < 4 * C; ++i)
+         {
+            const uint32_t dim = lane + 32u * i;
+            const bool ok = dim < d;
+            cp_async4(dst + dim, ok ? X + size_t(row) * d + dim : X, ok ? 4u : 0u);
+         }
+      }
+   }
+
+   // Sum w_j of reference warp j for this lane's candidate (stage buf, query qb).
+   __device__ __forceinline__ float warp_sum(uint32_t buf, uint32_t qb, uint32_t j, uint32_t lane) const
+   {
+      const float *b = st + buf * kStage + lane * kLd;
+      const float *a = sq + qb * kQ + 32u * j;
+      uint64_t v[16];
+#pragma unroll
+      for (int c = 0; c < C; ++c)
+#pragma unroll
+         for (int m = 0; m < 16; ++m)
+         {
+            const uint64_t bv = *reinterpret_cast<const uint64_t *>(b + c * 32 + 2 * m);
+            const uint64_t av = *reinterpret_cast<const uint64_t *>(a + c * 128 + 2 * m);
+            const uint64_t df = sub2_ftz(av, bv);
+            v[m] = fma2_ftz(df, df, c == 0 ? zero : v[m]);
+         }
+#pragma unroll
+      for (int h = 8; h >= 1; h >>= 1)
+#pragma unroll
+         for (int m = 0; m < h; ++m)
+            v[m] = add2_ftz(v[m], v[m + h]);
+      return add_ftz(__uint_as_float(uint32_t(v[0])), __uint_as_float(uint32_t(v[0] >> 32)));
+   }
+};
 
 constexpr int kRrWarps = 4;         // a block per work item: 4 warps x 32 rows
 constexpr int kRrLists = 3;         // the prefilter's lists per row (column thirds)
 constexpr int kRrDepth = 32;        // entries per list
 constexpr int kRrEntries = kRrLists * kRrDepth;
-constexpr int kRrMaxDim = 352;      // shared-memory row of each warp
+constexpr int kRrMaxDim = 352;      // three 128-dim segments per partial at most
+
+__device__ __forceinline__ uint64_t shfl64(uint64_t v, uint32_t src)
+{
+   const uint32_t lo = __shfl_sync(0xffffffffu, uint32_t(v), src);
+   const uint32_t hi = __shfl_sync(0xffffffffu, uint32_t(v >> 32), src);
+   return (uint64_t(hi) << 32) | lo;
+}
 
 // A block per work item (<= 128 rows of one group); warp w ranks rows 32 w .. 32 w + 31
 // one after the other, then every lane lays out one of them.  Per row: the 96 list
-// entries (lane l: l, l + 32, l + 64) get the reference's distance; the cand smallest by
-// (distance, local id) below FLT_MAX are the row's list (the reference's strict-<
-// inserts in ascending id from FLT_MAX keep exactly those).  Certificate: every column
-// outside the lists has a prefilter key >= T, the smallest last key of a full list, so
-// its reference distance is at least ((|a|^2 + T - bound)(1 - gref) - abs_err); when that
-// exceeds the cand-th distance no such column can enter.  A row whose lists are all
-// short saw every column.  Rejected rows are queued for the exact kernel.
+// entries (list e: lane l holds entry l) get the reference's distance, list by list
+// through the staged pipeline above (the next row's query and candidates are fetched
+// while the current row's last list is summed); the cand smallest by (distance, local
+// id) below FLT_MAX are the row's list (the reference's strict-< inserts in ascending
+// id from FLT_MAX keep exactly those).  Certificate: every column outside the lists has
+// a prefilter key >= T, the smallest last key of a list that dropped a column, so its
+// reference distance is at least ((|a|^2 + T - bound)(1 - gref) - abs_err); when that
+// exceeds the cand-th distance no such column can enter.  A row whose lists all saw
+// every one of their columns is exact as it stands.  Rejected rows are queued for the
+// exact kernel.
+template <int C, bool PAIRS>
 __global__ void __launch_bounds__(kRrWarps * 32) knn_rerank_kernel(const KnnRerankParams rp)
 {
-   __shared__ uint32_t s_top[kRrWarps][32][kKnnMax];
-   __shared__ float s_a[kRrWarps][kRrMaxDim];
+   using WD = WarpDist<C, PAIRS>;
+   extern __shared__ __align__(16) float rr_smem[];
    if (*reinterpret_cast<const volatile int *>(rp.status) != 0)
       return; // an aborted prefilter left the lists unwritten
    const KnnParams &p = rp.p;
    const WorkItem w = rp.items[blockIdx.x];
    const Segment sg = rp.segs[w.seg_begin];
    const uint32_t group = sg.group_id - 1u;
-   const uint32_t first = p.ranges[2 * group], n = p.ranges[2 * group + 1] - first;
+   const uint32_t first = p.ranges[2 * group], end = p.ranges[2 * group + 1], n = end - first;
    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+   const WD wd{rr_smem + warp * WD::kWarpFloats, rr_smem + warp * WD::kWarpFloats + 2 * WD::kStage, p.X, p.d,
+               uint64_t(p.d >> 31)};
+   uint32_t *s_top = reinterpret_cast<uint32_t *>(rr_smem + kRrWarps * WD::kWarpFloats) + warp * (32 * kKnnMax);
    uint32_t cand = p.candidate_k > 0 ? p.candidate_k - 1 : 0;
    cand = min(cand, uint32_t(kKnnMax));
    cand = min(cand, n > 0 ? n - 1 : 0u);
@@ -853,72 +971,125 @@ __global__ void __launch_bounds__(kRrWarps * 32) knn_rerank_kernel(const KnnRera
       }
    uint32_t n_cert = 0, n_fail = 0;
    const uint32_t r0 = warp * 32u;
-   for (uint32_t rr = 0; rr < 32u && r0 + rr < w.row_count; ++rr)
+   const uint32_t nrows = r0 < w.row_count ? min(32u, w.row_count - r0) : 0u;
+   // this lane's candidate row of each list of a row (kNoRow: empty, outside, itself)
+   auto cand_rows = [&](uint32_t rr, uint32_t (&c)[kRrLists]) {
+      const uint32_t row = w.row_begin + r0 + rr;
+      const uint32_t *cp = rp.cand_col + size_t(row) * kRrEntries;
+#pragma unroll
+      for (int e = 0; e < kRrLists; ++e)
+      {
+         const uint32_t v = cp[lane + 32u * e];
+         c[e] = v < end && v >= first && v != row ? v : kNoRow;
+      }
+   };
+   uint32_t cur[kRrLists], nxt[kRrLists];
+   if (nrows)
    {
+      cand_rows(0, cur);
+      wd.issue_query(0, w.row_begin + r0, lane);
+      wd.issue(0, cur[0], 0, lane);
+      cp_commit();
+      if (nrows > 1)
+         cand_rows(1, nxt);
+   }
+   float D[kRrLists] = {INFINITY, INFINITY, INFINITY};
+   float s02 = 0.f, s13 = 0.f;
+   const uint32_t stages = 12u * nrows; // (row, list, reference warp)
+   for (uint32_t t = 0; t < stages; ++t)
+   {
+      const uint32_t j = t & 3u, set = t >> 2, rr = set / 3u, e = set % 3u;
+      const uint32_t t1 = t + 1u;
+      if (t1 < stages)
+      {
+         const uint32_t set1 = t1 >> 2, rr1 = set1 / 3u, e1 = set1 % 3u;
+         const uint32_t *src = rr1 == rr ? cur : nxt;
+         const uint32_t row1 = e1 == 0u ? src[0] : (e1 == 1u ? src[1] : src[2]);
+         if (rr1 != rr)
+            wd.issue_query(rr1 & 1u, w.row_begin + r0 + rr1, lane);
+         wd.issue(t1 & 1u, row1, t1 & 3u, lane);
+         cp_commit();
+         cp_wait<1>();
+      }
+      else
+         cp_wait<0>();
+      __syncwarp();
+      const float ws = wd.warp_sum(t & 1u, rr & 1u, j, lane);
+      __syncwarp();
+      if (j == 0u)
+         s02 = ws;
+      else if (j == 1u)
+         s13 = ws;
+      else if (j == 2u)
+         s02 = add_ftz(s02, ws);
+      else
+      {
+         const float dd = add_ftz(s02, add_ftz(s13, ws));
+         const uint32_t my = e == 0u ? cur[0] : (e == 1u ? cur[1] : cur[2]);
+         const float dv = my != kNoRow && dd < FLT_MAX ? dd : INFINITY;
+         if (e == 0u)
+            D[0] = dv;
+         else if (e == 1u)
+            D[1] = dv;
+         else
+            D[2] = dv;
+      }
+      if (j != 3u || e != 2u)
+         continue;
+      // ---- row rr complete: rank, lay out, certify
       const uint32_t row = w.row_begin + r0 + rr; // global row of X
       const uint32_t s = row - first;             // local row
-      __syncwarp();
-      for (uint32_t dim = lane; dim < p.d; dim += 32)
-         s_a[warp][dim] = p.X[size_t(row) * p.d + dim];
-      __syncwarp();
       const float *kp = rp.cand_key + size_t(row) * kRrEntries;
-      const uint32_t *cp = rp.cand_col + size_t(row) * kRrEntries;
-      float D[kRrLists];
+      uint64_t key[kRrLists];
       uint32_t id[kRrLists];
       float T = INFINITY; // smallest last key of a list that dropped a column
       const uint32_t self_list = ((s % 192u) / 32u) % 3u;
 #pragma unroll
-      for (int e = 0; e < kRrLists; ++e)
+      for (int f = 0; f < kRrLists; ++f)
       {
-         const uint32_t c = cp[lane + 32u * e];
-         id[e] = 0xFFFFFFFFu;
-         D[e] = INFINITY;
-         if (c < p.ranges[2 * group + 1] && c >= first && c != row)
-         {
-            const float dd = block_l2_thread(s_a[warp], p.X + size_t(c) * p.d, p.d);
-            if (dd < FLT_MAX)
-            {
-               D[e] = dd;
-               id[e] = c - first;
-            }
-         }
-         // list e (entries 32 e .. 32 e + 31, ascending keys) dropped a column only when it
-         // saw more than 32 (every column it dropped has a key >= its last one)
-         const float last_k = __shfl_sync(0xffffffffu, kp[lane + 32u * e], 31);
-         if (seen[e] - (uint32_t(e) == self_list ? 1u : 0u) > uint32_t(kRrDepth))
-            T = fminf(T, last_k);
+         id[f] = D[f] != INFINITY ? cur[f] - first : 0xFFFFFFFFu;
+         key[f] = D[f] != INFINITY ? (uint64_t(__float_as_uint(D[f])) << 32) | id[f] : ~0ull;
+         // list f dropped a column only when it saw more than 32 (every column it
+         // dropped has a key >= its last one)
+         if (seen[f] - (uint32_t(f) == self_list ? 1u : 0u) > uint32_t(kRrDepth))
+            T = fminf(T, __ldg(kp + 32 * f + 31));
       }
-      // rank of each entry by (distance, local id); empty entries (+inf, UINT32_MAX) last
+      // the next row's candidates, one row ahead of the pipeline
+#pragma unroll
+      for (int f = 0; f < kRrLists; ++f)
+         cur[f] = nxt[f];
+      if (rr + 2u < nrows)
+         cand_rows(rr + 2u, nxt);
+      // rank of each entry by (distance, local id): distinct keys for valid entries
       uint32_t rk[kRrLists] = {0u, 0u, 0u};
-#pragma unroll 1
+#pragma unroll 2
       for (int src = 0; src < 32; ++src)
 #pragma unroll
          for (int f = 0; f < kRrLists; ++f)
          {
-            const float d2 = __shfl_sync(0xffffffffu, D[f], src);
-            const uint32_t i2 = __shfl_sync(0xffffffffu, id[f], src);
+            const uint64_t k2 = shfl64(key[f], src);
 #pragma unroll
-            for (int e = 0; e < kRrLists; ++e)
-               rk[e] += pair_less_knn(d2, i2, D[e], id[e]) ? 1u : 0u;
+            for (int e2 = 0; e2 < kRrLists; ++e2)
+               rk[e2] += k2 < key[e2] ? 1u : 0u;
          }
       uint32_t nvalid = 0, have_k = 0;
       float dk = INFINITY;
 #pragma unroll
-      for (int e = 0; e < kRrLists; ++e)
+      for (int f = 0; f < kRrLists; ++f)
       {
-         const bool valid = id[e] != 0xFFFFFFFFu;
+         const bool valid = id[f] != 0xFFFFFFFFu;
          nvalid += __popc(__ballot_sync(0xffffffffu, valid));
-         if (valid && rk[e] < cand)
-            s_top[warp][rr][rk[e]] = id[e];
-         const uint32_t at = __ballot_sync(0xffffffffu, valid && cand > 0 && rk[e] == cand - 1u);
+         if (valid && rk[f] < cand)
+            s_top[rr * kKnnMax + rk[f]] = id[f];
+         const uint32_t at = __ballot_sync(0xffffffffu, valid && cand > 0 && rk[f] == cand - 1u);
          if (at)
          {
             have_k = 1;
-            dk = __shfl_sync(0xffffffffu, D[e], __ffs(at) - 1);
+            dk = __shfl_sync(0xffffffffu, D[f], __ffs(at) - 1);
          }
       }
       for (uint32_t q = nvalid + lane; q < cand; q += 32)
-         s_top[warp][rr][q] = 0xFFFFFFFFu; // the reference's unfilled list slots
+         s_top[rr * kKnnMax + q] = 0xFFFFFFFFu; // the reference's unfilled list slots
       // certificate (warp-uniform)
       bool cert;
       if (cand == 0)
@@ -954,8 +1125,8 @@ __global__ void __launch_bounds__(kRrWarps * 32) knn_rerank_kernel(const KnnRera
       }
    }
    __syncwarp();
-   if (r0 + lane < w.row_count)
-      write_row(p, group, n, w.row_begin + r0 + lane - first, cand, s_top[warp][lane]);
+   if (lane < nrows)
+      write_row(p, group, n, w.row_begin + r0 + lane - first, cand, s_top + lane * kKnnMax);
    if (lane == 0)
    {
       if (n_cert)
@@ -965,95 +1136,227 @@ __global__ void __launch_bounds__(kRrWarps * 32) knn_rerank_kernel(const KnnRera
    }
 }
 
-// Rows the certificate rejected, a warp per row: every column of the row's group gets
-// the reference's distance (lane l: columns x0 + l of each 32-column step), and the
-// passing columns of a step are inserted in ascending id with the reference's strict <
-// against the list's last entry (FLT_MAX at first): a ballot gives the position, one
-// shuffle moves the tail.  Then the row is laid out as every other row.
-__global__ void __launch_bounds__(kRrWarps * 32) knn_fallback_rows_kernel(const KnnParams p,
-                                                                        const uint32_t *__restrict__ rows,
-                                                                        uint32_t count)
+// The reference's inserts of one 32-column step into a list of cand (<= 64) entries
+// held by the warp (lane l: entries l and l + 32): the columns whose distance beats the
+// last entry (strict <, FLT_MAX at first) are taken in ascending id; a ballot gives
+// each one's position and one shuffle moves the tail.
+__device__ __forceinline__ void list_insert(float dist, uint32_t x0, uint32_t cand, uint32_t lane, float &e0, float &e1,
+                                            uint32_t &i0, uint32_t &i1)
 {
-   __shared__ uint32_t s_top[kRrWarps][kKnnMax];
-   __shared__ float s_a[kRrWarps][kRrMaxDim];
-   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-   const uint32_t wi = blockIdx.x * kRrWarps + warp;
-   if (wi >= count)
-      return;
-   const uint32_t group = rows[2 * wi], s = rows[2 * wi + 1];
+   const uint32_t lc = cand > 0 ? (cand - 1u) & 31u : 0u;
+   const float last0 = __shfl_sync(0xffffffffu, cand > 32u ? e1 : e0, lc);
+   uint32_t m = __ballot_sync(0xffffffffu, dist < last0);
+   while (m)
+   {
+      const uint32_t b = __ffs(m) - 1u;
+      m &= m - 1u;
+      const float nd = __shfl_sync(0xffffffffu, dist, b);
+      const float last = __shfl_sync(0xffffffffu, cand > 32u ? e1 : e0, lc);
+      if (!(nd < last))
+         continue;
+      const uint32_t pos = __popc(__ballot_sync(0xffffffffu, lane < cand && e0 <= nd)) +
+                           __popc(__ballot_sync(0xffffffffu, lane + 32u < cand && e1 <= nd));
+      const float u0 = __shfl_up_sync(0xffffffffu, e0, 1), u1 = __shfl_up_sync(0xffffffffu, e1, 1);
+      const uint32_t v0 = __shfl_up_sync(0xffffffffu, i0, 1), v1 = __shfl_up_sync(0xffffffffu, i1, 1);
+      const float t31 = __shfl_sync(0xffffffffu, e0, 31);
+      const uint32_t j31 = __shfl_sync(0xffffffffu, i0, 31);
+      const float p1 = lane ? u1 : t31;
+      const uint32_t q1 = lane ? v1 : j31;
+      const uint32_t nid = x0 + b;
+      if (lane >= pos)
+      {
+         e0 = lane == pos ? nd : u0;
+         i0 = lane == pos ? nid : v0;
+      }
+      if (lane + 32u >= pos)
+      {
+         e1 = lane + 32u == pos ? nd : p1;
+         i1 = lane + 32u == pos ? nid : q1;
+      }
+   }
+}
+
+// Rows the certificate rejected, in tasks of up to kFbWarps rows of one group (rows
+// sorted by group, task = (first entry, count)): warp w takes the task's row w, and
+// every 32-column step of the group passes once through a block-wide staged pipeline
+// (three buffers, one barrier per stage) shared by the task's rows.  Lane l sums
+// column x0 + l for its warp's row; the passing columns of a step are inserted in
+// ascending id (list_insert).  Then the row is laid out as every other row.
+constexpr int kFbWarps = 8;
+
+template <int C, bool PAIRS>
+__global__ void __launch_bounds__(kFbWarps * 32) knn_fallback_rows_kernel(const KnnParams p,
+                                                                        const uint32_t *__restrict__ rows,
+                                                                        const uint32_t *__restrict__ tasks)
+{
+   using WD = WarpDist<C, PAIRS>;
+   extern __shared__ __align__(16) float fb_smem[];
+   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u, tid = threadIdx.x;
+   float *st = fb_smem;                                 // [3][32][kLd]
+   float *sq = fb_smem + 3 * WD::kStage;                // [kFbWarps][kQ]
+   uint32_t *s_top = reinterpret_cast<uint32_t *>(sq + kFbWarps * WD::kQ) + warp * kKnnMax;
+   const WD wd{st, sq, p.X, p.d, uint64_t(p.d >> 31)};
+   const uint32_t start = tasks[2 * blockIdx.x], cnt = tasks[2 * blockIdx.x + 1];
+   const uint32_t group = rows[2 * start];
    const uint32_t first = p.ranges[2 * group], n = p.ranges[2 * group + 1] - first;
+   const bool active = warp < cnt;
+   const uint32_t s = active ? rows[2 * (start + warp) + 1] : 0u;
    uint32_t cand = p.candidate_k > 0 ? p.candidate_k - 1 : 0;
    cand = min(cand, uint32_t(kKnnMax));
    cand = min(cand, n > 0 ? n - 1 : 0u);
-   for (uint32_t dim = lane; dim < p.d; dim += 32)
-      s_a[warp][dim] = p.X[size_t(first + s) * p.d + dim];
-   __syncwarp();
-   float e0 = FLT_MAX, e1 = FLT_MAX; // list entries lane and lane + 32
-   uint32_t i0 = 0xFFFFFFFFu, i1 = 0xFFFFFFFFu;
-   const uint32_t lc = cand > 0 ? (cand - 1u) & 31u : 0u;
-   if (cand > 0)
-      for (uint32_t x0 = 0; x0 < n; x0 += 32u)
+   const uint32_t d = p.d;
+   // copies of reference warp j's dimensions of columns 32 step .. + 31 into buffer buf
+   auto issue = [&](uint32_t buf, uint32_t step, uint32_t j) {
+      float *dst = st + buf * WD::kStage;
+      const uint32_t x0 = 32u * step;
+      if constexpr (PAIRS)
       {
-         const uint32_t x = x0 + lane;
-         const float dist = x < n && x != s ? block_l2_thread(s_a[warp], p.X + size_t(first + x) * p.d, p.d) : FLT_MAX;
-         const float last0 = __shfl_sync(0xffffffffu, cand > 32u ? e1 : e0, lc);
-         uint32_t m = __ballot_sync(0xffffffffu, dist < last0);
-         while (m)
+#pragma unroll
+         for (uint32_t e = tid; e < 512u * C; e += kFbWarps * 32u)
          {
-            const uint32_t b = __ffs(m) - 1u;
-            m &= m - 1u;
-            const float nd = __shfl_sync(0xffffffffu, dist, b);
-            const float last = __shfl_sync(0xffffffffu, cand > 32u ? e1 : e0, lc);
-            if (!(nd < last))
-               continue;
-            const uint32_t pos = __popc(__ballot_sync(0xffffffffu, lane < cand && e0 <= nd)) +
-                                 __popc(__ballot_sync(0xffffffffu, lane + 32u < cand && e1 <= nd));
-            const float u0 = __shfl_up_sync(0xffffffffu, e0, 1), u1 = __shfl_up_sync(0xffffffffu, e1, 1);
-            const uint32_t v0 = __shfl_up_sync(0xffffffffu, i0, 1), v1 = __shfl_up_sync(0xffffffffu, i1, 1);
-            const float t31 = __shfl_sync(0xffffffffu, e0, 31);
-            const uint32_t j31 = __shfl_sync(0xffffffffu, i0, 31);
-            const float p1 = lane ? u1 : t31;
-            const uint32_t q1 = lane ? v1 : j31;
-            const uint32_t nid = x0 + b;
-            if (lane >= pos)
-            {
-               e0 = lane == pos ? nd : u0;
-               i0 = lane == pos ? nid : v0;
-            }
-            if (lane + 32u >= pos)
-            {
-               e1 = lane + 32u == pos ? nd : p1;
-               i1 = lane + 32u == pos ? nid : q1;
-            }
+            const uint32_t r = e / (16u * C), q = e % (16u * C), c = q / 16u, m = q % 16u;
+            const uint32_t dim = 32u * j + 128u * c + 2u * m;
+            const bool ok = x0 + r < n && dim < d;
+            cp_async8(dst + r * WD::kLd + c * 32u + 2u * m, ok ? p.X + size_t(first + x0 + r) * d + dim : p.X,
+                      ok ? 8u : 0u);
          }
       }
-   s_top[warp][lane] = lane < cand ? i0 : 0xFFFFFFFFu;
-   s_top[warp][32u + lane] = lane + 32u < cand ? i1 : 0xFFFFFFFFu;
+      else
+      {
+#pragma unroll
+         for (uint32_t e = tid; e < 1024u * C; e += kFbWarps * 32u)
+         {
+            const uint32_t r = e / (32u * C), q = e % (32u * C), c = q / 32u, l = q % 32u;
+            const uint32_t dim = 32u * j + 128u * c + l;
+            const bool ok = x0 + r < n && dim < d;
+            cp_async4(dst + r * WD::kLd + c * 32u + l, ok ? p.X + size_t(first + x0 + r) * d + dim : p.X,
+                      ok ? 4u : 0u);
+         }
+      }
+   };
+   const uint32_t steps = cand > 0 ? (n + 31u) / 32u : 0u;
+   const uint32_t stages = 4u * steps;
+   if (active && stages)
+      wd.issue_query(warp, first + s, lane);
+   if (stages > 0u)
+      issue(0u, 0u, 0u);
+   cp_commit();
+   if (stages > 1u)
+      issue(1u, 0u, 1u);
+   cp_commit();
+   float e0 = FLT_MAX, e1 = FLT_MAX; // list entries lane and lane + 32
+   uint32_t i0 = 0xFFFFFFFFu, i1 = 0xFFFFFFFFu;
+   float s02 = 0.f, s13 = 0.f;
+   uint32_t buf = 0, buf2 = 2; // buffers of stages t and t + 2
+   for (uint32_t t = 0; t < stages; ++t)
+   {
+      cp_wait<1>(); // stage t has landed (t + 1 may be in flight)
+      __syncthreads(); // ... for every thread's copies; stage t - 1's buffer is free
+      if (t + 2u < stages)
+         issue(buf2, (t + 2u) >> 2, (t + 2u) & 3u);
+      cp_commit();
+      const uint32_t j = t & 3u;
+      if (active)
+      {
+         const float ws = wd.warp_sum(buf, warp, j, lane);
+         if (j == 0u)
+            s02 = ws;
+         else if (j == 1u)
+            s13 = ws;
+         else if (j == 2u)
+            s02 = add_ftz(s02, ws);
+         else
+         {
+            const uint32_t x0 = 32u * (t >> 2), x = x0 + lane;
+            list_insert(x < n && x != s ? add_ftz(s02, add_ftz(s13, ws)) : FLT_MAX, x0, cand, lane, e0, e1, i0, i1);
+         }
+      }
+      buf = buf == 2u ? 0u : buf + 1u;
+      buf2 = buf2 == 2u ? 0u : buf2 + 1u;
+   }
+   cp_wait<0>();
+   if (!active)
+      return;
+   s_top[lane] = lane < cand ? i0 : 0xFFFFFFFFu;
+   s_top[32u + lane] = lane + 32u < cand ? i1 : 0xFFFFFFFFu;
    __syncwarp();
    if (lane == 0)
-      write_row(p, group, n, s, cand, s_top[warp]);
+      write_row(p, group, n, s, cand, s_top);
 }
+
+// Dynamic shared memory of the rerank and fallback blocks for C segments per partial:
+// every warp's stages and query buffers, then its per-row output slots.
+size_t rr_smem_bytes(uint32_t c, size_t per_warp_extra)
+{
+   const size_t warp_floats = 2 * size_t(32) * (32 * c + 2) + 2 * size_t(128) * c;
+   return kRrWarps * (warp_floats * sizeof(float) + per_warp_extra);
+}
+
+template <int C, bool PAIRS>
+cudaError_t launch_rerank_t(const KnnRerankParams &p, uint32_t num_items, cudaStream_t s)
+{
+   const size_t smem = rr_smem_bytes(C, 32 * kKnnMax * sizeof(uint32_t));
+   cudaError_t e =
+       cudaFuncSetAttribute(knn_rerank_kernel<C, PAIRS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+   if (e != cudaSuccess)
+      return e;
+   knn_rerank_kernel<C, PAIRS><<<num_items, kRrWarps * 32, smem, s>>>(p);
+   return cudaGetLastError();
+}
+
+template <int C, bool PAIRS>
+cudaError_t launch_fallback_t(const KnnParams &p, const uint32_t *d_rows, const uint32_t *d_tasks, uint32_t num_tasks,
+                              cudaStream_t s)
+{
+   const size_t smem = (3 * size_t(WarpDist<C, PAIRS>::kStage) + kFbWarps * size_t(WarpDist<C, PAIRS>::kQ)) * sizeof(float) +
+                       kFbWarps * kKnnMax * sizeof(uint32_t);
+   cudaError_t e = cudaFuncSetAttribute(knn_fallback_rows_kernel<C, PAIRS>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+   if (e != cudaSuccess)
+      return e;
+   knn_fallback_rows_kernel<C, PAIRS><<<num_tasks, kFbWarps * 32, smem, s>>>(p, d_rows, d_tasks);
+   return cudaGetLastError();
+}
+
+// 8-byte copies need an even dimension and an 8-byte aligned base.
+bool rr_pairs(const KnnParams &p) { return (p.d % 2u) == 0 && (reinterpret_cast<uintptr_t>(p.X) % 8u) == 0; }
 
 } // namespace
 
-cudaError_t launch_knn_fallback_rows(const KnnParams &p, const uint32_t *d_rows, uint32_t count, cudaStream_t s)
+uint32_t knn_fallback_rows_per_task() { return kFbWarps; }
+
+cudaError_t launch_knn_fallback_rows(const KnnParams &p, const uint32_t *d_rows, const uint32_t *d_tasks,
+                                     uint32_t num_tasks, cudaStream_t s)
 {
-   if (count == 0)
+   if (num_tasks == 0)
       return cudaSuccess;
-   if (p.d > uint32_t(kRrMaxDim))
+   if (p.d > uint32_t(kRrMaxDim) || p.d == 0)
       return cudaErrorInvalidValue;
-   knn_fallback_rows_kernel<<<(count + kRrWarps - 1) / kRrWarps, kRrWarps * 32, 0, s>>>(p, d_rows, count);
-   return cudaGetLastError();
+   const uint32_t c = (p.d + 127) / 128;
+   const bool pairs = rr_pairs(p);
+   if (c == 1)
+      return pairs ? launch_fallback_t<1, true>(p, d_rows, d_tasks, num_tasks, s)
+                   : launch_fallback_t<1, false>(p, d_rows, d_tasks, num_tasks, s);
+   if (c == 2)
+      return pairs ? launch_fallback_t<2, true>(p, d_rows, d_tasks, num_tasks, s)
+                   : launch_fallback_t<2, false>(p, d_rows, d_tasks, num_tasks, s);
+   return pairs ? launch_fallback_t<3, true>(p, d_rows, d_tasks, num_tasks, s)
+                : launch_fallback_t<3, false>(p, d_rows, d_tasks, num_tasks, s);
 }
 
 cudaError_t launch_knn_rerank(const KnnRerankParams &p, uint32_t num_items, cudaStream_t s)
 {
    if (num_items == 0)
       return cudaSuccess;
-   if (p.p.d > uint32_t(kRrMaxDim))
+   if (p.p.d > uint32_t(kRrMaxDim) || p.p.d == 0)
       return cudaErrorInvalidValue;
-   knn_rerank_kernel<<<num_items, kRrWarps * 32, 0, s>>>(p);
-   return cudaGetLastError();
+   const uint32_t c = (p.p.d + 127) / 128;
+   const bool pairs = rr_pairs(p.p);
+   if (c == 1)
+      return pairs ? launch_rerank_t<1, true>(p, num_items, s) : launch_rerank_t<1, false>(p, num_items, s);
+   if (c == 2)
+      return pairs ? launch_rerank_t<2, true>(p, num_items, s) : launch_rerank_t<2, false>(p, num_items, s);
+   return pairs ? launch_rerank_t<3, true>(p, num_items, s) : launch_rerank_t<3, false>(p, num_items, s);
 }
 
 size_t knn_smem_bytes(uint32_t d)

@@ -60,7 +60,11 @@ def _cfg(k, deg, head, tail, slots, bidir, stride):
 ROUTES = {"tensor": nat.ROUTE_TENSOR, "exact": nat.ROUTE_EXACT}
 
 
-@pytest.mark.parametrize("d", [13, 96, 128, 200])
+# dims: one to three 128-dim segments per partial, odd and even (4- and 8-byte copies)
+DIMS = [13, 96, 128, 200, 259, 300]
+
+
+@pytest.mark.parametrize("d", DIMS)
 @pytest.mark.parametrize("name", list(CONFIGS))
 @pytest.mark.parametrize("route", list(ROUTES))
 def test_exact_knn_graph_matches_oracle(ctx, d, name, route):
@@ -91,7 +95,7 @@ def run_against_oracle(ctx, d, name, route=nat.ROUTE_AUTO):
     return X, ranges, cfg, got
 
 
-@pytest.mark.parametrize("d", [13, 96, 128, 200])
+@pytest.mark.parametrize("d", DIMS)
 @pytest.mark.parametrize("name", list(CONFIGS))
 @pytest.mark.parametrize("route", list(ROUTES))
 def test_exact_knn_graph_matches_reference_kernel(ctx, d, name, route):
@@ -131,7 +135,7 @@ def test_exact_knn_paths_match_oracle(ctx, monkeypatch, d, name, path):
     run_against_oracle(ctx, d, name, nat.ROUTE_EXACT)
 
 
-@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("d", [64, 128, 300])
 def test_tensor_route_large_groups_match_oracle(ctx, d):
     """Groups of 2,000 and 9,000 points (above the exact route's matrix limit) on the tensor
     route: rows equal the oracle's; the certificate clears nearly every row."""
