@@ -24,6 +24,8 @@
 // a few hundred instructions (a fully unrolled tree missed the instruction cache).
 #include <algorithm>
 #include <cfloat>
+#include <cstdlib>
+#include <type_traits>
 
 #include "kernels.h"
 
@@ -774,21 +776,29 @@ __global__ void __launch_bounds__(kRowWarps * 32) knn_rows_kernel(const KnnParam
 // ------------------------------------------------------------------ tensor-core route
 // Distances of one query row to 32 gathered candidate rows (lane l: candidate l), in
 // the reference's block summation.  The candidates' dimensions of reference warp j
-// (dims 32 j + l + 128 c, c < C) pass through a double-buffered per-warp stage in
-// shared memory, filled by cp.async: a row segment of 32 floats is 128 contiguous bytes
-// whatever rows are gathered, so the loads are coalesced, and nothing waits on them
-// while the previous stage is summed.  The stage's row stride is 32 C + 2 floats, so
-// that the 8-byte reads of a half warp (lane l: its own candidate's row) hit 32
-// distinct banks.  Lane l evaluates the 32 partials of reference warp j for its
-// candidate as 16 packed f32x2 pairs: the fma chains over c, the first one from a zero
-// accumulator as in the reference, then the __shfl_down tree (offsets 16 .. 2 are
-// packed adds of pairs m and m + off / 2; offset 1 adds the two halves), and the warp
-// sums as (w0 + w2) + (w1 + w3).  Padding past d is zero: 0 - 0 = +0 and fma(+0, +0,
-// acc) = acc for acc >= +0, so the padded sums equal the reference's.  The zero
-// accumulator is a register the compiler cannot prove zero: a packed square written as
-// a multiply (or an fma of a known zero) followed by the tree's first packed add was
-// contracted by ptxas into one fma, one rounding fewer than the reference's, which
-// moved about one distance in eight by an ulp.
+// (dims 32 j + l + 128 c, c < C) pass through a ring of NB per-warp stages in shared
+// memory, filled by cp.async: a row segment of 32 floats is 128 contiguous bytes
+// whatever rows are gathered, so the loads are coalesced, and NB - 1 stages are in
+// flight while one is summed.  W is the copy width: 16 bytes when d is a multiple of
+// 4 and X 16-byte aligned (row stride 32 C + 4 floats: the 16-byte reads of a quarter
+// warp, lane l reading its own candidate's row, hit 32 distinct banks), else 8 or 4
+// bytes (stride 32 C + 2: the 8-byte reads of a half warp are conflict-free).  Lane l
+// evaluates the 32 partials of reference warp j for its candidate as 16 packed f32x2
+// pairs: the fma chains over c, the first one from a zero accumulator as in the
+// reference, then the __shfl_down tree (offsets 16 .. 2 are packed adds of pairs m and
+// m + off / 2; offset 1 adds the two halves), and the warp sums as (w0 + w2) + (w1 +
+// w3).  Padding past d is zero: 0 - 0 = +0 and fma(+0, +0, acc) = acc for acc >= +0,
+// so the padded sums equal the reference's.  The zero accumulator is a register the
+// compiler cannot prove zero: a packed square written as a multiply (or an fma of a
+// known zero) followed by the tree's first packed add was contracted by ptxas into one
+// fma, one rounding fewer than the reference's, which moved about one distance in
+// eight by an ulp.
+__device__ __forceinline__ void cp_async16(float *dst, const float *src, uint32_t bytes)
+{
+   asm volatile("cp.async.ca.shared.global [%0], [%1], 16, %2;\n" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+                "l"(__cvta_generic_to_global(src)), "r"(bytes)
+                : "memory");
+}
 __device__ __forceinline__ void cp_async8(float *dst, const float *src, uint32_t bytes)
 {
    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
@@ -810,51 +820,75 @@ __device__ __forceinline__ void cp_wait()
 
 constexpr uint32_t kNoRow = 0xFFFFFFFFu;
 
-// C = ceil(d / 128) segments per partial; PAIRS: 8-byte copies (d even and X 8-byte
-// aligned), else 4-byte copies.
-template <int C, bool PAIRS>
+// Copy of W bytes (W / 4 floats) at dim of row rr of X into dst; zeros when rr is
+// kNoRow or dim >= d (d a multiple of W / 4).
+template <int W>
+__device__ __forceinline__ void stage_copy(float *dst, const float *X, uint32_t d, uint32_t rr, uint32_t dim)
+{
+   const bool ok = rr != kNoRow && dim < d;
+   const float *src = ok ? X + size_t(rr) * d + dim : X;
+   if constexpr (W == 16)
+      cp_async16(dst, src, ok ? 16u : 0u);
+   else if constexpr (W == 8)
+      cp_async8(dst, src, ok ? 8u : 0u);
+   else
+      cp_async4(dst, src, ok ? 4u : 0u);
+}
+
+// C = ceil(d / 128) segments per partial; W copy bytes; NB stages in the ring.
+template <int C, int W, int NB>
 struct WarpDist
 {
-   static constexpr int kLd = 32 * C + 2;  // stage row stride (floats)
-   static constexpr int kStage = 32 * kLd; // one buffer
-   static constexpr int kQ = 128 * C;      // the query row, zero padded
-   static constexpr int kWarpFloats = 2 * kStage + 2 * kQ;
+   static constexpr int kF = W / 4;                     // floats per copy
+   static constexpr int kLd = 32 * C + (W == 16 ? 4 : 2); // stage row stride (floats)
+   static constexpr int kStage = 32 * kLd;             // one buffer
+   static constexpr int kQ = 128 * C;                  // the query row, zero padded
+   static constexpr int kWarpFloats = NB * kStage + 2 * kQ;
+   static constexpr int kCopies = 32 * 32 * C / kF;    // copies of one stage (32 rows)
 
-   float *st; // [2][32][kLd]
+   float *st; // [NB][32][kLd]
    float *sq; // [2][kQ]
    const float *X;
    uint32_t d;
    uint64_t zero; // packed (+0, +0), not known to the compiler as a constant
 
+   // Copy i of a stage: row r, float offset o within the row's 32 C staged floats.
+   __device__ __forceinline__ static void copy_slot(uint32_t i, uint32_t &r, uint32_t &o)
+   {
+      r = i / (32u * C / kF);
+      o = (i % (32u * C / kF)) * kF;
+   }
+   // Dimension of staged float o of reference warp j.
+   __device__ __forceinline__ static uint32_t stage_dim(uint32_t j, uint32_t o)
+   {
+      return 32u * j + 128u * (o / 32u) + o % 32u;
+   }
+
    // Copies of reference warp j's dimensions of candidate rows shfl(row, r) into stage buf.
    __device__ __forceinline__ void issue(uint32_t buf, uint32_t row, uint32_t j, uint32_t lane) const
    {
       float *dst = st + buf * kStage;
-      if constexpr (PAIRS)
-      {
 #pragma unroll
-         for (int i = 0; i < 16 * C; ++i)
-         {
-            const uint32_t e = lane + 32u * i;
-            const uint32_t r = e / (16u * C), q = e % (16u * C), c = q / 16u, m = q % 16u;
-            const uint32_t rr = __shfl_sync(0xffffffffu, row, r);
-            const uint32_t dim = 32u * j + 128u * c + 2u * m;
-            const bool ok = rr != kNoRow && dim < d;
-            cp_async8(dst + r * kLd + c * 32u + 2u * m, ok ? X + size_t(rr) * d + dim : X, ok ? 8u : 0u);
-         }
-      }
-      else
+      for (int k = 0; k < kCopies / 32; ++k)
       {
-#pragma unroll 8
-         for (int i = 0; i < 32 * C; ++i)
-         {
-            const uint32_t e = lane + 32u * i;
-            const uint32_t r = e / (32u * C), q = e % (32u * C), c = q / 32u, l = q % 32u;
-            const uint32_t rr = __shfl_sync(0xffffffffu, row, r);
-            const uint32_t dim = 32u * j + 128u * c + l;
-            const bool ok = rr != kNoRow && dim < d;
-            cp_async4(dst + r * kLd + c * 32u + l, ok ? X + size_t(rr) * d + dim : X, ok ? 4u : 0u);
-         }
+         uint32_t r, o;
+         copy_slot(lane + 32u * k, r, o);
+         const uint32_t rr = __shfl_sync(0xffffffffu, row, r);
+         stage_copy<W>(dst + r * kLd + o, X, d, rr, stage_dim(j, o));
+      }
+   }
+
+   // The same copies for a block of `threads` threads (thread tid) and the contiguous
+   // candidate rows first + x0 + r (r < 32, those at or past `end` are kNoRow).
+   __device__ __forceinline__ void issue_block(uint32_t buf, uint32_t first, uint32_t x0, uint32_t n, uint32_t j,
+                                               uint32_t tid, uint32_t threads) const
+   {
+      float *dst = st + buf * kStage;
+      for (uint32_t i = tid; i < uint32_t(kCopies); i += threads)
+      {
+         uint32_t r, o;
+         copy_slot(i, r, o);
+         stage_copy<W>(dst + r * kLd + o, X, d, x0 + r < n ? first + x0 + r : kNoRow, stage_dim(j, o));
       }
    }
 
@@ -862,25 +896,11 @@ struct WarpDist
    __device__ __forceinline__ void issue_query(uint32_t qb, uint32_t row, uint32_t lane) const
    {
       float *dst = sq + qb * kQ;
-      if constexpr (PAIRS)
-      {
 #pragma unroll
-         for (int i = 0; i < 2 * C; ++i)
-         {
-            const uint32_t dim = 2u * (lane + 32u * i);
-            const bool ok = dim < d;
-            cp_async8(dst + dim, ok ? X + size_t(row) * d + dim : X, ok ? 8u : 0u);
-         }
-      }
-      else
+      for (int k = 0; k < kQ / kF / 32; ++k)
       {
-#pragma unroll
-         for (int i = 0; i < 4 * C; ++i)
-         {
-            const uint32_t dim = lane + 32u * i;
-            const bool ok = dim < d;
-            cp_async4(dst + dim, ok ? X + size_t(row) * d + dim : X, ok ? 4u : 0u);
-         }
+         const uint32_t dim = kF * (lane + 32u * k);
+         stage_copy<W>(dst + dim, X, d, row, dim);
       }
    }
 
@@ -893,12 +913,26 @@ struct WarpDist
 #pragma unroll
       for (int c = 0; c < C; ++c)
 #pragma unroll
-         for (int m = 0; m < 16; ++m)
+         for (int m = 0; m < 16; m += (W == 16 ? 2 : 1))
          {
-            const uint64_t bv = *reinterpret_cast<const uint64_t *>(b + c * 32 + 2 * m);
-            const uint64_t av = *reinterpret_cast<const uint64_t *>(a + c * 128 + 2 * m);
-            const uint64_t df = sub2_ftz(av, bv);
-            v[m] = fma2_ftz(df, df, c == 0 ? zero : v[m]);
+            uint64_t bv[2], av[2];
+            if constexpr (W == 16)
+            {
+               const ulonglong2 b2 = *reinterpret_cast<const ulonglong2 *>(b + c * 32 + 2 * m);
+               const ulonglong2 a2 = *reinterpret_cast<const ulonglong2 *>(a + c * 128 + 2 * m);
+               bv[0] = b2.x, bv[1] = b2.y, av[0] = a2.x, av[1] = a2.y;
+            }
+            else
+            {
+               bv[0] = *reinterpret_cast<const uint64_t *>(b + c * 32 + 2 * m);
+               av[0] = *reinterpret_cast<const uint64_t *>(a + c * 128 + 2 * m);
+            }
+#pragma unroll
+            for (int h = 0; h < (W == 16 ? 2 : 1); ++h)
+            {
+               const uint64_t df = sub2_ftz(av[h], bv[h]);
+               v[m + h] = fma2_ftz(df, df, c == 0 ? zero : v[m + h]);
+            }
          }
 #pragma unroll
       for (int h = 8; h >= 1; h >>= 1)
@@ -910,17 +944,11 @@ struct WarpDist
 };
 
 constexpr int kRrWarps = 4;         // a block per work item: 4 warps x 32 rows
+constexpr uint32_t kTopRows = 8;    // rows whose ranked lists a warp holds before laying them out
 constexpr int kRrLists = 3;         // the prefilter's lists per row (column thirds)
 constexpr int kRrDepth = 32;        // entries per list
 constexpr int kRrEntries = kRrLists * kRrDepth;
 constexpr int kRrMaxDim = 352;      // three 128-dim segments per partial at most
-
-__device__ __forceinline__ uint64_t shfl64(uint64_t v, uint32_t src)
-{
-   const uint32_t lo = __shfl_sync(0xffffffffu, uint32_t(v), src);
-   const uint32_t hi = __shfl_sync(0xffffffffu, uint32_t(v >> 32), src);
-   return (uint64_t(hi) << 32) | lo;
-}
 
 // A block per work item (<= 128 rows of one group); warp w ranks rows 32 w .. 32 w + 31
 // one after the other, then every lane lays out one of them.  Per row: the 96 list
@@ -934,10 +962,10 @@ __device__ __forceinline__ uint64_t shfl64(uint64_t v, uint32_t src)
 // exceeds the cand-th distance no such column can enter.  A row whose lists all saw
 // every one of their columns is exact as it stands.  Rejected rows are queued for the
 // exact kernel.
-template <int C, bool PAIRS>
+template <int C, int W, int NB>
 __global__ void __launch_bounds__(kRrWarps * 32) knn_rerank_kernel(const KnnRerankParams rp)
 {
-   using WD = WarpDist<C, PAIRS>;
+   using WD = WarpDist<C, W, NB>;
    extern __shared__ __align__(16) float rr_smem[];
    if (*reinterpret_cast<const volatile int *>(rp.status) != 0)
       return; // an aborted prefilter left the lists unwritten
@@ -947,9 +975,10 @@ __global__ void __launch_bounds__(kRrWarps * 32) knn_rerank_kernel(const KnnRera
    const uint32_t group = sg.group_id - 1u;
    const uint32_t first = p.ranges[2 * group], end = p.ranges[2 * group + 1], n = end - first;
    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-   const WD wd{rr_smem + warp * WD::kWarpFloats, rr_smem + warp * WD::kWarpFloats + 2 * WD::kStage, p.X, p.d,
+   const WD wd{rr_smem + warp * WD::kWarpFloats, rr_smem + warp * WD::kWarpFloats + NB * WD::kStage, p.X, p.d,
                uint64_t(p.d >> 31)};
-   uint32_t *s_top = reinterpret_cast<uint32_t *>(rr_smem + kRrWarps * WD::kWarpFloats) + warp * (32 * kKnnMax);
+   // the ranked lists of the warp's rows in flight: kTopRows rows, laid out together
+   uint32_t *s_top = reinterpret_cast<uint32_t *>(rr_smem + kRrWarps * WD::kWarpFloats) + warp * (kTopRows * kKnnMax);
    uint32_t cand = p.candidate_k > 0 ? p.candidate_k - 1 : 0;
    cand = min(cand, uint32_t(kKnnMax));
    cand = min(cand, n > 0 ? n - 1 : 0u);
@@ -983,38 +1012,62 @@ __global__ void __launch_bounds__(kRrWarps * 32) knn_rerank_kernel(const KnnRera
          c[e] = v < end && v >= first && v != row ? v : kNoRow;
       }
    };
+   // the certificate's inputs of a row: each list's last key (+inf when the list saw every
+   // one of its columns) and the row's squared norm, loaded a row ahead
+   auto cert_inputs = [&](uint32_t rr, float (&lk)[kRrLists], float &qn) {
+      const uint32_t row = w.row_begin + r0 + rr, sl = row - first;
+      const uint32_t self_list = ((sl % 192u) / 32u) % 3u;
+      const float *kp = rp.cand_key + size_t(row) * kRrEntries;
+#pragma unroll
+      for (int f = 0; f < kRrLists; ++f)
+         // list f dropped a column only when it saw more than 32 (every column it
+         // dropped has a key >= its last one)
+         lk[f] = seen[f] - (uint32_t(f) == self_list ? 1u : 0u) > uint32_t(kRrDepth) ? __ldg(kp + 32 * f + 31)
+                                                                                         : INFINITY;
+      qn = __ldg(rp.xnorm + row);
+   };
    uint32_t cur[kRrLists], nxt[kRrLists];
+   float ck[kRrLists], nk[kRrLists], cqn = 0.f, nqn = 0.f;
+   const uint32_t stages = 12u * nrows; // (row, list, reference warp)
+   // stage t1 of row rr1 (the current row rr or the next one) into its ring slot
+   auto issue_stage = [&](uint32_t t1, uint32_t rr) {
+      const uint32_t set1 = t1 >> 2, rr1 = set1 / 3u, e1 = set1 % 3u;
+      const uint32_t *src = rr1 == rr ? cur : nxt;
+      const uint32_t row1 = e1 == 0u ? src[0] : (e1 == 1u ? src[1] : src[2]);
+      if ((t1 % 12u) == 0u)
+         wd.issue_query(rr1 & 1u, w.row_begin + r0 + rr1, lane);
+      wd.issue(t1 % uint32_t(NB), row1, t1 & 3u, lane);
+   };
    if (nrows)
    {
       cand_rows(0, cur);
-      wd.issue_query(0, w.row_begin + r0, lane);
-      wd.issue(0, cur[0], 0, lane);
-      cp_commit();
+      cert_inputs(0, ck, cqn);
       if (nrows > 1)
+      {
          cand_rows(1, nxt);
+         cert_inputs(1, nk, nqn);
+      }
+   }
+   // the ring starts with stages 0 .. NB - 2 in flight (one commit group each)
+#pragma unroll
+   for (uint32_t t1 = 0; t1 + 1u < uint32_t(NB); ++t1)
+   {
+      if (t1 < stages)
+         issue_stage(t1, 0u);
+      cp_commit();
    }
    float D[kRrLists] = {INFINITY, INFINITY, INFINITY};
    float s02 = 0.f, s13 = 0.f;
-   const uint32_t stages = 12u * nrows; // (row, list, reference warp)
    for (uint32_t t = 0; t < stages; ++t)
    {
       const uint32_t j = t & 3u, set = t >> 2, rr = set / 3u, e = set % 3u;
-      const uint32_t t1 = t + 1u;
+      const uint32_t t1 = t + uint32_t(NB) - 1u; // its slot held stage t - 1, summed
       if (t1 < stages)
-      {
-         const uint32_t set1 = t1 >> 2, rr1 = set1 / 3u, e1 = set1 % 3u;
-         const uint32_t *src = rr1 == rr ? cur : nxt;
-         const uint32_t row1 = e1 == 0u ? src[0] : (e1 == 1u ? src[1] : src[2]);
-         if (rr1 != rr)
-            wd.issue_query(rr1 & 1u, w.row_begin + r0 + rr1, lane);
-         wd.issue(t1 & 1u, row1, t1 & 3u, lane);
-         cp_commit();
-         cp_wait<1>();
-      }
-      else
-         cp_wait<0>();
+         issue_stage(t1, rr);
+      cp_commit();
+      cp_wait<NB - 1>(); // stage t has landed
       __syncwarp();
-      const float ws = wd.warp_sum(t & 1u, rr & 1u, j, lane);
+      const float ws = wd.warp_sum(t % uint32_t(NB), rr & 1u, j, lane);
       __syncwarp();
       if (j == 0u)
          s02 = ws;
@@ -1039,39 +1092,66 @@ __global__ void __launch_bounds__(kRrWarps * 32) knn_rerank_kernel(const KnnRera
       // ---- row rr complete: rank, lay out, certify
       const uint32_t row = w.row_begin + r0 + rr; // global row of X
       const uint32_t s = row - first;             // local row
-      const float *kp = rp.cand_key + size_t(row) * kRrEntries;
-      uint64_t key[kRrLists];
-      uint32_t id[kRrLists];
-      float T = INFINITY; // smallest last key of a list that dropped a column
-      const uint32_t self_list = ((s % 192u) / 32u) % 3u;
+      uint32_t db[kRrLists], id[kRrLists];
+      const float T = fminf(ck[0], fminf(ck[1], ck[2])); // smallest last key of a list that dropped a column
+      const float qn_row = cqn;
 #pragma unroll
       for (int f = 0; f < kRrLists; ++f)
       {
          id[f] = D[f] != INFINITY ? cur[f] - first : 0xFFFFFFFFu;
-         key[f] = D[f] != INFINITY ? (uint64_t(__float_as_uint(D[f])) << 32) | id[f] : ~0ull;
-         // list f dropped a column only when it saw more than 32 (every column it
-         // dropped has a key >= its last one)
-         if (seen[f] - (uint32_t(f) == self_list ? 1u : 0u) > uint32_t(kRrDepth))
-            T = fminf(T, __ldg(kp + 32 * f + 31));
+         db[f] = __float_as_uint(D[f]); // non-negative: the bits order as the values
       }
-      // the next row's candidates, one row ahead of the pipeline
+      // the next row's candidates and certificate inputs, one row ahead of the pipeline
 #pragma unroll
       for (int f = 0; f < kRrLists; ++f)
+      {
          cur[f] = nxt[f];
+         ck[f] = nk[f];
+      }
+      cqn = nqn;
       if (rr + 2u < nrows)
+      {
          cand_rows(rr + 2u, nxt);
-      // rank of each entry by (distance, local id): distinct keys for valid entries
+         cert_inputs(rr + 2u, nk, nqn);
+      }
+      // rank of each entry by (distance, local id): first by distance alone; equal
+      // distances of valid entries share a rank then, which shows as a rank sum below
+      // 0 + 1 + ... + (nvalid - 1), and a second pass breaks those ties by id
       uint32_t rk[kRrLists] = {0u, 0u, 0u};
-#pragma unroll 2
+#pragma unroll 4
       for (int src = 0; src < 32; ++src)
 #pragma unroll
          for (int f = 0; f < kRrLists; ++f)
          {
-            const uint64_t k2 = shfl64(key[f], src);
+            const uint32_t d2 = __shfl_sync(0xffffffffu, db[f], src);
 #pragma unroll
             for (int e2 = 0; e2 < kRrLists; ++e2)
-               rk[e2] += k2 < key[e2] ? 1u : 0u;
+               rk[e2] += d2 < db[e2] ? 1u : 0u;
          }
+      {
+         uint32_t nv = 0, rsum = 0;
+#pragma unroll
+         for (int f = 0; f < kRrLists; ++f)
+         {
+            const bool valid = id[f] != 0xFFFFFFFFu;
+            nv += valid ? 1u : 0u;
+            rsum += valid ? rk[f] : 0u;
+         }
+         nv = __reduce_add_sync(0xffffffffu, nv);
+         rsum = __reduce_add_sync(0xffffffffu, rsum);
+         if (nv > 0 && rsum != nv * (nv - 1u) / 2u)
+#pragma unroll 1
+            for (int src = 0; src < 32; ++src)
+#pragma unroll
+               for (int f = 0; f < kRrLists; ++f)
+               {
+                  const uint32_t d2 = __shfl_sync(0xffffffffu, db[f], src);
+                  const uint32_t i2 = __shfl_sync(0xffffffffu, id[f], src);
+#pragma unroll
+                  for (int e2 = 0; e2 < kRrLists; ++e2)
+                     rk[e2] += d2 == db[e2] && i2 < id[e2] ? 1u : 0u;
+               }
+      }
       uint32_t nvalid = 0, have_k = 0;
       float dk = INFINITY;
 #pragma unroll
@@ -1080,7 +1160,7 @@ __global__ void __launch_bounds__(kRrWarps * 32) knn_rerank_kernel(const KnnRera
          const bool valid = id[f] != 0xFFFFFFFFu;
          nvalid += __popc(__ballot_sync(0xffffffffu, valid));
          if (valid && rk[f] < cand)
-            s_top[rr * kKnnMax + rk[f]] = id[f];
+            s_top[(rr % kTopRows) * kKnnMax + rk[f]] = id[f];
          const uint32_t at = __ballot_sync(0xffffffffu, valid && cand > 0 && rk[f] == cand - 1u);
          if (at)
          {
@@ -1089,7 +1169,7 @@ __global__ void __launch_bounds__(kRrWarps * 32) knn_rerank_kernel(const KnnRera
          }
       }
       for (uint32_t q = nvalid + lane; q < cand; q += 32)
-         s_top[rr * kKnnMax + q] = 0xFFFFFFFFu; // the reference's unfilled list slots
+         s_top[(rr % kTopRows) * kKnnMax + q] = 0xFFFFFFFFu; // the reference's unfilled list slots
       // certificate (warp-uniform)
       bool cert;
       if (cand == 0)
@@ -1102,7 +1182,7 @@ __global__ void __launch_bounds__(kRrWarps * 32) knn_rerank_kernel(const KnnRera
          cert = false;
       else
       {
-         const double qn = (double)__ldg(rp.xnorm + row);
+         const double qn = (double)qn_row;
          const double ahi = sqrt(qn * (1.0 + rp.gd));
          const double bound = (rp.c1 * ahi * bmax + rp.c2 * bmax * bmax + rp.c3 * inv_s * (ahi + bmax) +
                                rp.c4 * inv_s * inv_s) *
@@ -1123,10 +1203,16 @@ __global__ void __launch_bounds__(kRrWarps * 32) knn_rerank_kernel(const KnnRera
             ++n_fail;
          }
       }
+      // every kTopRows rows (and after the last), lane l lays out row rr0 + l
+      if ((rr + 1u) % kTopRows == 0u || rr + 1u == nrows)
+      {
+         const uint32_t rr0 = rr - rr % kTopRows;
+         __syncwarp();
+         if (lane <= rr - rr0)
+            write_row(p, group, n, w.row_begin + r0 + rr0 + lane - first, cand, s_top + lane * kKnnMax);
+         __syncwarp();
+      }
    }
-   __syncwarp();
-   if (lane < nrows)
-      write_row(p, group, n, w.row_begin + r0 + lane - first, cand, s_top + lane * kKnnMax);
    if (lane == 0)
    {
       if (n_cert)
@@ -1184,16 +1270,16 @@ __device__ __forceinline__ void list_insert(float dist, uint32_t x0, uint32_t ca
 // ascending id (list_insert).  Then the row is laid out as every other row.
 constexpr int kFbWarps = 8;
 
-template <int C, bool PAIRS>
+template <int C, int W, int NB>
 __global__ void __launch_bounds__(kFbWarps * 32) knn_fallback_rows_kernel(const KnnParams p,
                                                                         const uint32_t *__restrict__ rows,
                                                                         const uint32_t *__restrict__ tasks)
 {
-   using WD = WarpDist<C, PAIRS>;
+   using WD = WarpDist<C, W, NB>;
    extern __shared__ __align__(16) float fb_smem[];
    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u, tid = threadIdx.x;
-   float *st = fb_smem;                                 // [3][32][kLd]
-   float *sq = fb_smem + 3 * WD::kStage;                // [kFbWarps][kQ]
+   float *st = fb_smem;                  // [NB][32][kLd]
+   float *sq = fb_smem + NB * WD::kStage; // [kFbWarps][kQ]
    uint32_t *s_top = reinterpret_cast<uint32_t *>(sq + kFbWarps * WD::kQ) + warp * kKnnMax;
    const WD wd{st, sq, p.X, p.d, uint64_t(p.d >> 31)};
    const uint32_t start = tasks[2 * blockIdx.x], cnt = tasks[2 * blockIdx.x + 1];
@@ -1204,61 +1290,33 @@ __global__ void __launch_bounds__(kFbWarps * 32) knn_fallback_rows_kernel(const 
    uint32_t cand = p.candidate_k > 0 ? p.candidate_k - 1 : 0;
    cand = min(cand, uint32_t(kKnnMax));
    cand = min(cand, n > 0 ? n - 1 : 0u);
-   const uint32_t d = p.d;
-   // copies of reference warp j's dimensions of columns 32 step .. + 31 into buffer buf
-   auto issue = [&](uint32_t buf, uint32_t step, uint32_t j) {
-      float *dst = st + buf * WD::kStage;
-      const uint32_t x0 = 32u * step;
-      if constexpr (PAIRS)
-      {
-#pragma unroll
-         for (uint32_t e = tid; e < 512u * C; e += kFbWarps * 32u)
-         {
-            const uint32_t r = e / (16u * C), q = e % (16u * C), c = q / 16u, m = q % 16u;
-            const uint32_t dim = 32u * j + 128u * c + 2u * m;
-            const bool ok = x0 + r < n && dim < d;
-            cp_async8(dst + r * WD::kLd + c * 32u + 2u * m, ok ? p.X + size_t(first + x0 + r) * d + dim : p.X,
-                      ok ? 8u : 0u);
-         }
-      }
-      else
-      {
-#pragma unroll
-         for (uint32_t e = tid; e < 1024u * C; e += kFbWarps * 32u)
-         {
-            const uint32_t r = e / (32u * C), q = e % (32u * C), c = q / 32u, l = q % 32u;
-            const uint32_t dim = 32u * j + 128u * c + l;
-            const bool ok = x0 + r < n && dim < d;
-            cp_async4(dst + r * WD::kLd + c * 32u + l, ok ? p.X + size_t(first + x0 + r) * d + dim : p.X,
-                      ok ? 4u : 0u);
-         }
-      }
-   };
    const uint32_t steps = cand > 0 ? (n + 31u) / 32u : 0u;
-   const uint32_t stages = 4u * steps;
+   const uint32_t stages = 4u * steps; // (32-column step, reference warp)
    if (active && stages)
       wd.issue_query(warp, first + s, lane);
-   if (stages > 0u)
-      issue(0u, 0u, 0u);
-   cp_commit();
-   if (stages > 1u)
-      issue(1u, 0u, 1u);
-   cp_commit();
+   // the ring starts with stages 0 .. NB - 2 in flight (one commit group each)
+#pragma unroll
+   for (uint32_t t1 = 0; t1 + 1u < uint32_t(NB); ++t1)
+   {
+      if (t1 < stages)
+         wd.issue_block(t1, first, 32u * (t1 >> 2), n, t1 & 3u, tid, kFbWarps * 32u);
+      cp_commit();
+   }
    float e0 = FLT_MAX, e1 = FLT_MAX; // list entries lane and lane + 32
    uint32_t i0 = 0xFFFFFFFFu, i1 = 0xFFFFFFFFu;
    float s02 = 0.f, s13 = 0.f;
-   uint32_t buf = 0, buf2 = 2; // buffers of stages t and t + 2
    for (uint32_t t = 0; t < stages; ++t)
    {
-      cp_wait<1>(); // stage t has landed (t + 1 may be in flight)
-      __syncthreads(); // ... for every thread's copies; stage t - 1's buffer is free
-      if (t + 2u < stages)
-         issue(buf2, (t + 2u) >> 2, (t + 2u) & 3u);
+      cp_wait<NB - 2>(); // stage t has landed (the later ones may be in flight)
+      __syncthreads(); // ... for every thread's copies; stage t - 1's slot is free
+      const uint32_t t1 = t + uint32_t(NB) - 1u;
+      if (t1 < stages)
+         wd.issue_block(t1 % uint32_t(NB), first, 32u * (t1 >> 2), n, t1 & 3u, tid, kFbWarps * 32u);
       cp_commit();
       const uint32_t j = t & 3u;
       if (active)
       {
-         const float ws = wd.warp_sum(buf, warp, j, lane);
+         const float ws = wd.warp_sum(t % uint32_t(NB), warp, j, lane);
          if (j == 0u)
             s02 = ws;
          else if (j == 1u)
@@ -1271,8 +1329,6 @@ __global__ void __launch_bounds__(kFbWarps * 32) knn_fallback_rows_kernel(const 
             list_insert(x < n && x != s ? add_ftz(s02, add_ftz(s13, ws)) : FLT_MAX, x0, cand, lane, e0, e1, i0, i1);
          }
       }
-      buf = buf == 2u ? 0u : buf + 1u;
-      buf2 = buf2 == 2u ? 0u : buf2 + 1u;
    }
    cp_wait<0>();
    if (!active)
@@ -1284,42 +1340,75 @@ __global__ void __launch_bounds__(kFbWarps * 32) knn_fallback_rows_kernel(const 
       write_row(p, group, n, s, cand, s_top);
 }
 
-// Dynamic shared memory of the rerank and fallback blocks for C segments per partial:
-// every warp's stages and query buffers, then its per-row output slots.
-size_t rr_smem_bytes(uint32_t c, size_t per_warp_extra)
+template <int C, int W, int NB>
+cudaError_t launch_rerank_nb(const KnnRerankParams &p, uint32_t num_items, cudaStream_t s)
 {
-   const size_t warp_floats = 2 * size_t(32) * (32 * c + 2) + 2 * size_t(128) * c;
-   return kRrWarps * (warp_floats * sizeof(float) + per_warp_extra);
-}
-
-template <int C, bool PAIRS>
-cudaError_t launch_rerank_t(const KnnRerankParams &p, uint32_t num_items, cudaStream_t s)
-{
-   const size_t smem = rr_smem_bytes(C, 32 * kKnnMax * sizeof(uint32_t));
+   const size_t smem = kRrWarps * (size_t(WarpDist<C, W, NB>::kWarpFloats) * sizeof(float) +
+                                   kTopRows * kKnnMax * sizeof(uint32_t));
    cudaError_t e =
-       cudaFuncSetAttribute(knn_rerank_kernel<C, PAIRS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+       cudaFuncSetAttribute(knn_rerank_kernel<C, W, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
    if (e != cudaSuccess)
       return e;
-   knn_rerank_kernel<C, PAIRS><<<num_items, kRrWarps * 32, smem, s>>>(p);
+   knn_rerank_kernel<C, W, NB><<<num_items, kRrWarps * 32, smem, s>>>(p);
    return cudaGetLastError();
 }
 
-template <int C, bool PAIRS>
+// Ring depth: UNGX_KNN_RING (2 or 3) for one segment per partial, else 2.
+template <int C, int W>
+cudaError_t launch_rerank_t(const KnnRerankParams &p, uint32_t num_items, cudaStream_t s)
+{
+   const char *env = std::getenv("UNGX_KNN_RING");
+   if (C == 1 && env && std::atoi(env) == 3)
+      return launch_rerank_nb<C, W, 3>(p, num_items, s);
+   return launch_rerank_nb<C, W, 2>(p, num_items, s);
+}
+
+template <int C, int W>
 cudaError_t launch_fallback_t(const KnnParams &p, const uint32_t *d_rows, const uint32_t *d_tasks, uint32_t num_tasks,
                               cudaStream_t s)
 {
-   const size_t smem = (3 * size_t(WarpDist<C, PAIRS>::kStage) + kFbWarps * size_t(WarpDist<C, PAIRS>::kQ)) * sizeof(float) +
+   constexpr int NB = 4;
+   using WD = WarpDist<C, W, NB>;
+   static_assert(WD::kWarpFloats > 0, "the fallback's block shares one ring");
+   const size_t smem = (NB * size_t(WD::kStage) + kFbWarps * size_t(WD::kQ)) * sizeof(float) +
                        kFbWarps * kKnnMax * sizeof(uint32_t);
-   cudaError_t e = cudaFuncSetAttribute(knn_fallback_rows_kernel<C, PAIRS>,
+   cudaError_t e = cudaFuncSetAttribute(knn_fallback_rows_kernel<C, W, NB>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
    if (e != cudaSuccess)
       return e;
-   knn_fallback_rows_kernel<C, PAIRS><<<num_tasks, kFbWarps * 32, smem, s>>>(p, d_rows, d_tasks);
+   knn_fallback_rows_kernel<C, W, NB><<<num_tasks, kFbWarps * 32, smem, s>>>(p, d_rows, d_tasks);
    return cudaGetLastError();
 }
 
-// 8-byte copies need an even dimension and an 8-byte aligned base.
-bool rr_pairs(const KnnParams &p) { return (p.d % 2u) == 0 && (reinterpret_cast<uintptr_t>(p.X) % 8u) == 0; }
+// Copy width: 16 bytes when every row starts 16-byte aligned, else 8 or 4.
+int rr_width(const KnnParams &p)
+{
+   const uintptr_t x = reinterpret_cast<uintptr_t>(p.X);
+   if (p.d % 4u == 0 && x % 16u == 0)
+      return 16;
+   if (p.d % 2u == 0 && x % 8u == 0)
+      return 8;
+   return 4;
+}
+
+// f(integral_constant<C>, integral_constant<W>) for the call's dimension and width.
+template <class F>
+cudaError_t by_dim(uint32_t d, int width, F &&f)
+{
+   const uint32_t c = (d + 127) / 128;
+   auto by_w = [&](auto C) -> cudaError_t {
+      if (width == 16)
+         return f(C, std::integral_constant<int, 16>{});
+      if (width == 8)
+         return f(C, std::integral_constant<int, 8>{});
+      return f(C, std::integral_constant<int, 4>{});
+   };
+   if (c == 1)
+      return by_w(std::integral_constant<int, 1>{});
+   if (c == 2)
+      return by_w(std::integral_constant<int, 2>{});
+   return by_w(std::integral_constant<int, 3>{});
+}
 
 } // namespace
 
@@ -1332,16 +1421,9 @@ cudaError_t launch_knn_fallback_rows(const KnnParams &p, const uint32_t *d_rows,
       return cudaSuccess;
    if (p.d > uint32_t(kRrMaxDim) || p.d == 0)
       return cudaErrorInvalidValue;
-   const uint32_t c = (p.d + 127) / 128;
-   const bool pairs = rr_pairs(p);
-   if (c == 1)
-      return pairs ? launch_fallback_t<1, true>(p, d_rows, d_tasks, num_tasks, s)
-                   : launch_fallback_t<1, false>(p, d_rows, d_tasks, num_tasks, s);
-   if (c == 2)
-      return pairs ? launch_fallback_t<2, true>(p, d_rows, d_tasks, num_tasks, s)
-                   : launch_fallback_t<2, false>(p, d_rows, d_tasks, num_tasks, s);
-   return pairs ? launch_fallback_t<3, true>(p, d_rows, d_tasks, num_tasks, s)
-                : launch_fallback_t<3, false>(p, d_rows, d_tasks, num_tasks, s);
+   return by_dim(p.d, rr_width(p), [&](auto C, auto W) {
+      return launch_fallback_t<decltype(C)::value, decltype(W)::value>(p, d_rows, d_tasks, num_tasks, s);
+   });
 }
 
 cudaError_t launch_knn_rerank(const KnnRerankParams &p, uint32_t num_items, cudaStream_t s)
@@ -1350,13 +1432,9 @@ cudaError_t launch_knn_rerank(const KnnRerankParams &p, uint32_t num_items, cuda
       return cudaSuccess;
    if (p.p.d > uint32_t(kRrMaxDim) || p.p.d == 0)
       return cudaErrorInvalidValue;
-   const uint32_t c = (p.p.d + 127) / 128;
-   const bool pairs = rr_pairs(p.p);
-   if (c == 1)
-      return pairs ? launch_rerank_t<1, true>(p, num_items, s) : launch_rerank_t<1, false>(p, num_items, s);
-   if (c == 2)
-      return pairs ? launch_rerank_t<2, true>(p, num_items, s) : launch_rerank_t<2, false>(p, num_items, s);
-   return pairs ? launch_rerank_t<3, true>(p, num_items, s) : launch_rerank_t<3, false>(p, num_items, s);
+   return by_dim(p.p.d, rr_width(p.p), [&](auto C, auto W) {
+      return launch_rerank_t<decltype(C)::value, decltype(W)::value>(p, num_items, s);
+   });
 }
 
 size_t knn_smem_bytes(uint32_t d)

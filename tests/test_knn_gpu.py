@@ -60,8 +60,8 @@ def _cfg(k, deg, head, tail, slots, bidir, stride):
 ROUTES = {"tensor": nat.ROUTE_TENSOR, "exact": nat.ROUTE_EXACT}
 
 
-# dims: one to three 128-dim segments per partial, odd and even (4- and 8-byte copies)
-DIMS = [13, 96, 128, 200, 259, 300]
+# dims: one to three 128-dim segments per partial; 4-, 8- and 16-byte staging copies
+DIMS = [13, 96, 98, 128, 200, 259, 262, 300]
 
 
 @pytest.mark.parametrize("d", DIMS)
