@@ -470,10 +470,11 @@ class Context:
 
     def knn_phase_ms(self) -> dict:
         """Device time of the last kNN seeding by phase (prefilter, rerank, fallback: the
-        tensor route's; whole: the call)."""
-        out = (c_double * 4)()
+        tensor route's; whole: the call; the gaps before the prefilter and the fallback)."""
+        out = (c_double * 6)()
         lib.ungx_exact_knn_phase_ms(self.h, out)
-        return {"prefilter": out[0], "rerank": out[1], "fallback": out[2], "whole": out[3]}
+        return {"prefilter": out[0], "rerank": out[1], "fallback": out[2], "whole": out[3],
+                "before_prefilter": out[4], "before_fallback": out[5]}
 
     def graph_csr_device(self, num_points: int, topk: int, d_intra_offsets: int | None, d_intra_cols: int | None,
                          d_cross_ids: int | None, with_additional: bool, d_offsets: int, d_cols: int | None,

@@ -133,7 +133,7 @@ struct ungx_context
    uint64_t mem_limit = 0; // device budget of ungx_cross_edges_build (0: free memory)
    DevBuf pass_x, pass_ids, pass_dists, pass_ranges; // capacity path
    Plan knn_plan; // tensor-core kNN seeding: items of the groups' self-joins
-   DevBuf knn_items, knn_segs, knn_chunks, knn_gmax, knn_fb, knn_fbt, knn_cnt;
+   DevBuf knn_items, knn_segs, knn_chunks, knn_gmax, knn_fb, knn_fbt, knn_fbc, knn_cnt;
    uint32_t inject = UNGX_INJECT_NONE;
    PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
    // resident base vectors (a4)
@@ -153,7 +153,8 @@ struct ungx_context
        add_res, add_off, add_cols, add_qoff, add_loff, add_from, add_to, add_stats, scan_scratch, knn_ranges, knn_base,
        knn_tasks, knn_dist, knn_dbase, knn_tiles, knn_rows;
    uint64_t knn_rejected = 0; // rows the last tensor-route kNN seeding sent to the exact kernel
-   double knn_phase_ms[4] = {}; // last kNN seeding: prefilter, rerank, fallback, whole call
+   double knn_phase_ms[6] = {}; // last kNN seeding: prefilter, rerank, fallback, whole call,
+                                // start to prefilter, rerank to fallback
    uint32_t add_n = 0;     // points of the last additional-edge build
    uint64_t add_edges = 0; // its edges
    // merged adjacency of the last ungx_build_cross_group_edges call
@@ -750,9 +751,9 @@ int run_passes(ungx_context *ctx, const float *vectors, const ungx_cross_edge_pr
 // its certificate, then the exact kernel for the rows it rejected.  Every row is written
 // by the rerank; the fallback rewrites the rejected ones.
 int run_knn_tensor(ungx_context *ctx, const std::vector<uint32_t> &ranges, uint32_t num_groups,
-                   const ungx::KnnParams &kp, cudaStream_t s, uint32_t &rejected)
+                   const ungx::KnnParams &kp, cudaStream_t s, bool &launched)
 {
-   rejected = 0;
+   launched = false;
    // the self-join problem: group g (1-based) = the caller's group g - 1, out(g) = {g}
    std::vector<uint32_t> sr(2 * (size_t(num_groups) + 1), 0u), sid(num_groups);
    std::vector<uint64_t> so(size_t(num_groups) + 2, 0u);
@@ -797,10 +798,15 @@ int run_knn_tensor(ungx_context *ctx, const std::vector<uint32_t> &ranges, uint3
    uint64_t item_rows = 0;
    for (const auto &it : plan.items)
       item_rows += it.row_count;
-   UNGX_CUDA(ctx, ctx->knn_fb.ensure(2 * sizeof(uint32_t) * std::max<uint64_t>(item_rows, 1)), "fallback list");
+   const uint64_t rows_max = std::max<uint64_t>(item_rows, 1);
+   UNGX_CUDA(ctx, ctx->knn_fb.ensure(sizeof(uint32_t) * rows_max), "fallback list");
+   UNGX_CUDA(ctx, ctx->knn_fbt.ensure(3 * sizeof(uint32_t) * rows_max), "fallback tasks");
+   UNGX_CUDA(ctx, ctx->knn_fbc.ensure(sizeof(uint32_t) * std::max<uint32_t>(num_groups, 1)), "fallback counts");
+   UNGX_CUDA(ctx, cudaMemsetAsync(ctx->knn_fbc.p, 0, sizeof(uint32_t) * num_groups, s), "fallback counts");
    UNGX_CUDA(ctx, ctx->knn_cnt.ensure(64), "counters");
    UNGX_CUDA(ctx, cudaMemsetAsync(ctx->knn_cnt.p, 0, 64, s), "counters");
-   uint32_t *cnt = ctx->knn_cnt.as<uint32_t>(); // [0] item counter [1] fb count [2] status, [4..7] u64 x2
+   // [0] item counter [2] status [3] fallback tasks, [4..7] u64 x2: certified, rejected rows
+   uint32_t *cnt = ctx->knn_cnt.as<uint32_t>();
    ungx::TcMaps maps;
    if ((st = make_map(ctx, &maps.a, ctx->Xh.p, ctx->n, ctx->dp, 128)))
       return st;
@@ -848,55 +854,45 @@ int run_knn_tensor(ungx_context *ctx, const std::vector<uint32_t> &ranges, uint3
    rp.gref = (16.0 + 2.0 * ((ctx->d + 127) / 128)) * std::ldexp(1.0, -24);
    rp.abs_err = (double(ctx->d) + 128.0) * std::ldexp(1.0, -126) * 2.0;
    rp.fb_rows = ctx->knn_fb.as<uint32_t>();
-   rp.fb_count = cnt + 1;
+   rp.fb_group_count = ctx->knn_fbc.as<uint32_t>();
    rp.counters = reinterpret_cast<unsigned long long *>(cnt + 4);
    UNGX_CUDA(ctx, ungx::launch_knn_rerank(rp, (uint32_t)plan.items.size(), s), "kNN rerank launch");
-   // rejected rows: read back (count, rows), rewrite their 64-row blocks exactly
-   uint32_t hc[3] = {0, 0, 0};
-   UNGX_CUDA(ctx, cudaMemcpyAsync(hc, cnt, sizeof(hc), cudaMemcpyDeviceToHost, s), "kNN counters");
    UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[2], s), "event");
-   if ((st = wait_event(ctx, ctx->ev[2], "kNN tensor route")))
-      return st;
+   // the rejected rows, recomputed exactly with no host round trip: each group's rows
+   // cut into tasks of a few rows, which share every staged column tile
+   UNGX_CUDA(ctx,
+             ungx::launch_knn_fallback_tasks(ctx->knn_fbc.as<uint32_t>(), num_groups, ctx->knn_fbt.as<uint32_t>(),
+                                             (uint32_t)std::min<uint64_t>(rows_max, UINT32_MAX), cnt + 3, s),
+             "kNN fallback task kernel");
+   UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[5], s), "event");
+   UNGX_CUDA(ctx,
+             ungx::launch_knn_fallback_rows(kp, ctx->knn_fb.as<uint32_t>(), ctx->knn_fbt.as<uint32_t>(), cnt + 3,
+                                            ctx->num_sms, s),
+             "kNN fallback kernel");
+   launched = true;
+   return UNGX_OK;
+}
+
+// After the tensor route's kernels are done: the prefilter's status, the rejected-row
+// count and the phase times.
+int finish_knn_tensor(ungx_context *ctx, uint64_t &rejected)
+{
+   uint32_t hc[8] = {};
+   UNGX_CUDA(ctx, cudaMemcpy(hc, ctx->knn_cnt.p, sizeof(hc), cudaMemcpyDeviceToHost), "kNN counters");
    if (hc[2] != 0)
       return fail(ctx, (int)hc[2], "kNN tensor-core kernel reported status " + std::to_string((int)hc[2]));
-   rejected = hc[1];
-   float a = 0.f, b = 0.f;
+   rejected = uint64_t(hc[6]) | (uint64_t(hc[7]) << 32);
+   float a = 0.f, b = 0.f, c = 0.f, f = 0.f, g = 0.f;
    cudaEventElapsedTime(&a, ctx->ev[3], ctx->ev[4]);
    cudaEventElapsedTime(&b, ctx->ev[4], ctx->ev[2]);
+   cudaEventElapsedTime(&c, ctx->ev[0], ctx->ev[3]);
+   cudaEventElapsedTime(&f, ctx->ev[5], ctx->ev[1]);
+   cudaEventElapsedTime(&g, ctx->ev[2], ctx->ev[5]);
    ctx->knn_phase_ms[0] = a;
    ctx->knn_phase_ms[1] = b;
-   // the rejected rows, recomputed exactly: the (group, row) list sorted by group and cut
-   // into tasks of a few rows of one group, which share every staged column tile
-   if (rejected)
-   {
-      std::vector<uint64_t> fb(rejected);
-      UNGX_CUDA(ctx, cudaMemcpy(fb.data(), ctx->knn_fb.p, size_t(rejected) * 8u, cudaMemcpyDeviceToHost),
-                "kNN fallback list");
-      // each pair reads as group | row << 32 (little-endian): order by (group, row)
-      for (uint64_t &v : fb)
-         v = (v << 32) | (v >> 32);
-      std::sort(fb.begin(), fb.end());
-      std::vector<uint32_t> rows(2 * size_t(rejected)), tasks;
-      const uint32_t per = ungx::knn_fallback_rows_per_task();
-      for (size_t i = 0; i < fb.size(); ++i)
-      {
-         rows[2 * i] = uint32_t(fb[i] >> 32);
-         rows[2 * i + 1] = uint32_t(fb[i]);
-         if (i == 0 || rows[2 * i] != rows[2 * i - 2] || tasks.back() == per)
-            tasks.insert(tasks.end(), {uint32_t(i), 0u});
-         ++tasks.back();
-      }
-      if ((st = upload(ctx, ctx->knn_fb, rows, "kNN fallback list")) ||
-          (st = upload(ctx, ctx->knn_fbt, tasks, "kNN fallback tasks")))
-         return st;
-      UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[5], s), "event");
-      UNGX_CUDA(ctx,
-                ungx::launch_knn_fallback_rows(kp, ctx->knn_fb.as<uint32_t>(), ctx->knn_fbt.as<uint32_t>(),
-                                               (uint32_t)(tasks.size() / 2), s),
-                "kNN fallback kernel");
-   }
-   else
-      UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[5], s), "event");
+   ctx->knn_phase_ms[2] = f;
+   ctx->knn_phase_ms[4] = c;
+   ctx->knn_phase_ms[5] = g;
    return UNGX_OK;
 }
 } // namespace
@@ -988,7 +984,7 @@ int ungx_context_destroy(ungx_context *ctx)
                      &ctx->knn_rows, &ctx->intra_off, &ctx->intra_cols, &ctx->graph_off, &ctx->graph_cols,
                      &ctx->own_runs, &ctx->all_runs, &ctx->recv, &ctx->pass_x, &ctx->pass_ids, &ctx->pass_dists,
                      &ctx->pass_ranges, &ctx->knn_items, &ctx->knn_segs, &ctx->knn_chunks, &ctx->knn_gmax,
-                     &ctx->knn_fb, &ctx->knn_fbt, &ctx->knn_cnt})
+                     &ctx->knn_fb, &ctx->knn_fbt, &ctx->knn_fbc, &ctx->knn_cnt})
       b->release();
    ctx->host_stage.release();
    for (auto &ev : ctx->ev)
@@ -2023,11 +2019,11 @@ void ungx_exact_knn_default_config(uint32_t candidate_k, uint32_t final_degree, 
 
 uint64_t ungx_exact_knn_rejected_rows(const ungx_context *ctx) { return ctx ? ctx->knn_rejected : 0; }
 
-void ungx_exact_knn_phase_ms(const ungx_context *ctx, double out[4])
+void ungx_exact_knn_phase_ms(const ungx_context *ctx, double out[6])
 {
    if (!out)
       return;
-   for (int i = 0; i < 4; ++i)
+   for (int i = 0; i < 6; ++i)
       out[i] = ctx ? ctx->knn_phase_ms[i] : 0.0;
 }
 
@@ -2100,12 +2096,11 @@ int ungx_exact_knn_graph_device(ungx_context *ctx, uint32_t num_groups, const ui
    for (double &v : ctx->knn_phase_ms)
       v = 0.0;
    const uint32_t route = cfg->route == UNGX_ROUTE_AUTO ? uint32_t(UNGX_ROUTE_TENSOR) : cfg->route;
+   bool tensor_launched = false;
    if (route == UNGX_ROUTE_TENSOR)
    {
-      uint32_t rejected = 0;
-      if ((st = run_knn_tensor(ctx, ranges, num_groups, kp, s, rejected)))
+      if ((st = run_knn_tensor(ctx, ranges, num_groups, kp, s, tensor_launched)))
          return st;
-      ctx->knn_rejected = rejected;
    }
    else if (max_n > std::min<uint64_t>(dist_max_n, ungx::kKnnDistMaxN))
    {
@@ -2180,12 +2175,8 @@ int ungx_exact_knn_graph_device(ungx_context *ctx, uint32_t num_groups, const ui
       return st;
    float ms = 0;
    cudaEventElapsedTime(&ms, ctx->ev[0], ctx->ev[1]);
-   if (route == UNGX_ROUTE_TENSOR)
-   {
-      float f = 0;
-      cudaEventElapsedTime(&f, ctx->ev[5], ctx->ev[1]);
-      ctx->knn_phase_ms[2] = f;
-   }
+   if (tensor_launched && (st = finish_knn_tensor(ctx, ctx->knn_rejected)))
+      return st;
    ctx->knn_phase_ms[3] = ms;
    if (kernel_ms)
       *kernel_ms = ms;

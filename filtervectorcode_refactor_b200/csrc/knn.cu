@@ -1197,9 +1197,8 @@ __global__ void __launch_bounds__(kRrWarps * 32) knn_rerank_kernel(const KnnRera
             ++n_cert;
          else
          {
-            const uint32_t pos = atomicAdd(rp.fb_count, 1u);
-            rp.fb_rows[2 * pos] = group;
-            rp.fb_rows[2 * pos + 1] = s;
+            const uint32_t slot = atomicAdd(rp.fb_group_count + group, 1u);
+            rp.fb_rows[p.base[group] + slot] = s;
             ++n_fail;
          }
       }
@@ -1262,18 +1261,20 @@ __device__ __forceinline__ void list_insert(float dist, uint32_t x0, uint32_t ca
    }
 }
 
-// Rows the certificate rejected, in tasks of up to kFbWarps rows of one group (rows
-// sorted by group, task = (first entry, count)): warp w takes the task's row w, and
-// every 32-column step of the group passes once through a block-wide staged pipeline
-// (three buffers, one barrier per stage) shared by the task's rows.  Lane l sums
-// column x0 + l for its warp's row; the passing columns of a step are inserted in
-// ascending id (list_insert).  Then the row is laid out as every other row.
+// Rows the certificate rejected, in tasks of up to kFbWarps rows of one group (task =
+// (group, first slot, rows); the rows' local ids at fb_rows[base[group] + slot]): warp w
+// takes the task's row w, and every 32-column step of the group passes once through a
+// block-wide staged ring (NB stages, one barrier per stage) shared by the task's rows.
+// Lane l sums column x0 + l for its warp's row; the passing columns of a step are
+// inserted in ascending id (list_insert).  Then the row is laid out as every other row.
+// A persistent grid takes the tasks in turn; their number is read on the device.
 constexpr int kFbWarps = 8;
 
 template <int C, int W, int NB>
 __global__ void __launch_bounds__(kFbWarps * 32) knn_fallback_rows_kernel(const KnnParams p,
-                                                                        const uint32_t *__restrict__ rows,
-                                                                        const uint32_t *__restrict__ tasks)
+                                                                        const uint32_t *__restrict__ fb_rows,
+                                                                        const uint32_t *__restrict__ tasks,
+                                                                        const uint32_t *__restrict__ num_tasks)
 {
    using WD = WarpDist<C, W, NB>;
    extern __shared__ __align__(16) float fb_smem[];
@@ -1282,62 +1283,111 @@ __global__ void __launch_bounds__(kFbWarps * 32) knn_fallback_rows_kernel(const 
    float *sq = fb_smem + NB * WD::kStage; // [kFbWarps][kQ]
    uint32_t *s_top = reinterpret_cast<uint32_t *>(sq + kFbWarps * WD::kQ) + warp * kKnnMax;
    const WD wd{st, sq, p.X, p.d, uint64_t(p.d >> 31)};
-   const uint32_t start = tasks[2 * blockIdx.x], cnt = tasks[2 * blockIdx.x + 1];
-   const uint32_t group = rows[2 * start];
-   const uint32_t first = p.ranges[2 * group], n = p.ranges[2 * group + 1] - first;
-   const bool active = warp < cnt;
-   const uint32_t s = active ? rows[2 * (start + warp) + 1] : 0u;
-   uint32_t cand = p.candidate_k > 0 ? p.candidate_k - 1 : 0;
-   cand = min(cand, uint32_t(kKnnMax));
-   cand = min(cand, n > 0 ? n - 1 : 0u);
-   const uint32_t steps = cand > 0 ? (n + 31u) / 32u : 0u;
-   const uint32_t stages = 4u * steps; // (32-column step, reference warp)
-   if (active && stages)
-      wd.issue_query(warp, first + s, lane);
-   // the ring starts with stages 0 .. NB - 2 in flight (one commit group each)
+   const uint32_t ntask = *num_tasks;
+   for (uint32_t task = blockIdx.x; task < ntask; task += gridDim.x)
+   {
+      __syncthreads(); // the previous task's ring is no longer read
+      const uint32_t group = tasks[3 * task], slot0 = tasks[3 * task + 1], cnt = tasks[3 * task + 2];
+      const uint32_t first = p.ranges[2 * group], n = p.ranges[2 * group + 1] - first;
+      const bool active = warp < cnt;
+      const uint32_t s = active ? fb_rows[p.base[group] + slot0 + warp] : 0u;
+      uint32_t cand = p.candidate_k > 0 ? p.candidate_k - 1 : 0;
+      cand = min(cand, uint32_t(kKnnMax));
+      cand = min(cand, n > 0 ? n - 1 : 0u);
+      const uint32_t steps = cand > 0 ? (n + 31u) / 32u : 0u;
+      const uint32_t stages = 4u * steps; // (32-column step, reference warp)
+      if (active && stages)
+         wd.issue_query(warp, first + s, lane);
+      // the ring starts with stages 0 .. NB - 2 in flight (one commit group each)
 #pragma unroll
-   for (uint32_t t1 = 0; t1 + 1u < uint32_t(NB); ++t1)
-   {
-      if (t1 < stages)
-         wd.issue_block(t1, first, 32u * (t1 >> 2), n, t1 & 3u, tid, kFbWarps * 32u);
-      cp_commit();
-   }
-   float e0 = FLT_MAX, e1 = FLT_MAX; // list entries lane and lane + 32
-   uint32_t i0 = 0xFFFFFFFFu, i1 = 0xFFFFFFFFu;
-   float s02 = 0.f, s13 = 0.f;
-   for (uint32_t t = 0; t < stages; ++t)
-   {
-      cp_wait<NB - 2>(); // stage t has landed (the later ones may be in flight)
-      __syncthreads(); // ... for every thread's copies; stage t - 1's slot is free
-      const uint32_t t1 = t + uint32_t(NB) - 1u;
-      if (t1 < stages)
-         wd.issue_block(t1 % uint32_t(NB), first, 32u * (t1 >> 2), n, t1 & 3u, tid, kFbWarps * 32u);
-      cp_commit();
-      const uint32_t j = t & 3u;
-      if (active)
+      for (uint32_t t1 = 0; t1 + 1u < uint32_t(NB); ++t1)
       {
-         const float ws = wd.warp_sum(t % uint32_t(NB), warp, j, lane);
-         if (j == 0u)
-            s02 = ws;
-         else if (j == 1u)
-            s13 = ws;
-         else if (j == 2u)
-            s02 = add_ftz(s02, ws);
-         else
+         if (t1 < stages)
+            wd.issue_block(t1, first, 32u * (t1 >> 2), n, t1 & 3u, tid, kFbWarps * 32u);
+         cp_commit();
+      }
+      float e0 = FLT_MAX, e1 = FLT_MAX; // list entries lane and lane + 32
+      uint32_t i0 = 0xFFFFFFFFu, i1 = 0xFFFFFFFFu;
+      float s02 = 0.f, s13 = 0.f;
+      for (uint32_t t = 0; t < stages; ++t)
+      {
+         cp_wait<NB - 2>(); // stage t has landed (the later ones may be in flight)
+         __syncthreads();   // ... for every thread's copies; stage t - 1's slot is free
+         const uint32_t t1 = t + uint32_t(NB) - 1u;
+         if (t1 < stages)
+            wd.issue_block(t1 % uint32_t(NB), first, 32u * (t1 >> 2), n, t1 & 3u, tid, kFbWarps * 32u);
+         cp_commit();
+         const uint32_t j = t & 3u;
+         if (active)
          {
-            const uint32_t x0 = 32u * (t >> 2), x = x0 + lane;
-            list_insert(x < n && x != s ? add_ftz(s02, add_ftz(s13, ws)) : FLT_MAX, x0, cand, lane, e0, e1, i0, i1);
+            const float ws = wd.warp_sum(t % uint32_t(NB), warp, j, lane);
+            if (j == 0u)
+               s02 = ws;
+            else if (j == 1u)
+               s13 = ws;
+            else if (j == 2u)
+               s02 = add_ftz(s02, ws);
+            else
+            {
+               const uint32_t x0 = 32u * (t >> 2), x = x0 + lane;
+               list_insert(x < n && x != s ? add_ftz(s02, add_ftz(s13, ws)) : FLT_MAX, x0, cand, lane, e0, e1, i0,
+                           i1);
+            }
          }
       }
+      cp_wait<0>();
+      if (active)
+      {
+         s_top[lane] = lane < cand ? i0 : 0xFFFFFFFFu;
+         s_top[32u + lane] = lane + 32u < cand ? i1 : 0xFFFFFFFFu;
+         __syncwarp();
+         if (lane == 0)
+            write_row(p, group, n, s, cand, s_top);
+         __syncwarp();
+      }
    }
-   cp_wait<0>();
-   if (!active)
-      return;
-   s_top[lane] = lane < cand ? i0 : 0xFFFFFFFFu;
-   s_top[32u + lane] = lane + 32u < cand ? i1 : 0xFFFFFFFFu;
-   __syncwarp();
-   if (lane == 0)
-      write_row(p, group, n, s, cand, s_top);
+}
+
+// One block: group g's fb_group_count[g] rejected rows become ceil(count / kFbWarps)
+// tasks (group, first slot, rows), in group order (a block-wide scan of the groups'
+// task counts gives each thread's first task).
+constexpr uint32_t kFbTaskThreads = 1024;
+
+__global__ void __launch_bounds__(kFbTaskThreads) knn_fallback_tasks_kernel(const uint32_t *__restrict__ group_count,
+                                                                            uint32_t G, uint32_t *__restrict__ tasks,
+                                                                            uint32_t max_tasks,
+                                                                            uint32_t *__restrict__ num_tasks)
+{
+   __shared__ uint32_t s_sum[kFbTaskThreads];
+   const uint32_t tid = threadIdx.x;
+   const uint32_t per = (G + kFbTaskThreads - 1) / kFbTaskThreads;
+   const uint32_t g0 = min(G, tid * per), g1 = min(G, g0 + per);
+   uint32_t local = 0;
+   for (uint32_t g = g0; g < g1; ++g)
+      local += (group_count[g] + kFbWarps - 1) / kFbWarps;
+   s_sum[tid] = local;
+   __syncthreads();
+   for (uint32_t off = 1; off < kFbTaskThreads; off <<= 1)
+   {
+      const uint32_t v = tid >= off ? s_sum[tid - off] : 0u;
+      __syncthreads();
+      s_sum[tid] += v;
+      __syncthreads();
+   }
+   uint32_t at = s_sum[tid] - local;
+   for (uint32_t g = g0; g < g1; ++g)
+   {
+      const uint32_t c = group_count[g];
+      for (uint32_t k = 0; k < c; k += kFbWarps, ++at)
+         if (at < max_tasks)
+         {
+            tasks[3 * at] = g;
+            tasks[3 * at + 1] = k;
+            tasks[3 * at + 2] = min(uint32_t(kFbWarps), c - k);
+         }
+   }
+   if (tid == kFbTaskThreads - 1)
+      *num_tasks = min(s_sum[tid], max_tasks);
 }
 
 template <int C, int W, int NB>
@@ -1364,19 +1414,23 @@ cudaError_t launch_rerank_t(const KnnRerankParams &p, uint32_t num_items, cudaSt
 }
 
 template <int C, int W>
-cudaError_t launch_fallback_t(const KnnParams &p, const uint32_t *d_rows, const uint32_t *d_tasks, uint32_t num_tasks,
-                              cudaStream_t s)
+cudaError_t launch_fallback_t(const KnnParams &p, const uint32_t *d_fb_rows, const uint32_t *d_tasks,
+                              const uint32_t *d_num_tasks, uint32_t num_sms, cudaStream_t s)
 {
    constexpr int NB = 4;
    using WD = WarpDist<C, W, NB>;
    static_assert(WD::kWarpFloats > 0, "the fallback's block shares one ring");
    const size_t smem = (NB * size_t(WD::kStage) + kFbWarps * size_t(WD::kQ)) * sizeof(float) +
                        kFbWarps * kKnnMax * sizeof(uint32_t);
-   cudaError_t e = cudaFuncSetAttribute(knn_fallback_rows_kernel<C, W, NB>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+   auto kern = knn_fallback_rows_kernel<C, W, NB>;
+   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
    if (e != cudaSuccess)
       return e;
-   knn_fallback_rows_kernel<C, W, NB><<<num_tasks, kFbWarps * 32, smem, s>>>(p, d_rows, d_tasks);
+   int per_sm = 0;
+   if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kFbWarps * 32, smem)) != cudaSuccess)
+      return e;
+   const uint32_t grid = std::max<uint32_t>(1u, num_sms) * uint32_t(std::max(per_sm, 1));
+   kern<<<grid, kFbWarps * 32, smem, s>>>(p, d_fb_rows, d_tasks, d_num_tasks);
    return cudaGetLastError();
 }
 
@@ -1412,17 +1466,21 @@ cudaError_t by_dim(uint32_t d, int width, F &&f)
 
 } // namespace
 
-uint32_t knn_fallback_rows_per_task() { return kFbWarps; }
-
-cudaError_t launch_knn_fallback_rows(const KnnParams &p, const uint32_t *d_rows, const uint32_t *d_tasks,
-                                     uint32_t num_tasks, cudaStream_t s)
+cudaError_t launch_knn_fallback_tasks(const uint32_t *d_group_count, uint32_t num_groups, uint32_t *d_tasks,
+                                      uint32_t max_tasks, uint32_t *d_num_tasks, cudaStream_t s)
 {
-   if (num_tasks == 0)
-      return cudaSuccess;
+   knn_fallback_tasks_kernel<<<1, kFbTaskThreads, 0, s>>>(d_group_count, num_groups, d_tasks, max_tasks, d_num_tasks);
+   return cudaGetLastError();
+}
+
+cudaError_t launch_knn_fallback_rows(const KnnParams &p, const uint32_t *d_fb_rows, const uint32_t *d_tasks,
+                                     const uint32_t *d_num_tasks, uint32_t num_sms, cudaStream_t s)
+{
    if (p.d > uint32_t(kRrMaxDim) || p.d == 0)
       return cudaErrorInvalidValue;
    return by_dim(p.d, rr_width(p), [&](auto C, auto W) {
-      return launch_fallback_t<decltype(C)::value, decltype(W)::value>(p, d_rows, d_tasks, num_tasks, s);
+      return launch_fallback_t<decltype(C)::value, decltype(W)::value>(p, d_fb_rows, d_tasks, d_num_tasks, num_sms,
+                                                                       s);
    });
 }
 

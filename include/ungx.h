@@ -438,8 +438,10 @@ void ungx_exact_knn_default_config(uint32_t candidate_k, uint32_t final_degree, 
 uint64_t ungx_exact_knn_rejected_rows(const ungx_context *ctx);
 /* Device time (CUDA events, ms) of the last ungx_exact_knn_graph_device call: out[0] the
  * tensor route's prefilter kernel, out[1] its rerank and certificate, out[2] the exact
- * kernel for the rejected rows (all 0 on the exact route), out[3] the whole call. */
-void ungx_exact_knn_phase_ms(const ungx_context *ctx, double out[4]);
+ * kernel for the rejected rows (all 0 on the exact route), out[3] the whole call,
+ * out[4] from the call's start to the prefilter (plan, uploads, group norms), out[5]
+ * from the rerank's end to the fallback's start (the rejected rows' task list). */
+void ungx_exact_knn_phase_ms(const ungx_context *ctx, double out[6]);
 
 /* Groups g = 0 .. num_groups-1 are rows [group_ranges[2g], group_ranges[2g+1]) of the
  * base vectors of ungx_prepare_base_vectors (any dim up to 352).  d_graph (device):
