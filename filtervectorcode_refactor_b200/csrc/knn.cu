@@ -322,6 +322,101 @@ __device__ void write_row(const KnnParams &p, uint32_t group, uint32_t n, uint32
       row[1 + j] = s;
 }
 
+// The same row written by a whole warp (one row per call, warp-uniform control flow):
+// lane i holds row entry i in h0 and entry 32 + i in h1, so "already in the row" is one
+// vote instead of a scan, and the row goes out in coalesced stores.  hops[t] (from
+// anchor_hops, or computed here when null) are the group's ring-anchor hops, which
+// depend only on the group's size and the layout.
+__device__ __forceinline__ uint32_t anchor_limit_of(const KnnParams &p, uint32_t cand)
+{
+   const uint32_t out_degree = min(p.final_degree, cand);
+   if (out_degree == 0)
+      return 0;
+   const uint32_t near_limit = min(out_degree, min(p.head_keep, p.final_degree));
+   const uint32_t remaining = p.final_degree > near_limit ? p.final_degree - near_limit : 0;
+   return p.anchor_tail ? (p.anchor_slots == 0 ? remaining : min(p.anchor_slots, remaining)) : 0;
+}
+
+// hops[t] = max(1, (t + 1) n / (anchor_limit + 1)) for t < anchor_limit (<= kKnnMax), lane-parallel.
+__device__ __forceinline__ void anchor_hops(const KnnParams &p, uint32_t n, uint32_t cand, uint32_t *hops,
+                                            uint32_t lane)
+{
+   const uint32_t A = min(anchor_limit_of(p, cand), uint32_t(kKnnMax));
+   for (uint32_t t = lane; t < A; t += 32)
+      hops[t] = max(1u, uint32_t((uint64_t(t + 1) * n) / (A + 1)));
+   __syncwarp();
+}
+
+__device__ void write_row_warp(const KnnParams &p, uint32_t group, uint32_t n, uint32_t s, uint32_t cand,
+                               const uint32_t *top, const uint32_t *hops, uint32_t lane)
+{
+   uint32_t *row = p.graph + size_t(p.base[group] + s) * p.graph_stride;
+   const uint32_t out_degree = min(p.final_degree, cand);
+   uint32_t h0 = 0xFFFFFFFFu, h1 = 0xFFFFFFFFu;
+   uint32_t write = 0;
+   auto member = [&](uint32_t c) {
+      return __any_sync(0xffffffffu, (lane < write && h0 == c) || (lane + 32u < write && h1 == c));
+   };
+   auto append = [&](uint32_t c) {
+      if (lane == write)
+         h0 = c;
+      else if (lane + 32u == write)
+         h1 = c;
+      ++write;
+   };
+   if (out_degree > 0)
+   {
+      const uint32_t near_limit = min(out_degree, min(p.head_keep, p.final_degree));
+      if (lane < near_limit)
+         h0 = top[lane];
+      if (lane + 32u < near_limit)
+         h1 = top[lane + 32u];
+      write = near_limit;
+      const uint32_t remaining = p.final_degree > write ? p.final_degree - write : 0;
+      const uint32_t anchor_limit =
+          p.anchor_tail ? (p.anchor_slots == 0 ? remaining : min(p.anchor_slots, remaining)) : 0;
+      if (anchor_limit > 0 && n > 1)
+         for (uint32_t t = 0; t < anchor_limit && write < out_degree; ++t)
+         {
+            const uint32_t hop = hops && t < uint32_t(kKnnMax)
+                                     ? hops[t]
+                                     : max(1u, uint32_t((uint64_t(t + 1) * n) / (anchor_limit + 1)));
+            const bool backward = p.bidir_anchor && (t & 1u);
+            // hop < n: (s + hop) % n and (s + n - hop) % n by one conditional subtraction
+            uint32_t c = backward ? s + n - hop : s + hop;
+            c = c >= n ? c - n : c;
+            for (uint32_t retry = 0; retry < n && write < out_degree;
+                 ++retry, c = backward ? (c == 0 ? n - 1 : c - 1) : (c + 1 == n ? 0 : c + 1))
+            {
+               if (c == s || member(c))
+                  continue;
+               append(c);
+               break;
+            }
+         }
+      const uint32_t tail_start = near_limit;
+      const uint32_t tail_count = cand > tail_start ? cand - tail_start : 0;
+      const uint32_t step = tail_count > remaining && remaining > 0 ? (tail_count + remaining - 1) / remaining : 1;
+      for (uint32_t sc = tail_start; sc < cand && write < out_degree; sc += step)
+         append(top[sc]);
+      for (uint32_t sc = tail_start; sc < cand && write < out_degree; ++sc)
+      {
+         const uint32_t c = top[sc];
+         if (!member(c))
+            append(c);
+      }
+   }
+   if (lane == 0)
+      row[0] = out_degree;
+   // entries the layout wrote, then the padding (slots write .. out_degree - 1, if any
+   // stayed empty, are left as they were, as write_row leaves them)
+   for (uint32_t i = lane; i + 1 < p.graph_stride; i += 32)
+      if (i < write)
+         row[1 + i] = i < 32u ? h0 : h1;
+      else if (i >= out_degree)
+         row[1 + i] = s;
+}
+
 struct KnnTask
 {
    uint32_t group, row0;
@@ -944,7 +1039,6 @@ struct WarpDist
 };
 
 constexpr int kRrWarps = 4;         // a block per work item: 4 warps x 32 rows
-constexpr uint32_t kTopRows = 8;    // rows whose ranked lists a warp holds before laying them out
 constexpr int kRrLists = 3;         // the prefilter's lists per row (column thirds)
 constexpr int kRrDepth = 32;        // entries per list
 constexpr int kRrEntries = kRrLists * kRrDepth;
@@ -977,13 +1071,15 @@ __global__ void __launch_bounds__(kRrWarps * 32) knn_rerank_kernel(const KnnRera
    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
    const WD wd{rr_smem + warp * WD::kWarpFloats, rr_smem + warp * WD::kWarpFloats + NB * WD::kStage, p.X, p.d,
                uint64_t(p.d >> 31)};
-   // the ranked lists of the warp's rows in flight: kTopRows rows, laid out together
-   uint32_t *s_top = reinterpret_cast<uint32_t *>(rr_smem + kRrWarps * WD::kWarpFloats) + warp * (kTopRows * kKnnMax);
+   // the ranked list of the warp's current row, and the group's anchor hops
+   uint32_t *s_top = reinterpret_cast<uint32_t *>(rr_smem + kRrWarps * WD::kWarpFloats) + warp * (2 * kKnnMax);
+   uint32_t *s_hops = s_top + kKnnMax;
    uint32_t cand = p.candidate_k > 0 ? p.candidate_k - 1 : 0;
    cand = min(cand, uint32_t(kKnnMax));
    cand = min(cand, n > 0 ? n - 1 : 0u);
    if (w.row_begin == first && threadIdx.x == 0 && p.entry_points)
       p.entry_points[group] = 0;
+   anchor_hops(p, n, cand, s_hops, lane);
    const double pk = 1.0 / 131072.0; // packed-key tolerance, 2^-17 relative
    const double bmax = sqrt((double)rp.group_maxn2[sg.group_id] * (1.0 + rp.gd));
    const double inv_s = (double)rp.scale->inv_s;
@@ -1160,7 +1256,7 @@ __global__ void __launch_bounds__(kRrWarps * 32) knn_rerank_kernel(const KnnRera
          const bool valid = id[f] != 0xFFFFFFFFu;
          nvalid += __popc(__ballot_sync(0xffffffffu, valid));
          if (valid && rk[f] < cand)
-            s_top[(rr % kTopRows) * kKnnMax + rk[f]] = id[f];
+            s_top[rk[f]] = id[f];
          const uint32_t at = __ballot_sync(0xffffffffu, valid && cand > 0 && rk[f] == cand - 1u);
          if (at)
          {
@@ -1169,7 +1265,7 @@ __global__ void __launch_bounds__(kRrWarps * 32) knn_rerank_kernel(const KnnRera
          }
       }
       for (uint32_t q = nvalid + lane; q < cand; q += 32)
-         s_top[(rr % kTopRows) * kKnnMax + q] = 0xFFFFFFFFu; // the reference's unfilled list slots
+         s_top[q] = 0xFFFFFFFFu; // the reference's unfilled list slots
       // certificate (warp-uniform)
       bool cert;
       if (cand == 0)
@@ -1202,15 +1298,9 @@ __global__ void __launch_bounds__(kRrWarps * 32) knn_rerank_kernel(const KnnRera
             ++n_fail;
          }
       }
-      // every kTopRows rows (and after the last), lane l lays out row rr0 + l
-      if ((rr + 1u) % kTopRows == 0u || rr + 1u == nrows)
-      {
-         const uint32_t rr0 = rr - rr % kTopRows;
-         __syncwarp();
-         if (lane <= rr - rr0)
-            write_row(p, group, n, w.row_begin + r0 + rr0 + lane - first, cand, s_top + lane * kKnnMax);
-         __syncwarp();
-      }
+      __syncwarp();
+      write_row_warp(p, group, n, s, cand, s_top, s_hops, lane);
+      __syncwarp();
    }
    if (lane == 0)
    {
@@ -1281,7 +1371,8 @@ __global__ void __launch_bounds__(kFbWarps * 32) knn_fallback_rows_kernel(const 
    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u, tid = threadIdx.x;
    float *st = fb_smem;                  // [NB][32][kLd]
    float *sq = fb_smem + NB * WD::kStage; // [kFbWarps][kQ]
-   uint32_t *s_top = reinterpret_cast<uint32_t *>(sq + kFbWarps * WD::kQ) + warp * kKnnMax;
+   uint32_t *s_top = reinterpret_cast<uint32_t *>(sq + kFbWarps * WD::kQ) + warp * (2 * kKnnMax);
+   uint32_t *s_hops = s_top + kKnnMax; // the task's group's anchor hops
    const WD wd{st, sq, p.X, p.d, uint64_t(p.d >> 31)};
    const uint32_t ntask = *num_tasks;
    for (uint32_t task = blockIdx.x; task < ntask; task += gridDim.x)
@@ -1340,9 +1431,8 @@ __global__ void __launch_bounds__(kFbWarps * 32) knn_fallback_rows_kernel(const 
       {
          s_top[lane] = lane < cand ? i0 : 0xFFFFFFFFu;
          s_top[32u + lane] = lane + 32u < cand ? i1 : 0xFFFFFFFFu;
-         __syncwarp();
-         if (lane == 0)
-            write_row(p, group, n, s, cand, s_top);
+         anchor_hops(p, n, cand, s_hops, lane);
+         write_row_warp(p, group, n, s, cand, s_top, s_hops, lane);
          __syncwarp();
       }
    }
@@ -1394,7 +1484,7 @@ template <int C, int W, int NB>
 cudaError_t launch_rerank_nb(const KnnRerankParams &p, uint32_t num_items, cudaStream_t s)
 {
    const size_t smem = kRrWarps * (size_t(WarpDist<C, W, NB>::kWarpFloats) * sizeof(float) +
-                                   kTopRows * kKnnMax * sizeof(uint32_t));
+                                   2 * kKnnMax * sizeof(uint32_t));
    cudaError_t e =
        cudaFuncSetAttribute(knn_rerank_kernel<C, W, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
    if (e != cudaSuccess)
@@ -1421,7 +1511,7 @@ cudaError_t launch_fallback_t(const KnnParams &p, const uint32_t *d_fb_rows, con
    using WD = WarpDist<C, W, NB>;
    static_assert(WD::kWarpFloats > 0, "the fallback's block shares one ring");
    const size_t smem = (NB * size_t(WD::kStage) + kFbWarps * size_t(WD::kQ)) * sizeof(float) +
-                       kFbWarps * kKnnMax * sizeof(uint32_t);
+                       kFbWarps * 2 * kKnnMax * sizeof(uint32_t);
    auto kern = knn_fallback_rows_kernel<C, W, NB>;
    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
    if (e != cudaSuccess)
