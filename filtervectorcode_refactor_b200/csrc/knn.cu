@@ -24,7 +24,6 @@
 // a few hundred instructions (a fully unrolled tree missed the instruction cache).
 #include <algorithm>
 #include <cfloat>
-#include <cstdlib>
 #include <type_traits>
 
 #include "kernels.h"
@@ -1057,7 +1056,7 @@ constexpr int kRrMaxDim = 352;      // three 128-dim segments per partial at mos
 // every one of their columns is exact as it stands.  Rejected rows are queued for the
 // exact kernel.
 template <int C, int W, int NB>
-__global__ void __launch_bounds__(kRrWarps * 32) knn_rerank_kernel(const KnnRerankParams rp)
+__global__ void __launch_bounds__(kRrWarps * 32, C == 1 ? 5 : 1) knn_rerank_kernel(const KnnRerankParams rp)
 {
    using WD = WarpDist<C, W, NB>;
    extern __shared__ __align__(16) float rr_smem[];
@@ -1493,13 +1492,11 @@ cudaError_t launch_rerank_nb(const KnnRerankParams &p, uint32_t num_items, cudaS
    return cudaGetLastError();
 }
 
-// Ring depth: UNGX_KNN_RING (2 or 3) for one segment per partial, else 2.
+// A two-stage ring: occupancy (five blocks of four warps per SM for C = 1) hides more
+// latency than deeper rings at fewer warps.
 template <int C, int W>
 cudaError_t launch_rerank_t(const KnnRerankParams &p, uint32_t num_items, cudaStream_t s)
 {
-   const char *env = std::getenv("UNGX_KNN_RING");
-   if (C == 1 && env && std::atoi(env) == 3)
-      return launch_rerank_nb<C, W, 3>(p, num_items, s);
    return launch_rerank_nb<C, W, 2>(p, num_items, s);
 }
 
