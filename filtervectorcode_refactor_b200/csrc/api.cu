@@ -139,7 +139,7 @@ struct ungx_context
    // resident base vectors (a4)
    bool have_vectors = false;
    const float *X = nullptr; // device, n x d
-   DevBuf X_owned, Xh, xnorm, mean, sums, range, scale; // Xh: fp16 operand [n x dp]
+   DevBuf X_owned, Xh, xnorm, mean, sums, range, scale, prep_flag; // Xh: fp16 operand [n x dp]
    uint32_t n = 0, d = 0, dp = 0;
    // per-call scratch
    DevBuf items, segs, empties, ranges, gmax, norm_chunks, counters, fb_rows, fb_items, rows, row_items, out_ids,
@@ -1067,16 +1067,13 @@ int ungx_prepare_base_vectors(ungx_context *ctx, const float *vectors, uint32_t 
    UNGX_CUDA(ctx, ctx->sums.ensure(size_t(d) * sizeof(double)), "mean allocation");
    UNGX_CUDA(ctx, ctx->range.ensure(size_t(d) * 2 * sizeof(uint32_t)), "range allocation");
    UNGX_CUDA(ctx, ctx->scale.ensure(sizeof(ungx::OperandScale)), "scale allocation");
-   UNGX_CUDA(ctx, ungx::launch_colsum(ctx->X, n, d, ctx->sums.as<double>(), ctx->range.as<uint32_t>(), ctx->stream),
-             "column-sum kernel");
+   UNGX_CUDA(ctx, ctx->prep_flag.ensure(sizeof(uint32_t)), "flag allocation");
    UNGX_CUDA(ctx,
-             ungx::launch_scale(ctx->sums.as<double>(), ctx->range.as<uint32_t>(), n, d, ctx->mean.as<float>(),
-                                ctx->scale.as<ungx::OperandScale>(), ctx->stream),
-             "scale kernel");
-   UNGX_CUDA(ctx,
-             ungx::launch_center(ctx->X, ctx->mean.as<float>(), ctx->scale.as<ungx::OperandScale>(), n, d, dp,
-                                 ctx->Xh.as<uint16_t>(), ctx->xnorm.as<float>(), ctx->stream),
-             "centre kernel");
+             ungx::launch_prepare_operand(ctx->X, n, d, dp, ctx->sums.as<double>(), ctx->range.as<uint32_t>(),
+                                          ctx->mean.as<float>(), ctx->scale.as<ungx::OperandScale>(),
+                                          ctx->Xh.as<uint16_t>(), ctx->xnorm.as<float>(), ctx->prep_flag.as<uint32_t>(),
+                                          ctx->stream),
+             "operand preparation kernels");
    // The preparation kernels run on while the caller goes on (a generate call plans on
    // the host meanwhile); work on the context's stream follows them in order, work on
    // another stream waits for this event, and a fault in them surfaces at that work's

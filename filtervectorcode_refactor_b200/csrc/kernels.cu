@@ -239,11 +239,18 @@ __device__ __forceinline__ void insert_pair(float (&kd)[K], uint32_t (&ki)[K], f
 // ------------------------------------------------------------------ prep
 // Column sums (fp64) and column ranges of X over a block of rows; thread = column,
 // four rows in flight per thread.
+// Column sums (fp64), minima and maxima over the rows i * stride (i < n sampled rows).
+// With a gate, the kernel runs only when *gate is non-zero (the full pass after a
+// sampled scale turned out too large for some element).
 __global__ void colsum_kernel(const float *__restrict__ X, uint32_t n, uint32_t d, double *__restrict__ sums,
-                              uint32_t *__restrict__ range, uint32_t rows_per_block)
+                              uint32_t *__restrict__ range, uint32_t rows_per_block, uint32_t stride,
+                              const uint32_t *__restrict__ gate)
 {
+   if (gate && *gate == 0u)
+      return;
    const uint64_t r0 = uint64_t(blockIdx.x) * rows_per_block;
    const uint64_t r1 = (r0 + rows_per_block < n) ? r0 + rows_per_block : uint64_t(n);
+   const uint64_t sd = uint64_t(stride) * d;
    for (uint32_t j = threadIdx.x; j < d; j += blockDim.x)
    {
       double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
@@ -251,8 +258,8 @@ __global__ void colsum_kernel(const float *__restrict__ X, uint32_t n, uint32_t 
       uint64_t r = r0;
       for (; r + 4 <= r1; r += 4)
       {
-         const float v0 = __ldg(X + r * d + j), v1 = __ldg(X + (r + 1) * d + j);
-         const float v2 = __ldg(X + (r + 2) * d + j), v3 = __ldg(X + (r + 3) * d + j);
+         const float v0 = __ldg(X + r * sd + j), v1 = __ldg(X + (r + 1) * sd + j);
+         const float v2 = __ldg(X + (r + 2) * sd + j), v3 = __ldg(X + (r + 3) * sd + j);
          a0 += (double)v0;
          a1 += (double)v1;
          a2 += (double)v2;
@@ -262,7 +269,7 @@ __global__ void colsum_kernel(const float *__restrict__ X, uint32_t n, uint32_t 
       }
       for (; r < r1; ++r)
       {
-         const float v = __ldg(X + r * d + j);
+         const float v = __ldg(X + r * sd + j);
          a0 += (double)v;
          mn = fminf(mn, v);
          mx = fmaxf(mx, v);
@@ -275,10 +282,14 @@ __global__ void colsum_kernel(const float *__restrict__ X, uint32_t n, uint32_t 
 
 // One block: the fp32 mean, the largest centred magnitude m = max_j max(fl(max_j -
 // mean_j), fl(mean_j - min_j)) (rounding is monotone, so no centred element exceeds
-// it), and the scale s = 2^e with 2^14 <= s m < 2^15.
+// it), and the scale s = 2^e with 2^(14 - headroom) <= s m < 2^(15 - headroom): from a
+// row sample, headroom bits leave room for elements beyond the sample's range.
 __global__ void scale_kernel(const double *__restrict__ sums, const uint32_t *__restrict__ range, uint32_t n,
-                             uint32_t d, float *__restrict__ mean, OperandScale *__restrict__ out)
+                             uint32_t d, float *__restrict__ mean, OperandScale *__restrict__ out, int headroom,
+                             const uint32_t *__restrict__ gate)
 {
+   if (gate && *gate == 0u)
+      return;
    __shared__ float s_m[32];
    float m = 0.f;
    bool bad = false;
@@ -307,7 +318,7 @@ __global__ void scale_kernel(const double *__restrict__ sums, const uint32_t *__
       int exact_only = bad ? 1 : 0;
       if (m > 0.f && !bad)
       {
-         e = 14 - ilogbf(m); // ilogb: floor(log2 m), also for subnormal m
+         e = 14 - headroom - ilogbf(m); // ilogb: floor(log2 m), also for subnormal m
          if (e > 60)
             e = 60; // tiny data: keep 1/s^2 a normal float (the certificate sees the loss)
          if (e < -60)
@@ -326,11 +337,16 @@ __global__ void scale_kernel(const double *__restrict__ sums, const uint32_t *__
 }
 
 // Warp per row: v = fl(x - mean), operand fp16(s v) (saturated; s v is exact), norm
-// = fp32 sum of v^2.  Columns d..dp-1 of the operand are zero.
+// = fp32 sum of v^2.  Columns d..dp-1 of the operand are zero.  An element with |s v|
+// above the fp16 range (or not finite) sets *saturated; with a gate the kernel runs
+// only when *gate is non-zero.
 __global__ void center_kernel(const float *__restrict__ X, const float *__restrict__ mean,
                               const OperandScale *__restrict__ scale, uint32_t n, uint32_t d, uint32_t dp,
-                              __half *__restrict__ Xh, float *__restrict__ xnorm)
+                              __half *__restrict__ Xh, float *__restrict__ xnorm, uint32_t *__restrict__ saturated,
+                              const uint32_t *__restrict__ gate)
 {
+   if (gate && *gate == 0u)
+      return;
    extern __shared__ float s_mean[];
    for (uint32_t j = threadIdx.x; j < d; j += blockDim.x)
       s_mean[j] = mean[j];
@@ -348,6 +364,8 @@ __global__ void center_kernel(const float *__restrict__ X, const float *__restri
             v0 = __fsub_rn(X[r * d + j], s_mean[j]);
          if (j + 1 < d)
             v1 = __fsub_rn(X[r * d + j + 1], s_mean[j + 1]);
+         if (saturated && !(fabsf(v0 * sc) <= 65504.f && fabsf(v1 * sc) <= 65504.f))
+            *saturated = 1u;
          const float w0 = fminf(fmaxf(v0 * sc, -65504.f), 65504.f);
          const float w1 = fminf(fmaxf(v1 * sc, -65504.f), 65504.f);
          *reinterpret_cast<__half2 *>(Xh + r * dp + j) = __halves2half2(__float2half_rn(w0), __float2half_rn(w1));
@@ -359,6 +377,74 @@ __global__ void center_kernel(const float *__restrict__ X, const float *__restri
          acc += __shfl_xor_sync(0xffffffffu, acc, o);
       if (lane == 0)
          xnorm[r] = acc;
+   }
+}
+
+// The same operand rows and norms for d % 4 == 0 with X 16-byte aligned: a lane takes
+// four consecutive columns (one 16-byte load, one 8-byte store), and a warp works on
+// four rows at once so that four loads per lane are in flight.  Each lane's fma chain
+// runs over its columns in ascending order before the warp's xor tree, as above.
+__global__ void center4_kernel(const float *__restrict__ X, const float *__restrict__ mean,
+                               const OperandScale *__restrict__ scale, uint32_t n, uint32_t d, uint32_t dp,
+                               __half *__restrict__ Xh, float *__restrict__ xnorm, uint32_t *__restrict__ saturated,
+                               const uint32_t *__restrict__ gate)
+{
+   if (gate && *gate == 0u)
+      return;
+   extern __shared__ float s_mean[];
+   for (uint32_t j = threadIdx.x; j < dp; j += blockDim.x)
+      s_mean[j] = j < d ? mean[j] : 0.f;
+   __syncthreads();
+   const float sc = scale->s;
+   const uint32_t lane = threadIdx.x & 31;
+   const uint64_t warps = (uint64_t(gridDim.x) * blockDim.x) >> 5;
+   const uint32_t q4 = dp / 4u, d4 = d / 4u;
+   constexpr uint32_t RW = 4; // rows per warp iteration
+   for (uint64_t r0 = ((uint64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5) * RW; r0 < n; r0 += warps * RW)
+   {
+      float acc[RW] = {0.f, 0.f, 0.f, 0.f};
+      for (uint32_t c = lane; c < q4; c += 32)
+      {
+         float4 x[RW];
+#pragma unroll
+         for (uint32_t i = 0; i < RW; ++i)
+            x[i] = (r0 + i < n && c < d4) ? __ldg(reinterpret_cast<const float4 *>(X + (r0 + i) * d) + c)
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+         const float4 mu = reinterpret_cast<const float4 *>(s_mean)[c];
+#pragma unroll
+         for (uint32_t i = 0; i < RW; ++i)
+         {
+            if (r0 + i >= n)
+               continue;
+            const bool in = c < d4; // padding columns stay exact zeros
+            const float v0 = in ? __fsub_rn(x[i].x, mu.x) : 0.f, v1 = in ? __fsub_rn(x[i].y, mu.y) : 0.f;
+            const float v2 = in ? __fsub_rn(x[i].z, mu.z) : 0.f, v3 = in ? __fsub_rn(x[i].w, mu.w) : 0.f;
+            if (saturated && !(fabsf(v0 * sc) <= 65504.f && fabsf(v1 * sc) <= 65504.f &&
+                               fabsf(v2 * sc) <= 65504.f && fabsf(v3 * sc) <= 65504.f))
+               *saturated = 1u;
+            const __half2 h01 = __halves2half2(__float2half_rn(fminf(fmaxf(v0 * sc, -65504.f), 65504.f)),
+                                               __float2half_rn(fminf(fmaxf(v1 * sc, -65504.f), 65504.f)));
+            const __half2 h23 = __halves2half2(__float2half_rn(fminf(fmaxf(v2 * sc, -65504.f), 65504.f)),
+                                               __float2half_rn(fminf(fmaxf(v3 * sc, -65504.f), 65504.f)));
+            uint2 pk;
+            pk.x = *reinterpret_cast<const uint32_t *>(&h01);
+            pk.y = *reinterpret_cast<const uint32_t *>(&h23);
+            *reinterpret_cast<uint2 *>(Xh + (r0 + i) * dp + 4u * c) = pk;
+            acc[i] = __fmaf_rn(v0, v0, acc[i]);
+            acc[i] = __fmaf_rn(v1, v1, acc[i]);
+            acc[i] = __fmaf_rn(v2, v2, acc[i]);
+            acc[i] = __fmaf_rn(v3, v3, acc[i]);
+         }
+      }
+#pragma unroll
+      for (uint32_t i = 0; i < RW; ++i)
+      {
+#pragma unroll
+         for (int o = 16; o; o >>= 1)
+            acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
+         if (lane == 0 && r0 + i < n)
+            xnorm[r0 + i] = acc[i];
+      }
    }
 }
 
@@ -1522,39 +1608,85 @@ void tc_certificate_constants(uint32_t d, uint32_t dp, RerankParams &p)
    p.gref = (double(d) + 8.0) * u24;
 }
 
-cudaError_t launch_colsum(const float *X, uint32_t n, uint32_t d, double *sums, uint32_t *range, cudaStream_t s)
+namespace
 {
-   cudaError_t e = cudaMemsetAsync(sums, 0, sizeof(double) * d, s);
-   if (e == cudaSuccess)
-      e = cudaMemsetAsync(range, 0, sizeof(uint32_t) * 2 * d, s);
-   if (e != cudaSuccess || n == 0)
-      return e;
+// Zeroes the column statistics when *gate is non-zero (before the full pass).
+__global__ void zero_stats_kernel(double *__restrict__ sums, uint32_t *__restrict__ range, uint32_t d,
+                                  const uint32_t *__restrict__ gate)
+{
+   if (*gate == 0u)
+      return;
+   for (uint32_t j = threadIdx.x; j < d; j += blockDim.x)
+   {
+      sums[j] = 0.0;
+      range[2 * j] = range[2 * j + 1] = 0u;
+   }
+}
+
+cudaError_t colsum_pass(const float *X, uint32_t n, uint32_t d, uint32_t stride, double *sums, uint32_t *range,
+                        const uint32_t *gate, cudaStream_t s)
+{
+   const uint32_t rows = (n + stride - 1) / stride;
    const uint32_t rows_per_block = 256;
-   const uint32_t blocks = (n + rows_per_block - 1) / rows_per_block;
-   colsum_kernel<<<blocks, d < 256 ? ((d + 31) / 32) * 32 : 256, 0, s>>>(X, n, d, sums, range, rows_per_block);
+   const uint32_t blocks = (rows + rows_per_block - 1) / rows_per_block;
+   colsum_kernel<<<blocks, d < 256 ? ((d + 31) / 32) * 32 : 256, 0, s>>>(X, rows, d, sums, range, rows_per_block,
+                                                                         stride, gate);
    return cudaGetLastError();
 }
 
-cudaError_t launch_scale(const double *sums, const uint32_t *range, uint32_t n, uint32_t d, float *mean,
-                         OperandScale *scale, cudaStream_t s)
+cudaError_t center_pass(const float *X, const float *mean, const OperandScale *scale, uint32_t n, uint32_t d,
+                        uint32_t dp, uint16_t *Xh, float *xnorm, uint32_t *saturated, const uint32_t *gate,
+                        cudaStream_t s)
 {
-   scale_kernel<<<1, 256, 0, s>>>(sums, range, n ? n : 1u, d, mean, scale);
-   return cudaGetLastError();
-}
-
-cudaError_t launch_center(const float *X, const float *mean, const OperandScale *scale, uint32_t n, uint32_t d,
-                          uint32_t dp, uint16_t *Xh, float *xnorm, cudaStream_t s)
-{
-   const size_t smem = sizeof(float) * d;
+   const size_t smem = sizeof(float) * dp;
+   const bool vec = d % 4u == 0 && reinterpret_cast<uintptr_t>(X) % 16u == 0;
+   auto kern = vec ? center4_kernel : center_kernel;
    if (smem > 48 * 1024)
    {
-      cudaError_t e = cudaFuncSetAttribute(center_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e != cudaSuccess)
          return e;
    }
-   const uint32_t blocks = n ? std::min<uint32_t>((n + 7) / 8, 148 * 16) : 1;
-   center_kernel<<<blocks, 256, smem, s>>>(X, mean, scale, n, d, dp, reinterpret_cast<__half *>(Xh), xnorm);
+   const uint32_t rows_per_block = vec ? 32u : 8u; // 8 warps of 4 rows, or of 1
+   const uint32_t blocks = std::min<uint32_t>((n + rows_per_block - 1) / rows_per_block, 148 * 16);
+   kern<<<blocks, 256, smem, s>>>(X, mean, scale, n, d, dp, reinterpret_cast<__half *>(Xh), xnorm, saturated, gate);
    return cudaGetLastError();
+}
+} // namespace
+
+uint32_t operand_sample_stride(uint32_t n) { return n > (1u << 18) ? n / (1u << 16) : 1u; }
+
+cudaError_t launch_prepare_operand(const float *X, uint32_t n, uint32_t d, uint32_t dp, double *sums, uint32_t *range,
+                                   float *mean, OperandScale *scale, uint16_t *Xh, float *xnorm, uint32_t *flag,
+                                   cudaStream_t s)
+{
+   if (n == 0)
+      return cudaErrorInvalidValue;
+   cudaError_t e;
+   if ((e = cudaMemsetAsync(sums, 0, sizeof(double) * d, s)) != cudaSuccess ||
+       (e = cudaMemsetAsync(range, 0, sizeof(uint32_t) * 2 * d, s)) != cudaSuccess ||
+       (e = cudaMemsetAsync(flag, 0, sizeof(uint32_t), s)) != cudaSuccess)
+      return e;
+   const uint32_t stride = operand_sample_stride(n);
+   const uint32_t rows = (n + stride - 1) / stride;
+   if ((e = colsum_pass(X, n, d, stride, sums, range, nullptr, s)) != cudaSuccess)
+      return e;
+   scale_kernel<<<1, 256, 0, s>>>(sums, range, rows, d, mean, scale, stride > 1 ? 2 : 0, nullptr);
+   if ((e = cudaGetLastError()) != cudaSuccess)
+      return e;
+   if ((e = center_pass(X, mean, scale, n, d, dp, Xh, xnorm, stride > 1 ? flag : nullptr, nullptr, s)) !=
+       cudaSuccess)
+      return e;
+   if (stride == 1)
+      return cudaSuccess; // every row was in the statistics: nothing can saturate
+   // an element outside the sample's reach: the exact full pass, gated on the flag
+   zero_stats_kernel<<<1, 256, 0, s>>>(sums, range, d, flag);
+   if ((e = cudaGetLastError()) != cudaSuccess || (e = colsum_pass(X, n, d, 1, sums, range, flag, s)) != cudaSuccess)
+      return e;
+   scale_kernel<<<1, 256, 0, s>>>(sums, range, n, d, mean, scale, 0, flag);
+   if ((e = cudaGetLastError()) != cudaSuccess)
+      return e;
+   return center_pass(X, mean, scale, n, d, dp, Xh, xnorm, nullptr, flag, s);
 }
 
 cudaError_t launch_group_maxnorm(const float *xnorm, const uint32_t *chunks, uint32_t nchunks, uint32_t G, float *out,

@@ -110,15 +110,16 @@ bool tc_a_resident(uint32_t dp);                  // A operand kept in TMEM per 
 size_t tc_smem_bytes(uint32_t dp, uint32_t k);
 void tc_certificate_constants(uint32_t d, uint32_t dp, RerankParams &p);
 
-// Column sums (fp64) and ranges of X; `range` holds, per column, the complement of the
-// minimum's and the maximum's order-preserving integer keys (both zeroed here).
-cudaError_t launch_colsum(const float *X, uint32_t n, uint32_t d, double *sums, uint32_t *range, cudaStream_t s);
-// mean (fp32) and the operand scale from the column sums and ranges.
-cudaError_t launch_scale(const double *sums, const uint32_t *range, uint32_t n, uint32_t d, float *mean,
-                         OperandScale *scale, cudaStream_t s);
-// fp16 operand rows Xh [n x dp] and fp32 norms of the centred rows.
-cudaError_t launch_center(const float *X, const float *mean, const OperandScale *scale, uint32_t n, uint32_t d,
-                          uint32_t dp, uint16_t *Xh, float *xnorm, cudaStream_t s);
+// The fp16 operand Xh [n x dp] (centred, scaled by a power of two) and the fp32 norms
+// of the centred rows.  The mean and the scale come from every row when n <= 2^18, else
+// from the rows i * operand_sample_stride(n), with two bits of headroom in the scale;
+// an element beyond the fp16 range then sets *flag, and gated kernels redo the
+// statistics and the operand from every row (the result is then the same as the full
+// pass's).  No host synchronisation.
+uint32_t operand_sample_stride(uint32_t n);
+cudaError_t launch_prepare_operand(const float *X, uint32_t n, uint32_t d, uint32_t dp, double *sums, uint32_t *range,
+                                   float *mean, OperandScale *scale, uint16_t *Xh, float *xnorm, uint32_t *flag,
+                                   cudaStream_t s);
 cudaError_t launch_group_maxnorm(const float *xnorm, const uint32_t *chunks, uint32_t nchunks, uint32_t G, float *out,
                                  cudaStream_t s);
 cudaError_t launch_fill_empty(const RowRange *ranges, uint32_t nranges, uint32_t k, uint32_t *ids, float *dists,
