@@ -1123,16 +1123,8 @@ __global__ void __launch_bounds__(kRrWarps * 32, C == 1 ? 5 : 1) knn_rerank_kern
    };
    uint32_t cur[kRrLists], nxt[kRrLists];
    float ck[kRrLists], nk[kRrLists], cqn = 0.f, nqn = 0.f;
-   const uint32_t stages = 12u * nrows; // (row, list, reference warp)
    // stage t1 of row rr1 (the current row rr or the next one) into its ring slot
-   auto issue_stage = [&](uint32_t t1, uint32_t rr) {
-      const uint32_t set1 = t1 >> 2, rr1 = set1 / 3u, e1 = set1 % 3u;
-      const uint32_t *src = rr1 == rr ? cur : nxt;
-      const uint32_t row1 = e1 == 0u ? src[0] : (e1 == 1u ? src[1] : src[2]);
-      if ((t1 % 12u) == 0u)
-         wd.issue_query(rr1 & 1u, w.row_begin + r0 + rr1, lane);
-      wd.issue(t1 % uint32_t(NB), row1, t1 & 3u, lane);
-   };
+   static_assert(NB == 2, "the rerank's stage loop is written for a two-stage ring");
    if (nrows)
    {
       cand_rows(0, cur);
@@ -1142,48 +1134,59 @@ __global__ void __launch_bounds__(kRrWarps * 32, C == 1 ? 5 : 1) knn_rerank_kern
          cand_rows(1, nxt);
          cert_inputs(1, nk, nqn);
       }
+      // row 0's query and its first stage (list 0, reference warp 0) into slot 0
+      wd.issue_query(0u, w.row_begin + r0, lane);
+      wd.issue(0u, cur[0], 0u, lane);
    }
-   // the ring starts with stages 0 .. NB - 2 in flight (one commit group each)
-#pragma unroll
-   for (uint32_t t1 = 0; t1 + 1u < uint32_t(NB); ++t1)
-   {
-      if (t1 < stages)
-         issue_stage(t1, 0u);
-      cp_commit();
-   }
+   cp_commit();
    float D[kRrLists] = {INFINITY, INFINITY, INFINITY};
-   float s02 = 0.f, s13 = 0.f;
-   for (uint32_t t = 0; t < stages; ++t)
+   // stages of a row: list e (run-time loop) x reference warp j (unrolled); stage 4 e + j
+   // sits in ring slot j & 1 (a row has 12 stages, an even count), and each iteration
+   // first puts the following stage in flight: the next reference warp, the next list
+   // or the next row's first list with its query
+   for (uint32_t rr = 0; rr < nrows; ++rr)
    {
-      const uint32_t j = t & 3u, set = t >> 2, rr = set / 3u, e = set % 3u;
-      const uint32_t t1 = t + uint32_t(NB) - 1u; // its slot held stage t - 1, summed
-      if (t1 < stages)
-         issue_stage(t1, rr);
-      cp_commit();
-      cp_wait<NB - 1>(); // stage t has landed
-      __syncwarp();
-      const float ws = wd.warp_sum(t % uint32_t(NB), rr & 1u, j, lane);
-      __syncwarp();
-      if (j == 0u)
-         s02 = ws;
-      else if (j == 1u)
-         s13 = ws;
-      else if (j == 2u)
-         s02 = add_ftz(s02, ws);
-      else
+      const uint32_t qb = rr & 1u;
+      for (uint32_t e = 0; e < uint32_t(kRrLists); ++e)
       {
-         const float dd = add_ftz(s02, add_ftz(s13, ws));
          const uint32_t my = e == 0u ? cur[0] : (e == 1u ? cur[1] : cur[2]);
-         const float dv = my != kNoRow && dd < FLT_MAX ? dd : INFINITY;
-         if (e == 0u)
-            D[0] = dv;
-         else if (e == 1u)
-            D[1] = dv;
-         else
-            D[2] = dv;
+         float s02 = 0.f, s13 = 0.f;
+#pragma unroll
+         for (uint32_t j = 0; j < 4u; ++j)
+         {
+            if (j < 3u)
+               wd.issue((j + 1u) & 1u, my, j + 1u, lane);
+            else if (e + 1u < uint32_t(kRrLists))
+               wd.issue(0u, e == 0u ? cur[1] : cur[2], 0u, lane);
+            else if (rr + 1u < nrows)
+            {
+               wd.issue_query(qb ^ 1u, w.row_begin + r0 + rr + 1u, lane);
+               wd.issue(0u, nxt[0], 0u, lane);
+            }
+            cp_commit();
+            cp_wait<1>(); // this stage has landed (the next may be in flight)
+            __syncwarp();
+            const float ws = wd.warp_sum(j & 1u, qb, j, lane);
+            __syncwarp();
+            if (j == 0u)
+               s02 = ws;
+            else if (j == 1u)
+               s13 = ws;
+            else if (j == 2u)
+               s02 = add_ftz(s02, ws);
+            else
+            {
+               const float dd = add_ftz(s02, add_ftz(s13, ws));
+               const float dv = my != kNoRow && dd < FLT_MAX ? dd : INFINITY;
+               if (e == 0u)
+                  D[0] = dv;
+               else if (e == 1u)
+                  D[1] = dv;
+               else
+                  D[2] = dv;
+            }
+         }
       }
-      if (j != 3u || e != 2u)
-         continue;
       // ---- row rr complete: rank, lay out, certify
       const uint32_t row = w.row_begin + r0 + rr; // global row of X
       const uint32_t s = row - first;             // local row
