@@ -162,3 +162,39 @@ def test_tensor_route_large_groups_match_oracle(ctx, d):
     assert bad.size == 0, f"{bad.size} rows differ; first {bad[0]}"
     print(f"kNN tensor route, groups {sizes}, d={d}: {rejected} of {pts} rows rejected")
     assert rejected <= 0.03 * pts
+
+
+def test_tensor_route_many_groups_equal_exact_route(ctx):
+    """Thousands of groups of 65..400 points and one of 70,000 (above 2^16, so local ids
+    and rejected-row slots need more than 16 bits): the tensor route's rows, with the
+    rejected rows grouped and recomputed on the device, equal the exact route's rows."""
+    rng = np.random.default_rng(2024)
+    sizes = list(rng.integers(65, 401, size=2500)) + [70000] + list(rng.integers(65, 401, size=500))
+    d = 16
+    n = int(sum(sizes))
+    X = rng.standard_normal((n, d)).astype(np.float32)
+    X[:n // 3] = np.round(X[:n // 3] * 4) / 4          # coarse values: equal distances, ties by id
+    ranges, at = [], 0
+    for sz in sizes:
+        ranges += [at, at + int(sz)]
+        at += int(sz)
+    ranges = np.array(ranges, dtype=np.uint32)
+    ctx.prepare_base_vectors(X, n, d, on_device=False)
+    rows = {}
+    try:
+        for name, route in ROUTES.items():
+            cfg = nat.exact_knn_default_config(64, 32)
+            cfg.route = route
+            g = torch.full((n, cfg.graph_stride), 7, dtype=torch.int32, device="cuda")
+            e = torch.full((len(sizes),), 9, dtype=torch.int32, device="cuda")
+            ctx.exact_knn_graph_device(ranges, cfg, g.data_ptr(), e.data_ptr())
+            rows[name] = (g.cpu().numpy(), e.cpu().numpy())
+            if route == nat.ROUTE_TENSOR:
+                rejected = ctx.knn_rejected_rows()
+    finally:
+        ctx.release_base_vectors()
+    assert np.array_equal(rows["tensor"][1], rows["exact"][1])
+    bad = np.nonzero(np.any(rows["tensor"][0] != rows["exact"][0], axis=1))[0]
+    assert bad.size == 0, f"{bad.size} rows differ; first {bad[0]}"
+    print(f"many groups: {rejected} of {n} rows rejected")
+    assert rejected > 0  # the fallback path ran
