@@ -962,7 +962,7 @@ struct WarpDist
    __device__ __forceinline__ void issue(uint32_t buf, uint32_t row, uint32_t j, uint32_t lane) const
    {
       float *dst = st + buf * kStage;
-#pragma unroll
+#pragma unroll 8
       for (int k = 0; k < kCopies / 32; ++k)
       {
          uint32_t r, o;
