@@ -657,6 +657,234 @@ __global__ void __launch_bounds__(256) exact_rows_kernel(const ExactParams p)
    }
 }
 
+// The same scan with the target columns staged through shared memory: warp w of the
+// block takes the 32-column steps w, w + 8, ... of each segment, lane l column x0 + l.
+// A step's 32 target rows pass through a two-buffer ring per warp in chunks of 32
+// dimensions, copied by cp.async as coalesced 128-byte row segments (the threads of
+// exact_rows_kernel each read their own target row, 32 rows per load instruction).
+// Lane l then reads its own row from shared memory (row stride 36 floats: the 16-byte
+// reads of a quarter warp hit distinct banks) and applies ref_l2's arithmetic in its
+// order: the 8-lane blocks in ascending dimension, the accumulators carried from chunk
+// to chunk, then the tails, which all lie in the last chunk.  The query row is staged
+// once per row.  W: copy bytes, 16 when d % 4 == 0 and X is 16-byte aligned, else 4.
+constexpr uint32_t kExLd = 36;                       // staged row stride (floats)
+constexpr uint32_t kExStage = 32u * kExLd;           // one buffer of a warp
+constexpr uint32_t kExWarpFloats = 2u * kExStage;    // a warp's two buffers
+constexpr uint32_t kExMaxDim = 8192;                 // query row staged in shared memory
+
+__device__ __forceinline__ void ex_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void ex_wait()
+{
+   asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+template <int W>
+__device__ __forceinline__ void ex_copy(float *dst, const float *src, bool ok)
+{
+   const uint32_t sa = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+   const size_t ga = __cvta_generic_to_global(src);
+   if constexpr (W == 16)
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 16, %2;\n" ::"r"(sa), "l"(ga), "r"(ok ? 16u : 0u) : "memory");
+   else
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(sa), "l"(ga), "r"(ok ? 4u : 0u) : "memory");
+}
+
+template <int KMAX, int W>
+__global__ void __launch_bounds__(256) exact_rows_staged_kernel(const ExactParams p)
+{
+   extern __shared__ __align__(16) float ex_smem[];
+   __shared__ float s_d[8][KMAX];
+   __shared__ uint32_t s_i[8][KMAX];
+   const uint32_t count = p.count_dev ? *(volatile const uint32_t *)p.count_dev : p.count_host;
+   const uint32_t lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+   float *buf = ex_smem + wid * kExWarpFloats;   // this warp's ring
+   float *sq = ex_smem + 8u * kExWarpFloats;     // the query row
+   const uint32_t d = p.d, d8 = d & ~7u, nch = (d + 31u) / 32u;
+   constexpr uint32_t F = W / 4, PER_ROW = 32u / F, PER_LANE = PER_ROW; // 32 rows x PER_ROW copies / 32 lanes
+   for (uint32_t w = blockIdx.x; w < count; w += gridDim.x)
+   {
+      const uint32_t row = p.rows[w];
+      const WorkItem it = p.items[p.row_items[w]];
+      __syncthreads(); // the previous row's query and lists are no longer read
+      for (uint32_t j = threadIdx.x; j < d; j += blockDim.x)
+         sq[j] = p.X[size_t(row) * d + j];
+      __syncthreads();
+      float bd[KMAX];
+      uint32_t bi[KMAX];
+#pragma unroll
+      for (int i = 0; i < KMAX; ++i)
+      {
+         bd[i] = INFINITY;
+         bi[i] = 0xFFFFFFFFu;
+      }
+      for (uint32_t s = 0; s < it.seg_count; ++s)
+      {
+         const Segment sg = p.segs[it.seg_begin + s];
+         const uint32_t end = sg.x_begin + sg.x_count;
+         const uint32_t nsteps = (sg.x_count + 31u) / 32u;
+         const uint32_t mine = nsteps > wid ? (nsteps - wid + 7u) / 8u : 0u;
+         const uint32_t U = mine * nch; // (step, chunk) stages of this warp
+         auto issue = [&](uint32_t u) {
+            const uint32_t i = u / nch, c = u - i * nch;
+            const uint32_t x0 = sg.x_begin + 32u * (wid + 8u * i);
+            float *dst = buf + (u & 1u) * kExStage;
+#pragma unroll
+            for (uint32_t k = 0; k < PER_LANE; ++k)
+            {
+               const uint32_t e = lane + 32u * k, r = e / PER_ROW, o = (e % PER_ROW) * F;
+               const uint32_t dim = 32u * c + o;
+               const bool ok = x0 + r < end && dim < d;
+               ex_copy<W>(dst + r * kExLd + o, ok ? p.X + size_t(x0 + r) * d + dim : p.X, ok);
+            }
+         };
+         if (U)
+            issue(0u);
+         ex_commit();
+         float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f, l4 = 0.f, l5 = 0.f, l6 = 0.f, l7 = 0.f;
+         for (uint32_t u = 0; u < U; ++u)
+         {
+            if (u + 1u < U)
+            {
+               issue(u + 1u);
+               ex_commit();
+               ex_wait<1>();
+            }
+            else
+               ex_wait<0>();
+            __syncwarp();
+            const uint32_t i = u / nch, c = u - i * nch;
+            const float *b = buf + (u & 1u) * kExStage + lane * kExLd; // this lane's column, dims 32c ..
+            const uint32_t base = 32u * c;
+            if (c == 0u)
+               l0 = l1 = l2 = l3 = l4 = l5 = l6 = l7 = 0.f;
+#define UNGX_LANE(l, x, y)                                                                                       \
+   {                                                                                                           \
+      const float t = __fsub_rn((x), (y));                                                                     \
+      l = __fadd_rn(l, __fmul_rn(t, t));                                                                       \
+   }
+#pragma unroll
+            for (uint32_t blk = 0; blk < 4u; ++blk)
+            {
+               const uint32_t i0 = base + 8u * blk;
+               if (i0 + 8u <= d8)
+               {
+                  const float4 b0 = *reinterpret_cast<const float4 *>(b + 8u * blk);
+                  const float4 b1 = *reinterpret_cast<const float4 *>(b + 8u * blk + 4u);
+                  const float *a = sq + i0;
+                  UNGX_LANE(l0, a[0], b0.x);
+                  UNGX_LANE(l1, a[1], b0.y);
+                  UNGX_LANE(l2, a[2], b0.z);
+                  UNGX_LANE(l3, a[3], b0.w);
+                  UNGX_LANE(l4, a[4], b1.x);
+                  UNGX_LANE(l5, a[5], b1.y);
+                  UNGX_LANE(l6, a[6], b1.z);
+                  UNGX_LANE(l7, a[7], b1.w);
+               }
+            }
+#undef UNGX_LANE
+            if (c + 1u == nch)
+            {
+               // the tails (dims d8 .. d - 1, inside this last chunk), then the column's place
+               float s0 = __fadd_rn(l4, l0), s1 = __fadd_rn(l5, l1), s2 = __fadd_rn(l6, l2), s3 = __fadd_rn(l7, l3);
+               uint32_t t0 = d8;
+               if (d - t0 >= 4u)
+               {
+                  const float *bt = b + (t0 - base);
+                  float t;
+                  t = __fsub_rn(sq[t0 + 0], bt[0]);
+                  s0 = __fmaf_rn(t, t, s0);
+                  t = __fsub_rn(sq[t0 + 1], bt[1]);
+                  s1 = __fmaf_rn(t, t, s1);
+                  t = __fsub_rn(sq[t0 + 2], bt[2]);
+                  s2 = __fmaf_rn(t, t, s2);
+                  t = __fsub_rn(sq[t0 + 3], bt[3]);
+                  s3 = __fmaf_rn(t, t, s3);
+                  t0 += 4u;
+               }
+               if (d > t0)
+               {
+                  const float *bt = b + (t0 - base);
+                  const uint32_t rem = d - t0;
+                  float t = __fsub_rn(sq[t0], bt[0]);
+                  s0 = __fmaf_rn(t, t, s0);
+                  if (rem > 1u)
+                  {
+                     t = __fsub_rn(sq[t0 + 1], bt[1]);
+                     s1 = __fmaf_rn(t, t, s1);
+                  }
+                  if (rem > 2u)
+                  {
+                     t = __fsub_rn(sq[t0 + 2], bt[2]);
+                     s2 = __fmaf_rn(t, t, s2);
+                  }
+               }
+               const float D = __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3));
+               const uint32_t x = sg.x_begin + 32u * (wid + 8u * i) + lane;
+               if (x < end && pair_less(D, x, bd[KMAX - 1], bi[KMAX - 1]))
+                  insert_pair<KMAX>(bd, bi, D, x);
+            }
+            __syncwarp(); // this buffer is refilled two stages on
+         }
+      }
+      // every warp's top-k by k rounds of a warp arg-min over (distance, id), then one
+      // thread merges the 8 lists (as exact_rows_kernel)
+      for (uint32_t o = 0; o < p.k; ++o)
+      {
+         float md = bd[0];
+         uint32_t mi = bi[0];
+#pragma unroll
+         for (int off = 16; off; off >>= 1)
+         {
+            const float od = __shfl_xor_sync(0xffffffffu, md, off);
+            const uint32_t oi = __shfl_xor_sync(0xffffffffu, mi, off);
+            if (pair_less(od, oi, md, mi))
+            {
+               md = od;
+               mi = oi;
+            }
+         }
+         if (mi != 0xFFFFFFFFu && bi[0] == mi)
+         {
+#pragma unroll
+            for (int i = 0; i < KMAX - 1; ++i)
+            {
+               bd[i] = bd[i + 1];
+               bi[i] = bi[i + 1];
+            }
+            bd[KMAX - 1] = INFINITY;
+            bi[KMAX - 1] = 0xFFFFFFFFu;
+         }
+         if (lane == 0)
+         {
+            s_d[wid][o] = md;
+            s_i[wid][o] = mi;
+         }
+      }
+      __syncthreads();
+      if (threadIdx.x == 0)
+      {
+#pragma unroll
+         for (int i = 0; i < KMAX; ++i)
+         {
+            bd[i] = INFINITY;
+            bi[i] = 0xFFFFFFFFu;
+         }
+         for (uint32_t wv = 0; wv < 8; ++wv)
+            for (uint32_t o = 0; o < p.k && s_i[wv][o] != 0xFFFFFFFFu; ++o)
+               insert_pair<KMAX>(bd, bi, s_d[wv][o], s_i[wv][o]);
+         const size_t slot = p.out_pos ? size_t(p.out_pos[w]) : size_t(row);
+#pragma unroll
+         for (int i = 0; i < KMAX; ++i)
+            if (uint32_t(i) < p.k)
+            {
+               p.out_ids[slot * p.k + i] = bi[i];
+               if (p.out_dists)
+                  p.out_dists[slot * p.k + i] = bd[i];
+            }
+      }
+   }
+}
+
 // A warp per row, for rows whose candidate columns are few (the additional-edge
 // queries scan one target group each): lanes stride over the columns keeping a sorted
 // top-KMAX each, then k rounds of a warp arg-min over (distance, id) give the row's
@@ -1552,6 +1780,17 @@ cudaError_t launch_exact_t(const ExactParams &p, uint32_t grid, cudaStream_t s)
          exact_rows_warp_kernel<KMAX <= 16 ? KMAX : 16, true><<<g, 256, 0, s>>>(p);
       else
          exact_rows_warp_kernel<KMAX <= 16 ? KMAX : 16, false><<<g, 256, 0, s>>>(p);
+      return cudaGetLastError();
+   }
+   if (KMAX <= 64 && p.d <= kExMaxDim) // (lists of 128 per lane spill either way)
+   {
+      const size_t smem = (8u * kExWarpFloats + p.d) * sizeof(float);
+      const bool w16 = (p.d & 3u) == 0 && reinterpret_cast<uintptr_t>(p.X) % 16u == 0;
+      auto kern = w16 ? exact_rows_staged_kernel<KMAX, 16> : exact_rows_staged_kernel<KMAX, 4>;
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess)
+         return e;
+      kern<<<grid, 256, smem, s>>>(p);
       return cudaGetLastError();
    }
    if ((p.d & 3u) == 0)
