@@ -208,6 +208,150 @@ __device__ __forceinline__ float ref_l2(const float *__restrict__ a, const float
    return __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3));
 }
 
+// ref_l2 for one candidate per lane of a group of TPR lanes (lanes j of `gmask`), the
+// candidate rows staged through shared memory: chunks of 32 dimensions of the group's
+// TPR candidate rows are copied by cp.async in coalesced 128-byte row segments (two
+// buffers of [TPR][36] floats, the next chunk in flight while this one is summed), so
+// that each lane reads its own candidate from shared memory instead of gathering
+// 16-byte pieces of TPR different rows from global memory.  The query row a is read from
+// global memory (the same address for the whole group).  The arithmetic is ref_l2's,
+// in its order: the 8-lane blocks in ascending dimension, then the tails, which all
+// lie in the last chunk.  Every lane of the group calls it (crow = UINT32_MAX: no row,
+// zeros staged, result unused).  W: copy bytes, 16 when d % 4 == 0 and X is 16-byte
+// aligned, else 4.  Used for wide rows (d > 256), where the gathered reads cost most.
+constexpr uint32_t kStLd = 36; // staged row stride (floats): 16-byte aligned, quarter-warp conflict-free
+
+template <int W>
+__device__ __forceinline__ void rr_copy(float *dst, const float *src, bool ok)
+{
+   const uint32_t sa = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+   const size_t ga = __cvta_generic_to_global(src);
+   if constexpr (W == 16)
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 16, %2;\n" ::"r"(sa), "l"(ga), "r"(ok ? 16u : 0u) : "memory");
+   else
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(sa), "l"(ga), "r"(ok ? 4u : 0u) : "memory");
+}
+
+template <int W, uint32_t TPR>
+__device__ float ref_l2_staged(const float *__restrict__ a, const float *__restrict__ X, uint32_t d, uint32_t crow,
+                               float *buf, uint32_t j, uint32_t gmask)
+{
+   constexpr uint32_t F = W / 4;          // floats per copy
+   constexpr uint32_t PER_ROW = 32u / F;  // copies per staged row segment
+   constexpr uint32_t STAGE = TPR * kStLd;
+   const uint32_t nch = (d + 31u) / 32u;
+   auto issue = [&](uint32_t c, uint32_t slot) {
+      float *dst = buf + slot * STAGE;
+#pragma unroll 8
+      for (uint32_t k = 0; k < PER_ROW; ++k) // TPR rows x PER_ROW copies over TPR lanes
+      {
+         const uint32_t i = j + TPR * k, r = i / PER_ROW, o = (i % PER_ROW) * F;
+         const uint32_t rr = __shfl_sync(gmask, crow, r, TPR);
+         const uint32_t dim = 32u * c + o;
+         const bool ok = rr != 0xFFFFFFFFu && dim < d;
+         rr_copy<W>(dst + r * kStLd + o, ok ? X + size_t(rr) * d + dim : X, ok);
+      }
+   };
+   float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f, l4 = 0.f, l5 = 0.f, l6 = 0.f, l7 = 0.f;
+#define UNGX_LANE(l, x, y)                                                                                       \
+   {                                                                                                           \
+      const float t = __fsub_rn((x), (y));                                                                     \
+      l = __fadd_rn(l, __fmul_rn(t, t));                                                                       \
+   }
+   const uint32_t d8 = d & ~7u; // dims of the 8-lane blocks
+   float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+   issue(0, 0);
+   asm volatile("cp.async.commit_group;\n" ::: "memory");
+   for (uint32_t c = 0; c < nch; ++c)
+   {
+      if (c + 1 < nch)
+      {
+         issue(c + 1, (c + 1) & 1u);
+         asm volatile("cp.async.commit_group;\n" ::: "memory");
+         asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+      }
+      else
+         asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+      __syncwarp(gmask);
+      const float *b = buf + (c & 1u) * STAGE + j * kStLd; // this lane's row, dims 32c ..
+      const uint32_t base = 32u * c;
+#pragma unroll
+      for (uint32_t blk = 0; blk < 4; ++blk)
+      {
+         const uint32_t i = base + 8u * blk;
+         if (i + 8u <= d8)
+         {
+            const float4 b0 = *reinterpret_cast<const float4 *>(b + 8u * blk);
+            const float4 b1 = *reinterpret_cast<const float4 *>(b + 8u * blk + 4u);
+            if (W == 16)
+            {
+               const float4 a0 = __ldg(reinterpret_cast<const float4 *>(a + i));
+               const float4 a1 = __ldg(reinterpret_cast<const float4 *>(a + i + 4));
+               UNGX_LANE(l0, a0.x, b0.x);
+               UNGX_LANE(l1, a0.y, b0.y);
+               UNGX_LANE(l2, a0.z, b0.z);
+               UNGX_LANE(l3, a0.w, b0.w);
+               UNGX_LANE(l4, a1.x, b1.x);
+               UNGX_LANE(l5, a1.y, b1.y);
+               UNGX_LANE(l6, a1.z, b1.z);
+               UNGX_LANE(l7, a1.w, b1.w);
+            }
+            else
+            {
+               UNGX_LANE(l0, __ldg(a + i + 0), b0.x);
+               UNGX_LANE(l1, __ldg(a + i + 1), b0.y);
+               UNGX_LANE(l2, __ldg(a + i + 2), b0.z);
+               UNGX_LANE(l3, __ldg(a + i + 3), b0.w);
+               UNGX_LANE(l4, __ldg(a + i + 4), b1.x);
+               UNGX_LANE(l5, __ldg(a + i + 5), b1.y);
+               UNGX_LANE(l6, __ldg(a + i + 6), b1.z);
+               UNGX_LANE(l7, __ldg(a + i + 7), b1.w);
+            }
+         }
+      }
+      if (c + 1 == nch)
+      {
+         // the tails: dims d8 .. d - 1, all inside this last chunk
+         s0 = __fadd_rn(l4, l0), s1 = __fadd_rn(l5, l1), s2 = __fadd_rn(l6, l2), s3 = __fadd_rn(l7, l3);
+         uint32_t i = d8;
+         if (d - i >= 4)
+         {
+            const float *bt = b + (i - base);
+            float t;
+            t = __fsub_rn(__ldg(a + i + 0), bt[0]);
+            s0 = __fmaf_rn(t, t, s0);
+            t = __fsub_rn(__ldg(a + i + 1), bt[1]);
+            s1 = __fmaf_rn(t, t, s1);
+            t = __fsub_rn(__ldg(a + i + 2), bt[2]);
+            s2 = __fmaf_rn(t, t, s2);
+            t = __fsub_rn(__ldg(a + i + 3), bt[3]);
+            s3 = __fmaf_rn(t, t, s3);
+            i += 4;
+         }
+         if (d > i)
+         {
+            const float *bt = b + (i - base);
+            const uint32_t rem = d - i;
+            float t = __fsub_rn(__ldg(a + i), bt[0]);
+            s0 = __fmaf_rn(t, t, s0);
+            if (rem > 1)
+            {
+               t = __fsub_rn(__ldg(a + i + 1), bt[1]);
+               s1 = __fmaf_rn(t, t, s1);
+            }
+            if (rem > 2)
+            {
+               t = __fsub_rn(__ldg(a + i + 2), bt[2]);
+               s2 = __fmaf_rn(t, t, s2);
+            }
+         }
+      }
+      __syncwarp(gmask); // this buffer is refilled two chunks on
+   }
+#undef UNGX_LANE
+   return __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3));
+}
+
 __device__ __forceinline__ bool pair_less(float d0, uint32_t i0, float d1, uint32_t i1)
 {
    return d0 < d1 || (d0 == d1 && i0 < i1);
@@ -1566,8 +1710,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
 //      key shows it cannot reach the top-k;
 //   3. the lanes rank their (distance, id) pairs the same way and write the first k;
 //   4. the certificate is evaluated by every lane, recorded by lane 0.
-template <int KP>
-__global__ void __launch_bounds__(256, 4) rerank_kernel(const RerankParams p)
+template <int KP, bool STAGED>
+__global__ void __launch_bounds__(256, STAGED ? 3 : 4) rerank_kernel(const RerankParams p)
 {
    constexpr uint32_t TPR = KP;           // lanes per row
    constexpr int KD = tc_list_depth(KP);  // depth of each of the row's lists
@@ -1612,6 +1756,9 @@ __global__ void __launch_bounds__(256, 4) rerank_kernel(const RerankParams p)
    const uint32_t grp = tid / TPR, j = tid % TPR;
    const uint32_t gmask = TPR == 32u ? 0xffffffffu : (0xffffu << (tid & 16u));
    const bool vec4 = (p.d & 3u) == 0;
+   const bool w16 = vec4 && reinterpret_cast<uintptr_t>(p.X) % 16u == 0;
+   extern __shared__ __align__(16) float rr_stage[]; // STAGED: [256 / TPR groups][2][TPR][kStLd]
+   float *stage = rr_stage + grp * (2u * TPR * kStLd);
    const double pk = 1.0 / 131072.0; // packed-key tolerance, 2^-17 relative
    const double bmax = sqrt((double)s_maxn2 * (1.0 + p.gd));
    const double inv_s = (double)p.scale->inv_s;
@@ -1678,7 +1825,20 @@ __global__ void __launch_bounds__(256, 4) rerank_kernel(const RerankParams p)
       const double kc = (double)key;
       const double lo = fmax(0.0, kc - fabs(kc) * pk + a2lo - bound) * (1.0 - p.gref);
       float D = INFINITY;
-      if (!(lo > lim) && mine.y < p.n) // a column outside the matrix is never read
+      const bool need = !(lo > lim) && mine.y < p.n; // a column outside the matrix is never read
+      if constexpr (STAGED)
+      {
+         if (__any_sync(gmask, need))
+         {
+            const float *qv = p.X + size_t(row) * p.d;
+            const uint32_t crow = need ? mine.y : 0xFFFFFFFFu;
+            const float Dv = w16 ? ref_l2_staged<16, TPR>(qv, p.X, p.d, crow, stage, j, gmask)
+                                 : ref_l2_staged<4, TPR>(qv, p.X, p.d, crow, stage, j, gmask);
+            if (need)
+               D = Dv;
+         }
+      }
+      else if (need)
       {
          const float *qv = p.X + size_t(row) * p.d;
          const float *xv = p.X + size_t(mine.y) * p.d;
@@ -2011,12 +2171,24 @@ cudaError_t launch_rerank(const RerankParams &p, uint32_t kp, uint32_t num_items
 {
    if (num_items == 0)
       return cudaSuccess;
-   if (kp == 16)
-      rerank_kernel<16><<<num_items, 256, 0, s>>>(p);
-   else if (kp == 32)
-      rerank_kernel<32><<<num_items, 256, 0, s>>>(p);
-   else
+   if (kp != 16 && kp != 32)
       return cudaErrorInvalidValue;
+   // wide rows (d > 256): the candidate rows staged through shared memory (config 3,
+   // d = 960: 13 vs 30 ms); narrow ones gather them from global memory (config 2: 0.96
+   // vs 1.22 ms staged)
+   if (p.d > 256)
+   {
+      const size_t smem = size_t(256) * 2 * kStLd * sizeof(float);
+      auto kern = kp == 16 ? rerank_kernel<16, true> : rerank_kernel<32, true>;
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess)
+         return e;
+      kern<<<num_items, 256, smem, s>>>(p);
+   }
+   else if (kp == 16)
+      rerank_kernel<16, false><<<num_items, 256, 0, s>>>(p);
+   else
+      rerank_kernel<32, false><<<num_items, 256, 0, s>>>(p);
    return cudaGetLastError();
 }
 
