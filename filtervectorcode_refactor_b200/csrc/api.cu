@@ -133,7 +133,7 @@ struct ungx_context
    uint64_t mem_limit = 0; // device budget of ungx_cross_edges_build (0: free memory)
    DevBuf pass_x, pass_ids, pass_dists, pass_ranges; // capacity path
    Plan knn_plan; // tensor-core kNN seeding: items of the groups' self-joins
-   DevBuf knn_items, knn_segs, knn_chunks, knn_gmax, knn_fb, knn_fbt, knn_fbc, knn_cnt;
+   DevBuf knn_items, knn_segs, knn_chunks, knn_gmax, knn_fb, knn_fbp, knn_fbt, knn_fbc, knn_pend, knn_cnt;
    uint32_t inject = UNGX_INJECT_NONE;
    PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
    // resident base vectors (a4)
@@ -799,13 +799,19 @@ int run_knn_tensor(ungx_context *ctx, const std::vector<uint32_t> &ranges, uint3
    for (const auto &it : plan.items)
       item_rows += it.row_count;
    const uint64_t rows_max = std::max<uint64_t>(item_rows, 1);
-   UNGX_CUDA(ctx, ctx->knn_fb.ensure(sizeof(uint32_t) * rows_max), "fallback list");
-   UNGX_CUDA(ctx, ctx->knn_fbt.ensure(3 * sizeof(uint32_t) * rows_max), "fallback tasks");
-   UNGX_CUDA(ctx, ctx->knn_fbc.ensure(sizeof(uint32_t) * std::max<uint32_t>(num_groups, 1)), "fallback counts");
-   UNGX_CUDA(ctx, cudaMemsetAsync(ctx->knn_fbc.p, 0, sizeof(uint32_t) * num_groups, s), "fallback counts");
+   // rejected rows: four buckets per group (a failing list 0, 1, 2, or the full rescan),
+   // each with room for the group's rows; pending entries for up to 2^17 partial rows
+   const uint32_t pend_cap = (uint32_t)std::min<uint64_t>(rows_max, 1u << 17);
+   UNGX_CUDA(ctx, ctx->knn_fb.ensure(4 * sizeof(uint32_t) * rows_max), "fallback list");
+   UNGX_CUDA(ctx, ctx->knn_fbp.ensure(4 * sizeof(uint32_t) * rows_max), "fallback list");
+   UNGX_CUDA(ctx, ctx->knn_fbt.ensure(4 * sizeof(uint32_t) * rows_max), "fallback tasks");
+   UNGX_CUDA(ctx, ctx->knn_fbc.ensure(4 * sizeof(uint32_t) * std::max<uint32_t>(num_groups, 1)), "fallback counts");
+   UNGX_CUDA(ctx, ctx->knn_pend.ensure(size_t(pend_cap) * 96 * sizeof(float2)), "fallback entries");
+   UNGX_CUDA(ctx, cudaMemsetAsync(ctx->knn_fbc.p, 0, 4 * sizeof(uint32_t) * num_groups, s), "fallback counts");
    UNGX_CUDA(ctx, ctx->knn_cnt.ensure(64), "counters");
    UNGX_CUDA(ctx, cudaMemsetAsync(ctx->knn_cnt.p, 0, 64, s), "counters");
-   // [0] item counter [2] status [3] fallback tasks, [4..7] u64 x2: certified, rejected rows
+   // [0] item counter [1] partial rows with pending entries [2] status [3] fallback tasks,
+   // [4..7] u64 x2: certified, rejected rows
    uint32_t *cnt = ctx->knn_cnt.as<uint32_t>();
    ungx::TcMaps maps;
    if ((st = make_map(ctx, &maps.a, ctx->Xh.p, ctx->n, ctx->dp, 128)))
@@ -854,7 +860,11 @@ int run_knn_tensor(ungx_context *ctx, const std::vector<uint32_t> &ranges, uint3
    rp.gref = (16.0 + 2.0 * ((ctx->d + 127) / 128)) * std::ldexp(1.0, -24);
    rp.abs_err = (double(ctx->d) + 128.0) * std::ldexp(1.0, -126) * 2.0;
    rp.fb_rows = ctx->knn_fb.as<uint32_t>();
+   rp.fb_pend_idx = ctx->knn_fbp.as<uint32_t>();
    rp.fb_group_count = ctx->knn_fbc.as<uint32_t>();
+   rp.fb_pend = ctx->knn_pend.as<float2>();
+   rp.fb_pend_count = cnt + 1;
+   rp.fb_pend_cap = pend_cap;
    rp.counters = reinterpret_cast<unsigned long long *>(cnt + 4);
    UNGX_CUDA(ctx, ungx::launch_knn_rerank(rp, (uint32_t)plan.items.size(), s), "kNN rerank launch");
    UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[2], s), "event");
@@ -866,7 +876,8 @@ int run_knn_tensor(ungx_context *ctx, const std::vector<uint32_t> &ranges, uint3
              "kNN fallback task kernel");
    UNGX_CUDA(ctx, cudaEventRecord(ctx->ev[5], s), "event");
    UNGX_CUDA(ctx,
-             ungx::launch_knn_fallback_rows(kp, ctx->knn_fb.as<uint32_t>(), ctx->knn_fbt.as<uint32_t>(), cnt + 3,
+             ungx::launch_knn_fallback_rows(kp, ctx->knn_fb.as<uint32_t>(), ctx->knn_fbp.as<uint32_t>(),
+                                            ctx->knn_pend.as<float2>(), ctx->knn_fbt.as<uint32_t>(), cnt + 3,
                                             ctx->num_sms, s),
              "kNN fallback kernel");
    launched = true;
@@ -984,7 +995,7 @@ int ungx_context_destroy(ungx_context *ctx)
                      &ctx->knn_rows, &ctx->intra_off, &ctx->intra_cols, &ctx->graph_off, &ctx->graph_cols,
                      &ctx->own_runs, &ctx->all_runs, &ctx->recv, &ctx->pass_x, &ctx->pass_ids, &ctx->pass_dists,
                      &ctx->pass_ranges, &ctx->knn_items, &ctx->knn_segs, &ctx->knn_chunks, &ctx->knn_gmax,
-                     &ctx->knn_fb, &ctx->knn_fbt, &ctx->knn_fbc, &ctx->knn_cnt})
+                     &ctx->knn_fb, &ctx->knn_fbp, &ctx->knn_fbt, &ctx->knn_fbc, &ctx->knn_pend, &ctx->knn_cnt})
       b->release();
    ctx->host_stage.release();
    for (auto &ev : ctx->ev)

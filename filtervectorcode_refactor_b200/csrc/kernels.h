@@ -187,21 +187,29 @@ struct KnnRerankParams
    const OperandScale *scale;
    const int *status;        // the prefilter's status word: non-zero = nothing to do
    double c1, c2, c3, c4, gd, gref, abs_err;
-   uint32_t *fb_rows;        // rows the certificate rejected: local row at base[group] + slot
-   uint32_t *fb_group_count; // [groups], zeroed before launch: the slots taken per group
+   // Rows the certificate rejected, in four buckets per group: bucket h < 3 holds rows
+   // whose lists all passed but list h (only list h's columns are rescanned), bucket 3
+   // the rows rescanned in full.  Local row at 4 base[group] + h n_group + slot.
+   uint32_t *fb_rows;
+   uint32_t *fb_pend_idx;       // same index: the row's pending entries (bucket h < 3)
+   uint32_t *fb_group_count;    // [4 groups], zeroed before launch: the slots taken per bucket
+   float2 *fb_pend;             // [fb_pend_cap][96]: the passing lists' (distance, id) by rank
+   uint32_t *fb_pend_count;     // zeroed before launch
+   uint32_t fb_pend_cap;
    unsigned long long *counters; // [0] certified rows, [1] rejected rows
 };
 cudaError_t launch_knn_rerank(const KnnRerankParams &p, uint32_t num_items, cudaStream_t s);
 // The exact seeding of the rows the rerank's certificate rejected, with no host round
-// trip: launch_knn_fallback_tasks cuts each group's rejected rows (fb_rows at base[g],
-// fb_group_count[g] of them) into tasks of up to 8 rows, d_tasks [3 x max_tasks] =
-// (group, first slot, rows) and *d_num_tasks (one block); launch_knn_fallback_rows then
-// runs them on a persistent grid (num_sms x a few blocks) that reads *d_num_tasks.
-// max_tasks bounds the task list (the number of points of the call suffices).
+// trip: launch_knn_fallback_tasks cuts each bucket (group, h) of rejected rows into
+// tasks of up to 8 rows, d_tasks [4 x max_tasks] = (group, bucket, first slot, rows) and
+// *d_num_tasks (one block); launch_knn_fallback_rows then runs them on a persistent grid
+// (num_sms x a few blocks) that reads *d_num_tasks.  max_tasks bounds the task list
+// (the number of points of the call suffices).
 cudaError_t launch_knn_fallback_tasks(const uint32_t *d_group_count, uint32_t num_groups, uint32_t *d_tasks,
                                       uint32_t max_tasks, uint32_t *d_num_tasks, cudaStream_t s);
-cudaError_t launch_knn_fallback_rows(const KnnParams &p, const uint32_t *d_fb_rows, const uint32_t *d_tasks,
-                                     const uint32_t *d_num_tasks, uint32_t num_sms, cudaStream_t s);
+cudaError_t launch_knn_fallback_rows(const KnnParams &p, const uint32_t *d_fb_rows, const uint32_t *d_pend_idx,
+                                     const float2 *d_pend, const uint32_t *d_tasks, const uint32_t *d_num_tasks,
+                                     uint32_t num_sms, cudaStream_t s);
 
 // ---- graph assembly (graph.cu)
 // group_of[v] = group of row v (1..G), G + 1 for rows outside every group.

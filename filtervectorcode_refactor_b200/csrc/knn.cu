@@ -1192,6 +1192,7 @@ __global__ void __launch_bounds__(kRrWarps * 32, C == 1 ? 5 : 1) knn_rerank_kern
       const uint32_t s = row - first;             // local row
       uint32_t db[kRrLists], id[kRrLists];
       const float T = fminf(ck[0], fminf(ck[1], ck[2])); // smallest last key of a list that dropped a column
+      const float ck_row[kRrLists] = {ck[0], ck[1], ck[2]};
       const float qn_row = cqn;
 #pragma unroll
       for (int f = 0; f < kRrLists; ++f)
@@ -1268,16 +1269,19 @@ __global__ void __launch_bounds__(kRrWarps * 32, C == 1 ? 5 : 1) knn_rerank_kern
       }
       for (uint32_t q = nvalid + lane; q < cand; q += 32)
          s_top[q] = 0xFFFFFFFFu; // the reference's unfilled list slots
-      // certificate (warp-uniform)
-      bool cert;
+      // certificate (warp-uniform), list by list: list f passes when it dropped no
+      // column or its last key clears the cand-th distance; one failing list is
+      // rescanned alone (its columns only, merged with the other lists' entries),
+      // more (or no usable bound) send the row to the full rescan
+      uint32_t bad = 0; // bit f: list f fails; 8: the row needs the full rescan
       if (cand == 0)
-         cert = true; // nothing to rank
+         bad = 0; // nothing to rank
       else if (exact_only)
-         cert = false; // keys of data outside the fp16 operand's range prove nothing
+         bad = 8; // keys of data outside the fp16 operand's range prove nothing
       else if (T == INFINITY)
-         cert = true; // no list dropped a column: every column was ranked
+         bad = 0; // no list dropped a column: every column was ranked
       else if (!have_k)
-         cert = false;
+         bad = 8;
       else
       {
          const double qn = (double)qn_row;
@@ -1285,18 +1289,53 @@ __global__ void __launch_bounds__(kRrWarps * 32, C == 1 ? 5 : 1) knn_rerank_kern
          const double bound = (rp.c1 * ahi * bmax + rp.c2 * bmax * bmax + rp.c3 * inv_s * (ahi + bmax) +
                                rp.c4 * inv_s * inv_s) *
                               (1.0 + 1.0 / 1024.0);
-         const double Tp = (double)T - fabs((double)T) * pk;
-         const double lhs = (qn * (1.0 - rp.gd) + Tp - bound) * (1.0 - rp.gref) - rp.abs_err;
-         cert = lhs > (double)dk;
+#pragma unroll
+         for (int f = 0; f < kRrLists; ++f)
+         {
+            const float Tf = ck_row[f];
+            if (Tf == INFINITY)
+               continue;
+            const double Tp = (double)Tf - fabs((double)Tf) * pk;
+            const double lhs = (qn * (1.0 - rp.gd) + Tp - bound) * (1.0 - rp.gref) - rp.abs_err;
+            if (!(lhs > (double)dk))
+               bad |= 1u << f;
+         }
+      }
+      uint32_t h = bad == 0 ? 4u : (bad == 8u || __popc(bad) > 1 ? 3u : uint32_t(__ffs(bad) - 1));
+      uint32_t pidx = 0;
+      if (h < 3u)
+      {
+         // the passing lists' entries by rank, for the partial rescan's merge
+         if (lane == 0)
+            pidx = atomicAdd(rp.fb_pend_count, 1u);
+         pidx = __shfl_sync(0xffffffffu, pidx, 0);
+         if (pidx >= rp.fb_pend_cap)
+            h = 3u; // no room: the full rescan
+         else
+         {
+            float2 *pe = rp.fb_pend + size_t(pidx) * kRrEntries;
+#pragma unroll
+            for (int f = 0; f < kRrLists; ++f)
+            {
+               const bool keep = id[f] != 0xFFFFFFFFu && uint32_t(f) != h;
+               if (id[f] != 0xFFFFFFFFu)
+                  pe[rk[f]] = keep ? make_float2(D[f], __uint_as_float(id[f]))
+                                   : make_float2(INFINITY, __uint_as_float(0xFFFFFFFFu));
+            }
+            for (uint32_t q = nvalid + lane; q < uint32_t(kRrEntries); q += 32)
+               pe[q] = make_float2(INFINITY, __uint_as_float(0xFFFFFFFFu));
+         }
       }
       if (lane == 0)
       {
-         if (cert)
+         if (h == 4u)
             ++n_cert;
          else
          {
-            const uint32_t slot = atomicAdd(rp.fb_group_count + group, 1u);
-            rp.fb_rows[p.base[group] + slot] = s;
+            const uint32_t slot = atomicAdd(rp.fb_group_count + 4u * group + h, 1u);
+            const size_t at = 4u * size_t(p.base[group]) + size_t(h) * n + slot;
+            rp.fb_rows[at] = s;
+            rp.fb_pend_idx[at] = pidx;
             ++n_fail;
          }
       }
@@ -1353,6 +1392,50 @@ __device__ __forceinline__ void list_insert(float dist, uint32_t x0, uint32_t ca
    }
 }
 
+// The same insert for a list seeded out of column order (the partial rescan starts
+// from the passing lists' entries): places and the threshold test compare (distance,
+// id) pairs, and a column enters only below FLT_MAX, so the list ends as the cand
+// smallest pairs below FLT_MAX, which is what the reference's inserts in ascending id
+// keep.
+__device__ __forceinline__ void list_insert_pair(float dist, uint32_t x0, uint32_t cand, uint32_t lane, float &e0,
+                                                 float &e1, uint32_t &i0, uint32_t &i1)
+{
+   const uint32_t lc = cand > 0 ? (cand - 1u) & 31u : 0u;
+   auto less = [](float da, uint32_t ia, float db, uint32_t ib) { return da < db || (da == db && ia < ib); };
+   const float last0 = __shfl_sync(0xffffffffu, cand > 32u ? e1 : e0, lc);
+   const uint32_t lid0 = __shfl_sync(0xffffffffu, cand > 32u ? i1 : i0, lc);
+   uint32_t m = __ballot_sync(0xffffffffu, dist < FLT_MAX && less(dist, x0 + lane, last0, lid0));
+   while (m)
+   {
+      const uint32_t b = __ffs(m) - 1u;
+      m &= m - 1u;
+      const float nd = __shfl_sync(0xffffffffu, dist, b);
+      const uint32_t nid = x0 + b;
+      const float last = __shfl_sync(0xffffffffu, cand > 32u ? e1 : e0, lc);
+      const uint32_t lid = __shfl_sync(0xffffffffu, cand > 32u ? i1 : i0, lc);
+      if (!less(nd, nid, last, lid))
+         continue;
+      const uint32_t pos = __popc(__ballot_sync(0xffffffffu, lane < cand && less(e0, i0, nd, nid))) +
+                           __popc(__ballot_sync(0xffffffffu, lane + 32u < cand && less(e1, i1, nd, nid)));
+      const float u0 = __shfl_up_sync(0xffffffffu, e0, 1), u1 = __shfl_up_sync(0xffffffffu, e1, 1);
+      const uint32_t v0 = __shfl_up_sync(0xffffffffu, i0, 1), v1 = __shfl_up_sync(0xffffffffu, i1, 1);
+      const float t31 = __shfl_sync(0xffffffffu, e0, 31);
+      const uint32_t j31 = __shfl_sync(0xffffffffu, i0, 31);
+      const float p1 = lane ? u1 : t31;
+      const uint32_t q1 = lane ? v1 : j31;
+      if (lane >= pos)
+      {
+         e0 = lane == pos ? nd : u0;
+         i0 = lane == pos ? nid : v0;
+      }
+      if (lane + 32u >= pos)
+      {
+         e1 = lane + 32u == pos ? nd : p1;
+         i1 = lane + 32u == pos ? nid : q1;
+      }
+   }
+}
+
 // Rows the certificate rejected, in tasks of up to kFbWarps rows of one group (task =
 // (group, first slot, rows); the rows' local ids at fb_rows[base[group] + slot]): warp w
 // takes the task's row w, and every 32-column step of the group passes once through a
@@ -1365,6 +1448,8 @@ constexpr int kFbWarps = 8;
 template <int C, int W, int NB>
 __global__ void __launch_bounds__(kFbWarps * 32) knn_fallback_rows_kernel(const KnnParams p,
                                                                         const uint32_t *__restrict__ fb_rows,
+                                                                        const uint32_t *__restrict__ fb_pend_idx,
+                                                                        const float2 *__restrict__ fb_pend,
                                                                         const uint32_t *__restrict__ tasks,
                                                                         const uint32_t *__restrict__ num_tasks)
 {
@@ -1380,14 +1465,20 @@ __global__ void __launch_bounds__(kFbWarps * 32) knn_fallback_rows_kernel(const 
    for (uint32_t task = blockIdx.x; task < ntask; task += gridDim.x)
    {
       __syncthreads(); // the previous task's ring is no longer read
-      const uint32_t group = tasks[3 * task], slot0 = tasks[3 * task + 1], cnt = tasks[3 * task + 2];
+      const uint32_t group = tasks[4 * task], h = tasks[4 * task + 1], slot0 = tasks[4 * task + 2],
+                     cnt = tasks[4 * task + 3];
       const uint32_t first = p.ranges[2 * group], n = p.ranges[2 * group + 1] - first;
       const bool active = warp < cnt;
-      const uint32_t s = active ? fb_rows[p.base[group] + slot0 + warp] : 0u;
+      const size_t at = 4u * size_t(p.base[group]) + size_t(h) * n + slot0 + warp;
+      const uint32_t s = active ? fb_rows[at] : 0u;
       uint32_t cand = p.candidate_k > 0 ? p.candidate_k - 1 : 0;
       cand = min(cand, uint32_t(kKnnMax));
       cand = min(cand, n > 0 ? n - 1 : 0u);
-      const uint32_t steps = cand > 0 ? (n + 31u) / 32u : 0u;
+      // bucket 3: every 32-column step; bucket h < 3: the steps of list h (k = h mod 3:
+      // chunks h and h + 3 of each 192-column tile from the group's first row)
+      const uint32_t all_steps = cand > 0 ? (n + 31u) / 32u : 0u;
+      const uint32_t steps = h == 3u ? all_steps : (all_steps > h ? (all_steps - h + 2u) / 3u : 0u);
+      const uint32_t sstep = h == 3u ? 1u : 3u, s0 = h == 3u ? 0u : h;
       const uint32_t stages = 4u * steps; // (32-column step, reference warp)
       if (active && stages)
          wd.issue_query(warp, first + s, lane);
@@ -1396,11 +1487,46 @@ __global__ void __launch_bounds__(kFbWarps * 32) knn_fallback_rows_kernel(const 
       for (uint32_t t1 = 0; t1 + 1u < uint32_t(NB); ++t1)
       {
          if (t1 < stages)
-            wd.issue_block(t1, first, 32u * (t1 >> 2), n, t1 & 3u, tid, kFbWarps * 32u);
+            wd.issue_block(t1, first, 32u * (s0 + sstep * (t1 >> 2)), n, t1 & 3u, tid, kFbWarps * 32u);
          cp_commit();
       }
       float e0 = FLT_MAX, e1 = FLT_MAX; // list entries lane and lane + 32
       uint32_t i0 = 0xFFFFFFFFu, i1 = 0xFFFFFFFFu;
+      if (active && h < 3u && cand > 0)
+      {
+         // the seed: the passing lists' entries in (distance, id) order, the failing
+         // list's places empty; compacted to the first cand places (s_top and s_hops
+         // hold the distances and ids meanwhile)
+         const float2 *pe = fb_pend + size_t(fb_pend_idx[at]) * kRrEntries;
+         float *sd = reinterpret_cast<float *>(s_top);
+         uint32_t base_pos = 0;
+#pragma unroll
+         for (int q = 0; q < kRrEntries / 32; ++q)
+         {
+            const float2 v = pe[lane + 32u * q];
+            const bool ok = __float_as_uint(v.y) != 0xFFFFFFFFu;
+            const uint32_t bal = __ballot_sync(0xffffffffu, ok);
+            const uint32_t pos = base_pos + __popc(bal & ((1u << lane) - 1u));
+            base_pos += __popc(bal);
+            if (ok && pos < cand)
+            {
+               sd[pos] = v.x;
+               s_top[kKnnMax + pos] = __float_as_uint(v.y);
+            }
+         }
+         __syncwarp();
+         if (lane < cand && lane < base_pos)
+         {
+            e0 = sd[lane];
+            i0 = s_top[kKnnMax + lane];
+         }
+         if (lane + 32u < cand && lane + 32u < base_pos)
+         {
+            e1 = sd[lane + 32u];
+            i1 = s_top[kKnnMax + lane + 32u];
+         }
+         __syncwarp();
+      }
       float s02 = 0.f, s13 = 0.f;
       for (uint32_t t = 0; t < stages; ++t)
       {
@@ -1408,7 +1534,8 @@ __global__ void __launch_bounds__(kFbWarps * 32) knn_fallback_rows_kernel(const 
          __syncthreads();   // ... for every thread's copies; stage t - 1's slot is free
          const uint32_t t1 = t + uint32_t(NB) - 1u;
          if (t1 < stages)
-            wd.issue_block(t1 % uint32_t(NB), first, 32u * (t1 >> 2), n, t1 & 3u, tid, kFbWarps * 32u);
+            wd.issue_block(t1 % uint32_t(NB), first, 32u * (s0 + sstep * (t1 >> 2)), n, t1 & 3u, tid,
+                           kFbWarps * 32u);
          cp_commit();
          const uint32_t j = t & 3u;
          if (active)
@@ -1422,9 +1549,13 @@ __global__ void __launch_bounds__(kFbWarps * 32) knn_fallback_rows_kernel(const 
                s02 = add_ftz(s02, ws);
             else
             {
-               const uint32_t x0 = 32u * (t >> 2), x = x0 + lane;
-               list_insert(x < n && x != s ? add_ftz(s02, add_ftz(s13, ws)) : FLT_MAX, x0, cand, lane, e0, e1, i0,
-                           i1);
+               const uint32_t x0 = 32u * (s0 + sstep * (t >> 2)), x = x0 + lane;
+               if (h == 3u)
+                  list_insert(x < n && x != s ? add_ftz(s02, add_ftz(s13, ws)) : FLT_MAX, x0, cand, lane, e0, e1,
+                              i0, i1);
+               else
+                  list_insert_pair(x < n && x != s ? add_ftz(s02, add_ftz(s13, ws)) : INFINITY, x0, cand, lane, e0,
+                                   e1, i0, i1);
             }
          }
       }
@@ -1440,9 +1571,9 @@ __global__ void __launch_bounds__(kFbWarps * 32) knn_fallback_rows_kernel(const 
    }
 }
 
-// One block: group g's fb_group_count[g] rejected rows become ceil(count / kFbWarps)
-// tasks (group, first slot, rows), in group order (a block-wide scan of the groups'
-// task counts gives each thread's first task).
+// One block: the rejected rows of bucket (g, h) (fb_group_count[4 g + h] of them)
+// become ceil(count / kFbWarps) tasks (group, bucket, first slot, rows), in bucket
+// order (a block-wide scan of the buckets' task counts gives each thread's first task).
 constexpr uint32_t kFbTaskThreads = 1024;
 
 __global__ void __launch_bounds__(kFbTaskThreads) knn_fallback_tasks_kernel(const uint32_t *__restrict__ group_count,
@@ -1452,11 +1583,12 @@ __global__ void __launch_bounds__(kFbTaskThreads) knn_fallback_tasks_kernel(cons
 {
    __shared__ uint32_t s_sum[kFbTaskThreads];
    const uint32_t tid = threadIdx.x;
-   const uint32_t per = (G + kFbTaskThreads - 1) / kFbTaskThreads;
-   const uint32_t g0 = min(G, tid * per), g1 = min(G, g0 + per);
+   const uint32_t B = 4u * G; // buckets
+   const uint32_t per = (B + kFbTaskThreads - 1) / kFbTaskThreads;
+   const uint32_t b0 = min(B, tid * per), b1 = min(B, b0 + per);
    uint32_t local = 0;
-   for (uint32_t g = g0; g < g1; ++g)
-      local += (group_count[g] + kFbWarps - 1) / kFbWarps;
+   for (uint32_t b = b0; b < b1; ++b)
+      local += (group_count[b] + kFbWarps - 1) / kFbWarps;
    s_sum[tid] = local;
    __syncthreads();
    for (uint32_t off = 1; off < kFbTaskThreads; off <<= 1)
@@ -1467,15 +1599,16 @@ __global__ void __launch_bounds__(kFbTaskThreads) knn_fallback_tasks_kernel(cons
       __syncthreads();
    }
    uint32_t at = s_sum[tid] - local;
-   for (uint32_t g = g0; g < g1; ++g)
+   for (uint32_t b = b0; b < b1; ++b)
    {
-      const uint32_t c = group_count[g];
+      const uint32_t c = group_count[b];
       for (uint32_t k = 0; k < c; k += kFbWarps, ++at)
          if (at < max_tasks)
          {
-            tasks[3 * at] = g;
-            tasks[3 * at + 1] = k;
-            tasks[3 * at + 2] = min(uint32_t(kFbWarps), c - k);
+            tasks[4 * at] = b >> 2;
+            tasks[4 * at + 1] = b & 3u;
+            tasks[4 * at + 2] = k;
+            tasks[4 * at + 3] = min(uint32_t(kFbWarps), c - k);
          }
    }
    if (tid == kFbTaskThreads - 1)
@@ -1504,8 +1637,9 @@ cudaError_t launch_rerank_t(const KnnRerankParams &p, uint32_t num_items, cudaSt
 }
 
 template <int C, int W>
-cudaError_t launch_fallback_t(const KnnParams &p, const uint32_t *d_fb_rows, const uint32_t *d_tasks,
-                              const uint32_t *d_num_tasks, uint32_t num_sms, cudaStream_t s)
+cudaError_t launch_fallback_t(const KnnParams &p, const uint32_t *d_fb_rows, const uint32_t *d_pend_idx,
+                              const float2 *d_pend, const uint32_t *d_tasks, const uint32_t *d_num_tasks,
+                              uint32_t num_sms, cudaStream_t s)
 {
    constexpr int NB = 4;
    using WD = WarpDist<C, W, NB>;
@@ -1520,7 +1654,7 @@ cudaError_t launch_fallback_t(const KnnParams &p, const uint32_t *d_fb_rows, con
    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kFbWarps * 32, smem)) != cudaSuccess)
       return e;
    const uint32_t grid = std::max<uint32_t>(1u, num_sms) * uint32_t(std::max(per_sm, 1));
-   kern<<<grid, kFbWarps * 32, smem, s>>>(p, d_fb_rows, d_tasks, d_num_tasks);
+   kern<<<grid, kFbWarps * 32, smem, s>>>(p, d_fb_rows, d_pend_idx, d_pend, d_tasks, d_num_tasks);
    return cudaGetLastError();
 }
 
@@ -1563,14 +1697,15 @@ cudaError_t launch_knn_fallback_tasks(const uint32_t *d_group_count, uint32_t nu
    return cudaGetLastError();
 }
 
-cudaError_t launch_knn_fallback_rows(const KnnParams &p, const uint32_t *d_fb_rows, const uint32_t *d_tasks,
-                                     const uint32_t *d_num_tasks, uint32_t num_sms, cudaStream_t s)
+cudaError_t launch_knn_fallback_rows(const KnnParams &p, const uint32_t *d_fb_rows, const uint32_t *d_pend_idx,
+                                     const float2 *d_pend, const uint32_t *d_tasks, const uint32_t *d_num_tasks,
+                                     uint32_t num_sms, cudaStream_t s)
 {
    if (p.d > uint32_t(kRrMaxDim) || p.d == 0)
       return cudaErrorInvalidValue;
    return by_dim(p.d, rr_width(p), [&](auto C, auto W) {
-      return launch_fallback_t<decltype(C)::value, decltype(W)::value>(p, d_fb_rows, d_tasks, d_num_tasks, num_sms,
-                                                                       s);
+      return launch_fallback_t<decltype(C)::value, decltype(W)::value>(p, d_fb_rows, d_pend_idx, d_pend, d_tasks,
+                                                                       d_num_tasks, num_sms, s);
    });
 }
 
