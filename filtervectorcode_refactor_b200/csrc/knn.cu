@@ -1192,26 +1192,12 @@ __global__ void __launch_bounds__(kRrWarps * 32, C == 1 ? 5 : 1) knn_rerank_kern
       const uint32_t s = row - first;             // local row
       uint32_t db[kRrLists], id[kRrLists];
       const float T = fminf(ck[0], fminf(ck[1], ck[2])); // smallest last key of a list that dropped a column
-      const float ck_row[kRrLists] = {ck[0], ck[1], ck[2]};
       const float qn_row = cqn;
 #pragma unroll
       for (int f = 0; f < kRrLists; ++f)
       {
          id[f] = D[f] != INFINITY ? cur[f] - first : 0xFFFFFFFFu;
          db[f] = __float_as_uint(D[f]); // non-negative: the bits order as the values
-      }
-      // the next row's candidates and certificate inputs, one row ahead of the pipeline
-#pragma unroll
-      for (int f = 0; f < kRrLists; ++f)
-      {
-         cur[f] = nxt[f];
-         ck[f] = nk[f];
-      }
-      cqn = nqn;
-      if (rr + 2u < nrows)
-      {
-         cand_rows(rr + 2u, nxt);
-         cert_inputs(rr + 2u, nk, nqn);
       }
       // rank of each entry by (distance, local id): first by distance alone; equal
       // distances of valid entries share a rank then, which shows as a rank sum below
@@ -1292,7 +1278,7 @@ __global__ void __launch_bounds__(kRrWarps * 32, C == 1 ? 5 : 1) knn_rerank_kern
 #pragma unroll
          for (int f = 0; f < kRrLists; ++f)
          {
-            const float Tf = ck_row[f];
+            const float Tf = ck[f];
             if (Tf == INFINITY)
                continue;
             const double Tp = (double)Tf - fabs((double)Tf) * pk;
@@ -1338,6 +1324,19 @@ __global__ void __launch_bounds__(kRrWarps * 32, C == 1 ? 5 : 1) knn_rerank_kern
             rp.fb_pend_idx[at] = pidx;
             ++n_fail;
          }
+      }
+      // the next row's candidates and certificate inputs, one row ahead of the pipeline
+#pragma unroll
+      for (int f = 0; f < kRrLists; ++f)
+      {
+         cur[f] = nxt[f];
+         ck[f] = nk[f];
+      }
+      cqn = nqn;
+      if (rr + 2u < nrows)
+      {
+         cand_rows(rr + 2u, nxt);
+         cert_inputs(rr + 2u, nk, nqn);
       }
       __syncwarp();
       write_row_warp(p, group, n, s, cand, s_top, s_hops, lane);
