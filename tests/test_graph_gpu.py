@@ -152,3 +152,36 @@ def test_build_cross_group_edges_device_vectors_global_ids(ctx, golden):
     ctx.release_base_vectors()
     e_off, e_cols = expected_merged_graph(golden, intra_off, intra_local, True)
     assert np.array_equal(off, e_off) and np.array_equal(cols, e_cols)
+
+
+@pytest.mark.parametrize("d", [3, 13, 64, 98, 130, 259])
+def test_additional_edges_random_dims(ctx, d):
+    """Additional edges of a configuration-2 label structure (6,000 points) over random
+    vectors of dimension d, against the C restatement of the reference's exact variant:
+    the query kernel's staged row scan at ragged dimensions, copy widths 4 and 16 bytes."""
+    import oracle as O
+    from filtervectorcode_refactor_b200 import datasets
+
+    c = datasets.make_config(2, seed=7 + d, n=6000)
+    lg = nat.LabelGraph(c["label_offsets"], c["labels"])
+    gf = np.concatenate([[0], lg.group_ranges[2::2], [lg.group_ranges[-1]]]).astype(np.uint32)
+    n, k = 6000, c["k"]
+    rng = np.random.default_rng(d)
+    Xr = rng.integers(-40, 40, size=(n, d)).astype(np.float32) / 8  # coarse values: ties
+    ids_ref, _, _ = O.oracle().cross_exact(Xr, k, gf, lg.out_offsets, lg.out_ids)
+    src_ref, dst_ref = O.oracle().additional_edges(Xr, k, gf, lg.out_offsets, lg.out_ids, ids_ref)
+    prob = nat.Problem(n, d, k, lg.group_ranges, lg.out_offsets, lg.out_ids, route=nat.ROUTE_EXACT)
+    ctx.prepare_base_vectors(Xr, n, d, on_device=False)
+    try:
+        d_ids = torch.empty((n, k), dtype=torch.int32, device="cuda")
+        d_dists = torch.empty((n, k), dtype=torch.float32, device="cuda")
+        ctx.generate_device(prob, d_ids.data_ptr(), d_dists.data_ptr())
+        torch.cuda.synchronize()
+        assert np.array_equal(d_ids.cpu().numpy().view(np.uint32).ravel(), ids_ref.ravel())
+        st = ctx.additional_edges(prob, d_ids.data_ptr())
+        src, dst, _, _ = ctx.additional_edges_copy(n, int(st.edges))
+    finally:
+        ctx.release_base_vectors()
+    assert src_ref.size > 0
+    assert np.array_equal(src, src_ref)
+    assert np.array_equal(dst, dst_ref)
