@@ -46,6 +46,7 @@ constexpr uint32_t kChunkK = 64;          // fp16 columns per K chunk: 128-byte 
 constexpr uint32_t kAChunk = 128 * 128;   // 128 rows x 64 fp16, 128-byte swizzled
 constexpr uint32_t kBChunk = kBN * 128;   // 192 rows x 64 fp16
 constexpr uint32_t kMaxStages = 16;
+constexpr uint32_t kKeyLd = 36;           // a lane's row of 32 chunk keys (16-byte stores hit distinct banks)
 constexpr uint32_t kSmemLimit = 232448;   // per-block opt-in maximum on sm_100
 constexpr uint32_t kNoItem = 0xFFFFFFFFu;
 // Limit of the waits that retire work already in flight before the CTA exits
@@ -54,14 +55,14 @@ constexpr uint64_t kDrainWaitNs = 2000000000ull;
 
 struct TcLayout
 {
-   uint32_t stages, stage_off, stage_bytes, colv_off, norm_off, bar_off, misc_off, total;
+   uint32_t stages, stage_off, stage_bytes, colv_off, norm_off, key_off, bar_off, misc_off, total;
 };
 
 // Stages of the ring: A resident (dp <= 256) -> one 24 KB target chunk per stage, the
 // item's source chunks (16 KB) pass through the same ring once per item; A streamed
 // -> 16 KB source + 24 KB target chunk per stage.  As many stages as fit (at most
 // 16), then the epilogue's column table (12 warps x list-depth slots x 32 lanes), the chunk
-// norms, barriers, and the item slots.
+// norms, the chunk keys (12 warps x 32 lanes x kKeyLd), barriers, and the item slots.
 __host__ __device__ inline TcLayout tc_layout(uint32_t dp, bool a_res, uint32_t kp)
 {
    (void)dp;
@@ -69,12 +70,14 @@ __host__ __device__ inline TcLayout tc_layout(uint32_t dp, bool a_res, uint32_t 
    L.stage_off = 0;
    L.stage_bytes = a_res ? kBChunk : kAChunk + kBChunk;
    const uint32_t kd = uint32_t(tc_list_depth(int(kp)));
-   const uint32_t fixed = kEpiWarps * kd * 32u * 4u + kEpiWarps * 32u * 4u + 48u * 8u + 128u + 1024u;
+   const uint32_t fixed =
+       kEpiWarps * kd * 32u * 4u + kEpiWarps * 32u * 4u + kEpiWarps * 32u * kKeyLd * 4u + 48u * 8u + 128u + 1024u;
    const uint32_t fit = fixed < kSmemLimit ? (kSmemLimit - fixed) / L.stage_bytes : 0u;
    L.stages = fit < kMaxStages ? fit : kMaxStages;
    L.colv_off = L.stage_off + L.stages * L.stage_bytes;
    L.norm_off = L.colv_off + kEpiWarps * kd * 32u * 4u;
-   L.bar_off = L.norm_off + kEpiWarps * 32u * 4u;
+   L.key_off = L.norm_off + kEpiWarps * 32u * 4u;
+   L.bar_off = L.key_off + kEpiWarps * 32u * kKeyLd * 4u;
    L.misc_off = L.bar_off + 48u * 8u;
    L.total = L.misc_off + 128u;
    return L;
@@ -89,25 +92,6 @@ __device__ __forceinline__ uint32_t float_key(float f)
 __device__ __forceinline__ float key_float(uint32_t k)
 {
    return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
-}
-
-// v[j] for a per-thread index j in 0..31, by a 5-level select tree (registers only).
-__device__ __forceinline__ uint32_t select32(const uint32_t (&v)[32], uint32_t j)
-{
-   uint32_t a[16], b[8], c[4], e[2];
-#pragma unroll
-   for (int i = 0; i < 16; ++i)
-      a[i] = (j & 1u) ? v[2 * i + 1] : v[2 * i];
-#pragma unroll
-   for (int i = 0; i < 8; ++i)
-      b[i] = (j & 2u) ? a[2 * i + 1] : a[2 * i];
-#pragma unroll
-   for (int i = 0; i < 4; ++i)
-      c[i] = (j & 4u) ? b[2 * i + 1] : b[2 * i];
-#pragma unroll
-   for (int i = 0; i < 2; ++i)
-      e[i] = (j & 8u) ? c[2 * i + 1] : c[2 * i];
-   return (j & 16u) ? e[1] : e[0];
 }
 
 // Two fp32 lanes per instruction (sm_100 f32x2 arithmetic); each lane rounds exactly
@@ -1189,6 +1173,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
    const uint32_t SR = L.stages / R; // stages per ring
    uint8_t *sStage = smem + L.stage_off;
    float *sNorm = reinterpret_cast<float *>(smem + L.norm_off);
+   float *sKey = reinterpret_cast<float *>(smem + L.key_off);
    uint32_t *sColv = reinterpret_cast<uint32_t *>(smem + L.colv_off);
    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bar_off);
    uint64_t *full = bars;              // [R * SR <= 16], ring r = stages [r SR, r SR + SR)
@@ -1548,6 +1533,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
       const uint32_t h = (warp - 2u) >> 2;
       const uint32_t r = q * 32u + lane;
       float *nrm = sNorm + (warp - 2u) * 32u;
+      float *mykey = sKey + ((warp - 2u) * 32u + lane) * kKeyLd; // this lane's keys of the chunk
       const float nis = p.scale->neg2_inv_s2; // keys in the unscaled centred domain
       uint32_t tseq = 0, iseq = 0;
       bool ok = true;
@@ -1619,10 +1605,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
                ptx::tmem_ld32(tmem_base + ((q * 32u) << 16) + kAccCol0 + b * kBN + j * 32u, raw);
                ptx::tmem_wait_ld();
                // key = fl(norm + nis * acc); the sign of fl(key - thr) is set exactly when
-               // key < thr (an exact zero difference is +0): element jj goes to bit 31 - jj
+               // key < thr (an exact zero difference is +0): element jj goes to bit 31 - jj.
+               // When some lane has a candidate, the keys go to the lane's row in shared
+               // memory, where the inserts read them.
                const float4 *n4 = reinterpret_cast<const float4 *>(nrm);
                const uint64_t nis2 = pack2(nis, nis), thr2 = pack2(thr, thr);
                uint32_t mask = 0;
+               uint64_t kv[16];
 #pragma unroll
                for (int g = 0; g < 8; ++g)
                {
@@ -1632,6 +1621,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
                   const uint64_t k23 =
                       fma2(nis2, pack2(__uint_as_float(raw[4 * g + 2]), __uint_as_float(raw[4 * g + 3])),
                            pack2(nv.z, nv.w));
+                  kv[2 * g] = k01;
+                  kv[2 * g + 1] = k23;
                   const uint64_t d01 = sub2(k01, thr2), d23 = sub2(k23, thr2);
                   mask = __funnelshift_l(uint32_t(d01), mask, 1);
                   mask = __funnelshift_l(uint32_t(d01 >> 32), mask, 1);
@@ -1647,10 +1638,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
                   if (off < 32u)
                      mask &= ~(0x80000000u >> off);
                }
+               if (__any_sync(0xffffffffu, mask != 0u))
+               {
+#pragma unroll
+                  for (int g = 0; g < 8; ++g)
+                     *reinterpret_cast<uint4 *>(mykey + 4 * g) = make_uint4(
+                         uint32_t(kv[2 * g]), uint32_t(kv[2 * g] >> 32), uint32_t(kv[2 * g + 1]), uint32_t(kv[2 * g + 1] >> 32));
+               }
                while (__any_sync(0xffffffffu, mask != 0u))
                {
                   const uint32_t jj = mask ? uint32_t(__clz(mask)) : 0u;
-                  const float kk = __fmaf_rn(nis, __uint_as_float(select32(raw, jj)), nrm[jj]);
+                  const float kk = mykey[jj];
                   const uint32_t ev = __float_as_uint(key[KD - 1]) & kSlotMask; // slot that drops out
                   const float v = __uint_as_float((__float_as_uint(kk) & ~kSlotMask) | ev);
                   const bool ins = mask != 0u && v < key[KD - 1];
