@@ -64,6 +64,32 @@ def test_reference_harness_reproduces_golden_additional_edges(golden):
     assert np.array_equal(src, golden["add_from"]) and np.array_equal(dst, golden["add_to"])
 
 
+@pytest.mark.parametrize("d", [3, 13, 259])
+def test_oracle_additional_edges_match_reference_at_ragged_dims(d):
+    """The C restatement's cross edges and additional edges equal the reference harness's
+    at dimensions with 8-wide and 4-wide tails (the oracle the device's ragged-dimension
+    additional-edge test compares with), on a configuration-2 label structure of 3,000
+    points with coarse, tie-heavy values."""
+    ref = O.reference()
+    if ref is None:
+        pytest.skip("reference build (oracle/_ref) not present on this machine")
+    from filtervectorcode_refactor_b200 import _native as nat
+    from filtervectorcode_refactor_b200 import datasets
+    c = datasets.make_config(2, seed=7 + d, n=3000)
+    lg = nat.LabelGraph(c["label_offsets"], c["labels"])
+    gf = np.concatenate([[0], lg.group_ranges[2::2], [lg.group_ranges[-1]]]).astype(np.uint32)
+    X = np.random.default_rng(d).integers(-40, 40, size=(3000, d)).astype(np.float32) / 8
+    k = c["k"]
+    ids, dists, _ = O.oracle().cross_exact(X, k, gf, lg.out_offsets, lg.out_ids)
+    rids, rdists, _ = ref.cross_exact(X, k, gf, lg.out_offsets, lg.out_ids)
+    assert np.array_equal(ids, rids)
+    assert np.array_equal(dists.view(np.uint32), rdists.view(np.uint32))
+    src, dst = O.oracle().additional_edges(X, k, gf, lg.out_offsets, lg.out_ids, ids)
+    rsrc, rdst = ref.additional_edges(X, k, gf, lg.out_offsets, lg.out_ids, rids)
+    assert src.size > 0
+    assert np.array_equal(src, rsrc) and np.array_equal(dst, rdst)
+
+
 def test_planted_mistake_is_caught(golden):
     """A mistake planted in the oracle's output (on the CPU) must fail the comparison
     the GPU tests use."""
